@@ -1,0 +1,149 @@
+// ggml block-quantised weight formats on the device.
+//
+// Q8_0 (34 bytes / 32 weights): f16 d, int8 q[32];          w = d * q
+// Q4_K (144 bytes / 256 weights): f16 d, f16 dmin, 12 bytes of packed
+//   6-bit (scale, min) pairs for 8 sub-blocks of 32, 128 bytes of nibbles;
+//   sub-block j: w = (d * sc_j) * q - (dmin * m_j).  Nibbles: byte l of
+//   the 32-byte group g holds element l of sub-block 2g (low nibble) and of
+//   sub-block 2g+1 (high nibble).
+// The arithmetic follows gguf-py 0.19.0 quants.py (Q8_0 :396-401, Q4_K
+// :475-523) operation by operation in f32 with round-to-nearest and no
+// contraction (__fmul_rn / __fsub_rn), so the f32 output is bit-identical.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace dcpp {
+
+namespace {
+
+__device__ __forceinline__ float half_bits_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+// Unpack the 6-bit scale and min of sub-block j (0..7) from the 12 packed
+// bytes (gguf-py Q4_K.get_scale_min: bytes 0-3 low scales, 4-7 low mins,
+// 8-11 high bits).
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+  if (j < 4) {
+    sc = s[j] & 0x3F;
+    m = s[j + 4] & 0x3F;
+  } else {
+    sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30);
+    m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30);
+  }
+}
+
+template <bool kBf16>
+__device__ __forceinline__ void store_val(void* out, int64_t i, float v) {
+  if (kBf16) {
+    __nv_bfloat16 b = __float2bfloat16_rn(v);
+    reinterpret_cast<__nv_bfloat16*>(out)[i] = b;
+  } else {
+    reinterpret_cast<float*>(out)[i] = v;
+  }
+}
+
+// One thread per 32-weight Q8_0 block.
+template <bool kBf16>
+__global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
+  int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (b >= nblocks) return;
+  const uint8_t* blk = blocks + b * 34;
+  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+#pragma unroll 8
+  for (int i = 0; i < 32; ++i) {
+    const float q = static_cast<float>(static_cast<int8_t>(blk[2 + i]));
+    store_val<kBf16>(out, b * 32 + i, __fmul_rn(q, d));
+  }
+}
+
+// One thread per 32-weight sub-block of a Q4_K super-block.
+template <bool kBf16>
+__global__ void dequant_q4_k_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
+  int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (t >= nblocks * 8) return;
+  const int64_t b = t >> 3;
+  const int j = static_cast<int>(t & 7);
+  const uint8_t* blk = blocks + b * 144;
+  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+  const float dmin = half_bits_to_f32(static_cast<uint16_t>(blk[2] | (blk[3] << 8)));
+  int sc, m;
+  q4k_scale_min(blk + 4, j, sc, m);
+  const float ds = __fmul_rn(d, static_cast<float>(sc));
+  const float dm = __fmul_rn(dmin, static_cast<float>(m));
+  const uint8_t* qs = blk + 16 + (j >> 1) * 32;
+  const int shift = (j & 1) * 4;
+#pragma unroll 8
+  for (int l = 0; l < 32; ++l) {
+    const float q = static_cast<float>((qs[l] >> shift) & 0x0F);
+    store_val<kBf16>(out, b * 256 + j * 32 + l, __fsub_rn(__fmul_rn(ds, q), dm));
+  }
+}
+
+template <bool kBf16>
+__global__ void dequant_f16_kernel(const uint16_t* __restrict__ in, int64_t n, void* out) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) store_val<kBf16>(out, i, half_bits_to_f32(in[i]));
+}
+
+template <bool kBf16>
+__global__ void dequant_bf16_kernel(const uint16_t* __restrict__ in, int64_t n, void* out) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    if (kBf16) reinterpret_cast<uint16_t*>(out)[i] = in[i];
+    else reinterpret_cast<float*>(out)[i] = bf16_bits_to_f32(in[i]);
+  }
+}
+
+template <bool kBf16>
+__global__ void dequant_f32_kernel(const float* __restrict__ in, int64_t n, void* out) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) store_val<kBf16>(out, i, in[i]);
+}
+
+inline unsigned grid_for(int64_t n, int threads) {
+  return static_cast<unsigned>((n + threads - 1) / threads);
+}
+
+template <bool kBf16>
+cudaError_t dequant_impl(int type, const void* blocks, int64_t n, void* out, cudaStream_t s) {
+  constexpr int T = 256;
+  switch (type) {
+    case kTypeQ8_0: {
+      if (n % 32) return cudaErrorInvalidValue;
+      int64_t nb = n / 32;
+      if (nb) dequant_q8_0_kernel<kBf16><<<grid_for(nb, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      break;
+    }
+    case kTypeQ4_K: {
+      if (n % 256) return cudaErrorInvalidValue;
+      int64_t nb = n / 256;
+      if (nb) dequant_q4_k_kernel<kBf16><<<grid_for(nb * 8, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      break;
+    }
+    case kTypeF16:
+      if (n) dequant_f16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
+      break;
+    case kTypeBF16:
+      if (n) dequant_bf16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
+      break;
+    case kTypeF32:
+      if (n) dequant_f32_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const float*>(blocks), n, out);
+      break;
+    default:
+      return cudaErrorNotSupported;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_dequant_f32(int type, const void* blocks, int64_t n, float* out, cudaStream_t s) {
+  return dequant_impl<false>(type, blocks, n, out, s);
+}
+
+cudaError_t launch_dequant_bf16(int type, const void* blocks, int64_t n, uint16_t* out, cudaStream_t s) {
+  return dequant_impl<true>(type, blocks, n, out, s);
+}
+
+}  // namespace dcpp

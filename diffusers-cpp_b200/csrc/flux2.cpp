@@ -1,0 +1,1194 @@
+// Flux2 DiT denoise step on sm_100a: the C++ model host and its C ABI.
+#include "flux2.hpp"
+
+#include <cuda_fp16.h>
+
+#include <string.h>
+
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <fstream>
+#include <sstream>
+
+namespace dcpp {
+
+size_t row_bytes_of(int type, int64_t n);
+
+namespace {
+
+int64_t block_size_of(int type) {
+  if (type == kTypeQ8_0) return 32;
+  if (type == kTypeQ4_K) return 256;
+  return 1;
+}
+size_t block_bytes_of(int type) {
+  switch (type) {
+    case kTypeQ8_0: return 34;
+    case kTypeQ4_K: return 144;
+    case kTypeF32: return 4;
+    default: return 2;
+  }
+}
+bool is_gemm_type(int t) {
+  return t == kTypeQ8_0 || t == kTypeQ4_K || t == kTypeBF16 || t == kTypeF16 || t == kTypeF32;
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+// ---- a small JSON reader for diffusers config.json (flat object with
+// numbers, booleans, null, strings and arrays of numbers).
+struct Json {
+  const std::string& s;
+  size_t i = 0;
+  explicit Json(const std::string& src) : s(src) {}
+  void ws() {
+    while (i < s.size() && isspace(static_cast<unsigned char>(s[i]))) ++i;
+  }
+  [[noreturn]] void bad() { fail(DCPP_ERR_INVALID_ARG, "config json: parse error at offset " + std::to_string(i)); }
+  std::string str() {
+    ws();
+    if (i >= s.size() || s[i] != '"') bad();
+    ++i;
+    std::string r;
+    while (i < s.size() && s[i] != '"') {
+      if (s[i] == '\\' && i + 1 < s.size()) ++i;
+      r += s[i++];
+    }
+    if (i >= s.size()) bad();
+    ++i;
+    return r;
+  }
+  // Returns a value as text: number, true/false/null, "string", or [a,b,..].
+  std::string value() {
+    ws();
+    if (i >= s.size()) bad();
+    if (s[i] == '"') return "\"" + str() + "\"";
+    if (s[i] == '[' || s[i] == '{') {
+      char open = s[i], close = open == '[' ? ']' : '}';
+      int depth = 0;
+      size_t st = i;
+      bool in_str = false;
+      for (; i < s.size(); ++i) {
+        char c = s[i];
+        if (in_str) {
+          if (c == '\\') ++i;
+          else if (c == '"') in_str = false;
+          continue;
+        }
+        if (c == '"') in_str = true;
+        else if (c == open) ++depth;
+        else if (c == close && --depth == 0) { ++i; return s.substr(st, i - st); }
+      }
+      bad();
+    }
+    size_t st = i;
+    while (i < s.size() && s[i] != ',' && s[i] != '}' && s[i] != ']' && !isspace(static_cast<unsigned char>(s[i]))) ++i;
+    return s.substr(st, i - st);
+  }
+  std::map<std::string, std::string> object() {
+    std::map<std::string, std::string> m;
+    ws();
+    if (i >= s.size() || s[i] != '{') bad();
+    ++i;
+    ws();
+    if (i < s.size() && s[i] == '}') { ++i; return m; }
+    for (;;) {
+      std::string k = str();
+      ws();
+      if (i >= s.size() || s[i] != ':') bad();
+      ++i;
+      m[k] = value();
+      ws();
+      if (i < s.size() && s[i] == ',') { ++i; continue; }
+      if (i < s.size() && s[i] == '}') { ++i; break; }
+      bad();
+    }
+    return m;
+  }
+};
+
+std::vector<int64_t> parse_int_list(const std::string& v) {
+  std::vector<int64_t> r;
+  std::string t;
+  for (char c : v) {
+    if (c == '[' || c == ']' || c == ',' || isspace(static_cast<unsigned char>(c))) {
+      if (!t.empty()) { r.push_back(static_cast<int64_t>(std::stod(t))); t.clear(); }
+    } else {
+      t += c;
+    }
+  }
+  if (!t.empty()) r.push_back(static_cast<int64_t>(std::stod(t)));
+  return r;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------- config
+Flux2Config Flux2Config::from_file(const std::string& path) {
+  std::ifstream f(path);
+  if (!f.is_open()) fail(DCPP_ERR_NOT_FOUND, "Failed to open configuration file: " + path);
+  std::stringstream ss;
+  ss << f.rdbuf();
+  std::string text = ss.str();
+  Json j(text);
+  auto m = j.object();
+  Flux2Config c;
+  auto num = [&](const char* k, auto& dst) {
+    auto it = m.find(k);
+    if (it == m.end() || it->second == "null") return;
+    using T = std::decay_t<decltype(dst)>;
+    dst = static_cast<T>(std::stod(it->second));
+  };
+  num("patch_size", c.patch_size);
+  num("in_channels", c.in_channels);
+  {
+    auto it = m.find("out_channels");
+    if (it != m.end()) c.out_channels = it->second == "null" ? -1 : static_cast<int64_t>(std::stod(it->second));
+  }
+  num("num_layers", c.num_layers);
+  num("num_single_layers", c.num_single_layers);
+  num("attention_head_dim", c.attention_head_dim);
+  num("num_attention_heads", c.num_attention_heads);
+  num("joint_attention_dim", c.joint_attention_dim);
+  num("timestep_guidance_channels", c.timestep_guidance_channels);
+  num("mlp_ratio", c.mlp_ratio);
+  num("rope_theta", c.rope_theta);
+  num("eps", c.eps);
+  {
+    auto it = m.find("axes_dims_rope");
+    if (it != m.end() && it->second != "null") c.axes_dims_rope = parse_int_list(it->second);
+    it = m.find("guidance_embeds");
+    if (it != m.end() && it->second != "null") c.guidance_embeds = it->second == "true";
+  }
+  return c;
+}
+
+Flux2Config Flux2Config::from_c(const dcpp_flux2_config& s) {
+  Flux2Config c;
+  c.patch_size = s.patch_size;
+  c.in_channels = s.in_channels;
+  c.out_channels = s.out_channels;
+  c.num_layers = s.num_layers;
+  c.num_single_layers = s.num_single_layers;
+  c.attention_head_dim = s.attention_head_dim;
+  c.num_attention_heads = s.num_attention_heads;
+  c.joint_attention_dim = s.joint_attention_dim;
+  c.timestep_guidance_channels = s.timestep_guidance_channels;
+  c.mlp_ratio = s.mlp_ratio;
+  if (s.n_axes < 1 || s.n_axes > 8) fail(DCPP_ERR_INVALID_ARG, "n_axes must be 1..8");
+  c.axes_dims_rope.assign(s.axes_dims_rope, s.axes_dims_rope + s.n_axes);
+  c.rope_theta = s.rope_theta;
+  c.eps = s.eps;
+  c.guidance_embeds = s.guidance_embeds != 0;
+  return c;
+}
+
+void Flux2Config::to_c(dcpp_flux2_config& s) const {
+  s.patch_size = patch_size;
+  s.in_channels = in_channels;
+  s.out_channels = out_channels;
+  s.num_layers = num_layers;
+  s.num_single_layers = num_single_layers;
+  s.attention_head_dim = attention_head_dim;
+  s.num_attention_heads = num_attention_heads;
+  s.joint_attention_dim = joint_attention_dim;
+  s.timestep_guidance_channels = timestep_guidance_channels;
+  s.mlp_ratio = mlp_ratio;
+  s.n_axes = static_cast<int64_t>(std::min<size_t>(axes_dims_rope.size(), 8));
+  for (int64_t i = 0; i < s.n_axes; ++i) s.axes_dims_rope[i] = axes_dims_rope[i];
+  s.rope_theta = rope_theta;
+  s.eps = eps;
+  s.guidance_embeds = guidance_embeds ? 1 : 0;
+}
+
+void FlowMatchEulerDiscreteScheduler::schedule(int n, std::vector<float>& timesteps, std::vector<float>& sigmas) const {
+  if (n <= 0) fail(DCPP_ERR_INVALID_ARG, "num_inference_steps must be positive");
+  sigmas.resize(n);
+  for (int i = 0; i < n; ++i) sigmas[i] = static_cast<float>(1.0 - static_cast<double>(i) / n);
+  for (float& s : sigmas) s = shift * s / (1.0f + (shift - 1.0f) * s);
+  timesteps.resize(n);
+  for (int i = 0; i < n; ++i) timesteps[i] = sigmas[i] * static_cast<float>(num_train_timesteps);
+  sigmas.push_back(0.0f);
+}
+
+// ----------------------------------------------------------------- model
+Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg) : ctx_(ctx), cfg_(cfg) {
+  if (cfg_.attention_head_dim != 128) fail(DCPP_ERR_UNSUPPORTED, "attention_head_dim must be 128");
+  if (cfg_.patch_size != 1) fail(DCPP_ERR_UNSUPPORTED, "patch_size must be 1");
+  int64_t tot = 0;
+  for (auto d : cfg_.axes_dims_rope) tot += d;
+  if (tot != cfg_.attention_head_dim) fail(DCPP_ERR_INVALID_ARG, "axes_dims_rope must sum to attention_head_dim");
+  build_registry();
+}
+
+Flux2Transformer2DModel::~Flux2Transformer2DModel() {
+  cudaSetDevice(ctx_.device);
+  cudaStreamSynchronize(ctx_.stream);
+  free_plan();
+  for (auto* w : weights_)
+    if (w->data) cudaFree(w->data);
+  for (auto* v : vectors_)
+    if (v->data) cudaFree(v->data);
+}
+
+void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks) {
+  if (nranks < 1 || rank < 0 || rank >= nranks) fail(DCPP_ERR_INVALID_ARG, "bad tensor-parallel rank");
+  for (auto* w : weights_)
+    if (w->type >= 0) fail(DCPP_ERR_STATE, "set_tensor_parallel must come before set_param");
+  const int64_t H = cfg_.num_attention_heads;
+  const int64_t F = cfg_.mlp_hidden();
+  if (H % nranks) fail(DCPP_ERR_UNSUPPORTED, "num_attention_heads must divide by the TP size");
+  if ((F / nranks) % 64 || F % nranks) fail(DCPP_ERR_UNSUPPORTED, "mlp hidden / TP size must be a multiple of 64");
+  rank_ = rank;
+  nranks_ = nranks;
+  build_registry();
+}
+
+void Flux2Transformer2DModel::build_registry() {
+  weights_.clear();
+  vectors_.clear();
+  setters_.clear();
+  D_ = cfg_.inner_dim();
+  F_ = cfg_.mlp_hidden();
+  H_ = cfg_.num_attention_heads;
+  Dl_ = D_ / nranks_;
+  Fl_ = F_ / nranks_;
+  Hl_ = H_ / nranks_;
+  const int64_t D = D_, F = F_, Dl = Dl_, Fl = Fl_;
+  const int64_t tg = cfg_.timestep_guidance_channels;
+  const int r = rank_;
+
+  auto init = [&](DevWeight& w, const std::string& name, int64_t rows, int64_t cols, std::set<std::string> parts) {
+    w = DevWeight();
+    w.name = name;
+    w.rows = rows;
+    w.cols = cols;
+    w.need = std::move(parts);
+    weights_.push_back(&w);
+  };
+  auto initv = [&](DevVector& v, const std::string& name, int64_t n) {
+    v = DevVector();
+    v.name = name;
+    v.n = n;
+    vectors_.push_back(&v);
+  };
+  using RowMap = std::function<int64_t(int64_t)>;
+  using Cols = std::vector<std::array<int64_t, 3>>;
+  auto ident = [](int64_t i) { return i; };
+  // Register `name` with full shape [rows, cols] feeding part `part` of w.
+  auto reg = [&](const std::string& name, DevWeight* w, const std::string& part, int64_t rows, int64_t cols,
+                 RowMap map, Cols cols_ranges) {
+    setters_[name] = [this, w, part, rows, cols, map, cols_ranges, name](int type, const std::vector<int64_t>& shape,
+                                                                         const void* data, size_t nbytes) {
+      if (shape.size() != 2 || shape[0] != rows || shape[1] != cols)
+        fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + name + "': Parameter shape mismatch: expected " +
+                                       shape_str({rows, cols}) + ", got " + shape_str(shape));
+      if (!is_gemm_type(type)) fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + name + "': unsupported type");
+      const size_t need = row_bytes_of(type, cols) * static_cast<size_t>(rows);
+      if (nbytes != need)
+        fail(DCPP_ERR_INVALID_ARG, "Tensor '" + name + "': expected " + std::to_string(need) + " bytes, got " +
+                                       std::to_string(nbytes));
+      place_rows(*w, part, type, shape, static_cast<const uint8_t*>(data), map, cols_ranges);
+    };
+  };
+  auto full_cols = [](int64_t c) { return Cols{{0, c, 0}}; };
+  // Rows of a [D, *] head-major projection kept by this rank, placed at region g.
+  auto head_rows = [=](int g) {
+    return RowMap([=](int64_t i) { return (i >= r * Dl && i < (r + 1) * Dl) ? g * Dl + (i - r * Dl) : -1; });
+  };
+  // Rows of a [F, *] gate/up projection kept by this rank, interleaved in
+  // 64-row blocks (gate block j, up block j, ...) after `base` rows.
+  auto mlp_rows = [=](int64_t base, bool up) {
+    return RowMap([=](int64_t i) {
+      if (i < r * Fl || i >= (r + 1) * Fl) return int64_t(-1);
+      const int64_t j = i - r * Fl;
+      return base + (j / 64) * 128 + (up ? 64 : 0) + (j % 64);
+    });
+  };
+
+  init(time1_, "time_guidance_embed.timestep_embedder.linear_1.weight", D, tg, {"all"});
+  init(time2_, "time_guidance_embed.timestep_embedder.linear_2.weight", D, D, {"all"});
+  reg(time1_.name, &time1_, "all", D, tg, ident, full_cols(tg));
+  reg(time2_.name, &time2_, "all", D, D, ident, full_cols(D));
+  if (cfg_.guidance_embeds) {
+    init(guid1_, "time_guidance_embed.guidance_embedder.linear_1.weight", D, tg, {"all"});
+    init(guid2_, "time_guidance_embed.guidance_embedder.linear_2.weight", D, D, {"all"});
+    reg(guid1_.name, &guid1_, "all", D, tg, ident, full_cols(tg));
+    reg(guid2_.name, &guid2_, "all", D, D, ident, full_cols(D));
+  }
+  init(mod_img_, "double_stream_modulation_img.linear.weight", 6 * D, D, {"all"});
+  init(mod_txt_, "double_stream_modulation_txt.linear.weight", 6 * D, D, {"all"});
+  init(mod_single_, "single_stream_modulation.linear.weight", 3 * D, D, {"all"});
+  reg(mod_img_.name, &mod_img_, "all", 6 * D, D, ident, full_cols(D));
+  reg(mod_txt_.name, &mod_txt_, "all", 6 * D, D, ident, full_cols(D));
+  reg(mod_single_.name, &mod_single_, "all", 3 * D, D, ident, full_cols(D));
+  init(x_embed_, "x_embedder.weight", D, cfg_.in_channels, {"all"});
+  init(ctx_embed_, "context_embedder.weight", D, cfg_.joint_attention_dim, {"all"});
+  reg(x_embed_.name, &x_embed_, "all", D, cfg_.in_channels, ident, full_cols(cfg_.in_channels));
+  reg(ctx_embed_.name, &ctx_embed_, "all", D, cfg_.joint_attention_dim, ident, full_cols(cfg_.joint_attention_dim));
+  init(norm_out_, "norm_out.linear.weight", 2 * D, D, {"all"});
+  init(proj_out_, "proj_out.weight", cfg_.out_ch(), D, {"all"});
+  reg(norm_out_.name, &norm_out_, "all", 2 * D, D, ident, full_cols(D));
+  reg(proj_out_.name, &proj_out_, "all", cfg_.out_ch(), D, ident, full_cols(D));
+
+  dbl_.assign(static_cast<size_t>(cfg_.num_layers), DoubleBlock());
+  for (int64_t b = 0; b < cfg_.num_layers; ++b) {
+    DoubleBlock& blk = dbl_[b];
+    const std::string p = "transformer_blocks." + std::to_string(b) + ".";
+    const char* stream_qkv[2][3] = {{"attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj"},
+                                    {"attn.to_q", "attn.to_k", "attn.to_v"}};
+    const char* stream_out[2] = {"attn.to_add_out", "attn.to_out.0"};
+    const char* stream_ff[2] = {"ff_context", "ff"};
+    const char* nq[2] = {"attn.norm_added_q", "attn.norm_q"};
+    const char* nk[2] = {"attn.norm_added_k", "attn.norm_k"};
+    for (int s = 0; s < 2; ++s) {
+      init(blk.qkv[s], p + (s ? "attn.to_qkv" : "attn.add_qkv"), 3 * Dl, D, {"q", "k", "v"});
+      for (int g = 0; g < 3; ++g)
+        reg(p + stream_qkv[s][g] + ".weight", &blk.qkv[s], std::string(1, "qkv"[g]), D, D, head_rows(g), full_cols(D));
+      init(blk.out[s], p + stream_out[s] + ".weight", D, Dl, {"all"});
+      reg(p + stream_out[s] + ".weight", &blk.out[s], "all", D, D, ident, Cols{{r * Dl, Dl, 0}});
+      const std::string ff = p + stream_ff[s];
+      init(blk.ff_in[s], ff + ".linear_in.weight", 2 * Fl, D, {"gate", "up"});
+      // fused GGUF tensor [2F, D]: rows [0, F) gate, [F, 2F) up (GGUFLoaderVisitor.cpp:370-408)
+      {
+        DevWeight* w = &blk.ff_in[s];
+        auto gate = mlp_rows(0, false), up = mlp_rows(0, true);
+        const std::string fname = ff + ".linear_in.weight";
+        setters_[fname] = [this, w, gate, up, D, F, fname](int type, const std::vector<int64_t>& shape,
+                                                            const void* data, size_t nbytes) {
+          if (shape.size() != 2 || shape[0] != 2 * F || shape[1] != D)
+            fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + fname +
+                                           "': Parameter shape mismatch: expected " + shape_str({2 * F, D}) +
+                                           ", got " + shape_str(shape));
+          const size_t rb = row_bytes_of(type, D);
+          if (nbytes != rb * 2 * F) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + fname + "': byte size mismatch");
+          const uint8_t* src = static_cast<const uint8_t*>(data);
+          place_rows(*w, "gate", type, {F, D}, src, gate, Cols{{0, D, 0}});
+          place_rows(*w, "up", type, {F, D}, src + rb * F, up, Cols{{0, D, 0}});
+        };
+      }
+      reg(ff + ".linear_in_gate.weight", &blk.ff_in[s], "gate", F, D, mlp_rows(0, false), full_cols(D));
+      reg(ff + ".linear_in_up.weight", &blk.ff_in[s], "up", F, D, mlp_rows(0, true), full_cols(D));
+      init(blk.ff_out[s], ff + ".linear_out.weight", D, Fl, {"all"});
+      reg(ff + ".linear_out.weight", &blk.ff_out[s], "all", D, F, ident, Cols{{r * Fl, Fl, 0}});
+      initv(blk.norm_q[s], p + nq[s] + ".weight", cfg_.attention_head_dim);
+      initv(blk.norm_k[s], p + nk[s] + ".weight", cfg_.attention_head_dim);
+    }
+  }
+  sgl_.assign(static_cast<size_t>(cfg_.num_single_layers), SingleBlock());
+  for (int64_t b = 0; b < cfg_.num_single_layers; ++b) {
+    SingleBlock& blk = sgl_[b];
+    const std::string p = "single_transformer_blocks." + std::to_string(b) + ".attn.";
+    init(blk.qkv_mlp, p + "to_qkv_mlp_proj.weight", 3 * Dl + 2 * Fl, D, {"q", "k", "v", "gate", "up"});
+    {
+      DevWeight* w = &blk.qkv_mlp;
+      const std::string fname = p + "to_qkv_mlp_proj.weight";
+      std::array<RowMap, 3> hr = {head_rows(0), head_rows(1), head_rows(2)};
+      auto gate = mlp_rows(3 * Dl, false), up = mlp_rows(3 * Dl, true);
+      // fused GGUF tensor [3D + 2F, D]: rows q | k | v | gate | up (GGUFLoaderVisitor.cpp:283-329)
+      setters_[fname] = [this, w, hr, gate, up, D, F, fname](int type, const std::vector<int64_t>& shape,
+                                                             const void* data, size_t nbytes) {
+        if (shape.size() != 2 || shape[0] != 3 * D + 2 * F || shape[1] != D)
+          fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + fname + "': Parameter shape mismatch: expected " +
+                                         shape_str({3 * D + 2 * F, D}) + ", got " + shape_str(shape));
+        const size_t rb = row_bytes_of(type, D);
+        if (nbytes != rb * (3 * D + 2 * F)) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + fname + "': byte size mismatch");
+        const uint8_t* src = static_cast<const uint8_t*>(data);
+        for (int g = 0; g < 3; ++g) place_rows(*w, std::string(1, "qkv"[g]), type, {D, D}, src + rb * g * D, hr[g], Cols{{0, D, 0}});
+        place_rows(*w, "gate", type, {F, D}, src + rb * 3 * D, gate, Cols{{0, D, 0}});
+        place_rows(*w, "up", type, {F, D}, src + rb * (3 * D + F), up, Cols{{0, D, 0}});
+      };
+    }
+    for (int g = 0; g < 3; ++g)
+      reg(p + "to_qkv_mlp_proj." + std::string(1, "qkv"[g]) + ".weight", &blk.qkv_mlp, std::string(1, "qkv"[g]), D, D,
+          head_rows(g), full_cols(D));
+    reg(p + "to_qkv_mlp_proj.mlp_in_gate.weight", &blk.qkv_mlp, "gate", F, D, mlp_rows(3 * Dl, false), full_cols(D));
+    reg(p + "to_qkv_mlp_proj.mlp_in_up.weight", &blk.qkv_mlp, "up", F, D, mlp_rows(3 * Dl, true), full_cols(D));
+    init(blk.out, p + "to_out.weight", D, Dl + Fl, {"attn", "mlp"});
+    {
+      DevWeight* w = &blk.out;
+      const std::string fname = p + "to_out.weight";
+      // fused GGUF tensor [D, D + F]: columns attn | mlp (GGUFLoaderVisitor.cpp:331-368)
+      setters_[fname] = [this, w, D, F, Dl, Fl, r, fname](int type, const std::vector<int64_t>& shape,
+                                                          const void* data, size_t nbytes) {
+        if (shape.size() != 2 || shape[0] != D || shape[1] != D + F)
+          fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + fname + "': Parameter shape mismatch: expected " +
+                                         shape_str({D, D + F}) + ", got " + shape_str(shape));
+        if (nbytes != row_bytes_of(type, D + F) * D) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + fname + "': byte size mismatch");
+        const uint8_t* src = static_cast<const uint8_t*>(data);
+        auto id = [](int64_t i) { return i; };
+        place_rows(*w, "attn", type, shape, src, id, Cols{{r * Dl, Dl, 0}});
+        place_rows(*w, "mlp", type, shape, src, id, Cols{{D + r * Fl, Fl, Dl}});
+      };
+    }
+    reg(p + "to_out.attn.weight", &blk.out, "attn", D, D, ident, Cols{{r * Dl, Dl, 0}});
+    reg(p + "to_out.mlp.weight", &blk.out, "mlp", D, F, ident, Cols{{r * Fl, Fl, Dl}});
+    initv(blk.norm_q, p + "norm_q.weight", cfg_.attention_head_dim);
+    initv(blk.norm_k, p + "norm_k.weight", cfg_.attention_head_dim);
+  }
+  for (auto* v : vectors_) {
+    DevVector* pv = v;
+    setters_[v->name] = [this, pv](int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes) {
+      set_vector(*pv, type, shape, data, nbytes);
+    };
+  }
+}
+
+void Flux2Transformer2DModel::place_rows(DevWeight& w, const std::string& part, int type,
+                                         const std::vector<int64_t>& shape, const uint8_t* src,
+                                         const std::function<int64_t(int64_t)>& row_map,
+                                         const std::vector<std::array<int64_t, 3>>& col_ranges) {
+  if (!w.need.count(part)) fail(DCPP_ERR_STATE, "Tensor '" + w.name + "': part '" + part + "' set twice");
+  if (w.type >= 0 && w.type != type)
+    fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + w.name + "': parts of one fused weight must share a ggml type");
+  const int64_t bs = block_size_of(type);
+  const size_t bb = block_bytes_of(type);
+  if (w.cols % bs) fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + w.name + "': columns not block aligned for this type");
+  for (auto& cr : col_ranges)
+    if (cr[0] % bs || cr[1] % bs || cr[2] % bs)
+      fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + w.name + "': column shard not aligned to the quantisation block");
+  if (w.type < 0) {
+    w.type = type;
+    w.row_bytes = row_bytes_of(type, w.cols);
+    w.staging.assign(w.row_bytes * static_cast<size_t>(w.rows), 0);
+  }
+  const size_t src_rb = row_bytes_of(type, shape[1]);
+  for (int64_t i = 0; i < shape[0]; ++i) {
+    const int64_t d = row_map(i);
+    if (d < 0) continue;
+    if (d >= w.rows) fail(DCPP_ERR_STATE, "internal: row map out of range for " + w.name);
+    for (auto& cr : col_ranges) {
+      const size_t so = static_cast<size_t>(cr[0] / bs) * bb;
+      const size_t n = static_cast<size_t>(cr[1] / bs) * bb;
+      const size_t dof = static_cast<size_t>(cr[2] / bs) * bb;
+      memcpy(w.staging.data() + static_cast<size_t>(d) * w.row_bytes + dof, src + static_cast<size_t>(i) * src_rb + so, n);
+    }
+  }
+  w.need.erase(part);
+  if (w.need.empty()) finish_weight(w);
+}
+
+void Flux2Transformer2DModel::finish_weight(DevWeight& w) {
+  const size_t bytes = w.staging.size();
+  if (cudaMalloc(&w.data, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    w.data = nullptr;
+    fail(DCPP_ERR_OOM, "weight allocation failed for " + w.name);
+  }
+  cuda_check(cudaMemcpy(w.data, w.staging.data(), bytes, cudaMemcpyHostToDevice), "upload weight");
+  std::vector<uint8_t>().swap(w.staging);
+  planned_ = false;
+}
+
+void Flux2Transformer2DModel::set_vector(DevVector& v, int type, const std::vector<int64_t>& shape, const void* data,
+                                         size_t nbytes) {
+  if (shape.size() != 1 || shape[0] != v.n)
+    fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + v.name + "': Parameter shape mismatch: expected " +
+                                   shape_str({v.n}) + ", got " + shape_str(shape));
+  std::vector<float> host(static_cast<size_t>(v.n));
+  const auto* u16 = static_cast<const uint16_t*>(data);
+  if (type == kTypeF32) {
+    if (nbytes != static_cast<size_t>(v.n) * 4) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + v.name + "': byte size mismatch");
+    memcpy(host.data(), data, nbytes);
+  } else if (type == kTypeBF16 || type == kTypeF16) {
+    if (nbytes != static_cast<size_t>(v.n) * 2) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + v.name + "': byte size mismatch");
+    for (int64_t i = 0; i < v.n; ++i) {
+      if (type == kTypeBF16) {
+        uint32_t b = static_cast<uint32_t>(u16[i]) << 16;
+        memcpy(&host[i], &b, 4);
+      } else {
+        host[i] = __half2float(__ushort_as_half(u16[i]));
+      }
+    }
+  } else {
+    fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + v.name + "': norm weights must be F32, F16 or BF16");
+  }
+  if (!v.data) cuda_check(cudaMalloc(&v.data, v.n * sizeof(float)), "alloc vector");
+  cuda_check(cudaMemcpy(v.data, host.data(), v.n * sizeof(float), cudaMemcpyHostToDevice), "upload vector");
+  v.set = true;
+  planned_ = false;
+}
+
+void Flux2Transformer2DModel::set_param(const std::string& name, int type, const std::vector<int64_t>& shape,
+                                        const void* data, size_t nbytes) {
+  auto it = setters_.find(name);
+  if (it == setters_.end()) fail(DCPP_ERR_NOT_FOUND, "Error while loading Tensor '" + name + "': Tensor not found");
+  if (!data) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + name + "': null data");
+  it->second(type, shape, data, nbytes);
+}
+
+std::vector<std::string> Flux2Transformer2DModel::missing() const {
+  std::vector<std::string> m;
+  for (auto* w : weights_)
+    for (auto& p : w->need) m.push_back(w->name + (p == "all" ? "" : " [" + p + "]"));
+  for (auto* v : vectors_)
+    if (!v->set) m.push_back(v->name);
+  return m;
+}
+
+// ----------------------------------------------------------------- plan
+void Flux2Transformer2DModel::free_plan() {
+  if (graph_fwd_) cudaGraphExecDestroy(graph_fwd_);
+  for (auto& g : graph_step_)
+    if (g) cudaGraphExecDestroy(g);
+  graph_fwd_ = nullptr;
+  graph_step_[0] = graph_step_[1] = nullptr;
+  for (void* p : allocs_) cudaFree(p);
+  allocs_.clear();
+  ops_fwd_.clear();
+  step_ops_[0].clear();
+  step_ops_[1].clear();
+  planned_ = false;
+}
+
+void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph) {
+  auto miss = missing();
+  if (!miss.empty()) fail(DCPP_ERR_STATE, "parameters not set: " + miss.front() + " (+" + std::to_string(miss.size() - 1) + " more)");
+  if (batch < 1 || batch > 4) fail(DCPP_ERR_UNSUPPORTED, "batch must be 1..4");
+  if (n_img < 1 || n_txt < 1) fail(DCPP_ERR_INVALID_ARG, "token counts must be positive");
+  if ((batch * (n_img + n_txt)) > (1 << 24)) fail(DCPP_ERR_UNSUPPORTED, "too many tokens");
+  if (planned_ && batch == B_ && n_img == Ni_ && n_txt == Nt_ && use_graph == use_graph_) return;
+  cudaStreamSynchronize(ctx_.stream);
+  free_plan();
+  B_ = batch;
+  Ni_ = n_img;
+  Nt_ = n_txt;
+  S_ = n_img + n_txt;
+  use_graph_ = use_graph;
+  build_plan();
+  planned_ = true;
+}
+
+void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
+                                       const DevWeight* w0, const DevWeight* w1, std::vector<GemmGroup> groups,
+                                       const EpilogueArgs& ep, int64_t N) {
+  (void)tag;
+  if (w0->cols != K || (w1 && (w1->cols != K || w1->rows != w0->rows)) || w0->rows != N)
+    fail(DCPP_ERR_STATE, "internal: GEMM shape mismatch for " + w0->name);
+  const uint16_t* b0 = w0->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w0->data) : wscratch_[0];
+  const uint16_t* b1 = b0;
+  if (w1) b1 = w1->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w1->data) : wscratch_[1];
+  int64_t a_rows = 0;
+  for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
+  auto st = std::make_shared<std::array<CUtensorMap, 3>>();
+  cuda_check(make_tmap_bf16(&(*st)[0], a, K, a_rows, lda, kGemmBM), "tensor map A");
+  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, kGemmBN), "tensor map B0");
+  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, kGemmBN), "tensor map B1");
+  GemmArgs args{};
+  args.N = static_cast<int32_t>(N);
+  args.K = static_cast<int32_t>(K);
+  if (groups.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
+  args.n_groups = static_cast<int32_t>(groups.size());
+  for (size_t i = 0; i < groups.size(); ++i) args.groups[i] = groups[i];
+  args.ep = ep;
+  args.err = ctx_.d_err;
+  gemm_finalize_groups(args);
+  Ctx* c = &ctx_;
+  if (w0->type != kTypeBF16) {
+    const DevWeight* w = w0;
+    uint16_t* dst = wscratch_[0];
+    building_->push_back({[w, dst](cudaStream_t s) {
+                            cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
+                          },
+                          1});
+  }
+  if (w1 && w1->type != kTypeBF16) {
+    const DevWeight* w = w1;
+    uint16_t* dst = wscratch_[1];
+    building_->push_back({[w, dst](cudaStream_t s) {
+                            cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
+                          },
+                          1});
+  }
+  building_->push_back({[st, args, c](cudaStream_t s) {
+                          cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
+                        },
+                        1});
+}
+
+void Flux2Transformer2DModel::add_norm(const NormArgs& a) {
+  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1});
+}
+
+void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y) {
+  const DevWeight* pw = &w;
+  const int B = static_cast<int>(B_);
+  building_->push_back({[pw, x, act_in, act_out, y, B](cudaStream_t s) {
+                          cuda_check(launch_gemv(pw->type, pw->data, pw->rows, pw->cols, x, B, act_in, act_out, y, s),
+                                     "gemv");
+                        },
+                        1});
+}
+
+void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
+  Ctx* c = &ctx_;
+  building_->push_back({[buf, count, c](cudaStream_t s) {
+                          auto& n = Nccl::get();
+                          int r = n.AllReduce(buf, buf, static_cast<size_t>(count), 7, 0, c->comm, s);
+                          if (r != 0) fail(DCPP_ERR_NCCL, std::string("ncclAllReduce: ") + n.GetErrorString(r));
+                        },
+                        0});
+}
+
+void Flux2Transformer2DModel::build_plan() {
+  const int64_t B = B_, S = S_, Ni = Ni_, Nt = Nt_, D = D_, Dl = Dl_, Fl = Fl_, Hl = Hl_;
+  const int64_t R = B * S;
+  const int64_t ldc = Dl + Fl;
+  const int64_t in_ch = cfg_.in_channels, jd = cfg_.joint_attention_dim, out_ch = cfg_.out_ch();
+  const int64_t tg = cfg_.timestep_guidance_channels;
+  const bool tp = nranks_ > 1;
+  if (tp && !ctx_.comm) fail(DCPP_ERR_STATE, "tensor-parallel model needs dcpp_tp_init on its context");
+  auto alloc = [&](size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, std::max<size_t>(bytes, 256)) != cudaSuccess) {
+      cudaGetLastError();
+      fail(DCPP_ERR_OOM, "activation allocation of " + std::to_string(bytes) + " bytes failed");
+    }
+    allocs_.push_back(p);
+    return p;
+  };
+  h_ = static_cast<float*>(alloc(R * D * 4));
+  part_ = tp ? static_cast<float*>(alloc(R * D * 4)) : nullptr;
+  a_ = static_cast<uint16_t*>(alloc(R * D * 2));
+  q_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
+  k_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
+  v_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
+  cat_ = static_cast<uint16_t*>(alloc(R * ldc * 2));
+  xb_ = static_cast<uint16_t*>(alloc(B * Ni * in_ch * 2));
+  eb_ = static_cast<uint16_t*>(alloc(B * Nt * jd * 2));
+  lat_[0] = static_cast<float*>(alloc(B * Ni * std::max(in_ch, out_ch) * 4));
+  lat_[1] = static_cast<float*>(alloc(B * Ni * std::max(in_ch, out_ch) * 4));
+  out_dev_ = static_cast<float*>(alloc(B * Ni * out_ch * 4));
+  enc_in_ = static_cast<float*>(alloc(B * Nt * jd * 4));
+  float* scal = static_cast<float*>(alloc(64 * 4));
+  t_dev_ = scal;
+  g_dev_ = scal + 8;
+  dt_dev_ = scal + 16;
+  ids_dev_ = static_cast<int32_t*>(alloc(S * cfg_.axes_dims_rope.size() * 4));
+  rope_ = static_cast<float2*>(alloc(S * 64 * sizeof(float2)));
+  tproj_ = static_cast<float*>(alloc(B * tg * 4));
+  th_ = static_cast<float*>(alloc(B * D * 4));
+  temb_ = static_cast<float*>(alloc(B * D * 4));
+  gproj_ = static_cast<float*>(alloc(B * tg * 4));
+  gh_ = static_cast<float*>(alloc(B * D * 4));
+  gemb_ = static_cast<float*>(alloc(B * D * 4));
+  mod_img_v_ = static_cast<float*>(alloc(B * 6 * D * 4));
+  mod_txt_v_ = static_cast<float*>(alloc(B * 6 * D * 4));
+  mod_s_v_ = static_cast<float*>(alloc(B * 3 * D * 4));
+  mod_o_v_ = static_cast<float*>(alloc(B * 2 * D * 4));
+  // Weight expansion scratch (bf16) for quantised GEMM weights.
+  size_t s0 = 0, s1 = 0;
+  for (auto* w : weights_)
+    if (w->type != kTypeBF16) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
+  for (auto& blk : dbl_)
+    for (DevWeight* w : {&blk.qkv[0], &blk.out[0], &blk.ff_in[0], &blk.ff_out[0]})
+      if (w->type != kTypeBF16) s1 = std::max(s1, static_cast<size_t>(w->rows * w->cols));
+  wscratch_[0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
+  wscratch_[1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
+
+  const int n_axes = static_cast<int>(cfg_.axes_dims_rope.size());
+  std::array<int32_t, 8> axes{};
+  for (int i = 0; i < n_axes; ++i) axes[i] = static_cast<int32_t>(cfg_.axes_dims_rope[i]);
+  const float theta = static_cast<float>(cfg_.rope_theta);
+  const float eps = cfg_.eps;
+
+  // Row groups over the joint [txt | img] buffer: one per (batch, stream).
+  auto stream_groups = [&](bool both_streams) {
+    std::vector<GemmGroup> g;
+    for (int64_t b = 0; b < B; ++b) {
+      GemmGroup t{};
+      t.row0 = t.orow0 = static_cast<int32_t>(b * S);
+      t.rows = static_cast<int32_t>(Nt);
+      t.wsel = 0;
+      t.sel = 0;
+      t.batch = static_cast<int32_t>(b);
+      t.tok0 = 0;
+      GemmGroup i = t;
+      i.row0 = i.orow0 = static_cast<int32_t>(b * S + Nt);
+      i.rows = static_cast<int32_t>(Ni);
+      i.wsel = both_streams ? 1 : 0;
+      i.sel = 1;
+      i.tok0 = static_cast<int32_t>(Nt);
+      g.push_back(t);
+      g.push_back(i);
+    }
+    return g;
+  };
+  auto norm_args = [&](const float* const* mods, int64_t mod_stride, int64_t shift_off, int64_t scale_off,
+                       bool img_only, uint16_t* y, int64_t dst_ld, const float* resid) {
+    NormArgs n{};
+    n.x = h_;
+    n.x_out = h_;
+    n.resid = resid;
+    n.y = y;
+    n.ld_x = D;
+    n.ld_y = dst_ld;
+    n.D = static_cast<int32_t>(D);
+    n.eps = eps;
+    int k = 0;
+    for (int64_t b = 0; b < B; ++b) {
+      if (!img_only) {
+        const float* m = mods[0] + b * mod_stride;
+        n.seg[k++] = {static_cast<int32_t>(b * S), static_cast<int32_t>(b * S), static_cast<int32_t>(Nt), m + shift_off,
+                      m + scale_off};
+      }
+      const float* m = mods[1] + b * mod_stride;
+      const int32_t dst = img_only ? static_cast<int32_t>(b * Ni) : static_cast<int32_t>(b * S + Nt);
+      n.seg[k++] = {static_cast<int32_t>(b * S + Nt), dst, static_cast<int32_t>(Ni), m + shift_off, m + scale_off};
+    }
+    n.n_segments = k;
+    return n;
+  };
+
+  auto build_ops = [&](std::vector<Op>& ops, float* lat_in, float* lat_out, bool euler) {
+    building_ = &ops;
+    // 1. timestep (and guidance) embedding, modulation vectors
+    //    (Flux2Transformer2DModel.cpp:199-214).
+    ops.push_back({[=](cudaStream_t s) {
+                     cuda_check(launch_timestep_proj(t_dev_, static_cast<int>(B), static_cast<int>(tg), 1000.0f, tproj_, s),
+                                "timestep_proj");
+                   },
+                   1});
+    add_gemv(time1_, tproj_, 0, 1, th_);
+    add_gemv(time2_, th_, 0, 0, temb_);
+    if (guidance_given_) {
+      ops.push_back({[=](cudaStream_t s) {
+                       cuda_check(launch_timestep_proj(g_dev_, static_cast<int>(B), static_cast<int>(tg), 1000.0f, gproj_, s),
+                                  "guidance_proj");
+                     },
+                     1});
+      add_gemv(guid1_, gproj_, 0, 1, gh_);
+      add_gemv(guid2_, gh_, 0, 0, gemb_);
+      ops.push_back({[=](cudaStream_t s) { cuda_check(launch_add_f32(temb_, gemb_, B * D, s), "add"); }, 1});
+    }
+    add_gemv(mod_img_, temb_, 1, 0, mod_img_v_);
+    add_gemv(mod_txt_, temb_, 1, 0, mod_txt_v_);
+    add_gemv(mod_single_, temb_, 1, 0, mod_s_v_);
+    add_gemv(norm_out_, temb_, 1, 0, mod_o_v_);
+    // 2. input projections into the joint residual stream h = [txt | img].
+    ops.push_back({[=](cudaStream_t s) {
+                     cuda_check(launch_f32_to_bf16(lat_in, B * Ni * in_ch, xb_, s), "to_bf16");
+                     cuda_check(launch_f32_to_bf16(enc_in_, B * Nt * jd, eb_, s), "to_bf16");
+                   },
+                   2});
+    {
+      std::vector<GemmGroup> gi, gt;
+      for (int64_t b = 0; b < B; ++b) {
+        GemmGroup g{};
+        g.row0 = static_cast<int32_t>(b * Ni);
+        g.orow0 = static_cast<int32_t>(b * S + Nt);
+        g.rows = static_cast<int32_t>(Ni);
+        g.batch = static_cast<int32_t>(b);
+        gi.push_back(g);
+        g.row0 = static_cast<int32_t>(b * Nt);
+        g.orow0 = static_cast<int32_t>(b * S);
+        g.rows = static_cast<int32_t>(Nt);
+        gt.push_back(g);
+      }
+      EpilogueArgs e{};
+      e.mode = kEpiF32;
+      e.out_f32 = h_;
+      e.ld_out = D;
+      add_gemm("x_embedder", xb_, in_ch, in_ch, &x_embed_, nullptr, gi, e, D);
+      add_gemm("context_embedder", eb_, jd, jd, &ctx_embed_, nullptr, gt, e, D);
+    }
+    // 3. rotary table from cat(txt_ids, img_ids) (Flux2Transformer2DModel.cpp:233-238).
+    ops.push_back({[=](cudaStream_t s) {
+                     cuda_check(launch_rope_table(ids_dev_, S, n_axes, axes.data(), theta, rope_, s), "rope_table");
+                   },
+                   1});
+    const float* resid = nullptr;  // pending all-reduced partial (TP)
+    AttnArgs at{};
+    at.q = q_;
+    at.k = k_;
+    at.v = v_;
+    at.o = cat_;
+    at.ld_o = ldc;
+    at.B = static_cast<int32_t>(B);
+    at.H = static_cast<int32_t>(Hl);
+    at.S = static_cast<int32_t>(S);
+    at.scale = 1.0f / std::sqrt(static_cast<float>(cfg_.attention_head_dim));
+    auto attn_op = [&]() {
+      ops.push_back({[at](cudaStream_t s) { cuda_check(launch_attention(at, s), "attention"); }, 1});
+    };
+    auto out_epi = [&](const float* g0, const float* g1, int64_t bstride) {
+      EpilogueArgs e{};
+      e.mode = tp ? kEpiGateF32 : kEpiResidGate;
+      e.out_f32 = tp ? part_ : h_;
+      e.ld_out = D;
+      e.gate[0] = g0;
+      e.gate[1] = g1;
+      e.gate_bstride = bstride;
+      return e;
+    };
+    const float* mods_dbl[2] = {mod_txt_v_, mod_img_v_};
+    // 4. double-stream blocks (Flux2TransformerBlock.hpp:45-117).
+    for (auto& blk : dbl_) {
+      add_norm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, resid));
+      resid = nullptr;
+      EpilogueArgs e{};
+      e.mode = kEpiQkvMlp;
+      e.qkv_cols = static_cast<int32_t>(3 * Dl);
+      e.inner = static_cast<int32_t>(Dl);
+      e.seq = static_cast<int32_t>(S);
+      e.heads = static_cast<int32_t>(Hl);
+      e.norm_q[0] = blk.norm_q[0].data;
+      e.norm_q[1] = blk.norm_q[1].data;
+      e.norm_k[0] = blk.norm_k[0].data;
+      e.norm_k[1] = blk.norm_k[1].data;
+      e.eps = eps;
+      e.rope = rope_;
+      e.q_out = q_;
+      e.k_out = k_;
+      e.v_out = v_;
+      e.mlp_out = cat_ + Dl;
+      e.ld_mlp = ldc;
+      add_gemm("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], stream_groups(true), e, 3 * Dl);
+      attn_op();
+      add_gemm("attn_out", cat_, ldc, Dl, &blk.out[0], &blk.out[1], stream_groups(true),
+               out_epi(mod_txt_v_ + 2 * D, mod_img_v_ + 2 * D, 6 * D), D);
+      if (tp) { add_allreduce(part_, R * D); resid = part_; }
+      add_norm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, resid));
+      resid = nullptr;
+      EpilogueArgs f = e;
+      f.qkv_cols = 0;
+      add_gemm("ff_in", a_, D, D, &blk.ff_in[0], &blk.ff_in[1], stream_groups(true), f, 2 * Fl);
+      add_gemm("ff_out", cat_ + Dl, ldc, Fl, &blk.ff_out[0], &blk.ff_out[1], stream_groups(true),
+               out_epi(mod_txt_v_ + 5 * D, mod_img_v_ + 5 * D, 6 * D), D);
+      if (tp) { add_allreduce(part_, R * D); resid = part_; }
+    }
+    // 5. single-stream blocks on the joint stream (Flux2SingleTransformerBlock.hpp:36-72).
+    const float* mods_s[2] = {mod_s_v_, mod_s_v_};
+    for (auto& blk : sgl_) {
+      add_norm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, resid));
+      resid = nullptr;
+      EpilogueArgs e{};
+      e.mode = kEpiQkvMlp;
+      e.qkv_cols = static_cast<int32_t>(3 * Dl);
+      e.inner = static_cast<int32_t>(Dl);
+      e.seq = static_cast<int32_t>(S);
+      e.heads = static_cast<int32_t>(Hl);
+      e.norm_q[0] = e.norm_q[1] = blk.norm_q.data;
+      e.norm_k[0] = e.norm_k[1] = blk.norm_k.data;
+      e.eps = eps;
+      e.rope = rope_;
+      e.q_out = q_;
+      e.k_out = k_;
+      e.v_out = v_;
+      e.mlp_out = cat_ + Dl;
+      e.ld_mlp = ldc;
+      add_gemm("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, stream_groups(false), e, 3 * Dl + 2 * Fl);
+      attn_op();
+      add_gemm("out", cat_, ldc, Dl + Fl, &blk.out, nullptr, stream_groups(false),
+               out_epi(mod_s_v_ + 2 * D, mod_s_v_ + 2 * D, 3 * D), D);
+      if (tp) { add_allreduce(part_, R * D); resid = part_; }
+    }
+    // 6. drop text tokens, norm_out (scale first, then shift; AdaLayerNormContinuous.inl:26-43), proj_out.
+    const float* mods_o[2] = {mod_o_v_, mod_o_v_};
+    add_norm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, resid));
+    {
+      std::vector<GemmGroup> g;
+      for (int64_t b = 0; b < B; ++b) {
+        GemmGroup gg{};
+        gg.row0 = gg.orow0 = static_cast<int32_t>(b * Ni);
+        gg.rows = static_cast<int32_t>(Ni);
+        gg.batch = static_cast<int32_t>(b);
+        g.push_back(gg);
+      }
+      EpilogueArgs e{};
+      e.ld_out = out_ch;
+      if (euler) {
+        e.mode = kEpiEuler;
+        e.out_f32 = lat_out;
+        e.x_in = lat_in;
+        e.dt = dt_dev_;
+      } else {
+        e.mode = kEpiF32;
+        e.out_f32 = lat_out;
+      }
+      add_gemm("proj_out", a_, D, D, &proj_out_, nullptr, g, e, out_ch);
+    }
+    building_ = nullptr;
+  };
+  guidance_given_ = cfg_.guidance_embeds;
+  build_ops(ops_fwd_, lat_[0], out_dev_, false);
+  // The Euler step needs noise prediction and latents of the same shape.
+  if (cfg_.out_ch() == cfg_.in_channels) {
+    build_ops(step_ops_[0], lat_[0], lat_[1], true);
+    build_ops(step_ops_[1], lat_[1], lat_[0], true);
+  }
+  launches_per_step_ = 0;
+  for (auto& o : (step_ops_[0].empty() ? ops_fwd_ : step_ops_[0])) launches_per_step_ += o.launches;
+}
+
+}  // namespace dcpp
+
+namespace dcpp {
+
+// ----------------------------------------------------------------- execution
+void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph) {
+  cudaStream_t s = ctx_.stream;
+  if (!use_graph_) {
+    for (auto& o : ops) o.fn(s);
+    return;
+  }
+  if (!*graph) {
+    cudaGraph_t g = nullptr;
+    cuda_check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      for (auto& o : ops) o.fn(s);
+    } catch (...) {
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cuda_check(cudaStreamEndCapture(s, &g), "end capture");
+    cudaError_t e = cudaGraphInstantiate(graph, g, 0);
+    cudaGraphDestroy(g);
+    cuda_check(e, "graph instantiate");
+  }
+  cuda_check(cudaGraphLaunch(*graph, s), "graph launch");
+}
+
+void Flux2Transformer2DModel::copy_inputs(const float* hidden, const float* encoder, const float* timestep,
+                                          const int32_t* img_ids, const int32_t* txt_ids, const float* guidance) {
+  cudaStream_t s = ctx_.stream;
+  const size_t na = cfg_.axes_dims_rope.size();
+  if (hidden)
+    cuda_check(cudaMemcpyAsync(lat_[cur_], hidden, B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, s), "copy hidden");
+  if (encoder)
+    cuda_check(cudaMemcpyAsync(enc_in_, encoder, B_ * Nt_ * cfg_.joint_attention_dim * 4, cudaMemcpyDefault, s),
+               "copy encoder");
+  if (timestep) cuda_check(cudaMemcpyAsync(t_dev_, timestep, B_ * 4, cudaMemcpyDefault, s), "copy timestep");
+  if (guidance) cuda_check(cudaMemcpyAsync(g_dev_, guidance, B_ * 4, cudaMemcpyDefault, s), "copy guidance");
+  if (txt_ids) cuda_check(cudaMemcpyAsync(ids_dev_, txt_ids, Nt_ * na * 4, cudaMemcpyDefault, s), "copy txt_ids");
+  if (img_ids)
+    cuda_check(cudaMemcpyAsync(ids_dev_ + Nt_ * na, img_ids, Ni_ * na * 4, cudaMemcpyDefault, s), "copy img_ids");
+}
+
+void Flux2Transformer2DModel::forward(const float* hidden, const float* encoder, const float* timestep,
+                                      const int32_t* img_ids, const int32_t* txt_ids, const float* guidance,
+                                      float* out) {
+  if (!planned_) fail(DCPP_ERR_STATE, "forward before prepare");
+  if (!hidden || !encoder || !timestep || !img_ids || !txt_ids || !out) fail(DCPP_ERR_INVALID_ARG, "forward: null input");
+  if (cfg_.guidance_embeds && !guidance) fail(DCPP_ERR_INVALID_ARG, "forward: guidance required (guidance_embeds)");
+  cur_ = 0;
+  copy_inputs(hidden, encoder, timestep, img_ids, txt_ids, guidance);
+  run_ops(ops_fwd_, &graph_fwd_);
+  cuda_check(cudaMemcpyAsync(out, out_dev_, B_ * Ni_ * cfg_.out_ch() * 4, cudaMemcpyDefault, ctx_.stream), "copy out");
+  ctx_.check_device_error();
+}
+
+void Flux2Transformer2DModel::denoise(const float* latents, const float* encoder, const float* timestep, float dt,
+                                      const int32_t* img_ids, const int32_t* txt_ids, float* latents_out) {
+  if (!planned_) fail(DCPP_ERR_STATE, "denoise before prepare");
+  if (step_ops_[0].empty()) fail(DCPP_ERR_UNSUPPORTED, "denoise needs out_channels == in_channels");
+  if (cfg_.guidance_embeds) fail(DCPP_ERR_UNSUPPORTED, "denoise passes no guidance (Flux2KleinPipeline.cpp:527)");
+  if (!latents || !encoder || !timestep || !img_ids || !txt_ids || !latents_out)
+    fail(DCPP_ERR_INVALID_ARG, "denoise: null input");
+  cur_ = 0;
+  copy_inputs(latents, encoder, timestep, img_ids, txt_ids, nullptr);
+  cuda_check(cudaMemcpyAsync(dt_dev_, &dt, 4, cudaMemcpyHostToDevice, ctx_.stream), "copy dt");
+  run_ops(step_ops_[0], &graph_step_[0]);
+  cuda_check(cudaMemcpyAsync(latents_out, lat_[1], B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, ctx_.stream),
+             "copy latents");
+  ctx_.check_device_error();
+}
+
+void Flux2Transformer2DModel::load_inputs(const float* latents, const float* encoder, const int32_t* img_ids,
+                                          const int32_t* txt_ids) {
+  if (!planned_) fail(DCPP_ERR_STATE, "load_inputs before prepare");
+  cur_ = 0;
+  copy_inputs(latents, encoder, nullptr, img_ids, txt_ids, nullptr);
+}
+
+void Flux2Transformer2DModel::set_timestep(float timestep, float dt) {
+  if (!planned_) fail(DCPP_ERR_STATE, "set_timestep before prepare");
+  float host[8];
+  for (int64_t b = 0; b < B_; ++b) host[b] = timestep;
+  cuda_check(cudaMemcpyAsync(t_dev_, host, B_ * 4, cudaMemcpyHostToDevice, ctx_.stream), "copy timestep");
+  cuda_check(cudaMemcpyAsync(dt_dev_, &dt, 4, cudaMemcpyHostToDevice, ctx_.stream), "copy dt");
+}
+
+void Flux2Transformer2DModel::run_resident_step() {
+  if (!planned_) fail(DCPP_ERR_STATE, "run before prepare");
+  if (step_ops_[0].empty()) fail(DCPP_ERR_UNSUPPORTED, "denoise needs out_channels == in_channels");
+  run_ops(step_ops_[cur_], &graph_step_[cur_]);
+  cur_ ^= 1;
+}
+
+void Flux2Transformer2DModel::read_latents(float* out) {
+  cuda_check(cudaMemcpyAsync(out, lat_[cur_], B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, ctx_.stream),
+             "copy latents");
+  ctx_.check_device_error();
+}
+
+}  // namespace dcpp
+
+// ----------------------------------------------------------------- C ABI
+namespace {
+
+template <class F>
+dcpp_status model_call(dcpp_flux2* m, const char* entry, F&& f) {
+  if (!m || !m->ctx) return DCPP_ERR_INVALID_ARG;
+  dcpp_ctx* ctx = m->ctx;
+  try {
+    ctx->maybe_inject(entry);
+    cudaSetDevice(ctx->device);
+    f(*m->model);
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    ctx->last_error = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    ctx->last_error = e.what();
+    return DCPP_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void dcpp_flux2_config_default(dcpp_flux2_config* cfg) {
+  if (cfg) dcpp::Flux2Config().to_c(*cfg);
+}
+
+dcpp_status dcpp_flux2_config_from_file(const char* path, dcpp_flux2_config* cfg) {
+  if (!path || !cfg) return DCPP_ERR_INVALID_ARG;
+  try {
+    dcpp::Flux2Config::from_file(path).to_c(*cfg);
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    return e.status;
+  } catch (const std::exception&) {
+    return DCPP_ERR_INVALID_ARG;
+  }
+}
+
+dcpp_status dcpp_flux2_create(dcpp_ctx* ctx, const dcpp_flux2_config* cfg, dcpp_flux2** out) {
+  if (!ctx || !cfg || !out) return DCPP_ERR_INVALID_ARG;
+  *out = nullptr;
+  try {
+    ctx->maybe_inject("dcpp_flux2_create");
+    cudaSetDevice(ctx->device);
+    auto* m = new dcpp_flux2();
+    m->ctx = ctx;
+    try {
+      m->model.reset(new dcpp::Flux2Transformer2DModel(*ctx, dcpp::Flux2Config::from_c(*cfg)));
+    } catch (...) {
+      delete m;
+      throw;
+    }
+    *out = m;
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    ctx->last_error = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    ctx->last_error = e.what();
+    return DCPP_ERR_INVALID_ARG;
+  }
+}
+
+dcpp_status dcpp_flux2_destroy(dcpp_flux2* m) {
+  if (!m) return DCPP_ERR_INVALID_ARG;
+  if (m->ctx) cudaSetDevice(m->ctx->device);
+  delete m;
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_flux2_set_param(dcpp_flux2* m, const char* name, int type, int n_dims, const int64_t* shape,
+                                 const void* data, size_t nbytes) {
+  return model_call(m, "dcpp_flux2_set_param", [&](dcpp::Flux2Transformer2DModel& mm) {
+    if (!name || !shape || n_dims < 1 || n_dims > 4) dcpp::fail(DCPP_ERR_INVALID_ARG, "set_param: bad name or shape");
+    mm.set_param(name, type, std::vector<int64_t>(shape, shape + n_dims), data, nbytes);
+  });
+}
+
+dcpp_status dcpp_flux2_missing(dcpp_flux2* m, int* count, char* first, size_t cap) {
+  return model_call(m, "dcpp_flux2_missing", [&](dcpp::Flux2Transformer2DModel& mm) {
+    auto miss = mm.missing();
+    if (count) *count = static_cast<int>(miss.size());
+    if (first && cap) {
+      std::string f = miss.empty() ? "" : miss.front();
+      size_t n = std::min(cap - 1, f.size());
+      memcpy(first, f.data(), n);
+      first[n] = 0;
+    }
+  });
+}
+
+dcpp_status dcpp_flux2_prepare(dcpp_flux2* m, int64_t batch, int64_t n_img, int64_t n_txt, int use_graph) {
+  return model_call(m, "dcpp_flux2_prepare",
+                    [&](dcpp::Flux2Transformer2DModel& mm) { mm.prepare(batch, n_img, n_txt, use_graph != 0); });
+}
+
+dcpp_status dcpp_flux2_forward(dcpp_flux2* m, const float* hidden, const float* encoder, const float* timestep,
+                               const int32_t* img_ids, const int32_t* txt_ids, const float* guidance, float* out) {
+  return model_call(m, "dcpp_flux2_forward", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.forward(hidden, encoder, timestep, img_ids, txt_ids, guidance, out);
+  });
+}
+
+dcpp_status dcpp_flux2_denoise_step(dcpp_flux2* m, const float* latents_in, const float* encoder,
+                                    const float* timestep, float dt, const int32_t* img_ids, const int32_t* txt_ids,
+                                    float* latents_out) {
+  return model_call(m, "dcpp_flux2_denoise_step", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.denoise(latents_in, encoder, timestep, dt, img_ids, txt_ids, latents_out);
+  });
+}
+
+dcpp_status dcpp_flux2_load_inputs(dcpp_flux2* m, const float* latents, const float* encoder, const int32_t* img_ids,
+                                   const int32_t* txt_ids) {
+  return model_call(m, "dcpp_flux2_load_inputs", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.load_inputs(latents, encoder, img_ids, txt_ids);
+  });
+}
+
+dcpp_status dcpp_flux2_set_timestep(dcpp_flux2* m, float timestep, float dt) {
+  return model_call(m, "dcpp_flux2_set_timestep",
+                    [&](dcpp::Flux2Transformer2DModel& mm) { mm.set_timestep(timestep, dt); });
+}
+
+dcpp_status dcpp_flux2_run_resident(dcpp_flux2* m) {
+  return model_call(m, "dcpp_flux2_run_resident", [&](dcpp::Flux2Transformer2DModel& mm) { mm.run_resident_step(); });
+}
+
+dcpp_status dcpp_flux2_read_latents(dcpp_flux2* m, float* out) {
+  return model_call(m, "dcpp_flux2_read_latents", [&](dcpp::Flux2Transformer2DModel& mm) { mm.read_latents(out); });
+}
+
+dcpp_status dcpp_flux2_launches_per_step(dcpp_flux2* m, int64_t* out) {
+  return model_call(m, "dcpp_flux2_launches_per_step", [&](dcpp::Flux2Transformer2DModel& mm) {
+    if (!out) dcpp::fail(DCPP_ERR_INVALID_ARG, "null output");
+    *out = mm.launches_per_step();
+  });
+}
+
+dcpp_status dcpp_flux2_set_tensor_parallel(dcpp_flux2* m, int rank, int nranks) {
+  return model_call(m, "dcpp_flux2_set_tensor_parallel",
+                    [&](dcpp::Flux2Transformer2DModel& mm) { mm.set_tensor_parallel(rank, nranks); });
+}
+
+dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float* sigmas) {
+  if (n <= 0 || !timesteps || !sigmas) return DCPP_ERR_INVALID_ARG;
+  try {
+    dcpp::FlowMatchEulerDiscreteScheduler sch;
+    sch.shift = shift;
+    std::vector<float> t, s;
+    sch.schedule(n, t, s);
+    memcpy(timesteps, t.data(), n * sizeof(float));
+    memcpy(sigmas, s.data(), (n + 1) * sizeof(float));
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    return e.status;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,189 @@
+// C++ host API of the Flux2 DiT denoise step.  Mirrors the reference's
+// module and pipeline surface:
+//   Flux2Transformer2DModel::Config / from_file  (Flux2Transformer2DModel.hpp:10-31, .cpp:322-353)
+//   Flux2Transformer2DModel::forward             (Flux2Transformer2DModel.cpp:180-300)
+//   Flux2KleinPipeline::denoise                  (Flux2KleinPipeline.cpp:496-537)
+//   FlowMatchEulerDiscreteScheduler::schedule / integrate (FlowMatchEulerDiscreteScheduler.cpp:68-222)
+// Parameters bind by their GGUF names (module paths, ModulePath.hpp) as the
+// GGUFLoaderVisitor does, including the fused tensors it byte-slices.
+// Execution is eager CUDA on one stream, optionally replayed from a CUDA
+// graph; every kernel comes from this library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <functional>
+#include <map>
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "runtime.hpp"
+
+namespace dcpp {
+
+struct Flux2Config {
+  int64_t patch_size = 1;
+  int64_t in_channels = 128;
+  int64_t out_channels = -1;  // <= 0: in_channels
+  int64_t num_layers = 8;
+  int64_t num_single_layers = 48;
+  int64_t attention_head_dim = 128;
+  int64_t num_attention_heads = 48;
+  int64_t joint_attention_dim = 15360;
+  int64_t timestep_guidance_channels = 256;
+  float mlp_ratio = 3.0f;
+  std::vector<int64_t> axes_dims_rope = {32, 32, 32, 32};
+  int64_t rope_theta = 2000;
+  float eps = 1e-6f;
+  bool guidance_embeds = true;
+
+  static Flux2Config from_file(const std::string& path);
+  static Flux2Config from_c(const dcpp_flux2_config& c);
+  void to_c(dcpp_flux2_config& c) const;
+  int64_t inner_dim() const { return num_attention_heads * attention_head_dim; }
+  int64_t mlp_hidden() const { return static_cast<int64_t>(inner_dim() * mlp_ratio); }
+  int64_t out_ch() const { return patch_size * patch_size * (out_channels > 0 ? out_channels : in_channels); }
+};
+
+// A weight matrix [rows, cols] of one ggml type, as raw GGUF rows on the
+// device, assembled from one or more named parts.
+struct DevWeight {
+  std::string name;
+  int type = -1;
+  int64_t rows = 0;
+  int64_t cols = 0;
+  size_t row_bytes = 0;
+  uint8_t* data = nullptr;             // device
+  std::vector<uint8_t> staging;        // host, until all parts arrived
+  std::set<std::string> need;          // part names still missing
+  bool ready() const { return data != nullptr && need.empty(); }
+};
+
+// An f32 vector parameter (RMSNorm weights).
+struct DevVector {
+  std::string name;
+  int64_t n = 0;
+  float* data = nullptr;
+  bool set = false;
+};
+
+class Flux2Transformer2DModel {
+ public:
+  Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg);
+  ~Flux2Transformer2DModel();
+
+  const Flux2Config& config() const { return cfg_; }
+  void set_tensor_parallel(int rank, int nranks);
+  void set_param(const std::string& name, int type, const std::vector<int64_t>& shape, const void* data,
+                 size_t nbytes);
+  std::vector<std::string> missing() const;
+
+  // Plan buffers / tensor maps / graph for B x (n_img + n_txt) tokens.
+  void prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph);
+
+  // forward(): output = noise prediction.  denoise(): output = latents + dt * v.
+  void forward(const float* hidden, const float* encoder, const float* timestep, const int32_t* img_ids,
+               const int32_t* txt_ids, const float* guidance, float* out);
+  void denoise(const float* latents, const float* encoder, const float* timestep, float dt,
+               const int32_t* img_ids, const int32_t* txt_ids, float* latents_out);
+
+  // Resident execution (inputs already in the model's device buffers):
+  // load the inputs once, then run steps; each run integrates the latent
+  // in place (ping-pong) so repeated runs follow a schedule.
+  void load_inputs(const float* latents, const float* encoder, const int32_t* img_ids, const int32_t* txt_ids);
+  void set_timestep(float timestep, float dt);
+  void run_resident_step();
+  void read_latents(float* out);
+  int64_t launches_per_step() const { return launches_per_step_; }
+
+ private:
+  struct DoubleBlock {
+    DevWeight qkv[2], out[2], ff_in[2], ff_out[2];  // [0] txt stream, [1] img stream
+    DevVector norm_q[2], norm_k[2];
+  };
+  struct SingleBlock {
+    DevWeight qkv_mlp, out;
+    DevVector norm_q, norm_k;
+  };
+  struct Op {
+    std::function<void(cudaStream_t)> fn;
+    int launches;
+  };
+
+  void build_registry();
+  void place_rows(DevWeight& w, const std::string& part, int type, const std::vector<int64_t>& shape,
+                  const uint8_t* src, const std::function<int64_t(int64_t)>& row_map,
+                  const std::vector<std::array<int64_t, 3>>& col_ranges);
+  void finish_weight(DevWeight& w);
+  void set_vector(DevVector& v, int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes);
+  void free_plan();
+  void build_plan();
+  void run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph);
+  void copy_inputs(const float* hidden, const float* encoder, const float* timestep, const int32_t* img_ids,
+                   const int32_t* txt_ids, const float* guidance);
+
+  // Plan helpers.
+  void add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K, const DevWeight* w0,
+                const DevWeight* w1, std::vector<GemmGroup> groups, const EpilogueArgs& ep, int64_t N);
+  void add_norm(const NormArgs& a);
+  void add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y);
+  void add_allreduce(float* buf, int64_t count);
+
+  Ctx& ctx_;
+  Flux2Config cfg_;
+  int rank_ = 0, nranks_ = 1;
+  int64_t D_ = 0, F_ = 0, H_ = 0, Dl_ = 0, Fl_ = 0, Hl_ = 0;
+
+  // Parameters.
+  DevWeight time1_, time2_, guid1_, guid2_, mod_img_, mod_txt_, mod_single_, x_embed_, ctx_embed_, norm_out_,
+      proj_out_;
+  std::vector<DoubleBlock> dbl_;
+  std::vector<SingleBlock> sgl_;
+  // name -> setter
+  std::map<std::string, std::function<void(int, const std::vector<int64_t>&, const void*, size_t)>> setters_;
+  std::vector<DevWeight*> weights_;
+  std::vector<DevVector*> vectors_;
+
+  // Plan state.
+  int64_t B_ = 0, Ni_ = 0, Nt_ = 0, S_ = 0;
+  bool use_graph_ = false;
+  bool planned_ = false;
+  bool guidance_given_ = false;
+  std::vector<void*> allocs_;
+  float *h_ = nullptr, *part_ = nullptr, *lat_[2] = {nullptr, nullptr}, *enc_in_ = nullptr, *t_dev_ = nullptr,
+        *g_dev_ = nullptr, *dt_dev_ = nullptr, *out_dev_ = nullptr;
+  float *tproj_ = nullptr, *th_ = nullptr, *temb_ = nullptr, *gproj_ = nullptr, *gh_ = nullptr, *gemb_ = nullptr;
+  float *mod_img_v_ = nullptr, *mod_txt_v_ = nullptr, *mod_s_v_ = nullptr, *mod_o_v_ = nullptr;
+  uint16_t *a_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *cat_ = nullptr, *xb_ = nullptr,
+           *eb_ = nullptr, *wscratch_[2] = {nullptr, nullptr};
+  int32_t* ids_dev_ = nullptr;
+  float2* rope_ = nullptr;
+  float* host_scalars_ = nullptr;  // pinned: t[B], dt
+  int cur_ = 0;                    // latent ping-pong index
+  std::vector<Op> ops_fwd_;        // forward (noise prediction) plan
+  std::vector<Op> step_ops_[2];    // denoise step plans (Euler fused), per latent parity
+  std::vector<Op>* building_ = nullptr;
+  cudaGraphExec_t graph_fwd_ = nullptr, graph_step_[2] = {nullptr, nullptr};
+  int64_t launches_per_step_ = 0;
+};
+
+// FlowMatchEulerDiscreteScheduler (default: shift 1, no dynamic shifting,
+// no terminal stretch, not inverted) with the pipeline's sigmas 1 - i/n.
+struct FlowMatchEulerDiscreteScheduler {
+  float shift = 1.0f;
+  int num_train_timesteps = 1000;
+  void schedule(int n, std::vector<float>& timesteps, std::vector<float>& sigmas) const;
+};
+
+}  // namespace dcpp
+
+struct dcpp_flux2 {
+  std::unique_ptr<dcpp::Flux2Transformer2DModel> model;
+  dcpp_ctx* ctx = nullptr;
+};

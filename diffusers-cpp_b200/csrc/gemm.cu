@@ -1,0 +1,430 @@
+// Grouped, persistent tcgen05 GEMM for sm_100a.
+//
+//   Y[rows, N] = X[rows, K] (bf16) . W_g[N, K]^T (bf16)   f32 accumulate in TMEM
+//
+// This is the ggml_mul_mat of every Linear on the Flux2 hot path
+// (src/nn/Linear.cpp:17-36).  Rows are split into groups that use
+// different weights: the double-stream block runs its text-stream
+// projections (add_q/k/v, to_add_out, ff_context) and image-stream
+// projections (to_q/k/v, to_out, ff) in one launch over the joint
+// [txt | img] token buffer (Flux2Attention.hpp:76-89, Flux2TransformerBlock.hpp).
+//
+// Warp roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer: A tile 128x64 and B tile 256x64 per stage
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> global
+// Two 128x256 f32 accumulators (512 TMEM columns) let the epilogue of
+// tile i overlap the main loop of tile i+1.
+#include "common.cuh"
+#include "gemm.cuh"
+
+#include <algorithm>
+
+namespace dcpp {
+
+namespace {
+
+constexpr int kAStageBytes = kGemmBM * kGemmBK * 2;  // 16 KB
+constexpr int kBStageBytes = kGemmBN * kGemmBK * 2;  // 32 KB
+constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 512;
+// smem: stages + barriers + tmem slot, plus 1 KB for 1024-byte alignment.
+constexpr int kGemmSmemBytes = kGemmStages * kStageBytes + 1024 + 256;
+
+struct TileCoord {
+  int g;       // group
+  int m_tile;  // within group
+  int n_tile;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmArgs& p, int t) {
+  int g = 0;
+#pragma unroll 1
+  for (int i = 1; i < p.n_groups; ++i)
+    if (t >= p.groups[i].tile0) g = i;
+  const GemmGroup& G = p.groups[g];
+  int local = t - G.tile0;
+  TileCoord c;
+  c.g = g;
+  c.n_tile = local / G.m_tiles;
+  c.m_tile = local - c.n_tile * G.m_tiles;
+  return c;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// ------------------------------------------------------------------ epilogue
+// One thread = one row of the tile; `taddr` addresses this warp's 32 TMEM
+// lanes at the accumulator's column 0.
+__device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_in_tile,
+                                             uint32_t taddr) {
+  const GemmGroup& G = p.groups[tc.g];
+  const EpilogueArgs& e = p.ep;
+  const int local_row = tc.m_tile * kGemmBM + row_in_tile;
+  const bool row_ok = local_row < G.rows;
+  const int64_t row = static_cast<int64_t>(G.orow0) + local_row;
+  const int col0 = tc.n_tile * kGemmBN;
+  const int sel = G.sel;
+
+  if (e.mode == kEpiQkvMlp) {
+    const int tok = G.tok0 + local_row;
+    // Two 128-column halves; each is one head of q, k or v, or 64 SwiGLU
+    // outputs (gate/up interleaved in 64-column blocks by the loader).
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = col0 + half * 128;
+      if (c0 >= p.N) break;
+      const uint32_t hbase = taddr + half * 128;
+      if (c0 < e.qkv_cols) {
+        const int region = c0 / e.inner;  // 0 q, 1 k, 2 v
+        const int head = (c0 - region * e.inner) >> 7;
+        uint16_t* dst_base = region == 0 ? e.q_out : (region == 1 ? e.k_out : e.v_out);
+        const int64_t dst_row =
+            ((static_cast<int64_t>(G.batch) * e.heads + head) * e.seq + tok) * 128;
+        if (region == 2) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(hbase + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              uint4* dst = reinterpret_cast<uint4*>(dst_base + dst_row + c * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint4 o;
+                o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+                o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+                o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+                o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+                dst[v] = o;
+              }
+            }
+          }
+        } else {
+          // RMSNorm over the head (RMSNorm.cpp:12-22, ggml_rms_norm) then
+          // RoPE NORMAL on adjacent pairs (Flux2PosEmbed.hpp:18-109).
+          float ss = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(hbase + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float v = __uint_as_float(r[j]);
+              ss = fmaf(v, v, ss);
+            }
+          }
+          const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + e.eps);
+          const float* w = region == 0 ? e.norm_q[sel] : e.norm_k[sel];
+          const float2* rp = e.rope + static_cast<int64_t>(tok) * 64;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(hbase + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              uint32_t o[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int d0 = c * 32 + 2 * j;
+                float x0 = __uint_as_float(r[2 * j]) * rs * __ldg(w + d0);
+                float x1 = __uint_as_float(r[2 * j + 1]) * rs * __ldg(w + d0 + 1);
+                float2 cs = __ldg(rp + (d0 >> 1));
+                float y0 = x0 * cs.x - x1 * cs.y;
+                float y1 = x0 * cs.y + x1 * cs.x;
+                o[j] = pack_bf16x2(y0, y1);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(dst_base + dst_row + c * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
+          }
+        }
+      } else {
+        // SwiGLU: silu(gate) * up (Flux2SwiGLU.hpp:17-21, SiLU.hpp:9-13).
+        const int64_t mcol = (c0 - e.qkv_cols) >> 1;  // first of 64 outputs
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(hbase + c * 32, g);
+          tmem_ld32(hbase + 64 + c * 32, u);
+          tmem_ld_wait();
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(e.mlp_out + row * e.ld_mlp + mcol + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t o[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int i = 8 * v + 2 * j;
+                float a0 = silu(__uint_as_float(g[i])) * __uint_as_float(u[i]);
+                float a1 = silu(__uint_as_float(g[i + 1])) * __uint_as_float(u[i + 1]);
+                o[j] = pack_bf16x2(a0, a1);
+              }
+              dst[v] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // Column-wise epilogues: 8 chunks of 32 columns.
+  const float* gate = nullptr;
+  if (e.mode == kEpiResidGate || e.mode == kEpiGateF32) {
+    gate = e.gate[sel];
+    if (gate) gate += static_cast<int64_t>(G.batch) * e.gate_bstride;
+  }
+  const float dt = (e.mode == kEpiEuler) ? __ldg(e.dt) : 0.f;
+#pragma unroll 1
+  for (int c = 0; c < kGemmBN / 32; ++c) {
+    const int cb = col0 + c * 32;
+    uint32_t r[32];
+    tmem_ld32(taddr + c * 32, r);
+    tmem_ld_wait();
+    if (!row_ok || cb >= p.N) continue;
+    const bool full = cb + 32 <= p.N;
+    if (e.mode == kEpiBf16) {
+      uint16_t* dst = e.out_bf16 + row * e.ld_out + cb;
+      if (full) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 o;
+          o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+          o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+          o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+          o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+          d4[v] = o;
+        }
+      } else {
+        for (int j = 0; j < 32 && cb + j < p.N; ++j) {
+          __nv_bfloat16 b = __float2bfloat16_rn(__uint_as_float(r[j]));
+          dst[j] = *reinterpret_cast<uint16_t*>(&b);
+        }
+      }
+      continue;
+    }
+    float* dst = e.out_f32 + row * e.ld_out + cb;
+    if (full) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float4 a = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        if (e.mode == kEpiF32) {
+          d4[v] = a;
+        } else if (e.mode == kEpiResidGate || e.mode == kEpiGateF32) {
+          float4 gg = gate ? __ldg(reinterpret_cast<const float4*>(gate + cb) + v)
+                           : make_float4(1.f, 1.f, 1.f, 1.f);
+          if (e.mode == kEpiResidGate) {
+            float4 h = d4[v];
+            h.x += gg.x * a.x; h.y += gg.y * a.y; h.z += gg.z * a.z; h.w += gg.w * a.w;
+            d4[v] = h;
+          } else {
+            d4[v] = make_float4(gg.x * a.x, gg.y * a.y, gg.z * a.z, gg.w * a.w);
+          }
+        } else {  // Euler
+          const float4 x = __ldg(reinterpret_cast<const float4*>(e.x_in + row * e.ld_out + cb) + v);
+          d4[v] = make_float4(x.x + dt * a.x, x.y + dt * a.y, x.z + dt * a.z, x.w + dt * a.w);
+        }
+      }
+    } else {
+      for (int j = 0; j < 32 && cb + j < p.N; ++j) {
+        float a = __uint_as_float(r[j]);
+        if (e.mode == kEpiF32) dst[j] = a;
+        else if (e.mode == kEpiResidGate) dst[j] += (gate ? gate[cb + j] : 1.f) * a;
+        else if (e.mode == kEpiGateF32) dst[j] = (gate ? gate[cb + j] : 1.f) * a;
+        else dst[j] = e.x_in[row * e.ld_out + cb + j] + dt * a;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + kGemmStages * kAStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGemmStages * kStageBytes);
+  uint64_t* full = bars;                       // [stages]
+  uint64_t* empty = bars + kGemmStages;        // [stages]
+  uint64_t* acc_full = bars + 2 * kGemmStages; // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    tma_prefetch_desc(&tmB1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(p, t);
+        const GemmGroup& G = p.groups[tc.g];
+        const int ya = G.row0 + tc.m_tile * kGemmBM;
+        const int yb = tc.n_tile * kGemmBN;
+        const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
+          tma_load_2d(smB + stage * kBStageBytes, tmB, &full[stage], kb * kGemmBK, yb);
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, kGemmBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smA + stage * kAStageBytes);
+          const uint32_t b0 = smem_u32(smB + stage * kBStageBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_bf16(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      bool ok = mbar_wait(&acc_full[acc], acc_phase, p.err, kDevTimeoutAccum);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const TileCoord tc = decode_tile(p, t);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
+      epilogue_row(p, tc, row_in_tile, taddr);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                           uint64_t ld_elems, uint32_t box_outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld_elems * 2) & 15)) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+void gemm_finalize_groups(GemmArgs& a) {
+  a.n_tiles_n = (a.N + kGemmBN - 1) / kGemmBN;
+  int t = 0;
+  for (int g = 0; g < a.n_groups; ++g) {
+    a.groups[g].m_tiles = (a.groups[g].rows + kGemmBM - 1) / kGemmBM;
+    a.groups[g].tile0 = t;
+    t += a.groups[g].m_tiles * a.n_tiles_n;
+  }
+  a.total_tiles = t;
+}
+
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
+                        int bsrc, int num_sms, cudaStream_t stream) {
+  if (bsrc != kBSrcBf16) return cudaErrorNotSupported;
+  if (args.total_tiles <= 0) return cudaSuccess;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kGemmSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int grid = std::min(args.total_tiles, num_sms);
+  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b0, b1, args);
+  return cudaGetLastError();
+}
+
+}  // namespace dcpp

@@ -1,0 +1,101 @@
+// Grouped tcgen05 GEMM: Y[rows, N] = X[rows, K] . W_g[N, K]^T with fused
+// epilogues.  Host-visible parameter structs and launch entry points.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dcpp {
+
+constexpr int kGemmBM = 128;      // rows per tile (TMEM lanes)
+constexpr int kGemmBN = 256;      // columns per tile (TMEM columns per accumulator)
+constexpr int kGemmBK = 64;       // K per smem stage (one 128-byte swizzle atom of bf16)
+constexpr int kGemmStages = 4;    // smem pipeline depth
+constexpr int kGemmMaxGroups = 8; // row groups (txt/img stream x batch)
+
+// B operand source of a GEMM launch.
+enum GemmBSource : int {
+  kBSrcBf16 = 0,   // bf16 weight [N, K] loaded by TMA (128B swizzle)
+  kBSrcQ8_0 = 1,   // Q8_0 weight repacked (int8 [N,K] + f16 scales [N,K/32]), dequantised in smem
+  kBSrcQ4_K = 2,   // Q4_K weight repacked (nibbles [N,K/2] + scale/min pairs), dequantised in smem
+};
+
+// Epilogue of a GEMM launch.  The accumulator is f32 in TMEM; each
+// epilogue thread owns one output row of the 128-row tile.
+enum GemmEpilogue : int {
+  kEpiF32 = 0,        // out_f32[r, c] = acc
+  kEpiBf16 = 1,       // out_bf16[r, c] = bf16(acc)
+  kEpiResidGate = 2,  // out_f32[r, c] += gate_g[c] * acc   (gated residual, Flux2TransformerBlock.hpp:86-87)
+  kEpiQkvMlp = 3,     // q/k: RMSNorm + RoPE -> [B,H,S,d]; v -> [B,H,S,d]; mlp gate/up -> SwiGLU
+  kEpiEuler = 4,      // out_f32[r, c] = x_in[r, c] + dt * acc  (FlowMatchEuler integrate)
+  kEpiGateF32 = 5,    // out_f32[r, c] = gate_g[c] * acc   (TP partial before the all-reduce)
+};
+
+struct GemmGroup {
+  int32_t row0;     // first row of this group in A
+  int32_t orow0;    // first row of this group in Y (the epilogue's output)
+  int32_t rows;     // number of rows
+  int32_t wsel;     // which weight (0 or 1)
+  int32_t batch;    // batch index of these rows
+  int32_t tile0;    // first linear tile index of the group
+  int32_t m_tiles;  // ceil(rows / 128)
+  int32_t sel;      // per-group parameter selector (0 = txt stream, 1 = img stream)
+  int32_t tok0;     // token index (within its batch) of row0
+};
+
+struct EpilogueArgs {
+  int mode;
+  float* out_f32;
+  uint16_t* out_bf16;
+  int64_t ld_out;            // row stride of out (elements)
+  const float* x_in;         // Euler: previous latents (same layout as out_f32)
+  const float* dt;           // Euler: device scalar
+  const float* gate[2];      // per selector: gate vector [N] (batch stride gate_bstride)
+  int64_t gate_bstride;
+  // kEpiQkvMlp
+  int32_t qkv_cols;          // columns holding q|k|v (3 * local inner dim); 0 = mlp only
+  int32_t inner;             // local inner dim (heads_local * 128)
+  int32_t seq;               // tokens per batch element (S)
+  int32_t heads;             // local heads
+  const float* norm_q[2];    // per selector RMSNorm weights [128]
+  const float* norm_k[2];
+  float eps;
+  const float2* rope;        // [S, 64] (cos, sin) per token and rotary pair
+  uint16_t* q_out;           // [B, H, S, 128]
+  uint16_t* k_out;
+  uint16_t* v_out;
+  uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
+  int64_t ld_mlp;
+};
+
+struct QuantB {
+  const void* qs;            // Q8_0: int8 [N, K]; Q4_K: uint8 [N, K/2]
+  const void* scales;        // Q8_0: f16 [N, K/32]; Q4_K: float2 [N, K/32] (scale, min)
+};
+
+struct GemmArgs {
+  int32_t N, K;
+  int32_t n_tiles_n;
+  int32_t total_tiles;
+  int32_t n_groups;
+  GemmGroup groups[kGemmMaxGroups];
+  EpilogueArgs ep;
+  QuantB qb[2];
+  int* err;
+};
+
+// Host-side: build a 2-D bf16 tensor map with 128-byte swizzle for a
+// K-major operand [outer rows, inner K] with row stride `ld` elements.
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                           uint64_t ld_elems, uint32_t box_outer);
+
+// Launch the grouped GEMM.  `a` maps X (box 64 x 128), b0/b1 map the two
+// bf16 weights (box 64 x 256) when bsrc == kBSrcBf16.
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                        const GemmArgs& args, int bsrc, int num_sms, cudaStream_t stream);
+
+// Fill the tile prefix sums of `args` from its groups.
+void gemm_finalize_groups(GemmArgs& args);
+
+}  // namespace dcpp

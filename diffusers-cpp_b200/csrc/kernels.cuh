@@ -1,0 +1,86 @@
+// Launch entry points of the non-GEMM kernels (host-callable, C++ linkage).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dcpp {
+
+// ggml type ids (ggml enum ggml_type).
+constexpr int kTypeF32 = 0;
+constexpr int kTypeF16 = 1;
+constexpr int kTypeQ8_0 = 8;
+constexpr int kTypeQ4_K = 12;
+constexpr int kTypeBF16 = 30;
+
+// ---- dequant.cu
+cudaError_t launch_dequant_f32(int type, const void* blocks, int64_t n, float* out, cudaStream_t s);
+cudaError_t launch_dequant_bf16(int type, const void* blocks, int64_t n, uint16_t* out, cudaStream_t s);
+
+// ---- rowops.cu
+constexpr int kMaxNormSegments = 8;
+
+// One contiguous run of rows normalised with one (shift, scale) pair.
+struct NormSegment {
+  int32_t src_row0;     // first row in x
+  int32_t dst_row0;     // first row in y
+  int32_t rows;
+  const float* shift;   // [D] (may be null -> 0)
+  const float* scale;   // [D] (may be null -> 0, i.e. factor 1)
+};
+
+struct NormArgs {
+  const float* x;       // f32 [*, D] (the residual stream)
+  float* x_out;         // if resid: x_out = x + resid (may alias x)
+  const float* resid;   // optional addend (TP all-reduced partials), same layout as x
+  uint16_t* y;          // bf16 [*, ld_y]
+  int64_t ld_x;
+  int64_t ld_y;
+  int32_t D;
+  float eps;
+  int32_t n_segments;
+  NormSegment seg[kMaxNormSegments];
+};
+
+// y = LayerNorm(x) * (1 + scale) + shift, one warp per row.
+cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s);
+
+cudaError_t launch_f32_to_bf16(const float* in, int64_t n, uint16_t* out, cudaStream_t s);
+
+// Rotary table [S, 64] of (cos, sin) for head_dim 128 split into axis
+// sections of axes_dims (ggml rope NORMAL, theta_scale = base^(-2/n_dims)).
+cudaError_t launch_rope_table(const int32_t* ids, int64_t S, int n_axes, const int32_t* axes_dims_dev,
+                              float theta, float2* table, cudaStream_t s);
+
+// Sinusoidal timestep features (Timesteps.cpp:17-46, flip_sin_to_cos):
+// out[b, :half] = cos(t_b * mult * f_i), out[b, half:] = sin(...),
+// f_i = exp(-ln(10000) * i / half).
+cudaError_t launch_timestep_proj(const float* t, int B, int channels, float mult, float* out, cudaStream_t s);
+
+// y[b, n] = act_out( sum_k act_in(x[b, k]) * W[n, k] ), W of ggml type wtype
+// in raw GGUF layout; B <= 4 rows.  act: 0 none, 1 SiLU.
+cudaError_t launch_gemv(int wtype, const void* W, int64_t N, int64_t K, const float* x, int B, int act_in,
+                        int act_out, float* y, cudaStream_t s);
+
+// In-place y += a (f32).
+cudaError_t launch_add_f32(float* y, const float* a, int64_t n, cudaStream_t s);
+
+// ---- attention.cu
+struct AttnArgs {
+  const uint16_t* q;   // [B, H, S, 128] bf16 (already normalised and rotated)
+  const uint16_t* k;
+  const uint16_t* v;
+  uint16_t* o;         // row (b*S + s), column h*128 + d, row stride ld_o
+  int64_t ld_o;
+  int32_t B, H, S;
+  float scale;         // softmax scale (1/sqrt(128))
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// Standalone q/k RMSNorm + RoPE + relayout from the fused qkv projection
+// rows [B*S, 3*H*128] into q/k/v [B, H, S, 128].
+cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t B, int64_t S, int64_t H, const float* norm_q,
+                                const float* norm_k, float eps, const float2* rope, uint16_t* q, uint16_t* k,
+                                uint16_t* v, cudaStream_t s);
+
+}  // namespace dcpp

@@ -1,0 +1,361 @@
+// Row-wise and small kernels of the Flux2 step: adaLN LayerNorm +
+// modulation, f32 -> bf16 conversion, the RoPE table, sinusoidal timestep
+// features and the batch-1 conditioning GEMVs.  All HBM-bound: coalesced
+// 16-byte accesses, warp-shuffle reductions.
+#include "common.cuh"
+#include "kernels.cuh"
+
+#include <math.h>
+
+namespace dcpp {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------ LayerNorm + mod
+// One CTA per destination row; each thread keeps up to kVec float4 of the
+// row in registers.  Two-pass mean / variance like ggml_norm
+// (LayerNorm.cpp:16-32 with elementwise_affine = false), then the adaLN
+// modulation (1 + scale) * n + shift (Flux2TransformerBlock.hpp:66,72,92,106;
+// Flux2SingleTransformerBlock.hpp:53-54; AdaLayerNormContinuous.inl:43).
+template <int kThreads, int kVec>
+__global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_constant__ NormArgs a) {
+  __shared__ float red[kThreads / 32];
+  __shared__ float stat;
+  int blk = blockIdx.x;
+  int sidx = 0;
+#pragma unroll 1
+  for (; sidx < a.n_segments; ++sidx) {
+    if (blk < a.seg[sidx].rows) break;
+    blk -= a.seg[sidx].rows;
+  }
+  if (sidx >= a.n_segments) return;
+  const NormSegment& sg = a.seg[sidx];
+  const int64_t src = sg.src_row0 + blk;
+  const int64_t dst = sg.dst_row0 + blk;
+  const int D = a.D;
+  const int nv = D >> 2;
+  const float4* x4 = reinterpret_cast<const float4*>(a.x + src * a.ld_x);
+  const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + src * a.ld_x) : nullptr;
+  float4* xo4 = a.resid ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
+
+  float4 v[kVec];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nv) {
+      float4 t = x4[idx];
+      if (r4) {
+        const float4 r = r4[idx];
+        t.x += r.x; t.y += r.y; t.z += r.z; t.w += r.w;
+        xo4[idx] = t;
+      }
+      v[i] = t;
+      sum += (t.x + t.y) + (t.z + t.w);
+    } else {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  sum = warp_sum(sum);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = threadIdx.x < kThreads / 32 ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) stat = s / static_cast<float>(D);
+  }
+  __syncthreads();
+  const float mean = stat;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nv) {
+      float4& t = v[i];
+      t.x -= mean; t.y -= mean; t.z -= mean; t.w -= mean;
+      sq += (t.x * t.x + t.y * t.y) + (t.z * t.z + t.w * t.w);
+    }
+  }
+  __syncthreads();
+  sq = warp_sum(sq);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = threadIdx.x < kThreads / 32 ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) stat = 1.0f / sqrtf(s / static_cast<float>(D) + a.eps);
+  }
+  __syncthreads();
+  const float rstd = stat;
+  const float4* sh4 = reinterpret_cast<const float4*>(sg.shift);
+  const float4* sc4 = reinterpret_cast<const float4*>(sg.scale);
+  uint2* y2 = reinterpret_cast<uint2*>(a.y + dst * a.ld_y);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nv) {
+      const float4 t = v[i];
+      const float4 sh = sh4 ? __ldg(sh4 + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 sc = sc4 ? __ldg(sc4 + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float o0 = (1.0f + sc.x) * (t.x * rstd) + sh.x;
+      float o1 = (1.0f + sc.y) * (t.y * rstd) + sh.y;
+      float o2 = (1.0f + sc.z) * (t.z * rstd) + sh.z;
+      float o3 = (1.0f + sc.w) * (t.w * rstd) + sh.w;
+      y2[idx] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    }
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float4* __restrict__ in, int64_t n4, uint2* __restrict__ out) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (; i < n4; i += stride) {
+    const float4 v = in[i];
+    out[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+__global__ void f32_to_bf16_tail_kernel(const float* __restrict__ in, int64_t start, int64_t n, uint16_t* out) {
+  int64_t i = start + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    __nv_bfloat16 b = __float2bfloat16_rn(in[i]);
+    out[i] = *reinterpret_cast<uint16_t*>(&b);
+  }
+}
+
+struct AxesDims {
+  int n;
+  int dims[8];
+};
+
+// ggml rope NORMAL cache (ggml_rope_cache_init with freq_scale 1,
+// ext_factor 0, attn_factor 1): theta starts at the position and is
+// multiplied by theta_scale = base^(-2/n_dims) once per rotary pair.
+__global__ void rope_table_kernel(const int32_t* __restrict__ ids, int64_t S, AxesDims ax, float base,
+                                  float2* __restrict__ table) {
+  int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (s >= S) return;
+  int pair = 0;
+#pragma unroll 1
+  for (int a = 0; a < ax.n; ++a) {
+    const int nd = ax.dims[a];
+    const float theta_scale = powf(base, -2.0f / static_cast<float>(nd));
+    float theta = static_cast<float>(ids[s * ax.n + a]);
+#pragma unroll 1
+    for (int p = 0; p < nd / 2; ++p) {
+      float sn, cs;
+      sincosf(theta, &sn, &cs);
+      table[s * 64 + pair] = make_float2(cs, sn);
+      ++pair;
+      theta *= theta_scale;
+    }
+  }
+}
+
+__global__ void timestep_proj_kernel(const float* __restrict__ t, int channels, float mult, float* __restrict__ out) {
+  const int b = blockIdx.x;
+  const int half = channels / 2;
+  const float c = -logf(10000.0f) / static_cast<float>(half);
+  const float tb = t[b] * mult;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = expf(static_cast<float>(i) * c);
+    const float arg = tb * f;
+    out[b * channels + i] = cosf(arg);
+    out[b * channels + half + i] = sinf(arg);
+  }
+  if ((channels & 1) && threadIdx.x == 0) out[b * channels + channels - 1] = 0.f;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// One warp per output feature; lanes stride over 32-weight sub-blocks.
+template <int kType>
+__global__ void __launch_bounds__(256) gemv_kernel(const uint8_t* __restrict__ W, int64_t N, int64_t K,
+                                                   const float* __restrict__ x, int B, int act_in, int act_out,
+                                                   float* __restrict__ y) {
+  extern __shared__ float xs[];  // [B, K]
+  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(B) * K; i += blockDim.x) {
+    float v = x[i];
+    xs[i] = act_in ? silu_f(v) : v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5);
+  if (n >= N) return;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t nsb = K / 32;
+  if (kType == kTypeQ4_K) {
+    const uint8_t* row = W + n * (K / 256) * 144;
+    for (int64_t sb = lane; sb < nsb; sb += 32) {
+      const uint8_t* blk = row + (sb >> 3) * 144;
+      const int j = static_cast<int>(sb & 7);
+      const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+      const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk + 2)));
+      const uint8_t* s = blk + 4;
+      int sc, m;
+      if (j < 4) { sc = s[j] & 0x3F; m = s[j + 4] & 0x3F; }
+      else { sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30); m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30); }
+      const float ds = d * static_cast<float>(sc);
+      const float dm = dmin * static_cast<float>(m);
+      const uint4* q4 = reinterpret_cast<const uint4*>(blk + 16 + (j >> 1) * 32);
+      const int shift = (j & 1) * 4;
+      uint4 qa = __ldg(q4), qb = __ldg(q4 + 1);
+      uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      for (int b = 0; b < B; ++b) {
+        const float* xv = xs + b * K + sb * 32;
+        float sq = 0.f, sx = 0.f;
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+          const float q = static_cast<float>((w[l >> 2] >> (8 * (l & 3) + shift)) & 0xF);
+          sq = fmaf(q, xv[l], sq);
+          sx += xv[l];
+        }
+        acc[b] += ds * sq - dm * sx;
+      }
+    }
+  } else if (kType == kTypeQ8_0) {
+    const uint8_t* row = W + n * nsb * 34;
+    for (int64_t sb = lane; sb < nsb; sb += 32) {
+      const uint8_t* blk = row + sb * 34;
+      const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
+      for (int b = 0; b < B; ++b) {
+        const float* xv = xs + b * K + sb * 32;
+        float sq = 0.f;
+#pragma unroll
+        for (int l = 0; l < 32; ++l) sq = fmaf(static_cast<float>(static_cast<int8_t>(blk[2 + l])), xv[l], sq);
+        acc[b] += d * sq;
+      }
+    }
+  } else if (kType == kTypeBF16 || kType == kTypeF16) {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(W) + n * K;
+    for (int64_t c = lane; c < K / 8; c += 32) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + c);
+      const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+      float wf[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (kType == kTypeBF16) {
+          wf[2 * i] = __uint_as_float(wv[i] << 16);
+          wf[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+        } else {
+          wf[2 * i] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] & 0xFFFF)));
+          wf[2 * i + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] >> 16)));
+        }
+      }
+      for (int b = 0; b < B; ++b) {
+        const float* xv = xs + b * K + c * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[b] = fmaf(wf[i], xv[i], acc[b]);
+      }
+    }
+  } else {  // F32
+    const float* row = reinterpret_cast<const float*>(W) + n * K;
+    for (int64_t c = lane; c < K; c += 32)
+      for (int b = 0; b < B; ++b) acc[b] = fmaf(row[c], xs[b * K + c], acc[b]);
+  }
+  for (int b = 0; b < B; ++b) {
+    float v = warp_sum(acc[b]);
+    if (lane == 0) y[b * N + n] = act_out ? silu_f(v) : v;
+  }
+}
+
+__global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (; i < n; i += stride) y[i] += a[i];
+}
+
+}  // namespace
+
+cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
+  if (a.D % 4 != 0 || a.D > 8192 || (a.ld_x % 4) || (a.ld_y % 4)) return cudaErrorInvalidValue;
+  int64_t rows = 0;
+  for (int i = 0; i < a.n_segments; ++i) rows += a.seg[i].rows;
+  if (rows == 0) return cudaSuccess;
+  if (a.D <= 128 * 4 * 8)
+    layernorm_mod_kernel<128, 8><<<static_cast<unsigned>(rows), 128, 0, s>>>(a);
+  else
+    layernorm_mod_kernel<256, 8><<<static_cast<unsigned>(rows), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_bf16(const float* in, int64_t n, uint16_t* out, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t n4 = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) ? 0 : n / 4;
+  if (n4) {
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    f32_to_bf16_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(reinterpret_cast<const float4*>(in), n4,
+                                                                       reinterpret_cast<uint2*>(out));
+  }
+  const int64_t rest = n - n4 * 4;
+  if (rest) f32_to_bf16_tail_kernel<<<static_cast<unsigned>((rest + 255) / 256), 256, 0, s>>>(in, n4 * 4, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(const int32_t* ids, int64_t S, int n_axes, const int32_t* axes_dims, float theta,
+                              float2* table, cudaStream_t s) {
+  AxesDims ax;
+  if (n_axes < 1 || n_axes > 8) return cudaErrorInvalidValue;
+  ax.n = n_axes;
+  int total = 0;
+  for (int i = 0; i < n_axes; ++i) {
+    ax.dims[i] = axes_dims[i];
+    if (axes_dims[i] <= 0 || (axes_dims[i] & 1)) return cudaErrorInvalidValue;
+    total += axes_dims[i];
+  }
+  if (total != 128) return cudaErrorInvalidValue;
+  if (S <= 0) return cudaSuccess;
+  rope_table_kernel<<<static_cast<unsigned>((S + 127) / 128), 128, 0, s>>>(ids, S, ax, theta, table);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_timestep_proj(const float* t, int B, int channels, float mult, float* out, cudaStream_t s) {
+  if (B <= 0) return cudaSuccess;
+  timestep_proj_kernel<<<B, 128, 0, s>>>(t, channels, mult, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(int wtype, const void* W, int64_t N, int64_t K, const float* x, int B, int act_in,
+                        int act_out, float* y, cudaStream_t s) {
+  if (B < 1 || B > 4) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(B) * K * sizeof(float);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>((N + 7) / 8);
+  const uint8_t* w = static_cast<const uint8_t*>(W);
+#define DCPP_GEMV(T)                                                                                   \
+  do {                                                                                                 \
+    static bool attr = false;                                                                          \
+    if (!attr) {                                                                                       \
+      cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);   \
+      attr = true;                                                                                     \
+    }                                                                                                  \
+    gemv_kernel<T><<<grid, 256, smem, s>>>(w, N, K, x, B, act_in, act_out, y);                         \
+  } while (0)
+  switch (wtype) {
+    case kTypeQ4_K: if (K % 256) return cudaErrorInvalidValue; DCPP_GEMV(kTypeQ4_K); break;
+    case kTypeQ8_0: if (K % 32) return cudaErrorInvalidValue; DCPP_GEMV(kTypeQ8_0); break;
+    case kTypeBF16: if (K % 8) return cudaErrorInvalidValue; DCPP_GEMV(kTypeBF16); break;
+    case kTypeF16: if (K % 8) return cudaErrorInvalidValue; DCPP_GEMV(kTypeF16); break;
+    case kTypeF32: DCPP_GEMV(kTypeF32); break;
+    default: return cudaErrorNotSupported;
+  }
+#undef DCPP_GEMV
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_f32(float* y, const float* a, int64_t n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  add_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(y, a, n);
+  return cudaGetLastError();
+}
+
+}  // namespace dcpp

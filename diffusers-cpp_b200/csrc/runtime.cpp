@@ -1,0 +1,392 @@
+// Context, memory, op-level and tensor-parallel entry points of the C ABI.
+#include "runtime.hpp"
+
+#include <dlfcn.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace dcpp {
+
+Nccl& Nccl::get() {
+  static Nccl n;
+  if (n.loaded) return n;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) fail(DCPP_ERR_NCCL, std::string("cannot load NCCL: ") + dlerror());
+  auto sym = [&](const char* name) {
+    void* p = dlsym(h, name);
+    if (!p) fail(DCPP_ERR_NCCL, std::string("NCCL symbol missing: ") + name);
+    return p;
+  };
+  n.GetUniqueId = reinterpret_cast<int (*)(UniqueId*)>(sym("ncclGetUniqueId"));
+  n.CommInitRank = reinterpret_cast<int (*)(Comm*, int, UniqueId, int)>(sym("ncclCommInitRank"));
+  n.CommDestroy = reinterpret_cast<int (*)(Comm)>(sym("ncclCommDestroy"));
+  n.CommAbort = reinterpret_cast<int (*)(Comm)>(sym("ncclCommAbort"));
+  n.AllReduce =
+      reinterpret_cast<int (*)(const void*, void*, size_t, int, int, Comm, cudaStream_t)>(sym("ncclAllReduce"));
+  n.GetErrorString = reinterpret_cast<const char* (*)(int)>(sym("ncclGetErrorString"));
+  n.loaded = true;
+  return n;
+}
+
+void Ctx::maybe_inject(const char* entry) {
+  if (fault_countdown <= 0 || fault_name != entry) return;
+  if (--fault_countdown == 0) {
+    fault_name.clear();
+    fail(DCPP_ERR_INJECTED, std::string("injected fault in ") + entry);
+  }
+}
+
+void* Ctx::ensure_scratch(size_t bytes) {
+  if (bytes <= scratch_bytes) return scratch;
+  if (scratch) cuda_check(cudaFree(scratch), "cudaFree(scratch)");
+  scratch = nullptr;
+  scratch_bytes = 0;
+  if (cudaMalloc(&scratch, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    fail(DCPP_ERR_OOM, "scratch allocation of " + std::to_string(bytes) + " bytes failed");
+  }
+  scratch_bytes = bytes;
+  return scratch;
+}
+
+const char* device_error_name(int code) {
+  switch (code) {
+    case kDevTimeoutFull: return "GEMM consumer timed out waiting for a shared-memory stage";
+    case kDevTimeoutEmpty: return "GEMM producer timed out waiting for a free stage";
+    case kDevTimeoutAccum: return "GEMM epilogue timed out waiting for an accumulator";
+    case kDevTimeoutAccumFree: return "GEMM MMA warp timed out waiting for a drained accumulator";
+    case kDevTimeoutDequant: return "GEMM dequant stage handshake timed out";
+    case kDevBadShape: return "kernel launched with an unsupported shape";
+    case kDevTimeoutAttn: return "attention pipeline wait timed out";
+    default: return "unknown device error";
+  }
+}
+
+void Ctx::check_device_error() {
+  int h = 0;
+  cuda_check(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream), "read error word");
+  cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+  if (h != 0) {
+    cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "clear error word");
+    fail(h == kDevBadShape ? DCPP_ERR_UNSUPPORTED : DCPP_ERR_TIMEOUT,
+         std::string("device error ") + std::to_string(h) + ": " + device_error_name(h));
+  }
+}
+
+size_t row_bytes_of(int type, int64_t n) {
+  switch (type) {
+    case kTypeF32: return static_cast<size_t>(n) * 4;
+    case kTypeF16:
+    case kTypeBF16: return static_cast<size_t>(n) * 2;
+    case kTypeQ8_0:
+      if (n % 32) fail(DCPP_ERR_INVALID_ARG, "Q8_0 row length must be a multiple of 32");
+      return static_cast<size_t>(n / 32) * 34;
+    case kTypeQ4_K:
+      if (n % 256) fail(DCPP_ERR_INVALID_ARG, "Q4_K row length must be a multiple of 256");
+      return static_cast<size_t>(n / 256) * 144;
+    default: fail(DCPP_ERR_UNSUPPORTED, "unsupported ggml type " + std::to_string(type));
+  }
+}
+
+// y[M,N] = x[M,K] . W^T through the tensor-core GEMM (weights expanded to
+// bf16 into the context scratch first).
+void gemm_op(Ctx& c, int wtype, const void* w, int64_t N, int64_t K, const uint16_t* x, int64_t M, float* y) {
+  if (N <= 0 || K <= 0 || M <= 0) fail(DCPP_ERR_INVALID_ARG, "dcpp_gemm: sizes must be positive");
+  if (K % 8) fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm: K must be a multiple of 8");
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2) fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm: size too large");
+  (void)row_bytes_of(wtype, K);
+  const uint16_t* wb = nullptr;
+  if (wtype == kTypeBF16) {
+    wb = static_cast<const uint16_t*>(w);
+  } else {
+    uint16_t* s = static_cast<uint16_t*>(c.ensure_scratch(static_cast<size_t>(N) * K * 2));
+    cuda_check(launch_dequant_bf16(wtype, w, N * K, s, c.stream), "dequant weight");
+    wb = s;
+  }
+  CUtensorMap ta, tb;
+  cuda_check(make_tmap_bf16(&ta, x, K, M, K, kGemmBM), "tensor map (x)");
+  cuda_check(make_tmap_bf16(&tb, wb, K, N, K, kGemmBN), "tensor map (W)");
+  GemmArgs a{};
+  a.N = static_cast<int32_t>(N);
+  a.K = static_cast<int32_t>(K);
+  a.n_groups = 1;
+  a.groups[0].row0 = 0;
+  a.groups[0].orow0 = 0;
+  a.groups[0].rows = static_cast<int32_t>(M);
+  a.ep.mode = kEpiF32;
+  a.ep.out_f32 = y;
+  a.ep.ld_out = N;
+  a.err = c.d_err;
+  gemm_finalize_groups(a);
+  cuda_check(launch_gemm(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm");
+}
+
+}  // namespace dcpp
+
+using dcpp::Ctx;
+using dcpp::Error;
+
+namespace {
+
+template <class F>
+dcpp_status guarded(dcpp_ctx* ctx, const char* entry, F&& f) {
+  if (!ctx) return DCPP_ERR_INVALID_ARG;
+  try {
+    ctx->maybe_inject(entry);
+    int prev = 0;
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != ctx->device) cudaSetDevice(ctx->device);
+    f();
+    return DCPP_OK;
+  } catch (const Error& e) {
+    ctx->last_error = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    ctx->last_error = e.what();
+    return DCPP_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* dcpp_version(void) { return "dcpp-b200 0.1 (sm_100a)"; }
+
+dcpp_status dcpp_init(int device, dcpp_ctx** out_ctx) {
+  if (!out_ctx) return DCPP_ERR_INVALID_ARG;
+  *out_ctx = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    return DCPP_ERR_CUDA;
+  }
+  auto* c = new dcpp_ctx();
+  c->device = device;
+  if (cudaSetDevice(device) != cudaSuccess) { delete c; return DCPP_ERR_CUDA; }
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) { delete c; return DCPP_ERR_CUDA; }
+  if (prop.major != 10) {
+    delete c;
+    return DCPP_ERR_UNSUPPORTED;  // built for sm_100a only
+  }
+  c->num_sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) { delete c; return DCPP_ERR_CUDA; }
+  c->stream = c->own_stream;
+  if (cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+    cudaStreamDestroy(c->own_stream);
+    delete c;
+    return DCPP_ERR_CUDA;
+  }
+  *out_ctx = c;
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_destroy(dcpp_ctx* ctx) {
+  if (!ctx) return DCPP_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  if (ctx->comm) {
+    try { dcpp::Nccl::get().CommDestroy(ctx->comm); } catch (...) {}
+  }
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return DCPP_OK;
+}
+
+const char* dcpp_last_error(const dcpp_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+dcpp_status dcpp_set_stream(dcpp_ctx* ctx, void* s) {
+  return guarded(ctx, "dcpp_set_stream", [&] {
+    ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+  });
+}
+
+dcpp_status dcpp_synchronize(dcpp_ctx* ctx) {
+  return guarded(ctx, "dcpp_synchronize", [&] { ctx->check_device_error(); });
+}
+
+dcpp_status dcpp_alloc(dcpp_ctx* ctx, size_t bytes, void** d_out) {
+  return guarded(ctx, "dcpp_alloc", [&] {
+    if (!d_out) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_alloc: null output");
+    *d_out = nullptr;
+    if (cudaMalloc(d_out, bytes ? bytes : 1) != cudaSuccess) {
+      cudaGetLastError();
+      dcpp::fail(DCPP_ERR_OOM, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+    }
+  });
+}
+
+dcpp_status dcpp_free(dcpp_ctx* ctx, void* p) {
+  return guarded(ctx, "dcpp_free", [&] { dcpp::cuda_check(cudaFree(p), "cudaFree"); });
+}
+
+dcpp_status dcpp_memcpy(dcpp_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  return guarded(ctx, "dcpp_memcpy", [&] {
+    dcpp::cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, ctx->stream), "cudaMemcpyAsync");
+    dcpp::cuda_check(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  });
+}
+
+dcpp_status dcpp_row_bytes(int type, int64_t n, size_t* out) {
+  if (!out || n < 0) return DCPP_ERR_INVALID_ARG;
+  try {
+    *out = dcpp::row_bytes_of(type, n);
+    return DCPP_OK;
+  } catch (const Error& e) {
+    return e.status;
+  }
+}
+
+dcpp_status dcpp_inject_fault(dcpp_ctx* ctx, const char* name, int nth) {
+  if (!ctx) return DCPP_ERR_INVALID_ARG;
+  if (!name || nth <= 0) {
+    ctx->fault_name.clear();
+    ctx->fault_countdown = 0;
+  } else {
+    ctx->fault_name = name;
+    ctx->fault_countdown = nth;
+  }
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_dequant(dcpp_ctx* ctx, int type, const void* blocks, int64_t n, float* out) {
+  return guarded(ctx, "dcpp_dequant", [&] {
+    if (!blocks || !out || n < 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_dequant: bad argument");
+    (void)dcpp::row_bytes_of(type, n);
+    dcpp::cuda_check(dcpp::launch_dequant_f32(type, blocks, n, out, ctx->stream), "dequant");
+  });
+}
+
+dcpp_status dcpp_dequant_bf16(dcpp_ctx* ctx, int type, const void* blocks, int64_t n, uint16_t* out) {
+  return guarded(ctx, "dcpp_dequant_bf16", [&] {
+    if (!blocks || !out || n < 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_dequant_bf16: bad argument");
+    (void)dcpp::row_bytes_of(type, n);
+    dcpp::cuda_check(dcpp::launch_dequant_bf16(type, blocks, n, out, ctx->stream), "dequant");
+  });
+}
+
+dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* in, int64_t n, uint16_t* out) {
+  return guarded(ctx, "dcpp_f32_to_bf16", [&] {
+    if (!in || !out || n < 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_f32_to_bf16: bad argument");
+    dcpp::cuda_check(dcpp::launch_f32_to_bf16(in, n, out, ctx->stream), "f32_to_bf16");
+  });
+}
+
+dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const uint16_t* x, int64_t M,
+                      float* y) {
+  return guarded(ctx, "dcpp_gemm", [&] {
+    if (!w || !x || !y) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_gemm: null pointer");
+    dcpp::gemm_op(*ctx, wtype, w, N, K, x, M, y);
+  });
+}
+
+dcpp_status dcpp_layernorm_mod(dcpp_ctx* ctx, const float* x, int64_t rows, int64_t D, const float* shift,
+                               const float* scale, float eps, uint16_t* y) {
+  return guarded(ctx, "dcpp_layernorm_mod", [&] {
+    if (!x || !y || rows < 0 || D <= 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_layernorm_mod: bad argument");
+    if (D % 4 || D > 8192) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_layernorm_mod: D must be a multiple of 4, <= 8192");
+    if (rows > INT32_MAX) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_layernorm_mod: too many rows");
+    dcpp::NormArgs a{};
+    a.x = x;
+    a.y = y;
+    a.ld_x = D;
+    a.ld_y = D;
+    a.D = static_cast<int32_t>(D);
+    a.eps = eps;
+    a.n_segments = 1;
+    a.seg[0] = {0, 0, static_cast<int32_t>(rows), shift, scale};
+    dcpp::cuda_check(dcpp::launch_layernorm_mod(a, ctx->stream), "layernorm_mod");
+  });
+}
+
+dcpp_status dcpp_attention(dcpp_ctx* ctx, const uint16_t* qkv, int64_t B, int64_t S, int64_t H, int64_t head_dim,
+                           const float* norm_q, const float* norm_k, float eps, const int32_t* ids, int n_axes,
+                           const int64_t* axes_dims, float theta, uint16_t* out) {
+  return guarded(ctx, "dcpp_attention", [&] {
+    if (!qkv || !out || !ids || !norm_q || !norm_k || !axes_dims || B <= 0 || S <= 0 || H <= 0)
+      dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_attention: bad argument");
+    if (head_dim != 128) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_attention: head_dim must be 128");
+    if (n_axes < 1 || n_axes > 8) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_attention: 1..8 rope axes");
+    int32_t dims[8];
+    int64_t tot = 0;
+    for (int i = 0; i < n_axes; ++i) {
+      dims[i] = static_cast<int32_t>(axes_dims[i]);
+      tot += axes_dims[i];
+    }
+    if (tot != head_dim) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_attention: axes dims must sum to head_dim");
+    const size_t qkv_elems = static_cast<size_t>(B * H * S * 128);
+    const size_t rope_bytes = static_cast<size_t>(S) * 64 * sizeof(float2);
+    const size_t need = 3 * qkv_elems * 2 + rope_bytes + 256;
+    uint8_t* s = static_cast<uint8_t*>(ctx->ensure_scratch(need));
+    auto* q = reinterpret_cast<uint16_t*>(s);
+    auto* k = q + qkv_elems;
+    auto* v = k + qkv_elems;
+    auto* rope = reinterpret_cast<float2*>(s + ((3 * qkv_elems * 2 + 255) & ~size_t(255)));
+    dcpp::cuda_check(dcpp::launch_rope_table(ids, S, n_axes, dims, theta, rope, ctx->stream), "rope table");
+    dcpp::cuda_check(dcpp::launch_qk_norm_rope(qkv, B, S, H, norm_q, norm_k, eps, rope, q, k, v, ctx->stream),
+                     "qk norm rope");
+    dcpp::AttnArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.o = out;
+    a.ld_o = H * 128;
+    a.B = static_cast<int32_t>(B);
+    a.H = static_cast<int32_t>(H);
+    a.S = static_cast<int32_t>(S);
+    a.scale = 1.0f / sqrtf(128.0f);
+    dcpp::cuda_check(dcpp::launch_attention(a, ctx->stream), "attention");
+  });
+}
+
+dcpp_status dcpp_tp_get_unique_id(void* id_out) {
+  if (!id_out) return DCPP_ERR_INVALID_ARG;
+  try {
+    auto& n = dcpp::Nccl::get();
+    dcpp::Nccl::UniqueId id;
+    if (n.GetUniqueId(&id) != 0) return DCPP_ERR_NCCL;
+    memcpy(id_out, &id, sizeof(id));
+    return DCPP_OK;
+  } catch (const Error& e) {
+    return e.status;
+  }
+}
+
+dcpp_status dcpp_tp_init(dcpp_ctx* ctx, int rank, int nranks, const void* nccl_id) {
+  return guarded(ctx, "dcpp_tp_init", [&] {
+    if (!nccl_id || nranks < 1 || rank < 0 || rank >= nranks) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_tp_init: bad rank");
+    auto& n = dcpp::Nccl::get();
+    dcpp::Nccl::UniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    dcpp::Nccl::Comm comm = nullptr;
+    int r = n.CommInitRank(&comm, nranks, id, rank);
+    if (r != 0) dcpp::fail(DCPP_ERR_NCCL, std::string("ncclCommInitRank: ") + n.GetErrorString(r));
+    ctx->comm = comm;
+    ctx->rank = rank;
+    ctx->nranks = nranks;
+  });
+}
+
+dcpp_status dcpp_allreduce(dcpp_ctx* ctx, void* buf, int64_t count, int dtype) {
+  return guarded(ctx, "dcpp_allreduce", [&] {
+    if (!ctx->comm) dcpp::fail(DCPP_ERR_STATE, "dcpp_allreduce: no TP group (call dcpp_tp_init)");
+    int nd;
+    if (dtype == DCPP_TYPE_F32) nd = 7;        // ncclFloat32
+    else if (dtype == DCPP_TYPE_BF16) nd = 9;  // ncclBfloat16
+    else dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_allreduce: F32 or BF16 only");
+    auto& n = dcpp::Nccl::get();
+    int r = n.AllReduce(buf, buf, static_cast<size_t>(count), nd, /*ncclSum*/ 0, ctx->comm, ctx->stream);
+    if (r != 0) dcpp::fail(DCPP_ERR_NCCL, std::string("ncclAllReduce: ") + n.GetErrorString(r));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,320 @@
+"""Python binding of libdcpp_b200.so, the B200 (sm_100a) Flux2 DiT denoise path.
+
+Thin ctypes wrapper over the C ABI declared in ``include/dcpp.h``; all
+arithmetic runs in the library's CUDA kernels.  There is no fallback: if the
+shared library is missing, importing ``lib()`` raises.
+
+The classes mirror the reference's C++ surface:
+``Flux2Model`` <-> ``Flux2Transformer2DModel`` (config, parameter binding by
+GGUF name, ``forward``) plus ``Flux2KleinPipeline::denoise``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Iterable, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdcpp_b200.so")
+
+DCPP_OK = 0
+STATUS_NAMES = {
+    0: "DCPP_OK", 1: "DCPP_ERR_INVALID_ARG", 2: "DCPP_ERR_UNSUPPORTED", 3: "DCPP_ERR_CUDA",
+    4: "DCPP_ERR_NCCL", 5: "DCPP_ERR_TIMEOUT", 6: "DCPP_ERR_OOM", 7: "DCPP_ERR_STATE",
+    8: "DCPP_ERR_NOT_FOUND", 9: "DCPP_ERR_INJECTED",
+}
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_BF16 = 0, 1, 8, 12, 30
+NCCL_ID_BYTES = 128
+
+_c_i64p = ctypes.POINTER(ctypes.c_int64)
+_vp = ctypes.c_void_p
+
+
+class DcppError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class Flux2ConfigC(ctypes.Structure):
+    _fields_ = [
+        ("patch_size", ctypes.c_int64),
+        ("in_channels", ctypes.c_int64),
+        ("out_channels", ctypes.c_int64),
+        ("num_layers", ctypes.c_int64),
+        ("num_single_layers", ctypes.c_int64),
+        ("attention_head_dim", ctypes.c_int64),
+        ("num_attention_heads", ctypes.c_int64),
+        ("joint_attention_dim", ctypes.c_int64),
+        ("timestep_guidance_channels", ctypes.c_int64),
+        ("mlp_ratio", ctypes.c_float),
+        ("n_axes", ctypes.c_int64),
+        ("axes_dims_rope", ctypes.c_int64 * 8),
+        ("rope_theta", ctypes.c_int64),
+        ("eps", ctypes.c_float),
+        ("guidance_embeds", ctypes.c_int32),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "dcpp_version": (ctypes.c_char_p, []),
+    "dcpp_init": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_vp)]),
+    "dcpp_destroy": (ctypes.c_int, [_vp]),
+    "dcpp_last_error": (ctypes.c_char_p, [_vp]),
+    "dcpp_set_stream": (ctypes.c_int, [_vp, _vp]),
+    "dcpp_synchronize": (ctypes.c_int, [_vp]),
+    "dcpp_alloc": (ctypes.c_int, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp)]),
+    "dcpp_free": (ctypes.c_int, [_vp, _vp]),
+    "dcpp_memcpy": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_size_t]),
+    "dcpp_row_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]),
+    "dcpp_inject_fault": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
+    "dcpp_dequant": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
+    "dcpp_dequant_bf16": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
+    "dcpp_f32_to_bf16": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
+    "dcpp_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, _vp]),
+    "dcpp_layernorm_mod": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_float, _vp]),
+    "dcpp_attention": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp,
+                                      ctypes.c_float, _vp, ctypes.c_int, _c_i64p, ctypes.c_float, _vp]),
+    "dcpp_flux2_config_default": (None, [ctypes.POINTER(Flux2ConfigC)]),
+    "dcpp_flux2_config_from_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(Flux2ConfigC)]),
+    "dcpp_flux2_create": (ctypes.c_int, [_vp, ctypes.POINTER(Flux2ConfigC), ctypes.POINTER(_vp)]),
+    "dcpp_flux2_destroy": (ctypes.c_int, [_vp]),
+    "dcpp_flux2_set_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _c_i64p, _vp, ctypes.c_size_t]),
+    "dcpp_flux2_missing": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t]),
+    "dcpp_flux2_prepare": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]),
+    "dcpp_flux2_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "dcpp_flux2_denoise_step": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]),
+    "dcpp_flux2_load_inputs": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "dcpp_flux2_set_timestep": (ctypes.c_int, [_vp, ctypes.c_float, ctypes.c_float]),
+    "dcpp_flux2_run_resident": (ctypes.c_int, [_vp]),
+    "dcpp_flux2_read_latents": (ctypes.c_int, [_vp, _vp]),
+    "dcpp_flux2_launches_per_step": (ctypes.c_int, [_vp, _c_i64p]),
+    "dcpp_flow_match_schedule": (ctypes.c_int, [ctypes.c_int, ctypes.c_float, _vp, _vp]),
+    "dcpp_tp_get_unique_id": (ctypes.c_int, [_vp]),
+    "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
+    "dcpp_flux2_set_tensor_parallel": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
+}
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libdcpp_b200.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C diffusers-cpp_b200` "
+                               "(or __graft_entry__.build()); there is no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def exported_symbols() -> Iterable[str]:
+    return _SIGNATURES.keys()
+
+
+def _ptr(x) -> Optional[int]:
+    """Address of a torch tensor / numpy array / int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        assert x.is_contiguous(), "tensors passed to dcpp must be contiguous"
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        assert x.flags["C_CONTIGUOUS"]
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+class Context:
+    """dcpp_ctx: one GPU, one stream."""
+
+    def __init__(self, device: int = 0):
+        h = _vp()
+        st = lib().dcpp_init(device, ctypes.byref(h))
+        if st != DCPP_OK:
+            raise DcppError(st, f"dcpp_init({device}) failed")
+        self.h = h
+        self.device = device
+
+    def check(self, status: int, what: str = ""):
+        if status != DCPP_OK:
+            msg = lib().dcpp_last_error(self.h).decode()
+            raise DcppError(status, f"{what}: {msg}" if what else msg)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dcpp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synchronize(self):
+        self.check(lib().dcpp_synchronize(self.h), "synchronize")
+
+    def set_stream(self, stream_ptr: Optional[int]):
+        self.check(lib().dcpp_set_stream(self.h, stream_ptr), "set_stream")
+
+    def inject_fault(self, name: Optional[str], nth: int = 1):
+        lib().dcpp_inject_fault(self.h, name.encode() if name else None, nth)
+
+    # op-level entry points (device pointers)
+    def dequant(self, gtype: int, blocks, n: int, out):
+        self.check(lib().dcpp_dequant(self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant")
+
+    def dequant_bf16(self, gtype: int, blocks, n: int, out):
+        self.check(lib().dcpp_dequant_bf16(self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant_bf16")
+
+    def f32_to_bf16(self, x, n: int, out):
+        self.check(lib().dcpp_f32_to_bf16(self.h, _ptr(x), n, _ptr(out)), "f32_to_bf16")
+
+    def gemm(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
+        self.check(lib().dcpp_gemm(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm")
+
+    def layernorm_mod(self, x, rows: int, D: int, shift, scale, eps: float, y):
+        self.check(lib().dcpp_layernorm_mod(self.h, _ptr(x), rows, D, _ptr(shift), _ptr(scale), eps, _ptr(y)),
+                   "layernorm_mod")
+
+    def attention(self, qkv, B: int, S: int, H: int, norm_q, norm_k, eps: float, ids, axes_dims: Sequence[int],
+                  theta: float, out):
+        arr = (ctypes.c_int64 * len(axes_dims))(*axes_dims)
+        self.check(lib().dcpp_attention(self.h, _ptr(qkv), B, S, H, 128, _ptr(norm_q), _ptr(norm_k), eps, _ptr(ids),
+                                        len(axes_dims), arr, theta, _ptr(out)), "attention")
+
+    # tensor parallelism
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+        st = lib().dcpp_tp_get_unique_id(buf)
+        if st != DCPP_OK:
+            raise DcppError(st, "dcpp_tp_get_unique_id")
+        return buf.raw
+
+    def tp_init(self, rank: int, nranks: int, uid: bytes):
+        buf = ctypes.create_string_buffer(uid, NCCL_ID_BYTES)
+        self.check(lib().dcpp_tp_init(self.h, rank, nranks, buf), "tp_init")
+
+    def allreduce(self, buf, count: int, dtype: int = TYPE_F32):
+        self.check(lib().dcpp_allreduce(self.h, _ptr(buf), count, dtype), "allreduce")
+
+
+def row_bytes(gtype: int, n: int) -> int:
+    out = ctypes.c_size_t()
+    st = lib().dcpp_row_bytes(gtype, n, ctypes.byref(out))
+    if st != DCPP_OK:
+        raise DcppError(st, f"row_bytes({gtype}, {n})")
+    return out.value
+
+
+def config_to_c(cfg) -> Flux2ConfigC:
+    c = Flux2ConfigC()
+    lib().dcpp_flux2_config_default(ctypes.byref(c))
+    for k in ("patch_size", "in_channels", "num_layers", "num_single_layers", "attention_head_dim",
+              "num_attention_heads", "joint_attention_dim", "timestep_guidance_channels", "rope_theta"):
+        setattr(c, k, int(getattr(cfg, k)))
+    c.out_channels = int(cfg.out_channels) if getattr(cfg, "out_channels", None) else -1
+    c.mlp_ratio = float(cfg.mlp_ratio)
+    c.eps = float(cfg.eps)
+    c.guidance_embeds = 1 if cfg.guidance_embeds else 0
+    c.n_axes = len(cfg.axes_dims_rope)
+    for i, d in enumerate(cfg.axes_dims_rope):
+        c.axes_dims_rope[i] = int(d)
+    return c
+
+
+class Flux2Model:
+    """dcpp_flux2: Flux2Transformer2DModel on one GPU (or one TP rank)."""
+
+    def __init__(self, ctx: Context, cfg, tp_rank: int = 0, tp_size: int = 1):
+        self.ctx = ctx
+        self.cfg = cfg
+        c = config_to_c(cfg)
+        h = _vp()
+        ctx.check(lib().dcpp_flux2_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "flux2_create")
+        self.h = h
+        if tp_size > 1:
+            ctx.check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dcpp_flux2_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_param(self, name: str, gtype: int, shape: Sequence[int], data):
+        """`data`: bytes-like / numpy uint8 array / CPU torch uint8 tensor holding raw GGUF bytes."""
+        if hasattr(data, "numpy"):
+            data = data.contiguous().cpu().numpy()
+        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
+        shp = (ctypes.c_int64 * len(shape))(*shape)
+        self.ctx.check(lib().dcpp_flux2_set_param(self.h, name.encode(), gtype, len(shape), shp, arr.ctypes.data,
+                                                  arr.nbytes), f"set_param({name})")
+
+    def load_params(self, params):
+        for name, (gtype, shape, data) in params.items():
+            self.set_param(name, gtype, shape, data)
+
+    def missing(self):
+        n = ctypes.c_int()
+        buf = ctypes.create_string_buffer(512)
+        self.ctx.check(lib().dcpp_flux2_missing(self.h, ctypes.byref(n), buf, 512), "missing")
+        return n.value, buf.value.decode()
+
+    def prepare(self, batch: int, n_img: int, n_txt: int, use_graph: bool = True):
+        self.ctx.check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
+
+    def forward(self, hidden, encoder, timestep, img_ids, txt_ids, out, guidance=None):
+        self.ctx.check(lib().dcpp_flux2_forward(self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
+                                                _ptr(txt_ids), _ptr(guidance), _ptr(out)), "forward")
+
+    def denoise_step(self, latents, encoder, timestep, dt: float, img_ids, txt_ids, latents_out):
+        self.ctx.check(lib().dcpp_flux2_denoise_step(self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
+                                                     _ptr(img_ids), _ptr(txt_ids), _ptr(latents_out)), "denoise_step")
+
+    def load_inputs(self, latents, encoder, img_ids, txt_ids):
+        self.ctx.check(lib().dcpp_flux2_load_inputs(self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
+                                                    _ptr(txt_ids)), "load_inputs")
+
+    def set_timestep(self, timestep: float, dt: float):
+        self.ctx.check(lib().dcpp_flux2_set_timestep(self.h, float(timestep), float(dt)), "set_timestep")
+
+    def run_resident(self):
+        self.ctx.check(lib().dcpp_flux2_run_resident(self.h), "run_resident")
+
+    def read_latents(self, out):
+        self.ctx.check(lib().dcpp_flux2_read_latents(self.h, _ptr(out)), "read_latents")
+
+    def launches_per_step(self) -> int:
+        v = ctypes.c_int64()
+        self.ctx.check(lib().dcpp_flux2_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
+        return v.value
+
+
+def flow_match_schedule(n: int, shift: float = 1.0):
+    ts = np.zeros(n, dtype=np.float32)
+    sg = np.zeros(n + 1, dtype=np.float32)
+    st = lib().dcpp_flow_match_schedule(n, shift, ts.ctypes.data, sg.ctypes.data)
+    if st != DCPP_OK:
+        raise DcppError(st, "flow_match_schedule")
+    return ts, sg

@@ -1,0 +1,161 @@
+"""Seeded synthetic Flux2 parameters and inputs in GGUF layout.
+
+Weights are N(0, 1/fan_in) from a per-tensor seeded torch generator (seed,
+tensor name), quantised with ``quant.py`` following the reference's per-tensor
+type map (utils/convert-model/flux2-klein-9b-q8.json): every projection in the
+blocks and the modulations in the chosen quantised type, the input / output
+projections and the time embedding in BF16, the RMSNorm weights in F32.
+Tensor names are the GGUF names, with the fused tensors the reference's
+loader byte-slices (GGUFLoaderVisitor.cpp:283-430) unless ``split=True``.
+"""
+from __future__ import annotations
+
+import hashlib
+import math
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import TYPE_BF16, TYPE_F32, TYPE_Q4_K, TYPE_Q8_0
+from .quant import quantize
+
+BF16_NAMES = (
+    "x_embedder.weight",
+    "context_embedder.weight",
+    "time_guidance_embed.timestep_embedder.linear_1.weight",
+    "time_guidance_embed.timestep_embedder.linear_2.weight",
+    "time_guidance_embed.guidance_embedder.linear_1.weight",
+    "time_guidance_embed.guidance_embedder.linear_2.weight",
+    "norm_out.linear.weight",
+    "proj_out.weight",
+)
+
+
+@dataclass
+class Flux2Cfg:
+    """Same fields as Flux2Transformer2DModel::Config."""
+    patch_size: int = 1
+    in_channels: int = 128
+    out_channels: Optional[int] = None
+    num_layers: int = 5
+    num_single_layers: int = 20
+    attention_head_dim: int = 128
+    num_attention_heads: int = 24
+    joint_attention_dim: int = 7680
+    timestep_guidance_channels: int = 256
+    mlp_ratio: float = 3.0
+    axes_dims_rope: Tuple[int, ...] = (32, 32, 32, 32)
+    rope_theta: int = 2000
+    eps: float = 1e-6
+    guidance_embeds: bool = False
+
+    @property
+    def inner_dim(self) -> int:
+        return self.num_attention_heads * self.attention_head_dim
+
+    @property
+    def mlp_hidden(self) -> int:
+        return int(self.inner_dim * self.mlp_ratio)
+
+
+def tensor_seed(seed: int, name: str) -> int:
+    h = hashlib.sha256(f"{seed}:{name}".encode()).digest()
+    return int.from_bytes(h[:8], "little") & ((1 << 63) - 1)
+
+
+def param_shapes(cfg: Flux2Cfg, split: bool = False) -> Dict[str, Tuple[int, ...]]:
+    D, F, tg = cfg.inner_dim, cfg.mlp_hidden, cfg.timestep_guidance_channels
+    out_ch = cfg.patch_size ** 2 * (cfg.out_channels or cfg.in_channels)
+    s: Dict[str, Tuple[int, ...]] = {
+        "time_guidance_embed.timestep_embedder.linear_1.weight": (D, tg),
+        "time_guidance_embed.timestep_embedder.linear_2.weight": (D, D),
+        "double_stream_modulation_img.linear.weight": (6 * D, D),
+        "double_stream_modulation_txt.linear.weight": (6 * D, D),
+        "single_stream_modulation.linear.weight": (3 * D, D),
+        "x_embedder.weight": (D, cfg.in_channels),
+        "context_embedder.weight": (D, cfg.joint_attention_dim),
+        "norm_out.linear.weight": (2 * D, D),
+        "proj_out.weight": (out_ch, D),
+    }
+    if cfg.guidance_embeds:
+        s["time_guidance_embed.guidance_embedder.linear_1.weight"] = (D, tg)
+        s["time_guidance_embed.guidance_embedder.linear_2.weight"] = (D, D)
+    hd = cfg.attention_head_dim
+    for i in range(cfg.num_layers):
+        p = f"transformer_blocks.{i}."
+        for n in ("to_q", "to_k", "to_v", "add_q_proj", "add_k_proj", "add_v_proj", "to_add_out", "to_out.0"):
+            s[p + "attn." + n + ".weight"] = (D, D)
+        for n in ("norm_q", "norm_k", "norm_added_q", "norm_added_k"):
+            s[p + "attn." + n + ".weight"] = (hd,)
+        for ff in ("ff", "ff_context"):
+            if split:
+                s[p + ff + ".linear_in_gate.weight"] = (F, D)
+                s[p + ff + ".linear_in_up.weight"] = (F, D)
+            else:
+                s[p + ff + ".linear_in.weight"] = (2 * F, D)
+            s[p + ff + ".linear_out.weight"] = (D, F)
+    for i in range(cfg.num_single_layers):
+        p = f"single_transformer_blocks.{i}.attn."
+        if split:
+            for n in ("q", "k", "v"):
+                s[p + "to_qkv_mlp_proj." + n + ".weight"] = (D, D)
+            s[p + "to_qkv_mlp_proj.mlp_in_gate.weight"] = (F, D)
+            s[p + "to_qkv_mlp_proj.mlp_in_up.weight"] = (F, D)
+            s[p + "to_out.attn.weight"] = (D, D)
+            s[p + "to_out.mlp.weight"] = (D, F)
+        else:
+            s[p + "to_qkv_mlp_proj.weight"] = (3 * D + 2 * F, D)
+            s[p + "to_out.weight"] = (D, D + F)
+        s[p + "norm_q.weight"] = (hd,)
+        s[p + "norm_k.weight"] = (hd,)
+    return s
+
+
+def type_for(name: str, shape, wtype: int) -> int:
+    if len(shape) == 1:
+        return TYPE_F32
+    if name in BF16_NAMES:
+        return TYPE_BF16
+    return wtype
+
+
+def make_params(cfg: Flux2Cfg, wtype: int = TYPE_Q4_K, seed: int = 0, device: str = "cpu", split: bool = False,
+                to_cpu: bool = True):
+    """Dict name -> (ggml type, shape, uint8 tensor of raw GGUF bytes)."""
+    out = {}
+    for name, shape in param_shapes(cfg, split).items():
+        g = torch.Generator(device=device)
+        g.manual_seed(tensor_seed(seed, name))
+        if len(shape) == 1:
+            w = 1.0 + 0.1 * torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+        else:
+            w = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * (1.0 / math.sqrt(shape[1]))
+        t = type_for(name, shape, wtype)
+        q = quantize(w, t).contiguous()
+        if to_cpu:
+            q = q.cpu()
+        out[name] = (t, tuple(shape), q)
+        del w
+    return out
+
+
+def make_inputs(cfg: Flux2Cfg, batch: int, grid_h: int, grid_w: int, n_txt: int, seed: int = 1, device: str = "cpu"):
+    """hidden [B, h*w, in] N(0,1) (seed), encoder [B, n_txt, jd] N(0,1) (seed+1),
+    img_ids [h*w, 4] = [0, y, x, 0], txt_ids [n_txt, 4] = [0, 0, 0, l]
+    (prepare_img_ids / prepare_txt_ids, Flux2KleinPipeline.cpp:26-72)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    n_img = grid_h * grid_w
+    hidden = torch.randn(batch, n_img, cfg.in_channels, generator=g, device=device)
+    g.manual_seed(seed + 1)
+    encoder = torch.randn(batch, n_txt, cfg.joint_attention_dim, generator=g, device=device)
+    ys, xs = torch.meshgrid(torch.arange(grid_h), torch.arange(grid_w), indexing="ij")
+    n_axes = len(cfg.axes_dims_rope)
+    img_ids = torch.zeros(n_img, n_axes, dtype=torch.int32)
+    txt_ids = torch.zeros(n_txt, n_axes, dtype=torch.int32)
+    if n_axes >= 3:
+        img_ids[:, 1] = ys.reshape(-1).int()
+        img_ids[:, 2] = xs.reshape(-1).int()
+    txt_ids[:, n_axes - 1] = torch.arange(n_txt, dtype=torch.int32)
+    return hidden, encoder, img_ids.to(device), txt_ids.to(device)

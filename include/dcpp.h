@@ -1,0 +1,271 @@
+/*
+ * dcpp.h -- C ABI of the B200 (sm_100a) Flux2 DiT denoise path.
+ *
+ * This is the drop-in boundary for the transformer step of diffusers-cpp.
+ * In the reference every model module records ggml ops through the virtual
+ * `Runtime` op set (src/ggml/Runtime.hpp:7-317), `ExecutionRuntime` executes
+ * the graph (src/ggml/ExecutionRuntime.hpp:29-40, .cpp:42-313) and every
+ * arithmetic kernel is a ggml op.  Here the same ops are hand-written CUDA
+ * kernels behind plain `extern "C"` entry points: device or host pointers,
+ * sizes, ggml type ids and an integer status.  No torch and no ggml types
+ * appear in any signature.
+ *
+ * Conventions
+ *   - Every call returns a dcpp_status; DCPP_OK == 0.  On error the context
+ *     keeps a message, read with dcpp_last_error().  Nothing aborts or traps
+ *     on the device: kernels that wait on barriers give up after a bounded
+ *     time and report DCPP_ERR_TIMEOUT.
+ *   - Tensor shapes are given in PyTorch order (outermost first), as in the
+ *     reference's Tensor wrapper (src/ggml/Tensor.hpp:16-401).  A weight of a
+ *     Linear is [out_features, in_features], rows contiguous, quantisation
+ *     blocks running along in_features, exactly as a GGUF file stores it.
+ *   - Pointers named d_* must be device pointers; pointers named p_* may be
+ *     host (pageable or pinned) or device pointers (copied with UVA).
+ *   - A context is bound to one GPU and one CUDA stream.  Calls on one
+ *     context are not re-entrant; use one context per host thread.
+ *   - bf16 values are passed as uint16_t bit patterns.
+ */
+#ifndef DCPP_H
+#define DCPP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference throws std::runtime_error / invalid_argument
+ * (e.g. src/ggml/ExecutionRuntime.cpp:227-228, GGUFLoaderVisitor.cpp:249-250);
+ * the C++ host wrapper (dcpp::check) turns a non-zero status back into a
+ * std::runtime_error carrying dcpp_last_error(). */
+typedef enum dcpp_status {
+    DCPP_OK = 0,
+    DCPP_ERR_INVALID_ARG = 1,  /* bad pointer, size, shape or name          */
+    DCPP_ERR_UNSUPPORTED = 2,  /* type / shape outside what the kernels do  */
+    DCPP_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed      */
+    DCPP_ERR_NCCL = 4,         /* an NCCL call failed                       */
+    DCPP_ERR_TIMEOUT = 5,      /* a bounded device or host wait ran out     */
+    DCPP_ERR_OOM = 6,          /* device allocation failed                  */
+    DCPP_ERR_STATE = 7,        /* call out of order (e.g. missing params)   */
+    DCPP_ERR_NOT_FOUND = 8,    /* unknown parameter name                    */
+    DCPP_ERR_INJECTED = 9      /* host-side fault injection (tests)         */
+} dcpp_status;
+
+/* ggml type ids, numerically identical to ggml's enum ggml_type
+ * (gguf-py 0.19.0 constants.py GGMLQuantizationType). */
+enum {
+    DCPP_TYPE_F32 = 0,
+    DCPP_TYPE_F16 = 1,
+    DCPP_TYPE_Q8_0 = 8,
+    DCPP_TYPE_Q4_K = 12,
+    DCPP_TYPE_BF16 = 30
+};
+
+typedef struct dcpp_ctx dcpp_ctx;
+
+/* ---------------------------------------------------------------------- */
+/* Context, memory, streams                                                */
+/* ---------------------------------------------------------------------- */
+
+/* Library version string and the device architecture it was built for. */
+const char* dcpp_version(void);
+
+/* Create a context on CUDA device `device`.  Replaces the reference's
+ * Backend/Device pair (src/ggml/Backend.hpp:5-31, Device.hpp:8-27). */
+dcpp_status dcpp_init(int device, dcpp_ctx** out_ctx);
+dcpp_status dcpp_destroy(dcpp_ctx* ctx);
+
+/* Message of the last failed call on this context (never NULL). */
+const char* dcpp_last_error(const dcpp_ctx* ctx);
+
+/* Use an external cudaStream_t (NULL = the context's own stream). */
+dcpp_status dcpp_set_stream(dcpp_ctx* ctx, void* cuda_stream);
+dcpp_status dcpp_synchronize(dcpp_ctx* ctx);
+
+dcpp_status dcpp_alloc(dcpp_ctx* ctx, size_t bytes, void** d_out);
+dcpp_status dcpp_free(dcpp_ctx* ctx, void* d_ptr);
+dcpp_status dcpp_memcpy(dcpp_ctx* ctx, void* p_dst, const void* p_src, size_t bytes);
+
+/* Size in bytes of one row of `n` elements of ggml type `type`
+ * (ggml_row_size semantics; n must be a multiple of the block size). */
+dcpp_status dcpp_row_bytes(int type, int64_t n, size_t* out_bytes);
+
+/* Host-side fault injection for failure-path tests: the `nth` next call
+ * (1 = the next one) of entry point `name` (e.g. "dcpp_gemm") returns
+ * DCPP_ERR_INJECTED without touching the GPU.  name == NULL clears. */
+dcpp_status dcpp_inject_fault(dcpp_ctx* ctx, const char* name, int nth);
+
+/* ---------------------------------------------------------------------- */
+/* Op-level entry points (device pointers)                                 */
+/* ---------------------------------------------------------------------- */
+
+/* Dequantise `n` weights of ggml type `type` (Q8_0, Q4_K, F16, BF16, F32)
+ * to f32, bit-identical to gguf-py 0.19.0 dequantize (quants.py:396-401 for
+ * Q8_0, :504-523 for Q4_K), which the reference's tests declare to be what
+ * ggml computes (test/utils/__init__.py:198-228).  n % block size == 0. */
+dcpp_status dcpp_dequant(dcpp_ctx* ctx, int type, const void* d_blocks, int64_t n, float* d_out);
+
+/* Same values rounded to bf16 (round-to-nearest-even); the GEMM operand. */
+dcpp_status dcpp_dequant_bf16(dcpp_ctx* ctx, int type, const void* d_blocks, int64_t n, uint16_t* d_out);
+
+/* Convert f32 -> bf16 (RNE). */
+dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* d_in, int64_t n, uint16_t* d_out);
+
+/* y[M,N] (f32) = x[M,K] (bf16) . W[N,K]^T, W of ggml type wtype.
+ * The ggml_mul_mat(W, x) of Linear::forward (src/nn/Linear.cpp:17-36,
+ * Runtime.hpp:136 mul_mat).  Runs on the tcgen05/TMEM tensor-core GEMM;
+ * quantised W is dequantised inside the GEMM (fused producer) unless
+ * the context's weight mode says otherwise.  K % 64 == 0 for tensor-map
+ * alignment; M, N arbitrary. */
+dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
+                      const uint16_t* d_x, int64_t M, float* d_y);
+
+/* LayerNorm without affine (ggml_norm, eps) followed by adaLN modulation
+ * y = norm(x) * (1 + scale) + shift  (Flux2TransformerBlock.hpp:65-66,
+ * LayerNorm.cpp:16-32).  x f32 [rows, D]; shift/scale f32 [D]; y bf16. */
+dcpp_status dcpp_layernorm_mod(dcpp_ctx* ctx, const float* d_x, int64_t rows, int64_t D,
+                               const float* d_shift, const float* d_scale, float eps,
+                               uint16_t* d_y);
+
+/* Joint attention with the Flux2 prologue fused:
+ *   q,k <- RMSNorm(q|k over head_dim, eps) * w_{q,k}   (RMSNorm.cpp:12-22)
+ *   q,k <- RoPE NORMAL per axis section (Flux2PosEmbed.hpp:18-109) using
+ *          ids[S,n_axes] (int32) and theta
+ *   o    = softmax(q k^T / sqrt(head_dim)) v            (FlashAttentionOp.cpp)
+ * qkv: bf16 [B, S, 3, H, head_dim] (the fused q|k|v projection output rows);
+ * o: bf16 [B, S, H, head_dim].  head_dim == 128; axes_dims sum to 128. */
+dcpp_status dcpp_attention(dcpp_ctx* ctx, const uint16_t* d_qkv, int64_t B, int64_t S, int64_t H,
+                           int64_t head_dim, const float* d_norm_q, const float* d_norm_k, float eps,
+                           const int32_t* d_ids, int n_axes, const int64_t* axes_dims, float theta,
+                           uint16_t* d_out);
+
+/* ---------------------------------------------------------------------- */
+/* Model-level entry points: Flux2Transformer2DModel + Euler step          */
+/* ---------------------------------------------------------------------- */
+
+/* Mirrors Flux2Transformer2DModel::Config (Flux2Transformer2DModel.hpp:10-31). */
+typedef struct dcpp_flux2_config {
+    int64_t patch_size;                 /* 1                          */
+    int64_t in_channels;                /* 128                        */
+    int64_t out_channels;               /* <= 0: same as in_channels  */
+    int64_t num_layers;                 /* double-stream blocks       */
+    int64_t num_single_layers;          /* single-stream blocks       */
+    int64_t attention_head_dim;         /* 128                        */
+    int64_t num_attention_heads;
+    int64_t joint_attention_dim;
+    int64_t timestep_guidance_channels; /* 256                        */
+    float mlp_ratio;                    /* 3.0                        */
+    int64_t n_axes;                     /* entries used in axes_dims_rope */
+    int64_t axes_dims_rope[8];          /* {32,32,32,32}              */
+    int64_t rope_theta;                 /* 2000                       */
+    float eps;                          /* 1e-6                       */
+    int32_t guidance_embeds;            /* 0 / 1                      */
+} dcpp_flux2_config;
+
+typedef struct dcpp_flux2 dcpp_flux2;
+
+/* Fill `cfg` with the reference's defaults (Flux2Transformer2DModel.hpp:13-30). */
+void dcpp_flux2_config_default(dcpp_flux2_config* cfg);
+
+/* Parse a diffusers transformer/config.json (Config::from_file,
+ * Flux2Transformer2DModel.cpp:322-353) into `cfg` (defaults kept for
+ * missing keys). */
+dcpp_status dcpp_flux2_config_from_file(const char* path, dcpp_flux2_config* cfg);
+
+/* Build the module tree (Flux2Transformer2DModel.cpp:104-178).  Device
+ * memory for parameters is allocated as they are set. */
+dcpp_status dcpp_flux2_create(dcpp_ctx* ctx, const dcpp_flux2_config* cfg, dcpp_flux2** out_model);
+dcpp_status dcpp_flux2_destroy(dcpp_flux2* model);
+
+/* Bind one parameter by its GGUF / module-path name (ModulePath.hpp:7-44),
+ * e.g. "single_transformer_blocks.3.attn.to_qkv_mlp_proj.weight".  Accepts
+ * the fused GGUF tensors (to_qkv_mlp_proj, to_out, ff.linear_in) that the
+ * reference's loader byte-slices (GGUFLoaderVisitor.cpp:283-430) as well as
+ * the split per-module names.  Shapes are checked like Parameter::set /
+ * GGUFLoaderVisitor::visit (:244-250).  `p_data` holds the raw GGUF bytes. */
+dcpp_status dcpp_flux2_set_param(dcpp_flux2* model, const char* name, int type, int n_dims,
+                                 const int64_t* shape, const void* p_data, size_t nbytes);
+
+/* Number of parameters still unbound; `first_missing` gets one name. */
+dcpp_status dcpp_flux2_missing(dcpp_flux2* model, int* count, char* first_missing, size_t cap);
+
+/* Plan the execution for a problem size: batch B, n_img image tokens and
+ * n_txt text tokens.  Allocates the activation arena, encodes tensor maps
+ * and (if use_graph) captures the per-step CUDA graph on first use. */
+dcpp_status dcpp_flux2_prepare(dcpp_flux2* model, int64_t batch, int64_t n_img, int64_t n_txt,
+                               int use_graph);
+
+/* Flux2Transformer2DModel::forward (Flux2Transformer2DModel.cpp:180-300):
+ *   hidden [B, n_img, in_channels] f32, encoder [B, n_txt, joint_dim] f32,
+ *   timestep [B] f32 (in [0,1]; multiplied by 1000 inside, :199),
+ *   img_ids [B?, n_img, n_axes] int32, txt_ids [B?, n_txt, n_axes] int32
+ *   (one id set shared by the batch), guidance [B] f32 or NULL,
+ *   out [B, n_img, out_channels] f32.  p_* are host or device pointers. */
+dcpp_status dcpp_flux2_forward(dcpp_flux2* model, const float* p_hidden, const float* p_encoder,
+                               const float* p_timestep, const int32_t* p_img_ids,
+                               const int32_t* p_txt_ids, const float* p_guidance, float* p_out);
+
+/* Flux2KleinPipeline::denoise (Flux2KleinPipeline.cpp:496-537) for one
+ * schedule step: latents <- latents + dt * forward(latents, ...), with the
+ * Euler update (FlowMatchEulerDiscreteScheduler.cpp:210-222) fused into the
+ * final projection.  `timestep` is sigma in [0,1] per batch element. */
+dcpp_status dcpp_flux2_denoise_step(dcpp_flux2* model, const float* p_latents_in,
+                                    const float* p_encoder, const float* p_timestep, float dt,
+                                    const int32_t* p_img_ids, const int32_t* p_txt_ids,
+                                    float* p_latents_out);
+
+/* Resident execution, for callers that keep the latent on the device across
+ * the schedule (the reference instead copies the latent through host
+ * memory every step, ExecutionRuntime.cpp:218-238,302-313):
+ *   load_inputs  copies latents / encoder states / ids into the model's
+ *                device buffers once;
+ *   set_timestep sets the step's timestep (sigma) and dt;
+ *   run_resident runs one denoise step on the resident latent in place;
+ *   read_latents copies the current latent out (and synchronises). */
+dcpp_status dcpp_flux2_load_inputs(dcpp_flux2* model, const float* p_latents, const float* p_encoder,
+                                   const int32_t* p_img_ids, const int32_t* p_txt_ids);
+dcpp_status dcpp_flux2_set_timestep(dcpp_flux2* model, float timestep, float dt);
+dcpp_status dcpp_flux2_run_resident(dcpp_flux2* model);
+dcpp_status dcpp_flux2_read_latents(dcpp_flux2* model, float* p_out);
+
+/* Number of this library's kernel launches in one denoise step. */
+dcpp_status dcpp_flux2_launches_per_step(dcpp_flux2* model, int64_t* out);
+
+/* FlowMatchEulerDiscreteScheduler::schedule (.cpp:68-208) with the
+ * pipeline's sigmas 1 - i/n (Flux2KleinPipeline.cpp:348-356) and the
+ * default (shift 1, no dynamic shift) scheduler: writes n timesteps
+ * (1000*sigma) and n+1 sigmas. */
+dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float* sigmas);
+
+/* ---------------------------------------------------------------------- */
+/* Tensor parallelism (the sharding planner's column/row layout)           */
+/* ---------------------------------------------------------------------- */
+
+/* Size of the opaque NCCL unique id blob (ncclUniqueId). */
+#define DCPP_NCCL_ID_BYTES 128
+
+/* Rank 0 creates the id; all ranks pass it to dcpp_tp_init.  NCCL is
+ * loaded at run time (dlopen of libnccl.so.2). */
+dcpp_status dcpp_tp_get_unique_id(void* id_out /* DCPP_NCCL_ID_BYTES */);
+
+/* Join a tensor-parallel group of `nranks` GPUs (one process per GPU).
+ * Replaces the reference's meta-backend device mesh (MetaDevice.hpp:24-111)
+ * and its AllReduce at every P->R bridge (ShardingRuntime.hpp:1082-1091). */
+dcpp_status dcpp_tp_init(dcpp_ctx* ctx, int rank, int nranks, const void* nccl_id);
+
+/* In-place sum all-reduce over the TP group (ncclAllReduce); dtype is a
+ * DCPP_TYPE_* (F32 or BF16). */
+dcpp_status dcpp_allreduce(dcpp_ctx* ctx, void* d_buf, int64_t count, int dtype);
+
+/* Shard a model created on this context: rank keeps heads/nranks heads and
+ * mlp_hidden/nranks MLP features.  Must be called before set_param.  The
+ * split follows ShardingRuntime.cpp:47-57 (column-parallel q/k/v/gate/up,
+ * row-parallel out projections, one all-reduce per row-parallel site). */
+dcpp_status dcpp_flux2_set_tensor_parallel(dcpp_flux2* model, int rank, int nranks);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DCPP_H */
