@@ -1,0 +1,385 @@
+"""Benchmark of the Flux2 DiT denoise step (BASELINE.json metric: DiT denoise
+steps/s at 1024^2, Q4_K, on 1/2/4/8 B200, plus tensor-pipe fraction of peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3]
+
+One step = one Flux2Transformer2DModel::forward + Euler update on the
+resident latent (hidden 3072, 24 heads x 128, 5 double +
+20 single blocks, Q4_K weights, 4096 image + 512 text tokens, batch 1).
+For N > 1 it is launched under torchrun, one process per GPU, and the model
+runs tensor-parallel over the N GPUs (column / row-parallel projections with
+an NCCL all-reduce after each row-parallel site); the total work per step is
+fixed, so scaling is "strong".
+
+--impl reference times the reference's CPU path on this box's host cores.
+The reference's ggml CPU backend cannot be built here (its ggml submodule is
+not vendored), so this leg runs the CPU restatement of the same forward
+(oracle/flux2_oracle.py, float32, all host threads) on a bounded sample of
+the step: one double-stream and one single-stream block at full size, plus
+the embeddings and output layers, extrapolated to the 5 + 20 blocks.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "diffusers-cpp_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "DiT denoise steps/s at 1024^2 (Q4_K)"
+
+CONFIGS = {
+    # full-depth Flux2-style DiT on 1 B200.
+    "2": dict(model=dict(num_layers=5, num_single_layers=20, num_attention_heads=24, joint_attention_dim=7680,
+                         in_channels=128, guidance_embeds=False),
+              wtype="Q4_K", batch=1, grid=(64, 64), n_txt=512,
+              workload="config2: full-depth Flux2 DiT (D 3072, 24x128 heads, 5 double + 20 single), Q4_K, "
+                       "B=1, 4096 img + 512 txt tokens, 4-step flow-match Euler schedule"),
+    # larger DiT, tensor-parallel.
+    "3": dict(model=dict(num_layers=8, num_single_layers=24, num_attention_heads=32, joint_attention_dim=12288,
+                         in_channels=128, guidance_embeds=False),
+              wtype="Q8_0", batch=2, grid=(64, 64), n_txt=512,
+              workload="config3: Flux2 DiT (D 4096, 32x128 heads, 8 double + 24 single), Q8_0, "
+                       "B=2, 4096 img + 512 txt tokens, 4-step flow-match Euler schedule"),
+}
+
+
+def algorithmic_flops(cfg, batch, n_img, n_txt):
+    """FLOPs of one DiT forward: per block 2*S*13*D^2 + 4*S^2*D, embedders,
+    batch-1 GEMVs; per batch element."""
+    D = cfg.inner_dim
+    S = n_img + n_txt
+    blocks = cfg.num_layers + cfg.num_single_layers
+    per = blocks * (2 * S * 13 * D * D + 4 * S * S * D)
+    per += 2 * n_img * cfg.in_channels * D * 2 + 2 * n_txt * cfg.joint_attention_dim * D
+    per += 2 * (15 * D * D + 2 * D * D + 256 * D + D * D)
+    return batch * per
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- reference arm
+def cpu_sample(cfg_name, steps, warmup, threads):
+    """Time the CPU restatement on a bounded sample of one step; returns
+    (seconds per step, sample description)."""
+    import torch
+
+    import flux2_oracle as fo
+    from dcpp_b200 import synth
+
+    spec = CONFIGS[cfg_name]
+    torch.set_num_threads(threads)
+    full = synth.Flux2Cfg(**spec["model"])
+    sample_cfg = synth.Flux2Cfg(**{**spec["model"], "num_layers": 1, "num_single_layers": 1})
+    wt = {"Q4_K": 12, "Q8_0": 8}[spec["wtype"]]
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    params = synth.make_params(sample_cfg, wt, seed=0, device=dev)
+    gh, gw = spec["grid"]
+    hid, enc, iid, tid = synth.make_inputs(sample_cfg, spec["batch"], gh, gw, spec["n_txt"], seed=1)
+    ocfg = fo.Config(**{k: getattr(sample_cfg, k) for k in fo.Config.__dataclass_fields__})
+    orc = fo.Flux2Oracle(ocfg, params, dtype=torch.float32)
+    t = torch.full((spec["batch"],), 0.75)
+    # Pre-dequantise the sample's weights (the ggml path keeps quantised
+    # weights; dequantisation is not part of the timed sample).
+    orc.forward(hid[:, :64], enc[:, :16], t, iid[:64], tid[:16], n_double=1, n_single=1)
+
+    def one():
+        t0 = time.perf_counter()
+        orc.forward(hid, enc, t, iid, tid, n_double=0, n_single=0)
+        t1 = time.perf_counter()
+        orc.forward(hid, enc, t, iid, tid, n_double=1, n_single=0)
+        t2 = time.perf_counter()
+        orc.forward(hid, enc, t, iid, tid, n_double=0, n_single=1)
+        t3 = time.perf_counter()
+        base = t1 - t0
+        dbl = (t2 - t1) - base
+        sgl = (t3 - t2) - base
+        return base + full.num_layers * dbl + full.num_single_layers * sgl
+
+    for _ in range(warmup):
+        one()
+    times = [one() for _ in range(steps)]
+    desc = (f"CPU restatement (oracle/flux2_oracle.py, torch float32, {threads} threads) of {spec['workload']}; "
+            f"each step = 1 double + 1 single block at full size plus embeddings/output, extrapolated to "
+            f"{full.num_layers} + {full.num_single_layers} blocks; ggml CPU path unavailable (submodule not vendored)")
+    return statistics.median(times), desc
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sec, desc = cpu_sample(args.config, args.steps, args.warmup, threads)
+    value = 1.0 / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": CONFIGS[args.config]["workload"], "global_batch": CONFIGS[args.config]["batch"],
+                   "seq_len": CONFIGS[args.config]["grid"][0] * CONFIGS[args.config]["grid"][1] + CONFIGS[args.config]["n_txt"],
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import dcpp_b200
+    from dcpp_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+
+    spec = CONFIGS[args.config]
+    cfg = synth.Flux2Cfg(**spec["model"])
+    wt = {"Q4_K": dcpp_b200.TYPE_Q4_K, "Q8_0": dcpp_b200.TYPE_Q8_0}[spec["wtype"]]
+    B, (gh, gw), nt = spec["batch"], spec["grid"], spec["n_txt"]
+    ni = gh * gw
+
+    ctx = dcpp_b200.Context(local)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    if world > 1:
+        uid = [dcpp_b200.Context.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.tp_init(rank, world, uid[0])
+    model = dcpp_b200.Flux2Model(ctx, cfg, tp_rank=rank, tp_size=world)
+    model.set_profiling(True)
+    t0 = time.time()
+    params = synth.make_params(cfg, wt, seed=0, device="cuda", to_cpu=False)
+    for name, (gt, shp, data) in params.items():
+        model.set_param(name, gt, shp, data.cpu())
+    del params
+    torch.cuda.empty_cache()
+    load_s = time.time() - t0
+    model.prepare(B, ni, nt, use_graph=not args.no_graph)
+
+    hid, enc, iid, tid = synth.make_inputs(cfg, B, gh, gw, nt, seed=1)
+    hid_p, enc_p = hid.pin_memory(), enc.pin_memory()
+    out_p = torch.empty_like(hid).pin_memory()
+    ts, sg = dcpp_b200.flow_match_schedule(4)
+    sched = [(float(ts[i]) / 1000.0, float(sg[i + 1] - sg[i])) for i in range(4)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timing (value)
+    model.load_inputs(hid_p, enc_p, iid, tid)
+    for i in range(args.warmup):
+        model.set_timestep(*sched[i % 4])
+        model.run_resident()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for i in range(args.steps):
+        model.set_timestep(*sched[i % 4])
+        model.run_resident()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    barrier()
+    # per-kind kernel times of the last timed step (event nodes in the graph)
+    prof = {k: model.profile(k) for k in dcpp_b200.Flux2Model.PROFILE_KINDS}
+    model.read_latents(out_p)
+    assert torch.isfinite(out_p).all(), "non-finite latents"
+
+    # ---- end-to-end through the public C ABI with host buffers (e2e)
+    for i in range(min(args.warmup, 2)):
+        model.denoise_step(hid_p, enc_p, torch.tensor([sched[0][0]]), sched[0][1], iid, tid, out_p)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tsteps = [torch.tensor([s[0]], dtype=torch.float32) for s in sched]
+    for i in range(args.steps):
+        model.denoise_step(hid_p, enc_p, tsteps[i % 4], sched[i % 4][1], iid, tid, out_p)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    barrier()
+
+    # max over ranks
+    vals = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(vals[0]), float(vals[1])
+    launches = model.launches_per_step()
+
+    if rank == 0:
+        peak_b, peak_s, hbm, peak_src = measured_peaks()
+        g_ms, g_fl, g_n = prof["gemm"]
+        achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else 0.0
+        step_flops = algorithmic_flops(cfg, B, ni, nt)
+        h2d = hid.numel() * 4 + enc.numel() * 4 + iid.numel() * 4 + tid.numel() * 4 + 4 * B + 4
+        d2h = hid.numel() * 4
+        line = {
+            "metric": METRIC,
+            "value": 1000.0 / ms,
+            "unit": "steps/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1/fan_in) weights quantised to %s; N(0,1) inputs)" % spec["wtype"],
+            "config": {
+                "workload": spec["workload"],
+                "global_batch": B,
+                "seq_len": ni + nt,
+                "parallelism": f"tp{world}",
+                "weights": spec["wtype"],
+                "l2": "no flush: each step streams > 2 GB of weights, far above the 126 MB L2",
+                "cuda_graph": not args.no_graph,
+            },
+            "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "dcpp_flux2_denoise_step with pinned host latents/encoder/ids in, latents out"},
+            "gpu_launches": launches * args.steps,
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "gemm_bf16_kernel (tcgen05 grouped GEMM)",
+                "achieved": achieved,
+                "peak": peak_s,
+                "unit": "TFLOP/s",
+                "frac": achieved / peak_s if peak_s else None,
+                "peak_kind": f"bf16 sustained ({peak_src})",
+                "traffic": None,
+                "gemm_ms_per_step": g_ms,
+                "gemm_launches_per_step": g_n,
+                "step_tflops": step_flops / 1e12,
+                "step_frac_of_peak": step_flops / (ms * 1e-3) / 1e12 / peak_s,
+            },
+            "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
+            "attention_tflops": (prof["attention"][1] / (prof["attention"][0] * 1e-3) / 1e12
+                                 if prof["attention"][0] > 0 else None),
+            "clocks": clk,
+            "load_seconds": load_s,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                threads = os.cpu_count() or 1
+                sec, desc = cpu_sample(args.config, 1, 0, threads)
+                line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "steps/s", "cores": threads, "kind": "port",
+                                        "sample": desc}
+            except Exception as e:  # the baseline is reported, never the target
+                line["cpu_baseline"] = {"value": None, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+                                        "sample": f"failed: {e}"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="2")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

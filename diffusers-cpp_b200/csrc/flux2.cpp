@@ -234,6 +234,7 @@ Flux2Transformer2DModel::~Flux2Transformer2DModel() {
     if (w->data) cudaFree(w->data);
   for (auto* v : vectors_)
     if (v->data) cudaFree(v->data);
+  for (auto e : ev_) cudaEventDestroy(e);
 }
 
 void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks) {
@@ -543,6 +544,7 @@ void Flux2Transformer2DModel::free_plan() {
   ops_fwd_.clear();
   step_ops_[0].clear();
   step_ops_[1].clear();
+  last_ops_ = nullptr;
   planned_ = false;
 }
 
@@ -595,7 +597,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     building_->push_back({[w, dst](cudaStream_t s) {
                             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
                           },
-                          1});
+                          1, kOpDequant});
   }
   if (w1 && w1->type != kTypeBF16) {
     const DevWeight* w = w1;
@@ -603,16 +605,18 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     building_->push_back({[w, dst](cudaStream_t s) {
                             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
                           },
-                          1});
+                          1, kOpDequant});
   }
+  double flops = 0.0;
+  for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
   building_->push_back({[st, args, c](cudaStream_t s) {
                           cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
                         },
-                        1});
+                        1, kOpGemm, flops});
 }
 
 void Flux2Transformer2DModel::add_norm(const NormArgs& a) {
-  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1});
+  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm});
 }
 
 void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y) {
@@ -622,7 +626,7 @@ void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int a
                           cuda_check(launch_gemv(pw->type, pw->data, pw->rows, pw->cols, x, B, act_in, act_out, y, s),
                                      "gemv");
                         },
-                        1});
+                        1, kOpGemv, 2.0 * B * static_cast<double>(pw->rows) * static_cast<double>(pw->cols)});
 }
 
 void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
@@ -632,7 +636,7 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
                           int r = n.AllReduce(buf, buf, static_cast<size_t>(count), 7, 0, c->comm, s);
                           if (r != 0) fail(DCPP_ERR_NCCL, std::string("ncclAllReduce: ") + n.GetErrorString(r));
                         },
-                        0});
+                        0, kOpAllreduce});
 }
 
 void Flux2Transformer2DModel::build_plan() {
@@ -814,7 +818,8 @@ void Flux2Transformer2DModel::build_plan() {
     at.S = static_cast<int32_t>(S);
     at.scale = 1.0f / std::sqrt(static_cast<float>(cfg_.attention_head_dim));
     auto attn_op = [&]() {
-      ops.push_back({[at](cudaStream_t s) { cuda_check(launch_attention(at, s), "attention"); }, 1});
+      ops.push_back({[at](cudaStream_t s) { cuda_check(launch_attention(at, s), "attention"); }, 1, kOpAttention,
+                     4.0 * at.B * at.H * static_cast<double>(at.S) * static_cast<double>(at.S) * 128.0});
     };
     auto out_epi = [&](const float* g0, const float* g1, int64_t bstride) {
       EpilogueArgs e{};
@@ -933,15 +938,34 @@ namespace dcpp {
 // ----------------------------------------------------------------- execution
 void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph) {
   cudaStream_t s = ctx_.stream;
+  last_ops_ = &ops;
+  auto issue = [&]() {
+    if (!profiling_) {
+      for (auto& o : ops) o.fn(s);
+      return;
+    }
+    if (ev_.size() < 2 * ops.size()) {
+      for (size_t i = ev_.size(); i < 2 * ops.size(); ++i) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+        ev_.push_back(e);
+      }
+    }
+    for (size_t i = 0; i < ops.size(); ++i) {
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], s, cudaEventRecordExternal), "event record");
+      ops[i].fn(s);
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], s, cudaEventRecordExternal), "event record");
+    }
+  };
   if (!use_graph_) {
-    for (auto& o : ops) o.fn(s);
+    issue();
     return;
   }
   if (!*graph) {
     cudaGraph_t g = nullptr;
     cuda_check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
-      for (auto& o : ops) o.fn(s);
+      issue();
     } catch (...) {
       cudaStreamEndCapture(s, &g);
       if (g) cudaGraphDestroy(g);
@@ -1020,6 +1044,33 @@ void Flux2Transformer2DModel::run_resident_step() {
   if (step_ops_[0].empty()) fail(DCPP_ERR_UNSUPPORTED, "denoise needs out_channels == in_channels");
   run_ops(step_ops_[cur_], &graph_step_[cur_]);
   cur_ ^= 1;
+}
+
+void Flux2Transformer2DModel::set_profiling(bool on) {
+  if (on == profiling_) return;
+  cudaStreamSynchronize(ctx_.stream);
+  free_plan();
+  profiling_ = on;
+}
+
+void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64_t* launches) {
+  if (!profiling_) fail(DCPP_ERR_STATE, "profiling is off (dcpp_flux2_set_profiling before prepare)");
+  if (!last_ops_) fail(DCPP_ERR_STATE, "no step has run yet");
+  cuda_check(cudaStreamSynchronize(ctx_.stream), "sync");
+  double t = 0.0, f = 0.0;
+  int64_t n = 0;
+  for (size_t i = 0; i < last_ops_->size(); ++i) {
+    const Op& o = (*last_ops_)[i];
+    if (o.kind != kind) continue;
+    float e = 0.f;
+    cuda_check(cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]), "cudaEventElapsedTime");
+    t += e;
+    f += o.flops;
+    n += o.launches;
+  }
+  if (ms) *ms = t;
+  if (flops) *flops = f;
+  if (launches) *launches = n;
 }
 
 void Flux2Transformer2DModel::read_latents(float* out) {
@@ -1168,6 +1219,17 @@ dcpp_status dcpp_flux2_launches_per_step(dcpp_flux2* m, int64_t* out) {
   return model_call(m, "dcpp_flux2_launches_per_step", [&](dcpp::Flux2Transformer2DModel& mm) {
     if (!out) dcpp::fail(DCPP_ERR_INVALID_ARG, "null output");
     *out = mm.launches_per_step();
+  });
+}
+
+dcpp_status dcpp_flux2_set_profiling(dcpp_flux2* m, int on) {
+  return model_call(m, "dcpp_flux2_set_profiling", [&](dcpp::Flux2Transformer2DModel& mm) { mm.set_profiling(on != 0); });
+}
+
+dcpp_status dcpp_flux2_profile(dcpp_flux2* m, int kind, double* ms, double* flops, int64_t* launches) {
+  return model_call(m, "dcpp_flux2_profile", [&](dcpp::Flux2Transformer2DModel& mm) {
+    if (kind < 0 || kind >= dcpp::Flux2Transformer2DModel::kOpKinds) dcpp::fail(DCPP_ERR_INVALID_ARG, "bad kind");
+    mm.profile(kind, ms, flops, launches);
   });
 }
 

@@ -102,6 +102,14 @@ class Flux2Transformer2DModel {
   void read_latents(float* out);
   int64_t launches_per_step() const { return launches_per_step_; }
 
+  // Profiling: when on (set before prepare), every kernel op of a step is
+  // bracketed by CUDA event records (captured into the graph as event
+  // nodes); profile() sums the last executed step's times per op kind.
+  enum ProfileKind { kOpGemm = 0, kOpAttention = 1, kOpNorm = 2, kOpGemv = 3, kOpDequant = 4, kOpOther = 5,
+                     kOpAllreduce = 6, kOpKinds = 7 };
+  void set_profiling(bool on);
+  void profile(int kind, double* ms, double* flops, int64_t* launches);
+
  private:
   struct DoubleBlock {
     DevWeight qkv[2], out[2], ff_in[2], ff_out[2];  // [0] txt stream, [1] img stream
@@ -114,6 +122,8 @@ class Flux2Transformer2DModel {
   struct Op {
     std::function<void(cudaStream_t)> fn;
     int launches;
+    int kind = kOpOther;   // ProfileKind
+    double flops = 0.0;    // algorithmic FLOPs of the op
   };
 
   void build_registry();
@@ -170,6 +180,9 @@ class Flux2Transformer2DModel {
   std::vector<Op> step_ops_[2];    // denoise step plans (Euler fused), per latent parity
   std::vector<Op>* building_ = nullptr;
   cudaGraphExec_t graph_fwd_ = nullptr, graph_step_[2] = {nullptr, nullptr};
+  bool profiling_ = false;
+  std::vector<Op>* last_ops_ = nullptr;
+  std::vector<cudaEvent_t> ev_;  // 2 per op of the largest plan
   int64_t launches_per_step_ = 0;
 };
 

@@ -186,9 +186,11 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     tmem_ld32(taddr + c * 32, r);
     tmem_ld_wait();
     if (!row_ok || cb >= p.N) continue;
-    const bool full = cb + 32 <= p.N;
+    // Vector stores need 16-byte aligned rows (ld_out % 4 floats / % 8 bf16).
+    bool full = cb + 32 <= p.N;
     if (e.mode == kEpiBf16) {
       uint16_t* dst = e.out_bf16 + row * e.ld_out + cb;
+      full = full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
       if (full) {
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -209,6 +211,9 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       continue;
     }
     float* dst = e.out_f32 + row * e.ld_out + cb;
+    full = full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) &&
+           (!gate || (reinterpret_cast<uintptr_t>(gate + cb) & 15) == 0) &&
+           (e.mode != kEpiEuler || (reinterpret_cast<uintptr_t>(e.x_in + row * e.ld_out + cb) & 15) == 0);
     if (full) {
       float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from typing import Iterable, Optional, Sequence
 
 import numpy as np
@@ -93,6 +94,9 @@ _SIGNATURES = {
     "dcpp_flux2_run_resident": (ctypes.c_int, [_vp]),
     "dcpp_flux2_read_latents": (ctypes.c_int, [_vp, _vp]),
     "dcpp_flux2_launches_per_step": (ctypes.c_int, [_vp, _c_i64p]),
+    "dcpp_flux2_set_profiling": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "dcpp_flux2_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_double), _c_i64p]),
     "dcpp_flow_match_schedule": (ctypes.c_int, [ctypes.c_int, ctypes.c_float, _vp, _vp]),
     "dcpp_tp_get_unique_id": (ctypes.c_int, [_vp]),
     "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
@@ -148,6 +152,7 @@ class Context:
             raise DcppError(st, f"dcpp_init({device}) failed")
         self.h = h
         self.device = device
+        self._children = weakref.WeakSet()
 
     def check(self, status: int, what: str = ""):
         if status != DCPP_OK:
@@ -156,6 +161,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            for child in list(self._children):
+                child.close()
             lib().dcpp_destroy(self.h)
             self.h = None
 
@@ -248,6 +255,7 @@ class Flux2Model:
         h = _vp()
         ctx.check(lib().dcpp_flux2_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "flux2_create")
         self.h = h
+        ctx._children.add(self)
         if tp_size > 1:
             ctx.check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
 
@@ -304,6 +312,17 @@ class Flux2Model:
 
     def read_latents(self, out):
         self.ctx.check(lib().dcpp_flux2_read_latents(self.h, _ptr(out)), "read_latents")
+
+    PROFILE_KINDS = {"gemm": 0, "attention": 1, "norm": 2, "gemv": 3, "dequant": 4, "other": 5, "allreduce": 6}
+
+    def set_profiling(self, on: bool):
+        self.ctx.check(lib().dcpp_flux2_set_profiling(self.h, 1 if on else 0), "set_profiling")
+
+    def profile(self, kind: str):
+        ms, fl, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+        self.ctx.check(lib().dcpp_flux2_profile(self.h, self.PROFILE_KINDS[kind], ctypes.byref(ms), ctypes.byref(fl),
+                                                ctypes.byref(n)), "profile")
+        return ms.value, fl.value, n.value
 
     def launches_per_step(self) -> int:
         v = ctypes.c_int64()

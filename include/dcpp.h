@@ -232,6 +232,16 @@ dcpp_status dcpp_flux2_read_latents(dcpp_flux2* model, float* p_out);
 /* Number of this library's kernel launches in one denoise step. */
 dcpp_status dcpp_flux2_launches_per_step(dcpp_flux2* model, int64_t* out);
 
+/* Per-kernel timing of the executed step (no counterpart in the reference,
+ * which has only a progress bar).  With profiling on (set before prepare),
+ * every kernel launch of a step is bracketed by CUDA event records, which
+ * the step's CUDA graph replays; dcpp_flux2_profile sums, for one kind
+ * (0 GEMM, 1 attention, 2 LayerNorm, 3 GEMV, 4 dequant, 5 other,
+ * 6 all-reduce), the last executed step's milliseconds, algorithmic FLOPs
+ * and launch count. */
+dcpp_status dcpp_flux2_set_profiling(dcpp_flux2* model, int on);
+dcpp_status dcpp_flux2_profile(dcpp_flux2* model, int kind, double* ms, double* flops, int64_t* launches);
+
 /* FlowMatchEulerDiscreteScheduler::schedule (.cpp:68-208) with the
  * pipeline's sigmas 1 - i/n (Flux2KleinPipeline.cpp:348-356) and the
  * default (shift 1, no dynamic shift) scheduler: writes n timesteps
