@@ -43,27 +43,47 @@ __device__ __forceinline__ void store_val(void* out, int64_t i, float v) {
   }
 }
 
-// One thread per 32-weight Q8_0 block.
+// Eight consecutive outputs per thread, written as one 16-byte (bf16) or
+// two 16-byte (f32) stores, so a warp writes 512 / 1024 contiguous bytes.
 template <bool kBf16>
-__global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
-  int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (b >= nblocks) return;
-  const uint8_t* blk = blocks + b * 34;
-  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
-#pragma unroll 8
-  for (int i = 0; i < 32; ++i) {
-    const float q = static_cast<float>(static_cast<int8_t>(blk[2 + i]));
-    store_val<kBf16>(out, b * 32 + i, __fmul_rn(q, d));
+__device__ __forceinline__ void store8(void* out, int64_t i0, const float (&v)[8]) {
+  if (kBf16) {
+    uint4 o = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                         pack_bf16x2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + i0) = o;
+  } else {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i0);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
 }
 
-// One thread per 32-weight sub-block of a Q4_K super-block.
+// One thread per 8 weights of a Q8_0 block (4 threads per block).
+template <bool kBf16>
+__global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
+  int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (t >= nblocks * 4) return;
+  const int64_t b = t >> 2;
+  const int part = static_cast<int>(t & 3);
+  const uint8_t* blk = blocks + b * 34;
+  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float q = static_cast<float>(static_cast<int8_t>(blk[2 + part * 8 + i]));
+    v[i] = __fmul_rn(q, d);
+  }
+  store8<kBf16>(out, b * 32 + part * 8, v);
+}
+
+// One thread per 8 weights of a Q4_K super-block (32 threads per block).
 template <bool kBf16>
 __global__ void dequant_q4_k_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
   int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (t >= nblocks * 8) return;
-  const int64_t b = t >> 3;
-  const int j = static_cast<int>(t & 7);
+  if (t >= nblocks * 32) return;
+  const int64_t b = t >> 5;
+  const int j = static_cast<int>((t >> 2) & 7);  // sub-block
+  const int l0 = static_cast<int>(t & 3) * 8;    // first element within the sub-block
   const uint8_t* blk = blocks + b * 144;
   const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
   const float dmin = half_bits_to_f32(static_cast<uint16_t>(blk[2] | (blk[3] << 8)));
@@ -71,13 +91,16 @@ __global__ void dequant_q4_k_kernel(const uint8_t* __restrict__ blocks, int64_t 
   q4k_scale_min(blk + 4, j, sc, m);
   const float ds = __fmul_rn(d, static_cast<float>(sc));
   const float dm = __fmul_rn(dmin, static_cast<float>(m));
-  const uint8_t* qs = blk + 16 + (j >> 1) * 32;
+  const uint2 raw = *reinterpret_cast<const uint2*>(blk + 16 + (j >> 1) * 32 + l0);
   const int shift = (j & 1) * 4;
-#pragma unroll 8
-  for (int l = 0; l < 32; ++l) {
-    const float q = static_cast<float>((qs[l] >> shift) & 0x0F);
-    store_val<kBf16>(out, b * 256 + j * 32 + l, __fsub_rn(__fmul_rn(ds, q), dm));
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t w = i < 4 ? raw.x : raw.y;
+    const float q = static_cast<float>((w >> (8 * (i & 3) + shift)) & 0x0F);
+    v[i] = __fsub_rn(__fmul_rn(ds, q), dm);
   }
+  store8<kBf16>(out, b * 256 + j * 32 + l0, v);
 }
 
 template <bool kBf16>
@@ -108,17 +131,20 @@ inline unsigned grid_for(int64_t n, int threads) {
 template <bool kBf16>
 cudaError_t dequant_impl(int type, const void* blocks, int64_t n, void* out, cudaStream_t s) {
   constexpr int T = 256;
+  // 16-byte vector stores; Q4_K reads its nibbles 8 bytes at a time.
+  if (reinterpret_cast<uintptr_t>(out) & 15) return cudaErrorMisalignedAddress;
+  if (type == kTypeQ4_K && (reinterpret_cast<uintptr_t>(blocks) & 7)) return cudaErrorMisalignedAddress;
   switch (type) {
     case kTypeQ8_0: {
       if (n % 32) return cudaErrorInvalidValue;
       int64_t nb = n / 32;
-      if (nb) dequant_q8_0_kernel<kBf16><<<grid_for(nb, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      if (nb) dequant_q8_0_kernel<kBf16><<<grid_for(nb * 4, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
       break;
     }
     case kTypeQ4_K: {
       if (n % 256) return cudaErrorInvalidValue;
       int64_t nb = n / 256;
-      if (nb) dequant_q4_k_kernel<kBf16><<<grid_for(nb * 8, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      if (nb) dequant_q4_k_kernel<kBf16><<<grid_for(nb * 32, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
       break;
     }
     case kTypeF16:

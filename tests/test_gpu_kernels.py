@@ -82,7 +82,8 @@ def test_gemm_matches_fp32_reference(ctx, gtype, M, N, K):
 def test_gemm_large_k_and_many_tiles(ctx):
     y, ref = gemm_case(ctx, fo.GGML_Q4_K, 4608, 2304, 9216, seed=7)
     rel = ((y - ref).norm() / ref.norm()).item()
-    assert rel < 1e-5, rel
+    # f32 accumulation over K = 9216 in the tensor-core order vs float64
+    assert rel < 3e-5, rel
 
 
 def test_layernorm_mod_matches_reference(ctx):
