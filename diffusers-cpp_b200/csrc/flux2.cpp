@@ -951,10 +951,15 @@ void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* gra
         ev_.push_back(e);
       }
     }
+    // Inside a capture the records become graph event nodes (external
+    // flag); outside they are ordinary stream records.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cuda_check(cudaStreamIsCapturing(s, &cs), "cudaStreamIsCapturing");
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
     for (size_t i = 0; i < ops.size(); ++i) {
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], s, cudaEventRecordExternal), "event record");
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], s, flags), "event record");
       ops[i].fn(s);
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], s, cudaEventRecordExternal), "event record");
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], s, flags), "event record");
     }
   };
   if (!use_graph_) {
