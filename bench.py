@@ -220,7 +220,12 @@ def run_ours(args):
     ni = gh * gw
 
     ctx = dcpp_b200.Context(local)
-    stream = torch.cuda.current_stream()
+    # A dedicated (non-default) stream shared by the library and the timing
+    # events: the legacy default stream has handle 0, which the library
+    # would read as "use your own stream".
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
     ctx.set_stream(stream.cuda_stream)
     if world > 1:
         uid = [dcpp_b200.Context.nccl_unique_id() if rank == 0 else None]
