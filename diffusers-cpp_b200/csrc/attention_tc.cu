@@ -1,0 +1,344 @@
+// Joint attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   O = softmax(Q K^T * scale) V, no mask (FlashAttentionOp.cpp:6-105,
+//   ggml_flash_attn_ext(q, k, v, nullptr, 1/sqrt(128)))
+//
+// Layouts (bf16): Q, K [B*H, S, 128] (row per token), V^T [B*H, 128, Sp]
+// (row per head-dim channel, Sp = S rounded up to 64, zero padded), so every
+// MMA operand is K-major and arrives through TMA with the 128-byte swizzle.
+//
+// One CTA = one 128-row query tile of one (batch, head); 192 threads:
+//   warp 0     TMA: Q once, then K_j / V_j^T tiles of 128 keys (2 stages)
+//   warp 1     TMEM allocation and the single MMA-issuing thread:
+//                S_j = Q K_j^T   (M 128, N 128 keys, K 128)   -> TMEM S[j % 2]
+//                O  += P_j V_j   (M 128, N 128, K 128 keys)   -> TMEM O
+//              S_{j+1} is issued before waiting for P_j, so the tensor core
+//              computes the next scores while the softmax runs.
+//   warps 2-5  softmax, one thread per query row (its TMEM lane): online
+//              softmax in the exp2 domain, P_j written to shared memory in
+//              the swizzled K-major layout; O is rescaled in TMEM only when
+//              a row maximum grows by more than 2^8 (otherwise the stale
+//              maximum is kept, which is exact because l uses the same one).
+//              At the end they normalise O by l and store bf16 rows.
+#include "attention_tc.cuh"
+#include "common.cuh"
+
+namespace dcpp {
+
+namespace {
+
+constexpr int kBQ = 128;                    // query rows per CTA
+constexpr int kBKV = 128;                   // keys per tile
+constexpr int kHalfBytes = 128 * 128;       // one 64-wide swizzle atom column block of 128 rows: 16 KB
+constexpr int kTileBytes = 2 * kHalfBytes;  // 128 x 128 bf16 = 32 KB
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;              // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int kSmemBytes = 6 * kTileBytes + 1024 + 256;  // Q, K x2, V x2, P + barriers
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnTcArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kTileBytes;       // 2 stages
+  uint8_t* sV = smem + 3 * kTileBytes;   // 2 stages
+  uint8_t* sP = smem + 5 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* p_empty = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qt = blockIdx.x;
+  const int bh = blockIdx.y;  // b * H + h
+  const int S = p.S;
+  const int nkv = (S + kBKV - 1) / kBKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_3d(sQ, &tmQ, q_full, 0, qt * kBQ, bh);
+      tma_load_3d(sQ + kHalfBytes, &tmQ, q_full, 64, qt * kBQ, bh);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
+        uint8_t* k = sK + st * kTileBytes;
+        uint8_t* v = sV + st * kTileBytes;
+        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bh);
+        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bh);
+        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bh);
+        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(128, 128);
+      const uint32_t tS[2] = {tmem_base, tmem_base + 128};
+      const uint32_t tO = tmem_base + 256;
+      const uint32_t aQ = smem_u32(sQ);
+      const uint32_t aP = smem_u32(sP);
+      auto issue_s = [&](int j) {
+        const int st = j & 1;
+        const uint32_t aK = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          umma_bf16(tS[st], make_sdesc_sw128(aQ + off), make_sdesc_sw128(aK + off), idesc, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn) && mbar_wait(&kv_full[0], 0, p.err, kDevTimeoutAttn);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv) {
+          const int st = (j + 1) & 1;
+          ok = mbar_wait(&kv_full[st], ((j + 1) >> 1) & 1, p.err, kDevTimeoutAttn) &&
+               mbar_wait(&s_empty[st], (((j + 1) >> 1) & 1) ^ 1, p.err, kDevTimeoutAttn);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutAttn)) break;
+        tc_fence_after();
+        const uint32_t aV = smem_u32(sV + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          umma_bf16(tO, make_sdesc_sw128(aP + off), make_sdesc_sw128(aV + off), idesc, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[j & 1]);
+        umma_commit(p_empty);
+      }
+    }
+  } else {
+    // Softmax warps 2..5 -> TMEM lane quarter (warp % 4); thread = query row.
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tO = tmem_base + lane_off + 256;
+    const float c = p.scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1, p.err, kDevTimeoutAttn));
+      if (!ok) break;
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t r[32];
+        const uint32_t tS = tmem_base + lane_off + st * 128;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          tmem_ld32(tS + ch * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[ch * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[st]);
+      const int kbase = j * kBKV;
+      if (kbase + kBKV > S) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (kbase + i >= S) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      mx *= c;
+      // Lazy rescale: keep the running maximum unless it grows by > 2^8.
+      const bool grow = mx > m + kRescaleThreshold;
+      const float m_use = grow ? mx : m;
+      const float alpha = grow ? ex2(m - m_use) : 1.0f;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        s[i] = ex2(fmaf(s[i], c, -m_use));
+        sum += s[i];
+      }
+      l = l * alpha + sum;
+      m = m_use;
+      if (j > 0) {
+        // PV_{j-1} done: the P buffer is free and O is current.
+        ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (j - 1) & 1, p.err, kDevTimeoutAttn));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tO + ch * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row -> shared memory, K-major 128-byte swizzle (two 64-key atoms).
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* v = s + kb * 64 + ch * 8;
+          const uint4 o = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                     pack_bf16x2(v[6], v[7]));
+          *reinterpret_cast<uint4*>(sP + kb * kHalfBytes + row * 128 + ((ch ^ (row & 7)) << 4)) = o;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (nkv - 1) & 1, p.err, kDevTimeoutAttn));
+    if (ok) {
+      tc_fence_after();
+      const int q = qt * kBQ + row;
+      const float inv = 1.0f / l;
+      uint16_t* dst = p.o + (static_cast<int64_t>(bh / p.H) * S + q) * p.ld_o + (bh % p.H) * 128;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tO + ch * 32, r);
+        tmem_ld_wait();
+        if (q < S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            d4[v] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * v]) * inv, __uint_as_float(r[8 * v + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(q);
+  }
+  return fn;
+}
+
+// 3-D bf16 map {inner, mid, outer} with box {64, 128, 1}, 128-byte swizzle.
+cudaError_t make_map3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[3] = {inner, mid, outer};
+  cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int64_t attn_vt_stride(int64_t S) { return (S + 63) / 64 * 64; }
+
+cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* k, const uint16_t* vt, int B, int H,
+                           int S) {
+  const uint64_t bh = static_cast<uint64_t>(B) * H;
+  cudaError_t e = make_map3(&maps->q, q, 128, S, bh);
+  if (e == cudaSuccess) e = make_map3(&maps->k, k, 128, S, bh);
+  if (e == cudaSuccess) e = make_map3(&maps->v, vt, attn_vt_stride(S), 128, bh);
+  return e;
+}
+
+cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s) {
+  if (a.S <= 0 || a.H <= 0 || a.B <= 0) return cudaSuccess;
+  if (a.ld_o % 8 || (reinterpret_cast<uintptr_t>(a.o) & 15)) return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid((a.S + kBQ - 1) / kBQ, a.B * a.H);
+  attn_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(maps.q, maps.k, maps.v, a);
+  return cudaGetLastError();
+}
+
+}  // namespace dcpp

@@ -1,0 +1,31 @@
+// tcgen05 joint attention: host-side types and launch entry points.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dcpp {
+
+struct AttnTcArgs {
+  uint16_t* o;     // output row (b * S + s), column h * 128 + d
+  int64_t ld_o;    // row stride of o (elements, multiple of 8)
+  int32_t B, H, S;
+  float scale;     // softmax scale
+  int* err;        // device error word for bounded waits
+};
+
+struct AttnTcMaps {
+  CUtensorMap q, k, v;
+};
+
+// Row stride (keys) of the transposed V buffer [B*H, 128, Sp]: S rounded up to 64.
+int64_t attn_vt_stride(int64_t S);
+
+// Tensor maps over q, k [B*H, S, 128] and vt [B*H, 128, Sp] (bf16).
+cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* k, const uint16_t* vt, int B, int H,
+                           int S);
+
+cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s);
+
+}  // namespace dcpp

@@ -1,5 +1,6 @@
 // Flux2 DiT denoise step on sm_100a: the C++ model host and its C ABI.
 #include "flux2.hpp"
+#include "attention_tc.cuh"
 
 #include <cuda_fp16.h>
 
@@ -661,7 +662,11 @@ void Flux2Transformer2DModel::build_plan() {
   a_ = static_cast<uint16_t*>(alloc(R * D * 2));
   q_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
   k_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
-  v_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
+  // V is kept transposed, [B, Hl, 128, Sp] with Sp = S rounded up to 64;
+  // the padding columns stay zero (finite) for the attention's P.V MMA.
+  const int64_t sp = attn_vt_stride(S);
+  v_ = static_cast<uint16_t*>(alloc(B * Hl * 128 * sp * 2));
+  cuda_check(cudaMemset(v_, 0, B * Hl * 128 * sp * 2), "memset vt");
   cat_ = static_cast<uint16_t*>(alloc(R * ldc * 2));
   xb_ = static_cast<uint16_t*>(alloc(B * Ni * in_ch * 2));
   eb_ = static_cast<uint16_t*>(alloc(B * Nt * jd * 2));
@@ -807,19 +812,20 @@ void Flux2Transformer2DModel::build_plan() {
                    },
                    1});
     const float* resid = nullptr;  // pending all-reduced partial (TP)
-    AttnArgs at{};
-    at.q = q_;
-    at.k = k_;
-    at.v = v_;
+    AttnTcArgs at{};
     at.o = cat_;
     at.ld_o = ldc;
     at.B = static_cast<int32_t>(B);
     at.H = static_cast<int32_t>(Hl);
     at.S = static_cast<int32_t>(S);
     at.scale = 1.0f / std::sqrt(static_cast<float>(cfg_.attention_head_dim));
+    at.err = ctx_.d_err;
+    auto maps = std::make_shared<AttnTcMaps>();
+    cuda_check(make_attn_maps(maps.get(), q_, k_, v_, static_cast<int>(B), static_cast<int>(Hl), static_cast<int>(S)),
+               "attention tensor maps");
     auto attn_op = [&]() {
-      ops.push_back({[at](cudaStream_t s) { cuda_check(launch_attention(at, s), "attention"); }, 1, kOpAttention,
-                     4.0 * at.B * at.H * static_cast<double>(at.S) * static_cast<double>(at.S) * 128.0});
+      ops.push_back({[at, maps](cudaStream_t s) { cuda_check(launch_attention_tc(*maps, at, s), "attention"); }, 1,
+                     kOpAttention, 4.0 * at.B * at.H * static_cast<double>(at.S) * static_cast<double>(at.S) * 128.0});
     };
     auto out_epi = [&](const float* g0, const float* g1, int64_t bstride) {
       EpilogueArgs e{};
@@ -851,6 +857,7 @@ void Flux2Transformer2DModel::build_plan() {
       e.q_out = q_;
       e.k_out = k_;
       e.v_out = v_;
+      e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
       add_gemm("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], stream_groups(true), e, 3 * Dl);
@@ -885,6 +892,7 @@ void Flux2Transformer2DModel::build_plan() {
       e.q_out = q_;
       e.k_out = k_;
       e.v_out = v_;
+      e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
       add_gemm("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, stream_groups(false), e, 3 * Dl + 2 * Fl);

@@ -83,21 +83,20 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
         const int64_t dst_row =
             ((static_cast<int64_t>(G.batch) * e.heads + head) * e.seq + tok) * 128;
         if (region == 2) {
+          // V is stored transposed, [B, H, 128, vt_stride]: the attention's
+          // P.V MMA then reads a K-major operand.  Lanes hold consecutive
+          // tokens, so each 2-byte store of the warp covers 64 contiguous bytes.
+          uint16_t* vt = e.v_out + (static_cast<int64_t>(G.batch) * e.heads + head) * 128 * e.vt_stride + tok;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
             tmem_ld32(hbase + c * 32, r);
             tmem_ld_wait();
             if (row_ok) {
-              uint4* dst = reinterpret_cast<uint4*>(dst_base + dst_row + c * 32);
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                uint4 o;
-                o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-                o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-                o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-                o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
-                dst[v] = o;
+              for (int j = 0; j < 32; ++j) {
+                __nv_bfloat16 b = __float2bfloat16_rn(__uint_as_float(r[j]));
+                vt[static_cast<int64_t>(c * 32 + j) * e.vt_stride] = *reinterpret_cast<uint16_t*>(&b);
               }
             }
           }

@@ -64,7 +64,8 @@ struct EpilogueArgs {
   const float2* rope;        // [S, 64] (cos, sin) per token and rotary pair
   uint16_t* q_out;           // [B, H, S, 128]
   uint16_t* k_out;
-  uint16_t* v_out;
+  uint16_t* v_out;           // transposed: [B, H, 128, vt_stride]
+  int64_t vt_stride;         // keys per V^T row (S rounded up to 64)
   uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
   int64_t ld_mlp;
 };

@@ -66,21 +66,11 @@ cudaError_t launch_gemv(int wtype, const void* W, int64_t N, int64_t K, const fl
 cudaError_t launch_add_f32(float* y, const float* a, int64_t n, cudaStream_t s);
 
 // ---- attention.cu
-struct AttnArgs {
-  const uint16_t* q;   // [B, H, S, 128] bf16 (already normalised and rotated)
-  const uint16_t* k;
-  const uint16_t* v;
-  uint16_t* o;         // row (b*S + s), column h*128 + d, row stride ld_o
-  int64_t ld_o;
-  int32_t B, H, S;
-  float scale;         // softmax scale (1/sqrt(128))
-};
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
-
 // Standalone q/k RMSNorm + RoPE + relayout from the fused qkv projection
-// rows [B*S, 3*H*128] into q/k/v [B, H, S, 128].
+// rows [B*S, 3*H*128] into q/k [B, H, S, 128] and transposed v
+// [B, H, 128, vt_stride] (the tcgen05 attention's operand layouts).
 cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t B, int64_t S, int64_t H, const float* norm_q,
                                 const float* norm_k, float eps, const float2* rope, uint16_t* q, uint16_t* k,
-                                uint16_t* v, cudaStream_t s);
+                                uint16_t* vt, int64_t vt_stride, cudaStream_t s);
 
 }  // namespace dcpp

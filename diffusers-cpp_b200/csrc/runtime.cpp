@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "attention_tc.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -323,28 +324,35 @@ dcpp_status dcpp_attention(dcpp_ctx* ctx, const uint16_t* qkv, int64_t B, int64_
       tot += axes_dims[i];
     }
     if (tot != head_dim) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_attention: axes dims must sum to head_dim");
-    const size_t qkv_elems = static_cast<size_t>(B * H * S * 128);
-    const size_t rope_bytes = static_cast<size_t>(S) * 64 * sizeof(float2);
-    const size_t need = 3 * qkv_elems * 2 + rope_bytes + 256;
+    if (B * H > 65535 || S > (1 << 24)) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_attention: size too large");
+    const int64_t sp = dcpp::attn_vt_stride(S);
+    const size_t qk_elems = static_cast<size_t>(B * H * S * 128);
+    const size_t vt_elems = static_cast<size_t>(B * H * 128 * sp);
+    const size_t rope_off = ((2 * qk_elems + vt_elems) * 2 + 255) & ~size_t(255);
+    const size_t need = rope_off + static_cast<size_t>(S) * 64 * sizeof(float2);
     uint8_t* s = static_cast<uint8_t*>(ctx->ensure_scratch(need));
     auto* q = reinterpret_cast<uint16_t*>(s);
-    auto* k = q + qkv_elems;
-    auto* v = k + qkv_elems;
-    auto* rope = reinterpret_cast<float2*>(s + ((3 * qkv_elems * 2 + 255) & ~size_t(255)));
+    auto* k = q + qk_elems;
+    auto* vt = k + qk_elems;
+    auto* rope = reinterpret_cast<float2*>(s + rope_off);
+    // The V^T padding columns [S, sp) must hold finite values (zeros).
+    dcpp::cuda_check(cudaMemsetAsync(vt, 0, vt_elems * 2, ctx->stream), "memset vt");
     dcpp::cuda_check(dcpp::launch_rope_table(ids, S, n_axes, dims, theta, rope, ctx->stream), "rope table");
-    dcpp::cuda_check(dcpp::launch_qk_norm_rope(qkv, B, S, H, norm_q, norm_k, eps, rope, q, k, v, ctx->stream),
+    dcpp::cuda_check(dcpp::launch_qk_norm_rope(qkv, B, S, H, norm_q, norm_k, eps, rope, q, k, vt, sp, ctx->stream),
                      "qk norm rope");
-    dcpp::AttnArgs a{};
-    a.q = q;
-    a.k = k;
-    a.v = v;
+    dcpp::AttnTcMaps maps;
+    dcpp::cuda_check(dcpp::make_attn_maps(&maps, q, k, vt, static_cast<int>(B), static_cast<int>(H),
+                                          static_cast<int>(S)),
+                     "attention tensor maps");
+    dcpp::AttnTcArgs a{};
     a.o = out;
     a.ld_o = H * 128;
     a.B = static_cast<int32_t>(B);
     a.H = static_cast<int32_t>(H);
     a.S = static_cast<int32_t>(S);
     a.scale = 1.0f / sqrtf(128.0f);
-    dcpp::cuda_check(dcpp::launch_attention(a, ctx->stream), "attention");
+    a.err = ctx->d_err;
+    dcpp::cuda_check(dcpp::launch_attention_tc(maps, a, ctx->stream), "attention");
   });
 }
 
