@@ -77,6 +77,8 @@ _SIGNATURES = {
     "dcpp_dequant_bf16": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
     "dcpp_f32_to_bf16": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
     "dcpp_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, _vp]),
+    "dcpp_gemm_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64,
+                                         _vp]),
     "dcpp_layernorm_mod": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_float, _vp]),
     "dcpp_attention": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp,
                                       ctypes.c_float, _vp, ctypes.c_int, _c_i64p, ctypes.c_float, _vp]),
@@ -193,6 +195,12 @@ class Context:
 
     def gemm(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
         self.check(lib().dcpp_gemm(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm")
+
+    def gemm_noalloc(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
+        """Like gemm(), but allocates no device memory: for callers whose
+        device memory is owned by someone else or must not change mid-run
+        (see dcpp_gemm_noalloc in include/dcpp.h for the limits)."""
+        self.check(lib().dcpp_gemm_noalloc(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_noalloc")
 
     def layernorm_mod(self, x, rows: int, D: int, shift, scale, eps: float, y):
         self.check(lib().dcpp_layernorm_mod(self.h, _ptr(x), rows, D, _ptr(shift), _ptr(scale), eps, _ptr(y)),

@@ -121,6 +121,23 @@ dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* d_in, int64_t n, uint16
 dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
                       const uint16_t* d_x, int64_t M, float* d_y);
 
+/* dcpp_gemm for callers that cannot allocate device memory.  No counterpart
+ * in the reference.  Same arguments, result and precision as dcpp_gemm, but
+ * it allocates nothing: a quantised W is expanded to bf16 in a fixed 32 MiB
+ * device array that is part of the loaded library (held on every GPU that
+ * loads it until the process exits), in row chunks that fit it.  This serves
+ * hosts that own all device memory through their own pool, code that must
+ * not make a synchronising cudaMalloc / cudaFree call mid-sequence, and
+ * deployments with a memory budget fixed in advance.
+ * Limits: K <= 65536 (else DCPP_ERR_UNSUPPORTED with the reason).  The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * The array is shared by every call on the device and keeps the last call's
+ * contents: calls whose GPU work overlaps (other streams or contexts on the
+ * same device) race on it and must be serialised by the caller. */
+dcpp_status dcpp_gemm_noalloc(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
+                              const uint16_t* d_x, int64_t M, float* d_y);
+
 /* LayerNorm without affine (ggml_norm, eps) followed by adaLN modulation
  * y = norm(x) * (1 + scale) + shift  (Flux2TransformerBlock.hpp:65-66,
  * LayerNorm.cpp:16-32).  x f32 [rows, D]; shift/scale f32 [D]; y bf16. */
