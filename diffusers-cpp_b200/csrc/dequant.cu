@@ -172,4 +172,112 @@ cudaError_t launch_dequant_bf16(int type, const void* blocks, int64_t n, uint16_
   return dequant_impl<true>(type, blocks, n, out, s);
 }
 
+// ------------------------------------------------------------------ packing
+// The fused-dequant GEMM reads a quantised weight [N, K] as stages of 256
+// rows x 64 K, each one contiguous block so that one bulk TMA copy brings it:
+//   Q4_K stage (10240 B): [256 x 32 B nibbles][256 x (s0, m0, s1, m1) bf16]
+//       the 32 nibble bytes are the GGUF block's qs[32 g .. 32 g + 31] for
+//       the stage's 64-wide group g (low nibble: sub-block 2g, high: 2g+1);
+//       s_j = d * sc_j and m_j = dmin * m_j are exact in f32, rounded once
+//       to bf16.
+//   Q8_0 stage (17408 B): [256 x 64 int8][256 x (d0, d1) bf16] for the
+//       stage's two 32-weight blocks.
+// Stage (n_tile, kb) starts at (n_tile * K/64 + kb) * stage bytes; rows
+// beyond N are zero.
+
+namespace {
+
+__device__ __forceinline__ uint16_t bf16_bits(float v) {
+  __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+
+template <int kType>
+__global__ void pack_weight_kernel(const uint8_t* __restrict__ raw, int64_t N, int64_t K, uint8_t* __restrict__ out,
+                                   int64_t total) {
+  const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (t >= total) return;
+  constexpr int kQs = kType == kTypeQ4_K ? 32 : 64;
+  constexpr int kSc = kType == kTypeQ4_K ? 8 : 4;
+  constexpr int kStage = 256 * (kQs + kSc);
+  const int64_t nkb = K / 64;
+  const int r = static_cast<int>(t & 255);
+  const int64_t stage = t >> 8;  // n_tile * nkb + kb
+  const int64_t kb = stage % nkb;
+  const int64_t n = (stage / nkb) * 256 + r;
+  uint8_t* qs_out = out + stage * kStage + r * kQs;
+  uint8_t* sc_out = out + stage * kStage + 256 * kQs + r * kSc;
+  if (n >= N) {
+    for (int i = 0; i < kQs; i += 16) *reinterpret_cast<uint4*>(qs_out + i) = make_uint4(0, 0, 0, 0);
+    if (kSc == 8) *reinterpret_cast<uint2*>(sc_out) = make_uint2(0, 0);
+    else *reinterpret_cast<uint32_t*>(sc_out) = 0;
+    return;
+  }
+  if (kType == kTypeQ4_K) {
+    const uint8_t* blk = raw + n * (K / 256) * 144 + (kb >> 2) * 144;
+    const int g = static_cast<int>(kb & 3);
+    const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+    const float dmin = half_bits_to_f32(static_cast<uint16_t>(blk[2] | (blk[3] << 8)));
+    int sc0, m0, sc1, m1;
+    q4k_scale_min(blk + 4, 2 * g, sc0, m0);
+    q4k_scale_min(blk + 4, 2 * g + 1, sc1, m1);
+    const uint16_t v[4] = {bf16_bits(__fmul_rn(d, static_cast<float>(sc0))),
+                           bf16_bits(__fmul_rn(dmin, static_cast<float>(m0))),
+                           bf16_bits(__fmul_rn(d, static_cast<float>(sc1))),
+                           bf16_bits(__fmul_rn(dmin, static_cast<float>(m1)))};
+    *reinterpret_cast<uint2*>(sc_out) =
+        make_uint2(v[0] | (static_cast<uint32_t>(v[1]) << 16), v[2] | (static_cast<uint32_t>(v[3]) << 16));
+    const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + g * 32);
+    reinterpret_cast<uint4*>(qs_out)[0] = q[0];
+    reinterpret_cast<uint4*>(qs_out)[1] = q[1];
+  } else {
+    const uint8_t* b0 = raw + n * (K / 32) * 34 + (2 * kb) * 34;
+    const uint8_t* b1 = b0 + 34;
+    const float d0 = half_bits_to_f32(static_cast<uint16_t>(b0[0] | (b0[1] << 8)));
+    const float d1 = half_bits_to_f32(static_cast<uint16_t>(b1[0] | (b1[1] << 8)));
+    *reinterpret_cast<uint32_t*>(sc_out) = bf16_bits(d0) | (static_cast<uint32_t>(bf16_bits(d1)) << 16);
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint8_t* s = i < 4 ? b0 + 2 + 4 * i : b1 + 2 + 4 * (i - 4);
+      w[i] = s[0] | (s[1] << 8) | (s[2] << 16) | (static_cast<uint32_t>(s[3]) << 24);
+    }
+    uint4* o = reinterpret_cast<uint4*>(qs_out);
+    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+}  // namespace
+
+int packed_stage_bytes(int type) {
+  if (type == kTypeQ4_K) return 256 * (32 + 8);
+  if (type == kTypeQ8_0) return 256 * (64 + 4);
+  return 0;
+}
+
+size_t packed_bytes(int type, int64_t N, int64_t K) {
+  const int sb = packed_stage_bytes(type);
+  if (!sb || K % 64) return 0;
+  return static_cast<size_t>((N + 255) / 256) * static_cast<size_t>(K / 64) * static_cast<size_t>(sb);
+}
+
+cudaError_t launch_pack_weight(int type, const void* raw, int64_t N, int64_t K, void* out, cudaStream_t s) {
+  if (N <= 0 || K <= 0) return cudaSuccess;
+  if ((type == kTypeQ4_K && K % 256) || (type == kTypeQ8_0 && K % 64)) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(out) & 15) return cudaErrorMisalignedAddress;
+  if (type == kTypeQ4_K && (reinterpret_cast<uintptr_t>(raw) & 15)) return cudaErrorMisalignedAddress;
+  const int64_t total = (N + 255) / 256 * 256 * (K / 64);
+  const unsigned grid = static_cast<unsigned>((total + 255) / 256);
+  if (type == kTypeQ4_K)
+    pack_weight_kernel<kTypeQ4_K><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(raw), N, K,
+                                                       static_cast<uint8_t*>(out), total);
+  else if (type == kTypeQ8_0)
+    pack_weight_kernel<kTypeQ8_0><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(raw), N, K,
+                                                       static_cast<uint8_t*>(out), total);
+  else
+    return cudaErrorNotSupported;
+  return cudaGetLastError();
+}
+
 }  // namespace dcpp

@@ -224,6 +224,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   int64_t tot = 0;
   for (auto d : cfg_.axes_dims_rope) tot += d;
   if (tot != cfg_.attention_head_dim) fail(DCPP_ERR_INVALID_ARG, "axes_dims_rope must sum to attention_head_dim");
+  if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) != "0";
   build_registry();
 }
 
@@ -231,8 +232,10 @@ Flux2Transformer2DModel::~Flux2Transformer2DModel() {
   cudaSetDevice(ctx_.device);
   cudaStreamSynchronize(ctx_.stream);
   free_plan();
-  for (auto* w : weights_)
+  for (auto* w : weights_) {
     if (w->data) cudaFree(w->data);
+    if (w->packed) cudaFree(w->packed);
+  }
   for (auto* v : vectors_)
     if (v->data) cudaFree(v->data);
   for (auto e : ev_) cudaEventDestroy(e);
@@ -433,6 +436,14 @@ void Flux2Transformer2DModel::build_registry() {
     initv(blk.norm_q, p + "norm_q.weight", cfg_.attention_head_dim);
     initv(blk.norm_k, p + "norm_k.weight", cfg_.attention_head_dim);
   }
+  // The block projections run on the fused-dequant GEMM.
+  for (auto& blk : dbl_)
+    for (int s = 0; s < 2; ++s)
+      for (DevWeight* w : {&blk.qkv[s], &blk.out[s], &blk.ff_in[s], &blk.ff_out[s]}) w->pack = true;
+  for (auto& blk : sgl_) {
+    blk.qkv_mlp.pack = true;
+    blk.out.pack = true;
+  }
   for (auto* v : vectors_) {
     DevVector* pv = v;
     setters_[v->name] = [this, pv](int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes) {
@@ -484,6 +495,21 @@ void Flux2Transformer2DModel::finish_weight(DevWeight& w) {
   }
   cuda_check(cudaMemcpy(w.data, w.staging.data(), bytes, cudaMemcpyHostToDevice), "upload weight");
   std::vector<uint8_t>().swap(w.staging);
+  // Block projections in Q4_K / Q8_0 are kept only in the packed stage layout
+  // that the fused-dequant GEMM reads (packed once here, on the device).
+  const bool packable = (w.type == kTypeQ4_K && w.cols % 256 == 0) || (w.type == kTypeQ8_0 && w.cols % 64 == 0);
+  if (w.pack && packable && fused_dequant_) {
+    const size_t pb = packed_bytes(w.type, w.rows, w.cols);
+    if (cudaMalloc(&w.packed, pb) != cudaSuccess) {
+      cudaGetLastError();
+      w.packed = nullptr;
+      fail(DCPP_ERR_OOM, "packed weight allocation failed for " + w.name);
+    }
+    cuda_check(launch_pack_weight(w.type, w.data, w.rows, w.cols, w.packed, ctx_.stream), "pack weight");
+    cuda_check(cudaStreamSynchronize(ctx_.stream), "pack weight");
+    cuda_check(cudaFree(w.data), "free raw weight");
+    w.data = nullptr;
+  }
   planned_ = false;
 }
 
@@ -573,6 +599,36 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   (void)tag;
   if (w0->cols != K || (w1 && (w1->cols != K || w1->rows != w0->rows)) || w0->rows != N)
     fail(DCPP_ERR_STATE, "internal: GEMM shape mismatch for " + w0->name);
+  // Fused dequantisation when every weight of the launch is packed and of
+  // one quantised type; otherwise expand to bf16 first (or use bf16 as is).
+  const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
+  if (fused) {
+    int64_t a_rows = 0;
+    for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
+    auto st = std::make_shared<CUtensorMap>();
+    cuda_check(make_tmap_bf16(st.get(), a, K, a_rows, lda, kGemmBM), "tensor map A");
+    GemmArgs args{};
+    args.N = static_cast<int32_t>(N);
+    args.K = static_cast<int32_t>(K);
+    if (groups.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
+    args.n_groups = static_cast<int32_t>(groups.size());
+    for (size_t i = 0; i < groups.size(); ++i) args.groups[i] = groups[i];
+    args.ep = ep;
+    args.err = ctx_.d_err;
+    args.qb[0].packed = w0->packed;
+    args.qb[1].packed = w1 ? w1->packed : w0->packed;
+    gemm_finalize_groups(args);
+    const int bsrc = w0->type == kTypeQ4_K ? kBSrcQ4_K : kBSrcQ8_0;
+    double flops = 0.0;
+    for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
+    Ctx* c = &ctx_;
+    building_->push_back({[st, args, c, bsrc](cudaStream_t s) {
+                            cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
+                          },
+                          1, kOpGemm, flops});
+    return;
+  }
+  if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
   const uint16_t* b0 = w0->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w0->data) : wscratch_[0];
   const uint16_t* b1 = b0;
   if (w1) b1 = w1->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w1->data) : wscratch_[1];
@@ -691,12 +747,19 @@ void Flux2Transformer2DModel::build_plan() {
   mod_s_v_ = static_cast<float*>(alloc(B * 3 * D * 4));
   mod_o_v_ = static_cast<float*>(alloc(B * 2 * D * 4));
   // Weight expansion scratch (bf16) for quantised GEMM weights.
+  // Only GEMM weights that are neither bf16 nor packed need it; the
+  // conditioning GEMVs read their raw GGUF rows directly.
   size_t s0 = 0, s1 = 0;
-  for (auto* w : weights_)
-    if (w->type != kTypeBF16) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
+  auto needs = [](const DevWeight* w) { return w->type != kTypeBF16 && !w->packed; };
+  for (const DevWeight* w : {&x_embed_, &ctx_embed_, &proj_out_})
+    if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
   for (auto& blk : dbl_)
-    for (DevWeight* w : {&blk.qkv[0], &blk.out[0], &blk.ff_in[0], &blk.ff_out[0]})
-      if (w->type != kTypeBF16) s1 = std::max(s1, static_cast<size_t>(w->rows * w->cols));
+    for (int s = 0; s < 2; ++s)
+      for (const DevWeight* w : {&blk.qkv[s], &blk.out[s], &blk.ff_in[s], &blk.ff_out[s]})
+        if (needs(w)) (s == 0 ? s1 : s0) = std::max(s == 0 ? s1 : s0, static_cast<size_t>(w->rows * w->cols));
+  for (auto& blk : sgl_)
+    for (const DevWeight* w : {&blk.qkv_mlp, &blk.out})
+      if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
   wscratch_[0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
   wscratch_[1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
 

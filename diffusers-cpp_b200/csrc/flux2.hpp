@@ -59,10 +59,12 @@ struct DevWeight {
   int64_t rows = 0;
   int64_t cols = 0;
   size_t row_bytes = 0;
-  uint8_t* data = nullptr;             // device
+  uint8_t* data = nullptr;             // device, raw GGUF rows (null once packed)
+  uint8_t* packed = nullptr;           // device, fused-dequant stage layout (block projections)
+  bool pack = false;                   // a block projection: pack when quantised
   std::vector<uint8_t> staging;        // host, until all parts arrived
   std::set<std::string> need;          // part names still missing
-  bool ready() const { return data != nullptr && need.empty(); }
+  bool ready() const { return (data != nullptr || packed != nullptr) && need.empty(); }
 };
 
 // An f32 vector parameter (RMSNorm weights).
@@ -181,6 +183,9 @@ class Flux2Transformer2DModel {
   std::vector<Op>* building_ = nullptr;
   cudaGraphExec_t graph_fwd_ = nullptr, graph_step_[2] = {nullptr, nullptr};
   bool profiling_ = false;
+  // Dequantisation fused into the GEMM (packed weights); DCPP_FUSED_DEQUANT=0
+  // selects the expand-then-GEMM path instead (for comparisons).
+  bool fused_dequant_ = true;
   std::vector<Op>* last_ops_ = nullptr;
   std::vector<cudaEvent_t> ev_;  // 2 per op of the largest plan
   int64_t launches_per_step_ = 0;

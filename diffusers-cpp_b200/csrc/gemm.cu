@@ -26,11 +26,7 @@ namespace {
 
 constexpr int kAStageBytes = kGemmBM * kGemmBK * 2;  // 16 KB
 constexpr int kBStageBytes = kGemmBN * kGemmBK * 2;  // 32 KB
-constexpr int kStageBytes = kAStageBytes + kBStageBytes;
-constexpr int kGemmThreads = 192;
 constexpr int kTmemCols = 512;
-// smem: stages + barriers + tmem slot, plus 1 KB for 1024-byte alignment.
-constexpr int kGemmSmemBytes = kGemmStages * kStageBytes + 1024 + 256;
 
 struct TileCoord {
   int g;       // group
@@ -248,19 +244,165 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
   }
 }
 
+// ------------------------------------------------------------------ fused dequant
+// Quantised B tiles arrive packed per (256-row, 64-K) stage (see
+// pack_weight in dequant.cu):
+//   Q4_K: [256 rows x 32 B nibbles][256 rows x (s0, m0, s1, m1) bf16]
+//   Q8_0: [256 rows x 64 B int8  ][256 rows x (d0, d1) bf16]
+// Dequant warps turn one row of a stage into the 64 bf16 values of the B
+// tile row, in the 128-byte swizzled K-major layout TMA would have written
+// (16-byte chunk c of row r at r*128 + ((c ^ (r & 7)) << 4)).  Arithmetic is
+// packed bf16x2: q is built exactly from a 0x4300 magic exponent, then
+// w = q * s - m (Q4_K) or w = q * d (Q8_0) with one rounding.
+template <int BSRC>
+struct BCfg;
+template <>
+struct BCfg<kBSrcBf16> {
+  static constexpr int kStages = 4;
+  static constexpr int kRawBytes = 0;
+  static constexpr int kDequantWarps = 0;
+};
+template <>
+struct BCfg<kBSrcQ4_K> {
+  static constexpr int kStages = 3;
+  static constexpr int kRawBytes = kGemmBN * 32 + kGemmBN * 8;  // 10 KB
+  static constexpr int kDequantWarps = 8;
+};
+template <>
+struct BCfg<kBSrcQ8_0> {
+  static constexpr int kStages = 3;
+  static constexpr int kRawBytes = kGemmBN * 64 + kGemmBN * 4;  // 17 KB
+  static constexpr int kDequantWarps = 8;
+};
+
+template <int BSRC>
+constexpr int gemm_threads() { return (6 + BCfg<BSRC>::kDequantWarps) * 32; }
+template <int BSRC>
+constexpr int gemm_stage_bytes() { return kAStageBytes + kBStageBytes + BCfg<BSRC>::kRawBytes; }
+template <int BSRC>
+constexpr int gemm_smem_bytes() { return BCfg<BSRC>::kStages * gemm_stage_bytes<BSRC>() + 1024 + 256; }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+constexpr uint32_t kBf16x2_128 = 0x43004300u;  // (128.0, 128.0)
+constexpr uint32_t kHi43 = 0x43434343u;        // byte source for the bf16 high bytes
+
+// prmt selectors: result bytes {a.b0, 0x43, a.b1, 0x43} and {a.b2, 0x43, a.b3, 0x43},
+// i.e. the bf16 pair (128 + byte, 128 + byte') for bytes below 128.
+constexpr uint32_t kSelLo = 0x5140u;
+constexpr uint32_t kSelHi = 0x7362u;
+
+// 8 nibbles (bytes b0..b7 of w0, w1, already masked to 0x0F) -> 4 bf16x2 of
+// q * s - m (s2 = (s, s), nm2 = (-m, -m)).
+__device__ __forceinline__ uint4 q4_chunk(uint32_t w0, uint32_t w1, uint32_t s2, uint32_t nm2) {
+  uint4 o;
+  o.x = bf2_fma(bf2_sub(prmt(w0, kHi43, kSelLo), kBf16x2_128), s2, nm2);
+  o.y = bf2_fma(bf2_sub(prmt(w0, kHi43, kSelHi), kBf16x2_128), s2, nm2);
+  o.z = bf2_fma(bf2_sub(prmt(w1, kHi43, kSelLo), kBf16x2_128), s2, nm2);
+  o.w = bf2_fma(bf2_sub(prmt(w1, kHi43, kSelHi), kBf16x2_128), s2, nm2);
+  return o;
+}
+
+// 8 int8 (bytes of w0, w1) -> 4 bf16x2 of q * d.  q is rebuilt exactly as
+// (128 + (b & 127)) - (128 or 256 by the sign bit).
+__device__ __forceinline__ uint32_t q8_pair(uint32_t lo7, uint32_t sgn, uint32_t sel, uint32_t d2) {
+  const uint32_t v = prmt(lo7, kHi43, sel);
+  const uint32_t sub = prmt(sgn, kHi43, sel);  // bytes {0x00|0x80, 0x43}: 128.0 or 256.0
+  return bf2_mul(bf2_sub(v, sub), d2);
+}
+__device__ __forceinline__ uint4 q8_chunk(uint32_t w0, uint32_t w1, uint32_t d2) {
+  const uint32_t l0 = w0 & 0x7F7F7F7Fu, s0 = w0 & 0x80808080u;
+  const uint32_t l1 = w1 & 0x7F7F7F7Fu, s1 = w1 & 0x80808080u;
+  uint4 o;
+  o.x = q8_pair(l0, s0, kSelLo, d2);
+  o.y = q8_pair(l0, s0, kSelHi, d2);
+  o.z = q8_pair(l1, s1, kSelLo, d2);
+  o.w = q8_pair(l1, s1, kSelHi, d2);
+  return o;
+}
+
+template <int BSRC>
+__device__ __forceinline__ void dequant_row(const uint8_t* raw, uint8_t* btile, int r) {
+  uint8_t* dst = btile + r * 128;
+  const int sw = r & 7;
+  if (BSRC == kBSrcQ4_K) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(raw + r * 32);
+    const uint4 qb = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
+    const uint2 sc = *reinterpret_cast<const uint2*>(raw + kGemmBN * 32 + r * 8);
+    // sc.x = (s0, m0), sc.y = (s1, m1) as bf16 (low half first)
+    const uint32_t s0 = prmt(sc.x, 0, 0x1010), nm0 = prmt(sc.x, 0, 0x3232) ^ 0x80008000u;
+    const uint32_t s1 = prmt(sc.y, 0, 0x1010), nm1 = prmt(sc.y, 0, 0x3232) ^ 0x80008000u;
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // low nibbles: K 8c .. 8c+7 (sub-block 2g)
+      const uint4 o = q4_chunk(w[2 * c] & 0x0F0F0F0Fu, w[2 * c + 1] & 0x0F0F0F0Fu, s0, nm0);
+      *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = o;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // high nibbles: K 32 + 8c .. (sub-block 2g+1)
+      const uint4 o = q4_chunk((w[2 * c] >> 4) & 0x0F0F0F0Fu, (w[2 * c + 1] >> 4) & 0x0F0F0F0Fu, s1, nm1);
+      *reinterpret_cast<uint4*>(dst + (((c + 4) ^ sw) << 4)) = o;
+    }
+  } else {
+    const uint4* q = reinterpret_cast<const uint4*>(raw + r * 64);
+    const uint32_t ds = *reinterpret_cast<const uint32_t*>(raw + kGemmBN * 64 + r * 4);
+    const uint32_t d0 = prmt(ds, 0, 0x1010), d1 = prmt(ds, 0, 0x3232);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {  // 16 bytes = K 16h .. 16h+15
+      const uint4 v = q[h];
+      const uint32_t d2 = h < 2 ? d0 : d1;
+      *reinterpret_cast<uint4*>(dst + (((2 * h) ^ sw) << 4)) = q8_chunk(v.x, v.y, d2);
+      *reinterpret_cast<uint4*>(dst + (((2 * h + 1) ^ sw) << 4)) = q8_chunk(v.z, v.w, d2);
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ------------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+template <int BSRC>
+__global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+  constexpr int kStages = BCfg<BSRC>::kStages;
+  constexpr int kRaw = BCfg<BSRC>::kRawBytes;
+  constexpr bool kQuant = BSRC != kBSrcBf16;
+  constexpr int kDqThreads = BCfg<BSRC>::kDequantWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
-  uint8_t* smB = smem + kGemmStages * kAStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGemmStages * kStageBytes);
-  uint64_t* full = bars;                       // [stages]
-  uint64_t* empty = bars + kGemmStages;        // [stages]
-  uint64_t* acc_full = bars + 2 * kGemmStages; // [2]
-  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint8_t* smB = smem + kStages * kAStageBytes;
+  uint8_t* smR = smB + kStages * kBStageBytes;  // raw quantised stages (kQuant)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw);
+  uint64_t* full = bars;                        // [stages] TMA A (+ raw B) landed
+  uint64_t* empty = bars + kStages;             // [stages] MMA done with the stage
+  uint64_t* bready = bars + 2 * kStages;        // [stages] dequantised B written (kQuant)
+  uint64_t* acc_full = bars + 3 * kStages;      // [2]
+  uint64_t* acc_empty = acc_full + 2;           // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -268,9 +410,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk = (p.K + kGemmBK - 1) / kGemmBK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&bready[s], kQuant ? BCfg<BSRC>::kDequantWarps : 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -284,8 +427,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB0);
-    tma_prefetch_desc(&tmB1);
+    if (!kQuant) {
+      tma_prefetch_desc(&tmB0);
+      tma_prefetch_desc(&tmB1);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -303,12 +448,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int ya = G.row0 + tc.m_tile * kGemmBM;
         const int yb = tc.n_tile * kGemmBN;
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
+        const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
-          tma_load_2d(smB + stage * kBStageBytes, tmB, &full[stage], kb * kGemmBK, yb);
-          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+          if (kQuant) {
+            mbar_arrive_expect_tx(&full[stage], kAStageBytes + kRaw);
+            tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
+            bulk_load(smR + stage * kRaw, packed + (static_cast<int64_t>(tc.n_tile) * nk + kb) * kRaw, kRaw,
+                      &full[stage]);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], kAStageBytes + kBStageBytes);
+            tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
+            tma_load_2d(smB + stage * kBStageBytes, tmB, &full[stage], kb * kGemmBK, yb);
+          }
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
@@ -325,7 +478,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kGemmBN;
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
+          uint64_t* ready = kQuant ? &bready[stage] : &full[stage];
+          if (!mbar_wait(ready, phase, p.err, kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(smA + stage * kAStageBytes);
           const uint32_t b0 = smem_u32(smB + stage * kBStageBytes);
@@ -335,14 +489,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
-          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         umma_commit(&acc_full[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
-  } else {
+  } else if (warp < 6) {
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
@@ -359,6 +513,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  } else if (kQuant) {
+    // Dequant warps 6.. : thread = one B tile row per stage.
+    const int r = threadIdx.x - 6 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nk; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, p.err, kDevTimeoutDequant));
+        if (!ok) break;
+        for (int rr = r; rr < kGemmBN; rr += kDqThreads)
+          dequant_row<BSRC>(smR + stage * kRaw, smB + stage * kBStageBytes, rr);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[stage]);
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
     }
   }
 
@@ -385,6 +557,21 @@ EncodeTiledFn get_encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   }
   return fn;
+}
+
+template <int BSRC>
+cudaError_t launch_gemm_t(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
+                          int num_sms, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm_smem_bytes<BSRC>());
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int grid = std::min(args.total_tiles, num_sms);
+  gemm_kernel<BSRC><<<grid, gemm_threads<BSRC>(), gemm_smem_bytes<BSRC>(), stream>>>(a, b0, b1, args);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -417,18 +604,20 @@ void gemm_finalize_groups(GemmArgs& a) {
 
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                         int bsrc, int num_sms, cudaStream_t stream) {
-  if (bsrc != kBSrcBf16) return cudaErrorNotSupported;
   if (args.total_tiles <= 0) return cudaSuccess;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kGemmSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  switch (bsrc) {
+    case kBSrcBf16: return launch_gemm_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
+    case kBSrcQ4_K:
+    case kBSrcQ8_0: {
+      if (args.K % kGemmBK) return cudaErrorInvalidValue;
+      for (int i = 0; i < args.n_groups; ++i)
+        if (!args.qb[args.groups[i].wsel].packed || (reinterpret_cast<uintptr_t>(args.qb[args.groups[i].wsel].packed) & 15))
+          return cudaErrorInvalidValue;
+      return bsrc == kBSrcQ4_K ? launch_gemm_t<kBSrcQ4_K>(a, b0, b1, args, num_sms, stream)
+                               : launch_gemm_t<kBSrcQ8_0>(a, b0, b1, args, num_sms, stream);
+    }
+    default: return cudaErrorNotSupported;
   }
-  const int grid = std::min(args.total_tiles, num_sms);
-  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b0, b1, args);
-  return cudaGetLastError();
 }
 
 }  // namespace dcpp

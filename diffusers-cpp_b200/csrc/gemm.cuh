@@ -17,8 +17,8 @@ constexpr int kGemmMaxGroups = 8; // row groups (txt/img stream x batch)
 // B operand source of a GEMM launch.
 enum GemmBSource : int {
   kBSrcBf16 = 0,   // bf16 weight [N, K] loaded by TMA (128B swizzle)
-  kBSrcQ8_0 = 1,   // Q8_0 weight repacked (int8 [N,K] + f16 scales [N,K/32]), dequantised in smem
-  kBSrcQ4_K = 2,   // Q4_K weight repacked (nibbles [N,K/2] + scale/min pairs), dequantised in smem
+  kBSrcQ8_0 = 1,   // Q8_0 weight in the packed stage layout, dequantised in smem inside the GEMM
+  kBSrcQ4_K = 2,   // Q4_K weight in the packed stage layout, dequantised in smem inside the GEMM
 };
 
 // Epilogue of a GEMM launch.  The accumulator is f32 in TMEM; each
@@ -70,9 +70,11 @@ struct EpilogueArgs {
   int64_t ld_mlp;
 };
 
+// A quantised weight packed per (256-row tile, 64-K stage) by
+// launch_pack_weight (dequant.cu); stage (n_tile, kb) starts at
+// packed + (n_tile * K/64 + kb) * packed_stage_bytes(type).
 struct QuantB {
-  const void* qs;            // Q8_0: int8 [N, K]; Q4_K: uint8 [N, K/2]
-  const void* scales;        // Q8_0: f16 [N, K/32]; Q4_K: float2 [N, K/32] (scale, min)
+  const void* packed;
 };
 
 struct GemmArgs {
@@ -95,6 +97,11 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, u
 // bf16 weights (box 64 x 256) when bsrc == kBSrcBf16.
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                         const GemmArgs& args, int bsrc, int num_sms, cudaStream_t stream);
+
+// Bytes of one packed (256-row, 64-K) stage: Q4_K 10240, Q8_0 17408.
+int packed_stage_bytes(int ggml_type);
+// Total bytes of a packed [N, K] weight (N padded to 256 rows).
+size_t packed_bytes(int ggml_type, int64_t N, int64_t K);
 
 // Fill the tile prefix sums of `args` from its groups.
 void gemm_finalize_groups(GemmArgs& args);

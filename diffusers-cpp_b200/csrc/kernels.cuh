@@ -16,6 +16,9 @@ constexpr int kTypeBF16 = 30;
 // ---- dequant.cu
 cudaError_t launch_dequant_f32(int type, const void* blocks, int64_t n, float* out, cudaStream_t s);
 cudaError_t launch_dequant_bf16(int type, const void* blocks, int64_t n, uint16_t* out, cudaStream_t s);
+// Raw GGUF rows [N, K] (Q4_K / Q8_0) -> the packed stage layout read by the
+// fused-dequant GEMM (gemm.cuh QuantB; packed_bytes(type, N, K) bytes).
+cudaError_t launch_pack_weight(int type, const void* raw, int64_t N, int64_t K, void* out, cudaStream_t s);
 
 // ---- rowops.cu
 constexpr int kMaxNormSegments = 8;

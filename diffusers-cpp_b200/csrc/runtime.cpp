@@ -290,6 +290,49 @@ dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* w, int64_t N, int64_
   });
 }
 
+dcpp_status dcpp_packed_bytes(int type, int64_t N, int64_t K, size_t* out) {
+  if (!out || N <= 0 || K <= 0) return DCPP_ERR_INVALID_ARG;
+  if ((type != DCPP_TYPE_Q4_K && type != DCPP_TYPE_Q8_0) || (type == DCPP_TYPE_Q4_K && K % 256) || K % 64)
+    return DCPP_ERR_UNSUPPORTED;
+  *out = dcpp::packed_bytes(type, N, K);
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_pack_weight(dcpp_ctx* ctx, int type, const void* raw, int64_t N, int64_t K, void* out) {
+  return guarded(ctx, "dcpp_pack_weight", [&] {
+    if (!raw || !out || N <= 0 || K <= 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_pack_weight: bad argument");
+    if ((type != DCPP_TYPE_Q4_K && type != DCPP_TYPE_Q8_0) || (type == DCPP_TYPE_Q4_K && K % 256) || K % 64)
+      dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_pack_weight: Q4_K (K % 256 == 0) or Q8_0 (K % 64 == 0) only");
+    dcpp::cuda_check(dcpp::launch_pack_weight(type, raw, N, K, out, ctx->stream), "pack weight");
+  });
+}
+
+dcpp_status dcpp_gemm_packed(dcpp_ctx* ctx, int wtype, const void* packed, int64_t N, int64_t K, const uint16_t* x,
+                             int64_t M, float* y) {
+  return guarded(ctx, "dcpp_gemm_packed", [&] {
+    if (!packed || !x || !y || N <= 0 || K <= 0 || M <= 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_gemm_packed: bad argument");
+    if ((wtype != DCPP_TYPE_Q4_K && wtype != DCPP_TYPE_Q8_0) || K % 64)
+      dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm_packed: packed Q4_K / Q8_0 weights with K % 64 == 0 only");
+    if (M > INT32_MAX / 2 || N > INT32_MAX / 2) dcpp::fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm_packed: size too large");
+    CUtensorMap ta;
+    dcpp::cuda_check(dcpp::make_tmap_bf16(&ta, x, K, M, K, dcpp::kGemmBM), "tensor map (x)");
+    dcpp::GemmArgs a{};
+    a.N = static_cast<int32_t>(N);
+    a.K = static_cast<int32_t>(K);
+    a.n_groups = 1;
+    a.groups[0].rows = static_cast<int32_t>(M);
+    a.ep.mode = dcpp::kEpiF32;
+    a.ep.out_f32 = y;
+    a.ep.ld_out = N;
+    a.qb[0].packed = packed;
+    a.qb[1].packed = packed;
+    a.err = ctx->d_err;
+    dcpp::gemm_finalize_groups(a);
+    const int bsrc = wtype == DCPP_TYPE_Q4_K ? dcpp::kBSrcQ4_K : dcpp::kBSrcQ8_0;
+    dcpp::cuda_check(dcpp::launch_gemm(ta, ta, ta, a, bsrc, ctx->num_sms, ctx->stream), "launch fused gemm");
+  });
+}
+
 dcpp_status dcpp_layernorm_mod(dcpp_ctx* ctx, const float* x, int64_t rows, int64_t D, const float* shift,
                                const float* scale, float eps, uint16_t* y) {
   return guarded(ctx, "dcpp_layernorm_mod", [&] {

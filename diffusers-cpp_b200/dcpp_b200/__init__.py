@@ -79,6 +79,10 @@ _SIGNATURES = {
     "dcpp_gemm": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, _vp]),
     "dcpp_gemm_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64,
                                          _vp]),
+    "dcpp_packed_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]),
+    "dcpp_pack_weight": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp]),
+    "dcpp_gemm_packed": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64,
+                                        _vp]),
     "dcpp_layernorm_mod": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, _vp, ctypes.c_float, _vp]),
     "dcpp_attention": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp,
                                       ctypes.c_float, _vp, ctypes.c_int, _c_i64p, ctypes.c_float, _vp]),
@@ -196,6 +200,12 @@ class Context:
     def gemm(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
         self.check(lib().dcpp_gemm(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm")
 
+    def pack_weight(self, wtype: int, raw, N: int, K: int, out):
+        self.check(lib().dcpp_pack_weight(self.h, wtype, _ptr(raw), N, K, _ptr(out)), "pack_weight")
+
+    def gemm_packed(self, wtype: int, packed, N: int, K: int, x_bf16, M: int, y):
+        self.check(lib().dcpp_gemm_packed(self.h, wtype, _ptr(packed), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_packed")
+
     def gemm_noalloc(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
         """Like gemm(), but allocates no device memory: for callers whose
         device memory is owned by someone else or must not change mid-run
@@ -227,6 +237,14 @@ class Context:
 
     def allreduce(self, buf, count: int, dtype: int = TYPE_F32):
         self.check(lib().dcpp_allreduce(self.h, _ptr(buf), count, dtype), "allreduce")
+
+
+def packed_bytes(gtype: int, N: int, K: int) -> int:
+    out = ctypes.c_size_t()
+    st = lib().dcpp_packed_bytes(gtype, N, K, ctypes.byref(out))
+    if st != DCPP_OK:
+        raise DcppError(st, f"packed_bytes({gtype}, {N}, {K})")
+    return out.value
 
 
 def row_bytes(gtype: int, n: int) -> int:

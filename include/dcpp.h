@@ -114,12 +114,25 @@ dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* d_in, int64_t n, uint16
 
 /* y[M,N] (f32) = x[M,K] (bf16) . W[N,K]^T, W of ggml type wtype.
  * The ggml_mul_mat(W, x) of Linear::forward (src/nn/Linear.cpp:17-36,
- * Runtime.hpp:136 mul_mat).  Runs on the tcgen05/TMEM tensor-core GEMM;
- * quantised W is dequantised inside the GEMM (fused producer) unless
- * the context's weight mode says otherwise.  K % 64 == 0 for tensor-map
- * alignment; M, N arbitrary. */
+ * Runtime.hpp:136 mul_mat).  Runs on the tcgen05/TMEM tensor-core GEMM; a
+ * non-bf16 W is first expanded to bf16 (the exact dequantised values rounded
+ * once) in a context scratch buffer.  K % 8 == 0; M, N arbitrary. */
 dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
                       const uint16_t* d_x, int64_t M, float* d_y);
+
+/* Dequantisation fused into the GEMM (what the model runs).  A Q4_K / Q8_0
+ * weight is first packed once (dcpp_pack_weight) from its GGUF rows into
+ * stages of 256 rows x 64 K, each one contiguous block that a bulk TMA copy
+ * brings into shared memory, holding the raw 4-bit / 8-bit codes and the
+ * block scales (Q4_K: d*sc and dmin*m per 32 weights, Q8_0: d) as bf16.
+ * dcpp_gemm_packed then dequantises each stage in shared memory with packed
+ * bf16x2 arithmetic (w = q*s - m, or q*d, one rounding) straight into the
+ * tensor-core operand layout.  Q4_K needs K % 256 == 0, Q8_0 K % 64 == 0.
+ * dcpp_packed_bytes gives the packed size (N padded to 256 rows). */
+dcpp_status dcpp_packed_bytes(int type, int64_t N, int64_t K, size_t* out_bytes);
+dcpp_status dcpp_pack_weight(dcpp_ctx* ctx, int type, const void* d_raw, int64_t N, int64_t K, void* d_packed);
+dcpp_status dcpp_gemm_packed(dcpp_ctx* ctx, int wtype, const void* d_packed, int64_t N, int64_t K,
+                             const uint16_t* d_x, int64_t M, float* d_y);
 
 /* dcpp_gemm for callers that cannot allocate device memory.  No counterpart
  * in the reference.  Same arguments, result and precision as dcpp_gemm, but
