@@ -18,7 +18,8 @@ def round_bf16(x: np.ndarray) -> np.ndarray:
 
 
 def _f16(b0, b1):
-    return np.frombuffer(np.stack([b0, b1], -1).astype(np.uint8).tobytes(), dtype=np.float16).astype(np.float64)
+    v = np.frombuffer(np.stack([b0, b1], -1).astype(np.uint8).tobytes(), dtype=np.float16).astype(np.float64)
+    return v.reshape(np.shape(b0))
 
 
 def fused_weights(gtype: int, raw: np.ndarray, N: int, K: int) -> np.ndarray:
