@@ -236,15 +236,16 @@ __global__ void pack_weight_kernel(const uint8_t* __restrict__ raw, int64_t N, i
     const float d0 = half_bits_to_f32(static_cast<uint16_t>(b0[0] | (b0[1] << 8)));
     const float d1 = half_bits_to_f32(static_cast<uint16_t>(b1[0] | (b1[1] << 8)));
     *reinterpret_cast<uint32_t*>(sc_out) = bf16_bits(d0) | (static_cast<uint32_t>(bf16_bits(d1)) << 16);
+    // 2 blocks x 32 int8 = 16 words (the blocks are only 2-byte aligned).
     uint32_t w[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint8_t* s = i < 4 ? b0 + 2 + 4 * i : b1 + 2 + 4 * (i - 4);
+    for (int i = 0; i < 16; ++i) {
+      const uint8_t* s = i < 8 ? b0 + 2 + 4 * i : b1 + 2 + 4 * (i - 8);
       w[i] = s[0] | (s[1] << 8) | (s[2] << 16) | (static_cast<uint32_t>(s[3]) << 24);
     }
     uint4* o = reinterpret_cast<uint4*>(qs_out);
-    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
   }
 }
 
