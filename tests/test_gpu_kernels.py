@@ -101,6 +101,36 @@ def test_layernorm_mod_matches_reference(ctx):
     assert ((y.cpu().double() - ref).norm() / ref.norm()).item() < 4e-3
 
 
+def test_attention_full_size_heads_subset(ctx):
+    """The config-2 attention shape (S = 4608, 24 heads); the oracle checks two heads."""
+    B, S, H = 1, 4608, 24
+    g = torch.Generator().manual_seed(11)
+    D = H * 128
+    qkv = torch.randn(B, S, 3 * D, generator=g).to(torch.bfloat16)
+    wq = 1 + 0.1 * torch.randn(128, generator=g)
+    wk = 1 + 0.1 * torch.randn(128, generator=g)
+    ids = torch.zeros(S, 4, dtype=torch.int32)
+    ids[512:, 1] = (torch.arange(S - 512, dtype=torch.int32) // 64)
+    ids[512:, 2] = (torch.arange(S - 512, dtype=torch.int32) % 64)
+    ids[:512, 3] = torch.arange(512, dtype=torch.int32)
+    out = torch.empty(B, S, D, dtype=torch.bfloat16, device="cuda")
+    ctx.attention(qkv.cuda(), B, S, H, wq.cuda(), wk.cuda(), 1e-6, ids.cuda(), (32, 32, 32, 32), 2000.0, out)
+    ctx.synchronize()
+    cos, sin = fo.rope_cos_sin(ids, (32, 32, 32, 32), 2000, torch.float64)
+    x = qkv.double()
+    for h in (0, H - 1):
+        sl = slice(h * 128, (h + 1) * 128)
+        q = x[..., sl].unsqueeze(2)
+        k = x[..., D:2 * D][..., sl].unsqueeze(2)
+        v = x[..., 2 * D:][..., sl].unsqueeze(2)
+        q = fo.apply_rope(fo.rms_norm(q, wq.double(), 1e-6), cos, sin)
+        k = fo.apply_rope(fo.rms_norm(k, wk.double(), 1e-6), cos, sin)
+        ref = fo.sdpa(q, k, v).flatten(2)
+        got = out[..., sl].cpu().double()
+        rel = ((got - ref).norm() / ref.norm()).item()
+        assert rel < 1e-2, (h, rel)
+
+
 @pytest.mark.parametrize("B,S,H", [(1, 200, 2), (2, 333, 3), (1, 1024, 4)])
 def test_attention_matches_oracle(ctx, B, S, H):
     g = torch.Generator().manual_seed(S)
