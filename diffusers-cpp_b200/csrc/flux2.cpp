@@ -602,6 +602,10 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   // Fused dequantisation when every weight of the launch is packed and of
   // one quantised type; otherwise expand to bf16 first (or use bf16 as is).
   const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
+  int64_t total_rows = 0;
+  for (auto& g : groups) total_rows += g.rows;
+  const bool pair = ctx_.use_pair(total_rows);
+  const int tile_m = pair ? 256 : kGemmBM;
   if (fused) {
     int64_t a_rows = 0;
     for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
@@ -617,13 +621,16 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     args.err = ctx_.d_err;
     args.qb[0].packed = w0->packed;
     args.qb[1].packed = w1 ? w1->packed : w0->packed;
-    gemm_finalize_groups(args);
+    gemm_finalize_groups(args, tile_m);
     const int bsrc = w0->type == kTypeQ4_K ? kBSrcQ4_K : kBSrcQ8_0;
     double flops = 0.0;
     for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
     Ctx* c = &ctx_;
-    building_->push_back({[st, args, c, bsrc](cudaStream_t s) {
-                            cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
+    building_->push_back({[st, args, c, bsrc, pair](cudaStream_t s) {
+                            if (pair)
+                              cuda_check(launch_gemm_pair(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm (pair)");
+                            else
+                              cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
                           },
                           1, kOpGemm, flops});
     return;
@@ -636,8 +643,8 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
   auto st = std::make_shared<std::array<CUtensorMap, 3>>();
   cuda_check(make_tmap_bf16(&(*st)[0], a, K, a_rows, lda, kGemmBM), "tensor map A");
-  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, kGemmBN), "tensor map B0");
-  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, kGemmBN), "tensor map B1");
+  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, pair ? 128 : kGemmBN), "tensor map B0");
+  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, pair ? 128 : kGemmBN), "tensor map B1");
   GemmArgs args{};
   args.N = static_cast<int32_t>(N);
   args.K = static_cast<int32_t>(K);
@@ -646,7 +653,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   for (size_t i = 0; i < groups.size(); ++i) args.groups[i] = groups[i];
   args.ep = ep;
   args.err = ctx_.d_err;
-  gemm_finalize_groups(args);
+  gemm_finalize_groups(args, tile_m);
   Ctx* c = &ctx_;
   if (w0->type != kTypeBF16) {
     const DevWeight* w = w0;
@@ -666,8 +673,12 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   }
   double flops = 0.0;
   for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
-  building_->push_back({[st, args, c](cudaStream_t s) {
-                          cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
+  building_->push_back({[st, args, c, pair](cudaStream_t s) {
+                          if (pair)
+                            cuda_check(launch_gemm_pair((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
+                                       "gemm (pair)");
+                          else
+                            cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
                         },
                         1, kOpGemm, flops});
 }

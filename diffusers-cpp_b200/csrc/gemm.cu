@@ -53,11 +53,14 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 // ------------------------------------------------------------------ epilogue
 // One thread = one row of the tile; `taddr` addresses this warp's 32 TMEM
 // lanes at the accumulator's column 0.
-__device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_in_tile,
+// `row_base` is the first row (within the group) of the 128 accumulator rows
+// this CTA holds: m_tile * 128 for 1-SM tiles, m_tile * 256 + rank * 128 for
+// the 2-SM pair.
+__device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_base, int row_in_tile,
                                              uint32_t taddr) {
   const GemmGroup& G = p.groups[tc.g];
   const EpilogueArgs& e = p.ep;
-  const int local_row = tc.m_tile * kGemmBM + row_in_tile;
+  const int local_row = row_base + row_in_tile;
   const bool row_ok = local_row < G.rows;
   const int64_t row = static_cast<int64_t>(G.orow0) + local_row;
   const int col0 = tc.n_tile * kGemmBN;
@@ -340,14 +343,16 @@ __device__ __forceinline__ uint4 q8_chunk(uint32_t w0, uint32_t w1, uint32_t d2)
   return o;
 }
 
-template <int BSRC>
+// kRows: rows in the raw stage (256 for the 1-SM tile, 128 per CTA of a pair):
+// [kRows x nibbles / int8][kRows x scales].
+template <int BSRC, int kRows = kGemmBN>
 __device__ __forceinline__ void dequant_row(const uint8_t* raw, uint8_t* btile, int r) {
   uint8_t* dst = btile + r * 128;
   const int sw = r & 7;
   if (BSRC == kBSrcQ4_K) {
     const uint4 qa = *reinterpret_cast<const uint4*>(raw + r * 32);
     const uint4 qb = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
-    const uint2 sc = *reinterpret_cast<const uint2*>(raw + kGemmBN * 32 + r * 8);
+    const uint2 sc = *reinterpret_cast<const uint2*>(raw + kRows * 32 + r * 8);
     // sc.x = (s0, m0), sc.y = (s1, m1) as bf16 (low half first)
     const uint32_t s0 = prmt(sc.x, 0, 0x1010), nm0 = prmt(sc.x, 0, 0x3232) ^ 0x80008000u;
     const uint32_t s1 = prmt(sc.y, 0, 0x1010), nm1 = prmt(sc.y, 0, 0x3232) ^ 0x80008000u;
@@ -364,7 +369,7 @@ __device__ __forceinline__ void dequant_row(const uint8_t* raw, uint8_t* btile, 
     }
   } else {
     const uint4* q = reinterpret_cast<const uint4*>(raw + r * 64);
-    const uint32_t ds = *reinterpret_cast<const uint32_t*>(raw + kGemmBN * 64 + r * 4);
+    const uint32_t ds = *reinterpret_cast<const uint32_t*>(raw + kRows * 64 + r * 4);
     const uint32_t d0 = prmt(ds, 0, 0x1010), d1 = prmt(ds, 0, 0x3232);
 #pragma unroll
     for (int h = 0; h < 4; ++h) {  // 16 bytes = K 16h .. 16h+15
@@ -509,7 +514,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
       tc_fence_after();
       const TileCoord tc = decode_tile(p, t);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-      epilogue_row(p, tc, row_in_tile, taddr);
+      epilogue_row(p, tc, tc.m_tile * kGemmBM, row_in_tile, taddr);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -539,6 +544,212 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ 2-SM kernel
+// A cluster of two CTAs (two SMs) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2: CTA rank r holds A rows [128 r, 128 r + 128) and
+// B rows (output columns) [128 r, 128 r + 128) of the tile in its own shared
+// memory and receives accumulator rows [128 r, 128 r + 128) x 256 in its own
+// TMEM.  Rank 0 issues the MMAs; every shared-memory stage holds half the
+// bytes of the 1-SM kernel per SM, and with quantised weights each SM
+// dequantises only its 128 B rows.  Barriers: full / bready / acc_empty live
+// in rank 0 (the MMA waits on them; rank 1 signals them through shared::cluster
+// addresses), empty / acc_full in both (the MMA's commit arrives in both).
+template <int BSRC>
+struct PairCfg;
+template <>
+struct PairCfg<kBSrcBf16> {
+  static constexpr int kStages = 6;
+  static constexpr int kQs = 0, kSc = 0;
+  static constexpr int kDequantWarps = 0;
+};
+template <>
+struct PairCfg<kBSrcQ4_K> {
+  static constexpr int kStages = 5;
+  static constexpr int kQs = 32, kSc = 8;
+  static constexpr int kDequantWarps = 4;
+};
+template <>
+struct PairCfg<kBSrcQ8_0> {
+  static constexpr int kStages = 5;
+  static constexpr int kQs = 64, kSc = 4;
+  static constexpr int kDequantWarps = 4;
+};
+constexpr int kPairA = 128 * kGemmBK * 2;  // 16 KB per CTA
+constexpr int kPairB = 128 * kGemmBK * 2;  // 16 KB per CTA (its half of the B tile)
+
+template <int BSRC>
+__host__ __device__ constexpr int pair_raw_bytes() { return 128 * (PairCfg<BSRC>::kQs + PairCfg<BSRC>::kSc); }
+template <int BSRC>
+__host__ __device__ constexpr int pair_threads() { return (6 + PairCfg<BSRC>::kDequantWarps) * 32; }
+template <int BSRC>
+__host__ __device__ constexpr int pair_smem_bytes() {
+  return PairCfg<BSRC>::kStages * (kPairA + kPairB + pair_raw_bytes<BSRC>()) + 1024 + 256;
+}
+
+template <int BSRC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>(), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+  constexpr int kStages = PairCfg<BSRC>::kStages;
+  constexpr bool kQuant = BSRC != kBSrcBf16;
+  constexpr int kQs = PairCfg<BSRC>::kQs, kSc = PairCfg<BSRC>::kSc;
+  constexpr int kRaw = pair_raw_bytes<BSRC>();
+  constexpr int kDqWarps = PairCfg<BSRC>::kDequantWarps;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smA + kStages * kPairA;
+  uint8_t* smR = smB + kStages * kPairB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw);
+  uint64_t* full = bars;                     // [stages] rank 0: A (+ B) bytes of both CTAs
+  uint64_t* empty = bars + kStages;          // [stages] both: the MMA released the stage
+  uint64_t* rfull = bars + 2 * kStages;      // [stages] both: this CTA's raw quantised rows landed
+  uint64_t* bready = bars + 3 * kStages;     // [stages] rank 0: dequantised B halves of both CTAs
+  uint64_t* acc_full = bars + 4 * kStages;   // [2] both
+  uint64_t* acc_empty = acc_full + 2;        // [2] rank 0: epilogue threads of both CTAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int nk = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&rfull[s], 1);
+      mbar_init(&bready[s], kQuant ? 2 * kDqWarps : 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 256);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    if (!kQuant) {
+      tma_prefetch_desc(&tmB0);
+      tma_prefetch_desc(&tmB1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive / TMA
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        const TileCoord tc = decode_tile(p, t);
+        const GemmGroup& G = p.groups[tc.g];
+        const int ya = G.row0 + tc.m_tile * 256 + static_cast<int>(rank) * 128;
+        const int yb = tc.n_tile * kGemmBN + static_cast<int>(rank) * 128;
+        const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
+        const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          const uint32_t full0 = mapa_shared(smem_u32(&full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPairB));
+          tma_load_2d_pair(smA + stage * kPairA, &tmA, full0, kb * kGemmBK, ya);
+          if (kQuant) {
+            const uint8_t* st = packed + (static_cast<int64_t>(tc.n_tile) * nk + kb) * (256 * (kQs + kSc));
+            mbar_arrive_expect_tx(&rfull[stage], kRaw);
+            bulk_load(smR + stage * kRaw, st + rank * 128 * kQs, 128 * kQs, &rfull[stage]);
+            bulk_load(smR + stage * kRaw + 128 * kQs, st + 256 * kQs + rank * 128 * kSc, 128 * kSc, &rfull[stage]);
+          } else {
+            tma_load_2d_pair(smB + stage * kPairB, tmB, full0, kb * kGemmBK, yb);
+          }
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(256, kGemmBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
+          if (kQuant && !mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smA + stage * kPairA);
+          const uint32_t b0 = smem_u32(smB + stage * kPairB);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
+                           (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc], 0x3);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else if (warp < 6) {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < p.total_tiles; t += npairs) {
+      bool ok = mbar_wait(&acc_full[acc], acc_phase, p.err, kDevTimeoutAccum);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const TileCoord tc = decode_tile(p, t);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
+      epilogue_row(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  } else if (kQuant) {
+    const int r = threadIdx.x - 6 * 32;  // B row within this CTA's half
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+      for (int kb = 0; kb < nk; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&rfull[stage], phase, p.err, kDevTimeoutDequant));
+        if (!ok) break;
+        dequant_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPairB, r);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bready[stage]), 0));
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no remote arrive may target a CTA that has exited
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -574,7 +785,58 @@ cudaError_t launch_gemm_t(const CUtensorMap& a, const CUtensorMap& b0, const CUt
   return cudaGetLastError();
 }
 
+template <int BSRC>
+cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                               const GemmArgs& args, int num_sms, cudaStream_t stream) {
+  static int max_clusters = 0;
+  if (max_clusters == 0) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pair_smem_bytes<BSRC>());
+    if (e != cudaSuccess) return e;
+    // Persistent grid: only as many pairs as can be resident at once (a GPC
+    // with an odd SM count leaves one SM out of the pairs).
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(pair_threads<BSRC>(), 1, 1);
+    cfg.dynamicSmemBytes = pair_smem_bytes<BSRC>();
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BSRC>, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    max_clusters = n;
+  }
+  const int pairs = std::min(args.total_tiles, max_clusters);
+  gemm_pair_kernel<BSRC><<<2 * pairs, pair_threads<BSRC>(), pair_smem_bytes<BSRC>(), stream>>>(a, b0, b1, args);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
+                             int bsrc, int num_sms, cudaStream_t stream) {
+  if (args.total_tiles <= 0) return cudaSuccess;
+  switch (bsrc) {
+    case kBSrcBf16: return launch_gemm_pair_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
+    case kBSrcQ4_K:
+    case kBSrcQ8_0: {
+      if (args.K % kGemmBK) return cudaErrorInvalidValue;
+      for (int i = 0; i < args.n_groups; ++i)
+        if (!args.qb[args.groups[i].wsel].packed ||
+            (reinterpret_cast<uintptr_t>(args.qb[args.groups[i].wsel].packed) & 15))
+          return cudaErrorInvalidValue;
+      return bsrc == kBSrcQ4_K ? launch_gemm_pair_t<kBSrcQ4_K>(a, b0, b1, args, num_sms, stream)
+                               : launch_gemm_pair_t<kBSrcQ8_0>(a, b0, b1, args, num_sms, stream);
+    }
+    default: return cudaErrorNotSupported;
+  }
+}
 
 cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                            uint64_t ld_elems, uint32_t box_outer) {
@@ -591,11 +853,11 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, u
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-void gemm_finalize_groups(GemmArgs& a) {
+void gemm_finalize_groups(GemmArgs& a, int tile_m) {
   a.n_tiles_n = (a.N + kGemmBN - 1) / kGemmBN;
   int t = 0;
   for (int g = 0; g < a.n_groups; ++g) {
-    a.groups[g].m_tiles = (a.groups[g].rows + kGemmBM - 1) / kGemmBM;
+    a.groups[g].m_tiles = (a.groups[g].rows + tile_m - 1) / tile_m;
     a.groups[g].tile0 = t;
     t += a.groups[g].m_tiles * a.n_tiles_n;
   }

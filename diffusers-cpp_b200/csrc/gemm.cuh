@@ -103,7 +103,14 @@ int packed_stage_bytes(int ggml_type);
 // Total bytes of a packed [N, K] weight (N padded to 256 rows).
 size_t packed_bytes(int ggml_type, int64_t N, int64_t K);
 
-// Fill the tile prefix sums of `args` from its groups.
-void gemm_finalize_groups(GemmArgs& args);
+// The 2-SM variant (CTA pairs, 256 x 256 tiles, tcgen05 cta_group::2).  `args`
+// must be finalised with tile_m = 256; bf16 B maps use a 128-row box (each
+// CTA of the pair loads half of the 256-row B tile).
+cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                             const GemmArgs& args, int bsrc, int num_sms, cudaStream_t stream);
+
+// Fill the tile prefix sums of `args` from its groups (M tile of tile_m rows:
+// 128 for launch_gemm, 256 for launch_gemm_pair).
+void gemm_finalize_groups(GemmArgs& args, int tile_m = kGemmBM);
 
 }  // namespace dcpp

@@ -113,7 +113,8 @@ void gemm_op(Ctx& c, int wtype, const void* w, int64_t N, int64_t K, const uint1
   }
   CUtensorMap ta, tb;
   cuda_check(make_tmap_bf16(&ta, x, K, M, K, kGemmBM), "tensor map (x)");
-  cuda_check(make_tmap_bf16(&tb, wb, K, N, K, kGemmBN), "tensor map (W)");
+  const bool pair = c.use_pair(M);
+  cuda_check(make_tmap_bf16(&tb, wb, K, N, K, pair ? 128 : kGemmBN), "tensor map (W)");
   GemmArgs a{};
   a.N = static_cast<int32_t>(N);
   a.K = static_cast<int32_t>(K);
@@ -125,8 +126,11 @@ void gemm_op(Ctx& c, int wtype, const void* w, int64_t N, int64_t K, const uint1
   a.ep.out_f32 = y;
   a.ep.ld_out = N;
   a.err = c.d_err;
-  gemm_finalize_groups(a);
-  cuda_check(launch_gemm(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm");
+  gemm_finalize_groups(a, pair ? 256 : kGemmBM);
+  if (pair)
+    cuda_check(launch_gemm_pair(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm (pair)");
+  else
+    cuda_check(launch_gemm(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm");
 }
 
 }  // namespace dcpp
@@ -290,6 +294,13 @@ dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* w, int64_t N, int64_
   });
 }
 
+dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind) {
+  return guarded(ctx, "dcpp_set_gemm_kernel", [&] {
+    if (kind < 0 || kind > 2) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_set_gemm_kernel: 0 auto, 1 single-SM, 2 CTA pairs");
+    ctx->gemm_kernel = kind;
+  });
+}
+
 dcpp_status dcpp_packed_bytes(int type, int64_t N, int64_t K, size_t* out) {
   if (!out || N <= 0 || K <= 0) return DCPP_ERR_INVALID_ARG;
   if ((type != DCPP_TYPE_Q4_K && type != DCPP_TYPE_Q8_0) || (type == DCPP_TYPE_Q4_K && K % 256) || K % 64)
@@ -327,9 +338,13 @@ dcpp_status dcpp_gemm_packed(dcpp_ctx* ctx, int wtype, const void* packed, int64
     a.qb[0].packed = packed;
     a.qb[1].packed = packed;
     a.err = ctx->d_err;
-    dcpp::gemm_finalize_groups(a);
+    const bool pair = ctx->use_pair(M);
+    dcpp::gemm_finalize_groups(a, pair ? 256 : dcpp::kGemmBM);
     const int bsrc = wtype == DCPP_TYPE_Q4_K ? dcpp::kBSrcQ4_K : dcpp::kBSrcQ8_0;
-    dcpp::cuda_check(dcpp::launch_gemm(ta, ta, ta, a, bsrc, ctx->num_sms, ctx->stream), "launch fused gemm");
+    if (pair)
+      dcpp::cuda_check(dcpp::launch_gemm_pair(ta, ta, ta, a, bsrc, ctx->num_sms, ctx->stream), "launch fused gemm (pair)");
+    else
+      dcpp::cuda_check(dcpp::launch_gemm(ta, ta, ta, a, bsrc, ctx->num_sms, ctx->stream), "launch fused gemm");
   });
 }
 

@@ -54,6 +54,10 @@ struct Ctx {
   // Scratch for the op-level GEMM (bf16 weights) and staging.
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  // GEMM kernel choice: 0 auto (CTA pairs when a launch has >= 256 rows),
+  // 1 single-SM 128 x 256 tiles, 2 CTA-pair 256 x 256 tiles.
+  int gemm_kernel = 0;
+  bool use_pair(int64_t rows) const { return gemm_kernel == 2 || (gemm_kernel == 0 && rows >= 256); }
   // Tensor parallelism.
   Nccl::Comm comm = nullptr;
   int rank = 0;

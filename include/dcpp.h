@@ -91,6 +91,12 @@ dcpp_status dcpp_memcpy(dcpp_ctx* ctx, void* p_dst, const void* p_src, size_t by
  * (ggml_row_size semantics; n must be a multiple of the block size). */
 dcpp_status dcpp_row_bytes(int type, int64_t n, size_t* out_bytes);
 
+/* GEMM kernel used by this context's GEMM entry points and the models it
+ * creates (read at dcpp_flux2_prepare): 0 = auto (CTA pairs for launches
+ * with >= 256 rows), 1 = single-SM tcgen05 kernel (128 x 256 tiles),
+ * 2 = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles). */
+dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind);
+
 /* Host-side fault injection for failure-path tests: the `nth` next call
  * (1 = the next one) of entry point `name` (e.g. "dcpp_gemm") returns
  * DCPP_ERR_INJECTED without touching the GPU.  name == NULL clears. */

@@ -34,3 +34,11 @@ def ctx():
     c = dcpp_b200.Context(0)
     yield c
     c.close()
+
+
+@pytest.fixture(params=[1, 2], ids=["single_sm", "cta_pair"])
+def gemm_kind(request, ctx):
+    """Run a GEMM test on the single-SM kernel and on the CTA-pair kernel."""
+    ctx.set_gemm_kernel(request.param)
+    yield request.param
+    ctx.set_gemm_kernel(0)

@@ -31,7 +31,7 @@ def run_fused(ctx, gtype, M, N, K, seed):
 
 @pytest.mark.parametrize("gtype", [fo.GGML_Q4_K, fo.GGML_Q8_0])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 520, 512), (7, 33, 768), (1024, 768, 3072)])
-def test_fused_gemm_matches_emulated_operands(ctx, gtype, M, N, K):
+def test_fused_gemm_matches_emulated_operands(ctx, gemm_kind, gtype, M, N, K):
     y, ref, ref_exact = run_fused(ctx, gtype, M, N, K, seed=M + N)
     scale = np.abs(ref).max()
     assert np.abs(y - ref).max() <= 1e-4 * max(scale, 1.0) + 1e-5
@@ -39,7 +39,7 @@ def test_fused_gemm_matches_emulated_operands(ctx, gtype, M, N, K):
     assert rel < 1e-2, rel
 
 
-def test_fused_gemm_many_tiles_large_k(ctx):
+def test_fused_gemm_many_tiles_large_k(ctx, gemm_kind):
     y, ref, _ = run_fused(ctx, fo.GGML_Q4_K, 4608, 2304, 9216, seed=3)
     rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
     assert rel < 3e-5, rel

@@ -71,7 +71,7 @@ def gemm_case(ctx, gtype, M, N, K, seed=0):
 
 @pytest.mark.parametrize("gtype", [fo.GGML_BF16, fo.GGML_Q8_0, fo.GGML_Q4_K, fo.GGML_F16])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 256), (300, 520, 512), (7, 33, 256), (1024, 768, 3072)])
-def test_gemm_matches_fp32_reference(ctx, gtype, M, N, K):
+def test_gemm_matches_fp32_reference(ctx, gemm_kind, gtype, M, N, K):
     y, ref = gemm_case(ctx, gtype, M, N, K)
     err = (y - ref).abs().max().item()
     scale = ref.abs().max().item()
@@ -79,7 +79,7 @@ def test_gemm_matches_fp32_reference(ctx, gtype, M, N, K):
     assert err <= 1e-4 * max(scale, 1.0) + 1e-5, (err, scale)
 
 
-def test_gemm_large_k_and_many_tiles(ctx):
+def test_gemm_large_k_and_many_tiles(ctx, gemm_kind):
     y, ref = gemm_case(ctx, fo.GGML_Q4_K, 4608, 2304, 9216, seed=7)
     rel = ((y - ref).norm() / ref.norm()).item()
     # f32 accumulation over K = 9216 in the tensor-core order vs float64
