@@ -343,6 +343,38 @@ __device__ __forceinline__ uint4 q8_chunk(uint32_t w0, uint32_t w1, uint32_t d2)
   return o;
 }
 
+// Half a row: 32 of the 64 K values (16-byte chunks 4h .. 4h + 3).  Q4_K:
+// h = 0 are the low nibbles (sub-block 2g), h = 1 the high nibbles
+// (sub-block 2g + 1); Q8_0: h selects the 32-weight block.
+template <int BSRC, int kRows>
+__device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* btile, int r, int h) {
+  uint8_t* dst = btile + r * 128;
+  const int sw = r & 7;
+  if (BSRC == kBSrcQ4_K) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(raw + r * 32);
+    const uint4 qb = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + kRows * 32 + r * 8 + h * 4);  // (s, m)
+    const uint32_t s2 = prmt(sc, 0, 0x1010), nm2 = prmt(sc, 0, 0x3232) ^ 0x80008000u;
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    const int sh = 4 * h;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 o = q4_chunk((w[2 * c] >> sh) & 0x0F0F0F0Fu, (w[2 * c + 1] >> sh) & 0x0F0F0F0Fu, s2, nm2);
+      *reinterpret_cast<uint4*>(dst + (((c + 4 * h) ^ sw) << 4)) = o;
+    }
+  } else {
+    const uint4* q = reinterpret_cast<const uint4*>(raw + r * 64 + h * 32);
+    const uint32_t ds = *reinterpret_cast<const uint32_t*>(raw + kRows * 64 + r * 4);
+    const uint32_t d2 = h ? prmt(ds, 0, 0x3232) : prmt(ds, 0, 0x1010);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // 16 bytes = K 32h + 16i .. + 15
+      const uint4 v = q[i];
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 2 * i) ^ sw) << 4)) = q8_chunk(v.x, v.y, d2);
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 2 * i + 1) ^ sw) << 4)) = q8_chunk(v.z, v.w, d2);
+    }
+  }
+}
+
 // kRows: rows in the raw stage (256 for the 1-SM tile, 128 per CTA of a pair):
 // [kRows x nibbles / int8][kRows x scales].
 template <int BSRC, int kRows = kGemmBN>
@@ -565,17 +597,19 @@ struct PairCfg<kBSrcBf16> {
   static constexpr int kQs = 0, kSc = 0;
   static constexpr int kDequantWarps = 0;
 };
+// Eight dequant warps per CTA: thread t dequantises half of B row t % 128
+// (two warps per SM sub-partition, so their instruction latencies overlap).
 template <>
 struct PairCfg<kBSrcQ4_K> {
   static constexpr int kStages = 5;
   static constexpr int kQs = 32, kSc = 8;
-  static constexpr int kDequantWarps = 4;
+  static constexpr int kDequantWarps = 8;
 };
 template <>
 struct PairCfg<kBSrcQ8_0> {
   static constexpr int kStages = 5;
   static constexpr int kQs = 64, kSc = 4;
-  static constexpr int kDequantWarps = 4;
+  static constexpr int kDequantWarps = 8;
 };
 constexpr int kPairA = 128 * kGemmBK * 2;  // 16 KB per CTA
 constexpr int kPairB = 128 * kGemmBK * 2;  // 16 KB per CTA (its half of the B tile)
@@ -727,7 +761,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   } else if (kQuant) {
-    const int r = threadIdx.x - 6 * 32;  // B row within this CTA's half
+    const int t_dq = threadIdx.x - 6 * 32;
+    const int r = t_dq & 127;  // B row within this CTA's half
+    const int h = t_dq >> 7;   // which 32 of the row's 64 K values
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -735,7 +771,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       for (int kb = 0; kb < nk; ++kb) {
         ok = __all_sync(0xffffffffu, mbar_wait(&rfull[stage], phase, p.err, kDevTimeoutDequant));
         if (!ok) break;
-        dequant_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPairB, r);
+        dequant_half_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPairB, r, h);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bready[stage]), 0));
