@@ -641,8 +641,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
   uint64_t* full = bars;                     // [stages] rank 0: A (+ B) bytes of both CTAs
   uint64_t* empty = bars + kStages;          // [stages] both: the MMA released the stage
   uint64_t* rfull = bars + 2 * kStages;      // [stages] both: this CTA's raw quantised rows landed
-  uint64_t* bready = bars + 3 * kStages;     // [stages] rank 0: dequantised B halves of both CTAs
-  uint64_t* acc_full = bars + 4 * kStages;   // [2] both
+  uint64_t* bready = bars + 3 * kStages;     // [stages] both: this CTA's dequant warps wrote its B half
+  uint64_t* bpeer = bars + 4 * kStages;      // [stages] rank 0: rank 1's B half is ready
+  uint64_t* acc_full = bars + 5 * kStages;   // [2] both
   uint64_t* acc_empty = acc_full + 2;        // [2] rank 0: epilogue threads of both CTAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
@@ -658,7 +659,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&rfull[s], 1);
-      mbar_init(&bready[s], kQuant ? 2 * kDqWarps : 1);
+      mbar_init(&bready[s], kQuant ? kDqWarps : 1);
+      mbar_init(&bpeer[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -726,7 +728,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         const uint32_t d_tmem = tmem_base + acc * kGemmBN;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
-          if (kQuant && !mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant)) { ok = false; break; }
+          if (kQuant && (!mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant) ||
+                         !mbar_wait_cluster(&bpeer[stage], phase, p.err, kDevTimeoutDequant))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t a0 = smem_u32(smA + stage * kPairA);
           const uint32_t b0 = smem_u32(smB + stage * kPairB);
@@ -741,6 +747,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         if (!ok) break;
         umma_commit_pair(&acc_full[acc], 0x3);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    } else if (lane == 0 && kQuant) {
+      // Rank 1: forward "my B half is dequantised" to rank 0 with one
+      // cluster-scope arrive per stage, so the dequant warps themselves only
+      // arrive on a local barrier.
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant)) { ok = false; break; }
+          mbar_arrive_cluster(mapa_shared(smem_u32(&bpeer[stage]), 0));
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
       }
     }
   } else if (warp < 6) {
@@ -774,7 +794,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         dequant_half_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPairB, r, h);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bready[stage]), 0));
+        if (lane == 0) mbar_arrive(&bready[stage]);
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
