@@ -337,6 +337,8 @@ def run_ours(args):
                 "weights": spec["wtype"],
                 "l2": "no flush: each step streams > 2 GB of weights, far above the 126 MB L2",
                 "cuda_graph": not args.no_graph,
+                "dequant": ("fused into the GEMM" if os.environ.get("DCPP_FUSED_DEQUANT") == "1"
+                            else "per-projection expansion to bf16 before each GEMM"),
             },
             "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "dcpp_flux2_denoise_step with pinned host latents/encoder/ids in, latents out"},

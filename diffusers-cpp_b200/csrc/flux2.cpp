@@ -224,7 +224,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   int64_t tot = 0;
   for (auto d : cfg_.axes_dims_rope) tot += d;
   if (tot != cfg_.attention_head_dim) fail(DCPP_ERR_INVALID_ARG, "axes_dims_rope must sum to attention_head_dim");
-  if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) != "0";
+  if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) == "1";
   build_registry();
 }
 
@@ -604,7 +604,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
   const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
   int64_t total_rows = 0;
   for (auto& g : groups) total_rows += g.rows;
-  const bool pair = ctx_.use_pair(total_rows);
+  const bool pair = ctx_.use_pair(total_rows, fused);
   const int tile_m = pair ? 256 : kGemmBM;
   if (fused) {
     int64_t a_rows = 0;

@@ -338,7 +338,7 @@ dcpp_status dcpp_gemm_packed(dcpp_ctx* ctx, int wtype, const void* packed, int64
     a.qb[0].packed = packed;
     a.qb[1].packed = packed;
     a.err = ctx->d_err;
-    const bool pair = ctx->use_pair(M);
+    const bool pair = ctx->use_pair(M, /*fused_dequant=*/true);
     dcpp::gemm_finalize_groups(a, pair ? 256 : dcpp::kGemmBM);
     const int bsrc = wtype == DCPP_TYPE_Q4_K ? dcpp::kBSrcQ4_K : dcpp::kBSrcQ8_0;
     if (pair)

@@ -54,10 +54,14 @@ struct Ctx {
   // Scratch for the op-level GEMM (bf16 weights) and staging.
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
-  // GEMM kernel choice: 0 auto (CTA pairs when a launch has >= 256 rows),
-  // 1 single-SM 128 x 256 tiles, 2 CTA-pair 256 x 256 tiles.
+  // GEMM kernel choice: 0 auto, 1 single-SM 128 x 256 tiles, 2 CTA-pair
+  // 256 x 256 tiles.  Auto takes CTA pairs for bf16 weights and >= 256 rows,
+  // and the single-SM kernel for fused dequantisation (measured faster: the
+  // pair kernel is bound by shared-memory bandwidth once B is written there).
   int gemm_kernel = 0;
-  bool use_pair(int64_t rows) const { return gemm_kernel == 2 || (gemm_kernel == 0 && rows >= 256); }
+  bool use_pair(int64_t rows, bool fused_dequant = false) const {
+    return gemm_kernel == 2 || (gemm_kernel == 0 && rows >= 256 && !fused_dequant);
+  }
   // Tensor parallelism.
   Nccl::Comm comm = nullptr;
   int rank = 0;

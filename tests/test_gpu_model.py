@@ -56,6 +56,21 @@ def test_forward_matches_oracle(ctx, wtype):
     assert r < V_TOL, r
 
 
+@pytest.mark.parametrize("wtype", [fo.GGML_Q8_0, fo.GGML_Q4_K])
+def test_forward_fused_dequant_matches_oracle(ctx, monkeypatch, wtype):
+    """The block projections run on the fused-dequant GEMM (weights packed at load)."""
+    monkeypatch.setenv("DCPP_FUSED_DEQUANT", "1")
+    c = cfg_small(num_layers=2, num_single_layers=2)
+    m, params = build(ctx, c, wtype, seed=21, gh=16, gw=16, nt=40)
+    hid, enc, iid, tid = synth.make_inputs(c, 1, 16, 16, 40, seed=22)
+    t = torch.tensor([0.6], dtype=torch.float32)
+    out = torch.empty(1, 256, c.in_channels, dtype=torch.float32)
+    m.forward(hid, enc, t, iid, tid, out)
+    ref = fo.Flux2Oracle(oracle_cfg(c), params).forward(hid, enc, t, iid, tid)
+    r = rel(out, ref)
+    assert r < V_TOL, r
+
+
 def test_forward_batch2_ragged_text_guidance(ctx):
     c = cfg_small(num_layers=2, num_single_layers=2, guidance_embeds=True)
     m, params = build(ctx, c, fo.GGML_Q8_0, seed=4, B=2, gh=10, gw=13, nt=131)
