@@ -201,20 +201,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max as 8 independent chains (a single 128-long dependent chain
+      // would dominate the softmax latency).
+      float mp[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      for (int k = 0; k < 8; ++k) mp[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mp[i & 7] = fmaxf(mp[i & 7], s[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       mx *= c;
       // Lazy rescale: keep the running maximum unless it grows by > 2^8.
       const bool grow = mx > m + kRescaleThreshold;
       const float m_use = grow ? mx : m;
       const float alpha = grow ? ex2(m - m_use) : 1.0f;
-      float sum = 0.f;
+      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
         s[i] = ex2(fmaf(s[i], c, -m_use));
-        sum += s[i];
+        sp[i & 7] += s[i];
       }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
       m = m_use;
       if (j > 0) {
