@@ -5,21 +5,24 @@
 //
 // Layouts (bf16): Q, K [B*H, S, 128] (row per token), V^T [B*H, 128, Sp]
 // (row per head-dim channel, Sp = S rounded up to 64, zero padded), so every
-// MMA operand is K-major and arrives through TMA with the 128-byte swizzle.
+// shared-memory operand is K-major and arrives through TMA with the 128-byte
+// swizzle.
 //
 // One CTA = one 128-row query tile of one (batch, head); 192 threads:
-//   warp 0     TMA: Q once, then K_j / V_j^T tiles of 128 keys (2 stages)
+//   warp 0     TMA: Q once, then K_j / V_j^T tiles of 128 keys (3 stages)
 //   warp 1     TMEM allocation and the single MMA-issuing thread:
-//                S_j = Q K_j^T   (M 128, N 128 keys, K 128)   -> TMEM S[j % 2]
-//                O  += P_j V_j   (M 128, N 128, K 128 keys)   -> TMEM O
-//              S_{j+1} is issued before waiting for P_j, so the tensor core
-//              computes the next scores while the softmax runs.
+//                S_j = Q K_j^T   (M 128, N 128 keys, K 128) -> TMEM buffer j % 3
+//                O  += P_j V_j   (A = P_j read from TMEM, B = V_j^T from smem)
+//              Order S_0, S_1, PV_0, S_2, PV_1, ...: the scores of the next
+//              tiles are computed while the softmax runs.
 //   warps 2-5  softmax, one thread per query row (its TMEM lane): online
-//              softmax in the exp2 domain, P_j written to shared memory in
-//              the swizzled K-major layout; O is rescaled in TMEM only when
-//              a row maximum grows by more than 2^8 (otherwise the stale
-//              maximum is kept, which is exact because l uses the same one).
-//              At the end they normalise O by l and store bf16 rows.
+//              softmax in the exp2 domain; P_j (bf16) is written back over
+//              its own S_j in TMEM (no shared memory, no proxy fence); O is
+//              rescaled in TMEM only when a row maximum grows by more than
+//              2^8 (otherwise the stale maximum is kept, which is exact
+//              because l uses the same one).  At the end they normalise O
+//              by l and store bf16 rows.
+// TMEM: S/P buffers at columns 0, 128, 256 and O at 384 (512 allocated).
 #include "attention_tc.cuh"
 #include "common.cuh"
 
@@ -29,14 +32,17 @@ namespace {
 
 constexpr int kBQ = 128;                    // query rows per CTA
 constexpr int kBKV = 128;                   // keys per tile
-constexpr int kHalfBytes = 128 * 128;       // one 64-wide swizzle atom column block of 128 rows: 16 KB
+constexpr int kKVStages = 3;
+constexpr int kSBufs = 3;
+constexpr int kHalfBytes = 128 * 128;       // one 64-wide swizzle-atom column block of 128 rows: 16 KB
 constexpr int kTileBytes = 2 * kHalfBytes;  // 128 x 128 bf16 = 32 KB
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 512;              // S0 [0,128), S1 [128,256), O [256,384)
-constexpr int kSmemBytes = 6 * kTileBytes + 1024 + 256;  // Q, K x2, V x2, P + barriers
+constexpr int kTmemCols = 512;
+constexpr int kOCol = 384;
+constexpr int kSmemBytes = (1 + 2 * kKVStages) * kTileBytes + 1024 + 256;  // Q, (K, V) x 3 + barriers
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
       " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -48,6 +54,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// O (+)= A[tmem] * B[smem desc]^T, A (M x K bf16) read from TMEM.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -61,18 +78,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTileBytes;       // 2 stages
-  uint8_t* sV = smem + 3 * kTileBytes;   // 2 stages
-  uint8_t* sP = smem + 5 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* p_empty = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint8_t* sK = smem + kTileBytes;                      // kKVStages stages
+  uint8_t* sV = smem + (1 + kKVStages) * kTileBytes;    // kKVStages stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (1 + 2 * kKVStages) * kTileBytes);
+  uint64_t* q_full = bars;                     // Q landed
+  uint64_t* kv_full = bars + 1;                // [3] K_j, V_j landed
+  uint64_t* kv_empty = kv_full + kKVStages;    // [3] PV_j done with the stage
+  uint64_t* s_full = kv_empty + kKVStages;     // [3] S_j computed in buffer j % 3
+  uint64_t* s_free = s_full + kSBufs;          // [3] PV_j read P_j: buffer free
+  uint64_t* p_full = s_free + kSBufs;          // P_j written, O rescaled (128 arrivals)
+  uint64_t* o_done = p_full + 1;               // PV_j done: O current
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -83,14 +99,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_free[i], 1);
     }
     mbar_init(p_full, 128);
-    mbar_init(p_empty, 1);
+    mbar_init(o_done, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -113,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_3d(sQ, &tmQ, q_full, 0, qt * kBQ, bh);
       tma_load_3d(sQ + kHalfBytes, &tmQ, q_full, 64, qt * kBQ, bh);
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
+        const int st = j % kKVStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kKVStages) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
         uint8_t* k = sK + st * kTileBytes;
         uint8_t* v = sV + st * kTileBytes;
@@ -127,44 +145,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(128, 128);
-      const uint32_t tS[2] = {tmem_base, tmem_base + 128};
-      const uint32_t tO = tmem_base + 256;
+      const uint32_t tO = tmem_base + kOCol;
       const uint32_t aQ = smem_u32(sQ);
-      const uint32_t aP = smem_u32(sP);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
+      // S_j = Q K_j^T into buffer j % 3.
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kKVStages;
+        const int b = j % kSBufs;
+        if (!mbar_wait(&kv_full[st], (j / kKVStages) & 1, p.err, kDevTimeoutAttn)) return false;
+        if (!mbar_wait(&s_free[b], ((j / kSBufs) & 1) ^ 1, p.err, kDevTimeoutAttn)) return false;
+        tc_fence_after();
         const uint32_t aK = smem_u32(sK + st * kTileBytes);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          umma_bf16(tS[st], make_sdesc_sw128(aQ + off), make_sdesc_sw128(aK + off), idesc, k > 0 ? 1u : 0u);
+          umma_bf16(tmem_base + b * 128, make_sdesc_sw128(aQ + off), make_sdesc_sw128(aK + off), idesc,
+                    k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[b]);
+        return true;
       };
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn) && mbar_wait(&kv_full[0], 0, p.err, kDevTimeoutAttn);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
+      if (ok) ok = issue_s(0);
+      if (ok && nkv > 1) ok = issue_s(1);
       for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv) {
-          const int st = (j + 1) & 1;
-          ok = mbar_wait(&kv_full[st], ((j + 1) >> 1) & 1, p.err, kDevTimeoutAttn) &&
-               mbar_wait(&s_empty[st], (((j + 1) >> 1) & 1) ^ 1, p.err, kDevTimeoutAttn);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
         if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutAttn)) break;
         tc_fence_after();
-        const uint32_t aV = smem_u32(sV + (j & 1) * kTileBytes);
+        const int st = j % kKVStages;
+        const int b = j % kSBufs;
+        const uint32_t aV = smem_u32(sV + st * kTileBytes);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
+          // A = P_j: 16 keys = 8 packed bf16x2 TMEM columns per MMA.
           const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          umma_bf16(tO, make_sdesc_sw128(aP + off), make_sdesc_sw128(aV + off), idesc, (j > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tO, tmem_base + b * 128 + k * 8, make_sdesc_sw128(aV + off), idesc,
+                       (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&kv_empty[j & 1]);
-        umma_commit(p_empty);
+        umma_commit(&s_free[b]);
+        umma_commit(&kv_empty[st]);
+        umma_commit(o_done);
+        if (j + 2 < nkv) ok = issue_s(j + 2);
       }
     }
   } else {
@@ -172,37 +191,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tO = tmem_base + lane_off + 256;
+    const uint32_t tO = tmem_base + lane_off + kOCol;
     const float c = p.scale * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1, p.err, kDevTimeoutAttn));
+      const int b = j % kSBufs;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j / kSBufs) & 1, p.err, kDevTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t tS = tmem_base + lane_off + b * 128;
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld32(tS, r0);
+      tmem_ld32(tS + 32, r1);
+      tmem_ld32(tS + 64, r2);
+      tmem_ld32(tS + 96, r3);
+      tmem_ld_wait();
       float s[128];
-      {
-        uint32_t r[32];
-        const uint32_t tS = tmem_base + lane_off + st * 128;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          tmem_ld32(tS + ch * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[ch * 32 + i] = __uint_as_float(r[i]);
-        }
+      for (int i = 0; i < 32; ++i) {
+        s[i] = __uint_as_float(r0[i]);
+        s[32 + i] = __uint_as_float(r1[i]);
+        s[64 + i] = __uint_as_float(r2[i]);
+        s[96 + i] = __uint_as_float(r3[i]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[st]);
       const int kbase = j * kBKV;
       if (kbase + kBKV > S) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) s[i] = -INFINITY;
       }
-      // Row max as 8 independent chains (a single 128-long dependent chain
-      // would dominate the softmax latency).
+      // Row max as 8 independent chains.
       float mp[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mp[k] = s[k];
@@ -215,17 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_use = grow ? mx : m;
       const float alpha = grow ? ex2(m - m_use) : 1.0f;
       float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[64];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = ex2(fmaf(s[i], c, -m_use));
-        sp[i & 7] += s[i];
+      for (int i = 0; i < 64; ++i) {
+        const float e0 = ex2(fmaf(s[2 * i], c, -m_use));
+        const float e1 = ex2(fmaf(s[2 * i + 1], c, -m_use));
+        sp[(2 * i) & 7] += e0;
+        sp[(2 * i + 1) & 7] += e1;
+        pk[i] = pack_bf16x2(e0, e1);
       }
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
       m = m_use;
       if (j > 0) {
-        // PV_{j-1} done: the P buffer is free and O is current.
-        ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (j - 1) & 1, p.err, kDevTimeoutAttn));
+        // PV_{j-1} done: O is current (and buffer (j-1) % 3 is being recycled).
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.err, kDevTimeoutAttn));
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
@@ -238,37 +261,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
             tmem_st32(tO + ch * 32, r);
           }
-          tmem_st_wait();
         }
       }
-      // P row -> shared memory, K-major 128-byte swizzle (two 64-key atoms).
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* v = s + kb * 64 + ch * 8;
-          const uint4 o = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                                     pack_bf16x2(v[6], v[7]));
-          *reinterpret_cast<uint4*>(sP + kb * kHalfBytes + row * 128 + ((ch ^ (row & 7)) << 4)) = o;
-        }
-      }
-      fence_proxy_async_smem();
+      // P_j (bf16, two keys per column) over the first 64 columns of S_j.
+      tmem_st32(tS, pk);
+      tmem_st32(tS + 32, pk + 32);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (nkv - 1) & 1, p.err, kDevTimeoutAttn));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nkv - 1) & 1, p.err, kDevTimeoutAttn));
     if (ok) {
       tc_fence_after();
       const int q = qt * kBQ + row;
       const float inv = 1.0f / l;
       uint16_t* dst = p.o + (static_cast<int64_t>(bh / p.H) * S + q) * p.ld_o + (bh % p.H) * 128;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tO + ch * 32, r);
-        tmem_ld_wait();
-        if (q < S) {
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld32(tO, r0);
+      tmem_ld32(tO + 32, r1);
+      tmem_ld32(tO + 64, r2);
+      tmem_ld32(tO + 96, r3);
+      tmem_ld_wait();
+      if (q < S) {
+        const uint32_t* rs[4] = {r0, r1, r2, r3};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+          const uint32_t* r = rs[ch];
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             d4[v] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * v]) * inv, __uint_as_float(r[8 * v + 1]) * inv),
