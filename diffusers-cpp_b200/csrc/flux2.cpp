@@ -31,6 +31,55 @@ size_t block_bytes_of(int type) {
     default: return 2;
   }
 }
+uint16_t host_f32_to_bf16(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return static_cast<uint16_t>((b >> 16) | 0x40);  // quiet NaN
+  b += 0x7FFFu + ((b >> 16) & 1u);  // round to nearest even
+  return static_cast<uint16_t>(b >> 16);
+}
+
+float host_f16_to_f32(const uint8_t* p) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
+}
+
+// Dequantise one GGUF row of n weights to f32 (the gguf-py arithmetic: Q8_0
+// d * q; Q4_K (d * sc) * q - dmin * m), for load-time expansion only.
+void host_dequant_row(int type, const uint8_t* src, int64_t n, float* out) {
+  if (type == kTypeQ8_0) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = src + b * 34;
+      const float d = host_f16_to_f32(blk);
+      for (int i = 0; i < 32; ++i) out[b * 32 + i] = static_cast<float>(static_cast<int8_t>(blk[2 + i])) * d;
+    }
+  } else if (type == kTypeQ4_K) {
+    for (int64_t b = 0; b < n / 256; ++b) {
+      const uint8_t* blk = src + b * 144;
+      const float d = host_f16_to_f32(blk), dmin = host_f16_to_f32(blk + 2);
+      const uint8_t* s = blk + 4;
+      for (int j = 0; j < 8; ++j) {
+        int sc, m;
+        if (j < 4) {
+          sc = s[j] & 0x3F;
+          m = s[j + 4] & 0x3F;
+        } else {
+          sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30);
+          m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30);
+        }
+        const float ds = d * static_cast<float>(sc), dm = dmin * static_cast<float>(m);
+        const uint8_t* qs = blk + 16 + (j / 2) * 32;
+        for (int l = 0; l < 32; ++l) {
+          const float q = static_cast<float>((qs[l] >> ((j & 1) * 4)) & 0x0F);
+          const float prod = ds * q;
+          out[b * 256 + j * 32 + l] = prod - dm;
+        }
+      }
+    }
+  } else {
+    fail(DCPP_ERR_UNSUPPORTED, "host dequantisation: Q8_0 / Q4_K only");
+  }
+}
+
 bool is_gemm_type(int t) {
   return t == kTypeQ8_0 || t == kTypeQ4_K || t == kTypeBF16 || t == kTypeF16 || t == kTypeF32;
 }
@@ -218,7 +267,8 @@ void FlowMatchEulerDiscreteScheduler::schedule(int n, std::vector<float>& timest
 }
 
 // ----------------------------------------------------------------- model
-Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg) : ctx_(ctx), cfg_(cfg) {
+Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg, bool host_only)
+    : ctx_(ctx), cfg_(cfg), host_only_(host_only) {
   if (cfg_.attention_head_dim != 128) fail(DCPP_ERR_UNSUPPORTED, "attention_head_dim must be 128");
   if (cfg_.patch_size != 1) fail(DCPP_ERR_UNSUPPORTED, "patch_size must be 1");
   int64_t tot = 0;
@@ -229,6 +279,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
 }
 
 Flux2Transformer2DModel::~Flux2Transformer2DModel() {
+  if (host_only_) return;
   cudaSetDevice(ctx_.device);
   cudaStreamSynchronize(ctx_.stream);
   free_plan();
@@ -457,6 +508,30 @@ void Flux2Transformer2DModel::place_rows(DevWeight& w, const std::string& part, 
                                          const std::function<int64_t(int64_t)>& row_map,
                                          const std::vector<std::array<int64_t, 3>>& col_ranges) {
   if (!w.need.count(part)) fail(DCPP_ERR_STATE, "Tensor '" + w.name + "': part '" + part + "' set twice");
+  {
+    // A tensor-parallel column shard that does not fall on quantisation
+    // block boundaries (e.g. Q4_K's 256 columns vs 384-column head shards)
+    // cannot be sliced in the block format: expand those rows to bf16 on the
+    // host (exact dequantised values, rounded once), as the GEMM would.
+    const int64_t qbs = block_size_of(type);
+    bool unaligned = w.cols % qbs != 0;
+    for (auto& cr : col_ranges) unaligned = unaligned || cr[0] % qbs || cr[1] % qbs || cr[2] % qbs;
+    // Parts already placed in a quantised type are expanded as well, so one
+    // fused weight always ends up in one type.
+    if ((unaligned && qbs > 1) || (type == kTypeBF16 && block_size_of(w.type) > 1)) expand_staging_bf16(w);
+    if (qbs > 1 && (unaligned || w.type == kTypeBF16)) {
+      std::vector<uint16_t> conv(static_cast<size_t>(shape[0]) * shape[1]);
+      const size_t src_rb_q = row_bytes_of(type, shape[1]);
+      std::vector<float> rowf(static_cast<size_t>(shape[1]));
+      for (int64_t i = 0; i < shape[0]; ++i) {
+        if (row_map(i) < 0) continue;
+        host_dequant_row(type, src + static_cast<size_t>(i) * src_rb_q, shape[1], rowf.data());
+        for (int64_t c = 0; c < shape[1]; ++c) conv[static_cast<size_t>(i) * shape[1] + c] = host_f32_to_bf16(rowf[c]);
+      }
+      place_rows(w, part, kTypeBF16, shape, reinterpret_cast<const uint8_t*>(conv.data()), row_map, col_ranges);
+      return;
+    }
+  }
   if (w.type >= 0 && w.type != type)
     fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + w.name + "': parts of one fused weight must share a ggml type");
   const int64_t bs = block_size_of(type);
@@ -486,7 +561,25 @@ void Flux2Transformer2DModel::place_rows(DevWeight& w, const std::string& part, 
   if (w.need.empty()) finish_weight(w);
 }
 
+void Flux2Transformer2DModel::expand_staging_bf16(DevWeight& w) {
+  if (w.type < 0 || block_size_of(w.type) == 1) return;
+  std::vector<uint8_t> conv(static_cast<size_t>(w.rows) * w.cols * 2);
+  std::vector<float> rowf(static_cast<size_t>(w.cols));
+  for (int64_t i = 0; i < w.rows; ++i) {
+    host_dequant_row(w.type, w.staging.data() + static_cast<size_t>(i) * w.row_bytes, w.cols, rowf.data());
+    auto* dst = reinterpret_cast<uint16_t*>(conv.data()) + static_cast<size_t>(i) * w.cols;
+    for (int64_t c = 0; c < w.cols; ++c) dst[c] = host_f32_to_bf16(rowf[c]);
+  }
+  w.type = kTypeBF16;
+  w.row_bytes = static_cast<size_t>(w.cols) * 2;
+  w.staging.swap(conv);
+}
+
 void Flux2Transformer2DModel::finish_weight(DevWeight& w) {
+  if (host_only_) {  // keep the assembled rows on the host (read_param)
+    w.on_host = true;
+    return;
+  }
   const size_t bytes = w.staging.size();
   if (cudaMalloc(&w.data, bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -536,6 +629,11 @@ void Flux2Transformer2DModel::set_vector(DevVector& v, int type, const std::vect
   } else {
     fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + v.name + "': norm weights must be F32, F16 or BF16");
   }
+  if (host_only_) {
+    v.host.swap(host);
+    v.set = true;
+    return;
+  }
   if (!v.data) cuda_check(cudaMalloc(&v.data, v.n * sizeof(float)), "alloc vector");
   cuda_check(cudaMemcpy(v.data, host.data(), v.n * sizeof(float), cudaMemcpyHostToDevice), "upload vector");
   v.set = true;
@@ -548,6 +646,52 @@ void Flux2Transformer2DModel::set_param(const std::string& name, int type, const
   if (it == setters_.end()) fail(DCPP_ERR_NOT_FOUND, "Error while loading Tensor '" + name + "': Tensor not found");
   if (!data) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + name + "': null data");
   it->second(type, shape, data, nbytes);
+}
+
+void Flux2Transformer2DModel::require_device(const char* what) const {
+  if (host_only_) fail(DCPP_ERR_STATE, std::string(what) + ": a host-only model cannot execute");
+}
+
+void Flux2Transformer2DModel::read_param(const std::string& name, int* type, int64_t* rows, int64_t* cols, void* dst,
+                                         size_t cap, size_t* nbytes) {
+  for (auto* w : weights_) {
+    if (w->name != name) continue;
+    if (!w->ready()) fail(DCPP_ERR_STATE, "parameter '" + name + "' is not fully set");
+    if (w->packed) fail(DCPP_ERR_UNSUPPORTED, "parameter '" + name + "' is held only in the packed GEMM layout");
+    const size_t n = w->row_bytes * static_cast<size_t>(w->rows);
+    if (type) *type = w->type;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (nbytes) *nbytes = n;
+    if (!dst) return;
+    if (cap < n) fail(DCPP_ERR_INVALID_ARG, "read_param: buffer too small for '" + name + "'");
+    if (w->on_host) {
+      memcpy(dst, w->staging.data(), n);
+    } else {
+      cuda_check(cudaStreamSynchronize(ctx_.stream), "read_param");
+      cuda_check(cudaMemcpy(dst, w->data, n, cudaMemcpyDeviceToHost), "read_param");
+    }
+    return;
+  }
+  for (auto* v : vectors_) {
+    if (v->name != name) continue;
+    if (!v->set) fail(DCPP_ERR_STATE, "parameter '" + name + "' is not set");
+    const size_t n = static_cast<size_t>(v->n) * sizeof(float);
+    if (type) *type = kTypeF32;
+    if (rows) *rows = 1;
+    if (cols) *cols = v->n;
+    if (nbytes) *nbytes = n;
+    if (!dst) return;
+    if (cap < n) fail(DCPP_ERR_INVALID_ARG, "read_param: buffer too small for '" + name + "'");
+    if (host_only_) {
+      memcpy(dst, v->host.data(), n);
+    } else {
+      cuda_check(cudaStreamSynchronize(ctx_.stream), "read_param");
+      cuda_check(cudaMemcpy(dst, v->data, n, cudaMemcpyDeviceToHost), "read_param");
+    }
+    return;
+  }
+  fail(DCPP_ERR_NOT_FOUND, "read_param: no parameter named '" + name + "'");
 }
 
 std::vector<std::string> Flux2Transformer2DModel::missing() const {
@@ -576,6 +720,7 @@ void Flux2Transformer2DModel::free_plan() {
 }
 
 void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph) {
+  require_device("prepare");
   auto miss = missing();
   if (!miss.empty()) fail(DCPP_ERR_STATE, "parameters not set: " + miss.front() + " (+" + std::to_string(miss.size() - 1) + " more)");
   if (batch < 1 || batch > 4) fail(DCPP_ERR_UNSUPPORTED, "batch must be 1..4");
@@ -1134,6 +1279,7 @@ void Flux2Transformer2DModel::run_resident_step() {
 }
 
 void Flux2Transformer2DModel::set_profiling(bool on) {
+  require_device("set_profiling");
   if (on == profiling_) return;
   cudaStreamSynchronize(ctx_.stream);
   free_plan();
@@ -1161,6 +1307,7 @@ void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64
 }
 
 void Flux2Transformer2DModel::read_latents(float* out) {
+  if (!planned_) fail(DCPP_ERR_STATE, "read_latents before prepare");
   cuda_check(cudaMemcpyAsync(out, lat_[cur_], B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, ctx_.stream),
              "copy latents");
   ctx_.check_device_error();
@@ -1177,7 +1324,7 @@ dcpp_status model_call(dcpp_flux2* m, const char* entry, F&& f) {
   dcpp_ctx* ctx = m->ctx;
   try {
     ctx->maybe_inject(entry);
-    cudaSetDevice(ctx->device);
+    if (ctx->device >= 0) cudaSetDevice(ctx->device);
     f(*m->model);
     return DCPP_OK;
   } catch (const dcpp::Error& e) {
@@ -1234,9 +1381,42 @@ dcpp_status dcpp_flux2_create(dcpp_ctx* ctx, const dcpp_flux2_config* cfg, dcpp_
   }
 }
 
+dcpp_status dcpp_flux2_create_host(const dcpp_flux2_config* cfg, dcpp_flux2** out) {
+  if (!cfg || !out) return DCPP_ERR_INVALID_ARG;
+  *out = nullptr;
+  auto* m = new dcpp_flux2();
+  m->own_ctx.reset(new dcpp_ctx());
+  m->own_ctx->device = -1;
+  m->ctx = m->own_ctx.get();
+  try {
+    m->model.reset(new dcpp::Flux2Transformer2DModel(*m->ctx, dcpp::Flux2Config::from_c(*cfg), true));
+  } catch (const dcpp::Error& e) {
+    delete m;
+    return e.status;
+  } catch (const std::exception&) {
+    delete m;
+    return DCPP_ERR_INVALID_ARG;
+  }
+  *out = m;
+  return DCPP_OK;
+}
+
+const char* dcpp_flux2_last_error(dcpp_flux2* m) {
+  if (!m || !m->ctx) return "invalid model handle";
+  return m->ctx->last_error.c_str();
+}
+
+dcpp_status dcpp_flux2_read_param(dcpp_flux2* m, const char* name, int* type, int64_t* rows, int64_t* cols, void* dst,
+                                  size_t cap, size_t* nbytes) {
+  return model_call(m, "dcpp_flux2_read_param", [&](dcpp::Flux2Transformer2DModel& mm) {
+    if (!name) dcpp::fail(DCPP_ERR_INVALID_ARG, "read_param: null name");
+    mm.read_param(name, type, rows, cols, dst, cap, nbytes);
+  });
+}
+
 dcpp_status dcpp_flux2_destroy(dcpp_flux2* m) {
   if (!m) return DCPP_ERR_INVALID_ARG;
-  if (m->ctx) cudaSetDevice(m->ctx->device);
+  if (m->ctx && m->ctx->device >= 0) cudaSetDevice(m->ctx->device);
   delete m;
   return DCPP_OK;
 }

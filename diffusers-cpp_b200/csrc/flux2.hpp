@@ -62,9 +62,10 @@ struct DevWeight {
   uint8_t* data = nullptr;             // device, raw GGUF rows (null once packed)
   uint8_t* packed = nullptr;           // device, fused-dequant stage layout (block projections)
   bool pack = false;                   // a block projection: pack when quantised
+  bool on_host = false;                // host-only model: assembled rows kept in `staging`
   std::vector<uint8_t> staging;        // host, until all parts arrived
   std::set<std::string> need;          // part names still missing
-  bool ready() const { return (data != nullptr || packed != nullptr) && need.empty(); }
+  bool ready() const { return (data != nullptr || packed != nullptr || on_host) && need.empty(); }
 };
 
 // An f32 vector parameter (RMSNorm weights).
@@ -72,12 +73,16 @@ struct DevVector {
   std::string name;
   int64_t n = 0;
   float* data = nullptr;
+  std::vector<float> host;  // host-only model
   bool set = false;
 };
 
 class Flux2Transformer2DModel {
  public:
-  Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg);
+  // host_only: parameters are assembled (and tensor-parallel sharded) on
+  // the host and never uploaded; the model cannot execute.  Used to inspect
+  // the exact shards a rank would load, without a GPU.
+  Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg, bool host_only = false);
   ~Flux2Transformer2DModel();
 
   const Flux2Config& config() const { return cfg_; }
@@ -85,6 +90,11 @@ class Flux2Transformer2DModel {
   void set_param(const std::string& name, int type, const std::vector<int64_t>& shape, const void* data,
                  size_t nbytes);
   std::vector<std::string> missing() const;
+  // Copy an assembled parameter by its model name (weights: the fused name,
+  // e.g. transformer_blocks.0.attn.to_qkv; vectors: the GGUF name).  With
+  // dst == nullptr only the type, shape and byte size are returned.
+  void read_param(const std::string& name, int* type, int64_t* rows, int64_t* cols, void* dst, size_t cap,
+                  size_t* nbytes);
 
   // Plan buffers / tensor maps / graph for B x (n_img + n_txt) tokens.
   void prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph);
@@ -133,6 +143,8 @@ class Flux2Transformer2DModel {
                   const uint8_t* src, const std::function<int64_t(int64_t)>& row_map,
                   const std::vector<std::array<int64_t, 3>>& col_ranges);
   void finish_weight(DevWeight& w);
+  void expand_staging_bf16(DevWeight& w);
+  void require_device(const char* what) const;
   void set_vector(DevVector& v, int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes);
   void free_plan();
   void build_plan();
@@ -149,6 +161,7 @@ class Flux2Transformer2DModel {
 
   Ctx& ctx_;
   Flux2Config cfg_;
+  bool host_only_ = false;
   int rank_ = 0, nranks_ = 1;
   int64_t D_ = 0, F_ = 0, H_ = 0, Dl_ = 0, Fl_ = 0, Hl_ = 0;
 
@@ -206,4 +219,5 @@ struct FlowMatchEulerDiscreteScheduler {
 struct dcpp_flux2 {
   std::unique_ptr<dcpp::Flux2Transformer2DModel> model;
   dcpp_ctx* ctx = nullptr;
+  std::unique_ptr<dcpp_ctx> own_ctx;  // host-only models: error text, no device
 };

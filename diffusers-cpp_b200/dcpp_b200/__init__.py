@@ -109,6 +109,10 @@ _SIGNATURES = {
     "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
     "dcpp_flux2_set_tensor_parallel": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
+    "dcpp_flux2_create_host": (ctypes.c_int, [ctypes.POINTER(Flux2ConfigC), ctypes.POINTER(_vp)]),
+    "dcpp_flux2_last_error": (ctypes.c_char_p, [_vp]),
+    "dcpp_flux2_read_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), _c_i64p, _c_i64p, _vp,
+                                             ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
 }
 
 _LIB = None
@@ -278,18 +282,42 @@ def config_to_c(cfg) -> Flux2ConfigC:
 
 
 class Flux2Model:
-    """dcpp_flux2: Flux2Transformer2DModel on one GPU (or one TP rank)."""
+    """dcpp_flux2: Flux2Transformer2DModel on one GPU (or one TP rank).
 
-    def __init__(self, ctx: Context, cfg, tp_rank: int = 0, tp_size: int = 1):
+    ``ctx=None`` makes a host-only model (dcpp_flux2_create_host): parameters
+    are assembled and sharded exactly as on a device, but stay on the host
+    (``read_param``) and the model cannot execute."""
+
+    def __init__(self, ctx: Optional[Context], cfg, tp_rank: int = 0, tp_size: int = 1):
         self.ctx = ctx
         self.cfg = cfg
         c = config_to_c(cfg)
         h = _vp()
-        ctx.check(lib().dcpp_flux2_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "flux2_create")
+        if ctx is None:
+            st = lib().dcpp_flux2_create_host(ctypes.byref(c), ctypes.byref(h))
+            if st != DCPP_OK:
+                raise DcppError(st, "flux2_create_host")
+        else:
+            ctx.check(lib().dcpp_flux2_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "flux2_create")
+            ctx._children.add(self)
         self.h = h
-        ctx._children.add(self)
         if tp_size > 1:
-            ctx.check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
+            self._check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
+
+    def _check(self, status: int, what: str = ""):
+        if status != DCPP_OK:
+            msg = lib().dcpp_flux2_last_error(self.h).decode()
+            raise DcppError(status, f"{what}: {msg}" if what else msg)
+
+    def read_param(self, name: str):
+        """(ggml type, (rows, cols), uint8 array) of an assembled parameter."""
+        t, r, c, n = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_size_t()
+        self._check(lib().dcpp_flux2_read_param(self.h, name.encode(), ctypes.byref(t), ctypes.byref(r),
+                                                ctypes.byref(c), None, 0, ctypes.byref(n)), f"read_param({name})")
+        buf = np.empty(n.value, dtype=np.uint8)
+        self._check(lib().dcpp_flux2_read_param(self.h, name.encode(), None, None, None, buf.ctypes.data, buf.nbytes,
+                                                ctypes.byref(n)), f"read_param({name})")
+        return t.value, (r.value, c.value), buf
 
     def close(self):
         if getattr(self, "h", None):
@@ -308,7 +336,7 @@ class Flux2Model:
             data = data.contiguous().cpu().numpy()
         arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
         shp = (ctypes.c_int64 * len(shape))(*shape)
-        self.ctx.check(lib().dcpp_flux2_set_param(self.h, name.encode(), gtype, len(shape), shp, arr.ctypes.data,
+        self._check(lib().dcpp_flux2_set_param(self.h, name.encode(), gtype, len(shape), shp, arr.ctypes.data,
                                                   arr.nbytes), f"set_param({name})")
 
     def load_params(self, params):
@@ -318,47 +346,47 @@ class Flux2Model:
     def missing(self):
         n = ctypes.c_int()
         buf = ctypes.create_string_buffer(512)
-        self.ctx.check(lib().dcpp_flux2_missing(self.h, ctypes.byref(n), buf, 512), "missing")
+        self._check(lib().dcpp_flux2_missing(self.h, ctypes.byref(n), buf, 512), "missing")
         return n.value, buf.value.decode()
 
     def prepare(self, batch: int, n_img: int, n_txt: int, use_graph: bool = True):
-        self.ctx.check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
+        self._check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
 
     def forward(self, hidden, encoder, timestep, img_ids, txt_ids, out, guidance=None):
-        self.ctx.check(lib().dcpp_flux2_forward(self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
+        self._check(lib().dcpp_flux2_forward(self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
                                                 _ptr(txt_ids), _ptr(guidance), _ptr(out)), "forward")
 
     def denoise_step(self, latents, encoder, timestep, dt: float, img_ids, txt_ids, latents_out):
-        self.ctx.check(lib().dcpp_flux2_denoise_step(self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
+        self._check(lib().dcpp_flux2_denoise_step(self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
                                                      _ptr(img_ids), _ptr(txt_ids), _ptr(latents_out)), "denoise_step")
 
     def load_inputs(self, latents, encoder, img_ids, txt_ids):
-        self.ctx.check(lib().dcpp_flux2_load_inputs(self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
+        self._check(lib().dcpp_flux2_load_inputs(self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
                                                     _ptr(txt_ids)), "load_inputs")
 
     def set_timestep(self, timestep: float, dt: float):
-        self.ctx.check(lib().dcpp_flux2_set_timestep(self.h, float(timestep), float(dt)), "set_timestep")
+        self._check(lib().dcpp_flux2_set_timestep(self.h, float(timestep), float(dt)), "set_timestep")
 
     def run_resident(self):
-        self.ctx.check(lib().dcpp_flux2_run_resident(self.h), "run_resident")
+        self._check(lib().dcpp_flux2_run_resident(self.h), "run_resident")
 
     def read_latents(self, out):
-        self.ctx.check(lib().dcpp_flux2_read_latents(self.h, _ptr(out)), "read_latents")
+        self._check(lib().dcpp_flux2_read_latents(self.h, _ptr(out)), "read_latents")
 
     PROFILE_KINDS = {"gemm": 0, "attention": 1, "norm": 2, "gemv": 3, "dequant": 4, "other": 5, "allreduce": 6}
 
     def set_profiling(self, on: bool):
-        self.ctx.check(lib().dcpp_flux2_set_profiling(self.h, 1 if on else 0), "set_profiling")
+        self._check(lib().dcpp_flux2_set_profiling(self.h, 1 if on else 0), "set_profiling")
 
     def profile(self, kind: str):
         ms, fl, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
-        self.ctx.check(lib().dcpp_flux2_profile(self.h, self.PROFILE_KINDS[kind], ctypes.byref(ms), ctypes.byref(fl),
+        self._check(lib().dcpp_flux2_profile(self.h, self.PROFILE_KINDS[kind], ctypes.byref(ms), ctypes.byref(fl),
                                                 ctypes.byref(n)), "profile")
         return ms.value, fl.value, n.value
 
     def launches_per_step(self) -> int:
         v = ctypes.c_int64()
-        self.ctx.check(lib().dcpp_flux2_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
+        self._check(lib().dcpp_flux2_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
         return v.value
 
 

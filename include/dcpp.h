@@ -310,6 +310,29 @@ dcpp_status dcpp_allreduce(dcpp_ctx* ctx, void* d_buf, int64_t count, int dtype)
  * row-parallel out projections, one all-reduce per row-parallel site). */
 dcpp_status dcpp_flux2_set_tensor_parallel(dcpp_flux2* model, int rank, int nranks);
 
+/* A model that assembles parameters on the host only: set_param and
+ * set_tensor_parallel work as on a device model (same checks, same shard
+ * layout, same load-time conversions), nothing is uploaded and the model
+ * cannot execute (prepare returns DCPP_ERR_STATE).  No counterpart in the
+ * reference; it lets a loader, or a test without a GPU, inspect the exact
+ * shard each rank would hold.  Errors: dcpp_flux2_last_error. */
+dcpp_status dcpp_flux2_create_host(const dcpp_flux2_config* cfg, dcpp_flux2** out_model);
+
+/* Text of the last error raised by a call on `model` (also the context's
+ * dcpp_last_error for device models). */
+const char* dcpp_flux2_last_error(dcpp_flux2* model);
+
+/* Copy an assembled parameter out (host memory), by model name: weights
+ * under their fused name (e.g. "transformer_blocks.0.attn.to_qkv",
+ * "single_transformer_blocks.0.attn.to_out.weight"; rows and columns are
+ * this rank's shard), RMSNorm vectors under their GGUF name (returned as
+ * F32, rows 1).  A tensor-parallel column shard that does not fall on the
+ * quantisation blocks is held as BF16.  With dst NULL only type, shape and
+ * byte size are returned.  Weights held only in the fused-dequant packed
+ * layout return DCPP_ERR_UNSUPPORTED. */
+dcpp_status dcpp_flux2_read_param(dcpp_flux2* model, const char* name, int* type, int64_t* rows,
+                                  int64_t* cols, void* dst, size_t cap, size_t* nbytes);
+
 #ifdef __cplusplus
 }
 #endif
