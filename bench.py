@@ -339,6 +339,10 @@ def run_ours(args):
                 "cuda_graph": not args.no_graph,
                 "dequant": ("fused into the GEMM" if os.environ.get("DCPP_FUSED_DEQUANT") == "1"
                             else "per-projection expansion to bf16 before each GEMM"),
+                "tp_exchange": (None if world == 1 else
+                                "ncclAllReduce of the row-parallel partials" if os.environ.get("DCPP_TP_COMM") == "nccl"
+                                else "GEMM epilogue stores partials into the owner GPU (NVLink peer memory); "
+                                     "owner LayerNorm + all-gather stores; cross-GPU flag barriers"),
             },
             "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "dcpp_flux2_denoise_step with pinned host latents/encoder/ids in, latents out"},

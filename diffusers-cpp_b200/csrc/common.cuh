@@ -24,6 +24,7 @@ enum DeviceError : int {
   kDevTimeoutDequant = 5,   // dequant stage handshake timed out
   kDevBadShape = 6,         // a launch got a shape its kernel cannot run
   kDevTimeoutAttn = 7,      // attention pipeline wait timed out
+  kDevTimeoutPeer = 8,      // tensor-parallel barrier: a peer GPU did not arrive
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;  // 1 s

@@ -275,6 +275,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   for (auto d : cfg_.axes_dims_rope) tot += d;
   if (tot != cfg_.attention_head_dim) fail(DCPP_ERR_INVALID_ARG, "axes_dims_rope must sum to attention_head_dim");
   if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) == "1";
+  if (const char* e = getenv("DCPP_TP_COMM")) tp_peer_ = std::string(e) != "nccl";
   build_registry();
 }
 
@@ -712,6 +713,13 @@ void Flux2Transformer2DModel::free_plan() {
   graph_step_[0] = graph_step_[1] = nullptr;
   for (void* p : allocs_) cudaFree(p);
   allocs_.clear();
+  sym_.close(ctx_);
+  for (int j = 0; j < 8; ++j) {
+    recv_peer_[j] = nullptr;
+    a_peer_[j] = nullptr;
+    flags_peer_[j] = nullptr;
+  }
+  epoch_ = nullptr;
   ops_fwd_.clear();
   step_ops_[0].clear();
   step_ops_[1].clear();
@@ -852,6 +860,16 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
                         0, kOpAllreduce});
 }
 
+void Flux2Transformer2DModel::add_tp_barrier() {
+  TpBarrierArgs a{};
+  for (int j = 0; j < nranks_; ++j) a.flags[j] = flags_peer_[j];
+  a.epoch = epoch_;
+  a.err = ctx_.d_err;
+  a.rank = rank_;
+  a.nranks = nranks_;
+  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce});
+}
+
 void Flux2Transformer2DModel::build_plan() {
   const int64_t B = B_, S = S_, Ni = Ni_, Nt = Nt_, D = D_, Dl = Dl_, Fl = Fl_, Hl = Hl_;
   const int64_t R = B * S;
@@ -860,6 +878,9 @@ void Flux2Transformer2DModel::build_plan() {
   const int64_t tg = cfg_.timestep_guidance_channels;
   const bool tp = nranks_ > 1;
   if (tp && !ctx_.comm) fail(DCPP_ERR_STATE, "tensor-parallel model needs dcpp_tp_init on its context");
+  if (tp && (ctx_.nranks != nranks_ || ctx_.rank != rank_))
+    fail(DCPP_ERR_STATE, "model tensor-parallel rank/size differ from the context's dcpp_tp_init");
+  const bool peer = tp && tp_peer_;
   auto alloc = [&](size_t bytes) {
     void* p = nullptr;
     if (cudaMalloc(&p, std::max<size_t>(bytes, 256)) != cudaSuccess) {
@@ -870,8 +891,32 @@ void Flux2Transformer2DModel::build_plan() {
     return p;
   };
   h_ = static_cast<float*>(alloc(R * D * 4));
-  part_ = tp ? static_cast<float*>(alloc(R * D * 4)) : nullptr;
-  a_ = static_cast<uint16_t*>(alloc(R * D * 2));
+  part_ = tp && !peer ? static_cast<float*>(alloc(R * D * 4)) : nullptr;
+  if (peer) {
+    // One IPC-mapped block per rank: a_ | recv slots | barrier flags.
+    chunk_ = (R + nranks_ - 1) / nranks_;
+    auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+    const size_t off_recv = up(R * D * 2);
+    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * chunk_ * D * 4);
+    sym_.open(ctx_, off_flags + 256);
+    for (int j = 0; j < nranks_; ++j) {
+      a_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j]);
+      recv_peer_[j] = reinterpret_cast<float*>(sym_.peer[j] + off_recv);
+      flags_peer_[j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags);
+    }
+    a_ = a_peer_[rank_];
+    epoch_ = static_cast<uint32_t*>(alloc(256));
+    cuda_check(cudaMemsetAsync(epoch_, 0, 256, ctx_.stream), "clear epoch");
+    // Every rank's flags are zero before any rank's first barrier.
+    cuda_check(cudaStreamSynchronize(ctx_.stream), "peer buffers");
+    float* one = static_cast<float*>(alloc(256));
+    auto& nc = Nccl::get();
+    int rc = nc.AllReduce(one, one, 1, 7, 0, ctx_.comm, ctx_.stream);
+    if (rc != 0) fail(DCPP_ERR_NCCL, std::string("ncclAllReduce: ") + nc.GetErrorString(rc));
+    cuda_check(cudaStreamSynchronize(ctx_.stream), "peer buffers");
+  } else {
+    a_ = static_cast<uint16_t*>(alloc(R * D * 2));
+  }
   q_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
   k_ = static_cast<uint16_t*>(alloc(R * Dl * 2));
   // V is kept transposed, [B, Hl, 128, Sp] with Sp = S rounded up to 64;
@@ -1030,7 +1075,6 @@ void Flux2Transformer2DModel::build_plan() {
                      cuda_check(launch_rope_table(ids_dev_, S, n_axes, axes.data(), theta, rope_, s), "rope_table");
                    },
                    1});
-    const float* resid = nullptr;  // pending all-reduced partial (TP)
     AttnTcArgs at{};
     at.o = cat_;
     at.ld_o = ldc;
@@ -1048,19 +1092,62 @@ void Flux2Transformer2DModel::build_plan() {
     };
     auto out_epi = [&](const float* g0, const float* g1, int64_t bstride) {
       EpilogueArgs e{};
-      e.mode = tp ? kEpiGateF32 : kEpiResidGate;
+      e.mode = tp ? (peer ? kEpiGatePeer : kEpiGateF32) : kEpiResidGate;
       e.out_f32 = tp ? part_ : h_;
       e.ld_out = D;
       e.gate[0] = g0;
       e.gate[1] = g1;
       e.gate_bstride = bstride;
+      if (peer) {
+        for (int j = 0; j < nranks_; ++j) e.peer_out[j] = recv_peer_[j];
+        e.chunk_rows = static_cast<int32_t>(chunk_);
+        e.peer_slot = rank_;
+      }
       return e;
+    };
+    // The exchange after a row-parallel GEMM and the LayerNorm that consumes
+    // it.  NCCL: all-reduce the partials, every rank normalises every row.
+    // Peer: barrier (partials landed), the owner of each row sums its slots
+    // into the residual and stores the normalised row to all ranks, barrier
+    // (activations landed).
+    bool pending = false;
+    auto site = [&]() {
+      if (!tp) return;
+      if (peer) add_tp_barrier();
+      else add_allreduce(part_, R * D);
+      pending = true;
+    };
+    auto site_norm = [&](NormArgs n) {
+      if (pending && !peer) n.resid = part_;
+      if (pending && peer) {
+        const int64_t lo = rank_ * chunk_, hi = std::min<int64_t>(R, lo + chunk_);
+        int k = 0;
+        for (int i = 0; i < n.n_segments; ++i) {
+          NormSegment sg = n.seg[i];
+          const int64_t a0 = std::max<int64_t>(lo, sg.src_row0), a1 = std::min<int64_t>(hi, sg.src_row0 + sg.rows);
+          if (a1 <= a0) continue;
+          sg.dst_row0 += static_cast<int32_t>(a0 - sg.src_row0);
+          sg.src_row0 = static_cast<int32_t>(a0);
+          sg.rows = static_cast<int32_t>(a1 - a0);
+          n.seg[k++] = sg;
+        }
+        n.n_segments = k;
+        n.resid = recv_peer_[rank_];
+        n.n_slots = nranks_;
+        n.slot_stride = chunk_ * D;
+        n.slot_row0 = lo;
+        n.n_peer_out = 0;
+        for (int j = 0; j < nranks_; ++j)
+          if (j != rank_) n.y_peer[n.n_peer_out++] = a_peer_[j] + (n.y - a_);
+      }
+      add_norm(n);
+      if (pending && peer) add_tp_barrier();
+      pending = false;
     };
     const float* mods_dbl[2] = {mod_txt_v_, mod_img_v_};
     // 4. double-stream blocks (Flux2TransformerBlock.hpp:45-117).
     for (auto& blk : dbl_) {
-      add_norm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, resid));
-      resid = nullptr;
+      site_norm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, nullptr));
       EpilogueArgs e{};
       e.mode = kEpiQkvMlp;
       e.qkv_cols = static_cast<int32_t>(3 * Dl);
@@ -1083,21 +1170,19 @@ void Flux2Transformer2DModel::build_plan() {
       attn_op();
       add_gemm("attn_out", cat_, ldc, Dl, &blk.out[0], &blk.out[1], stream_groups(true),
                out_epi(mod_txt_v_ + 2 * D, mod_img_v_ + 2 * D, 6 * D), D);
-      if (tp) { add_allreduce(part_, R * D); resid = part_; }
-      add_norm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, resid));
-      resid = nullptr;
+      site();
+      site_norm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, nullptr));
       EpilogueArgs f = e;
       f.qkv_cols = 0;
       add_gemm("ff_in", a_, D, D, &blk.ff_in[0], &blk.ff_in[1], stream_groups(true), f, 2 * Fl);
       add_gemm("ff_out", cat_ + Dl, ldc, Fl, &blk.ff_out[0], &blk.ff_out[1], stream_groups(true),
                out_epi(mod_txt_v_ + 5 * D, mod_img_v_ + 5 * D, 6 * D), D);
-      if (tp) { add_allreduce(part_, R * D); resid = part_; }
+      site();
     }
     // 5. single-stream blocks on the joint stream (Flux2SingleTransformerBlock.hpp:36-72).
     const float* mods_s[2] = {mod_s_v_, mod_s_v_};
     for (auto& blk : sgl_) {
-      add_norm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, resid));
-      resid = nullptr;
+      site_norm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, nullptr));
       EpilogueArgs e{};
       e.mode = kEpiQkvMlp;
       e.qkv_cols = static_cast<int32_t>(3 * Dl);
@@ -1118,11 +1203,11 @@ void Flux2Transformer2DModel::build_plan() {
       attn_op();
       add_gemm("out", cat_, ldc, Dl + Fl, &blk.out, nullptr, stream_groups(false),
                out_epi(mod_s_v_ + 2 * D, mod_s_v_ + 2 * D, 3 * D), D);
-      if (tp) { add_allreduce(part_, R * D); resid = part_; }
+      site();
     }
     // 6. drop text tokens, norm_out (scale first, then shift; AdaLayerNormContinuous.inl:26-43), proj_out.
     const float* mods_o[2] = {mod_o_v_, mod_o_v_};
-    add_norm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, resid));
+    site_norm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, nullptr));
     {
       std::vector<GemmGroup> g;
       for (int64_t b = 0; b < B; ++b) {

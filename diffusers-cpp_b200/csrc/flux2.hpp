@@ -158,6 +158,7 @@ class Flux2Transformer2DModel {
   void add_norm(const NormArgs& a);
   void add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y);
   void add_allreduce(float* buf, int64_t count);
+  void add_tp_barrier();
 
   Ctx& ctx_;
   Flux2Config cfg_;
@@ -189,6 +190,19 @@ class Flux2Transformer2DModel {
            *eb_ = nullptr, *wscratch_[2] = {nullptr, nullptr};
   int32_t* ids_dev_ = nullptr;
   float2* rope_ = nullptr;
+  // Tensor parallelism over peer memory (the default exchange): the
+  // row-parallel GEMMs store their gated partials straight into the owning
+  // rank's receive slots (recv, [nranks][chunk_ rows][D] f32 on each GPU),
+  // the owner's LayerNorm sums the slots into its residual rows and stores
+  // the normalised bf16 rows into every rank's activation buffer (a_).
+  // DCPP_TP_COMM=nccl selects ncclAllReduce of the partials instead.
+  bool tp_peer_ = true;
+  PeerBuffer sym_;
+  int64_t chunk_ = 0;
+  float* recv_peer_[8] = {};
+  uint16_t* a_peer_[8] = {};
+  uint32_t* flags_peer_[8] = {};
+  uint32_t* epoch_ = nullptr;
   float* host_scalars_ = nullptr;  // pinned: t[B], dt
   int cur_ = 0;                    // latent ping-pong index
   std::vector<Op> ops_fwd_;        // forward (noise prediction) plan

@@ -56,8 +56,13 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 // `row_base` is the first row (within the group) of the 128 accumulator rows
 // this CTA holds: m_tile * 128 for 1-SM tiles, m_tile * 256 + rank * 128 for
 // the 2-SM pair.
+// Per-warp staging for the peer-store epilogue: 32 rows x 32 columns f32,
+// row stride 36 floats (16-byte aligned rows, conflict-free float4 access).
+constexpr int kEpiStageStride = 36;
+constexpr int kEpiStageBytes = 4 * 32 * kEpiStageStride * 4;
+
 __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_base, int row_in_tile,
-                                             uint32_t taddr) {
+                                             uint32_t taddr, float* stage) {
   const GemmGroup& G = p.groups[tc.g];
   const EpilogueArgs& e = p.ep;
   const int local_row = row_base + row_in_tile;
@@ -172,9 +177,51 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
 
   // Column-wise epilogues: 8 chunks of 32 columns.
   const float* gate = nullptr;
-  if (e.mode == kEpiResidGate || e.mode == kEpiGateF32) {
+  const bool gate_only = e.mode == kEpiGateF32 || e.mode == kEpiGatePeer;
+  if (e.mode == kEpiResidGate || gate_only) {
     gate = e.gate[sel];
     if (gate) gate += static_cast<int64_t>(G.batch) * e.gate_bstride;
+  }
+  if (e.mode == kEpiGatePeer) {
+    // Rows go to other GPUs over NVLink: transpose each 32 x 32 chunk through
+    // shared memory so every store instruction writes 4 rows x 128
+    // contiguous bytes (whole lines) instead of 32 scattered 16-byte pieces.
+    const int lane = row_in_tile & 31;
+    uintptr_t rdst = 0;
+    if (row_ok) {
+      const int64_t owner = row / e.chunk_rows;
+      rdst = reinterpret_cast<uintptr_t>(
+          e.peer_out[owner] + (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out);
+    }
+    const int sub = lane >> 3, q = lane & 7;
+#pragma unroll 1
+    for (int c = 0; c < kGemmBN / 32; ++c) {
+      const int cb = col0 + c * 32;
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_ld_wait();
+      float4* st4 = reinterpret_cast<float4*>(stage + lane * kEpiStageStride);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        st4[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                             __uint_as_float(r[4 * v + 3]));
+      __syncwarp();
+      const int col = cb + 4 * q;
+      const bool col_ok = col + 4 <= p.N;
+      const float4 g = (gate && col_ok) ? __ldg(reinterpret_cast<const float4*>(gate + col))
+                                        : make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + sub;
+        const uintptr_t d = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(rdst), rr);
+        const float4 a = *reinterpret_cast<const float4*>(stage + rr * kEpiStageStride + 4 * q);
+        if (d && col_ok)
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(d) + col) =
+              make_float4(g.x * a.x, g.y * a.y, g.z * a.z, g.w * a.w);
+      }
+      __syncwarp();
+    }
+    return;
   }
   const float dt = (e.mode == kEpiEuler) ? __ldg(e.dt) : 0.f;
 #pragma unroll 1
@@ -208,7 +255,13 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       }
       continue;
     }
-    float* dst = e.out_f32 + row * e.ld_out + cb;
+    float* dst;
+    if (e.mode == kEpiGatePeer) {
+      const int64_t owner = row / e.chunk_rows;
+      dst = e.peer_out[owner] + (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out + cb;
+    } else {
+      dst = e.out_f32 + row * e.ld_out + cb;
+    }
     full = full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) &&
            (!gate || (reinterpret_cast<uintptr_t>(gate + cb) & 15) == 0) &&
            (e.mode != kEpiEuler || (reinterpret_cast<uintptr_t>(e.x_in + row * e.ld_out + cb) & 15) == 0);
@@ -220,7 +273,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
                                __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
         if (e.mode == kEpiF32) {
           d4[v] = a;
-        } else if (e.mode == kEpiResidGate || e.mode == kEpiGateF32) {
+        } else if (e.mode == kEpiResidGate || gate_only) {
           float4 gg = gate ? __ldg(reinterpret_cast<const float4*>(gate + cb) + v)
                            : make_float4(1.f, 1.f, 1.f, 1.f);
           if (e.mode == kEpiResidGate) {
@@ -240,7 +293,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
         float a = __uint_as_float(r[j]);
         if (e.mode == kEpiF32) dst[j] = a;
         else if (e.mode == kEpiResidGate) dst[j] += (gate ? gate[cb + j] : 1.f) * a;
-        else if (e.mode == kEpiGateF32) dst[j] = (gate ? gate[cb + j] : 1.f) * a;
+        else if (gate_only) dst[j] = (gate ? gate[cb + j] : 1.f) * a;
         else dst[j] = e.x_in[row * e.ld_out + cb + j] + dt * a;
       }
     }
@@ -283,7 +336,9 @@ constexpr int gemm_threads() { return (6 + BCfg<BSRC>::kDequantWarps) * 32; }
 template <int BSRC>
 constexpr int gemm_stage_bytes() { return kAStageBytes + kBStageBytes + BCfg<BSRC>::kRawBytes; }
 template <int BSRC>
-constexpr int gemm_smem_bytes() { return BCfg<BSRC>::kStages * gemm_stage_bytes<BSRC>() + 1024 + 256; }
+constexpr int gemm_smem_bytes() {
+  return BCfg<BSRC>::kStages * gemm_stage_bytes<BSRC>() + kEpiStageBytes + 1024 + 256;
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -434,7 +489,8 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + kStages * kAStageBytes;
   uint8_t* smR = smB + kStages * kBStageBytes;  // raw quantised stages (kQuant)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw);
+  float* epi_stage = reinterpret_cast<float*>(smR + kStages * kRaw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw + kEpiStageBytes);
   uint64_t* full = bars;                        // [stages] TMA A (+ raw B) landed
   uint64_t* empty = bars + kStages;             // [stages] MMA done with the stage
   uint64_t* bready = bars + 2 * kStages;        // [stages] dequantised B written (kQuant)
@@ -546,7 +602,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
       tc_fence_after();
       const TileCoord tc = decode_tile(p, t);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-      epilogue_row(p, tc, tc.m_tile * kGemmBM, row_in_tile, taddr);
+      epilogue_row(p, tc, tc.m_tile * kGemmBM, row_in_tile, taddr, epi_stage + quarter * 32 * kEpiStageStride);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -620,8 +676,13 @@ template <int BSRC>
 __host__ __device__ constexpr int pair_threads() { return (6 + PairCfg<BSRC>::kDequantWarps) * 32; }
 template <int BSRC>
 __host__ __device__ constexpr int pair_smem_bytes() {
-  return PairCfg<BSRC>::kStages * (kPairA + kPairB + pair_raw_bytes<BSRC>()) + 1024 + 256;
+  return PairCfg<BSRC>::kStages * (kPairA + kPairB + pair_raw_bytes<BSRC>()) + kEpiStageBytes + 1024 + 256;
 }
+
+static_assert(gemm_smem_bytes<kBSrcBf16>() <= 232448 && gemm_smem_bytes<kBSrcQ4_K>() <= 232448 &&
+                  gemm_smem_bytes<kBSrcQ8_0>() <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
+static_assert(pair_smem_bytes<kBSrcBf16>() <= 232448 && pair_smem_bytes<kBSrcQ4_K>() <= 232448 &&
+                  pair_smem_bytes<kBSrcQ8_0>() <= 232448, "pair GEMM shared memory above the 227 KB per-CTA limit");
 
 template <int BSRC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>(), 1)
@@ -637,7 +698,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
   uint8_t* smA = smem;
   uint8_t* smB = smA + kStages * kPairA;
   uint8_t* smR = smB + kStages * kPairB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw);
+  float* epi_stage = reinterpret_cast<float*>(smR + kStages * kRaw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw + kEpiStageBytes);
   uint64_t* full = bars;                     // [stages] rank 0: A (+ B) bytes of both CTAs
   uint64_t* empty = bars + kStages;          // [stages] both: the MMA released the stage
   uint64_t* rfull = bars + 2 * kStages;      // [stages] both: this CTA's raw quantised rows landed
@@ -775,7 +837,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       tc_fence_after();
       const TileCoord tc = decode_tile(p, t);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-      epilogue_row(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr);
+      epilogue_row(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr,
+                   epi_stage + quarter * 32 * kEpiStageStride);
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }

@@ -30,6 +30,7 @@ enum GemmEpilogue : int {
   kEpiQkvMlp = 3,     // q/k: RMSNorm + RoPE -> [B,H,S,d]; v -> [B,H,S,d]; mlp gate/up -> SwiGLU
   kEpiEuler = 4,      // out_f32[r, c] = x_in[r, c] + dt * acc  (FlowMatchEuler integrate)
   kEpiGateF32 = 5,    // out_f32[r, c] = gate_g[c] * acc   (TP partial before the all-reduce)
+  kEpiGatePeer = 6,   // gate_g[c] * acc stored into the owning rank's receive slot (TP reduce-scatter)
 };
 
 struct GemmGroup {
@@ -68,6 +69,13 @@ struct EpilogueArgs {
   int64_t vt_stride;         // keys per V^T row (S rounded up to 64)
   uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
   int64_t ld_mlp;
+  // kEpiGatePeer: output row r belongs to rank o = r / chunk_rows, whose
+  // receive buffer (peer_out[o], mapped from that GPU) holds one slot of
+  // chunk_rows rows per source rank; this rank writes slot peer_slot:
+  //   peer_out[o] + (peer_slot * chunk_rows + r - o * chunk_rows) * ld_out.
+  float* peer_out[8];
+  int32_t chunk_rows;
+  int32_t peer_slot;
 };
 
 // A quantised weight packed per (256-row tile, 64-K stage) by

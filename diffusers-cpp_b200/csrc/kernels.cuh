@@ -35,7 +35,7 @@ struct NormSegment {
 struct NormArgs {
   const float* x;       // f32 [*, D] (the residual stream)
   float* x_out;         // if resid: x_out = x + resid (may alias x)
-  const float* resid;   // optional addend (TP all-reduced partials), same layout as x
+  const float* resid;   // optional addend (TP partials), same layout as x, or n_slots slots (below)
   uint16_t* y;          // bf16 [*, ld_y]
   int64_t ld_x;
   int64_t ld_y;
@@ -43,7 +43,31 @@ struct NormArgs {
   float eps;
   int32_t n_segments;
   NormSegment seg[kMaxNormSegments];
+  // Tensor-parallel reduce + all-gather form (n_slots > 0): the addend of
+  // row r is the sum over s < n_slots of resid[s * slot_stride + (r - slot_row0) * ld_x],
+  // added in slot order; the bf16 output row is also stored to y_peer[k]
+  // (k < n_peer_out, other GPUs' buffers mapped into this process).
+  int32_t n_slots;
+  int64_t slot_stride;
+  int64_t slot_row0;
+  int32_t n_peer_out;
+  uint16_t* y_peer[7];
 };
+
+// Cross-GPU barrier of a tensor-parallel group.  flags[j] is rank j's flag
+// array (mapped from its GPU), one uint32 per source rank; each barrier
+// bumps the local epoch, writes it into every rank's flags[.][rank] and waits
+// (bounded: kDevTimeoutPeer into err after 1 s) until all of this rank's
+// flags reach it.  All writes issued before the barrier on this stream are
+// visible to the peers after it.
+struct TpBarrierArgs {
+  uint32_t* flags[8];
+  uint32_t* epoch;   // local device counter
+  int* err;
+  int32_t rank;
+  int32_t nranks;
+};
+cudaError_t launch_tp_barrier(const TpBarrierArgs& a, cudaStream_t s);
 
 // y = LayerNorm(x) * (1 + scale) + shift, one warp per row.
 cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s);

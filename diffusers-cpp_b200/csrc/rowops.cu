@@ -41,7 +41,10 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
   const int D = a.D;
   const int nv = D >> 2;
   const float4* x4 = reinterpret_cast<const float4*>(a.x + src * a.ld_x);
-  const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + src * a.ld_x) : nullptr;
+  const int nsl = a.n_slots > 0 ? a.n_slots : 1;
+  const int64_t roff = a.n_slots > 0 ? (src - a.slot_row0) * a.ld_x : src * a.ld_x;
+  const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + roff) : nullptr;
+  const int64_t slot4 = a.slot_stride >> 2;
   float4* xo4 = a.resid ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
 
   float4 v[kVec];
@@ -52,8 +55,11 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
     if (idx < nv) {
       float4 t = x4[idx];
       if (r4) {
-        const float4 r = r4[idx];
-        t.x += r.x; t.y += r.y; t.z += r.z; t.w += r.w;
+#pragma unroll 1
+        for (int sl = 0; sl < nsl; ++sl) {
+          const float4 r = r4[sl * slot4 + idx];
+          t.x += r.x; t.y += r.y; t.z += r.z; t.w += r.w;
+        }
         xo4[idx] = t;
       }
       v[i] = t;
@@ -107,9 +113,38 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
       float o1 = (1.0f + sc.y) * (t.y * rstd) + sh.y;
       float o2 = (1.0f + sc.z) * (t.z * rstd) + sh.z;
       float o3 = (1.0f + sc.w) * (t.w * rstd) + sh.w;
-      y2[idx] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+      const uint2 o = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+      y2[idx] = o;
+      for (int k = 0; k < a.n_peer_out; ++k) reinterpret_cast<uint2*>(a.y_peer[k] + dst * a.ld_y)[idx] = o;
     }
   }
+}
+
+// One CTA of up to 32 threads; thread j exchanges arrivals with rank j.
+__global__ void tp_barrier_kernel(const __grid_constant__ TpBarrierArgs a) {
+  __shared__ uint32_t ep_s;
+  if (threadIdx.x == 0) ep_s = *a.epoch + 1u;
+  __syncthreads();
+  const uint32_t ep = ep_s;
+  const int j = threadIdx.x;
+  if (j < a.nranks) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[j] + a.rank), "r"(ep) : "memory");
+    const uint32_t* mine = a.flags[a.rank] + j;
+    const unsigned long long t0 = globaltimer();
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (static_cast<int32_t>(v - ep) >= 0) break;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        atomicCAS(a.err, 0, kDevTimeoutPeer);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.epoch = ep;
 }
 
 __global__ void f32_to_bf16_kernel(const float4* __restrict__ in, int64_t n4, uint2* __restrict__ out) {
@@ -174,94 +209,138 @@ __global__ void timestep_proj_kernel(const float* __restrict__ t, int channels, 
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-// One warp per output feature; lanes stride over 32-weight sub-blocks.
+// Batch-1..4 GEMV y[b] = W x[b] for the conditioning path (timestep /
+// guidance embedders, the three modulation projections, norm_out), reading
+// the raw GGUF rows.  One warp per row, kGemvRowsPerWarp rows per warp so a
+// CTA's fill of x into shared memory (with the optional SiLU of the input)
+// serves 32 rows.  Lanes walk a row so that each quarter-warp reads 128
+// contiguous bytes of x (conflict-free float4 shared loads) and the warp
+// reads contiguous weight bytes:
+//   Q4_K: lane L = 8m + t takes nibble bytes [4t, 4t+4) of 32-byte group m of
+//         each 256-weight block: weights 4t..4t+3 of sub-blocks 2m (low
+//         nibbles) and 2m+1 (high nibbles);
+//   Q8_0: 8 lanes per 32-weight block, 4 weights each, 4 blocks per step;
+//   BF16 / F16: 8 consecutive weights per lane (one 16-byte load).
+// Weights are dequantised exactly as dequant.cu does (d*sc*q - dmin*m with
+// separate roundings), then accumulated with FMAs in f32.
+constexpr int kGemvRowsPerWarp = 4;
+constexpr int kGemvRowsPerCta = 8 * kGemvRowsPerWarp;
+
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int& sc, int& m) {
+  if (j < 4) {
+    sc = s[j] & 0x3F;
+    m = s[j + 4] & 0x3F;
+  } else {
+    sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30);
+    m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30);
+  }
+}
+
 template <int kType>
 __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t* __restrict__ W, int64_t N, int64_t K,
                                                    const float* __restrict__ x, int B, int act_in, int act_out,
                                                    float* __restrict__ y) {
-  extern __shared__ float xs[];  // [B, K]
+  extern __shared__ float4 xs4[];  // [B, K]
+  float* xs = reinterpret_cast<float*>(xs4);
   for (int64_t i = threadIdx.x; i < static_cast<int64_t>(B) * K; i += blockDim.x) {
     float v = x[i];
     xs[i] = act_in ? silu_f(v) : v;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5);
-  if (n >= N) return;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const int64_t nsb = K / 32;
-  if (kType == kTypeQ4_K) {
-    const uint8_t* row = W + n * (K / 256) * 144;
-    for (int64_t sb = lane; sb < nsb; sb += 32) {
-      const uint8_t* blk = row + (sb >> 3) * 144;
-      const int j = static_cast<int>(sb & 7);
-      const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
-      const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk + 2)));
-      const uint8_t* s = blk + 4;
-      int sc, m;
-      if (j < 4) { sc = s[j] & 0x3F; m = s[j + 4] & 0x3F; }
-      else { sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30); m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30); }
-      const float ds = d * static_cast<float>(sc);
-      const float dm = dmin * static_cast<float>(m);
-      const uint4* q4 = reinterpret_cast<const uint4*>(blk + 16 + (j >> 1) * 32);
-      const int shift = (j & 1) * 4;
-      uint4 qa = __ldg(q4), qb = __ldg(q4 + 1);
-      uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-      for (int b = 0; b < B; ++b) {
-        const float* xv = xs + b * K + sb * 32;
-        float sq = 0.f, sx = 0.f;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * kGemvRowsPerWarp;
+#pragma unroll 1
+  for (int rr = 0; rr < kGemvRowsPerWarp; ++rr) {
+    const int64_t n = row0 + rr;
+    if (n >= N) break;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (kType == kTypeQ4_K) {
+      const int m = lane >> 3, t = lane & 7;
+      const int64_t nblk = K / 256;
+      const uint8_t* row = W + n * nblk * 144;
+#pragma unroll 4
+      for (int64_t bk = 0; bk < nblk; ++bk) {
+        const uint8_t* bp = row + bk * 144;
+        const uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(bp));
+        const uint32_t q = __ldg(reinterpret_cast<const uint32_t*>(bp + 16 + m * 32 + 4 * t));
+        const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(dd & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half(static_cast<uint16_t>(dd >> 16)));
+        int sc0, m0, sc1, m1;
+        q4k_scale_min(2 * m, bp + 4, sc0, m0);
+        q4k_scale_min(2 * m + 1, bp + 4, sc1, m1);
+        const float ds0 = __fmul_rn(d, static_cast<float>(sc0)), dm0 = __fmul_rn(dmin, static_cast<float>(m0));
+        const float ds1 = __fmul_rn(d, static_cast<float>(sc1)), dm1 = __fmul_rn(dmin, static_cast<float>(m1));
+        float w0[4], w1[4];
 #pragma unroll
-        for (int l = 0; l < 32; ++l) {
-          const float q = static_cast<float>((w[l >> 2] >> (8 * (l & 3) + shift)) & 0xF);
-          sq = fmaf(q, xv[l], sq);
-          sx += xv[l];
+        for (int i = 0; i < 4; ++i) {
+          w0[i] = __fsub_rn(__fmul_rn(ds0, static_cast<float>((q >> (8 * i)) & 0xF)), dm0);
+          w1[i] = __fsub_rn(__fmul_rn(ds1, static_cast<float>((q >> (8 * i + 4)) & 0xF)), dm1);
         }
-        acc[b] += ds * sq - dm * sx;
-      }
-    }
-  } else if (kType == kTypeQ8_0) {
-    const uint8_t* row = W + n * nsb * 34;
-    for (int64_t sb = lane; sb < nsb; sb += 32) {
-      const uint8_t* blk = row + sb * 34;
-      const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
-      for (int b = 0; b < B; ++b) {
-        const float* xv = xs + b * K + sb * 32;
-        float sq = 0.f;
-#pragma unroll
-        for (int l = 0; l < 32; ++l) sq = fmaf(static_cast<float>(static_cast<int8_t>(blk[2 + l])), xv[l], sq);
-        acc[b] += d * sq;
-      }
-    }
-  } else if (kType == kTypeBF16 || kType == kTypeF16) {
-    const uint16_t* row = reinterpret_cast<const uint16_t*>(W) + n * K;
-    for (int64_t c = lane; c < K / 8; c += 32) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + c);
-      const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-      float wf[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (kType == kTypeBF16) {
-          wf[2 * i] = __uint_as_float(wv[i] << 16);
-          wf[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
-        } else {
-          wf[2 * i] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] & 0xFFFF)));
-          wf[2 * i + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] >> 16)));
+        for (int b = 0; b < B; ++b) {
+          const float* xb = xs + b * K + bk * 256 + 4 * t;
+          const float4 x0 = *reinterpret_cast<const float4*>(xb + (2 * m) * 32);
+          const float4 x1 = *reinterpret_cast<const float4*>(xb + (2 * m + 1) * 32);
+          float a = acc[b];
+          a = fmaf(w0[0], x0.x, a); a = fmaf(w0[1], x0.y, a); a = fmaf(w0[2], x0.z, a); a = fmaf(w0[3], x0.w, a);
+          a = fmaf(w1[0], x1.x, a); a = fmaf(w1[1], x1.y, a); a = fmaf(w1[2], x1.z, a); a = fmaf(w1[3], x1.w, a);
+          acc[b] = a;
         }
       }
-      for (int b = 0; b < B; ++b) {
-        const float* xv = xs + b * K + c * 8;
+    } else if (kType == kTypeQ8_0) {
+      const int t = lane & 7;
+      const int64_t nblk = K / 32;
+      const uint8_t* row = W + n * nblk * 34;
+#pragma unroll 2
+      for (int64_t bk = lane >> 3; bk < nblk; bk += 4) {
+        const uint16_t* bp = reinterpret_cast<const uint16_t*>(row + bk * 34);
+        const float d = __half2float(__ushort_as_half(__ldg(bp)));
+        const uint32_t lo = __ldg(bp + 1 + 2 * t), hi = __ldg(bp + 2 + 2 * t);
+        const uint32_t q = lo | (hi << 16);
+        float w[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[b] = fmaf(wf[i], xv[i], acc[b]);
+        for (int i = 0; i < 4; ++i) w[i] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>((q >> (8 * i)) & 0xFF)));
+        for (int b = 0; b < B; ++b) {
+          const float4 xv = *reinterpret_cast<const float4*>(xs + b * K + bk * 32 + 4 * t);
+          float a = acc[b];
+          a = fmaf(w[0], xv.x, a); a = fmaf(w[1], xv.y, a); a = fmaf(w[2], xv.z, a); a = fmaf(w[3], xv.w, a);
+          acc[b] = a;
+        }
       }
+    } else if (kType == kTypeBF16 || kType == kTypeF16) {
+      const uint16_t* row = reinterpret_cast<const uint16_t*>(W) + n * K;
+#pragma unroll 2
+      for (int64_t c = lane; c < K / 8; c += 32) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + c);
+        const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+        float wf[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (kType == kTypeBF16) {
+            wf[2 * i] = __uint_as_float(wv[i] << 16);
+            wf[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
+          } else {
+            wf[2 * i] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] & 0xFFFF)));
+            wf[2 * i + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[i] >> 16)));
+          }
+        }
+        for (int b = 0; b < B; ++b) {
+          const float4 xa = *reinterpret_cast<const float4*>(xs + b * K + c * 8);
+          const float4 xb = *reinterpret_cast<const float4*>(xs + b * K + c * 8 + 4);
+          float a = acc[b];
+          a = fmaf(wf[0], xa.x, a); a = fmaf(wf[1], xa.y, a); a = fmaf(wf[2], xa.z, a); a = fmaf(wf[3], xa.w, a);
+          a = fmaf(wf[4], xb.x, a); a = fmaf(wf[5], xb.y, a); a = fmaf(wf[6], xb.z, a); a = fmaf(wf[7], xb.w, a);
+          acc[b] = a;
+        }
+      }
+    } else {  // F32
+      const float* row = reinterpret_cast<const float*>(W) + n * K;
+      for (int64_t c = lane; c < K; c += 32)
+        for (int b = 0; b < B; ++b) acc[b] = fmaf(row[c], xs[b * K + c], acc[b]);
     }
-  } else {  // F32
-    const float* row = reinterpret_cast<const float*>(W) + n * K;
-    for (int64_t c = lane; c < K; c += 32)
-      for (int b = 0; b < B; ++b) acc[b] = fmaf(row[c], xs[b * K + c], acc[b]);
-  }
-  for (int b = 0; b < B; ++b) {
-    float v = warp_sum(acc[b]);
-    if (lane == 0) y[b * N + n] = act_out ? silu_f(v) : v;
+    for (int b = 0; b < B; ++b) {
+      float v = warp_sum(acc[b]);
+      if (lane == 0) y[b * N + n] = act_out ? silu_f(v) : v;
+    }
   }
 }
 
@@ -275,6 +354,8 @@ __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ 
 
 cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
   if (a.D % 4 != 0 || a.D > 8192 || (a.ld_x % 4) || (a.ld_y % 4)) return cudaErrorInvalidValue;
+  if (a.n_slots < 0 || a.n_slots > 8 || (a.slot_stride % 4) || a.n_peer_out < 0 || a.n_peer_out > 7)
+    return cudaErrorInvalidValue;
   int64_t rows = 0;
   for (int i = 0; i < a.n_segments; ++i) rows += a.seg[i].rows;
   if (rows == 0) return cudaSuccess;
@@ -282,6 +363,15 @@ cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
     layernorm_mod_kernel<128, 8><<<static_cast<unsigned>(rows), 128, 0, s>>>(a);
   else
     layernorm_mod_kernel<256, 8><<<static_cast<unsigned>(rows), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_barrier(const TpBarrierArgs& a, cudaStream_t s) {
+  if (a.nranks < 1 || a.nranks > 8 || a.rank < 0 || a.rank >= a.nranks || !a.epoch || !a.err)
+    return cudaErrorInvalidValue;
+  for (int j = 0; j < a.nranks; ++j)
+    if (!a.flags[j]) return cudaErrorInvalidValue;
+  tp_barrier_kernel<<<1, 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -327,7 +417,7 @@ cudaError_t launch_gemv(int wtype, const void* W, int64_t N, int64_t K, const fl
   if (B < 1 || B > 4) return cudaErrorInvalidValue;
   const size_t smem = static_cast<size_t>(B) * K * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  const unsigned grid = static_cast<unsigned>((N + 7) / 8);
+  const unsigned grid = static_cast<unsigned>((N + kGemvRowsPerCta - 1) / kGemvRowsPerCta);
   const uint8_t* w = static_cast<const uint8_t*>(W);
 #define DCPP_GEMV(T)                                                                                   \
   do {                                                                                                 \

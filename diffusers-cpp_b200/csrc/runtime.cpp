@@ -31,6 +31,7 @@ Nccl& Nccl::get() {
   n.CommAbort = reinterpret_cast<int (*)(Comm)>(sym("ncclCommAbort"));
   n.AllReduce =
       reinterpret_cast<int (*)(const void*, void*, size_t, int, int, Comm, cudaStream_t)>(sym("ncclAllReduce"));
+  n.AllGather = reinterpret_cast<int (*)(const void*, void*, size_t, int, Comm, cudaStream_t)>(sym("ncclAllGather"));
   n.GetErrorString = reinterpret_cast<const char* (*)(int)>(sym("ncclGetErrorString"));
   n.loaded = true;
   return n;
@@ -57,6 +58,69 @@ void* Ctx::ensure_scratch(size_t bytes) {
   return scratch;
 }
 
+void PeerBuffer::open(Ctx& ctx, size_t nbytes) {
+  if (local) fail(DCPP_ERR_STATE, "peer buffer already open");
+  if (!ctx.comm || ctx.nranks < 2 || ctx.nranks > 8) fail(DCPP_ERR_STATE, "peer buffer needs a TP group of 2..8");
+  auto& n = Nccl::get();
+  bytes = nbytes;
+  if (cudaMalloc(&local, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    local = nullptr;
+    fail(DCPP_ERR_OOM, "peer buffer allocation failed");
+  }
+  cuda_check(cudaMemsetAsync(local, 0, bytes, ctx.stream), "clear peer buffer");
+  cudaIpcMemHandle_t mine;
+  cuda_check(cudaIpcGetMemHandle(&mine, local), "cudaIpcGetMemHandle");
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  uint8_t* dev = nullptr;
+  cuda_check(cudaMalloc(&dev, hb * (ctx.nranks + 1)), "handle exchange buffer");
+  std::vector<uint8_t> all(hb * ctx.nranks);
+  try {
+    cuda_check(cudaMemcpyAsync(dev + hb * ctx.nranks, &mine, hb, cudaMemcpyHostToDevice, ctx.stream), "copy handle");
+    int r = n.AllGather(dev + hb * ctx.nranks, dev, hb, /*ncclUint8*/ 1, ctx.comm, ctx.stream);
+    if (r != 0) fail(DCPP_ERR_NCCL, std::string("ncclAllGather: ") + n.GetErrorString(r));
+    cuda_check(cudaMemcpyAsync(all.data(), dev, hb * ctx.nranks, cudaMemcpyDeviceToHost, ctx.stream), "copy handles");
+    cuda_check(cudaStreamSynchronize(ctx.stream), "handle exchange");
+  } catch (...) {
+    cudaFree(dev);
+    throw;
+  }
+  cudaFree(dev);
+  for (int j = 0; j < ctx.nranks; ++j) {
+    if (j == ctx.rank) {
+      peer[j] = local;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, all.data() + hb * j, hb);
+    void* p = nullptr;
+    cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    peer[j] = static_cast<uint8_t*>(p);
+  }
+}
+
+void PeerBuffer::close(Ctx& ctx) {
+  if (!local) return;
+  cudaStreamSynchronize(ctx.stream);
+  for (int j = 0; j < 8; ++j) {
+    if (peer[j] && peer[j] != local) cudaIpcCloseMemHandle(peer[j]);
+    peer[j] = nullptr;
+  }
+  // Every rank has unmapped this rank's buffer before it is freed.
+  if (ctx.comm) {
+    auto& n = Nccl::get();
+    float* one = nullptr;
+    if (cudaMalloc(&one, sizeof(float)) == cudaSuccess) {
+      n.AllReduce(one, one, 1, /*ncclFloat32*/ 7, /*ncclSum*/ 0, ctx.comm, ctx.stream);
+      cudaStreamSynchronize(ctx.stream);
+      cudaFree(one);
+    }
+  }
+  cudaFree(local);
+  local = nullptr;
+  bytes = 0;
+}
+
 const char* device_error_name(int code) {
   switch (code) {
     case kDevTimeoutFull: return "GEMM consumer timed out waiting for a shared-memory stage";
@@ -66,6 +130,7 @@ const char* device_error_name(int code) {
     case kDevTimeoutDequant: return "GEMM dequant stage handshake timed out";
     case kDevBadShape: return "kernel launched with an unsupported shape";
     case kDevTimeoutAttn: return "attention pipeline wait timed out";
+    case kDevTimeoutPeer: return "tensor-parallel barrier timed out waiting for a peer GPU";
     default: return "unknown device error";
   }
 }

@@ -36,6 +36,7 @@ struct Nccl {
   int (*CommDestroy)(Comm) = nullptr;
   int (*CommAbort)(Comm) = nullptr;
   int (*AllReduce)(const void*, void*, size_t, int, int, Comm, cudaStream_t) = nullptr;
+  int (*AllGather)(const void*, void*, size_t, int, Comm, cudaStream_t) = nullptr;
   const char* (*GetErrorString)(int) = nullptr;
   bool loaded = false;
   static Nccl& get();  // loads on first use; throws DCPP_ERR_NCCL when missing
@@ -74,6 +75,19 @@ struct Ctx {
 };
 
 const char* device_error_name(int code);
+
+// A device buffer of the same size on every rank of the context's TP group,
+// with every peer's copy mapped into this process (CUDA IPC; the handles are
+// exchanged with an NCCL all-gather).  open() and close() are collective.
+// peer[j] is rank j's buffer (peer[rank] == local); kernels of this library
+// store into peers' buffers over NVLink with plain loads and stores.
+struct PeerBuffer {
+  uint8_t* local = nullptr;
+  size_t bytes = 0;
+  uint8_t* peer[8] = {};
+  void open(Ctx& ctx, size_t bytes);
+  void close(Ctx& ctx);
+};
 
 }  // namespace dcpp
 

@@ -1,0 +1,60 @@
+"""Tensor parallelism on 2 GPUs over NCCL: the sharded model (column-parallel
+q/k/v/gate/up, row-parallel output projections, an all-reduce after each) must
+match the float64 oracle like the single-GPU model does.  Runs the ranks as
+child processes under torch.distributed.run, bounded by a timeout that kills
+the whole process group; skipped with fewer than 2 GPUs."""
+import json
+import os
+import signal
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+import flux2_oracle as fo
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+V_TOL = 3e-2
+LAT_TOL = 1e-2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_ranks(tmp_path, heads, wtype, comm, n=2, timeout=600):
+    out = tmp_path / "tp.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(HERE, "tp_gpu_worker.py"), str(out), str(heads), str(wtype), comm]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    p = subprocess.Popen(cmd, env=env, start_new_session=True, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+    try:
+        log, _ = p.communicate(timeout=timeout)
+    except subprocess.TimeoutExpired:
+        os.killpg(p.pid, signal.SIGKILL)
+        log, _ = p.communicate()
+        pytest.fail("TP ranks timed out:\n" + log.decode(errors="replace")[-4000:])
+    assert p.returncode == 0, log.decode(errors="replace")[-4000:]
+    return json.loads(out.read_text())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("heads,wtype,comm", [(4, fo.GGML_Q8_0, "peer"), (6, fo.GGML_Q4_K, "peer"),
+                                              (4, fo.GGML_Q8_0, "nccl"), (6, fo.GGML_Q4_K, "nccl")],
+                         ids=["q8_0_peer", "q4_k_bf16_shards_peer", "q8_0_nccl", "q4_k_bf16_shards_nccl"])
+def test_tp2_matches_oracle(tmp_path, heads, wtype, comm):
+    """peer: partials stored into the owning GPU's memory by the GEMM epilogue,
+    LayerNorm + all-gather by the owner; nccl: ncclAllReduce of the partials."""
+    r = run_ranks(tmp_path, heads, wtype, comm)
+    assert r["ranks_identical"], r
+    assert r["replay_identical"], r
+    assert r["forward_rel"] < V_TOL, r
+    assert r["denoise_rel"] < LAT_TOL, r
+    assert r["resident_rel"] < LAT_TOL, r
