@@ -66,56 +66,98 @@ def algorithmic_flops(cfg, batch, n_img, n_txt):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 5 ms through
+    NVML during the timed region (nvidia-smi at its 200 ms minimum period
+    would see no sample of a sub-second region); nvidia-smi when NVML is
+    unavailable.  Reasons reported: hw_slowdown, hw_thermal_slowdown,
+    sw_thermal_slowdown, sw_power_cap."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.stop_evt = threading.Event()
+        self.t = None
+        self.h = None
+        self.src = "nvml"
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:
+                pr = torch.cuda.get_device_properties(cuda_index)
+                bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.h = None
+            self.src = "nvidia-smi"
+
+    def _poll(self):
+        nv = self.nv
+        while not self.stop_evt.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h) if hasattr(
+                    nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for name, bit in self.BITS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def start(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.lines = []
+            self.t = threading.Thread(target=lambda: [self.lines.append(x.strip()) for x in self.proc.stdout],
+                                      daemon=True)
             self.t.start()
         except OSError:
             self.proc = None
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.t.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
+        if self.h is not None:
+            self.stop_evt.set()
+            self.t.join(timeout=2)
+        elif getattr(self, "proc", None):
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self.lines:
+                parts = [p.strip() for p in ln.split(",")]
+                try:
+                    self.samples.append(float(parts[0]))
+                    self.max_mhz = float(parts[1])
+                except (ValueError, IndexError):
+                    continue
+                for n, v in zip(names, parts[2:6]):
+                    if v.lower().startswith("active"):
+                        self.reasons.add(n)
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": self.src}
 
 
 def measured_peaks():
@@ -262,6 +304,11 @@ def run_ours(args):
     clocks.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    # One untimed step queued right before the start event: its in-step
+    # cross-GPU exchanges line the ranks' streams up, so the host-side skew
+    # of leaving the barrier above is not timed as device work.
+    model.set_timestep(*sched[0])
+    model.run_resident()
     ev0.record(stream)
     for i in range(args.steps):
         model.set_timestep(*sched[i % 4])
@@ -280,8 +327,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     tsteps = [torch.tensor([s[0]], dtype=torch.float32) for s in sched]
+    model.denoise_step(hid_p, enc_p, tsteps[0], sched[0][1], iid, tid, out_p)  # aligns the ranks (untimed)
+    e0.record(stream)
     for i in range(args.steps):
         model.denoise_step(hid_p, enc_p, tsteps[i % 4], sched[i % 4][1], iid, tid, out_p)
     e1.record(stream)
@@ -299,7 +347,10 @@ def run_ours(args):
         model.set_timestep(*sched[i % 4])
         model.run_resident()
     torch.cuda.synchronize()
+    if args.ops_csv and rank == 0:
+        os.environ["DCPP_PROFILE_OPS"] = os.path.join(args.ops_csv, f"ops_config{args.config}_tp{world}.csv")
     prof = {k: model.profile(k) for k in dcpp_b200.Flux2Model.PROFILE_KINDS}
+    os.environ.pop("DCPP_PROFILE_OPS", None)
     prof_step_ms = sum(v[0] for v in prof.values())
 
     # max over ranks
@@ -396,6 +447,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="2")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -749,7 +749,6 @@ void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_tx
 void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
                                        const DevWeight* w0, const DevWeight* w1, std::vector<GemmGroup> groups,
                                        const EpilogueArgs& ep, int64_t N) {
-  (void)tag;
   if (w0->cols != K || (w1 && (w1->cols != K || w1->rows != w0->rows)) || w0->rows != N)
     fail(DCPP_ERR_STATE, "internal: GEMM shape mismatch for " + w0->name);
   // Fused dequantisation when every weight of the launch is packed and of
@@ -785,7 +784,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
                             else
                               cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
                           },
-                          1, kOpGemm, flops});
+                          1, kOpGemm, flops, tag + " (fused dequant)"});
     return;
   }
   if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
@@ -814,7 +813,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     building_->push_back({[w, dst](cudaStream_t s) {
                             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
                           },
-                          1, kOpDequant});
+                          1, kOpDequant, 0.0, "dequant " + tag});
   }
   if (w1 && w1->type != kTypeBF16) {
     const DevWeight* w = w1;
@@ -822,7 +821,7 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     building_->push_back({[w, dst](cudaStream_t s) {
                             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
                           },
-                          1, kOpDequant});
+                          1, kOpDequant, 0.0, "dequant " + tag});
   }
   double flops = 0.0;
   for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
@@ -833,11 +832,12 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
                           else
                             cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
                         },
-                        1, kOpGemm, flops});
+                        1, kOpGemm, flops, tag});
 }
 
 void Flux2Transformer2DModel::add_norm(const NormArgs& a) {
-  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm});
+  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm,
+                        0.0, a.n_slots ? "layernorm+allgather" : "layernorm"});
 }
 
 void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y) {
@@ -847,7 +847,7 @@ void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int a
                           cuda_check(launch_gemv(pw->type, pw->data, pw->rows, pw->cols, x, B, act_in, act_out, y, s),
                                      "gemv");
                         },
-                        1, kOpGemv, 2.0 * B * static_cast<double>(pw->rows) * static_cast<double>(pw->cols)});
+                        1, kOpGemv, 2.0 * B * static_cast<double>(pw->rows) * static_cast<double>(pw->cols), w.name});
 }
 
 void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
@@ -857,7 +857,7 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
                           int r = n.AllReduce(buf, buf, static_cast<size_t>(count), 7, 0, c->comm, s);
                           if (r != 0) fail(DCPP_ERR_NCCL, std::string("ncclAllReduce: ") + n.GetErrorString(r));
                         },
-                        0, kOpAllreduce});
+                        0, kOpAllreduce, 0.0, "nccl_allreduce"});
 }
 
 void Flux2Transformer2DModel::add_tp_barrier() {
@@ -867,7 +867,8 @@ void Flux2Transformer2DModel::add_tp_barrier() {
   a.err = ctx_.d_err;
   a.rank = rank_;
   a.nranks = nranks_;
-  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce});
+  building_->push_back(
+      {[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce, 0.0, "tp_barrier"});
 }
 
 void Flux2Transformer2DModel::build_plan() {
@@ -897,11 +898,11 @@ void Flux2Transformer2DModel::build_plan() {
     chunk_ = (R + nranks_ - 1) / nranks_;
     auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
     const size_t off_recv = up(R * D * 2);
-    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * chunk_ * D * 4);
+    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * chunk_ * D * 2);
     sym_.open(ctx_, off_flags + 256);
     for (int j = 0; j < nranks_; ++j) {
       a_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j]);
-      recv_peer_[j] = reinterpret_cast<float*>(sym_.peer[j] + off_recv);
+      recv_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j] + off_recv);
       flags_peer_[j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags);
     }
     a_ = a_peer_[rank_];
@@ -1088,7 +1089,8 @@ void Flux2Transformer2DModel::build_plan() {
                "attention tensor maps");
     auto attn_op = [&]() {
       ops.push_back({[at, maps](cudaStream_t s) { cuda_check(launch_attention_tc(*maps, at, s), "attention"); }, 1,
-                     kOpAttention, 4.0 * at.B * at.H * static_cast<double>(at.S) * static_cast<double>(at.S) * 128.0});
+                     kOpAttention, 4.0 * at.B * at.H * static_cast<double>(at.S) * static_cast<double>(at.S) * 128.0,
+                     "attention"});
     };
     auto out_epi = [&](const float* g0, const float* g1, int64_t bstride) {
       EpilogueArgs e{};
@@ -1099,7 +1101,7 @@ void Flux2Transformer2DModel::build_plan() {
       e.gate[1] = g1;
       e.gate_bstride = bstride;
       if (peer) {
-        for (int j = 0; j < nranks_; ++j) e.peer_out[j] = recv_peer_[j];
+        for (int j = 0; j < nranks_; ++j) e.peer_bf16[j] = recv_peer_[j];
         e.chunk_rows = static_cast<int32_t>(chunk_);
         e.peer_slot = rank_;
       }
@@ -1132,7 +1134,7 @@ void Flux2Transformer2DModel::build_plan() {
           n.seg[k++] = sg;
         }
         n.n_segments = k;
-        n.resid = recv_peer_[rank_];
+        n.slots = recv_peer_[rank_];
         n.n_slots = nranks_;
         n.slot_stride = chunk_ * D;
         n.slot_row0 = lo;
@@ -1389,6 +1391,22 @@ void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64
   if (ms) *ms = t;
   if (flops) *flops = f;
   if (launches) *launches = n;
+  // DCPP_PROFILE_OPS=<path>: also write every op of the step (index, tag,
+  // kind, milliseconds, algorithmic FLOPs) as CSV, once per executed step.
+  const char* path = getenv("DCPP_PROFILE_OPS");
+  if (path && kind == kOpGemm) {
+    FILE* f = fopen(path, "w");
+    if (f) {
+      fprintf(f, "index,tag,kind,ms,flops\n");
+      for (size_t i = 0; i < last_ops_->size(); ++i) {
+        const Op& o = (*last_ops_)[i];
+        float e = 0.f;
+        cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]);
+        fprintf(f, "%zu,%s,%d,%.5f,%.6g\n", i, o.tag.c_str(), o.kind, e, o.flops);
+      }
+      fclose(f);
+    }
+  }
 }
 
 void Flux2Transformer2DModel::read_latents(float* out) {

@@ -136,6 +136,7 @@ class Flux2Transformer2DModel {
     int launches;
     int kind = kOpOther;   // ProfileKind
     double flops = 0.0;    // algorithmic FLOPs of the op
+    std::string tag;       // what the op is (profile dumps)
   };
 
   void build_registry();
@@ -191,15 +192,15 @@ class Flux2Transformer2DModel {
   int32_t* ids_dev_ = nullptr;
   float2* rope_ = nullptr;
   // Tensor parallelism over peer memory (the default exchange): the
-  // row-parallel GEMMs store their gated partials straight into the owning
-  // rank's receive slots (recv, [nranks][chunk_ rows][D] f32 on each GPU),
-  // the owner's LayerNorm sums the slots into its residual rows and stores
-  // the normalised bf16 rows into every rank's activation buffer (a_).
+  // row-parallel GEMMs store their gated partials (bf16) straight into the
+  // owning rank's receive slots (recv, [nranks][chunk_ rows][D] on each
+  // GPU), the owner's LayerNorm sums the slots into its residual rows and
+  // stores the normalised bf16 rows into every rank's activation buffer (a_).
   // DCPP_TP_COMM=nccl selects ncclAllReduce of the partials instead.
   bool tp_peer_ = true;
   PeerBuffer sym_;
   int64_t chunk_ = 0;
-  float* recv_peer_[8] = {};
+  uint16_t* recv_peer_[8] = {};  // bf16 receive slots
   uint16_t* a_peer_[8] = {};
   uint32_t* flags_peer_[8] = {};
   uint32_t* epoch_ = nullptr;

@@ -56,10 +56,12 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 // `row_base` is the first row (within the group) of the 128 accumulator rows
 // this CTA holds: m_tile * 128 for 1-SM tiles, m_tile * 256 + rank * 128 for
 // the 2-SM pair.
-// Per-warp staging for the peer-store epilogue: 32 rows x 32 columns f32,
-// row stride 36 floats (16-byte aligned rows, conflict-free float4 access).
-constexpr int kEpiStageStride = 36;
-constexpr int kEpiStageBytes = 4 * 32 * kEpiStageStride * 4;
+// Per-warp staging for the peer-store epilogue: 32 rows x 64 columns bf16,
+// row stride 144 bytes (16-byte aligned rows; conflict-free 16-byte access
+// both row-wise and column-wise).
+constexpr int kEpiStageRowBytes = 144;
+constexpr int kEpiStageStride = kEpiStageRowBytes / 4;  // in floats
+constexpr int kEpiStageBytes = 4 * 32 * kEpiStageRowBytes;
 
 __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_base, int row_in_tile,
                                              uint32_t taddr, float* stage) {
@@ -183,41 +185,62 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     if (gate) gate += static_cast<int64_t>(G.batch) * e.gate_bstride;
   }
   if (e.mode == kEpiGatePeer) {
-    // Rows go to other GPUs over NVLink: transpose each 32 x 32 chunk through
-    // shared memory so every store instruction writes 4 rows x 128
-    // contiguous bytes (whole lines) instead of 32 scattered 16-byte pieces.
+    // Rows go to other GPUs over NVLink as bf16: gate and round 64 columns
+    // of the warp's 32 rows into shared memory, then store them transposed
+    // so that every store instruction writes 4 rows x 128 contiguous bytes
+    // (whole lines) instead of 32 scattered pieces.
     const int lane = row_in_tile & 31;
     uintptr_t rdst = 0;
     if (row_ok) {
       const int64_t owner = row / e.chunk_rows;
       rdst = reinterpret_cast<uintptr_t>(
-          e.peer_out[owner] + (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out);
+          e.peer_bf16[owner] +
+          (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out);
     }
     const int sub = lane >> 3, q = lane & 7;
+    uint8_t* srow = reinterpret_cast<uint8_t*>(stage) + lane * kEpiStageRowBytes;
 #pragma unroll 1
-    for (int c = 0; c < kGemmBN / 32; ++c) {
-      const int cb = col0 + c * 32;
-      uint32_t r[32];
-      tmem_ld32(taddr + c * 32, r);
-      tmem_ld_wait();
-      float4* st4 = reinterpret_cast<float4*>(stage + lane * kEpiStageStride);
+    for (int c = 0; c < kGemmBN / 64; ++c) {
+      const int cb = col0 + c * 64;
 #pragma unroll
-      for (int v = 0; v < 8; ++v)
-        st4[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
-                             __uint_as_float(r[4 * v + 3]));
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 64 + h * 32, r);
+        tmem_ld_wait();
+        const int gc = cb + h * 32;
+        const bool g_ok = gate && gc + 32 <= p.N;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float gv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) gv[i] = 1.f;
+          if (g_ok) {
+            const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + gc) + 2 * v);
+            const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + gc) + 2 * v + 1);
+            gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+            gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+          } else if (gate) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) gv[i] = (gc + 8 * v + i < p.N) ? gate[gc + 8 * v + i] : 0.f;
+          }
+          uint4 o;
+          o.x = pack_bf16x2(gv[0] * __uint_as_float(r[8 * v + 0]), gv[1] * __uint_as_float(r[8 * v + 1]));
+          o.y = pack_bf16x2(gv[2] * __uint_as_float(r[8 * v + 2]), gv[3] * __uint_as_float(r[8 * v + 3]));
+          o.z = pack_bf16x2(gv[4] * __uint_as_float(r[8 * v + 4]), gv[5] * __uint_as_float(r[8 * v + 5]));
+          o.w = pack_bf16x2(gv[6] * __uint_as_float(r[8 * v + 6]), gv[7] * __uint_as_float(r[8 * v + 7]));
+          *reinterpret_cast<uint4*>(srow + h * 64 + v * 16) = o;
+        }
+      }
       __syncwarp();
-      const int col = cb + 4 * q;
-      const bool col_ok = col + 4 <= p.N;
-      const float4 g = (gate && col_ok) ? __ldg(reinterpret_cast<const float4*>(gate + col))
-                                        : make_float4(1.f, 1.f, 1.f, 1.f);
+      const int col = cb + 8 * q;
+      const bool col_ok = col + 8 <= p.N;
 #pragma unroll
       for (int it = 0; it < 8; ++it) {
         const int rr = it * 4 + sub;
         const uintptr_t d = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(rdst), rr);
-        const float4 a = *reinterpret_cast<const float4*>(stage + rr * kEpiStageStride + 4 * q);
-        if (d && col_ok)
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(d) + col) =
-              make_float4(g.x * a.x, g.y * a.y, g.z * a.z, g.w * a.w);
+        const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(stage) +
+                                                         rr * kEpiStageRowBytes + q * 16);
+        if (d && col_ok) *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(d) + col) = a;
       }
       __syncwarp();
     }
@@ -255,13 +278,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       }
       continue;
     }
-    float* dst;
-    if (e.mode == kEpiGatePeer) {
-      const int64_t owner = row / e.chunk_rows;
-      dst = e.peer_out[owner] + (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out + cb;
-    } else {
-      dst = e.out_f32 + row * e.ld_out + cb;
-    }
+    float* dst = e.out_f32 + row * e.ld_out + cb;
     full = full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) &&
            (!gate || (reinterpret_cast<uintptr_t>(gate + cb) & 15) == 0) &&
            (e.mode != kEpiEuler || (reinterpret_cast<uintptr_t>(e.x_in + row * e.ld_out + cb) & 15) == 0);

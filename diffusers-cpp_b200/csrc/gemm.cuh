@@ -30,7 +30,7 @@ enum GemmEpilogue : int {
   kEpiQkvMlp = 3,     // q/k: RMSNorm + RoPE -> [B,H,S,d]; v -> [B,H,S,d]; mlp gate/up -> SwiGLU
   kEpiEuler = 4,      // out_f32[r, c] = x_in[r, c] + dt * acc  (FlowMatchEuler integrate)
   kEpiGateF32 = 5,    // out_f32[r, c] = gate_g[c] * acc   (TP partial before the all-reduce)
-  kEpiGatePeer = 6,   // gate_g[c] * acc stored into the owning rank's receive slot (TP reduce-scatter)
+  kEpiGatePeer = 6,   // bf16(gate_g[c] * acc) stored into the owning rank's receive slot (TP reduce-scatter)
 };
 
 struct GemmGroup {
@@ -70,10 +70,10 @@ struct EpilogueArgs {
   uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
   int64_t ld_mlp;
   // kEpiGatePeer: output row r belongs to rank o = r / chunk_rows, whose
-  // receive buffer (peer_out[o], mapped from that GPU) holds one slot of
-  // chunk_rows rows per source rank; this rank writes slot peer_slot:
-  //   peer_out[o] + (peer_slot * chunk_rows + r - o * chunk_rows) * ld_out.
-  float* peer_out[8];
+  // receive buffer (peer_bf16[o], mapped from that GPU) holds one bf16 slot
+  // of chunk_rows rows per source rank; this rank writes slot peer_slot:
+  //   peer_bf16[o] + (peer_slot * chunk_rows + r - o * chunk_rows) * ld_out.
+  uint16_t* peer_bf16[8];
   int32_t chunk_rows;
   int32_t peer_slot;
 };

@@ -44,9 +44,11 @@ struct NormArgs {
   int32_t n_segments;
   NormSegment seg[kMaxNormSegments];
   // Tensor-parallel reduce + all-gather form (n_slots > 0): the addend of
-  // row r is the sum over s < n_slots of resid[s * slot_stride + (r - slot_row0) * ld_x],
-  // added in slot order; the bf16 output row is also stored to y_peer[k]
-  // (k < n_peer_out, other GPUs' buffers mapped into this process).
+  // row r is the sum over s < n_slots of the bf16 partials
+  // slots[s * slot_stride + (r - slot_row0) * ld_x], added in slot order;
+  // the bf16 output row is also stored to y_peer[k] (k < n_peer_out, other
+  // GPUs' buffers mapped into this process).
+  const uint16_t* slots;
   int32_t n_slots;
   int64_t slot_stride;
   int64_t slot_row0;

@@ -23,8 +23,24 @@ __device__ __forceinline__ float warp_sum(float v) {
 // (LayerNorm.cpp:16-32 with elementwise_affine = false), then the adaLN
 // modulation (1 + scale) * n + shift (Flux2TransformerBlock.hpp:66,72,92,106;
 // Flux2SingleTransformerBlock.hpp:53-54; AdaLayerNormContinuous.inl:43).
-template <int kThreads, int kVec>
+template <int kW>
+struct PackOut;
+template <>
+struct PackOut<4> { using T = uint2; };
+template <>
+struct PackOut<8> { using T = uint4; };
+
+__device__ __forceinline__ void add_bf16x4(float4& t, uint2 u) {
+  t.x += __uint_as_float(u.x << 16); t.y += __uint_as_float(u.x & 0xFFFF0000u);
+  t.z += __uint_as_float(u.y << 16); t.w += __uint_as_float(u.y & 0xFFFF0000u);
+}
+
+// kW elements (4 or 8) per thread and step: one or two float4 loads of x,
+// one 8- or 16-byte bf16 store per output buffer.
+template <int kThreads, int kVec, int kW>
 __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_constant__ NormArgs a) {
+  constexpr int kF4 = kW / 4;
+  using OutT = typename PackOut<kW>::T;
   __shared__ float red[kThreads / 32];
   __shared__ float stat;
   int blk = blockIdx.x;
@@ -39,33 +55,36 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
   const int64_t src = sg.src_row0 + blk;
   const int64_t dst = sg.dst_row0 + blk;
   const int D = a.D;
-  const int nv = D >> 2;
+  const int ng = D / kW;
   const float4* x4 = reinterpret_cast<const float4*>(a.x + src * a.ld_x);
-  const int nsl = a.n_slots > 0 ? a.n_slots : 1;
-  const int64_t roff = a.n_slots > 0 ? (src - a.slot_row0) * a.ld_x : src * a.ld_x;
-  const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + roff) : nullptr;
-  const int64_t slot4 = a.slot_stride >> 2;
-  float4* xo4 = a.resid ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
+  const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + src * a.ld_x) : nullptr;
+  const uint16_t* sl = a.n_slots > 0 ? a.slots + (src - a.slot_row0) * a.ld_x : nullptr;
+  float4* xo4 = (a.resid || sl) ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
 
-  float4 v[kVec];
+  float4 v[kVec][kF4];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int idx = threadIdx.x + i * kThreads;
-    if (idx < nv) {
-      float4 t = x4[idx];
-      if (r4) {
-#pragma unroll 1
-        for (int sl = 0; sl < nsl; ++sl) {
-          const float4 r = r4[sl * slot4 + idx];
+#pragma unroll
+    for (int f = 0; f < kF4; ++f) {
+      if (idx < ng) {
+        float4 t = x4[idx * kF4 + f];
+        if (r4) {
+          const float4 r = r4[idx * kF4 + f];
           t.x += r.x; t.y += r.y; t.z += r.z; t.w += r.w;
         }
-        xo4[idx] = t;
+        if (sl) {
+#pragma unroll 1
+          for (int k = 0; k < a.n_slots; ++k)
+            add_bf16x4(t, reinterpret_cast<const uint2*>(sl + k * a.slot_stride)[idx * kF4 + f]);
+        }
+        if (xo4) xo4[idx * kF4 + f] = t;
+        v[i][f] = t;
+        sum += (t.x + t.y) + (t.z + t.w);
+      } else {
+        v[i][f] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      v[i] = t;
-      sum += (t.x + t.y) + (t.z + t.w);
-    } else {
-      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   sum = warp_sum(sum);
@@ -82,10 +101,13 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int idx = threadIdx.x + i * kThreads;
-    if (idx < nv) {
-      float4& t = v[i];
-      t.x -= mean; t.y -= mean; t.z -= mean; t.w -= mean;
-      sq += (t.x * t.x + t.y * t.y) + (t.z * t.z + t.w * t.w);
+    if (idx < ng) {
+#pragma unroll
+      for (int f = 0; f < kF4; ++f) {
+        float4& t = v[i][f];
+        t.x -= mean; t.y -= mean; t.z -= mean; t.w -= mean;
+        sq += (t.x * t.x + t.y * t.y) + (t.z * t.z + t.w * t.w);
+      }
     }
   }
   __syncthreads();
@@ -101,21 +123,25 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
   const float rstd = stat;
   const float4* sh4 = reinterpret_cast<const float4*>(sg.shift);
   const float4* sc4 = reinterpret_cast<const float4*>(sg.scale);
-  uint2* y2 = reinterpret_cast<uint2*>(a.y + dst * a.ld_y);
+  OutT* yo = reinterpret_cast<OutT*>(a.y + dst * a.ld_y);
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int idx = threadIdx.x + i * kThreads;
-    if (idx < nv) {
-      const float4 t = v[i];
-      const float4 sh = sh4 ? __ldg(sh4 + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 sc = sc4 ? __ldg(sc4 + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float o0 = (1.0f + sc.x) * (t.x * rstd) + sh.x;
-      float o1 = (1.0f + sc.y) * (t.y * rstd) + sh.y;
-      float o2 = (1.0f + sc.z) * (t.z * rstd) + sh.z;
-      float o3 = (1.0f + sc.w) * (t.w * rstd) + sh.w;
-      const uint2 o = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
-      y2[idx] = o;
-      for (int k = 0; k < a.n_peer_out; ++k) reinterpret_cast<uint2*>(a.y_peer[k] + dst * a.ld_y)[idx] = o;
+    if (idx < ng) {
+      uint32_t pk[2 * kF4];
+#pragma unroll
+      for (int f = 0; f < kF4; ++f) {
+        const float4 t = v[i][f];
+        const float4 sh = sh4 ? __ldg(sh4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 sc = sc4 ? __ldg(sc4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        pk[2 * f] = pack_bf16x2((1.0f + sc.x) * (t.x * rstd) + sh.x, (1.0f + sc.y) * (t.y * rstd) + sh.y);
+        pk[2 * f + 1] = pack_bf16x2((1.0f + sc.z) * (t.z * rstd) + sh.z, (1.0f + sc.w) * (t.w * rstd) + sh.w);
+      }
+      OutT o;
+      if constexpr (kW == 8) o = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      else o = make_uint2(pk[0], pk[1]);
+      yo[idx] = o;
+      for (int k = 0; k < a.n_peer_out; ++k) reinterpret_cast<OutT*>(a.y_peer[k] + dst * a.ld_y)[idx] = o;
     }
   }
 }
@@ -354,15 +380,27 @@ __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ 
 
 cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
   if (a.D % 4 != 0 || a.D > 8192 || (a.ld_x % 4) || (a.ld_y % 4)) return cudaErrorInvalidValue;
-  if (a.n_slots < 0 || a.n_slots > 8 || (a.slot_stride % 4) || a.n_peer_out < 0 || a.n_peer_out > 7)
+  if (a.n_slots < 0 || a.n_slots > 8 || (a.slot_stride % 8) || a.n_peer_out < 0 || a.n_peer_out > 7)
     return cudaErrorInvalidValue;
+  if (a.n_slots > 0 && (!a.slots || (reinterpret_cast<uintptr_t>(a.slots) & 15))) return cudaErrorInvalidValue;
   int64_t rows = 0;
   for (int i = 0; i < a.n_segments; ++i) rows += a.seg[i].rows;
   if (rows == 0) return cudaSuccess;
-  if (a.D <= 128 * 4 * 8)
-    layernorm_mod_kernel<128, 8><<<static_cast<unsigned>(rows), 128, 0, s>>>(a);
-  else
-    layernorm_mod_kernel<256, 8><<<static_cast<unsigned>(rows), 256, 0, s>>>(a);
+  const bool w8 = a.D % 8 == 0 && a.ld_y % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  for (int k = 0; k < a.n_peer_out; ++k)
+    if (reinterpret_cast<uintptr_t>(a.y_peer[k]) & (w8 ? 15 : 7)) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>(rows);
+  if (w8) {
+    if (a.D <= 128 * 8 * 4)
+      layernorm_mod_kernel<128, 4, 8><<<grid, 128, 0, s>>>(a);
+    else
+      layernorm_mod_kernel<256, 4, 8><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (a.D <= 128 * 4 * 8)
+      layernorm_mod_kernel<128, 8, 4><<<grid, 128, 0, s>>>(a);
+    else
+      layernorm_mod_kernel<256, 8, 4><<<grid, 256, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
