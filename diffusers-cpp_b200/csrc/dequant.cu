@@ -58,49 +58,65 @@ __device__ __forceinline__ void store8(void* out, int64_t i0, const float (&v)[8
   }
 }
 
-// One thread per 8 weights of a Q8_0 block (4 threads per block).
+// One thread per 8 weights of a Q8_0 block (4 threads per block), grid-stride
+// over blocks; the 8 quants are read as four 2-byte loads (blocks are only
+// 2-byte aligned).
 template <bool kBf16>
-__global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
-  int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (t >= nblocks * 4) return;
-  const int64_t b = t >> 2;
-  const int part = static_cast<int>(t & 3);
-  const uint8_t* blk = blocks + b * 34;
-  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
-  float v[8];
+__global__ void __launch_bounds__(256) dequant_q8_0_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks,
+                                                           void* out) {
+  const int64_t n = nblocks * 4;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = t >> 2;
+    const int part = static_cast<int>(t & 3);
+    const uint16_t* blk = reinterpret_cast<const uint16_t*>(blocks + b * 34);
+    const float d = half_bits_to_f32(__ldg(blk));
+    float v[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float q = static_cast<float>(static_cast<int8_t>(blk[2 + part * 8 + i]));
-    v[i] = __fmul_rn(q, d);
+    for (int i = 0; i < 4; ++i) {
+      const uint16_t q2 = __ldg(blk + 1 + part * 4 + i);
+      v[2 * i] = __fmul_rn(static_cast<float>(static_cast<int8_t>(q2 & 0xFF)), d);
+      v[2 * i + 1] = __fmul_rn(static_cast<float>(static_cast<int8_t>(q2 >> 8)), d);
+    }
+    store8<kBf16>(out, b * 32 + part * 8, v);
   }
-  store8<kBf16>(out, b * 32 + part * 8, v);
 }
 
-// One thread per 8 weights of a Q4_K super-block (32 threads per block).
+// One thread per 8 weights of a Q4_K super-block (32 threads per block),
+// grid-stride over blocks; the 16-byte header (d, dmin, 12 scale bytes) is
+// one vector load (blocks are 16-byte aligned: 144 = 9 x 16).
 template <bool kBf16>
-__global__ void dequant_q4_k_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, void* out) {
-  int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (t >= nblocks * 32) return;
-  const int64_t b = t >> 5;
-  const int j = static_cast<int>((t >> 2) & 7);  // sub-block
-  const int l0 = static_cast<int>(t & 3) * 8;    // first element within the sub-block
-  const uint8_t* blk = blocks + b * 144;
-  const float d = half_bits_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
-  const float dmin = half_bits_to_f32(static_cast<uint16_t>(blk[2] | (blk[3] << 8)));
-  int sc, m;
-  q4k_scale_min(blk + 4, j, sc, m);
-  const float ds = __fmul_rn(d, static_cast<float>(sc));
-  const float dm = __fmul_rn(dmin, static_cast<float>(m));
-  const uint2 raw = *reinterpret_cast<const uint2*>(blk + 16 + (j >> 1) * 32 + l0);
-  const int shift = (j & 1) * 4;
-  float v[8];
+__global__ void __launch_bounds__(256) dequant_q4_k_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks,
+                                                           void* out) {
+  const int64_t n = nblocks * 32;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = t >> 5;
+    const int j = static_cast<int>((t >> 2) & 7);  // sub-block
+    const int l0 = static_cast<int>(t & 3) * 8;    // first element within the sub-block
+    const uint8_t* blk = blocks + b * 144;
+    const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(blk + 16 + (j >> 1) * 32 + l0));
+    const float d = half_bits_to_f32(static_cast<uint16_t>(h.x & 0xFFFF));
+    const float dmin = half_bits_to_f32(static_cast<uint16_t>(h.x >> 16));
+    uint8_t sb[12];
+    const uint32_t hw[3] = {h.y, h.z, h.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t w = i < 4 ? raw.x : raw.y;
-    const float q = static_cast<float>((w >> (8 * (i & 3) + shift)) & 0x0F);
-    v[i] = __fsub_rn(__fmul_rn(ds, q), dm);
+    for (int i = 0; i < 12; ++i) sb[i] = static_cast<uint8_t>(hw[i >> 2] >> (8 * (i & 3)));
+    int sc, m;
+    q4k_scale_min(sb, j, sc, m);
+    const float ds = __fmul_rn(d, static_cast<float>(sc));
+    const float dm = __fmul_rn(dmin, static_cast<float>(m));
+    const int shift = (j & 1) * 4;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t w = i < 4 ? raw.x : raw.y;
+      const float q = static_cast<float>((w >> (8 * (i & 3) + shift)) & 0x0F);
+      v[i] = __fsub_rn(__fmul_rn(ds, q), dm);
+    }
+    store8<kBf16>(out, b * 256 + j * 32 + l0, v);
   }
-  store8<kBf16>(out, b * 256 + j * 32 + l0, v);
 }
 
 template <bool kBf16>
@@ -124,6 +140,41 @@ __global__ void dequant_f32_kernel(const float* __restrict__ in, int64_t n, void
   if (i < n) store_val<kBf16>(out, i, in[i]);
 }
 
+// Eight elements per thread (16-byte loads of f16 / bf16, two of f32;
+// 16-byte bf16 or two 16-byte f32 stores) when n % 8 == 0 and the input is
+// 16-byte aligned.
+template <int kType, bool kBf16>
+__global__ void convert8_kernel(const void* __restrict__ in, int64_t n8, void* out) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n8) return;
+  float v[8];
+  if (kType == kTypeF32) {
+    const float4* p = reinterpret_cast<const float4*>(in) + 2 * i;
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(in) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (kType == kTypeBF16) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      } else {
+        v[2 * k] = half_bits_to_f32(static_cast<uint16_t>(w[k] & 0xFFFF));
+        v[2 * k + 1] = half_bits_to_f32(static_cast<uint16_t>(w[k] >> 16));
+      }
+    }
+  }
+  store8<kBf16>(out, i * 8, v);
+}
+
+// Grid-stride kernels: at most 16 CTAs of 256 threads per SM (148 SMs).
+inline unsigned grid_cap(int64_t n, int threads) {
+  const int64_t g = (n + threads - 1) / threads;
+  return static_cast<unsigned>(g < 148 * 16 ? g : 148 * 16);
+}
+
 inline unsigned grid_for(int64_t n, int threads) {
   return static_cast<unsigned>((n + threads - 1) / threads);
 }
@@ -133,28 +184,33 @@ cudaError_t dequant_impl(int type, const void* blocks, int64_t n, void* out, cud
   constexpr int T = 256;
   // 16-byte vector stores; Q4_K reads its nibbles 8 bytes at a time.
   if (reinterpret_cast<uintptr_t>(out) & 15) return cudaErrorMisalignedAddress;
-  if (type == kTypeQ4_K && (reinterpret_cast<uintptr_t>(blocks) & 7)) return cudaErrorMisalignedAddress;
+  if (type == kTypeQ4_K && (reinterpret_cast<uintptr_t>(blocks) & 15)) return cudaErrorMisalignedAddress;
+  if (type == kTypeQ8_0 && (reinterpret_cast<uintptr_t>(blocks) & 1)) return cudaErrorMisalignedAddress;
+  const bool vec8 = n > 0 && n % 8 == 0 && (reinterpret_cast<uintptr_t>(blocks) & 15) == 0;
   switch (type) {
     case kTypeQ8_0: {
       if (n % 32) return cudaErrorInvalidValue;
       int64_t nb = n / 32;
-      if (nb) dequant_q8_0_kernel<kBf16><<<grid_for(nb * 4, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      if (nb) dequant_q8_0_kernel<kBf16><<<grid_cap(nb * 4, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
       break;
     }
     case kTypeQ4_K: {
       if (n % 256) return cudaErrorInvalidValue;
       int64_t nb = n / 256;
-      if (nb) dequant_q4_k_kernel<kBf16><<<grid_for(nb * 32, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
+      if (nb) dequant_q4_k_kernel<kBf16><<<grid_cap(nb * 32, T), T, 0, s>>>(static_cast<const uint8_t*>(blocks), nb, out);
       break;
     }
     case kTypeF16:
-      if (n) dequant_f16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
+      if (vec8) convert8_kernel<kTypeF16, kBf16><<<grid_for(n / 8, T), T, 0, s>>>(blocks, n / 8, out);
+      else if (n) dequant_f16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
       break;
     case kTypeBF16:
-      if (n) dequant_bf16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
+      if (vec8) convert8_kernel<kTypeBF16, kBf16><<<grid_for(n / 8, T), T, 0, s>>>(blocks, n / 8, out);
+      else if (n) dequant_bf16_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const uint16_t*>(blocks), n, out);
       break;
     case kTypeF32:
-      if (n) dequant_f32_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const float*>(blocks), n, out);
+      if (vec8) convert8_kernel<kTypeF32, kBf16><<<grid_for(n / 8, T), T, 0, s>>>(blocks, n / 8, out);
+      else if (n) dequant_f32_kernel<kBf16><<<grid_for(n, T), T, 0, s>>>(static_cast<const float*>(blocks), n, out);
       break;
     default:
       return cudaErrorNotSupported;

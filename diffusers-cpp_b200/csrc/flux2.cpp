@@ -276,6 +276,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   if (tot != cfg_.attention_head_dim) fail(DCPP_ERR_INVALID_ARG, "axes_dims_rope must sum to attention_head_dim");
   if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) == "1";
   if (const char* e = getenv("DCPP_TP_COMM")) tp_peer_ = std::string(e) != "nccl";
+  if (const char* e = getenv("DCPP_TP_PIECES")) tp_pieces_ = std::string(e) == "1" ? 1 : 2;
   build_registry();
 }
 
@@ -291,6 +292,7 @@ Flux2Transformer2DModel::~Flux2Transformer2DModel() {
   for (auto* v : vectors_)
     if (v->data) cudaFree(v->data);
   for (auto e : ev_) cudaEventDestroy(e);
+  if (side_) cudaStreamDestroy(side_);
 }
 
 void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks) {
@@ -714,12 +716,14 @@ void Flux2Transformer2DModel::free_plan() {
   for (void* p : allocs_) cudaFree(p);
   allocs_.clear();
   sym_.close(ctx_);
+  for (auto e : plan_events_) cudaEventDestroy(e);
+  plan_events_.clear();
   for (int j = 0; j < 8; ++j) {
     recv_peer_[j] = nullptr;
     a_peer_[j] = nullptr;
-    flags_peer_[j] = nullptr;
+    flags_peer_[0][j] = flags_peer_[1][j] = nullptr;
   }
-  epoch_ = nullptr;
+  epoch_[0] = epoch_[1] = nullptr;
   ops_fwd_.clear();
   step_ops_[0].clear();
   step_ops_[1].clear();
@@ -749,8 +753,17 @@ void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_tx
 void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
                                        const DevWeight* w0, const DevWeight* w1, std::vector<GemmGroup> groups,
                                        const EpilogueArgs& ep, int64_t N) {
+  add_gemm_pieces(tag, a, lda, K, w0, w1, {groups}, ep, N, nullptr);
+}
+
+void Flux2Transformer2DModel::add_gemm_pieces(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
+                                              const DevWeight* w0, const DevWeight* w1,
+                                              const std::vector<std::vector<GemmGroup>>& pieces, const EpilogueArgs& ep,
+                                              int64_t N, const std::function<void(int)>& before_piece) {
   if (w0->cols != K || (w1 && (w1->cols != K || w1->rows != w0->rows)) || w0->rows != N)
     fail(DCPP_ERR_STATE, "internal: GEMM shape mismatch for " + w0->name);
+  std::vector<GemmGroup> groups;
+  for (auto& pg : pieces) groups.insert(groups.end(), pg.begin(), pg.end());
   // Fused dequantisation when every weight of the launch is packed and of
   // one quantised type; otherwise expand to bf16 first (or use bf16 as is).
   const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
@@ -763,81 +776,107 @@ void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a
     for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
     auto st = std::make_shared<CUtensorMap>();
     cuda_check(make_tmap_bf16(st.get(), a, K, a_rows, lda, kGemmBM), "tensor map A");
-    GemmArgs args{};
-    args.N = static_cast<int32_t>(N);
-    args.K = static_cast<int32_t>(K);
-    if (groups.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
-    args.n_groups = static_cast<int32_t>(groups.size());
-    for (size_t i = 0; i < groups.size(); ++i) args.groups[i] = groups[i];
-    args.ep = ep;
-    args.err = ctx_.d_err;
-    args.qb[0].packed = w0->packed;
-    args.qb[1].packed = w1 ? w1->packed : w0->packed;
-    gemm_finalize_groups(args, tile_m);
     const int bsrc = w0->type == kTypeQ4_K ? kBSrcQ4_K : kBSrcQ8_0;
-    double flops = 0.0;
-    for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
     Ctx* c = &ctx_;
-    building_->push_back({[st, args, c, bsrc, pair](cudaStream_t s) {
-                            if (pair)
-                              cuda_check(launch_gemm_pair(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm (pair)");
-                            else
-                              cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
-                          },
-                          1, kOpGemm, flops, tag + " (fused dequant)"});
+    for (size_t p = 0; p < pieces.size(); ++p) {
+      if (before_piece) before_piece(static_cast<int>(p));
+      const auto& pg = pieces[p];
+      GemmArgs args{};
+      args.N = static_cast<int32_t>(N);
+      args.K = static_cast<int32_t>(K);
+      if (pg.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
+      args.n_groups = static_cast<int32_t>(pg.size());
+      for (size_t i = 0; i < pg.size(); ++i) args.groups[i] = pg[i];
+      args.ep = ep;
+      args.err = ctx_.d_err;
+      args.qb[0].packed = w0->packed;
+      args.qb[1].packed = w1 ? w1->packed : w0->packed;
+      gemm_finalize_groups(args, tile_m);
+      double flops = 0.0;
+      for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
+      building_->push_back({[st, args, c, bsrc, pair](cudaStream_t s) {
+                              if (pair)
+                                cuda_check(launch_gemm_pair(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm (pair)");
+                              else
+                                cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
+                            },
+                            1, kOpGemm, flops, tag + " (fused dequant)"});
+    }
     return;
   }
   if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
-  const uint16_t* b0 = w0->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w0->data) : wscratch_[0];
+  const bool expand0 = w0->type != kTypeBF16, expand1 = w1 && w1->type != kTypeBF16;
+  const int pair_idx = scratch_pair_;
+  if (expand0 || expand1) scratch_pair_ ^= 1;
+  uint16_t* const* sc = wscratch_[pair_idx];
+  const uint16_t* b0 = expand0 ? sc[0] : reinterpret_cast<const uint16_t*>(w0->data);
   const uint16_t* b1 = b0;
-  if (w1) b1 = w1->type == kTypeBF16 ? reinterpret_cast<const uint16_t*>(w1->data) : wscratch_[1];
+  if (w1) b1 = expand1 ? sc[1] : reinterpret_cast<const uint16_t*>(w1->data);
   int64_t a_rows = 0;
   for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
   auto st = std::make_shared<std::array<CUtensorMap, 3>>();
   cuda_check(make_tmap_bf16(&(*st)[0], a, K, a_rows, lda, kGemmBM), "tensor map A");
   cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, pair ? 128 : kGemmBN), "tensor map B0");
   cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, pair ? 128 : kGemmBN), "tensor map B1");
-  GemmArgs args{};
-  args.N = static_cast<int32_t>(N);
-  args.K = static_cast<int32_t>(K);
-  if (groups.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
-  args.n_groups = static_cast<int32_t>(groups.size());
-  for (size_t i = 0; i < groups.size(); ++i) args.groups[i] = groups[i];
-  args.ep = ep;
-  args.err = ctx_.d_err;
-  gemm_finalize_groups(args, tile_m);
   Ctx* c = &ctx_;
-  if (w0->type != kTypeBF16) {
-    const DevWeight* w = w0;
-    uint16_t* dst = wscratch_[0];
-    building_->push_back({[w, dst](cudaStream_t s) {
-                            cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
-                          },
-                          1, kOpDequant, 0.0, "dequant " + tag});
+  // Weight expansion on the side stream: it waits only for the last GEMM
+  // that read this scratch pair (two expanding GEMMs back), so it overlaps
+  // the GEMMs, attention and norms in between; the GEMM waits for it.
+  if (expand0 || expand1) {
+    add_wait(scratch_free_[pair_idx] ? scratch_free_[pair_idx] : plan_start_, 1);
+    for (int k = 0; k < 2; ++k) {
+      const DevWeight* w = k == 0 ? w0 : w1;
+      if (!(k == 0 ? expand0 : expand1)) continue;
+      uint16_t* dst = sc[k];
+      Op o{[w, dst](cudaStream_t s) {
+             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
+           },
+           1, kOpDequant, 0.0, "dequant " + tag};
+      o.stream = 1;
+      building_->push_back(o);
+    }
   }
-  if (w1 && w1->type != kTypeBF16) {
-    const DevWeight* w = w1;
-    uint16_t* dst = wscratch_[1];
-    building_->push_back({[w, dst](cudaStream_t s) {
-                            cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
-                          },
-                          1, kOpDequant, 0.0, "dequant " + tag});
+  cudaEvent_t ready = nullptr;
+  if (expand0 || expand1) {
+    ready = plan_event();
+    add_record(ready, 1);
   }
-  double flops = 0.0;
-  for (auto& g : groups) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
-  building_->push_back({[st, args, c, pair](cudaStream_t s) {
-                          if (pair)
-                            cuda_check(launch_gemm_pair((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
-                                       "gemm (pair)");
-                          else
-                            cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s), "gemm");
-                        },
-                        1, kOpGemm, flops, tag});
+  for (size_t p = 0; p < pieces.size(); ++p) {
+    if (before_piece) before_piece(static_cast<int>(p));
+    if (p == 0 && ready) add_wait(ready, 0);
+    const auto& pg = pieces[p];
+    GemmArgs args{};
+    args.N = static_cast<int32_t>(N);
+    args.K = static_cast<int32_t>(K);
+    if (pg.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
+    args.n_groups = static_cast<int32_t>(pg.size());
+    for (size_t i = 0; i < pg.size(); ++i) args.groups[i] = pg[i];
+    args.ep = ep;
+    args.err = ctx_.d_err;
+    gemm_finalize_groups(args, tile_m);
+    double flops = 0.0;
+    for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
+    building_->push_back({[st, args, c, pair](cudaStream_t s) {
+                            if (pair)
+                              cuda_check(launch_gemm_pair((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
+                                         "gemm (pair)");
+                            else
+                              cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
+                                         "gemm");
+                          },
+                          1, kOpGemm, flops, tag});
+  }
+  if (expand0 || expand1) {
+    scratch_free_[pair_idx] = plan_event();
+    add_record(scratch_free_[pair_idx], 0);
+  }
 }
 
-void Flux2Transformer2DModel::add_norm(const NormArgs& a) {
-  building_->push_back({[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm,
-                        0.0, a.n_slots ? "layernorm+allgather" : "layernorm"});
+void Flux2Transformer2DModel::add_norm(const NormArgs& a, int stream) {
+  Op o{[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm, 0.0,
+       a.n_slots ? "layernorm+allgather" : "layernorm"};
+  o.stream = stream;
+  building_->push_back(o);
 }
 
 void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y) {
@@ -860,15 +899,37 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
                         0, kOpAllreduce, 0.0, "nccl_allreduce"});
 }
 
-void Flux2Transformer2DModel::add_tp_barrier() {
+cudaEvent_t Flux2Transformer2DModel::plan_event() {
+  cudaEvent_t e;
+  cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+  plan_events_.push_back(e);
+  return e;
+}
+
+void Flux2Transformer2DModel::add_record(cudaEvent_t e, int stream) {
+  Op o{[e](cudaStream_t s) { cuda_check(cudaEventRecord(e, s), "event record"); }, 0, kOpOther, 0.0, "record"};
+  o.stream = stream;
+  o.timed = false;
+  building_->push_back(o);
+}
+
+void Flux2Transformer2DModel::add_wait(cudaEvent_t e, int stream) {
+  Op o{[e](cudaStream_t s) { cuda_check(cudaStreamWaitEvent(s, e, 0), "stream wait"); }, 0, kOpOther, 0.0, "wait"};
+  o.stream = stream;
+  o.timed = false;
+  building_->push_back(o);
+}
+
+void Flux2Transformer2DModel::add_tp_barrier(int set, int stream) {
   TpBarrierArgs a{};
-  for (int j = 0; j < nranks_; ++j) a.flags[j] = flags_peer_[j];
-  a.epoch = epoch_;
+  for (int j = 0; j < nranks_; ++j) a.flags[j] = flags_peer_[set][j];
+  a.epoch = epoch_[set];
   a.err = ctx_.d_err;
   a.rank = rank_;
   a.nranks = nranks_;
-  building_->push_back(
-      {[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce, 0.0, "tp_barrier"});
+  Op o{[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce, 0.0, "tp_barrier"};
+  o.stream = stream;
+  building_->push_back(o);
 }
 
 void Flux2Transformer2DModel::build_plan() {
@@ -894,20 +955,23 @@ void Flux2Transformer2DModel::build_plan() {
   h_ = static_cast<float*>(alloc(R * D * 4));
   part_ = tp && !peer ? static_cast<float*>(alloc(R * D * 4)) : nullptr;
   if (peer) {
-    // One IPC-mapped block per rank: a_ | recv slots | barrier flags.
-    chunk_ = (R + nranks_ - 1) / nranks_;
+    // One IPC-mapped block per rank: a_ | recv slots | barrier flags (2 sets).
+    piece_rows_ = (R + tp_pieces_ - 1) / tp_pieces_;
+    chunk_ = (piece_rows_ + nranks_ - 1) / nranks_;
     auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
     const size_t off_recv = up(R * D * 2);
-    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * chunk_ * D * 2);
-    sym_.open(ctx_, off_flags + 256);
+    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * tp_pieces_ * chunk_ * D * 2);
+    sym_.open(ctx_, off_flags + 512);
     for (int j = 0; j < nranks_; ++j) {
       a_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j]);
       recv_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j] + off_recv);
-      flags_peer_[j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags);
+      flags_peer_[0][j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags);
+      flags_peer_[1][j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags + 256);
     }
     a_ = a_peer_[rank_];
-    epoch_ = static_cast<uint32_t*>(alloc(256));
-    cuda_check(cudaMemsetAsync(epoch_, 0, 256, ctx_.stream), "clear epoch");
+    epoch_[0] = static_cast<uint32_t*>(alloc(256));
+    epoch_[1] = epoch_[0] + 32;
+    cuda_check(cudaMemsetAsync(epoch_[0], 0, 256, ctx_.stream), "clear epoch");
     // Every rank's flags are zero before any rank's first barrier.
     cuda_check(cudaStreamSynchronize(ctx_.stream), "peer buffers");
     float* one = static_cast<float*>(alloc(256));
@@ -962,8 +1026,15 @@ void Flux2Transformer2DModel::build_plan() {
   for (auto& blk : sgl_)
     for (const DevWeight* w : {&blk.qkv_mlp, &blk.out})
       if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
-  wscratch_[0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
-  wscratch_[1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
+  for (int pi = 0; pi < 2; ++pi) {
+    wscratch_[pi][0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
+    wscratch_[pi][1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
+  }
+  if (!side_) {
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    cuda_check(cudaStreamCreateWithPriority(&side_, cudaStreamNonBlocking, lo), "side stream");
+  }
 
   const int n_axes = static_cast<int>(cfg_.axes_dims_rope.size());
   std::array<int32_t, 8> axes{};
@@ -1021,6 +1092,11 @@ void Flux2Transformer2DModel::build_plan() {
 
   auto build_ops = [&](std::vector<Op>& ops, float* lat_in, float* lat_out, bool euler) {
     building_ = &ops;
+    scratch_pair_ = 0;
+    scratch_free_[0] = scratch_free_[1] = nullptr;
+    plan_start_ = plan_event();
+    add_record(plan_start_, 0);
+    add_wait(plan_start_, 1);  // the side stream joins the plan (and a capture) at its start
     // 1. timestep (and guidance) embedding, modulation vectors
     //    (Flux2Transformer2DModel.cpp:199-214).
     ops.push_back({[=](cudaStream_t s) {
@@ -1103,53 +1179,116 @@ void Flux2Transformer2DModel::build_plan() {
       if (peer) {
         for (int j = 0; j < nranks_; ++j) e.peer_bf16[j] = recv_peer_[j];
         e.chunk_rows = static_cast<int32_t>(chunk_);
+        e.piece_rows = static_cast<int32_t>(piece_rows_);
+        e.slot_rows = static_cast<int32_t>(tp_pieces_ * chunk_);
         e.peer_slot = rank_;
       }
       return e;
     };
-    // The exchange after a row-parallel GEMM and the LayerNorm that consumes
-    // it.  NCCL: all-reduce the partials, every rank normalises every row.
-    // Peer: barrier (partials landed), the owner of each row sums its slots
-    // into the residual and stores the normalised row to all ranks, barrier
-    // (activations landed).
+    // The exchange after a row-parallel GEMM, the LayerNorm that consumes it
+    // and the GEMM that consumes the LayerNorm.  NCCL: all-reduce the
+    // partials, every rank normalises every row.  Peer: a barrier (partials
+    // landed); per row piece, the owner of each row sums its slots into the
+    // residual and stores the normalised row into every rank's `a`; a
+    // barrier (rows landed) before the GEMM reads that piece.  With two
+    // pieces, piece 1's LayerNorm + all-gather runs on the side stream while
+    // the GEMM works on piece 0.
     bool pending = false;
     auto site = [&]() {
       if (!tp) return;
-      if (peer) add_tp_barrier();
+      if (peer) add_tp_barrier(0, 0);
       else add_allreduce(part_, R * D);
       pending = true;
     };
-    auto site_norm = [&](NormArgs n) {
-      if (pending && !peer) n.resid = part_;
-      if (pending && peer) {
-        const int64_t lo = rank_ * chunk_, hi = std::min<int64_t>(R, lo + chunk_);
-        int k = 0;
-        for (int i = 0; i < n.n_segments; ++i) {
-          NormSegment sg = n.seg[i];
-          const int64_t a0 = std::max<int64_t>(lo, sg.src_row0), a1 = std::min<int64_t>(hi, sg.src_row0 + sg.rows);
-          if (a1 <= a0) continue;
-          sg.dst_row0 += static_cast<int32_t>(a0 - sg.src_row0);
-          sg.src_row0 = static_cast<int32_t>(a0);
-          sg.rows = static_cast<int32_t>(a1 - a0);
-          n.seg[k++] = sg;
-        }
-        n.n_segments = k;
-        n.slots = recv_peer_[rank_];
-        n.n_slots = nranks_;
-        n.slot_stride = chunk_ * D;
-        n.slot_row0 = lo;
-        n.n_peer_out = 0;
-        for (int j = 0; j < nranks_; ++j)
-          if (j != rank_) n.y_peer[n.n_peer_out++] = a_peer_[j] + (n.y - a_);
+    auto piece_range = [&](int p) {
+      const int64_t lo = p * piece_rows_;
+      return std::array<int64_t, 2>{lo, std::min<int64_t>(R, lo + piece_rows_)};
+    };
+    auto own_range = [&](int p) {
+      const auto pr = piece_range(p);
+      const int64_t lo = std::min<int64_t>(pr[1], pr[0] + rank_ * chunk_);
+      return std::array<int64_t, 2>{lo, std::min<int64_t>(pr[1], lo + chunk_)};
+    };
+    auto peer_norm = [&](NormArgs n, int p) {
+      const auto own = own_range(p);
+      int k = 0;
+      for (int i = 0; i < n.n_segments; ++i) {
+        NormSegment sg = n.seg[i];
+        const int64_t a0 = std::max<int64_t>(own[0], sg.src_row0), a1 = std::min<int64_t>(own[1], sg.src_row0 + sg.rows);
+        if (a1 <= a0) continue;
+        sg.dst_row0 += static_cast<int32_t>(a0 - sg.src_row0);
+        sg.src_row0 = static_cast<int32_t>(a0);
+        sg.rows = static_cast<int32_t>(a1 - a0);
+        n.seg[k++] = sg;
       }
-      add_norm(n);
-      if (pending && peer) add_tp_barrier();
+      n.n_segments = k;
+      n.slots = recv_peer_[rank_];
+      n.n_slots = nranks_;
+      n.slot_stride = tp_pieces_ * chunk_ * D;
+      n.slot_row0 = own[0] - p * chunk_;  // slot row of source row r: p * chunk + (r - own[0])
+      n.n_peer_out = 0;
+      for (int j = 0; j < nranks_; ++j)
+        if (j != rank_) n.y_peer[n.n_peer_out++] = a_peer_[j] + (n.y - a_);
+      return n;
+    };
+    auto split_groups = [&](const std::vector<GemmGroup>& groups) {
+      std::vector<std::vector<GemmGroup>> out(tp_pieces_);
+      for (int p = 0; p < tp_pieces_; ++p) {
+        const auto pr = piece_range(p);
+        for (GemmGroup g : groups) {
+          const int64_t a0 = std::max<int64_t>(pr[0], g.row0), a1 = std::min<int64_t>(pr[1], g.row0 + g.rows);
+          if (a1 <= a0) continue;
+          const int32_t d = static_cast<int32_t>(a0 - g.row0);
+          g.row0 += d;
+          g.orow0 += d;
+          g.tok0 += d;
+          g.rows = static_cast<int32_t>(a1 - a0);
+          out[p].push_back(g);
+        }
+      }
+      return out;
+    };
+    using Emit = std::function<void(const std::vector<std::vector<GemmGroup>>&, const std::function<void(int)>&)>;
+    // joint_rows: the LayerNorm writes row r of `a` from row r of h (block
+    // norms); norm_out drops the text rows, so its GEMM is not split.
+    auto norm_gemm = [&](NormArgs n, bool joint_rows, const std::vector<GemmGroup>& groups, const Emit& emit) {
+      if (!(pending && peer)) {
+        if (pending) n.resid = part_;
+        add_norm(n);
+        pending = false;
+        emit({groups}, nullptr);
+        return;
+      }
       pending = false;
+      if (!joint_rows || tp_pieces_ == 1) {
+        for (int p = 0; p < tp_pieces_; ++p) {
+          NormArgs q = peer_norm(n, p);
+          if (q.n_segments) add_norm(q);
+        }
+        add_tp_barrier(0, 0);
+        emit({groups}, nullptr);
+        return;
+      }
+      cudaEvent_t ln0 = plan_event(), done1 = plan_event();
+      emit(split_groups(groups), [&, n, ln0, done1](int p) {
+        if (p == 0) {
+          NormArgs q0 = peer_norm(n, 0);
+          if (q0.n_segments) add_norm(q0);
+          add_record(ln0, 0);
+          add_tp_barrier(0, 0);
+          add_wait(ln0, 1);
+          NormArgs q1 = peer_norm(n, 1);
+          if (q1.n_segments) add_norm(q1, 1);
+          add_tp_barrier(1, 1);
+          add_record(done1, 1);
+        } else {
+          add_wait(done1, 0);
+        }
+      });
     };
     const float* mods_dbl[2] = {mod_txt_v_, mod_img_v_};
     // 4. double-stream blocks (Flux2TransformerBlock.hpp:45-117).
     for (auto& blk : dbl_) {
-      site_norm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, nullptr));
       EpilogueArgs e{};
       e.mode = kEpiQkvMlp;
       e.qkv_cols = static_cast<int32_t>(3 * Dl);
@@ -1168,15 +1307,20 @@ void Flux2Transformer2DModel::build_plan() {
       e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
-      add_gemm("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], stream_groups(true), e, 3 * Dl);
+      norm_gemm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, nullptr), true, stream_groups(true),
+                [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
+                  add_gemm_pieces("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], pcs, e, 3 * Dl, hook);
+                });
       attn_op();
       add_gemm("attn_out", cat_, ldc, Dl, &blk.out[0], &blk.out[1], stream_groups(true),
                out_epi(mod_txt_v_ + 2 * D, mod_img_v_ + 2 * D, 6 * D), D);
       site();
-      site_norm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, nullptr));
       EpilogueArgs f = e;
       f.qkv_cols = 0;
-      add_gemm("ff_in", a_, D, D, &blk.ff_in[0], &blk.ff_in[1], stream_groups(true), f, 2 * Fl);
+      norm_gemm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, nullptr), true, stream_groups(true),
+                [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
+                  add_gemm_pieces("ff_in", a_, D, D, &blk.ff_in[0], &blk.ff_in[1], pcs, f, 2 * Fl, hook);
+                });
       add_gemm("ff_out", cat_ + Dl, ldc, Fl, &blk.ff_out[0], &blk.ff_out[1], stream_groups(true),
                out_epi(mod_txt_v_ + 5 * D, mod_img_v_ + 5 * D, 6 * D), D);
       site();
@@ -1184,7 +1328,6 @@ void Flux2Transformer2DModel::build_plan() {
     // 5. single-stream blocks on the joint stream (Flux2SingleTransformerBlock.hpp:36-72).
     const float* mods_s[2] = {mod_s_v_, mod_s_v_};
     for (auto& blk : sgl_) {
-      site_norm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, nullptr));
       EpilogueArgs e{};
       e.mode = kEpiQkvMlp;
       e.qkv_cols = static_cast<int32_t>(3 * Dl);
@@ -1201,7 +1344,10 @@ void Flux2Transformer2DModel::build_plan() {
       e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
-      add_gemm("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, stream_groups(false), e, 3 * Dl + 2 * Fl);
+      norm_gemm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, nullptr), true, stream_groups(false),
+                [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
+                  add_gemm_pieces("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, pcs, e, 3 * Dl + 2 * Fl, hook);
+                });
       attn_op();
       add_gemm("out", cat_, ldc, Dl + Fl, &blk.out, nullptr, stream_groups(false),
                out_epi(mod_s_v_ + 2 * D, mod_s_v_ + 2 * D, 3 * D), D);
@@ -1209,7 +1355,6 @@ void Flux2Transformer2DModel::build_plan() {
     }
     // 6. drop text tokens, norm_out (scale first, then shift; AdaLayerNormContinuous.inl:26-43), proj_out.
     const float* mods_o[2] = {mod_o_v_, mod_o_v_};
-    site_norm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, nullptr));
     {
       std::vector<GemmGroup> g;
       for (int64_t b = 0; b < B; ++b) {
@@ -1230,8 +1375,16 @@ void Flux2Transformer2DModel::build_plan() {
         e.mode = kEpiF32;
         e.out_f32 = lat_out;
       }
-      add_gemm("proj_out", a_, D, D, &proj_out_, nullptr, g, e, out_ch);
+      norm_gemm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, nullptr), false, g,
+                [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
+                  add_gemm_pieces("proj_out", a_, D, D, &proj_out_, nullptr, pcs, e, out_ch, hook);
+                });
     }
+    // Join the side stream back into the main stream (a captured graph must
+    // end on its origin stream).
+    cudaEvent_t side_done = plan_event();
+    add_record(side_done, 1);
+    add_wait(side_done, 0);
     building_ = nullptr;
   };
   guidance_given_ = cfg_.guidance_embeds;
@@ -1255,7 +1408,7 @@ void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* gra
   last_ops_ = &ops;
   auto issue = [&]() {
     if (!profiling_) {
-      for (auto& o : ops) o.fn(s);
+      for (auto& o : ops) o.fn(o.stream ? side_ : s);
       return;
     }
     if (ev_.size() < 2 * ops.size()) {
@@ -1271,9 +1424,14 @@ void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* gra
     cuda_check(cudaStreamIsCapturing(s, &cs), "cudaStreamIsCapturing");
     const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
     for (size_t i = 0; i < ops.size(); ++i) {
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], s, flags), "event record");
-      ops[i].fn(s);
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], s, flags), "event record");
+      cudaStream_t os = ops[i].stream ? side_ : s;
+      if (!ops[i].timed) {  // stream record / wait
+        ops[i].fn(os);
+        continue;
+      }
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], os, flags), "event record");
+      ops[i].fn(os);
+      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], os, flags), "event record");
     }
   };
   if (!use_graph_) {
@@ -1381,7 +1539,7 @@ void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64
   int64_t n = 0;
   for (size_t i = 0; i < last_ops_->size(); ++i) {
     const Op& o = (*last_ops_)[i];
-    if (o.kind != kind) continue;
+    if (o.kind != kind || !o.timed) continue;
     float e = 0.f;
     cuda_check(cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]), "cudaEventElapsedTime");
     t += e;
@@ -1397,12 +1555,13 @@ void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64
   if (path && kind == kOpGemm) {
     FILE* f = fopen(path, "w");
     if (f) {
-      fprintf(f, "index,tag,kind,ms,flops\n");
+      fprintf(f, "index,tag,kind,ms,flops,stream\n");
       for (size_t i = 0; i < last_ops_->size(); ++i) {
         const Op& o = (*last_ops_)[i];
+        if (!o.timed) continue;
         float e = 0.f;
         cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]);
-        fprintf(f, "%zu,%s,%d,%.5f,%.6g\n", i, o.tag.c_str(), o.kind, e, o.flops);
+        fprintf(f, "%zu,%s,%d,%.5f,%.6g,%d\n", i, o.tag.c_str(), o.kind, e, o.flops, o.stream);
       }
       fclose(f);
     }

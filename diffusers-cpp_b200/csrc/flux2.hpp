@@ -6,8 +6,10 @@
 //   FlowMatchEulerDiscreteScheduler::schedule / integrate (FlowMatchEulerDiscreteScheduler.cpp:68-222)
 // Parameters bind by their GGUF names (module paths, ModulePath.hpp) as the
 // GGUFLoaderVisitor does, including the fused tensors it byte-slices.
-// Execution is eager CUDA on one stream, optionally replayed from a CUDA
-// graph; every kernel comes from this library.
+// Execution is a fixed list of launches on the context's stream plus one
+// side stream (weight expansion ahead of its GEMM), joined by events and
+// optionally replayed from a CUDA graph; every kernel comes from this
+// library.
 #pragma once
 
 #include <cuda.h>
@@ -137,6 +139,8 @@ class Flux2Transformer2DModel {
     int kind = kOpOther;   // ProfileKind
     double flops = 0.0;    // algorithmic FLOPs of the op
     std::string tag;       // what the op is (profile dumps)
+    int stream = 0;        // 0: the context's stream, 1: the model's side stream
+    bool timed = true;     // false for stream records / waits (not profiled)
   };
 
   void build_registry();
@@ -156,10 +160,19 @@ class Flux2Transformer2DModel {
   // Plan helpers.
   void add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K, const DevWeight* w0,
                 const DevWeight* w1, std::vector<GemmGroup> groups, const EpilogueArgs& ep, int64_t N);
-  void add_norm(const NormArgs& a);
+  // The same GEMM launched once per row piece (weights expanded once);
+  // before_piece(p) emits what must precede piece p.
+  void add_gemm_pieces(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K, const DevWeight* w0,
+                       const DevWeight* w1, const std::vector<std::vector<GemmGroup>>& pieces, const EpilogueArgs& ep,
+                       int64_t N, const std::function<void(int)>& before_piece);
+  void add_norm(const NormArgs& a, int stream = 0);
   void add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y);
   void add_allreduce(float* buf, int64_t count);
-  void add_tp_barrier();
+  void add_tp_barrier(int set, int stream);
+  // Cross-stream dependencies inside a plan (graph edges when captured).
+  cudaEvent_t plan_event();
+  void add_record(cudaEvent_t e, int stream);
+  void add_wait(cudaEvent_t e, int stream);
 
   Ctx& ctx_;
   Flux2Config cfg_;
@@ -188,7 +201,16 @@ class Flux2Transformer2DModel {
   float *tproj_ = nullptr, *th_ = nullptr, *temb_ = nullptr, *gproj_ = nullptr, *gh_ = nullptr, *gemb_ = nullptr;
   float *mod_img_v_ = nullptr, *mod_txt_v_ = nullptr, *mod_s_v_ = nullptr, *mod_o_v_ = nullptr;
   uint16_t *a_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *cat_ = nullptr, *xb_ = nullptr,
-           *eb_ = nullptr, *wscratch_[2] = {nullptr, nullptr};
+           *eb_ = nullptr;
+  // bf16 expansion of quantised GEMM weights: two pairs (txt / img stream
+  // weight of one launch), used alternately, so that the expansion of the
+  // next projection runs on the side stream while the current GEMM computes.
+  uint16_t* wscratch_[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+  int scratch_pair_ = 0;
+  cudaEvent_t scratch_free_[2] = {nullptr, nullptr};  // last GEMM that read the pair (null: none yet)
+  cudaEvent_t plan_start_ = nullptr;                   // recorded on the main stream first in a plan
+  cudaStream_t side_ = nullptr;
+  std::vector<cudaEvent_t> plan_events_;
   int32_t* ids_dev_ = nullptr;
   float2* rope_ = nullptr;
   // Tensor parallelism over peer memory (the default exchange): the
@@ -197,13 +219,17 @@ class Flux2Transformer2DModel {
   // GPU), the owner's LayerNorm sums the slots into its residual rows and
   // stores the normalised bf16 rows into every rank's activation buffer (a_).
   // DCPP_TP_COMM=nccl selects ncclAllReduce of the partials instead.
+  // The token rows are cut into tp_pieces_ pieces (default 2), each split
+  // evenly over the ranks, so that the LayerNorm + all-gather of piece 1
+  // (side stream) overlaps the column-parallel GEMM of piece 0.
   bool tp_peer_ = true;
+  int tp_pieces_ = 2;
   PeerBuffer sym_;
-  int64_t chunk_ = 0;
+  int64_t piece_rows_ = 0, chunk_ = 0;
   uint16_t* recv_peer_[8] = {};  // bf16 receive slots
   uint16_t* a_peer_[8] = {};
-  uint32_t* flags_peer_[8] = {};
-  uint32_t* epoch_ = nullptr;
+  uint32_t* flags_peer_[2][8] = {};  // barrier flag sets: 0 main stream, 1 side stream
+  uint32_t* epoch_[2] = {};
   float* host_scalars_ = nullptr;  // pinned: t[B], dt
   int cur_ = 0;                    // latent ping-pong index
   std::vector<Op> ops_fwd_;        // forward (noise prediction) plan

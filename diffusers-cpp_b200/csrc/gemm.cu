@@ -192,10 +192,12 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     const int lane = row_in_tile & 31;
     uintptr_t rdst = 0;
     if (row_ok) {
-      const int64_t owner = row / e.chunk_rows;
-      rdst = reinterpret_cast<uintptr_t>(
-          e.peer_bf16[owner] +
-          (static_cast<int64_t>(e.peer_slot) * e.chunk_rows + (row - owner * e.chunk_rows)) * e.ld_out);
+      const int64_t pc = row / e.piece_rows;
+      const int64_t rp = row - pc * e.piece_rows;
+      const int64_t owner = rp / e.chunk_rows;
+      const int64_t l = pc * e.chunk_rows + (rp - owner * e.chunk_rows);
+      rdst = reinterpret_cast<uintptr_t>(e.peer_bf16[owner] +
+                                         (static_cast<int64_t>(e.peer_slot) * e.slot_rows + l) * e.ld_out);
     }
     const int sub = lane >> 3, q = lane & 7;
     uint8_t* srow = reinterpret_cast<uint8_t*>(stage) + lane * kEpiStageRowBytes;

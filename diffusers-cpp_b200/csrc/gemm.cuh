@@ -69,12 +69,17 @@ struct EpilogueArgs {
   int64_t vt_stride;         // keys per V^T row (S rounded up to 64)
   uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
   int64_t ld_mlp;
-  // kEpiGatePeer: output row r belongs to rank o = r / chunk_rows, whose
-  // receive buffer (peer_bf16[o], mapped from that GPU) holds one bf16 slot
-  // of chunk_rows rows per source rank; this rank writes slot peer_slot:
-  //   peer_bf16[o] + (peer_slot * chunk_rows + r - o * chunk_rows) * ld_out.
+  // kEpiGatePeer: the rows are cut into pieces of piece_rows rows, each
+  // piece into chunks of chunk_rows rows owned by ranks 0, 1, ...: row r of
+  // piece p = r / piece_rows belongs to rank o = (r - p piece_rows) / chunk_rows
+  // and is row l = p chunk_rows + (r - p piece_rows - o chunk_rows) of that
+  // rank's receive slots (peer_bf16[o], mapped from its GPU; slot_rows rows
+  // per source rank).  This rank writes slot peer_slot:
+  //   peer_bf16[o] + (peer_slot * slot_rows + l) * ld_out.
   uint16_t* peer_bf16[8];
   int32_t chunk_rows;
+  int32_t piece_rows;
+  int32_t slot_rows;
   int32_t peer_slot;
 };
 

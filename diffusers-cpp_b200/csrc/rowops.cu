@@ -370,6 +370,164 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t* __restrict__ W
   }
 }
 
+// GEMV for K % 256 == 0: one thread per 256-weight unit of a row (a Q4_K
+// super-block, eight Q8_0 blocks or 256 bf16 / f16 weights), read with
+// independent 16-byte loads (9 / 17 / 32 per unit), so a warp keeps 4.5-16 KB
+// of weights in flight.  A CTA covers whole rows (kGemvUnitsPerCta / U rows);
+// each thread's partial dot products go to shared memory and one thread per
+// row adds its U partials in order (deterministic, no atomics).  x sits in
+// shared memory with 4 floats of padding per 256, so the 8 lanes of a
+// quarter-warp reading the same offset of 8 consecutive units hit distinct
+// banks.
+constexpr int kGemvUnitsPerCta = 256;
+constexpr int kGemvUnitStride = 260;  // floats per 256-weight unit of x in smem
+
+template <int kType>
+__global__ void __launch_bounds__(256) gemv_unit_kernel(const uint8_t* __restrict__ W, int64_t N, int64_t K,
+                                                        const float* __restrict__ x, int B, int act_in, int act_out,
+                                                        float* __restrict__ y) {
+  extern __shared__ float4 sm4[];
+  float* xs = reinterpret_cast<float*>(sm4);            // [B][U * 260]
+  const int U = static_cast<int>(K >> 8);
+  float* part = xs + static_cast<int64_t>(B) * U * kGemvUnitStride;  // [256][B]
+  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(B) * K; i += blockDim.x) {
+    const int b = static_cast<int>(i / K);
+    const int k = static_cast<int>(i - static_cast<int64_t>(b) * K);
+    const float v = x[i];
+    xs[static_cast<int64_t>(b) * U * kGemvUnitStride + (k >> 8) * kGemvUnitStride + (k & 255)] = act_in ? silu_f(v) : v;
+  }
+  __syncthreads();
+  const int rows_per_cta = kGemvUnitsPerCta / U;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+  const int t = threadIdx.x;
+  const int r_local = t / U;
+  const int u = t - r_local * U;
+  const int64_t row = row0 + r_local;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (r_local < rows_per_cta && row < N) {
+    const float* xu = xs + u * kGemvUnitStride;
+    const int64_t xb = static_cast<int64_t>(U) * kGemvUnitStride;
+    if (kType == kTypeQ4_K) {
+      const uint4* p = reinterpret_cast<const uint4*>(W + (row * U + u) * 144);
+      uint4 w[9];
+#pragma unroll
+      for (int i = 0; i < 9; ++i) w[i] = __ldg(p + i);
+      const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(w[0].x & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half(static_cast<uint16_t>(w[0].x >> 16)));
+      uint8_t sb[12];
+      const uint32_t hw[3] = {w[0].y, w[0].z, w[0].w};
+#pragma unroll
+      for (int i = 0; i < 12; ++i) sb[i] = static_cast<uint8_t>(hw[i >> 2] >> (8 * (i & 3)));
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {  // 32-byte nibble group g: sub-blocks 2g (low), 2g+1 (high)
+        int sc0, m0, sc1, m1;
+        q4k_scale_min(2 * g, sb, sc0, m0);
+        q4k_scale_min(2 * g + 1, sb, sc1, m1);
+        const float ds0 = __fmul_rn(d, static_cast<float>(sc0)), dm0 = __fmul_rn(dmin, static_cast<float>(m0));
+        const float ds1 = __fmul_rn(d, static_cast<float>(sc1)), dm1 = __fmul_rn(dmin, static_cast<float>(m1));
+        const uint32_t q[8] = {w[1 + 2 * g].x, w[1 + 2 * g].y, w[1 + 2 * g].z, w[1 + 2 * g].w,
+                               w[2 + 2 * g].x, w[2 + 2 * g].y, w[2 + 2 * g].z, w[2 + 2 * g].w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float lo[4], hi[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            lo[i] = __fsub_rn(__fmul_rn(ds0, static_cast<float>((q[c] >> (8 * i)) & 0xF)), dm0);
+            hi[i] = __fsub_rn(__fmul_rn(ds1, static_cast<float>((q[c] >> (8 * i + 4)) & 0xF)), dm1);
+          }
+          #pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            if (b >= B) break;
+            const float4 x0 = *reinterpret_cast<const float4*>(xu + b * xb + (2 * g) * 32 + 4 * c);
+            const float4 x1 = *reinterpret_cast<const float4*>(xu + b * xb + (2 * g + 1) * 32 + 4 * c);
+            float a = acc[b];
+            a = fmaf(lo[0], x0.x, a); a = fmaf(lo[1], x0.y, a); a = fmaf(lo[2], x0.z, a); a = fmaf(lo[3], x0.w, a);
+            a = fmaf(hi[0], x1.x, a); a = fmaf(hi[1], x1.y, a); a = fmaf(hi[2], x1.z, a); a = fmaf(hi[3], x1.w, a);
+            acc[b] = a;
+          }
+        }
+      }
+    } else if (kType == kTypeQ8_0) {
+      // Eight 34-byte blocks = 272 bytes = 17 aligned uint4 (rows are K/32*34
+      // bytes, a multiple of 272 since K % 256 == 0).
+      const uint4* p = reinterpret_cast<const uint4*>(W + (row * U + u) * 272);
+      uint32_t w[68];
+#pragma unroll
+      for (int i = 0; i < 17; ++i) {
+        const uint4 v = __ldg(p + i);
+        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+      }
+      auto byte_at = [&](int off) -> uint32_t { return (w[off >> 2] >> (8 * (off & 3))) & 0xFF; };
+#pragma unroll
+      for (int blk = 0; blk < 8; ++blk) {
+        const int o = blk * 34;
+        const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(byte_at(o) | (byte_at(o + 1) << 8))));
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float wv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            wv[i] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(byte_at(o + 2 + 4 * c + i))));
+          #pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            if (b >= B) break;
+            const float4 xv = *reinterpret_cast<const float4*>(xu + b * xb + blk * 32 + 4 * c);
+            float a = acc[b];
+            a = fmaf(wv[0], xv.x, a); a = fmaf(wv[1], xv.y, a); a = fmaf(wv[2], xv.z, a); a = fmaf(wv[3], xv.w, a);
+            acc[b] = a;
+          }
+        }
+      }
+    } else {  // BF16 / F16: 256 weights = 32 uint4, in 4 batches of 8
+      const uint4* p = reinterpret_cast<const uint4*>(W + (row * U + u) * 512);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        uint4 w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = __ldg(p + 8 * h + i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t wv[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+          float wf[8];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (kType == kTypeBF16) {
+              wf[2 * k] = __uint_as_float(wv[k] << 16);
+              wf[2 * k + 1] = __uint_as_float(wv[k] & 0xFFFF0000u);
+            } else {
+              wf[2 * k] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[k] & 0xFFFF)));
+              wf[2 * k + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(wv[k] >> 16)));
+            }
+          }
+          const int e = (8 * h + i) * 8;
+          #pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            if (b >= B) break;
+            const float4 xa = *reinterpret_cast<const float4*>(xu + b * xb + e);
+            const float4 xc = *reinterpret_cast<const float4*>(xu + b * xb + e + 4);
+            float a = acc[b];
+            a = fmaf(wf[0], xa.x, a); a = fmaf(wf[1], xa.y, a); a = fmaf(wf[2], xa.z, a); a = fmaf(wf[3], xa.w, a);
+            a = fmaf(wf[4], xc.x, a); a = fmaf(wf[5], xc.y, a); a = fmaf(wf[6], xc.z, a); a = fmaf(wf[7], xc.w, a);
+            acc[b] = a;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < 4; ++b) part[t * 4 + b] = acc[b];
+  __syncthreads();
+  if (t < rows_per_cta && row0 + t < N) {
+    #pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            if (b >= B) break;
+      float v = 0.f;
+      for (int i = 0; i < U; ++i) v += part[(t * U + i) * 4 + b];
+      y[b * N + row0 + t] = act_out ? silu_f(v) : v;
+    }
+  }
+}
+
 __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
   int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -453,6 +611,33 @@ cudaError_t launch_timestep_proj(const float* t, int B, int channels, float mult
 cudaError_t launch_gemv(int wtype, const void* W, int64_t N, int64_t K, const float* x, int B, int act_in,
                         int act_out, float* y, cudaStream_t s) {
   if (B < 1 || B > 4) return cudaErrorInvalidValue;
+  const uint8_t* wb = static_cast<const uint8_t*>(W);
+  if (K % 256 == 0 && K / 256 <= kGemvUnitsPerCta && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
+      (wtype == kTypeQ4_K || wtype == kTypeQ8_0 || wtype == kTypeBF16 || wtype == kTypeF16)) {
+    const int U = static_cast<int>(K / 256);
+    const size_t usmem = (static_cast<size_t>(B) * U * kGemvUnitStride + kGemvUnitsPerCta * 4) * sizeof(float);
+    if (usmem <= 200 * 1024) {
+      const int rows_per_cta = kGemvUnitsPerCta / U;
+      const unsigned ugrid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
+#define DCPP_GEMV_U(T)                                                                                   \
+  do {                                                                                                   \
+    static bool attr = false;                                                                            \
+    if (!attr) {                                                                                         \
+      cudaFuncSetAttribute(gemv_unit_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+      attr = true;                                                                                       \
+    }                                                                                                    \
+    gemv_unit_kernel<T><<<ugrid, 256, usmem, s>>>(wb, N, K, x, B, act_in, act_out, y);                   \
+  } while (0)
+      switch (wtype) {
+        case kTypeQ4_K: DCPP_GEMV_U(kTypeQ4_K); break;
+        case kTypeQ8_0: DCPP_GEMV_U(kTypeQ8_0); break;
+        case kTypeBF16: DCPP_GEMV_U(kTypeBF16); break;
+        default: DCPP_GEMV_U(kTypeF16); break;
+      }
+#undef DCPP_GEMV_U
+      return cudaGetLastError();
+    }
+  }
   const size_t smem = static_cast<size_t>(B) * K * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>((N + kGemvRowsPerCta - 1) / kGemvRowsPerCta);

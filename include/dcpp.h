@@ -109,7 +109,9 @@ dcpp_status dcpp_inject_fault(dcpp_ctx* ctx, const char* name, int nth);
 /* Dequantise `n` weights of ggml type `type` (Q8_0, Q4_K, F16, BF16, F32)
  * to f32, bit-identical to gguf-py 0.19.0 dequantize (quants.py:396-401 for
  * Q8_0, :504-523 for Q4_K), which the reference's tests declare to be what
- * ggml computes (test/utils/__init__.py:198-228).  n % block size == 0. */
+ * ggml computes (test/utils/__init__.py:198-228).  n % block size == 0.
+ * Alignment: d_out 16 bytes; Q4_K blocks 16 bytes (144-byte blocks keep
+ * every row of a cudaMalloc'd tensor aligned); Q8_0 blocks 2 bytes. */
 dcpp_status dcpp_dequant(dcpp_ctx* ctx, int type, const void* d_blocks, int64_t n, float* d_out);
 
 /* Same values rounded to bf16 (round-to-nearest-even); the GEMM operand. */

@@ -31,10 +31,12 @@ def test_dequant_golden_bit_exact(ctx, kind):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("gtype", [fo.GGML_Q8_0, fo.GGML_Q4_K, fo.GGML_F16, fo.GGML_BF16, fo.GGML_F32])
-def test_dequant_random_bit_exact_vs_oracle(ctx, gtype):
+@pytest.mark.parametrize("gtype,n", [(fo.GGML_Q8_0, 256 * 37), (fo.GGML_Q4_K, 256 * 37), (fo.GGML_F16, 256 * 37),
+                                     (fo.GGML_BF16, 256 * 37), (fo.GGML_F32, 256 * 37), (fo.GGML_F16, 1001),
+                                     (fo.GGML_BF16, 999), (fo.GGML_F32, 13)])
+def test_dequant_random_bit_exact_vs_oracle(ctx, gtype, n):
+    """Block formats, and the element formats on both the 8-wide and the ragged path."""
     g = torch.Generator().manual_seed(gtype)
-    n = 256 * 37
     x = torch.randn(n, generator=g) * 0.1
     blocks = quant.quantize(x.reshape(1, -1), gtype).reshape(-1).numpy()
     ref = fo.dequant(gtype, blocks, n)

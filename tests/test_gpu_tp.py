@@ -28,11 +28,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def run_ranks(tmp_path, heads, wtype, comm, n=2, timeout=600):
+def run_ranks(tmp_path, heads, wtype, comm, pieces=2, n=2, timeout=600):
     out = tmp_path / "tp.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(HERE, "tp_gpu_worker.py"), str(out), str(heads), str(wtype), comm]
+           os.path.join(HERE, "tp_gpu_worker.py"), str(out), str(heads), str(wtype), comm, str(pieces)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     p = subprocess.Popen(cmd, env=env, start_new_session=True, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
     try:
@@ -46,13 +46,16 @@ def run_ranks(tmp_path, heads, wtype, comm, n=2, timeout=600):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("heads,wtype,comm", [(4, fo.GGML_Q8_0, "peer"), (6, fo.GGML_Q4_K, "peer"),
-                                              (4, fo.GGML_Q8_0, "nccl"), (6, fo.GGML_Q4_K, "nccl")],
-                         ids=["q8_0_peer", "q4_k_bf16_shards_peer", "q8_0_nccl", "q4_k_bf16_shards_nccl"])
-def test_tp2_matches_oracle(tmp_path, heads, wtype, comm):
+@pytest.mark.parametrize("heads,wtype,comm,pieces", [(4, fo.GGML_Q8_0, "peer", 2), (6, fo.GGML_Q4_K, "peer", 2),
+                                                     (4, fo.GGML_Q8_0, "peer", 1), (4, fo.GGML_Q8_0, "nccl", 1),
+                                                     (6, fo.GGML_Q4_K, "nccl", 1)],
+                         ids=["q8_0_peer", "q4_k_bf16_shards_peer", "q8_0_peer_one_piece", "q8_0_nccl",
+                              "q4_k_bf16_shards_nccl"])
+def test_tp2_matches_oracle(tmp_path, heads, wtype, comm, pieces):
     """peer: partials stored into the owning GPU's memory by the GEMM epilogue,
-    LayerNorm + all-gather by the owner; nccl: ncclAllReduce of the partials."""
-    r = run_ranks(tmp_path, heads, wtype, comm)
+    LayerNorm + all-gather by the owner, in one or two row pieces (the second
+    overlapping the first piece's GEMM); nccl: ncclAllReduce of the partials."""
+    r = run_ranks(tmp_path, heads, wtype, comm, pieces)
     assert r["ranks_identical"], r
     assert r["replay_identical"], r
     assert r["forward_rel"] < V_TOL, r

@@ -34,6 +34,8 @@ def rel(a, b):
 def main():
     out_path, heads, wtype, comm = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
     os.environ["DCPP_TP_COMM"] = comm  # "peer" (default) or "nccl"; read when a model is created
+    if len(sys.argv) > 5:
+        os.environ["DCPP_TP_PIECES"] = sys.argv[5]  # row pieces of the peer exchange (1 or 2)
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
