@@ -219,11 +219,13 @@ class Flux2Transformer2DModel {
   // GPU), the owner's LayerNorm sums the slots into its residual rows and
   // stores the normalised bf16 rows into every rank's activation buffer (a_).
   // DCPP_TP_COMM=nccl selects ncclAllReduce of the partials instead.
-  // The token rows are cut into tp_pieces_ pieces (default 2), each split
-  // evenly over the ranks, so that the LayerNorm + all-gather of piece 1
-  // (side stream) overlaps the column-parallel GEMM of piece 0.
+  // The token rows are cut into tp_pieces_ pieces (1 or 2), each split
+  // evenly over the ranks; with two, the LayerNorm + all-gather of piece 1
+  // (side stream) overlaps the column-parallel GEMM of piece 0.  Chosen per
+  // plan from the exchange size unless DCPP_TP_PIECES sets it.
   bool tp_peer_ = true;
-  int tp_pieces_ = 2;
+  int tp_pieces_ = 1;
+  int tp_pieces_env_ = 0;
   PeerBuffer sym_;
   int64_t piece_rows_ = 0, chunk_ = 0;
   uint16_t* recv_peer_[8] = {};  // bf16 receive slots
