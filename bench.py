@@ -269,6 +269,8 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     assert stream.cuda_stream != 0
     ctx.set_stream(stream.cuda_stream)
+    if args.attn_kernel:
+        ctx.set_attention_kernel(args.attn_kernel)
     if world > 1:
         uid = [dcpp_b200.Context.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -448,6 +450,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
+    ap.add_argument("--attn-kernel", type=int, default=0, help="0 auto, 1 one query tile per CTA, 2 two tiles")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

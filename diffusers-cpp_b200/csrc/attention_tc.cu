@@ -72,6 +72,81 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed f32x2 arithmetic (two lanes of a 64-bit register per instruction).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x of a pair on the FMA / integer pipes, for a share of the softmax exponentials
+// (the MUFU unit alone would limit the softmax: one ex2 per 512 tensor
+// FLOPs is exactly its throughput).  Range reduction x = n + f with
+// n = round(x) (the 1.5 * 2^23 rounding trick), f in [-1/2, 1/2]; 2^f by a
+// degree-3 polynomial fitted here to minimise the maximum relative error on
+// that interval (7.5e-5, far below the bf16 rounding P gets next); 2^n is
+// added to the exponent field.  x is clamped to -126 (masked keys give
+// ~2^-126 instead of 0, which vanishes in bf16 sums of O(1) terms).
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x) {
+  x = f2(fmaxf(f2lo(x), -126.0f), fmaxf(f2hi(x), -126.0f));
+  const uint64_t magic = f2(12582912.0f, 12582912.0f), neg_magic = f2(-12582912.0f, -12582912.0f);
+  const uint64_t t = add2(x, magic);
+  const uint64_t n = add2(t, neg_magic);
+  const uint64_t f = fma2(n, f2(-1.0f, -1.0f), x);
+  uint64_t p = fma2(f2(0.0551716648f, 0.0551716648f), f, f2(0.24261114f, 0.24261114f));
+  p = fma2(p, f, f2(0.693260968f, 0.693260968f));
+  p = fma2(p, f, f2(0.999928057f, 0.999928057f));
+  const uint32_t lo = static_cast<uint32_t>(p) + ((static_cast<uint32_t>(t) - 0x4B400000u) << 23);
+  const uint32_t hi = static_cast<uint32_t>(p >> 32) + ((static_cast<uint32_t>(t >> 32) - 0x4B400000u) << 23);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+// Softmax numerators of one row's n scores (n % 8 == 0) against the running
+// maximum: row max with three-input max in 8 chains, then for each pair
+// x = s * c - m (packed FMA), 2^x on MUFU (three pairs in four) or the FMA
+// pipe (the fourth), packed partial sums, bf16x2 packing of P.  Returns the
+// new maximum in m_use (lazy: kept unless the tile's maximum exceeds it by
+// more than the threshold), the row sum of the numerators in *sum.
+template <int n>
+__device__ __forceinline__ void softmax_tile(const float (&s)[n], float c, float m, float& m_use, float& alpha,
+                                             bool& grow, float& sum, uint32_t (&pk)[n / 2]) {
+  float mp[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) mp[k] = s[k];
+#pragma unroll
+  for (int i = 8; i < n; i += 2) mp[(i >> 1) & 7] = max3(mp[(i >> 1) & 7], s[i], s[i + 1]);
+  const float mx = c * max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+  grow = mx > m + kRescaleThreshold;
+  m_use = grow ? mx : m;
+  alpha = grow ? ex2(m - m_use) : 1.0f;
+  const uint64_t c2 = f2(c, c), nm2 = f2(-m_use, -m_use);
+  uint64_t sp[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < n / 2; ++i) {
+    const uint64_t x = fma2(f2(s[2 * i], s[2 * i + 1]), c2, nm2);
+    const uint64_t e = (i & 3) == 3 ? ex2_poly2(x) : f2(ex2(f2lo(x)), ex2(f2hi(x)));
+    sp[i & 3] = add2(sp[i & 3], e);
+    pk[i] = pack_bf16x2(f2lo(e), f2hi(e));
+  }
+  const uint64_t t = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
+  sum = f2lo(t) + f2hi(t);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnTcArgs p) {
@@ -221,29 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) s[i] = -INFINITY;
       }
-      // Row max as 8 independent chains.
-      float mp[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mp[k] = s[k];
-#pragma unroll
-      for (int i = 8; i < 128; ++i) mp[i & 7] = fmaxf(mp[i & 7], s[i]);
-      float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      mx *= c;
-      // Lazy rescale: keep the running maximum unless it grows by > 2^8.
-      const bool grow = mx > m + kRescaleThreshold;
-      const float m_use = grow ? mx : m;
-      const float alpha = grow ? ex2(m - m_use) : 1.0f;
-      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float m_use, alpha, sum;
+      bool grow;
       uint32_t pk[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float e0 = ex2(fmaf(s[2 * i], c, -m_use));
-        const float e1 = ex2(fmaf(s[2 * i + 1], c, -m_use));
-        sp[(2 * i) & 7] += e0;
-        sp[(2 * i + 1) & 7] += e1;
-        pk[i] = pack_bf16x2(e0, e1);
-      }
-      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      softmax_tile<128>(s, c, m, m_use, alpha, grow, sum, pk);
       l = l * alpha + sum;
       m = m_use;
       if (j > 0) {
@@ -308,6 +364,242 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two-tile variant: one CTA = two 128-row query tiles (A, B) of one (batch,
+// head), 64-key K / V tiles, 320 threads:
+//   warp 0      TMA: Q_A, Q_B once, then K_j (64 keys x 128) and V_j^T
+//               (128 x 64 keys) into a 4-stage ring
+//   warp 1      TMEM allocation and the MMA thread; order
+//                 S_A0 S_B0 S_A1 S_B1 | PV_A0 PV_B0 S_A2 S_B2 | PV_A1 PV_B1 S_A3 ...
+//               so the tensor core computes one tile's P.V and the next
+//               scores while the other tile's softmax runs
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B (one thread
+//               per query row), as in the one-tile kernel.
+// TMEM (512 columns): S_X[buf] at X * 128 + buf * 64 (double-buffered per
+// tile; P_X(j) is written over S_X[j % 2]), O_A at 256, O_B at 384.  S_X(j+2)
+// reuses the buffer of S_X(j) only after PV_X(j) has completed.
+constexpr int k2Tiles = 2;
+constexpr int k2BKV = 64;
+constexpr int k2Stages = 4;
+constexpr int k2QBytes = 128 * 128 * 2;  // one query tile: two 16 KB swizzle-atom halves
+constexpr int k2KHalf = 64 * 128;        // 64 keys x 64 dims x 2 bytes = 8 KB
+constexpr int k2KBytes = 2 * k2KHalf;
+constexpr int k2VBytes = 128 * 64 * 2;   // 128 channels x 64 keys
+constexpr int k2Threads = 320;
+constexpr int k2SmemBytes = k2Tiles * k2QBytes + k2Stages * (k2KBytes + k2VBytes) + 1024 + 256;
+
+__global__ void __launch_bounds__(k2Threads, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnTcArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                    // Q_A | Q_B
+  uint8_t* sK = smem + k2Tiles * k2QBytes;               // k2Stages x 16 KB
+  uint8_t* sV = sK + k2Stages * k2KBytes;                // k2Stages x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + k2Stages * k2VBytes);
+  uint64_t* q_full = bars;                               // Q_A and Q_B landed
+  uint64_t* kv_full = q_full + 1;                        // [4]
+  uint64_t* kv_empty = kv_full + k2Stages;               // [4]
+  uint64_t* s_full = kv_empty + k2Stages;                // [tile][buf]
+  uint64_t* p_full = s_full + 4;                         // [tile], 128 arrivals
+  uint64_t* pv_done = p_full + 2;                        // [tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * (k2Tiles * 128);
+  const int bh = blockIdx.y;
+  const int S = p.S;
+  const int nkv = (S + k2BKV - 1) / k2BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < k2Stages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&p_full[x], 128);
+      mbar_init(&pv_done[x], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, k2Tiles * k2QBytes);
+      for (int x = 0; x < k2Tiles; ++x) {
+        tma_load_3d(sQ + x * k2QBytes, &tmQ, q_full, 0, q0 + x * 128, bh);
+        tma_load_3d(sQ + x * k2QBytes + kHalfBytes, &tmQ, q_full, 64, q0 + x * 128, bh);
+      }
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j % k2Stages;
+        if (!mbar_wait(&kv_empty[st], ((j / k2Stages) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
+        mbar_arrive_expect_tx(&kv_full[st], k2KBytes + k2VBytes);
+        uint8_t* k = sK + st * k2KBytes;
+        tma_load_3d(k, &tmK, &kv_full[st], 0, j * k2BKV, bh);
+        tma_load_3d(k + k2KHalf, &tmK, &kv_full[st], 64, j * k2BKV, bh);
+        tma_load_3d(sV + st * k2VBytes, &tmV, &kv_full[st], j * k2BKV, 0, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 64);
+      constexpr uint32_t idesc_o = make_idesc_bf16(128, 128);
+      const uint32_t aQ = smem_u32(sQ);
+      auto issue_s = [&](int x, int j) -> bool {
+        const int st = j % k2Stages;
+        if (!mbar_wait(&kv_full[st], (j / k2Stages) & 1, p.err, kDevTimeoutAttn)) return false;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sK + st * k2KBytes);
+        const uint32_t d = tmem_base + x * 128 + (j & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t offq = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          const uint32_t offk = (k >> 2) * k2KHalf + (k & 3) * 32;
+          umma_bf16(d, make_sdesc_sw128(aQ + x * k2QBytes + offq), make_sdesc_sw128(aK + offk), idesc_s,
+                    k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[x * 2 + (j & 1)]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
+      for (int j = 0; j < 2 && j < nkv && ok; ++j)
+        for (int x = 0; x < k2Tiles && ok; ++x) ok = issue_s(x, j);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % k2Stages;
+        const uint32_t aV = smem_u32(sV + st * k2VBytes);
+        for (int x = 0; x < k2Tiles && ok; ++x) {
+          if (!mbar_wait(&p_full[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tO = tmem_base + 256 + x * 128;
+          const uint32_t tP = tmem_base + x * 128 + (j & 1) * 64;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16_ts(tO, tP + k * 8, make_sdesc_sw128(aV + k * 32), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&pv_done[x]);
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[st]);
+        if (j + 2 < nkv) {
+          for (int x = 0; x < k2Tiles && ok; ++x) {
+            // S_X(j+2) overwrites the buffer PV_X(j) reads.
+            if (!mbar_wait(&pv_done[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+            ok = issue_s(x, j + 2);
+          }
+        }
+      }
+    }
+  } else {
+    // Softmax: warps 2-5 tile A, 6-9 tile B; TMEM lane quarter = warp % 4.
+    const int x = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tO = tmem_base + lane_off + 256 + x * 128;
+    const float c = p.scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x * 2 + (j & 1)], (j >> 1) & 1, p.err, kDevTimeoutAttn));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tS = tmem_base + lane_off + x * 128 + (j & 1) * 64;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tS, r0);
+      tmem_ld32(tS + 32, r1);
+      tmem_ld_wait();
+      float sv[64];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        sv[i] = __uint_as_float(r0[i]);
+        sv[32 + i] = __uint_as_float(r1[i]);
+      }
+      const int kbase = j * k2BKV;
+      if (kbase + k2BKV > S) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (kbase + i >= S) sv[i] = -INFINITY;
+      }
+      float m_use, alpha, sum;
+      bool grow;
+      uint32_t pk[32];
+      softmax_tile<64>(sv, c, m, m_use, alpha, grow, sum, pk);
+      l = l * alpha + sum;
+      m = m_use;
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (j - 1) & 1, p.err, kDevTimeoutAttn));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tO + ch * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+        }
+      }
+      tmem_st32(tS, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv - 1) & 1, p.err, kDevTimeoutAttn));
+    if (ok) {
+      tc_fence_after();
+      const int q = q0 + x * 128 + row;
+      const float inv = 1.0f / l;
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld32(tO, r0);
+      tmem_ld32(tO + 32, r1);
+      tmem_ld32(tO + 64, r2);
+      tmem_ld32(tO + 96, r3);
+      tmem_ld_wait();
+      if (q < S) {
+        uint16_t* dst = p.o + (static_cast<int64_t>(bh / p.H) * S + q) * p.ld_o + (bh % p.H) * 128;
+        const uint32_t* rs[4] = {r0, r1, r2, r3};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+          const uint32_t* r = rs[ch];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            d4[v] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * v]) * inv, __uint_as_float(r[8 * v + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -324,14 +616,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 map {inner, mid, outer} with box {64, 128, 1}, 128-byte swizzle.
-cudaError_t make_map3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer) {
+// 3-D bf16 map {inner, mid, outer} with box {64, box_mid, 1}, 128-byte swizzle.
+cudaError_t make_map3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer,
+                      uint32_t box_mid = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16) return cudaErrorMisalignedAddress;
   cuuint64_t dims[3] = {inner, mid, outer};
   cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_mid, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -349,12 +642,34 @@ cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* 
   cudaError_t e = make_map3(&maps->q, q, 128, S, bh);
   if (e == cudaSuccess) e = make_map3(&maps->k, k, 128, S, bh);
   if (e == cudaSuccess) e = make_map3(&maps->v, vt, attn_vt_stride(S), 128, bh);
+  if (e == cudaSuccess) e = make_map3(&maps->k64, k, 128, S, bh, 64);
   return e;
+}
+
+int attention_kernel_for(int B, int H, int S, int requested) {
+  (void)B;
+  (void)H;
+  (void)S;
+  // The two-tile kernel measured slower at every config-2 / config-3 shape
+  // (64-key steps double the per-step handshakes; 572 vs 784 TFLOP/s at
+  // S 4608, 24 heads), so auto takes the one-tile kernel.
+  return requested == 2 ? 2 : 1;
 }
 
 cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s) {
   if (a.S <= 0 || a.H <= 0 || a.B <= 0) return cudaSuccess;
   if (a.ld_o % 8 || (reinterpret_cast<uintptr_t>(a.o) & 15)) return cudaErrorInvalidValue;
+  if (attention_kernel_for(a.B, a.H, a.S, a.kernel) == 2) {
+    static bool attr2 = false;
+    if (!attr2) {
+      cudaError_t e = cudaFuncSetAttribute(attn_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k2SmemBytes);
+      if (e != cudaSuccess) return e;
+      attr2 = true;
+    }
+    dim3 grid2((a.S + 255) / 256, a.B * a.H);
+    attn_tc2_kernel<<<grid2, k2Threads, k2SmemBytes, s>>>(maps.q, maps.k64, maps.v, a);
+    return cudaGetLastError();
+  }
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);

@@ -13,11 +13,16 @@ struct AttnTcArgs {
   int32_t B, H, S;
   float scale;     // softmax scale
   int* err;        // device error word for bounded waits
+  int32_t kernel;  // 0 auto, 1 one query tile per CTA, 2 two query tiles per CTA
 };
 
 struct AttnTcMaps {
-  CUtensorMap q, k, v;
+  CUtensorMap q, k, v;  // boxes of 128 rows
+  CUtensorMap k64;      // K with 64-row boxes (two-tile kernel)
 };
+
+// Which kernel a launch uses for (B, H, S): 1 or 2 (requested 0 = auto).
+int attention_kernel_for(int B, int H, int S, int requested);
 
 // Row stride (keys) of the transposed V buffer [B*H, 128, Sp]: S rounded up to 64.
 int64_t attn_vt_stride(int64_t S);

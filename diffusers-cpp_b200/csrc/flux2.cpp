@@ -1164,6 +1164,7 @@ void Flux2Transformer2DModel::build_plan() {
     at.S = static_cast<int32_t>(S);
     at.scale = 1.0f / std::sqrt(static_cast<float>(cfg_.attention_head_dim));
     at.err = ctx_.d_err;
+    at.kernel = ctx_.attn_kernel;
     auto maps = std::make_shared<AttnTcMaps>();
     cuda_check(make_attn_maps(maps.get(), q_, k_, v_, static_cast<int>(B), static_cast<int>(Hl), static_cast<int>(S)),
                "attention tensor maps");

@@ -366,6 +366,13 @@ dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind) {
   });
 }
 
+dcpp_status dcpp_set_attention_kernel(dcpp_ctx* ctx, int kind) {
+  return guarded(ctx, "dcpp_set_attention_kernel", [&] {
+    if (kind < 0 || kind > 2) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_set_attention_kernel: 0 auto, 1 one tile, 2 two tiles");
+    ctx->attn_kernel = kind;
+  });
+}
+
 dcpp_status dcpp_packed_bytes(int type, int64_t N, int64_t K, size_t* out) {
   if (!out || N <= 0 || K <= 0) return DCPP_ERR_INVALID_ARG;
   if ((type != DCPP_TYPE_Q4_K && type != DCPP_TYPE_Q8_0) || (type == DCPP_TYPE_Q4_K && K % 256) || K % 64)
@@ -475,6 +482,7 @@ dcpp_status dcpp_attention(dcpp_ctx* ctx, const uint16_t* qkv, int64_t B, int64_
     a.S = static_cast<int32_t>(S);
     a.scale = 1.0f / sqrtf(128.0f);
     a.err = ctx->d_err;
+    a.kernel = ctx->attn_kernel;
     dcpp::cuda_check(dcpp::launch_attention_tc(maps, a, ctx->stream), "attention");
   });
 }

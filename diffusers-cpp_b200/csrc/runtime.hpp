@@ -60,6 +60,7 @@ struct Ctx {
   // and the single-SM kernel for fused dequantisation (measured faster: the
   // pair kernel is bound by shared-memory bandwidth once B is written there).
   int gemm_kernel = 0;
+  int attn_kernel = 0;  // 0 auto, 1 one query tile per CTA, 2 two tiles
   bool use_pair(int64_t rows, bool fused_dequant = false) const {
     return gemm_kernel == 2 || (gemm_kernel == 0 && rows >= 256 && !fused_dequant);
   }

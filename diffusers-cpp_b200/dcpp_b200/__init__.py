@@ -74,6 +74,7 @@ _SIGNATURES = {
     "dcpp_row_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]),
     "dcpp_inject_fault": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
     "dcpp_set_gemm_kernel": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "dcpp_set_attention_kernel": (ctypes.c_int, [_vp, ctypes.c_int]),
     "dcpp_dequant": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
     "dcpp_dequant_bf16": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
     "dcpp_f32_to_bf16": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
@@ -193,6 +194,11 @@ class Context:
 
     def set_gemm_kernel(self, kind: int):
         self.check(lib().dcpp_set_gemm_kernel(self.h, kind), "set_gemm_kernel")
+
+    ATTN_AUTO, ATTN_ONE_TILE, ATTN_TWO_TILES = 0, 1, 2
+
+    def set_attention_kernel(self, kind: int):
+        self.check(lib().dcpp_set_attention_kernel(self.h, kind), "set_attention_kernel")
 
     def inject_fault(self, name: Optional[str], nth: int = 1):
         lib().dcpp_inject_fault(self.h, name.encode() if name else None, nth)

@@ -97,6 +97,13 @@ dcpp_status dcpp_row_bytes(int type, int64_t n, size_t* out_bytes);
  * 2 = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles). */
 dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind);
 
+/* Attention kernel used by dcpp_attention and the models this context
+ * creates (read at dcpp_flux2_prepare): 0 = auto (currently the one-tile
+ * kernel, the faster on every measured shape), 1 = one 128-row query tile
+ * per CTA with 128-key tiles, 2 = two query tiles per CTA (ping-pong of
+ * their softmax and MMAs) with 64-key tiles. */
+dcpp_status dcpp_set_attention_kernel(dcpp_ctx* ctx, int kind);
+
 /* Host-side fault injection for failure-path tests: the `nth` next call
  * (1 = the next one) of entry point `name` (e.g. "dcpp_gemm") returns
  * DCPP_ERR_INJECTED without touching the GPU.  name == NULL clears. */

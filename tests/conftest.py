@@ -42,3 +42,11 @@ def gemm_kind(request, ctx):
     ctx.set_gemm_kernel(request.param)
     yield request.param
     ctx.set_gemm_kernel(0)
+
+
+@pytest.fixture(params=[1, 2], ids=["one_tile", "two_tiles"])
+def attn_kind(request, ctx):
+    """Run an attention test on the one-tile and on the two-tile kernel."""
+    ctx.set_attention_kernel(request.param)
+    yield request.param
+    ctx.set_attention_kernel(0)

@@ -103,7 +103,7 @@ def test_layernorm_mod_matches_reference(ctx):
     assert ((y.cpu().double() - ref).norm() / ref.norm()).item() < 4e-3
 
 
-def test_attention_full_size_heads_subset(ctx):
+def test_attention_full_size_heads_subset(ctx, attn_kind):
     """The config-2 attention shape (S = 4608, 24 heads); the oracle checks two heads."""
     B, S, H = 1, 4608, 24
     g = torch.Generator().manual_seed(11)
@@ -133,8 +133,8 @@ def test_attention_full_size_heads_subset(ctx):
         assert rel < 1e-2, (h, rel)
 
 
-@pytest.mark.parametrize("B,S,H", [(1, 200, 2), (2, 333, 3), (1, 1024, 4)])
-def test_attention_matches_oracle(ctx, B, S, H):
+@pytest.mark.parametrize("B,S,H", [(1, 200, 2), (2, 333, 3), (1, 1024, 4), (1, 64, 1), (1, 300, 1)])
+def test_attention_matches_oracle(ctx, attn_kind, B, S, H):
     g = torch.Generator().manual_seed(S)
     D = H * 128
     qkv = torch.randn(B, S, 3 * D, generator=g).to(torch.bfloat16)

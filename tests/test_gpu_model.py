@@ -71,6 +71,25 @@ def test_forward_fused_dequant_matches_oracle(ctx, monkeypatch, wtype):
     assert r < V_TOL, r
 
 
+@pytest.mark.parametrize("attn", [1, 2], ids=["one_tile", "two_tiles"])
+def test_forward_each_attention_kernel(ctx, attn):
+    """The model with each attention kernel forced (auto picks by grid size)."""
+    c = cfg_small(num_layers=1, num_single_layers=2)
+    ctx.set_attention_kernel(attn)
+    try:
+        m, params = build(ctx, c, fo.GGML_Q8_0, seed=23, gh=12, gw=20, nt=37)
+        hid, enc, iid, tid = synth.make_inputs(c, 1, 12, 20, 37, seed=24)
+        t = torch.tensor([0.45], dtype=torch.float32)
+        out = torch.empty(1, 240, c.in_channels, dtype=torch.float32)
+        m.forward(hid, enc, t, iid, tid, out)
+        m.close()
+    finally:
+        ctx.set_attention_kernel(0)
+    ref = fo.Flux2Oracle(oracle_cfg(c), params).forward(hid, enc, t, iid, tid)
+    r = rel(out, ref)
+    assert r < V_TOL, r
+
+
 def test_forward_batch2_ragged_text_guidance(ctx):
     c = cfg_small(num_layers=2, num_single_layers=2, guidance_embeds=True)
     m, params = build(ctx, c, fo.GGML_Q8_0, seed=4, B=2, gh=10, gw=13, nt=131)
