@@ -8,7 +8,12 @@
 // shared-memory operand is K-major and arrives through TMA with the 128-byte
 // swizzle.
 //
-// One CTA = one 128-row query tile of one (batch, head); 192 threads:
+// Two kernels share the softmax code: the one-tile kernel below and a
+// two-tile kernel (further down) whose two query tiles ping-pong between the
+// tensor core and the softmax warps; launch_attention_tc picks by how many
+// waves of 148 SMs each needs.
+//
+// One-tile kernel: one CTA = one 128-row query tile of one (batch, head); 192 threads:
 //   warp 0     TMA: Q once, then K_j / V_j^T tiles of 128 keys (3 stages)
 //   warp 1     TMEM allocation and the single MMA-issuing thread:
 //                S_j = Q K_j^T   (M 128, N 128 keys, K 128) -> TMEM buffer j % 3
@@ -366,27 +371,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Two-tile variant: one CTA = two 128-row query tiles (A, B) of one (batch,
-// head), 64-key K / V tiles, 320 threads:
-//   warp 0      TMA: Q_A, Q_B once, then K_j (64 keys x 128) and V_j^T
-//               (128 x 64 keys) into a 4-stage ring
+// head), 128-key K / V tiles, 320 threads:
+//   warp 0      TMA: Q_A, Q_B once, then K_j and V_j^T into a 2-stage ring
 //   warp 1      TMEM allocation and the MMA thread; order
-//                 S_A0 S_B0 S_A1 S_B1 | PV_A0 PV_B0 S_A2 S_B2 | PV_A1 PV_B1 S_A3 ...
-//               so the tensor core computes one tile's P.V and the next
-//               scores while the other tile's softmax runs
+//                 S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 PV_B1 S_B2 ...
+//               so that while one tile's softmax runs, the tensor core
+//               computes the other tile's P.V and next scores
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B (one thread
-//               per query row), as in the one-tile kernel.
-// TMEM (512 columns): S_X[buf] at X * 128 + buf * 64 (double-buffered per
-// tile; P_X(j) is written over S_X[j % 2]), O_A at 256, O_B at 384.  S_X(j+2)
-// reuses the buffer of S_X(j) only after PV_X(j) has completed.
+//               per query row), as in the one-tile kernel; two softmax warps
+//               per SM sub-partition hide each other's latencies.
+// TMEM (512 columns): S_A / P_A at 0, S_B / P_B at 128, O_A at 256, O_B at
+// 384.  S_X(j+1) overwrites S_X only after PV_X(j) (which reads P_X(j) from
+// it) has completed.
 constexpr int k2Tiles = 2;
-constexpr int k2BKV = 64;
-constexpr int k2Stages = 4;
-constexpr int k2QBytes = 128 * 128 * 2;  // one query tile: two 16 KB swizzle-atom halves
-constexpr int k2KHalf = 64 * 128;        // 64 keys x 64 dims x 2 bytes = 8 KB
-constexpr int k2KBytes = 2 * k2KHalf;
-constexpr int k2VBytes = 128 * 64 * 2;   // 128 channels x 64 keys
+constexpr int k2Stages = 2;
 constexpr int k2Threads = 320;
-constexpr int k2SmemBytes = k2Tiles * k2QBytes + k2Stages * (k2KBytes + k2VBytes) + 1024 + 256;
+constexpr int k2SmemBytes = (k2Tiles + 2 * k2Stages) * kTileBytes + 1024 + 256;
 
 __global__ void __launch_bounds__(k2Threads, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -394,23 +394,23 @@ __global__ void __launch_bounds__(k2Threads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                    // Q_A | Q_B
-  uint8_t* sK = smem + k2Tiles * k2QBytes;               // k2Stages x 16 KB
-  uint8_t* sV = sK + k2Stages * k2KBytes;                // k2Stages x 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + k2Stages * k2VBytes);
+  uint8_t* sK = smem + k2Tiles * kTileBytes;             // k2Stages x 32 KB
+  uint8_t* sV = sK + k2Stages * kTileBytes;              // k2Stages x 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + k2Stages * kTileBytes);
   uint64_t* q_full = bars;                               // Q_A and Q_B landed
-  uint64_t* kv_full = q_full + 1;                        // [4]
-  uint64_t* kv_empty = kv_full + k2Stages;               // [4]
-  uint64_t* s_full = kv_empty + k2Stages;                // [tile][buf]
-  uint64_t* p_full = s_full + 4;                         // [tile], 128 arrivals
+  uint64_t* kv_full = q_full + 1;                        // [2]
+  uint64_t* kv_empty = kv_full + k2Stages;               // [2]
+  uint64_t* s_full = kv_empty + k2Stages;                // [tile]
+  uint64_t* p_full = s_full + 2;                         // [tile], 128 arrivals
   uint64_t* pv_done = p_full + 2;                        // [tile]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * (k2Tiles * 128);
+  const int q0 = blockIdx.x * (k2Tiles * kBQ);
   const int bh = blockIdx.y;
   const int S = p.S;
-  const int nkv = (S + k2BKV - 1) / k2BKV;
+  const int nkv = (S + kBKV - 1) / kBKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -418,8 +418,8 @@ __global__ void __launch_bounds__(k2Threads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
     for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 128);
       mbar_init(&pv_done[x], 1);
     }
@@ -441,65 +441,62 @@ __global__ void __launch_bounds__(k2Threads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, k2Tiles * k2QBytes);
+      mbar_arrive_expect_tx(q_full, k2Tiles * kTileBytes);
       for (int x = 0; x < k2Tiles; ++x) {
-        tma_load_3d(sQ + x * k2QBytes, &tmQ, q_full, 0, q0 + x * 128, bh);
-        tma_load_3d(sQ + x * k2QBytes + kHalfBytes, &tmQ, q_full, 64, q0 + x * 128, bh);
+        tma_load_3d(sQ + x * kTileBytes, &tmQ, q_full, 0, q0 + x * kBQ, bh);
+        tma_load_3d(sQ + x * kTileBytes + kHalfBytes, &tmQ, q_full, 64, q0 + x * kBQ, bh);
       }
       for (int j = 0; j < nkv; ++j) {
         const int st = j % k2Stages;
         if (!mbar_wait(&kv_empty[st], ((j / k2Stages) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
-        mbar_arrive_expect_tx(&kv_full[st], k2KBytes + k2VBytes);
-        uint8_t* k = sK + st * k2KBytes;
-        tma_load_3d(k, &tmK, &kv_full[st], 0, j * k2BKV, bh);
-        tma_load_3d(k + k2KHalf, &tmK, &kv_full[st], 64, j * k2BKV, bh);
-        tma_load_3d(sV + st * k2VBytes, &tmV, &kv_full[st], j * k2BKV, 0, bh);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
+        uint8_t* k = sK + st * kTileBytes;
+        uint8_t* v = sV + st * kTileBytes;
+        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bh);
+        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bh);
+        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bh);
+        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bh);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 64);
-      constexpr uint32_t idesc_o = make_idesc_bf16(128, 128);
+      constexpr uint32_t idesc = make_idesc_bf16(128, 128);
       const uint32_t aQ = smem_u32(sQ);
       auto issue_s = [&](int x, int j) -> bool {
         const int st = j % k2Stages;
         if (!mbar_wait(&kv_full[st], (j / k2Stages) & 1, p.err, kDevTimeoutAttn)) return false;
         tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * k2KBytes);
-        const uint32_t d = tmem_base + x * 128 + (j & 1) * 64;
+        const uint32_t aK = smem_u32(sK + st * kTileBytes);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t offq = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          const uint32_t offk = (k >> 2) * k2KHalf + (k & 3) * 32;
-          umma_bf16(d, make_sdesc_sw128(aQ + x * k2QBytes + offq), make_sdesc_sw128(aK + offk), idesc_s,
-                    k > 0 ? 1u : 0u);
+          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+          umma_bf16(tmem_base + x * 128, make_sdesc_sw128(aQ + x * kTileBytes + off), make_sdesc_sw128(aK + off),
+                    idesc, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[x * 2 + (j & 1)]);
+        umma_commit(&s_full[x]);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
-      for (int j = 0; j < 2 && j < nkv && ok; ++j)
-        for (int x = 0; x < k2Tiles && ok; ++x) ok = issue_s(x, j);
+      for (int x = 0; x < k2Tiles && ok; ++x) ok = issue_s(x, 0);
       for (int j = 0; j < nkv && ok; ++j) {
         const int st = j % k2Stages;
-        const uint32_t aV = smem_u32(sV + st * k2VBytes);
+        const uint32_t aV = smem_u32(sV + st * kTileBytes);
         for (int x = 0; x < k2Tiles && ok; ++x) {
           if (!mbar_wait(&p_full[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
           tc_fence_after();
           const uint32_t tO = tmem_base + 256 + x * 128;
-          const uint32_t tP = tmem_base + x * 128 + (j & 1) * 64;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16_ts(tO, tP + k * 8, make_sdesc_sw128(aV + k * 32), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+            umma_bf16_ts(tO, tmem_base + x * 128 + k * 8, make_sdesc_sw128(aV + off), idesc,
+                         (j > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(&pv_done[x]);
-        }
-        if (!ok) break;
-        umma_commit(&kv_empty[st]);
-        if (j + 2 < nkv) {
-          for (int x = 0; x < k2Tiles && ok; ++x) {
-            // S_X(j+2) overwrites the buffer PV_X(j) reads.
+          if (x == k2Tiles - 1) umma_commit(&kv_empty[st]);
+          if (j + 1 < nkv) {
+            // S_X(j+1) overwrites P_X(j): wait until PV_X(j) has read it.
             if (!mbar_wait(&pv_done[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-            ok = issue_s(x, j + 2);
+            ok = issue_s(x, j + 1);
           }
         }
       }
@@ -510,35 +507,39 @@ __global__ void __launch_bounds__(k2Threads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + x * 128;
     const uint32_t tO = tmem_base + lane_off + 256 + x * 128;
     const float c = p.scale * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x * 2 + (j & 1)], (j >> 1) & 1, p.err, kDevTimeoutAttn));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, p.err, kDevTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tS = tmem_base + lane_off + x * 128 + (j & 1) * 64;
-      uint32_t r0[32], r1[32];
+      uint32_t r0[32], r1[32], r2[32], r3[32];
       tmem_ld32(tS, r0);
       tmem_ld32(tS + 32, r1);
+      tmem_ld32(tS + 64, r2);
+      tmem_ld32(tS + 96, r3);
       tmem_ld_wait();
-      float sv[64];
+      float sv[128];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         sv[i] = __uint_as_float(r0[i]);
         sv[32 + i] = __uint_as_float(r1[i]);
+        sv[64 + i] = __uint_as_float(r2[i]);
+        sv[96 + i] = __uint_as_float(r3[i]);
       }
-      const int kbase = j * k2BKV;
-      if (kbase + k2BKV > S) {
+      const int kbase = j * kBKV;
+      if (kbase + kBKV > S) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) sv[i] = -INFINITY;
       }
       float m_use, alpha, sum;
       bool grow;
-      uint32_t pk[32];
-      softmax_tile<64>(sv, c, m, m_use, alpha, grow, sum, pk);
+      uint32_t pk[64];
+      softmax_tile<128>(sv, c, m, m_use, alpha, grow, sum, pk);
       l = l * alpha + sum;
       m = m_use;
       if (j > 0) {
@@ -558,6 +559,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
         }
       }
       tmem_st32(tS, pk);
+      tmem_st32(tS + 32, pk + 32);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
@@ -565,7 +567,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv - 1) & 1, p.err, kDevTimeoutAttn));
     if (ok) {
       tc_fence_after();
-      const int q = q0 + x * 128 + row;
+      const int q = q0 + x * kBQ + row;
       const float inv = 1.0f / l;
       uint32_t r0[32], r1[32], r2[32], r3[32];
       tmem_ld32(tO, r0);
@@ -647,13 +649,14 @@ cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* 
 }
 
 int attention_kernel_for(int B, int H, int S, int requested) {
-  (void)B;
-  (void)H;
-  (void)S;
-  // The two-tile kernel measured slower at every config-2 / config-3 shape
-  // (64-key steps double the per-step handshakes; 572 vs 784 TFLOP/s at
-  // S 4608, 24 heads), so auto takes the one-tile kernel.
-  return requested == 2 ? 2 : 1;
+  if (requested == 1 || requested == 2) return requested;
+  // The two-tile kernel does a CTA's two tiles in ~1.55x the time the
+  // one-tile kernel takes for one (measured per SM clock at S 4608, 24
+  // heads: 29% more work per clock).  Compare whole waves of 148 SMs.
+  const int64_t bh = static_cast<int64_t>(B) * H;
+  const int64_t c1 = (S + 127) / 128 * bh, c2 = (S + 255) / 256 * bh;
+  const double t1 = static_cast<double>((c1 + 147) / 148), t2 = 1.55 * static_cast<double>((c2 + 147) / 148);
+  return t2 < t1 ? 2 : 1;
 }
 
 cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s) {
@@ -667,7 +670,7 @@ cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cud
       attr2 = true;
     }
     dim3 grid2((a.S + 255) / 256, a.B * a.H);
-    attn_tc2_kernel<<<grid2, k2Threads, k2SmemBytes, s>>>(maps.q, maps.k64, maps.v, a);
+    attn_tc2_kernel<<<grid2, k2Threads, k2SmemBytes, s>>>(maps.q, maps.k, maps.v, a);
     return cudaGetLastError();
   }
   static bool attr = false;

@@ -98,10 +98,10 @@ dcpp_status dcpp_row_bytes(int type, int64_t n, size_t* out_bytes);
 dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind);
 
 /* Attention kernel used by dcpp_attention and the models this context
- * creates (read at dcpp_flux2_prepare): 0 = auto (currently the one-tile
- * kernel, the faster on every measured shape), 1 = one 128-row query tile
- * per CTA with 128-key tiles, 2 = two query tiles per CTA (ping-pong of
- * their softmax and MMAs) with 64-key tiles. */
+ * creates (read at dcpp_flux2_prepare): 0 = auto (by the number of waves
+ * each needs on 148 SMs), 1 = one 128-row query tile per CTA,
+ * 2 = two query tiles per CTA (ping-pong of their softmax and MMAs); both
+ * use 128-key tiles. */
 dcpp_status dcpp_set_attention_kernel(dcpp_ctx* ctx, int kind);
 
 /* Host-side fault injection for failure-path tests: the `nth` next call
