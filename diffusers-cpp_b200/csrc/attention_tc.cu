@@ -175,7 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int qt = blockIdx.x;
   const int bh = blockIdx.y;  // b * H + h
   const int S = p.S;
-  const int nkv = (S + kBKV - 1) / kBKV;
+  const int hkv = p.H_kv > 0 ? p.H_kv : p.H;
+  const int bhkv = (bh / p.H) * hkv + (bh % p.H) / (p.H / hkv);  // K / V head of this query head
+  // Causal: query tile qt sees key tiles 0..qt (kBQ == kBKV).
+  const int nkv = p.causal ? min((S + kBKV - 1) / kBKV, qt + 1) : (S + kBKV - 1) / kBKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -216,10 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
         uint8_t* k = sK + st * kTileBytes;
         uint8_t* v = sV + st * kTileBytes;
-        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bh);
-        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bh);
-        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bh);
-        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bh);
+        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bhkv);
+        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bhkv);
+        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bhkv);
+        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bhkv);
       }
     }
   } else if (warp == 1) {
@@ -300,6 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) s[i] = -INFINITY;
+      }
+      if (p.causal && j == nkv - 1) {  // the diagonal tile
+        const int qrow = qt * kBQ + row;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (kbase + i > qrow) s[i] = -INFINITY;
       }
       float m_use, alpha, sum;
       bool grow;
@@ -410,7 +419,10 @@ __global__ void __launch_bounds__(k2Threads, 1)
   const int q0 = blockIdx.x * (k2Tiles * kBQ);
   const int bh = blockIdx.y;
   const int S = p.S;
-  const int nkv = (S + kBKV - 1) / kBKV;
+  const int hkv = p.H_kv > 0 ? p.H_kv : p.H;
+  const int bhkv = (bh / p.H) * hkv + (bh % p.H) / (p.H / hkv);
+  // Causal: the CTA's query tiles 2 qt2 and 2 qt2 + 1 see key tiles up to 2 qt2 + 1.
+  const int nkv = p.causal ? min((S + kBKV - 1) / kBKV, static_cast<int>(blockIdx.x) * 2 + 2) : (S + kBKV - 1) / kBKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -452,10 +464,10 @@ __global__ void __launch_bounds__(k2Threads, 1)
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
         uint8_t* k = sK + st * kTileBytes;
         uint8_t* v = sV + st * kTileBytes;
-        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bh);
-        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bh);
-        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bh);
-        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bh);
+        tma_load_3d(k, &tmK, &kv_full[st], 0, j * kBKV, bhkv);
+        tma_load_3d(k + kHalfBytes, &tmK, &kv_full[st], 64, j * kBKV, bhkv);
+        tma_load_3d(v, &tmV, &kv_full[st], j * kBKV, 0, bhkv);
+        tma_load_3d(v + kHalfBytes, &tmV, &kv_full[st], j * kBKV + 64, 0, bhkv);
       }
     }
   } else if (warp == 1) {
@@ -535,6 +547,12 @@ __global__ void __launch_bounds__(k2Threads, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (kbase + i >= S) sv[i] = -INFINITY;
+      }
+      if (p.causal && kbase + kBKV - 1 > q0 + x * kBQ) {  // tiles reaching past this tile's first query
+        const int qrow = q0 + x * kBQ + row;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (kbase + i > qrow) sv[i] = -INFINITY;
       }
       float m_use, alpha, sum;
       bool grow;
@@ -639,12 +657,13 @@ cudaError_t make_map3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
 int64_t attn_vt_stride(int64_t S) { return (S + 63) / 64 * 64; }
 
 cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* k, const uint16_t* vt, int B, int H,
-                           int S) {
+                           int S, int H_kv) {
   const uint64_t bh = static_cast<uint64_t>(B) * H;
+  const uint64_t bhkv = static_cast<uint64_t>(B) * (H_kv > 0 ? H_kv : H);
   cudaError_t e = make_map3(&maps->q, q, 128, S, bh);
-  if (e == cudaSuccess) e = make_map3(&maps->k, k, 128, S, bh);
-  if (e == cudaSuccess) e = make_map3(&maps->v, vt, attn_vt_stride(S), 128, bh);
-  if (e == cudaSuccess) e = make_map3(&maps->k64, k, 128, S, bh, 64);
+  if (e == cudaSuccess) e = make_map3(&maps->k, k, 128, S, bhkv);
+  if (e == cudaSuccess) e = make_map3(&maps->v, vt, attn_vt_stride(S), 128, bhkv);
+  if (e == cudaSuccess) e = make_map3(&maps->k64, k, 128, S, bhkv, 64);
   return e;
 }
 
@@ -662,6 +681,7 @@ int attention_kernel_for(int B, int H, int S, int requested) {
 cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s) {
   if (a.S <= 0 || a.H <= 0 || a.B <= 0) return cudaSuccess;
   if (a.ld_o % 8 || (reinterpret_cast<uintptr_t>(a.o) & 15)) return cudaErrorInvalidValue;
+  if (a.H_kv < 0 || (a.H_kv > 0 && a.H % a.H_kv)) return cudaErrorInvalidValue;
   if (attention_kernel_for(a.B, a.H, a.S, a.kernel) == 2) {
     static bool attr2 = false;
     if (!attr2) {

@@ -14,6 +14,8 @@ struct AttnTcArgs {
   float scale;     // softmax scale
   int* err;        // device error word for bounded waits
   int32_t kernel;  // 0 auto, 1 one query tile per CTA, 2 two query tiles per CTA
+  int32_t causal;  // 1: key j attends to query i only if j <= i
+  int32_t H_kv;    // key / value heads (grouped-query attention: H % H_kv == 0); 0: = H
 };
 
 struct AttnTcMaps {
@@ -27,9 +29,10 @@ int attention_kernel_for(int B, int H, int S, int requested);
 // Row stride (keys) of the transposed V buffer [B*H, 128, Sp]: S rounded up to 64.
 int64_t attn_vt_stride(int64_t S);
 
-// Tensor maps over q, k [B*H, S, 128] and vt [B*H, 128, Sp] (bf16).
+// Tensor maps over q [B*H, S, 128], k [B*H_kv, S, 128] and vt
+// [B*H_kv, 128, Sp] (bf16); H_kv = 0 means H.
 cudaError_t make_attn_maps(AttnTcMaps* maps, const uint16_t* q, const uint16_t* k, const uint16_t* vt, int B, int H,
-                           int S);
+                           int S, int H_kv = 0);
 
 cudaError_t launch_attention_tc(const AttnTcMaps& maps, const AttnTcArgs& a, cudaStream_t s);
 

@@ -25,6 +25,7 @@ enum DeviceError : int {
   kDevBadShape = 6,         // a launch got a shape its kernel cannot run
   kDevTimeoutAttn = 7,      // attention pipeline wait timed out
   kDevTimeoutPeer = 8,      // tensor-parallel barrier: a peer GPU did not arrive
+  kDevBadIndex = 9,         // an embedding id outside the table
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;  // 1 s

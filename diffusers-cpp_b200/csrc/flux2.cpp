@@ -14,179 +14,9 @@
 
 namespace dcpp {
 
-size_t row_bytes_of(int type, int64_t n);
-
-namespace {
-
-int64_t block_size_of(int type) {
-  if (type == kTypeQ8_0) return 32;
-  if (type == kTypeQ4_K) return 256;
-  return 1;
-}
-size_t block_bytes_of(int type) {
-  switch (type) {
-    case kTypeQ8_0: return 34;
-    case kTypeQ4_K: return 144;
-    case kTypeF32: return 4;
-    default: return 2;
-  }
-}
-uint16_t host_f32_to_bf16(float f) {
-  uint32_t b;
-  memcpy(&b, &f, 4);
-  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return static_cast<uint16_t>((b >> 16) | 0x40);  // quiet NaN
-  b += 0x7FFFu + ((b >> 16) & 1u);  // round to nearest even
-  return static_cast<uint16_t>(b >> 16);
-}
-
-float host_f16_to_f32(const uint8_t* p) {
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
-}
-
-// Dequantise one GGUF row of n weights to f32 (the gguf-py arithmetic: Q8_0
-// d * q; Q4_K (d * sc) * q - dmin * m), for load-time expansion only.
-void host_dequant_row(int type, const uint8_t* src, int64_t n, float* out) {
-  if (type == kTypeQ8_0) {
-    for (int64_t b = 0; b < n / 32; ++b) {
-      const uint8_t* blk = src + b * 34;
-      const float d = host_f16_to_f32(blk);
-      for (int i = 0; i < 32; ++i) out[b * 32 + i] = static_cast<float>(static_cast<int8_t>(blk[2 + i])) * d;
-    }
-  } else if (type == kTypeQ4_K) {
-    for (int64_t b = 0; b < n / 256; ++b) {
-      const uint8_t* blk = src + b * 144;
-      const float d = host_f16_to_f32(blk), dmin = host_f16_to_f32(blk + 2);
-      const uint8_t* s = blk + 4;
-      for (int j = 0; j < 8; ++j) {
-        int sc, m;
-        if (j < 4) {
-          sc = s[j] & 0x3F;
-          m = s[j + 4] & 0x3F;
-        } else {
-          sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30);
-          m = (s[j + 4] >> 4) | ((s[j] >> 2) & 0x30);
-        }
-        const float ds = d * static_cast<float>(sc), dm = dmin * static_cast<float>(m);
-        const uint8_t* qs = blk + 16 + (j / 2) * 32;
-        for (int l = 0; l < 32; ++l) {
-          const float q = static_cast<float>((qs[l] >> ((j & 1) * 4)) & 0x0F);
-          const float prod = ds * q;
-          out[b * 256 + j * 32 + l] = prod - dm;
-        }
-      }
-    }
-  } else {
-    fail(DCPP_ERR_UNSUPPORTED, "host dequantisation: Q8_0 / Q4_K only");
-  }
-}
-
-bool is_gemm_type(int t) {
-  return t == kTypeQ8_0 || t == kTypeQ4_K || t == kTypeBF16 || t == kTypeF16 || t == kTypeF32;
-}
-
-std::string shape_str(const std::vector<int64_t>& s) {
-  std::string r = "[";
-  for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
-  return r + "]";
-}
-
-// ---- a small JSON reader for diffusers config.json (flat object with
-// numbers, booleans, null, strings and arrays of numbers).
-struct Json {
-  const std::string& s;
-  size_t i = 0;
-  explicit Json(const std::string& src) : s(src) {}
-  void ws() {
-    while (i < s.size() && isspace(static_cast<unsigned char>(s[i]))) ++i;
-  }
-  [[noreturn]] void bad() { fail(DCPP_ERR_INVALID_ARG, "config json: parse error at offset " + std::to_string(i)); }
-  std::string str() {
-    ws();
-    if (i >= s.size() || s[i] != '"') bad();
-    ++i;
-    std::string r;
-    while (i < s.size() && s[i] != '"') {
-      if (s[i] == '\\' && i + 1 < s.size()) ++i;
-      r += s[i++];
-    }
-    if (i >= s.size()) bad();
-    ++i;
-    return r;
-  }
-  // Returns a value as text: number, true/false/null, "string", or [a,b,..].
-  std::string value() {
-    ws();
-    if (i >= s.size()) bad();
-    if (s[i] == '"') return "\"" + str() + "\"";
-    if (s[i] == '[' || s[i] == '{') {
-      char open = s[i], close = open == '[' ? ']' : '}';
-      int depth = 0;
-      size_t st = i;
-      bool in_str = false;
-      for (; i < s.size(); ++i) {
-        char c = s[i];
-        if (in_str) {
-          if (c == '\\') ++i;
-          else if (c == '"') in_str = false;
-          continue;
-        }
-        if (c == '"') in_str = true;
-        else if (c == open) ++depth;
-        else if (c == close && --depth == 0) { ++i; return s.substr(st, i - st); }
-      }
-      bad();
-    }
-    size_t st = i;
-    while (i < s.size() && s[i] != ',' && s[i] != '}' && s[i] != ']' && !isspace(static_cast<unsigned char>(s[i]))) ++i;
-    return s.substr(st, i - st);
-  }
-  std::map<std::string, std::string> object() {
-    std::map<std::string, std::string> m;
-    ws();
-    if (i >= s.size() || s[i] != '{') bad();
-    ++i;
-    ws();
-    if (i < s.size() && s[i] == '}') { ++i; return m; }
-    for (;;) {
-      std::string k = str();
-      ws();
-      if (i >= s.size() || s[i] != ':') bad();
-      ++i;
-      m[k] = value();
-      ws();
-      if (i < s.size() && s[i] == ',') { ++i; continue; }
-      if (i < s.size() && s[i] == '}') { ++i; break; }
-      bad();
-    }
-    return m;
-  }
-};
-
-std::vector<int64_t> parse_int_list(const std::string& v) {
-  std::vector<int64_t> r;
-  std::string t;
-  for (char c : v) {
-    if (c == '[' || c == ']' || c == ',' || isspace(static_cast<unsigned char>(c))) {
-      if (!t.empty()) { r.push_back(static_cast<int64_t>(std::stod(t))); t.clear(); }
-    } else {
-      t += c;
-    }
-  }
-  if (!t.empty()) r.push_back(static_cast<int64_t>(std::stod(t)));
-  return r;
-}
-
-}  // namespace
-
 // ----------------------------------------------------------------- config
 Flux2Config Flux2Config::from_file(const std::string& path) {
-  std::ifstream f(path);
-  if (!f.is_open()) fail(DCPP_ERR_NOT_FOUND, "Failed to open configuration file: " + path);
-  std::stringstream ss;
-  ss << f.rdbuf();
-  std::string text = ss.str();
-  Json j(text);
-  auto m = j.object();
+  auto m = read_json_object(path);
   Flux2Config c;
   auto num = [&](const char* k, auto& dst) {
     auto it = m.find(k);
@@ -268,7 +98,7 @@ void FlowMatchEulerDiscreteScheduler::schedule(int n, std::vector<float>& timest
 
 // ----------------------------------------------------------------- model
 Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cfg, bool host_only)
-    : ctx_(ctx), cfg_(cfg), host_only_(host_only) {
+    : StepPlanner(ctx), cfg_(cfg), host_only_(host_only) {
   if (cfg_.attention_head_dim != 128) fail(DCPP_ERR_UNSUPPORTED, "attention_head_dim must be 128");
   if (cfg_.patch_size != 1) fail(DCPP_ERR_UNSUPPORTED, "patch_size must be 1");
   int64_t tot = 0;
@@ -291,8 +121,6 @@ Flux2Transformer2DModel::~Flux2Transformer2DModel() {
   }
   for (auto* v : vectors_)
     if (v->data) cudaFree(v->data);
-  for (auto e : ev_) cudaEventDestroy(e);
-  if (side_) cudaStreamDestroy(side_);
 }
 
 void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks) {
@@ -611,35 +439,7 @@ void Flux2Transformer2DModel::finish_weight(DevWeight& w) {
 
 void Flux2Transformer2DModel::set_vector(DevVector& v, int type, const std::vector<int64_t>& shape, const void* data,
                                          size_t nbytes) {
-  if (shape.size() != 1 || shape[0] != v.n)
-    fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + v.name + "': Parameter shape mismatch: expected " +
-                                   shape_str({v.n}) + ", got " + shape_str(shape));
-  std::vector<float> host(static_cast<size_t>(v.n));
-  const auto* u16 = static_cast<const uint16_t*>(data);
-  if (type == kTypeF32) {
-    if (nbytes != static_cast<size_t>(v.n) * 4) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + v.name + "': byte size mismatch");
-    memcpy(host.data(), data, nbytes);
-  } else if (type == kTypeBF16 || type == kTypeF16) {
-    if (nbytes != static_cast<size_t>(v.n) * 2) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + v.name + "': byte size mismatch");
-    for (int64_t i = 0; i < v.n; ++i) {
-      if (type == kTypeBF16) {
-        uint32_t b = static_cast<uint32_t>(u16[i]) << 16;
-        memcpy(&host[i], &b, 4);
-      } else {
-        host[i] = __half2float(__ushort_as_half(u16[i]));
-      }
-    }
-  } else {
-    fail(DCPP_ERR_UNSUPPORTED, "Tensor '" + v.name + "': norm weights must be F32, F16 or BF16");
-  }
-  if (host_only_) {
-    v.host.swap(host);
-    v.set = true;
-    return;
-  }
-  if (!v.data) cuda_check(cudaMalloc(&v.data, v.n * sizeof(float)), "alloc vector");
-  cuda_check(cudaMemcpy(v.data, host.data(), v.n * sizeof(float), cudaMemcpyHostToDevice), "upload vector");
-  v.set = true;
+  set_vector_param(v, type, shape, data, nbytes, host_only_);
   planned_ = false;
 }
 
@@ -716,8 +516,7 @@ void Flux2Transformer2DModel::free_plan() {
   for (void* p : allocs_) cudaFree(p);
   allocs_.clear();
   sym_.close(ctx_);
-  for (auto e : plan_events_) cudaEventDestroy(e);
-  plan_events_.clear();
+  release_plan_events();
   for (int j = 0; j < 8; ++j) {
     recv_peer_[j] = nullptr;
     a_peer_[j] = nullptr;
@@ -750,144 +549,9 @@ void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_tx
   planned_ = true;
 }
 
-void Flux2Transformer2DModel::add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
-                                       const DevWeight* w0, const DevWeight* w1, std::vector<GemmGroup> groups,
-                                       const EpilogueArgs& ep, int64_t N) {
-  add_gemm_pieces(tag, a, lda, K, w0, w1, {groups}, ep, N, nullptr);
-}
 
-void Flux2Transformer2DModel::add_gemm_pieces(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K,
-                                              const DevWeight* w0, const DevWeight* w1,
-                                              const std::vector<std::vector<GemmGroup>>& pieces, const EpilogueArgs& ep,
-                                              int64_t N, const std::function<void(int)>& before_piece) {
-  if (w0->cols != K || (w1 && (w1->cols != K || w1->rows != w0->rows)) || w0->rows != N)
-    fail(DCPP_ERR_STATE, "internal: GEMM shape mismatch for " + w0->name);
-  std::vector<GemmGroup> groups;
-  for (auto& pg : pieces) groups.insert(groups.end(), pg.begin(), pg.end());
-  // Fused dequantisation when every weight of the launch is packed and of
-  // one quantised type; otherwise expand to bf16 first (or use bf16 as is).
-  const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
-  int64_t total_rows = 0;
-  for (auto& g : groups) total_rows += g.rows;
-  const bool pair = ctx_.use_pair(total_rows, fused);
-  const int tile_m = pair ? 256 : kGemmBM;
-  if (fused) {
-    int64_t a_rows = 0;
-    for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
-    auto st = std::make_shared<CUtensorMap>();
-    cuda_check(make_tmap_bf16(st.get(), a, K, a_rows, lda, kGemmBM), "tensor map A");
-    const int bsrc = w0->type == kTypeQ4_K ? kBSrcQ4_K : kBSrcQ8_0;
-    Ctx* c = &ctx_;
-    for (size_t p = 0; p < pieces.size(); ++p) {
-      if (before_piece) before_piece(static_cast<int>(p));
-      const auto& pg = pieces[p];
-      GemmArgs args{};
-      args.N = static_cast<int32_t>(N);
-      args.K = static_cast<int32_t>(K);
-      if (pg.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
-      args.n_groups = static_cast<int32_t>(pg.size());
-      for (size_t i = 0; i < pg.size(); ++i) args.groups[i] = pg[i];
-      args.ep = ep;
-      args.err = ctx_.d_err;
-      args.qb[0].packed = w0->packed;
-      args.qb[1].packed = w1 ? w1->packed : w0->packed;
-      gemm_finalize_groups(args, tile_m);
-      double flops = 0.0;
-      for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
-      building_->push_back({[st, args, c, bsrc, pair](cudaStream_t s) {
-                              if (pair)
-                                cuda_check(launch_gemm_pair(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm (pair)");
-                              else
-                                cuda_check(launch_gemm(*st, *st, *st, args, bsrc, c->num_sms, s), "fused gemm");
-                            },
-                            1, kOpGemm, flops, tag + " (fused dequant)"});
-    }
-    return;
-  }
-  if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
-  const bool expand0 = w0->type != kTypeBF16, expand1 = w1 && w1->type != kTypeBF16;
-  const int pair_idx = scratch_pair_;
-  if (expand0 || expand1) scratch_pair_ ^= 1;
-  uint16_t* const* sc = wscratch_[pair_idx];
-  const uint16_t* b0 = expand0 ? sc[0] : reinterpret_cast<const uint16_t*>(w0->data);
-  const uint16_t* b1 = b0;
-  if (w1) b1 = expand1 ? sc[1] : reinterpret_cast<const uint16_t*>(w1->data);
-  int64_t a_rows = 0;
-  for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
-  auto st = std::make_shared<std::array<CUtensorMap, 3>>();
-  cuda_check(make_tmap_bf16(&(*st)[0], a, K, a_rows, lda, kGemmBM), "tensor map A");
-  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, pair ? 128 : kGemmBN), "tensor map B0");
-  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, pair ? 128 : kGemmBN), "tensor map B1");
-  Ctx* c = &ctx_;
-  // Weight expansion on the side stream: it waits only for the last GEMM
-  // that read this scratch pair (two expanding GEMMs back), so it overlaps
-  // the GEMMs, attention and norms in between; the GEMM waits for it.
-  if (expand0 || expand1) {
-    add_wait(scratch_free_[pair_idx] ? scratch_free_[pair_idx] : plan_start_, 1);
-    for (int k = 0; k < 2; ++k) {
-      const DevWeight* w = k == 0 ? w0 : w1;
-      if (!(k == 0 ? expand0 : expand1)) continue;
-      uint16_t* dst = sc[k];
-      Op o{[w, dst](cudaStream_t s) {
-             cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
-           },
-           1, kOpDequant, 0.0, "dequant " + tag};
-      o.stream = 1;
-      building_->push_back(o);
-    }
-  }
-  cudaEvent_t ready = nullptr;
-  if (expand0 || expand1) {
-    ready = plan_event();
-    add_record(ready, 1);
-  }
-  for (size_t p = 0; p < pieces.size(); ++p) {
-    if (before_piece) before_piece(static_cast<int>(p));
-    if (p == 0 && ready) add_wait(ready, 0);
-    const auto& pg = pieces[p];
-    GemmArgs args{};
-    args.N = static_cast<int32_t>(N);
-    args.K = static_cast<int32_t>(K);
-    if (pg.size() > static_cast<size_t>(kGemmMaxGroups)) fail(DCPP_ERR_UNSUPPORTED, "too many GEMM row groups");
-    args.n_groups = static_cast<int32_t>(pg.size());
-    for (size_t i = 0; i < pg.size(); ++i) args.groups[i] = pg[i];
-    args.ep = ep;
-    args.err = ctx_.d_err;
-    gemm_finalize_groups(args, tile_m);
-    double flops = 0.0;
-    for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
-    building_->push_back({[st, args, c, pair](cudaStream_t s) {
-                            if (pair)
-                              cuda_check(launch_gemm_pair((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
-                                         "gemm (pair)");
-                            else
-                              cuda_check(launch_gemm((*st)[0], (*st)[1], (*st)[2], args, kBSrcBf16, c->num_sms, s),
-                                         "gemm");
-                          },
-                          1, kOpGemm, flops, tag});
-  }
-  if (expand0 || expand1) {
-    scratch_free_[pair_idx] = plan_event();
-    add_record(scratch_free_[pair_idx], 0);
-  }
-}
 
-void Flux2Transformer2DModel::add_norm(const NormArgs& a, int stream) {
-  Op o{[a](cudaStream_t s) { cuda_check(launch_layernorm_mod(a, s), "layernorm_mod"); }, 1, kOpNorm, 0.0,
-       a.n_slots ? "layernorm+allgather" : "layernorm"};
-  o.stream = stream;
-  building_->push_back(o);
-}
 
-void Flux2Transformer2DModel::add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y) {
-  const DevWeight* pw = &w;
-  const int B = static_cast<int>(B_);
-  building_->push_back({[pw, x, act_in, act_out, y, B](cudaStream_t s) {
-                          cuda_check(launch_gemv(pw->type, pw->data, pw->rows, pw->cols, x, B, act_in, act_out, y, s),
-                                     "gemv");
-                        },
-                        1, kOpGemv, 2.0 * B * static_cast<double>(pw->rows) * static_cast<double>(pw->cols), w.name});
-}
 
 void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
   Ctx* c = &ctx_;
@@ -899,26 +563,8 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
                         0, kOpAllreduce, 0.0, "nccl_allreduce"});
 }
 
-cudaEvent_t Flux2Transformer2DModel::plan_event() {
-  cudaEvent_t e;
-  cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
-  plan_events_.push_back(e);
-  return e;
-}
 
-void Flux2Transformer2DModel::add_record(cudaEvent_t e, int stream) {
-  Op o{[e](cudaStream_t s) { cuda_check(cudaEventRecord(e, s), "event record"); }, 0, kOpOther, 0.0, "record"};
-  o.stream = stream;
-  o.timed = false;
-  building_->push_back(o);
-}
 
-void Flux2Transformer2DModel::add_wait(cudaEvent_t e, int stream) {
-  Op o{[e](cudaStream_t s) { cuda_check(cudaStreamWaitEvent(s, e, 0), "stream wait"); }, 0, kOpOther, 0.0, "wait"};
-  o.stream = stream;
-  o.timed = false;
-  building_->push_back(o);
-}
 
 void Flux2Transformer2DModel::add_tp_barrier(int set, int stream) {
   TpBarrierArgs a{};
@@ -1030,15 +676,7 @@ void Flux2Transformer2DModel::build_plan() {
   for (auto& blk : sgl_)
     for (const DevWeight* w : {&blk.qkv_mlp, &blk.out})
       if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
-  for (int pi = 0; pi < 2; ++pi) {
-    wscratch_[pi][0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
-    wscratch_[pi][1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
-  }
-  if (!side_) {
-    int lo = 0, hi = 0;
-    cudaDeviceGetStreamPriorityRange(&lo, &hi);
-    cuda_check(cudaStreamCreateWithPriority(&side_, cudaStreamNonBlocking, lo), "side stream");
-  }
+  alloc_expansion_scratch(alloc, s0, s1);
 
   const int n_axes = static_cast<int>(cfg_.axes_dims_rope.size());
   std::array<int32_t, 8> axes{};
@@ -1095,12 +733,7 @@ void Flux2Transformer2DModel::build_plan() {
   };
 
   auto build_ops = [&](std::vector<Op>& ops, float* lat_in, float* lat_out, bool euler) {
-    building_ = &ops;
-    scratch_pair_ = 0;
-    scratch_free_[0] = scratch_free_[1] = nullptr;
-    plan_start_ = plan_event();
-    add_record(plan_start_, 0);
-    add_wait(plan_start_, 1);  // the side stream joins the plan (and a capture) at its start
+    begin_ops(ops);
     // 1. timestep (and guidance) embedding, modulation vectors
     //    (Flux2Transformer2DModel.cpp:199-214).
     ops.push_back({[=](cudaStream_t s) {
@@ -1108,22 +741,22 @@ void Flux2Transformer2DModel::build_plan() {
                                 "timestep_proj");
                    },
                    1});
-    add_gemv(time1_, tproj_, 0, 1, th_);
-    add_gemv(time2_, th_, 0, 0, temb_);
+    add_gemv(time1_, tproj_, static_cast<int>(B), 0, 1, th_);
+    add_gemv(time2_, th_, static_cast<int>(B), 0, 0, temb_);
     if (guidance_given_) {
       ops.push_back({[=](cudaStream_t s) {
                        cuda_check(launch_timestep_proj(g_dev_, static_cast<int>(B), static_cast<int>(tg), 1000.0f, gproj_, s),
                                   "guidance_proj");
                      },
                      1});
-      add_gemv(guid1_, gproj_, 0, 1, gh_);
-      add_gemv(guid2_, gh_, 0, 0, gemb_);
+      add_gemv(guid1_, gproj_, static_cast<int>(B), 0, 1, gh_);
+      add_gemv(guid2_, gh_, static_cast<int>(B), 0, 0, gemb_);
       ops.push_back({[=](cudaStream_t s) { cuda_check(launch_add_f32(temb_, gemb_, B * D, s), "add"); }, 1});
     }
-    add_gemv(mod_img_, temb_, 1, 0, mod_img_v_);
-    add_gemv(mod_txt_, temb_, 1, 0, mod_txt_v_);
-    add_gemv(mod_single_, temb_, 1, 0, mod_s_v_);
-    add_gemv(norm_out_, temb_, 1, 0, mod_o_v_);
+    add_gemv(mod_img_, temb_, static_cast<int>(B), 1, 0, mod_img_v_);
+    add_gemv(mod_txt_, temb_, static_cast<int>(B), 1, 0, mod_txt_v_);
+    add_gemv(mod_single_, temb_, static_cast<int>(B), 1, 0, mod_s_v_);
+    add_gemv(norm_out_, temb_, static_cast<int>(B), 1, 0, mod_o_v_);
     // 2. input projections into the joint residual stream h = [txt | img].
     ops.push_back({[=](cudaStream_t s) {
                      cuda_check(launch_f32_to_bf16(lat_in, B * Ni * in_ch, xb_, s), "to_bf16");
@@ -1385,12 +1018,7 @@ void Flux2Transformer2DModel::build_plan() {
                   add_gemm_pieces("proj_out", a_, D, D, &proj_out_, nullptr, pcs, e, out_ch, hook);
                 });
     }
-    // Join the side stream back into the main stream (a captured graph must
-    // end on its origin stream).
-    cudaEvent_t side_done = plan_event();
-    add_record(side_done, 1);
-    add_wait(side_done, 0);
-    building_ = nullptr;
+    end_ops();
   };
   guidance_given_ = cfg_.guidance_embeds;
   build_ops(ops_fwd_, lat_[0], out_dev_, false);
@@ -1408,58 +1036,6 @@ void Flux2Transformer2DModel::build_plan() {
 namespace dcpp {
 
 // ----------------------------------------------------------------- execution
-void Flux2Transformer2DModel::run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph) {
-  cudaStream_t s = ctx_.stream;
-  last_ops_ = &ops;
-  auto issue = [&]() {
-    if (!profiling_) {
-      for (auto& o : ops) o.fn(o.stream ? side_ : s);
-      return;
-    }
-    if (ev_.size() < 2 * ops.size()) {
-      for (size_t i = ev_.size(); i < 2 * ops.size(); ++i) {
-        cudaEvent_t e;
-        cuda_check(cudaEventCreate(&e), "cudaEventCreate");
-        ev_.push_back(e);
-      }
-    }
-    // Inside a capture the records become graph event nodes (external
-    // flag); outside they are ordinary stream records.
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    cuda_check(cudaStreamIsCapturing(s, &cs), "cudaStreamIsCapturing");
-    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
-    for (size_t i = 0; i < ops.size(); ++i) {
-      cudaStream_t os = ops[i].stream ? side_ : s;
-      if (!ops[i].timed) {  // stream record / wait
-        ops[i].fn(os);
-        continue;
-      }
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i], os, flags), "event record");
-      ops[i].fn(os);
-      cuda_check(cudaEventRecordWithFlags(ev_[2 * i + 1], os, flags), "event record");
-    }
-  };
-  if (!use_graph_) {
-    issue();
-    return;
-  }
-  if (!*graph) {
-    cudaGraph_t g = nullptr;
-    cuda_check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
-    try {
-      issue();
-    } catch (...) {
-      cudaStreamEndCapture(s, &g);
-      if (g) cudaGraphDestroy(g);
-      throw;
-    }
-    cuda_check(cudaStreamEndCapture(s, &g), "end capture");
-    cudaError_t e = cudaGraphInstantiate(graph, g, 0);
-    cudaGraphDestroy(g);
-    cuda_check(e, "graph instantiate");
-  }
-  cuda_check(cudaGraphLaunch(*graph, s), "graph launch");
-}
 
 void Flux2Transformer2DModel::copy_inputs(const float* hidden, const float* encoder, const float* timestep,
                                           const int32_t* img_ids, const int32_t* txt_ids, const float* guidance) {
@@ -1536,42 +1112,6 @@ void Flux2Transformer2DModel::set_profiling(bool on) {
   profiling_ = on;
 }
 
-void Flux2Transformer2DModel::profile(int kind, double* ms, double* flops, int64_t* launches) {
-  if (!profiling_) fail(DCPP_ERR_STATE, "profiling is off (dcpp_flux2_set_profiling before prepare)");
-  if (!last_ops_) fail(DCPP_ERR_STATE, "no step has run yet");
-  cuda_check(cudaStreamSynchronize(ctx_.stream), "sync");
-  double t = 0.0, f = 0.0;
-  int64_t n = 0;
-  for (size_t i = 0; i < last_ops_->size(); ++i) {
-    const Op& o = (*last_ops_)[i];
-    if (o.kind != kind || !o.timed) continue;
-    float e = 0.f;
-    cuda_check(cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]), "cudaEventElapsedTime");
-    t += e;
-    f += o.flops;
-    n += o.launches;
-  }
-  if (ms) *ms = t;
-  if (flops) *flops = f;
-  if (launches) *launches = n;
-  // DCPP_PROFILE_OPS=<path>: also write every op of the step (index, tag,
-  // kind, milliseconds, algorithmic FLOPs) as CSV, once per executed step.
-  const char* path = getenv("DCPP_PROFILE_OPS");
-  if (path && kind == kOpGemm) {
-    FILE* f = fopen(path, "w");
-    if (f) {
-      fprintf(f, "index,tag,kind,ms,flops,stream\n");
-      for (size_t i = 0; i < last_ops_->size(); ++i) {
-        const Op& o = (*last_ops_)[i];
-        if (!o.timed) continue;
-        float e = 0.f;
-        cudaEventElapsedTime(&e, ev_[2 * i], ev_[2 * i + 1]);
-        fprintf(f, "%zu,%s,%d,%.5f,%.6g,%d\n", i, o.tag.c_str(), o.kind, e, o.flops, o.stream);
-      }
-      fclose(f);
-    }
-  }
-}
 
 void Flux2Transformer2DModel::read_latents(float* out) {
   if (!planned_) fail(DCPP_ERR_STATE, "read_latents before prepare");

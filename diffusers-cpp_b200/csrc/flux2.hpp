@@ -25,6 +25,7 @@
 
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "plan.hpp"
 #include "runtime.hpp"
 
 namespace dcpp {
@@ -53,33 +54,7 @@ struct Flux2Config {
   int64_t out_ch() const { return patch_size * patch_size * (out_channels > 0 ? out_channels : in_channels); }
 };
 
-// A weight matrix [rows, cols] of one ggml type, as raw GGUF rows on the
-// device, assembled from one or more named parts.
-struct DevWeight {
-  std::string name;
-  int type = -1;
-  int64_t rows = 0;
-  int64_t cols = 0;
-  size_t row_bytes = 0;
-  uint8_t* data = nullptr;             // device, raw GGUF rows (null once packed)
-  uint8_t* packed = nullptr;           // device, fused-dequant stage layout (block projections)
-  bool pack = false;                   // a block projection: pack when quantised
-  bool on_host = false;                // host-only model: assembled rows kept in `staging`
-  std::vector<uint8_t> staging;        // host, until all parts arrived
-  std::set<std::string> need;          // part names still missing
-  bool ready() const { return (data != nullptr || packed != nullptr || on_host) && need.empty(); }
-};
-
-// An f32 vector parameter (RMSNorm weights).
-struct DevVector {
-  std::string name;
-  int64_t n = 0;
-  float* data = nullptr;
-  std::vector<float> host;  // host-only model
-  bool set = false;
-};
-
-class Flux2Transformer2DModel {
+class Flux2Transformer2DModel : public StepPlanner {
  public:
   // host_only: parameters are assembled (and tensor-parallel sharded) on
   // the host and never uploaded; the model cannot execute.  Used to inspect
@@ -114,15 +89,11 @@ class Flux2Transformer2DModel {
   void set_timestep(float timestep, float dt);
   void run_resident_step();
   void read_latents(float* out);
-  int64_t launches_per_step() const { return launches_per_step_; }
 
   // Profiling: when on (set before prepare), every kernel op of a step is
-  // bracketed by CUDA event records (captured into the graph as event
-  // nodes); profile() sums the last executed step's times per op kind.
-  enum ProfileKind { kOpGemm = 0, kOpAttention = 1, kOpNorm = 2, kOpGemv = 3, kOpDequant = 4, kOpOther = 5,
-                     kOpAllreduce = 6, kOpKinds = 7 };
+  // bracketed by CUDA event records; profile() (StepPlanner) sums the last
+  // executed step's times per op kind.
   void set_profiling(bool on);
-  void profile(int kind, double* ms, double* flops, int64_t* launches);
 
  private:
   struct DoubleBlock {
@@ -133,16 +104,6 @@ class Flux2Transformer2DModel {
     DevWeight qkv_mlp, out;
     DevVector norm_q, norm_k;
   };
-  struct Op {
-    std::function<void(cudaStream_t)> fn;
-    int launches;
-    int kind = kOpOther;   // ProfileKind
-    double flops = 0.0;    // algorithmic FLOPs of the op
-    std::string tag;       // what the op is (profile dumps)
-    int stream = 0;        // 0: the context's stream, 1: the model's side stream
-    bool timed = true;     // false for stream records / waits (not profiled)
-  };
-
   void build_registry();
   void place_rows(DevWeight& w, const std::string& part, int type, const std::vector<int64_t>& shape,
                   const uint8_t* src, const std::function<int64_t(int64_t)>& row_map,
@@ -153,28 +114,13 @@ class Flux2Transformer2DModel {
   void set_vector(DevVector& v, int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes);
   void free_plan();
   void build_plan();
-  void run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph);
   void copy_inputs(const float* hidden, const float* encoder, const float* timestep, const int32_t* img_ids,
                    const int32_t* txt_ids, const float* guidance);
 
-  // Plan helpers.
-  void add_gemm(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K, const DevWeight* w0,
-                const DevWeight* w1, std::vector<GemmGroup> groups, const EpilogueArgs& ep, int64_t N);
-  // The same GEMM launched once per row piece (weights expanded once);
-  // before_piece(p) emits what must precede piece p.
-  void add_gemm_pieces(const std::string& tag, const uint16_t* a, int64_t lda, int64_t K, const DevWeight* w0,
-                       const DevWeight* w1, const std::vector<std::vector<GemmGroup>>& pieces, const EpilogueArgs& ep,
-                       int64_t N, const std::function<void(int)>& before_piece);
-  void add_norm(const NormArgs& a, int stream = 0);
-  void add_gemv(const DevWeight& w, const float* x, int act_in, int act_out, float* y);
+  // Plan helpers (tensor parallelism).
   void add_allreduce(float* buf, int64_t count);
   void add_tp_barrier(int set, int stream);
-  // Cross-stream dependencies inside a plan (graph edges when captured).
-  cudaEvent_t plan_event();
-  void add_record(cudaEvent_t e, int stream);
-  void add_wait(cudaEvent_t e, int stream);
 
-  Ctx& ctx_;
   Flux2Config cfg_;
   bool host_only_ = false;
   int rank_ = 0, nranks_ = 1;
@@ -192,7 +138,6 @@ class Flux2Transformer2DModel {
 
   // Plan state.
   int64_t B_ = 0, Ni_ = 0, Nt_ = 0, S_ = 0;
-  bool use_graph_ = false;
   bool planned_ = false;
   bool guidance_given_ = false;
   std::vector<void*> allocs_;
@@ -202,15 +147,6 @@ class Flux2Transformer2DModel {
   float *mod_img_v_ = nullptr, *mod_txt_v_ = nullptr, *mod_s_v_ = nullptr, *mod_o_v_ = nullptr;
   uint16_t *a_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *cat_ = nullptr, *xb_ = nullptr,
            *eb_ = nullptr;
-  // bf16 expansion of quantised GEMM weights: two pairs (txt / img stream
-  // weight of one launch), used alternately, so that the expansion of the
-  // next projection runs on the side stream while the current GEMM computes.
-  uint16_t* wscratch_[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
-  int scratch_pair_ = 0;
-  cudaEvent_t scratch_free_[2] = {nullptr, nullptr};  // last GEMM that read the pair (null: none yet)
-  cudaEvent_t plan_start_ = nullptr;                   // recorded on the main stream first in a plan
-  cudaStream_t side_ = nullptr;
-  std::vector<cudaEvent_t> plan_events_;
   int32_t* ids_dev_ = nullptr;
   float2* rope_ = nullptr;
   // Tensor parallelism over peer memory (the default exchange): the
@@ -236,17 +172,12 @@ class Flux2Transformer2DModel {
   int cur_ = 0;                    // latent ping-pong index
   std::vector<Op> ops_fwd_;        // forward (noise prediction) plan
   std::vector<Op> step_ops_[2];    // denoise step plans (Euler fused), per latent parity
-  std::vector<Op>* building_ = nullptr;
   cudaGraphExec_t graph_fwd_ = nullptr, graph_step_[2] = {nullptr, nullptr};
-  bool profiling_ = false;
   // Dequantisation fused into the GEMM (weights packed at load) when
   // DCPP_FUSED_DEQUANT=1.  The default expands each quantised projection to
   // bf16 right before its GEMM, which measured faster for these 4608-row
   // GEMMs (the fused kernels are bound by shared-memory traffic).
   bool fused_dequant_ = false;
-  std::vector<Op>* last_ops_ = nullptr;
-  std::vector<cudaEvent_t> ev_;  // 2 per op of the largest plan
-  int64_t launches_per_step_ = 0;
 };
 
 // FlowMatchEulerDiscreteScheduler (default: shift 1, no dynamic shifting,

@@ -83,16 +83,18 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       if (c0 >= p.N) break;
       const uint32_t hbase = taddr + half * 128;
       if (c0 < e.qkv_cols) {
-        const int region = c0 / e.inner;  // 0 q, 1 k, 2 v
-        const int head = (c0 - region * e.inner) >> 7;
+        const int kvi = e.kv_inner ? e.kv_inner : e.inner;
+        const int hkv = e.heads_kv ? e.heads_kv : e.heads;
+        const int region = c0 < e.inner ? 0 : (c0 < e.inner + kvi ? 1 : 2);  // q, k, v
+        const int head = (c0 - (region == 0 ? 0 : (region == 1 ? e.inner : e.inner + kvi))) >> 7;
+        const int nh = region == 0 ? e.heads : hkv;
         uint16_t* dst_base = region == 0 ? e.q_out : (region == 1 ? e.k_out : e.v_out);
-        const int64_t dst_row =
-            ((static_cast<int64_t>(G.batch) * e.heads + head) * e.seq + tok) * 128;
+        const int64_t dst_row = ((static_cast<int64_t>(G.batch) * nh + head) * e.seq + tok) * 128;
         if (region == 2) {
-          // V is stored transposed, [B, H, 128, vt_stride]: the attention's
+          // V is stored transposed, [B, H_kv, 128, vt_stride]: the attention's
           // P.V MMA then reads a K-major operand.  Lanes hold consecutive
           // tokens, so each 2-byte store of the warp covers 64 contiguous bytes.
-          uint16_t* vt = e.v_out + (static_cast<int64_t>(G.batch) * e.heads + head) * 128 * e.vt_stride + tok;
+          uint16_t* vt = e.v_out + (static_cast<int64_t>(G.batch) * nh + head) * 128 * e.vt_stride + tok;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
@@ -124,6 +126,43 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
           const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + e.eps);
           const float* w = region == 0 ? e.norm_q[sel] : e.norm_k[sel];
           const float2* rp = e.rope + static_cast<int64_t>(tok) * 64;
+          if (e.rope_neox) {
+            // RoPE NEOX (ggml GGML_ROPE_TYPE_NEOX, Qwen3RotaryEmbedding.cpp:15-33):
+            // channel d rotates with d + 64 by the angle of pair d.
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t a[32], b[32];
+              tmem_ld32(hbase + c * 32, a);
+              tmem_ld32(hbase + (c + 2) * 32, b);
+              tmem_ld_wait();
+              if (row_ok) {
+                uint32_t olo[16], ohi[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  float ylo[2], yhi[2];
+#pragma unroll
+                  for (int t = 0; t < 2; ++t) {
+                    const int d = c * 32 + 2 * j + t;
+                    const float xa = __uint_as_float(a[2 * j + t]) * rs * __ldg(w + d);
+                    const float xb = __uint_as_float(b[2 * j + t]) * rs * __ldg(w + d + 64);
+                    const float2 cs = __ldg(rp + d);
+                    ylo[t] = xa * cs.x - xb * cs.y;
+                    yhi[t] = xb * cs.x + xa * cs.y;
+                  }
+                  olo[j] = pack_bf16x2(ylo[0], ylo[1]);
+                  ohi[j] = pack_bf16x2(yhi[0], yhi[1]);
+                }
+                uint4* dlo = reinterpret_cast<uint4*>(dst_base + dst_row + c * 32);
+                uint4* dhi = reinterpret_cast<uint4*>(dst_base + dst_row + (c + 2) * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  dlo[v] = make_uint4(olo[4 * v], olo[4 * v + 1], olo[4 * v + 2], olo[4 * v + 3]);
+                  dhi[v] = make_uint4(ohi[4 * v], ohi[4 * v + 1], ohi[4 * v + 2], ohi[4 * v + 3]);
+                }
+              }
+            }
+            continue;
+          }
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];

@@ -55,17 +55,20 @@ struct EpilogueArgs {
   const float* gate[2];      // per selector: gate vector [N] (batch stride gate_bstride)
   int64_t gate_bstride;
   // kEpiQkvMlp
-  int32_t qkv_cols;          // columns holding q|k|v (3 * local inner dim); 0 = mlp only
-  int32_t inner;             // local inner dim (heads_local * 128)
+  int32_t qkv_cols;          // columns holding q|k|v (inner + 2 * kv_inner); 0 = mlp only
+  int32_t inner;             // local q dim (heads_local * 128)
+  int32_t kv_inner;          // local k / v dim (heads_kv * 128); 0: = inner
   int32_t seq;               // tokens per batch element (S)
-  int32_t heads;             // local heads
+  int32_t heads;             // local q heads
+  int32_t heads_kv;          // local k / v heads (grouped-query attention); 0: = heads
+  int32_t rope_neox;         // 0: rotate adjacent pairs (2i, 2i+1); 1: rotate (i, i + 64)
   const float* norm_q[2];    // per selector RMSNorm weights [128]
   const float* norm_k[2];
   float eps;
   const float2* rope;        // [S, 64] (cos, sin) per token and rotary pair
   uint16_t* q_out;           // [B, H, S, 128]
-  uint16_t* k_out;
-  uint16_t* v_out;           // transposed: [B, H, 128, vt_stride]
+  uint16_t* k_out;           // [B, H_kv, S, 128]
+  uint16_t* v_out;           // transposed: [B, H_kv, 128, vt_stride]
   int64_t vt_stride;         // keys per V^T row (S rounded up to 64)
   uint16_t* mlp_out;         // SwiGLU output, row stride ld_mlp
   int64_t ld_mlp;

@@ -54,7 +54,18 @@ struct NormArgs {
   int64_t slot_row0;
   int32_t n_peer_out;
   uint16_t* y_peer[7];
+  // RMSNorm form (rms != 0): no mean subtraction, y = weight * x / rms(x)
+  // (weight may be null); the segments' shift / scale are not used.
+  int32_t rms;
+  const float* weight;
+  float* y_f32;         // optional f32 copy of the output (row stride ld_y)
 };
+
+// out[i, :] = dequantised row ids[i] of table [n_rows, dim] (ggml_get_rows,
+// Embedding::forward).  An id outside [0, n_rows) gives a zero row and
+// records kDevBadIndex in err.
+cudaError_t launch_get_rows(int type, const void* table, int64_t n_rows, int64_t dim, const int32_t* ids,
+                            int64_t n_ids, float* out, int* err, cudaStream_t s);
 
 // Cross-GPU barrier of a tensor-parallel group.  flags[j] is rank j's flag
 // array (mapped from its GPU), one uint32 per source rank; each barrier

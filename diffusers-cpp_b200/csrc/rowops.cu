@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
     if (threadIdx.x == 0) stat = s / static_cast<float>(D);
   }
   __syncthreads();
-  const float mean = stat;
+  const float mean = a.rms ? 0.f : stat;  // RMSNorm: no centring
   float sq = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
@@ -132,10 +132,20 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
 #pragma unroll
       for (int f = 0; f < kF4; ++f) {
         const float4 t = v[i][f];
-        const float4 sh = sh4 ? __ldg(sh4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 sc = sc4 ? __ldg(sc4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-        pk[2 * f] = pack_bf16x2((1.0f + sc.x) * (t.x * rstd) + sh.x, (1.0f + sc.y) * (t.y * rstd) + sh.y);
-        pk[2 * f + 1] = pack_bf16x2((1.0f + sc.z) * (t.z * rstd) + sh.z, (1.0f + sc.w) * (t.w * rstd) + sh.w);
+        float4 o;
+        if (a.rms) {  // Qwen3RMSNorm.cpp:11-19: weight * (x * rsqrt(mean(x^2) + eps))
+          const float4 w = a.weight ? __ldg(reinterpret_cast<const float4*>(a.weight) + idx * kF4 + f)
+                                    : make_float4(1.f, 1.f, 1.f, 1.f);
+          o = make_float4(w.x * (t.x * rstd), w.y * (t.y * rstd), w.z * (t.z * rstd), w.w * (t.w * rstd));
+        } else {
+          const float4 sh = sh4 ? __ldg(sh4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 sc = sc4 ? __ldg(sc4 + idx * kF4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+          o = make_float4((1.0f + sc.x) * (t.x * rstd) + sh.x, (1.0f + sc.y) * (t.y * rstd) + sh.y,
+                          (1.0f + sc.z) * (t.z * rstd) + sh.z, (1.0f + sc.w) * (t.w * rstd) + sh.w);
+        }
+        if (a.y_f32) reinterpret_cast<float4*>(a.y_f32 + dst * a.ld_y)[idx * kF4 + f] = o;
+        pk[2 * f] = pack_bf16x2(o.x, o.y);
+        pk[2 * f + 1] = pack_bf16x2(o.z, o.w);
       }
       OutT o;
       if constexpr (kW == 8) o = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -528,6 +538,50 @@ __global__ void __launch_bounds__(256) gemv_unit_kernel(const uint8_t* __restric
   }
 }
 
+// Embedding row gather with dequantisation (ggml_get_rows on Q8_0 / Q4_K /
+// F16 / BF16 / F32 tables; Embedding::forward).  One CTA per id.
+__global__ void __launch_bounds__(256) get_rows_kernel(int type, const uint8_t* __restrict__ table, int64_t n_rows,
+                                                       int64_t dim, const int32_t* __restrict__ ids,
+                                                       float* __restrict__ out, int* err) {
+  const int64_t i = blockIdx.x;
+  const int32_t id = ids[i];
+  float* o = out + i * dim;
+  if (id < 0 || id >= n_rows) {
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) o[c] = 0.f;
+    if (threadIdx.x == 0 && err) atomicCAS(err, 0, kDevBadIndex);
+    return;
+  }
+  if (type == kTypeQ8_0) {
+    const uint8_t* row = table + static_cast<int64_t>(id) * (dim / 32) * 34;
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) {
+      const uint8_t* blk = row + (c / 32) * 34;
+      const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
+      o[c] = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + (c & 31)])), d);
+    }
+  } else if (type == kTypeQ4_K) {
+    const uint8_t* row = table + static_cast<int64_t>(id) * (dim / 256) * 144;
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) {
+      const uint8_t* blk = row + (c / 256) * 144;
+      const int e = static_cast<int>(c & 255), j = e / 32, l = e & 31;
+      const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
+      const float dmin = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[2] | (blk[3] << 8))));
+      int sc, m;
+      q4k_scale_min(j, blk + 4, sc, m);
+      const float q = static_cast<float>((blk[16 + (j >> 1) * 32 + l] >> ((j & 1) * 4)) & 0xF);
+      o[c] = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), q), __fmul_rn(dmin, static_cast<float>(m)));
+    }
+  } else if (type == kTypeF32) {
+    const float* row = reinterpret_cast<const float*>(table) + static_cast<int64_t>(id) * dim;
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) o[c] = row[c];
+  } else {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(table) + static_cast<int64_t>(id) * dim;
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) {
+      const uint16_t h = row[c];
+      o[c] = type == kTypeBF16 ? __uint_as_float(static_cast<uint32_t>(h) << 16) : __half2float(__ushort_as_half(h));
+    }
+  }
+}
+
 __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
   int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -559,6 +613,18 @@ cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
     else
       layernorm_mod_kernel<256, 8, 4><<<grid, 256, 0, s>>>(a);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_get_rows(int type, const void* table, int64_t n_rows, int64_t dim, const int32_t* ids,
+                            int64_t n_ids, float* out, int* err, cudaStream_t s) {
+  if (n_ids <= 0) return cudaSuccess;
+  if (!table || !ids || !out || n_rows <= 0 || dim <= 0) return cudaErrorInvalidValue;
+  if ((type == kTypeQ8_0 && dim % 32) || (type == kTypeQ4_K && dim % 256)) return cudaErrorInvalidValue;
+  if (type != kTypeQ8_0 && type != kTypeQ4_K && type != kTypeF32 && type != kTypeF16 && type != kTypeBF16)
+    return cudaErrorNotSupported;
+  get_rows_kernel<<<static_cast<unsigned>(n_ids), 256, 0, s>>>(type, static_cast<const uint8_t*>(table), n_rows, dim,
+                                                                ids, out, err);
   return cudaGetLastError();
 }
 

@@ -131,6 +131,7 @@ const char* device_error_name(int code) {
     case kDevBadShape: return "kernel launched with an unsupported shape";
     case kDevTimeoutAttn: return "attention pipeline wait timed out";
     case kDevTimeoutPeer: return "tensor-parallel barrier timed out waiting for a peer GPU";
+    case kDevBadIndex: return "token id outside the embedding table";
     default: return "unknown device error";
   }
 }
@@ -141,7 +142,7 @@ void Ctx::check_device_error() {
   cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
   if (h != 0) {
     cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "clear error word");
-    fail(h == kDevBadShape ? DCPP_ERR_UNSUPPORTED : DCPP_ERR_TIMEOUT,
+    fail(h == kDevBadShape ? DCPP_ERR_UNSUPPORTED : (h == kDevBadIndex ? DCPP_ERR_INVALID_ARG : DCPP_ERR_TIMEOUT),
          std::string("device error ") + std::to_string(h) + ": " + device_error_name(h));
   }
 }
