@@ -60,6 +60,20 @@ class Flux2ConfigC(ctypes.Structure):
     ]
 
 
+class Qwen3ConfigC(ctypes.Structure):
+    _fields_ = [
+        ("vocab_size", ctypes.c_int64),
+        ("hidden_size", ctypes.c_int64),
+        ("intermediate_size", ctypes.c_int64),
+        ("num_hidden_layers", ctypes.c_int64),
+        ("num_attention_heads", ctypes.c_int64),
+        ("num_key_value_heads", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("rms_norm_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "dcpp_version": (ctypes.c_char_p, []),
@@ -111,6 +125,19 @@ _SIGNATURES = {
     "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
     "dcpp_flux2_set_tensor_parallel": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
     "dcpp_flux2_create_host": (ctypes.c_int, [ctypes.POINTER(Flux2ConfigC), ctypes.POINTER(_vp)]),
+    "dcpp_qwen3_config_default": (None, [ctypes.POINTER(Qwen3ConfigC)]),
+    "dcpp_qwen3_config_from_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(Qwen3ConfigC)]),
+    "dcpp_qwen3_create": (ctypes.c_int, [_vp, ctypes.POINTER(Qwen3ConfigC), ctypes.POINTER(_vp)]),
+    "dcpp_qwen3_destroy": (ctypes.c_int, [_vp]),
+    "dcpp_qwen3_set_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _c_i64p, _vp, ctypes.c_size_t]),
+    "dcpp_qwen3_missing": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t]),
+    "dcpp_qwen3_prepare": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                          ctypes.c_int]),
+    "dcpp_qwen3_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    "dcpp_qwen3_set_profiling": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "dcpp_qwen3_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_double), _c_i64p]),
+    "dcpp_qwen3_launches_per_step": (ctypes.c_int, [_vp, _c_i64p]),
     "dcpp_flux2_last_error": (ctypes.c_char_p, [_vp]),
     "dcpp_flux2_read_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), _c_i64p, _c_i64p, _vp,
                                              ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
@@ -403,3 +430,80 @@ def flow_match_schedule(n: int, shift: float = 1.0):
     if st != DCPP_OK:
         raise DcppError(st, "flow_match_schedule")
     return ts, sg
+
+
+def qwen3_config_to_c(cfg) -> Qwen3ConfigC:
+    c = Qwen3ConfigC()
+    lib().dcpp_qwen3_config_default(ctypes.byref(c))
+    for k in ("vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
+              "num_key_value_heads", "head_dim"):
+        setattr(c, k, int(getattr(cfg, k)))
+    c.rms_norm_eps = float(cfg.rms_norm_eps)
+    c.rope_theta = float(cfg.rope_theta)
+    return c
+
+
+class Qwen3Model:
+    """dcpp_qwen3: the Qwen3 text-encoder prefill (Qwen3Model::forward) on one GPU."""
+
+    def __init__(self, ctx: Context, cfg):
+        self.ctx = ctx
+        self.cfg = cfg
+        c = qwen3_config_to_c(cfg)
+        h = _vp()
+        ctx.check(lib().dcpp_qwen3_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "qwen3_create")
+        ctx._children.add(self)
+        self.h = h
+        self.n_taps = 0
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dcpp_qwen3_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_param(self, name: str, gtype: int, shape: Sequence[int], data):
+        if hasattr(data, "numpy"):
+            data = data.contiguous().cpu().numpy()
+        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
+        shp = (ctypes.c_int64 * len(shape))(*shape)
+        self.ctx.check(lib().dcpp_qwen3_set_param(self.h, name.encode(), gtype, len(shape), shp, arr.ctypes.data,
+                                                  arr.nbytes), f"set_param({name})")
+
+    def load_params(self, params):
+        for name, (gtype, shape, data) in params.items():
+            self.set_param(name, gtype, shape, data)
+
+    def missing(self):
+        n = ctypes.c_int()
+        buf = ctypes.create_string_buffer(512)
+        self.ctx.check(lib().dcpp_qwen3_missing(self.h, ctypes.byref(n), buf, 512), "missing")
+        return n.value, buf.value.decode()
+
+    def prepare(self, batch: int, seq: int, taps: Sequence[int] = (), use_graph: bool = True):
+        arr = (ctypes.c_int * max(len(taps), 1))(*taps)
+        self.ctx.check(lib().dcpp_qwen3_prepare(self.h, batch, seq, len(taps), arr, 1 if use_graph else 0), "prepare")
+        self.n_taps = len(taps)
+
+    def forward(self, input_ids, last_hidden=None, taps=None):
+        """input_ids [B, S] int32; last_hidden [B, S, D] f32; taps [B, S, n_taps * D] f32."""
+        self.ctx.check(lib().dcpp_qwen3_forward(self.h, _ptr(input_ids), _ptr(last_hidden), _ptr(taps)), "forward")
+
+    def set_profiling(self, on: bool):
+        self.ctx.check(lib().dcpp_qwen3_set_profiling(self.h, 1 if on else 0), "set_profiling")
+
+    def profile(self, kind: str):
+        ms, fl, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+        self.ctx.check(lib().dcpp_qwen3_profile(self.h, Flux2Model.PROFILE_KINDS[kind], ctypes.byref(ms),
+                                                ctypes.byref(fl), ctypes.byref(n)), "profile")
+        return ms.value, fl.value, n.value
+
+    def launches_per_step(self) -> int:
+        v = ctypes.c_int64()
+        self.ctx.check(lib().dcpp_qwen3_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
+        return v.value

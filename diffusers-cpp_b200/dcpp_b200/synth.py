@@ -159,3 +159,65 @@ def make_inputs(cfg: Flux2Cfg, batch: int, grid_h: int, grid_w: int, n_txt: int,
         img_ids[:, 2] = xs.reshape(-1).int()
     txt_ids[:, n_axes - 1] = torch.arange(n_txt, dtype=torch.int32)
     return hidden, encoder, img_ids.to(device), txt_ids.to(device)
+
+
+# --------------------------------------------------------------------------- Qwen3 text encoder
+@dataclass
+class Qwen3Cfg:
+    """Same fields as Qwen3Config (the prefill's subset); defaults: the text
+    encoder of the reference benchmark's Qwen3 prefill configuration."""
+    vocab_size: int = 151936
+    hidden_size: int = 2560
+    intermediate_size: int = 9728
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+
+
+def qwen3_param_shapes(cfg: Qwen3Cfg):
+    D, I = cfg.hidden_size, cfg.intermediate_size
+    Dq, Dkv = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+    s = {"model.embed_tokens.weight": (cfg.vocab_size, D), "model.norm.weight": (D,)}
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        s[p + "self_attn.q_proj.weight"] = (Dq, D)
+        s[p + "self_attn.k_proj.weight"] = (Dkv, D)
+        s[p + "self_attn.v_proj.weight"] = (Dkv, D)
+        s[p + "self_attn.o_proj.weight"] = (D, Dq)
+        s[p + "self_attn.q_norm.weight"] = (cfg.head_dim,)
+        s[p + "self_attn.k_norm.weight"] = (cfg.head_dim,)
+        s[p + "mlp.gate_proj.weight"] = (I, D)
+        s[p + "mlp.up_proj.weight"] = (I, D)
+        s[p + "mlp.down_proj.weight"] = (D, I)
+        s[p + "input_layernorm.weight"] = (D,)
+        s[p + "post_attention_layernorm.weight"] = (D,)
+    return s
+
+
+def make_qwen3_params(cfg: Qwen3Cfg, wtype: int = TYPE_Q8_0, seed: int = 0, device: str = "cpu",
+                      to_cpu: bool = True):
+    """Dict name -> (ggml type, shape, uint8 tensor): matrices N(0, 0.02)
+    quantised to `wtype`, norm weights 1 + 0.1 N(0, 1) in F32."""
+    out = {}
+    for name, shape in qwen3_param_shapes(cfg).items():
+        g = torch.Generator(device=device)
+        g.manual_seed(tensor_seed(seed, name))
+        if len(shape) == 1:
+            w = 1.0 + 0.1 * torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+            t = TYPE_F32
+        else:
+            w = 0.02 * torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+            t = wtype
+        q = quantize(w, t).contiguous()
+        out[name] = (t, tuple(shape), q.cpu() if to_cpu else q)
+    return out
+
+
+def make_qwen3_ids(cfg: Qwen3Cfg, batch: int, seq: int, seed: int = 1):
+    """Token ids [batch, seq] int32, uniform in [0, vocab_size)."""
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return torch.randint(0, cfg.vocab_size, (batch, seq), generator=g, dtype=torch.int64).to(torch.int32)

@@ -342,6 +342,67 @@ const char* dcpp_flux2_last_error(dcpp_flux2* model);
 dcpp_status dcpp_flux2_read_param(dcpp_flux2* model, const char* name, int* type, int64_t* rows,
                                   int64_t* cols, void* dst, size_t cap, size_t* nbytes);
 
+/* ---------------------------------------------------------------------- */
+/* Qwen3 text-encoder prefill (the Flux2 Klein pipeline's prompt encoder)  */
+/* ---------------------------------------------------------------------- */
+
+/* Qwen3Config (src/transformers/models/qwen3/Qwen3Config.hpp) fields used
+ * by the prefill. */
+typedef struct dcpp_qwen3_config {
+    int64_t vocab_size;             /* 151936 */
+    int64_t hidden_size;            /* 2560   */
+    int64_t intermediate_size;      /* 9728   */
+    int64_t num_hidden_layers;      /* 36     */
+    int64_t num_attention_heads;    /* 32     */
+    int64_t num_key_value_heads;    /* 8      */
+    int64_t head_dim;               /* 128 (the only value supported) */
+    float rms_norm_eps;             /* 1e-6   */
+    float rope_theta;               /* 1e6    */
+} dcpp_qwen3_config;
+
+typedef struct dcpp_qwen3 dcpp_qwen3;
+
+/* Defaults of the text encoder the Flux2 Klein pipeline loads (the
+ * reference benchmark's Qwen3 prefill configuration). */
+void dcpp_qwen3_config_default(dcpp_qwen3_config* cfg);
+/* Parse a transformers config.json (Qwen3Config::from_file,
+ * Qwen3Config.cpp:26-68); defaults kept for missing keys. */
+dcpp_status dcpp_qwen3_config_from_file(const char* path, dcpp_qwen3_config* cfg);
+
+/* Build the module tree (Qwen3Model.cpp:11-34). */
+dcpp_status dcpp_qwen3_create(dcpp_ctx* ctx, const dcpp_qwen3_config* cfg, dcpp_qwen3** out_model);
+dcpp_status dcpp_qwen3_destroy(dcpp_qwen3* model);
+
+/* Bind one parameter by its GGUF / module-path name, with or without the
+ * "model." prefix of Qwen3ForCausalLM (e.g. "model.layers.3.mlp.up_proj.weight",
+ * "model.embed_tokens.weight", "model.norm.weight"); "lm_head.weight" is
+ * accepted and ignored (the prefill returns hidden states).  Linear and
+ * embedding weights: Q8_0, Q4_K, F16, BF16 or F32; norm weights F32 / F16 /
+ * BF16. */
+dcpp_status dcpp_qwen3_set_param(dcpp_qwen3* model, const char* name, int type, int n_dims, const int64_t* shape,
+                                 const void* p_data, size_t nbytes);
+dcpp_status dcpp_qwen3_missing(dcpp_qwen3* model, int* count, char* first_missing, size_t cap);
+
+/* Plan a prefill of `batch` prompts of `seq` tokens.  tap_layers[n_taps]:
+ * layer indices t in [0, num_hidden_layers] whose input hidden states
+ * (t = num_hidden_layers: the final normed output) the forward returns,
+ * stacked along the feature axis (the pipeline taps 9, 18, 27,
+ * Flux2KleinPipeline.cpp:481-491). */
+dcpp_status dcpp_qwen3_prepare(dcpp_qwen3* model, int64_t batch, int64_t seq, int n_taps, const int* tap_layers,
+                               int use_graph);
+
+/* Qwen3Model::forward (Qwen3Model.cpp:99-208) over input_ids [B, S]
+ * (int32, positions 0..S-1, causal attention, no padding mask):
+ * last_hidden [B, S, hidden] f32 after the final RMSNorm (may be NULL),
+ * taps [B, S, n_taps * hidden] f32 (may be NULL).  Host or device pointers.
+ * Ids outside the vocabulary give DCPP_ERR_INVALID_ARG. */
+dcpp_status dcpp_qwen3_forward(dcpp_qwen3* model, const int32_t* p_input_ids, float* p_last_hidden, float* p_taps);
+
+/* Profiling of the prefill plan, as dcpp_flux2_set_profiling / _profile. */
+dcpp_status dcpp_qwen3_set_profiling(dcpp_qwen3* model, int on);
+dcpp_status dcpp_qwen3_profile(dcpp_qwen3* model, int kind, double* ms, double* flops, int64_t* launches);
+dcpp_status dcpp_qwen3_launches_per_step(dcpp_qwen3* model, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif
