@@ -121,6 +121,18 @@ __device__ __forceinline__ uint64_t ex2_poly2(uint64_t x) {
   return (static_cast<uint64_t>(hi) << 32) | lo;
 }
 
+// Key padding mask of a 128-key tile: four 32-bit words per batch row.
+__device__ __forceinline__ void apply_key_bits(const AttnTcArgs& p, int b, int kbase, float (&s)[128]) {
+  const uint32_t* w = p.key_bits + static_cast<int64_t>(b) * p.key_words + (kbase >> 5);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t bits = ((kbase >> 5) + q < p.key_words) ? __ldg(w + q) : 0u;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (!((bits >> i) & 1u)) s[q * 32 + i] = -INFINITY;
+  }
+}
+
 // Softmax numerators of one row's n scores (n % 8 == 0) against the running
 // maximum: row max with three-input max in 8 chains, then for each pair
 // x = s * c - m (packed FMA), 2^x on MUFU (three pairs in four) or the FMA
@@ -310,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (kbase + i > qrow) s[i] = -INFINITY;
       }
+      if (p.key_bits) apply_key_bits(p, bh / p.H, kbase, s);
       float m_use, alpha, sum;
       bool grow;
       uint32_t pk[64];
@@ -554,6 +567,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
         for (int i = 0; i < 128; ++i)
           if (kbase + i > qrow) sv[i] = -INFINITY;
       }
+      if (p.key_bits) apply_key_bits(p, bh / p.H, kbase, sv);
       float m_use, alpha, sum;
       bool grow;
       uint32_t pk[64];

@@ -16,6 +16,10 @@ struct AttnTcArgs {
   int32_t kernel;  // 0 auto, 1 one query tile per CTA, 2 two query tiles per CTA
   int32_t causal;  // 1: key j attends to query i only if j <= i
   int32_t H_kv;    // key / value heads (grouped-query attention: H % H_kv == 0); 0: = H
+  // Optional key padding mask: bit (k % 32) of key_bits[b * key_words + k / 32]
+  // set = key k of batch element b is attended; clear = masked (-inf).
+  const uint32_t* key_bits;
+  int32_t key_words;
 };
 
 struct AttnTcMaps {

@@ -67,6 +67,11 @@ struct NormArgs {
 cudaError_t launch_get_rows(int type, const void* table, int64_t n_rows, int64_t dim, const int32_t* ids,
                             int64_t n_ids, float* out, int* err, cudaStream_t s);
 
+// Attention mask [B, S] (nonzero = attend, as the reference's float mask)
+// -> bits [B, words] (bit k % 32 of word k / 32); words >= ceil(S / 32),
+// the tail bits are clear.
+cudaError_t launch_mask_bits(const float* mask, int64_t B, int64_t S, int64_t words, uint32_t* bits, cudaStream_t s);
+
 // Cross-GPU barrier of a tensor-parallel group.  flags[j] is rank j's flag
 // array (mapped from its GPU), one uint32 per source rank; each barrier
 // bumps the local epoch, writes it into every rank's flags[.][rank] and waits

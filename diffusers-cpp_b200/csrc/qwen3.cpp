@@ -203,6 +203,8 @@ void Qwen3Model::free_plan() {
   graph_ = nullptr;
   for (void* p : allocs_) cudaFree(p);
   allocs_.clear();
+  if (ones_host_) cudaFreeHost(ones_host_);
+  ones_host_ = nullptr;
   ops_.clear();
   last_ops_ = nullptr;
   release_plan_events();
@@ -262,6 +264,11 @@ void Qwen3Model::build_plan() {
     cuda_check(cudaMemcpy(pos_dev_, pos.data(), S * 4, cudaMemcpyHostToDevice), "positions");
   }
   rope_ = static_cast<float2*>(alloc(S * 64 * sizeof(float2)));
+  const int64_t words = (S + 31) / 32;
+  mask_dev_ = static_cast<float*>(alloc(R * 4));
+  mask_bits_ = static_cast<uint32_t*>(alloc(B * words * 4));
+  cuda_check(cudaMallocHost(&ones_host_, R * 4), "pinned ones");
+  for (int64_t i = 0; i < R; ++i) ones_host_[i] = 1.0f;
   size_t s0 = 0;
   for (auto& L : layers_)
     for (const DevWeight* w : {&L.qkv, &L.o, &L.gate_up, &L.down})
@@ -278,6 +285,16 @@ void Qwen3Model::build_plan() {
                     cuda_check(launch_rope_table(pos, S, 1, axes, theta, rope, s), "rope_table");
                   },
                   1, kOpOther, 0.0, "rope_table"});
+  // Key padding bits from the call's attention mask (Qwen3Model.cpp:78-94 adds
+  // (1 - mask) * -1e9, which the f16 mask turns into -inf).
+  {
+    const float* mk = mask_dev_;
+    uint32_t* bits = mask_bits_;
+    ops_.push_back({[mk, bits, B, S, words](cudaStream_t s) {
+                      cuda_check(launch_mask_bits(mk, B, S, words, bits, s), "mask bits");
+                    },
+                    1, kOpOther, 0.0, "mask_bits"});
+  }
   // Embedding::forward (ggml_get_rows).
   {
     const DevWeight* e = &embed_;
@@ -336,6 +353,8 @@ void Qwen3Model::build_plan() {
   at.kernel = ctx_.attn_kernel;
   at.causal = 1;
   at.H_kv = static_cast<int32_t>(Hkv);
+  at.key_bits = mask_bits_;
+  at.key_words = static_cast<int32_t>(words);
   auto maps = std::make_shared<AttnTcMaps>();
   cuda_check(make_attn_maps(maps.get(), q_, k_, v_, static_cast<int>(B), static_cast<int>(Hq), static_cast<int>(S),
                             static_cast<int>(Hkv)),
@@ -387,11 +406,14 @@ void Qwen3Model::build_plan() {
   for (auto& o : ops_) launches_per_step_ += o.launches;
 }
 
-void Qwen3Model::forward(const int32_t* input_ids, float* last_hidden, float* taps_out) {
+void Qwen3Model::forward(const int32_t* input_ids, const float* attention_mask, float* last_hidden, float* taps_out) {
   if (!planned_) fail(DCPP_ERR_STATE, "forward before prepare");
   if (!input_ids) fail(DCPP_ERR_INVALID_ARG, "forward: null input_ids");
   const int64_t R = B_ * S_, D = cfg_.hidden_size;
   cuda_check(cudaMemcpyAsync(ids_dev_, input_ids, R * 4, cudaMemcpyDefault, ctx_.stream), "copy ids");
+  cuda_check(cudaMemcpyAsync(mask_dev_, attention_mask ? attention_mask : ones_host_, R * 4, cudaMemcpyDefault,
+                             ctx_.stream),
+             "copy mask");
   run_ops(ops_, &graph_);
   if (last_hidden)
     cuda_check(cudaMemcpyAsync(last_hidden, last_, R * D * 4, cudaMemcpyDefault, ctx_.stream), "copy hidden");
@@ -513,9 +535,10 @@ dcpp_status dcpp_qwen3_prepare(dcpp_qwen3* m, int64_t batch, int64_t seq, int n_
   });
 }
 
-dcpp_status dcpp_qwen3_forward(dcpp_qwen3* m, const int32_t* ids, float* last_hidden, float* taps) {
+dcpp_status dcpp_qwen3_forward(dcpp_qwen3* m, const int32_t* ids, const float* attention_mask, float* last_hidden,
+                               float* taps) {
   return qwen_call(m, "dcpp_qwen3_forward",
-                   [&](dcpp::Qwen3Model& mm) { mm.forward(ids, last_hidden, taps); });
+                   [&](dcpp::Qwen3Model& mm) { mm.forward(ids, attention_mask, last_hidden, taps); });
 }
 
 dcpp_status dcpp_qwen3_set_profiling(dcpp_qwen3* m, int on) {

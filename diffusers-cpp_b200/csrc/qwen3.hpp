@@ -7,7 +7,7 @@
 //   Qwen3DecoderLayer / Qwen3Attention / Qwen3MLP / Qwen3RMSNorm / Qwen3RotaryEmbedding
 // Parameters bind by GGUF name ("model.layers.3.self_attn.q_proj.weight", or
 // without the "model." prefix).  Prefill only: causal self-attention over the
-// whole prompt, no KV cache, no padding mask.
+// whole prompt with an optional key padding mask, no KV cache.
 #pragma once
 
 #include <cuda.h>
@@ -54,9 +54,10 @@ class Qwen3Model : public StepPlanner {
   // states (t = num_hidden_layers: the final normed output) forward()
   // returns stacked along the feature axis.
   void prepare(int64_t batch, int64_t seq, const std::vector<int>& taps, bool use_graph);
-  // input_ids [B, S] int32; last_hidden [B, S, D] f32 (final RMSNorm) or
-  // null; taps_out [B, S, n_taps * D] f32 or null.  Host or device pointers.
-  void forward(const int32_t* input_ids, float* last_hidden, float* taps_out);
+  // input_ids [B, S] int32; attention_mask [B, S] f32 (nonzero = attend,
+  // zero = padding key) or null; last_hidden [B, S, D] f32 (final RMSNorm)
+  // or null; taps_out [B, S, n_taps * D] f32 or null.  Host or device pointers.
+  void forward(const int32_t* input_ids, const float* attention_mask, float* last_hidden, float* taps_out);
   void set_profiling(bool on);
 
  private:
@@ -85,6 +86,9 @@ class Qwen3Model : public StepPlanner {
   float *h_ = nullptr, *last_ = nullptr, *taps_dev_ = nullptr;
   uint16_t *a_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *att_ = nullptr, *mlp_ = nullptr;
   int32_t *ids_dev_ = nullptr, *pos_dev_ = nullptr;
+  float* mask_dev_ = nullptr;       // [B, S] attention mask of the call
+  uint32_t* mask_bits_ = nullptr;   // [B, words] key bits the attention reads
+  float* ones_host_ = nullptr;      // pinned [B, S] of 1 (calls without a mask)
   float2* rope_ = nullptr;
   std::vector<Op> ops_;
   cudaGraphExec_t graph_ = nullptr;

@@ -582,6 +582,18 @@ __global__ void __launch_bounds__(256) get_rows_kernel(int type, const uint8_t* 
   }
 }
 
+__global__ void mask_bits_kernel(const float* __restrict__ mask, int64_t S, int64_t words, uint32_t* __restrict__ bits) {
+  const int64_t b = blockIdx.y;
+  const int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (w >= words) return;
+  uint32_t v = 0;
+  for (int i = 0; i < 32; ++i) {
+    const int64_t k = w * 32 + i;
+    if (k < S && mask[b * S + k] != 0.f) v |= 1u << i;
+  }
+  bits[b * words + w] = v;
+}
+
 __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
   int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -625,6 +637,14 @@ cudaError_t launch_get_rows(int type, const void* table, int64_t n_rows, int64_t
     return cudaErrorNotSupported;
   get_rows_kernel<<<static_cast<unsigned>(n_ids), 256, 0, s>>>(type, static_cast<const uint8_t*>(table), n_rows, dim,
                                                                 ids, out, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mask_bits(const float* mask, int64_t B, int64_t S, int64_t words, uint32_t* bits, cudaStream_t s) {
+  if (B <= 0 || S <= 0) return cudaSuccess;
+  if (!mask || !bits || words * 32 < S) return cudaErrorInvalidValue;
+  dim3 grid(static_cast<unsigned>((words + 127) / 128), static_cast<unsigned>(B));
+  mask_bits_kernel<<<grid, 128, 0, s>>>(mask, S, words, bits);
   return cudaGetLastError();
 }
 

@@ -133,7 +133,7 @@ _SIGNATURES = {
     "dcpp_qwen3_missing": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t]),
     "dcpp_qwen3_prepare": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                           ctypes.c_int]),
-    "dcpp_qwen3_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp]),
+    "dcpp_qwen3_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "dcpp_qwen3_set_profiling": (ctypes.c_int, [_vp, ctypes.c_int]),
     "dcpp_qwen3_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_double), _c_i64p]),
@@ -490,9 +490,11 @@ class Qwen3Model:
         self.ctx.check(lib().dcpp_qwen3_prepare(self.h, batch, seq, len(taps), arr, 1 if use_graph else 0), "prepare")
         self.n_taps = len(taps)
 
-    def forward(self, input_ids, last_hidden=None, taps=None):
-        """input_ids [B, S] int32; last_hidden [B, S, D] f32; taps [B, S, n_taps * D] f32."""
-        self.ctx.check(lib().dcpp_qwen3_forward(self.h, _ptr(input_ids), _ptr(last_hidden), _ptr(taps)), "forward")
+    def forward(self, input_ids, last_hidden=None, taps=None, attention_mask=None):
+        """input_ids [B, S] int32; attention_mask [B, S] f32 (1 attend, 0 padding)
+        or None; last_hidden [B, S, D] f32; taps [B, S, n_taps * D] f32."""
+        self.ctx.check(lib().dcpp_qwen3_forward(self.h, _ptr(input_ids), _ptr(attention_mask), _ptr(last_hidden),
+                                                _ptr(taps)), "forward")
 
     def set_profiling(self, on: bool):
         self.ctx.check(lib().dcpp_qwen3_set_profiling(self.h, 1 if on else 0), "set_profiling")

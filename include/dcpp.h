@@ -392,11 +392,13 @@ dcpp_status dcpp_qwen3_prepare(dcpp_qwen3* model, int64_t batch, int64_t seq, in
                                int use_graph);
 
 /* Qwen3Model::forward (Qwen3Model.cpp:99-208) over input_ids [B, S]
- * (int32, positions 0..S-1, causal attention, no padding mask):
- * last_hidden [B, S, hidden] f32 after the final RMSNorm (may be NULL),
- * taps [B, S, n_taps * hidden] f32 (may be NULL).  Host or device pointers.
- * Ids outside the vocabulary give DCPP_ERR_INVALID_ARG. */
-dcpp_status dcpp_qwen3_forward(dcpp_qwen3* model, const int32_t* p_input_ids, float* p_last_hidden, float* p_taps);
+ * (int32, positions 0..S-1, causal attention): attention_mask [B, S] f32
+ * (the tokenizer's mask: nonzero = attend, zero = padding key; NULL = all
+ * attend), last_hidden [B, S, hidden] f32 after the final RMSNorm (may be
+ * NULL), taps [B, S, n_taps * hidden] f32 (may be NULL).  Host or device
+ * pointers.  Ids outside the vocabulary give DCPP_ERR_INVALID_ARG. */
+dcpp_status dcpp_qwen3_forward(dcpp_qwen3* model, const int32_t* p_input_ids, const float* p_attention_mask,
+                               float* p_last_hidden, float* p_taps);
 
 /* Profiling of the prefill plan, as dcpp_flux2_set_profiling / _profile. */
 dcpp_status dcpp_qwen3_set_profiling(dcpp_qwen3* model, int on);

@@ -65,11 +65,16 @@ def rope_neox(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
     return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
 
 
-def causal_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-    """q [B, S, H, d], k / v [B, S, Hkv, d] -> [B, S, H, d]; key j <= query i."""
+def causal_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [B, S, H, d], k / v [B, S, Hkv, d] -> [B, S, H, d]; key j <= query i,
+    and (key_mask [B, S], zero = padding) padding keys masked with -inf (the
+    reference's (1 - mask) * -1e9 in an f16 mask, Qwen3Model.cpp:78-94)."""
     B, S, H, d = q.shape
     g = H // k.shape[2]
-    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), diagonal=1)
+    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), diagonal=1)[None]
+    if key_mask is not None:
+        mask = mask | (key_mask == 0)[:, None, :]
     out = torch.empty_like(q)
     for h in range(H):
         qh = q[:, :, h]
@@ -86,7 +91,7 @@ class Qwen3Oracle:
         self.w = Weights(params, dtype)
         self.dtype = dtype
 
-    def layer(self, i: int, h: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    def layer(self, i: int, h: torch.Tensor, pos: torch.Tensor, key_mask=None) -> torch.Tensor:
         c, w = self.cfg, self.w
         p = f"model.layers.{i}."
         B, S, _ = h.shape
@@ -96,14 +101,16 @@ class Qwen3Oracle:
         v = linear(x, w.get(p + "self_attn.v_proj.weight")).unflatten(-1, (c.num_key_value_heads, c.head_dim))
         q = rope_neox(rms_norm(q, w.get(p + "self_attn.q_norm.weight"), c.rms_norm_eps), pos, c.rope_theta)
         k = rope_neox(rms_norm(k, w.get(p + "self_attn.k_norm.weight"), c.rms_norm_eps), pos, c.rope_theta)
-        o = causal_sdpa(q, k, v).flatten(2)
+        o = causal_sdpa(q, k, v, key_mask).flatten(2)
         h = h + linear(o, w.get(p + "self_attn.o_proj.weight"))
         x = rms_norm(h, w.get(p + "post_attention_layernorm.weight"), c.rms_norm_eps)
         m = silu(linear(x, w.get(p + "mlp.gate_proj.weight"))) * linear(x, w.get(p + "mlp.up_proj.weight"))
         return h + linear(m, w.get(p + "mlp.down_proj.weight"))
 
-    def forward(self, input_ids: torch.Tensor, taps: Sequence[int] = (), n_layers: Optional[int] = None):
-        """input_ids [B, S] -> (last_hidden [B, S, D], {tap: hidden before layer tap}).
+    def forward(self, input_ids: torch.Tensor, taps: Sequence[int] = (), n_layers: Optional[int] = None,
+                attention_mask: Optional[torch.Tensor] = None):
+        """input_ids [B, S] -> (last_hidden [B, S, D], {tap: hidden before layer tap});
+        attention_mask [B, S] (zero = padding key) optional.
         n_layers limits the layers run (bounded CPU samples); the final norm
         is then applied to that layer's output."""
         c, w = self.cfg, self.w
@@ -116,7 +123,7 @@ class Qwen3Oracle:
         for i in range(nl):
             if i in taps:
                 got[i] = h.clone()
-            h = self.layer(i, h, pos)
+            h = self.layer(i, h, pos, attention_mask)
         h = rms_norm(h, w.get("model.norm.weight"), c.rms_norm_eps)
         if nl in taps:
             got[nl] = h.clone()

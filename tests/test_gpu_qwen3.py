@@ -62,6 +62,32 @@ def test_prefill_matches_oracle(ctx, attn):
     assert rel(tp[..., :D], ref_taps[0]) < 1e-7
 
 
+def test_prefill_right_padded_prompts_match_oracle(ctx):
+    """Prompts padded on the right (the tokenizer's mask): padding keys are
+    masked for every query."""
+    c = synth.Qwen3Cfg(vocab_size=500, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2)
+    B, S = 3, 200
+    lengths = (200, 131, 7)
+    m, params = build(ctx, c, seed=31, B=B, S=S, taps=(1,))
+    ids = synth.make_qwen3_ids(c, B, S, seed=32)
+    mask = torch.zeros(B, S)
+    for b, n in enumerate(lengths):
+        mask[b, :n] = 1
+    last = torch.empty(B, S, c.hidden_size)
+    tp = torch.empty(B, S, c.hidden_size)
+    m.forward(ids, last, tp, attention_mask=mask)
+    o = qo.Qwen3Oracle(qo.Qwen3Config(**c.__dict__), params)
+    ref, ref_t = o.forward(ids, taps=(1,), attention_mask=mask)
+    assert rel(last, ref) < H_TOL, rel(last, ref)
+    assert rel(tp, ref_t[1]) < H_TOL
+    # Without the mask the real tokens of a right-padded prompt are unchanged
+    # (causal: they never see the later padding).
+    m.forward(ids, last)
+    assert rel(last[1, :131], ref[1, :131]) < H_TOL
+    m.close()
+
+
 def test_prefill_golden_config_and_graph_eager_bitwise(ctx):
     g = np.load(__file__.replace("test_gpu_qwen3.py", "golden/qwen3_golden.npz"))
     keys = ("vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
