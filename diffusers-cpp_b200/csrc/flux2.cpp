@@ -1,6 +1,7 @@
 // Flux2 DiT denoise step on sm_100a: the C++ model host and its C ABI.
 #include "flux2.hpp"
 #include "attention_tc.cuh"
+#include "gguf.hpp"
 
 #include <cuda_fp16.h>
 
@@ -1325,6 +1326,58 @@ dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float
   } catch (const dcpp::Error& e) {
     return e.status;
   }
+}
+
+}  // extern "C"
+
+// GGUF checkpoints.
+extern "C" {
+
+dcpp_status dcpp_flux2_load_gguf(dcpp_flux2* m, const dcpp_gguf* f, int64_t* n_bound, int64_t* n_unused) {
+  return model_call(m, "dcpp_flux2_load_gguf", [&](dcpp::Flux2Transformer2DModel& mm) {
+    if (!f || !f->file) dcpp::fail(DCPP_ERR_INVALID_ARG, "load_gguf: null file");
+    int64_t unused = 0;
+    const int64_t bound = dcpp::gguf_bind_all(
+        *f->file,
+        [&](const std::string& name, int type, const std::vector<int64_t>& shape, const void* data, size_t nbytes) {
+          mm.set_param(name, type, shape, data, nbytes);
+        },
+        &unused);
+    if (n_bound) *n_bound = bound;
+    if (n_unused) *n_unused = unused;
+    const auto miss = mm.missing();
+    if (!miss.empty()) dcpp::fail(DCPP_ERR_NOT_FOUND, "Error while loading Tensor '" + miss.front() + "': Tensor not found");
+  });
+}
+
+dcpp_status dcpp_flux2_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_flux2** out) {
+  if (!ctx || !dir || !out) return DCPP_ERR_INVALID_ARG;
+  *out = nullptr;
+  dcpp_flux2_config cfg;
+  try {
+    dcpp::Flux2Config::from_file(std::string(dir) + "/config.json").to_c(cfg);
+  } catch (const dcpp::Error& e) {
+    ctx->last_error = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    ctx->last_error = e.what();
+    return DCPP_ERR_INVALID_ARG;
+  }
+  dcpp_gguf* g = nullptr;
+  char err[1024];
+  dcpp_status st = dcpp_gguf_open(dir, &g, err, sizeof(err));
+  if (st != DCPP_OK) {
+    ctx->last_error = err;
+    return st;
+  }
+  st = dcpp_flux2_create(ctx, &cfg, out);
+  if (st == DCPP_OK) st = dcpp_flux2_load_gguf(*out, g, nullptr, nullptr);
+  dcpp_gguf_close(g);
+  if (st != DCPP_OK && *out) {
+    dcpp_flux2_destroy(*out);
+    *out = nullptr;
+  }
+  return st;
 }
 
 }  // extern "C"

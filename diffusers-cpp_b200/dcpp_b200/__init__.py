@@ -139,6 +139,23 @@ _SIGNATURES = {
                                           ctypes.POINTER(ctypes.c_double), _c_i64p]),
     "dcpp_qwen3_launches_per_step": (ctypes.c_int, [_vp, _c_i64p]),
     "dcpp_flux2_last_error": (ctypes.c_char_p, [_vp]),
+    "dcpp_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.c_char_p, ctypes.c_size_t]),
+    "dcpp_gguf_close": (None, [_vp]),
+    "dcpp_gguf_info": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(ctypes.c_uint64), _c_i64p, _c_i64p]),
+    "dcpp_gguf_tensor": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_int),
+                                        ctypes.POINTER(ctypes.c_int), _c_i64p, ctypes.POINTER(ctypes.c_uint64),
+                                        ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_vp)]),
+    "dcpp_gguf_find_tensor": (ctypes.c_int64, [_vp, ctypes.c_char_p]),
+    "dcpp_gguf_kv": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_uint32),
+                                    ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint64)]),
+    "dcpp_gguf_get_int": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int64, _c_i64p]),
+    "dcpp_gguf_get_float": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_double)]),
+    "dcpp_gguf_get_string": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int64, ctypes.c_char_p, ctypes.c_size_t]),
+    "dcpp_flux2_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
+    "dcpp_qwen3_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
+    "dcpp_flux2_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "dcpp_qwen3_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "dcpp_flux2_read_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), _c_i64p, _c_i64p, _vp,
                                              ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
 }
@@ -337,6 +354,22 @@ class Flux2Model:
         if tp_size > 1:
             self._check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
 
+    @classmethod
+    def from_pretrained(cls, ctx: Context, path):
+        """config.json + the GGUF file of a transformer folder
+        (Flux2KleinPipeline::from_pretrained's "<model>/transformer")."""
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        c = Flux2ConfigC()
+        ctx.check(lib().dcpp_flux2_config_from_file(os.path.join(os.fspath(path), "config.json").encode(),
+                                                    ctypes.byref(c)), "config_from_file")
+        self.cfg = c
+        h = _vp()
+        ctx.check(lib().dcpp_flux2_from_pretrained(ctx.h, os.fspath(path).encode(), ctypes.byref(h)), "from_pretrained")
+        ctx._children.add(self)
+        self.h = h
+        return self
+
     def _check(self, status: int, what: str = ""):
         if status != DCPP_OK:
             msg = lib().dcpp_flux2_last_error(self.h).decode()
@@ -375,6 +408,15 @@ class Flux2Model:
     def load_params(self, params):
         for name, (gtype, shape, data) in params.items():
             self.set_param(name, gtype, shape, data)
+
+    def load_gguf(self, source):
+        """Bind every tensor of a GGUF checkpoint (a GGUFFile, a .gguf path or a
+        folder holding one); returns (tensors bound, tensors the model did not
+        know).  Raises if a parameter is not in the file."""
+        f = source if isinstance(source, GGUFFile) else GGUFFile(source)
+        nb, nu = ctypes.c_int64(), ctypes.c_int64()
+        self._check(lib().dcpp_flux2_load_gguf(self.h, f.h, ctypes.byref(nb), ctypes.byref(nu)), "load_gguf")
+        return nb.value, nu.value
 
     def missing(self):
         n = ctypes.c_int()
@@ -423,6 +465,113 @@ class Flux2Model:
         return v.value
 
 
+GGUF_VALUE_TYPES = {0: "u8", 1: "i8", 2: "u16", 3: "i16", 4: "u32", 5: "i32", 6: "f32", 7: "bool", 8: "string",
+                    9: "array", 10: "u64", 11: "i64", 12: "f64"}
+
+
+class GGUFFile:
+    """dcpp_gguf: a memory-mapped GGUF checkpoint (a .gguf file, or a component
+    folder holding one), as GGUFLoaderVisitor opens it."""
+
+    def __init__(self, path):
+        h = _vp()
+        err = ctypes.create_string_buffer(2048)
+        st = lib().dcpp_gguf_open(os.fspath(path).encode(), ctypes.byref(h), err, len(err))
+        if st != DCPP_OK:
+            raise DcppError(st, err.value.decode())
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dcpp_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def info(self):
+        v, a, d = ctypes.c_uint32(), ctypes.c_uint64(), ctypes.c_uint64()
+        nt, nk = ctypes.c_int64(), ctypes.c_int64()
+        st = lib().dcpp_gguf_info(self.h, ctypes.byref(v), ctypes.byref(a), ctypes.byref(d), ctypes.byref(nt),
+                                  ctypes.byref(nk))
+        if st != DCPP_OK:
+            raise DcppError(st, "gguf_info")
+        return {"version": v.value, "alignment": a.value, "data_offset": d.value, "n_tensors": nt.value,
+                "n_kv": nk.value}
+
+    def tensor(self, i: int):
+        """dict(name, type, ne (ggml order, n_dims entries), offset, nbytes, data address)."""
+        name, t, nd = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int()
+        ne = (ctypes.c_int64 * 4)()
+        off, nb, data = ctypes.c_uint64(), ctypes.c_uint64(), _vp()
+        st = lib().dcpp_gguf_tensor(self.h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), ne,
+                                    ctypes.byref(off), ctypes.byref(nb), ctypes.byref(data))
+        if st != DCPP_OK:
+            raise DcppError(st, f"gguf_tensor({i})")
+        return {"name": name.value.decode(), "type": t.value, "ne": tuple(ne[:nd.value]), "offset": off.value,
+                "nbytes": nb.value, "data": data.value}
+
+    def tensors(self):
+        return [self.tensor(i) for i in range(self.info()["n_tensors"])]
+
+    def find(self, name: str) -> int:
+        return int(lib().dcpp_gguf_find_tensor(self.h, name.encode()))
+
+    def tensor_bytes(self, name: str) -> np.ndarray:
+        i = self.find(name)
+        if i < 0:
+            raise KeyError(name)
+        t = self.tensor(i)
+        return np.ctypeslib.as_array((ctypes.c_uint8 * t["nbytes"]).from_address(t["data"])).copy()
+
+    def _get(self, key: str, vtype: int, index: int):
+        k = key.encode()
+        if vtype == 8:
+            cap = 256
+            while True:
+                buf = ctypes.create_string_buffer(cap)
+                st = lib().dcpp_gguf_get_string(self.h, k, index, buf, cap)
+                if st == DCPP_OK:
+                    return buf.value.decode("utf-8", errors="surrogateescape")
+                if cap > (1 << 26):
+                    raise DcppError(st, f"gguf_get_string({key})")
+                cap *= 4
+        if vtype in (6, 12):
+            out = ctypes.c_double()
+            st = lib().dcpp_gguf_get_float(self.h, k, index, ctypes.byref(out))
+        else:
+            out = ctypes.c_int64()
+            st = lib().dcpp_gguf_get_int(self.h, k, index, ctypes.byref(out))
+        if st != DCPP_OK:
+            raise DcppError(st, f"gguf_get({key})")
+        return bool(out.value) if vtype == 7 else out.value
+
+    def metadata(self):
+        """{key: (type name, value)}; arrays as ("array[<elem type>]", list)."""
+        out = {}
+        for i in range(self.info()["n_kv"]):
+            key, t, et, n = ctypes.c_char_p(), ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint64()
+            st = lib().dcpp_gguf_kv(self.h, i, ctypes.byref(key), ctypes.byref(t), ctypes.byref(et), ctypes.byref(n))
+            if st != DCPP_OK:
+                raise DcppError(st, f"gguf_kv({i})")
+            k = key.value.decode()
+            if t.value == 9:
+                out[k] = (f"array[{GGUF_VALUE_TYPES.get(et.value, et.value)}]",
+                          [self._get(k, et.value, j) for j in range(n.value)])
+            else:
+                out[k] = (GGUF_VALUE_TYPES.get(t.value, t.value), self._get(k, t.value, -1))
+        return out
+
+
 def flow_match_schedule(n: int, shift: float = 1.0):
     ts = np.zeros(n, dtype=np.float32)
     sg = np.zeros(n + 1, dtype=np.float32)
@@ -456,6 +605,23 @@ class Qwen3Model:
         self.h = h
         self.n_taps = 0
 
+    @classmethod
+    def from_pretrained(cls, ctx: Context, path):
+        """config.json + the GGUF file of a text-encoder folder
+        (Flux2KleinPipeline::from_pretrained's "<model>/text_encoder")."""
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        c = Qwen3ConfigC()
+        ctx.check(lib().dcpp_qwen3_config_from_file(os.path.join(os.fspath(path), "config.json").encode(),
+                                                    ctypes.byref(c)), "config_from_file")
+        self.cfg = c
+        h = _vp()
+        ctx.check(lib().dcpp_qwen3_from_pretrained(ctx.h, os.fspath(path).encode(), ctypes.byref(h)), "from_pretrained")
+        ctx._children.add(self)
+        self.h = h
+        self.n_taps = 0
+        return self
+
     def close(self):
         if getattr(self, "h", None):
             lib().dcpp_qwen3_destroy(self.h)
@@ -478,6 +644,13 @@ class Qwen3Model:
     def load_params(self, params):
         for name, (gtype, shape, data) in params.items():
             self.set_param(name, gtype, shape, data)
+
+    def load_gguf(self, source):
+        """As Flux2Model.load_gguf, for the text encoder's checkpoint."""
+        f = source if isinstance(source, GGUFFile) else GGUFFile(source)
+        nb, nu = ctypes.c_int64(), ctypes.c_int64()
+        self.ctx.check(lib().dcpp_qwen3_load_gguf(self.h, f.h, ctypes.byref(nb), ctypes.byref(nu)), "load_gguf")
+        return nb.value, nu.value
 
     def missing(self):
         n = ctypes.c_int()

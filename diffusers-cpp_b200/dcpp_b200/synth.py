@@ -197,10 +197,18 @@ def qwen3_param_shapes(cfg: Qwen3Cfg):
     return s
 
 
+# The reference converter's per-tensor types for the Klein text encoder
+# (utils/convert-model/flux2-klein-9b-q8.json, "text_encoder": attention
+# projections BF16, norms F32, everything else Q8_0).
+QWEN3_KLEIN_TYPES = {"self_attn.q_proj.weight": TYPE_BF16, "self_attn.k_proj.weight": TYPE_BF16,
+                     "self_attn.v_proj.weight": TYPE_BF16, "self_attn.o_proj.weight": TYPE_BF16}
+
+
 def make_qwen3_params(cfg: Qwen3Cfg, wtype: int = TYPE_Q8_0, seed: int = 0, device: str = "cpu",
-                      to_cpu: bool = True):
+                      to_cpu: bool = True, types: Optional[Dict[str, int]] = None):
     """Dict name -> (ggml type, shape, uint8 tensor): matrices N(0, 0.02)
-    quantised to `wtype`, norm weights 1 + 0.1 N(0, 1) in F32."""
+    quantised to `wtype` (or to types[suffix] for names ending in a key of
+    `types`), norm weights 1 + 0.1 N(0, 1) in F32."""
     out = {}
     for name, shape in qwen3_param_shapes(cfg).items():
         g = torch.Generator(device=device)
@@ -210,7 +218,7 @@ def make_qwen3_params(cfg: Qwen3Cfg, wtype: int = TYPE_Q8_0, seed: int = 0, devi
             t = TYPE_F32
         else:
             w = 0.02 * torch.randn(shape, generator=g, device=device, dtype=torch.float32)
-            t = wtype
+            t = next((v for k, v in (types or {}).items() if name.endswith(k)), wtype)
         q = quantize(w, t).contiguous()
         out[name] = (t, tuple(shape), q.cpu() if to_cpu else q)
     return out

@@ -405,6 +405,65 @@ dcpp_status dcpp_qwen3_set_profiling(dcpp_qwen3* model, int on);
 dcpp_status dcpp_qwen3_profile(dcpp_qwen3* model, int kind, double* ms, double* flops, int64_t* launches);
 dcpp_status dcpp_qwen3_launches_per_step(dcpp_qwen3* model, int64_t* out);
 
+/* ---------------------------------------------------------------------- */
+/* GGUF checkpoints (GGUFLoaderVisitor, src/ggml/GGUFLoaderVisitor.cpp)    */
+/* ---------------------------------------------------------------------- */
+
+/* A memory-mapped GGUF file (v2 / v3, little-endian).  Replaces the
+ * metadata parse of GGUFLoaderVisitor::GGUFLoaderVisitor
+ * (GGUFLoaderVisitor.cpp:131-173) and its per-tensor file reads (:15-97,
+ * :235-266): tensors are bound straight from the mapping. */
+typedef struct dcpp_gguf dcpp_gguf;
+
+/* Open a .gguf file, or the first *.gguf (in name order) of a directory.
+ * On failure *out is NULL and err (if err_cap > 0) holds the message
+ * ("No such GGUF file in path: ...", "Failed to initialize GGUF file: ...
+ * truncated while reading ...", ...). */
+dcpp_status dcpp_gguf_open(const char* path, dcpp_gguf** out, char* err, size_t err_cap);
+void dcpp_gguf_close(dcpp_gguf* file);
+dcpp_status dcpp_gguf_info(const dcpp_gguf* file, uint32_t* version, uint64_t* alignment, uint64_t* data_offset,
+                           int64_t* n_tensors, int64_t* n_kv);
+/* Tensor i (file order): name (valid while open), ggml type, dimensions in
+ * ggml order (ne[0] = row length; unused entries 1), the absolute file
+ * offset and byte size of its data, and its bytes in the mapping.  Any
+ * output may be NULL. */
+dcpp_status dcpp_gguf_tensor(const dcpp_gguf* file, int64_t i, const char** name, int* type, int* n_dims,
+                             int64_t ne[4], uint64_t* offset, uint64_t* nbytes, const void** data);
+/* Index of the named tensor, -1 if absent. */
+int64_t dcpp_gguf_find_tensor(const dcpp_gguf* file, const char* name);
+/* Metadata entry i: key (valid while open), GGUF value type (0 u8, 1 i8,
+ * 2 u16, 3 i16, 4 u32, 5 i32, 6 f32, 7 bool, 8 string, 9 array, 10 u64,
+ * 11 i64, 12 f64), array element type and length (0 for scalars). */
+dcpp_status dcpp_gguf_kv(const dcpp_gguf* file, int64_t i, const char** key, uint32_t* type, uint32_t* elem_type,
+                         uint64_t* count);
+/* Metadata values by key; index -1 reads a scalar, index k >= 0 element k
+ * of an array.  Integers and bools through get_int, floats through
+ * get_float, strings copied NUL-terminated through get_string.  Unknown
+ * key: DCPP_ERR_NOT_FOUND; wrong type, index or too small a buffer:
+ * DCPP_ERR_INVALID_ARG. */
+dcpp_status dcpp_gguf_get_int(const dcpp_gguf* file, const char* key, int64_t index, int64_t* out);
+dcpp_status dcpp_gguf_get_float(const dcpp_gguf* file, const char* key, int64_t index, double* out);
+dcpp_status dcpp_gguf_get_string(const dcpp_gguf* file, const char* key, int64_t index, char* buf, size_t cap);
+
+/* Bind every tensor of the file that the model knows, with set_param's
+ * name / shape / type rules (the shape is the file's dimensions with
+ * trailing unit dimensions dropped, in row-major order, as
+ * GGUFLoaderVisitor::visit builds it, :244-258).  Tensors the model does
+ * not know are skipped and counted in *n_unused (the reference's validate()
+ * only reports them, :175-189).  Afterwards a parameter the file did not
+ * provide fails with DCPP_ERR_NOT_FOUND: "Error while loading Tensor
+ * '<name>': Tensor not found".  Tensor-parallel models
+ * (dcpp_flux2_set_tensor_parallel first) slice their shards from the
+ * mapping. */
+dcpp_status dcpp_flux2_load_gguf(dcpp_flux2* model, const dcpp_gguf* file, int64_t* n_bound, int64_t* n_unused);
+dcpp_status dcpp_qwen3_load_gguf(dcpp_qwen3* model, const dcpp_gguf* file, int64_t* n_bound, int64_t* n_unused);
+/* config.json + the GGUF file of one pipeline component folder
+ * (Flux2KleinPipeline::from_pretrained, Flux2KleinPipeline.cpp:559-590:
+ * "<model>/transformer", "<model>/text_encoder").  Errors: the context's
+ * dcpp_last_error. */
+dcpp_status dcpp_flux2_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_flux2** out_model);
+dcpp_status dcpp_qwen3_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_qwen3** out_model);
+
 #ifdef __cplusplus
 }
 #endif
