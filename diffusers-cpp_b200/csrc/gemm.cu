@@ -216,6 +216,99 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     return;
   }
 
+  if (e.mode == kEpiConv) {
+    // Convolution output: pixel row -> output row (2x upsample phase), bias,
+    // residual, f32 and / or bf16 NHWC stores or an f32 NCHW store.
+    int64_t orow = row;
+    bool pix_ok = true;
+    if (p.conv.taps) {
+      const ConvGeom& g = p.conv;
+      const int64_t blk = row >> 7;
+      const int r = static_cast<int>(row & 127);
+      const int64_t per_img = static_cast<int64_t>(g.tiles_x) * g.tiles_y;
+      const int64_t bb = blk / per_img;
+      const int rem = static_cast<int>(blk - bb * per_img);
+      const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+      const int y = ty * g.tile_h + r / g.tile_w, x = tx * g.tile_w + r % g.tile_w;
+      pix_ok = y < g.H && x < g.W;
+      if (e.up_phase >= 0)
+        orow = (bb * 2 * g.H + 2 * y + (e.up_phase >> 1)) * (2 * static_cast<int64_t>(g.W)) + 2 * x +
+               (e.up_phase & 1);
+      else
+        orow = (bb * g.H + y) * static_cast<int64_t>(g.W) + x;
+    }
+#pragma unroll 1
+    for (int c = 0; c < kGemmBN / 32; ++c) {
+      const int cb = col0 + c * 32;
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_ld_wait();
+      if (!row_ok || !pix_ok || cb >= p.N) continue;
+      const int nv = min(32, p.N - cb);
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if (e.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nv) v[j] += __ldg(e.bias + cb + j);
+      }
+      if (e.resid) {
+        const float* rs = e.resid + orow * e.ld_resid + cb;
+        if (nv == 32 && (reinterpret_cast<uintptr_t>(rs) & 15) == 0) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(rs) + q);
+            v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nv) v[j] += rs[j];
+        }
+      }
+      if (e.nchw_hw > 0) {
+        const int64_t bb = orow / e.nchw_hw, hw = orow - bb * e.nchw_hw;
+        float* base = e.out_f32 + (bb * p.N + cb) * e.nchw_hw + hw;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nv) base[static_cast<int64_t>(j) * e.nchw_hw] = v[j];
+        continue;
+      }
+      if (e.out_f32) {
+        float* dst = e.out_f32 + orow * e.ld_out + cb;
+        if (nv == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nv) dst[j] = v[j];
+        }
+      }
+      if (e.out_bf16) {
+        uint16_t* dst = e.out_bf16 + orow * e.ld_out + cb;
+        if (nv == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            reinterpret_cast<uint4*>(dst)[q] =
+                make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                           pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < nv) {
+              __nv_bfloat16 b = __float2bfloat16_rn(v[j]);
+              dst[j] = *reinterpret_cast<uint16_t*>(&b);
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+
   // Column-wise epilogues: 8 chunks of 32 columns.
   const float* gate = nullptr;
   const bool gate_only = e.mode == kEpiGateF32 || e.mode == kEpiGatePeer;
@@ -356,6 +449,27 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       }
     }
   }
+}
+
+// ------------------------------------------------------------------ implicit conv
+// TMA coordinates (channel, x, y, batch) of the A box of rows [m, m + 128)
+// for K block kb (ConvGeom).
+struct ConvCoord {
+  int32_t c, x, y, b;
+};
+__device__ __forceinline__ ConvCoord conv_coord(const ConvGeom& g, int m, int kb) {
+  const int blk = m >> 7;
+  const int per_img = g.tiles_x * g.tiles_y;
+  ConvCoord o;
+  o.b = blk / per_img;
+  const int rem = blk - o.b * per_img;
+  const int ty = rem / g.tiles_x;
+  const int tx = rem - ty * g.tiles_x;
+  const int tap = kb / g.cin_blocks;
+  o.c = (kb - tap * g.cin_blocks) * 64;
+  o.x = tx * g.tile_w + g.dx[tap];
+  o.y = ty * g.tile_h + g.dy[tap];
+  return o;
 }
 
 // ------------------------------------------------------------------ fused dequant
@@ -609,7 +723,12 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
                       &full[stage]);
           } else {
             mbar_arrive_expect_tx(&full[stage], kAStageBytes + kBStageBytes);
-            tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
+            if (p.conv.taps) {
+              const ConvCoord cc = conv_coord(p.conv, ya, kb);
+              tma_load_4d(smA + stage * kAStageBytes, &tmA, &full[stage], cc.c, cc.x, cc.y, cc.b);
+            } else {
+              tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
+            }
             tma_load_2d(smB + stage * kBStageBytes, tmB, &full[stage], kb * kGemmBK, yb);
           }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -821,7 +940,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           const uint32_t full0 = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPairB));
-          tma_load_2d_pair(smA + stage * kPairA, &tmA, full0, kb * kGemmBK, ya);
+          if (!kQuant && p.conv.taps) {
+            const ConvCoord cc = conv_coord(p.conv, ya, kb);
+            tma_load_4d_pair(smA + stage * kPairA, &tmA, full0, cc.c, cc.x, cc.y, cc.b);
+          } else {
+            tma_load_2d_pair(smA + stage * kPairA, &tmA, full0, kb * kGemmBK, ya);
+          }
           if (kQuant) {
             const uint8_t* st = packed + (static_cast<int64_t>(tc.n_tile) * nk + kb) * (256 * (kQs + kSc));
             mbar_arrive_expect_tx(&rfull[stage], kRaw);
@@ -1027,6 +1151,25 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, u
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t make_tmap_conv(CUtensorMap* map, const void* base, int64_t B, int64_t H, int64_t W, int64_t C,
+                           int tile_w, int tile_h) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
+  if (C % 64 != 0 || tile_w < 1 || tile_h < 1 || tile_w > 256 || tile_h > 256 || tile_w * tile_h != kGemmBM)
+    return cudaErrorInvalidValue;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C * 2), static_cast<cuuint64_t>(W * C * 2),
+                           static_cast<cuuint64_t>(H * W * C * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tile_w), static_cast<cuuint32_t>(tile_h), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 

@@ -31,6 +31,7 @@ enum GemmEpilogue : int {
   kEpiEuler = 4,      // out_f32[r, c] = x_in[r, c] + dt * acc  (FlowMatchEuler integrate)
   kEpiGateF32 = 5,    // out_f32[r, c] = gate_g[c] * acc   (TP partial before the all-reduce)
   kEpiGatePeer = 6,   // bf16(gate_g[c] * acc) stored into the owning rank's receive slot (TP reduce-scatter)
+  kEpiConv = 7,       // v = acc + bias[c] (+ resid[r', c]) -> out_f32 and / or out_bf16 at row r' (convolutions)
 };
 
 struct GemmGroup {
@@ -84,6 +85,37 @@ struct EpilogueArgs {
   int32_t piece_rows;
   int32_t slot_rows;
   int32_t peer_slot;
+  // kEpiConv: output row r' of accumulator row r is r itself for a plain
+  //   GEMM, and for an implicit convolution (ConvGeom) the row-major index
+  //   (b H + y) W + x of the pixel the row computes (rows outside the image
+  //   are dropped).  bias [N] (may be null); resid: f32 [rows', ld_resid]
+  //   added (may be null); up_phase >= 0: the output grid is the 2x
+  //   nearest-upsampled one and this launch computes its phase
+  //   (a, b) = (up_phase / 2, up_phase % 2): pixel (y, x) goes to
+  //   (2y + a, 2x + b) of the [2H, 2W] grid; nchw_hw > 0: out_f32 is NCHW,
+  //   element (r', c) at ((b N + c) nchw_hw + r' % nchw_hw).
+  const float* bias;
+  const float* resid;
+  int64_t ld_resid;
+  int32_t up_phase;
+  int32_t nchw_hw;
+};
+
+// Implicit-GEMM convolution A operand over an NHWC bf16 image [B, H, W, C]
+// (C a multiple of 64).  K runs over (tap, channel); every 128 rows of A are
+// one tile_h x tile_w pixel rectangle (tile_w * tile_h = 128), rectangles
+// ordered (b, ty, tx) over a tiles_y x tiles_x cover of the image, so row
+// r of block k is pixel (ty tile_h + r / tile_w, tx tile_w + r % tile_w):
+// A[row, t C + c] = X[b, y + dy_t, x + dx_t, c], zero outside the image.
+// Each (tap, 64-channel block) of a rectangle is one 4-D TMA load at the
+// tap's shifted coordinates; TMA's zero fill is the padding.
+struct ConvGeom {
+  int32_t taps;        // 0: plain 2-D A
+  int32_t cin_blocks;  // C / 64
+  int32_t H, W;
+  int32_t tile_w, tile_h;
+  int32_t tiles_x, tiles_y;
+  int8_t dy[9], dx[9];
 };
 
 // A quantised weight packed per (256-row tile, 64-K stage) by
@@ -101,6 +133,7 @@ struct GemmArgs {
   GemmGroup groups[kGemmMaxGroups];
   EpilogueArgs ep;
   QuantB qb[2];
+  ConvGeom conv;
   int* err;
 };
 
@@ -108,6 +141,12 @@ struct GemmArgs {
 // K-major operand [outer rows, inner K] with row stride `ld` elements.
 cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                            uint64_t ld_elems, uint32_t box_outer);
+
+// Host-side: 4-D tensor map over an NHWC bf16 image [B, H, W, C] with a
+// (64 channel, tile_w, tile_h, 1) box and 128-byte swizzle: the A operand
+// of an implicit-GEMM convolution (ConvGeom).
+cudaError_t make_tmap_conv(CUtensorMap* map, const void* base, int64_t B, int64_t H, int64_t W, int64_t C,
+                           int tile_w, int tile_h);
 
 // Launch the grouped GEMM.  `a` maps X (box 64 x 128), b0/b1 map the two
 // bf16 weights (box 64 x 256) when bsrc == kBSrcBf16.

@@ -118,4 +118,27 @@ cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t B, int64_t S, int64
                                 const float* norm_k, float eps, const float2* rope, uint16_t* q, uint16_t* k,
                                 uint16_t* vt, int64_t vt_stride, cudaStream_t s);
 
+// Flux2 VAE decode (vae_ops.cu).  Images are NHWC (row (b H + y) W + x).
+// Packed latent tokens [B, ph*pw, 4C] f32 -> BatchNorm de-normalised,
+// unpatchified z [B, 2ph, 2pw, Cpad] bf16 (channels >= C zero).
+cudaError_t launch_latent_unpack(const float* lat, const float* mean, const float* var, float eps, int B, int ph,
+                                 int pw, int C, int Cpad, uint16_t* out, cudaStream_t s);
+// GroupNorm statistics: stats[b, g] += (sum, sum of squares) in double over
+// x [B, HW, C] (f32, or bf16 when bf16); stats must be zeroed first.
+cudaError_t launch_gn_stats(const void* x, bool bf16, int B, int64_t HW, int C, int G, double* stats,
+                            cudaStream_t s);
+// y = GroupNorm(x) * gamma + beta (then SiLU when silu), bf16 [B, HW, C].
+cudaError_t launch_gn_apply(const void* x, bool bf16, int B, int64_t HW, int C, int G, const double* stats,
+                            const float* gamma, const float* beta, float eps, bool silu, uint16_t* y,
+                            cudaStream_t s);
+// P = softmax(scale * S) over each row of n columns (bf16 out).
+cudaError_t launch_softmax_rows(const float* S, int64_t rows, int64_t n, int64_t ld_s, float scale, uint16_t* P,
+                                int64_t ld_p, cudaStream_t s);
+cudaError_t launch_transpose_bf16(const uint16_t* in, int64_t rows, int64_t cols, int64_t ld_in, uint16_t* out,
+                                  int64_t ld_out, cudaStream_t s);
+// 3x3 convolution (pad 1) with Cout in {1, 3, 4}: X bf16 NHWC [B, H, W, C],
+// w f32 [Cout][9][C] (tap = 3 ky + kx), bias [Cout] -> out f32 NCHW.
+cudaError_t launch_conv3x3_small(const uint16_t* X, int B, int H, int W, int C, int Cout, const float* w,
+                                 const float* bias, float* out, cudaStream_t s);
+
 }  // namespace dcpp

@@ -236,14 +236,14 @@ void StepPlanner::alloc_expansion_scratch(const std::function<void*(size_t)>& al
     wscratch_[pi][0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
     wscratch_[pi][1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
   }
+}
+
+void StepPlanner::begin_ops(std::vector<Op>& ops) {
   if (!side_) {
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
     cuda_check(cudaStreamCreateWithPriority(&side_, cudaStreamNonBlocking, lo), "side stream");
   }
-}
-
-void StepPlanner::begin_ops(std::vector<Op>& ops) {
   building_ = &ops;
   scratch_pair_ = 0;
   scratch_free_[0] = scratch_free_[1] = nullptr;

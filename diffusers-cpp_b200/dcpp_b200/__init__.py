@@ -74,6 +74,26 @@ class Qwen3ConfigC(ctypes.Structure):
     ]
 
 
+class VAEConfigC(ctypes.Structure):
+    _fields_ = [
+        ("in_channels", ctypes.c_int64),
+        ("out_channels", ctypes.c_int64),
+        ("block_out_channels", ctypes.c_int64 * 8),
+        ("n_blocks", ctypes.c_int32),
+        ("layers_per_block", ctypes.c_int64),
+        ("latent_channels", ctypes.c_int64),
+        ("norm_num_groups", ctypes.c_int64),
+        ("sample_size", ctypes.c_int64),
+        ("force_upcast", ctypes.c_int32),
+        ("use_quant_conv", ctypes.c_int32),
+        ("use_post_quant_conv", ctypes.c_int32),
+        ("mid_block_add_attention", ctypes.c_int32),
+        ("batch_norm_eps", ctypes.c_float),
+        ("batch_norm_momentum", ctypes.c_float),
+        ("patch_size", ctypes.c_int64 * 2),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "dcpp_version": (ctypes.c_char_p, []),
@@ -155,6 +175,20 @@ _SIGNATURES = {
     "dcpp_flux2_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
     "dcpp_qwen3_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
     "dcpp_flux2_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "dcpp_vae_config_default": (None, [ctypes.POINTER(VAEConfigC)]),
+    "dcpp_vae_config_from_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(VAEConfigC)]),
+    "dcpp_vae_create": (ctypes.c_int, [_vp, ctypes.POINTER(VAEConfigC), ctypes.POINTER(_vp)]),
+    "dcpp_vae_destroy": (ctypes.c_int, [_vp]),
+    "dcpp_vae_set_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _c_i64p, _vp, ctypes.c_size_t]),
+    "dcpp_vae_missing": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t]),
+    "dcpp_vae_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
+    "dcpp_vae_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "dcpp_vae_prepare": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]),
+    "dcpp_vae_decode": (ctypes.c_int, [_vp, _vp, _vp]),
+    "dcpp_vae_set_profiling": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "dcpp_vae_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(ctypes.c_double), _c_i64p]),
+    "dcpp_vae_launches_per_step": (ctypes.c_int, [_vp, _c_i64p]),
     "dcpp_qwen3_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "dcpp_flux2_read_param": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), _c_i64p, _c_i64p, _vp,
                                              ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
@@ -681,4 +715,109 @@ class Qwen3Model:
     def launches_per_step(self) -> int:
         v = ctypes.c_int64()
         self.ctx.check(lib().dcpp_qwen3_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
+        return v.value
+
+
+def vae_config_to_c(cfg) -> VAEConfigC:
+    """VAEConfigC from an object with AutoencoderKLFlux2::Config's field names."""
+    c = VAEConfigC()
+    lib().dcpp_vae_config_default(ctypes.byref(c))
+    for k in ("in_channels", "out_channels", "layers_per_block", "latent_channels", "norm_num_groups"):
+        if hasattr(cfg, k):
+            setattr(c, k, int(getattr(cfg, k)))
+    ch = list(cfg.block_out_channels)
+    c.n_blocks = len(ch)
+    for i, v in enumerate(ch):
+        c.block_out_channels[i] = int(v)
+    for k in ("use_post_quant_conv", "mid_block_add_attention"):
+        if hasattr(cfg, k):
+            setattr(c, k, 1 if getattr(cfg, k) else 0)
+    if hasattr(cfg, "batch_norm_eps"):
+        c.batch_norm_eps = float(cfg.batch_norm_eps)
+    return c
+
+
+class VAEModel:
+    """dcpp_vae: the Flux2 VAE decode (Flux2KleinPipeline::decode) on one GPU."""
+
+    PROFILE_KINDS = Flux2Model.PROFILE_KINDS
+
+    def __init__(self, ctx: Context, cfg):
+        self.ctx = ctx
+        self.cfg = cfg
+        c = vae_config_to_c(cfg)
+        h = _vp()
+        ctx.check(lib().dcpp_vae_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "vae_create")
+        ctx._children.add(self)
+        self.h = h
+
+    @classmethod
+    def from_pretrained(cls, ctx: Context, path):
+        """config.json + the GGUF file of the pipeline's vae folder."""
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        c = VAEConfigC()
+        ctx.check(lib().dcpp_vae_config_from_file(os.path.join(os.fspath(path), "config.json").encode(),
+                                                  ctypes.byref(c)), "config_from_file")
+        self.cfg = c
+        h = _vp()
+        ctx.check(lib().dcpp_vae_from_pretrained(ctx.h, os.fspath(path).encode(), ctypes.byref(h)), "from_pretrained")
+        ctx._children.add(self)
+        self.h = h
+        return self
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dcpp_vae_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_param(self, name: str, gtype: int, shape: Sequence[int], data):
+        if hasattr(data, "numpy"):
+            data = data.contiguous().cpu().numpy()
+        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
+        shp = (ctypes.c_int64 * len(shape))(*shape)
+        self.ctx.check(lib().dcpp_vae_set_param(self.h, name.encode(), gtype, len(shape), shp, arr.ctypes.data,
+                                                arr.nbytes), f"set_param({name})")
+
+    def load_params(self, params):
+        for name, (gtype, shape, data) in params.items():
+            self.set_param(name, gtype, shape, data)
+
+    def load_gguf(self, source):
+        f = source if isinstance(source, GGUFFile) else GGUFFile(source)
+        nb, nu = ctypes.c_int64(), ctypes.c_int64()
+        self.ctx.check(lib().dcpp_vae_load_gguf(self.h, f.h, ctypes.byref(nb), ctypes.byref(nu)), "load_gguf")
+        return nb.value, nu.value
+
+    def missing(self):
+        n = ctypes.c_int()
+        buf = ctypes.create_string_buffer(512)
+        self.ctx.check(lib().dcpp_vae_missing(self.h, ctypes.byref(n), buf, 512), "missing")
+        return n.value, buf.value.decode()
+
+    def prepare(self, batch: int, packed_h: int, packed_w: int, use_graph: bool = True):
+        self.ctx.check(lib().dcpp_vae_prepare(self.h, batch, packed_h, packed_w, 1 if use_graph else 0), "prepare")
+
+    def decode(self, latents, image):
+        """latents [B, ph*pw, 4*latent_channels] f32 -> image [B, out_channels, H, W] f32."""
+        self.ctx.check(lib().dcpp_vae_decode(self.h, _ptr(latents), _ptr(image)), "decode")
+
+    def set_profiling(self, on: bool):
+        self.ctx.check(lib().dcpp_vae_set_profiling(self.h, 1 if on else 0), "set_profiling")
+
+    def profile(self, kind: str):
+        ms, fl, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+        self.ctx.check(lib().dcpp_vae_profile(self.h, self.PROFILE_KINDS[kind], ctypes.byref(ms), ctypes.byref(fl),
+                                              ctypes.byref(n)), "profile")
+        return ms.value, fl.value, n.value
+
+    def launches_per_step(self) -> int:
+        v = ctypes.c_int64()
+        self.ctx.check(lib().dcpp_vae_launches_per_step(self.h, ctypes.byref(v)), "launches_per_step")
         return v.value

@@ -229,3 +229,103 @@ def make_qwen3_ids(cfg: Qwen3Cfg, batch: int, seq: int, seed: int = 1):
     g = torch.Generator()
     g.manual_seed(seed)
     return torch.randint(0, cfg.vocab_size, (batch, seq), generator=g, dtype=torch.int64).to(torch.int32)
+
+
+# --------------------------------------------------------------------------- Flux2 VAE decoder
+@dataclass
+class VAECfg:
+    """Same fields as AutoencoderKLFlux2::Config (decode subset); defaults:
+    the Flux2 VAE (1024-pixel images from 64 x 64 packed tokens)."""
+    in_channels: int = 3
+    out_channels: int = 3
+    block_out_channels: Tuple[int, ...] = (128, 256, 512, 512)
+    layers_per_block: int = 2
+    latent_channels: int = 32
+    norm_num_groups: int = 32
+    batch_norm_eps: float = 1e-4
+    use_post_quant_conv: bool = True
+    mid_block_add_attention: bool = True
+
+
+def vae_param_shapes(cfg: VAECfg) -> Dict[str, Tuple[int, ...]]:
+    """Decode-path parameter names (diffusers AutoencoderKLFlux2 state dict)
+    and PyTorch shapes."""
+    s: Dict[str, Tuple[int, ...]] = {}
+    L, ch = cfg.latent_channels, list(cfg.block_out_channels)
+    s["bn.running_mean"] = (4 * L,)
+    s["bn.running_var"] = (4 * L,)
+    if cfg.use_post_quant_conv:
+        s["post_quant_conv.weight"] = (L, L, 1, 1)
+        s["post_quant_conv.bias"] = (L,)
+
+    def conv(n, cin, cout, k):
+        s[n + ".weight"] = (cout, cin, k, k)
+        s[n + ".bias"] = (cout,)
+
+    def norm(n, c):
+        s[n + ".weight"] = (c,)
+        s[n + ".bias"] = (c,)
+
+    def resnet(n, cin, cout):
+        norm(n + ".norm1", cin)
+        conv(n + ".conv1", cin, cout, 3)
+        norm(n + ".norm2", cout)
+        conv(n + ".conv2", cout, cout, 3)
+        if cin != cout:
+            conv(n + ".conv_shortcut", cin, cout, 1)
+
+    top = ch[-1]
+    conv("decoder.conv_in", L, top, 3)
+    resnet("decoder.mid_block.resnets.0", top, top)
+    if cfg.mid_block_add_attention:
+        p = "decoder.mid_block.attentions.0"
+        norm(p + ".group_norm", top)
+        for n in ("to_q", "to_k", "to_v", "to_out.0"):
+            s[f"{p}.{n}.weight"] = (top, top)
+            s[f"{p}.{n}.bias"] = (top,)
+    resnet("decoder.mid_block.resnets.1", top, top)
+    rev = ch[::-1]
+    prev = rev[0]
+    for i, out in enumerate(rev):
+        for j in range(cfg.layers_per_block + 1):
+            resnet(f"decoder.up_blocks.{i}.resnets.{j}", prev if j == 0 else out, out)
+        if i < len(rev) - 1:
+            conv(f"decoder.up_blocks.{i}.upsamplers.0.conv", out, out, 3)
+        prev = out
+    norm("decoder.conv_norm_out", ch[0])
+    conv("decoder.conv_out", ch[0], cfg.out_channels, 3)
+    return s
+
+
+def make_vae_params(cfg: VAECfg, seed: int = 0, device: str = "cpu", to_cpu: bool = True):
+    """Dict name -> (ggml type, shape, uint8 tensor), all F32 (the reference
+    converter's type map stores the VAE in F32): conv / linear weights
+    N(0, 1/fan_in), biases N(0, 0.02^2), GroupNorm scale 1 + 0.1 N and shift
+    0.1 N, BatchNorm running mean 0.1 N and variance 1 + 0.5 U."""
+    out = {}
+    for name, shape in vae_param_shapes(cfg).items():
+        g = torch.Generator(device=device)
+        g.manual_seed(tensor_seed(seed, name))
+        r = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+        if name == "bn.running_var":
+            w = 1.0 + 0.5 * torch.rand(shape, generator=g, device=device, dtype=torch.float32)
+        elif name == "bn.running_mean":
+            w = 0.1 * r
+        elif len(shape) >= 2:
+            fan_in = math.prod(shape[1:])
+            w = r / math.sqrt(fan_in)
+        elif ".norm" in name or "group_norm" in name or "conv_norm_out" in name:
+            w = (1.0 + 0.1 * r) if name.endswith(".weight") else 0.1 * r
+        else:
+            w = 0.02 * r
+        q = w.contiguous().view(torch.uint8).reshape(-1)
+        out[name] = (TYPE_F32, tuple(shape), q.cpu() if to_cpu else q)
+    return out
+
+
+def make_vae_latents(cfg: VAECfg, batch: int, packed_h: int, packed_w: int, seed: int = 3, device: str = "cpu"):
+    """Packed denoised tokens [batch, packed_h * packed_w, 4 * latent_channels] f32, N(0, 1)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return torch.randn(batch, packed_h * packed_w, 4 * cfg.latent_channels, generator=g, device=device,
+                       dtype=torch.float32)

@@ -464,6 +464,62 @@ dcpp_status dcpp_qwen3_load_gguf(dcpp_qwen3* model, const dcpp_gguf* file, int64
 dcpp_status dcpp_flux2_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_flux2** out_model);
 dcpp_status dcpp_qwen3_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_qwen3** out_model);
 
+/* ---------------------------------------------------------------------- */
+/* Flux2 VAE decode (the pipeline step after the denoise loop)             */
+/* ---------------------------------------------------------------------- */
+
+/* AutoencoderKLFlux2::Config (AutoencoderKLFlux2.hpp:10-33). */
+typedef struct dcpp_vae_config {
+    int64_t in_channels;              /* 3 */
+    int64_t out_channels;             /* 3 (1, 3 or 4 supported) */
+    int64_t block_out_channels[8];    /* 128, 256, 512, 512 (multiples of 64) */
+    int32_t n_blocks;                 /* 4 */
+    int64_t layers_per_block;         /* 2 */
+    int64_t latent_channels;          /* 32 */
+    int64_t norm_num_groups;          /* 32 */
+    int64_t sample_size;              /* 1024 */
+    int32_t force_upcast;             /* 1 */
+    int32_t use_quant_conv;           /* 1 (encoder side, unused by decode) */
+    int32_t use_post_quant_conv;      /* 1 */
+    int32_t mid_block_add_attention;  /* 1 */
+    float batch_norm_eps;             /* 1e-4 */
+    float batch_norm_momentum;        /* 0.1 */
+    int64_t patch_size[2];            /* 2, 2 (the only value supported) */
+} dcpp_vae_config;
+
+typedef struct dcpp_vae dcpp_vae;
+
+void dcpp_vae_config_default(dcpp_vae_config* cfg);
+/* AutoencoderKLFlux2::Config::from_file (AutoencoderKLFlux2.cpp:422-468). */
+dcpp_status dcpp_vae_config_from_file(const char* path, dcpp_vae_config* cfg);
+/* The decoder of AutoencoderKLFlux2 (post_quant_conv, Decoder, the
+ * BatchNorm running statistics the pipeline de-normalises with). */
+dcpp_status dcpp_vae_create(dcpp_ctx* ctx, const dcpp_vae_config* cfg, dcpp_vae** out_model);
+dcpp_status dcpp_vae_destroy(dcpp_vae* model);
+/* Bind one parameter by its GGUF name ("decoder.conv_in.weight",
+ * "decoder.up_blocks.0.resnets.1.norm2.bias", "bn.running_var", ...).
+ * F32, F16, BF16, Q8_0 or Q4_K; shapes as PyTorch's (conv weights
+ * [Cout, Cin, k, k]).  Encoder-side names give DCPP_ERR_NOT_FOUND;
+ * "bn.num_batches_tracked" is accepted and ignored. */
+dcpp_status dcpp_vae_set_param(dcpp_vae* model, const char* name, int type, int n_dims, const int64_t* shape,
+                               const void* p_data, size_t nbytes);
+dcpp_status dcpp_vae_missing(dcpp_vae* model, int* count, char* first_missing, size_t cap);
+/* As dcpp_flux2_load_gguf (a full VAE checkpoint's encoder tensors count
+ * as unused). */
+dcpp_status dcpp_vae_load_gguf(dcpp_vae* model, const dcpp_gguf* file, int64_t* n_bound, int64_t* n_unused);
+/* config.json + the GGUF file of the pipeline's "<model>/vae" folder. */
+dcpp_status dcpp_vae_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_vae** out_model);
+/* Plan the decode of `batch` packed latents of packed_h x packed_w tokens
+ * (the DiT's image tokens; image = 2 * scale_factor * packed_h pixels high). */
+dcpp_status dcpp_vae_prepare(dcpp_vae* model, int64_t batch, int64_t packed_h, int64_t packed_w, int use_graph);
+/* Flux2KleinPipeline::decode (Flux2KleinPipeline.cpp:538-556, untiled):
+ * latents [B, packed_h * packed_w, 4 * latent_channels] f32 (the denoised
+ * tokens) -> image [B, out_channels, H, W] f32.  Host or device pointers. */
+dcpp_status dcpp_vae_decode(dcpp_vae* model, const float* p_latents, float* p_image);
+dcpp_status dcpp_vae_set_profiling(dcpp_vae* model, int on);
+dcpp_status dcpp_vae_profile(dcpp_vae* model, int kind, double* ms, double* flops, int64_t* launches);
+dcpp_status dcpp_vae_launches_per_step(dcpp_vae* model, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif
