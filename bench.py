@@ -556,13 +556,122 @@ def run_qwen3(args):
     return 0
 
 
+VAE_METRIC = "Flux2 VAE decode images/s at 1024x1024"
+
+
+def run_vae(args):
+    """The pipeline's VAE decode (Flux2KleinPipeline::decode, untiled) of one
+    1024 x 1024 image from 64 x 64 packed tokens, the Flux2 VAE config
+    (block_out_channels 128/256/512/512, 2 layers per block, 32 latent
+    channels), F32 weights as the reference's converter stores them.  Not a
+    BASELINE config: the measurement of the widening row after the denoise
+    step.  One GPU."""
+    import torch
+
+    import dcpp_b200
+    from dcpp_b200 import synth
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--config vae runs on one GPU")
+    c = synth.VAECfg()
+    B, ph, pw = 1, 64, 64
+    ctx = dcpp_b200.Context(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    m = dcpp_b200.VAEModel(ctx, c)
+    t0 = time.time()
+    params = synth.make_vae_params(c, seed=0, device="cuda", to_cpu=False)
+    for name, (gt, shp, data) in params.items():
+        m.set_param(name, gt, shp, data.cpu())
+    del params
+    load_s = time.time() - t0
+    m.prepare(B, ph, pw, use_graph=not args.no_graph)
+    lat = synth.make_vae_latents(c, B, ph, pw, seed=1)
+    lat_dev = lat.cuda()
+    lat_p = lat.pin_memory()
+    H = W = 2 * ph * 8
+    img = torch.empty(B, c.out_channels, H, W, device="cuda")
+    img_p = torch.empty(B, c.out_channels, H, W).pin_memory()
+    for _ in range(args.warmup):
+        m.decode(lat_dev, img)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        m.decode(lat_dev, img)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        m.decode(lat_p, img_p)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    assert torch.isfinite(img_p).all(), "non-finite image"
+    if args.ops_csv:
+        os.makedirs(args.ops_csv, exist_ok=True)
+        os.environ["DCPP_PROFILE_OPS"] = os.path.join(args.ops_csv, "ops_vae_1024.csv")
+    m.set_profiling(True)
+    m.prepare(B, ph, pw, use_graph=False)
+    for _ in range(2):
+        m.decode(lat_dev, img)
+    torch.cuda.synchronize()
+    prof = {k: m.profile(k) for k in dcpp_b200.Flux2Model.PROFILE_KINDS}
+    launches = m.launches_per_step()
+    peak_b, peak_s, hbm, peak_src = measured_peaks()
+    g_ms, g_fl, _ = prof["gemm"]
+    achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else 0.0
+    total_fl = sum(v[1] for v in prof.values())
+    line = {
+        "metric": VAE_METRIC,
+        "value": B / (ms * 1e-3),
+        "unit": "images/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1/fan_in) F32 weights; N(0,1) packed latents)",
+        "config": {"workload": "vae: Flux2 VAE decode (128/256/512/512 channels, 2 layers per block, 32 latent "
+                               "channels), 64 x 64 packed tokens -> 1024 x 1024 image, untiled",
+                   "global_batch": B, "parallelism": "tp1",
+                   "l2": "no flush: every decode streams > 10 GB of activations through the 126 MB L2",
+                   "cuda_graph": not args.no_graph},
+        "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "images/s", "h2d_bytes_per_step": lat.numel() * 4,
+                "d2h_bytes_per_step": img_p.numel() * 4,
+                "path": "dcpp_vae_decode with pinned host latents in, the f32 image out"},
+        "gpu_launches": launches * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (implicit-GEMM convolutions)",
+                     "achieved": achieved, "peak": peak_s, "unit": "TFLOP/s",
+                     "frac": achieved / peak_s if peak_s else None, "peak_kind": f"bf16 sustained ({peak_src})",
+                     "traffic": None, "step_tflops": total_fl / 1e12,
+                     "step_frac_of_peak": total_fl / (ms * 1e-3) / 1e12 / peak_s},
+        "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
+        "clocks": clk,
+        "load_seconds": load_s,
+    }
+    print(json.dumps(line), flush=True)
+    m.close()
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["4"], default="2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["4", "vae"], default="2")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
@@ -575,6 +684,11 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "config 4 has no CPU reference arm in this bench"}))
             return 0
         return run_qwen3(args)
+    if args.config == "vae":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the VAE decode has no CPU reference arm in this bench"}))
+            return 0
+        return run_vae(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
