@@ -25,7 +25,6 @@ namespace dcpp {
 namespace {
 
 constexpr int kAStageBytes = kGemmBM * kGemmBK * 2;  // 16 KB
-constexpr int kBStageBytes = kGemmBN * kGemmBK * 2;  // 32 KB
 constexpr int kTmemCols = 512;
 
 struct TileCoord {
@@ -63,6 +62,49 @@ constexpr int kEpiStageRowBytes = 144;
 constexpr int kEpiStageStride = kEpiStageRowBytes / 4;  // in floats
 constexpr int kEpiStageBytes = 4 * 32 * kEpiStageRowBytes;
 
+// Warp transpose-reduce: afterwards lane l holds the sum over the warp's
+// lanes of a[l] (recursive halving, 31 shuffles for 32 values).
+__device__ __forceinline__ float warp_reduce_32(float a[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? a[i] : a[i + off];
+      const float keep = upper ? a[i + off] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return a[0];
+}
+
+// GroupNorm partial sums of one 32-column chunk (groups of CPG channels);
+// warp-collective.  slot_ok: the warp's 32 rows lie inside the launch.
+template <int CPG>
+__device__ __forceinline__ void gn_chunk_stats(const EpilogueArgs& e, const float v[32], bool valid, bool slot_ok,
+                                               int nv, int cb, int64_t row) {
+  constexpr int NG = 32 / CPG;
+  float a[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) a[i] = 0.f;
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nv) {
+        a[2 * (j / CPG)] += v[j];
+        a[2 * (j / CPG) + 1] += v[j] * v[j];
+      }
+    }
+  }
+  const float t = warp_reduce_32(a);
+  const int lane = threadIdx.x & 31;
+  if (slot_ok && lane < 2 * NG) e.gn_part[(row >> 5) * (2 * e.gn_groups) + (cb / CPG) * 2 + lane] = t;
+}
+
+// kConv: whether the kernel carries the convolution epilogue (bf16-weight
+// kernels; the fused-dequant kernels leave it out for their registers).
+template <int BN, bool kConv>
 __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord& tc, int row_base, int row_in_tile,
                                              uint32_t taddr, float* stage) {
   const GemmGroup& G = p.groups[tc.g];
@@ -70,7 +112,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
   const int local_row = row_base + row_in_tile;
   const bool row_ok = local_row < G.rows;
   const int64_t row = static_cast<int64_t>(G.orow0) + local_row;
-  const int col0 = tc.n_tile * kGemmBN;
+  const int col0 = tc.n_tile * BN;
   const int sel = G.sel;
 
   if (e.mode == kEpiQkvMlp) {
@@ -216,7 +258,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     return;
   }
 
-  if (e.mode == kEpiConv) {
+  if (kConv && e.mode == kEpiConv) {
     // Convolution output: pixel row -> output row (2x upsample phase), bias,
     // residual, f32 and / or bf16 NHWC stores or an f32 NCHW store.
     int64_t orow = row;
@@ -237,13 +279,118 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       else
         orow = (bb * g.H + y) * static_cast<int64_t>(g.W) + x;
     }
+    const bool valid = row_ok && pix_ok;
+    // Coalesced path: each 32-row x 32-column chunk is staged in shared
+    // memory and handled transposed -- lane t owns column quad t & 7 of
+    // rows (t >> 3) + 4 i -- so every global load and store of the warp
+    // covers whole 128-byte (f32) or 64-byte (bf16) row segments, the
+    // residual of the next chunk is loaded while this one is stored, and the
+    // GroupNorm partial sums reduce over a few lanes.
+    if (e.nchw_hw == 0 && (p.N & 3) == 0 && (e.ld_out & 3) == 0 && (!e.resid || (e.ld_resid & 3) == 0)) {
+      const int lane = row_in_tile & 31;
+      const int q = lane & 7, rsub = lane >> 3;
+      int64_t orows[8];
+      bool oks[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        orows[i] = __shfl_sync(0xffffffffu, static_cast<long long>(orow), rsub + 4 * i);
+        oks[i] = __shfl_sync(0xffffffffu, valid ? 1 : 0, rsub + 4 * i) != 0;
+      }
+      const bool slot_ok = __shfl_sync(0xffffffffu, row_ok ? 1 : 0, 0) != 0;
+      const int nch = BN / 32;
+      float4 rc[8], rn[8];
+      auto load_resid = [&](int cbx, float4* dst) {
+        const int col = cbx + 4 * q;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = (oks[i] && col < p.N) ? __ldg(reinterpret_cast<const float4*>(e.resid + orows[i] * e.ld_resid + col))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      };
+      if (e.resid) load_resid(col0, rc);
 #pragma unroll 1
-    for (int c = 0; c < kGemmBN / 32; ++c) {
+      for (int c = 0; c < nch; ++c) {
+        const int cb = col0 + c * 32;
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (cb >= p.N) continue;  // warp-uniform
+        float4* srow = reinterpret_cast<float4*>(stage + lane * kEpiStageStride);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          srow[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                                __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+        __syncwarp();
+        if (e.resid && c + 1 < nch && cb + 32 < p.N) load_resid(cb + 32, rn);
+        const int col = cb + 4 * q;
+        const bool col_ok = col < p.N;
+        const float4 bia = (e.bias && col_ok) ? __ldg(reinterpret_cast<const float4*>(e.bias + col))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        float gs0 = 0.f, gs1 = 0.f, gq0 = 0.f, gq1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 v = *reinterpret_cast<const float4*>(stage + (rsub + 4 * i) * kEpiStageStride + 4 * q);
+          v.x += bia.x; v.y += bia.y; v.z += bia.z; v.w += bia.w;
+          if (e.resid) {
+            v.x += rc[i].x; v.y += rc[i].y; v.z += rc[i].z; v.w += rc[i].w;
+          }
+          if (oks[i] && col_ok) {
+            if (e.out_f32) *reinterpret_cast<float4*>(e.out_f32 + orows[i] * e.ld_out + col) = v;
+            if (e.out_bf16)
+              *reinterpret_cast<uint2*>(e.out_bf16 + orows[i] * e.ld_out + col) =
+                  make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+            gs0 += v.x + v.y;
+            gq0 += v.x * v.x + v.y * v.y;
+            gs1 += v.z + v.w;
+            gq1 += v.z * v.z + v.w * v.w;
+          }
+        }
+        __syncwarp();  // the stage is rewritten by the next chunk
+        if (e.gn_part) {
+          float* part = e.gn_part + (row >> 5) * (2 * e.gn_groups);
+          const int cpg = e.gn_cpg;
+          if (cpg == 2) {  // channel pairs (col, col + 1) and (col + 2, col + 3) are two groups
+#pragma unroll
+            for (int o = 8; o <= 16; o <<= 1) {
+              gs0 += __shfl_xor_sync(0xffffffffu, gs0, o);
+              gq0 += __shfl_xor_sync(0xffffffffu, gq0, o);
+              gs1 += __shfl_xor_sync(0xffffffffu, gs1, o);
+              gq1 += __shfl_xor_sync(0xffffffffu, gq1, o);
+            }
+            if (slot_ok && rsub == 0 && col_ok) {
+              *reinterpret_cast<float4*>(part + col) = make_float4(gs0, gq0, gs1, gq1);
+            }
+          } else {
+            float gs = gs0 + gs1, gq = gq0 + gq1;
+#pragma unroll
+            for (int o = 8; o <= 16; o <<= 1) {
+              gs += __shfl_xor_sync(0xffffffffu, gs, o);
+              gq += __shfl_xor_sync(0xffffffffu, gq, o);
+            }
+            for (int o = 1; o < cpg / 4; o <<= 1) {
+              gs += __shfl_xor_sync(0xffffffffu, gs, o);
+              gq += __shfl_xor_sync(0xffffffffu, gq, o);
+            }
+            if (slot_ok && rsub == 0 && col_ok && (q & (cpg / 4 - 1)) == 0) {
+              const int g = col / cpg;
+              part[2 * g] = gs;
+              part[2 * g + 1] = gq;
+            }
+          }
+        }
+        if (e.resid) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rc[i] = rn[i];
+        }
+      }
+      return;
+    }
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
       const int cb = col0 + c * 32;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_ld_wait();
-      if (!row_ok || !pix_ok || cb >= p.N) continue;
+      if (cb >= p.N) continue;  // warp-uniform
       const int nv = min(32, p.N - cb);
       float v[32];
 #pragma unroll
@@ -253,7 +400,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
         for (int j = 0; j < 32; ++j)
           if (j < nv) v[j] += __ldg(e.bias + cb + j);
       }
-      if (e.resid) {
+      if (valid && e.resid) {
         const float* rs = e.resid + orow * e.ld_resid + cb;
         if (nv == 32 && (reinterpret_cast<uintptr_t>(rs) & 15) == 0) {
 #pragma unroll
@@ -267,6 +414,16 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
             if (j < nv) v[j] += rs[j];
         }
       }
+      if (e.gn_part) {
+        switch (e.gn_cpg) {
+          case 2: gn_chunk_stats<2>(e, v, valid, row_ok, nv, cb, row); break;
+          case 4: gn_chunk_stats<4>(e, v, valid, row_ok, nv, cb, row); break;
+          case 8: gn_chunk_stats<8>(e, v, valid, row_ok, nv, cb, row); break;
+          case 16: gn_chunk_stats<16>(e, v, valid, row_ok, nv, cb, row); break;
+          default: gn_chunk_stats<32>(e, v, valid, row_ok, nv, cb, row); break;
+        }
+      }
+      if (!valid) continue;
       if (e.nchw_hw > 0) {
         const int64_t bb = orow / e.nchw_hw, hw = orow - bb * e.nchw_hw;
         float* base = e.out_f32 + (bb * p.N + cb) * e.nchw_hw + hw;
@@ -334,7 +491,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     const int sub = lane >> 3, q = lane & 7;
     uint8_t* srow = reinterpret_cast<uint8_t*>(stage) + lane * kEpiStageRowBytes;
 #pragma unroll 1
-    for (int c = 0; c < kGemmBN / 64; ++c) {
+    for (int c = 0; c < BN / 64; ++c) {
       const int cb = col0 + c * 64;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -382,7 +539,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
   }
   const float dt = (e.mode == kEpiEuler) ? __ldg(e.dt) : 0.f;
 #pragma unroll 1
-  for (int c = 0; c < kGemmBN / 32; ++c) {
+  for (int c = 0; c < BN / 32; ++c) {
     const int cb = col0 + c * 32;
     uint32_t r[32];
     tmem_ld32(taddr + c * 32, r);
@@ -505,11 +662,16 @@ struct BCfg<kBSrcQ8_0> {
 
 template <int BSRC>
 constexpr int gemm_threads() { return (6 + BCfg<BSRC>::kDequantWarps) * 32; }
-template <int BSRC>
-constexpr int gemm_stage_bytes() { return kAStageBytes + kBStageBytes + BCfg<BSRC>::kRawBytes; }
-template <int BSRC>
-constexpr int gemm_smem_bytes() {
-  return BCfg<BSRC>::kStages * gemm_stage_bytes<BSRC>() + kEpiStageBytes + 1024 + 256;
+// Narrower N tiles (bf16 weights only) buy deeper pipelines.
+template <int BSRC, int BN>
+__host__ __device__ constexpr int gemm_stages() {
+  return BSRC != kBSrcBf16 || BN >= 256 ? BCfg<BSRC>::kStages : (BN >= 128 ? 6 : 8);
+}
+template <int BSRC, int BN>
+__host__ __device__ constexpr int gemm_stage_bytes() { return kAStageBytes + BN * kGemmBK * 2 + BCfg<BSRC>::kRawBytes; }
+template <int BSRC, int BN = kGemmBN>
+__host__ __device__ constexpr int gemm_smem_bytes() {
+  return gemm_stages<BSRC, BN>() * gemm_stage_bytes<BSRC, BN>() + kEpiStageBytes + 1024 + 256;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -648,19 +810,21 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 // ------------------------------------------------------------------ kernel
-template <int BSRC>
+template <int BSRC, int BN>
 __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                 const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
-  constexpr int kStages = BCfg<BSRC>::kStages;
+  constexpr int kStages = gemm_stages<BSRC, BN>();
   constexpr int kRaw = BCfg<BSRC>::kRawBytes;
   constexpr bool kQuant = BSRC != kBSrcBf16;
   constexpr int kDqThreads = BCfg<BSRC>::kDequantWarps * 32;
+  constexpr int kBSt = BN * kGemmBK * 2;  // B stage bytes
+  static_assert(!kQuant || BN == kGemmBN, "fused dequantisation uses 256-column tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + kStages * kAStageBytes;
-  uint8_t* smR = smB + kStages * kBStageBytes;  // raw quantised stages (kQuant)
+  uint8_t* smR = smB + kStages * kBSt;  // raw quantised stages (kQuant)
   float* epi_stage = reinterpret_cast<float*>(smR + kStages * kRaw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw + kEpiStageBytes);
   uint64_t* full = bars;                        // [stages] TMA A (+ raw B) landed
@@ -711,7 +875,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
         const TileCoord tc = decode_tile(p, t);
         const GemmGroup& G = p.groups[tc.g];
         const int ya = G.row0 + tc.m_tile * kGemmBM;
-        const int yb = tc.n_tile * kGemmBN;
+        const int yb = tc.n_tile * BN;
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
         const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
         for (int kb = 0; kb < nk; ++kb) {
@@ -722,14 +886,14 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
             bulk_load(smR + stage * kRaw, packed + (static_cast<int64_t>(tc.n_tile) * nk + kb) * kRaw, kRaw,
                       &full[stage]);
           } else {
-            mbar_arrive_expect_tx(&full[stage], kAStageBytes + kBStageBytes);
+            mbar_arrive_expect_tx(&full[stage], kAStageBytes + kBSt);
             if (p.conv.taps) {
               const ConvCoord cc = conv_coord(p.conv, ya, kb);
               tma_load_4d(smA + stage * kAStageBytes, &tmA, &full[stage], cc.c, cc.x, cc.y, cc.b);
             } else {
               tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
             }
-            tma_load_2d(smB + stage * kBStageBytes, tmB, &full[stage], kb * kGemmBK, yb);
+            tma_load_2d(smB + stage * kBSt, tmB, &full[stage], kb * kGemmBK, yb);
           }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
@@ -737,7 +901,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, kGemmBN);
+      constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -746,13 +910,13 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
       for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < nk; ++kb) {
           uint64_t* ready = kQuant ? &bready[stage] : &full[stage];
           if (!mbar_wait(ready, phase, p.err, kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(smA + stage * kAStageBytes);
-          const uint32_t b0 = smem_u32(smB + stage * kBStageBytes);
+          const uint32_t b0 = smem_u32(smB + stage * kBSt);
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             umma_bf16(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
@@ -778,8 +942,8 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
       if (!ok) break;
       tc_fence_after();
       const TileCoord tc = decode_tile(p, t);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-      epilogue_row(p, tc, tc.m_tile * kGemmBM, row_in_tile, taddr, epi_stage + quarter * 32 * kEpiStageStride);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      epilogue_row<BN, !kQuant>(p, tc, tc.m_tile * kGemmBM, row_in_tile, taddr, epi_stage + quarter * 32 * kEpiStageStride);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -795,7 +959,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, p.err, kDevTimeoutDequant));
         if (!ok) break;
         for (int rr = r; rr < kGemmBN; rr += kDqThreads)
-          dequant_row<BSRC>(smR + stage * kRaw, smB + stage * kBStageBytes, rr);
+          dequant_row<BSRC>(smR + stage * kRaw, smB + stage * kBSt, rr);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bready[stage]);
@@ -845,28 +1009,37 @@ struct PairCfg<kBSrcQ8_0> {
   static constexpr int kDequantWarps = 8;
 };
 constexpr int kPairA = 128 * kGemmBK * 2;  // 16 KB per CTA
-constexpr int kPairB = 128 * kGemmBK * 2;  // 16 KB per CTA (its half of the B tile)
 
 template <int BSRC>
 __host__ __device__ constexpr int pair_raw_bytes() { return 128 * (PairCfg<BSRC>::kQs + PairCfg<BSRC>::kSc); }
 template <int BSRC>
 __host__ __device__ constexpr int pair_threads() { return (6 + PairCfg<BSRC>::kDequantWarps) * 32; }
-template <int BSRC>
+template <int BSRC, int BN>
+__host__ __device__ constexpr int pair_stages() {
+  return BSRC != kBSrcBf16 || BN >= 256 ? PairCfg<BSRC>::kStages : 8;
+}
+template <int BSRC, int BN = kGemmBN>
 __host__ __device__ constexpr int pair_smem_bytes() {
-  return PairCfg<BSRC>::kStages * (kPairA + kPairB + pair_raw_bytes<BSRC>()) + kEpiStageBytes + 1024 + 256;
+  return pair_stages<BSRC, BN>() * (kPairA + (BN / 2) * kGemmBK * 2 + pair_raw_bytes<BSRC>()) + kEpiStageBytes +
+         1024 + 256;
 }
 
 static_assert(gemm_smem_bytes<kBSrcBf16>() <= 232448 && gemm_smem_bytes<kBSrcQ4_K>() <= 232448 &&
-                  gemm_smem_bytes<kBSrcQ8_0>() <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
+                  gemm_smem_bytes<kBSrcQ8_0>() <= 232448 && gemm_smem_bytes<kBSrcBf16, 128>() <= 232448 &&
+                  gemm_smem_bytes<kBSrcBf16, 64>() <= 232448 && gemm_smem_bytes<kBSrcBf16, 32>() <= 232448,
+              "GEMM shared memory above the 227 KB per-CTA limit");
 static_assert(pair_smem_bytes<kBSrcBf16>() <= 232448 && pair_smem_bytes<kBSrcQ4_K>() <= 232448 &&
-                  pair_smem_bytes<kBSrcQ8_0>() <= 232448, "pair GEMM shared memory above the 227 KB per-CTA limit");
+                  pair_smem_bytes<kBSrcQ8_0>() <= 232448 && pair_smem_bytes<kBSrcBf16, 128>() <= 232448,
+              "pair GEMM shared memory above the 227 KB per-CTA limit");
 
-template <int BSRC>
+template <int BSRC, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>(), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                      const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
-  constexpr int kStages = PairCfg<BSRC>::kStages;
+  constexpr int kStages = pair_stages<BSRC, BN>();
+  constexpr int kPB = (BN / 2) * kGemmBK * 2;  // this CTA's half of the B stage
   constexpr bool kQuant = BSRC != kBSrcBf16;
+  static_assert(!kQuant || BN == kGemmBN, "fused dequantisation uses 256-column tiles");
   constexpr int kQs = PairCfg<BSRC>::kQs, kSc = PairCfg<BSRC>::kSc;
   constexpr int kRaw = pair_raw_bytes<BSRC>();
   constexpr int kDqWarps = PairCfg<BSRC>::kDequantWarps;
@@ -874,7 +1047,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smA + kStages * kPairA;
-  uint8_t* smR = smB + kStages * kPairB;
+  uint8_t* smR = smB + kStages * kPB;
   float* epi_stage = reinterpret_cast<float*>(smR + kStages * kRaw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smR + kStages * kRaw + kEpiStageBytes);
   uint64_t* full = bars;                     // [stages] rank 0: A (+ B) bytes of both CTAs
@@ -933,13 +1106,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         const TileCoord tc = decode_tile(p, t);
         const GemmGroup& G = p.groups[tc.g];
         const int ya = G.row0 + tc.m_tile * 256 + static_cast<int>(rank) * 128;
-        const int yb = tc.n_tile * kGemmBN + static_cast<int>(rank) * 128;
+        const int yb = tc.n_tile * BN + static_cast<int>(rank) * (BN / 2);
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
         const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           const uint32_t full0 = mapa_shared(smem_u32(&full[stage]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPairB));
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPB));
           if (!kQuant && p.conv.taps) {
             const ConvCoord cc = conv_coord(p.conv, ya, kb);
             tma_load_4d_pair(smA + stage * kPairA, &tmA, full0, cc.c, cc.x, cc.y, cc.b);
@@ -952,7 +1125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
             bulk_load(smR + stage * kRaw, st + rank * 128 * kQs, 128 * kQs, &rfull[stage]);
             bulk_load(smR + stage * kRaw + 128 * kQs, st + 256 * kQs + rank * 128 * kSc, 128 * kSc, &rfull[stage]);
           } else {
-            tma_load_2d_pair(smB + stage * kPairB, tmB, full0, kb * kGemmBK, yb);
+            tma_load_2d_pair(smB + stage * kPB, tmB, full0, kb * kGemmBK, yb);
           }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
@@ -960,7 +1133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(256, kGemmBN);
+      constexpr uint32_t idesc = make_idesc_bf16(256, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -969,7 +1142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       for (int t = pair; t < p.total_tiles && ok; t += npairs) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
           if (kQuant && (!mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant) ||
@@ -979,7 +1152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(smA + stage * kPairA);
-          const uint32_t b0 = smem_u32(smB + stage * kPairB);
+          const uint32_t b0 = smem_u32(smB + stage * kPB);
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
@@ -1018,8 +1191,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       if (!ok) break;
       tc_fence_after();
       const TileCoord tc = decode_tile(p, t);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-      epilogue_row(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr,
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      epilogue_row<BN, !kQuant>(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr,
                    epi_stage + quarter * 32 * kEpiStageStride);
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
@@ -1036,7 +1209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       for (int kb = 0; kb < nk; ++kb) {
         ok = __all_sync(0xffffffffu, mbar_wait(&rfull[stage], phase, p.err, kDevTimeoutDequant));
         if (!ok) break;
-        dequant_half_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPairB, r, h);
+        dequant_half_row<BSRC, 128>(smR + stage * kRaw, smB + stage * kPB, r, h);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bready[stage]);
@@ -1071,35 +1244,35 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-template <int BSRC>
+template <int BSRC, int BN = kGemmBN>
 cudaError_t launch_gemm_t(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                           int num_sms, cudaStream_t stream) {
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         gemm_smem_bytes<BSRC>());
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BSRC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm_smem_bytes<BSRC, BN>());
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   const int grid = std::min(args.total_tiles, num_sms);
-  gemm_kernel<BSRC><<<grid, gemm_threads<BSRC>(), gemm_smem_bytes<BSRC>(), stream>>>(a, b0, b1, args);
+  gemm_kernel<BSRC, BN><<<grid, gemm_threads<BSRC>(), gemm_smem_bytes<BSRC, BN>(), stream>>>(a, b0, b1, args);
   return cudaGetLastError();
 }
 
-template <int BSRC>
+template <int BSRC, int BN = kGemmBN>
 cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                                const GemmArgs& args, int num_sms, cudaStream_t stream) {
   static int max_clusters = 0;
   if (max_clusters == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pair_smem_bytes<BSRC>());
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<BSRC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pair_smem_bytes<BSRC, BN>());
     if (e != cudaSuccess) return e;
     // Persistent grid: only as many pairs as can be resident at once (a GPC
     // with an odd SM count leaves one SM out of the pairs).
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
     cfg.blockDim = dim3(pair_threads<BSRC>(), 1, 1);
-    cfg.dynamicSmemBytes = pair_smem_bytes<BSRC>();
+    cfg.dynamicSmemBytes = pair_smem_bytes<BSRC, BN>();
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -1108,13 +1281,14 @@ cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, cons
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BSRC>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BSRC, BN>, &cfg);
     if (e != cudaSuccess) return e;
     if (n <= 0) return cudaErrorInvalidConfiguration;
     max_clusters = n;
   }
   const int pairs = std::min(args.total_tiles, max_clusters);
-  gemm_pair_kernel<BSRC><<<2 * pairs, pair_threads<BSRC>(), pair_smem_bytes<BSRC>(), stream>>>(a, b0, b1, args);
+  gemm_pair_kernel<BSRC, BN><<<2 * pairs, pair_threads<BSRC>(), pair_smem_bytes<BSRC, BN>(), stream>>>(a, b0, b1,
+                                                                                                       args);
   return cudaGetLastError();
 }
 
@@ -1123,8 +1297,11 @@ cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, cons
 cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                              int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
+  if (args.tile_n != kGemmBN && (bsrc != kBSrcBf16 || args.tile_n != 128)) return cudaErrorInvalidValue;
   switch (bsrc) {
-    case kBSrcBf16: return launch_gemm_pair_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
+    case kBSrcBf16:
+      return args.tile_n == 128 ? launch_gemm_pair_t<kBSrcBf16, 128>(a, b0, b1, args, num_sms, stream)
+                                : launch_gemm_pair_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
     case kBSrcQ4_K:
     case kBSrcQ8_0: {
       if (args.K % kGemmBK) return cudaErrorInvalidValue;
@@ -1173,8 +1350,9 @@ cudaError_t make_tmap_conv(CUtensorMap* map, const void* base, int64_t B, int64_
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-void gemm_finalize_groups(GemmArgs& a, int tile_m) {
-  a.n_tiles_n = (a.N + kGemmBN - 1) / kGemmBN;
+void gemm_finalize_groups(GemmArgs& a, int tile_m, int tile_n) {
+  a.tile_n = tile_n;
+  a.n_tiles_n = (a.N + tile_n - 1) / tile_n;
   int t = 0;
   for (int g = 0; g < a.n_groups; ++g) {
     a.groups[g].m_tiles = (a.groups[g].rows + tile_m - 1) / tile_m;
@@ -1187,8 +1365,16 @@ void gemm_finalize_groups(GemmArgs& a, int tile_m) {
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                         int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
+  if (args.tile_n != kGemmBN && bsrc != kBSrcBf16) return cudaErrorInvalidValue;
   switch (bsrc) {
-    case kBSrcBf16: return launch_gemm_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
+    case kBSrcBf16:
+      switch (args.tile_n) {
+        case 256: return launch_gemm_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
+        case 128: return launch_gemm_t<kBSrcBf16, 128>(a, b0, b1, args, num_sms, stream);
+        case 64: return launch_gemm_t<kBSrcBf16, 64>(a, b0, b1, args, num_sms, stream);
+        case 32: return launch_gemm_t<kBSrcBf16, 32>(a, b0, b1, args, num_sms, stream);
+        default: return cudaErrorInvalidValue;
+      }
     case kBSrcQ4_K:
     case kBSrcQ8_0: {
       if (args.K % kGemmBK) return cudaErrorInvalidValue;

@@ -99,6 +99,14 @@ struct EpilogueArgs {
   int64_t ld_resid;
   int32_t up_phase;
   int32_t nchw_hw;
+  // GroupNorm statistics of the stored values (implicit convolutions only):
+  // each warp's 32 accumulator rows write, per group g of gn_cpg channels
+  // in its columns, (sum, sum of squares) to
+  // gn_part[(row / 32) * 2 gn_groups + 2 g + {0, 1}] (rows outside the image
+  // count as zeros).  gn_cpg in {2, 4, 8, 16, 32}; null: none.
+  float* gn_part;
+  int32_t gn_cpg;
+  int32_t gn_groups;
 };
 
 // Implicit-GEMM convolution A operand over an NHWC bf16 image [B, H, W, C]
@@ -134,6 +142,7 @@ struct GemmArgs {
   EpilogueArgs ep;
   QuantB qb[2];
   ConvGeom conv;
+  int32_t tile_n;  // columns per tile (set by gemm_finalize_groups)
   int* err;
 };
 
@@ -165,7 +174,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
                              const GemmArgs& args, int bsrc, int num_sms, cudaStream_t stream);
 
 // Fill the tile prefix sums of `args` from its groups (M tile of tile_m rows:
-// 128 for launch_gemm, 256 for launch_gemm_pair).
-void gemm_finalize_groups(GemmArgs& args, int tile_m = kGemmBM);
+// 128 for launch_gemm, 256 for launch_gemm_pair; N tile of tile_n columns:
+// 256, or for bf16 weights 128 (both kernels) and 64 / 32 (launch_gemm) --
+// the B tensor map's box is tile_n rows, tile_n / 2 for the pair).
+void gemm_finalize_groups(GemmArgs& args, int tile_m = kGemmBM, int tile_n = kGemmBN);
 
 }  // namespace dcpp

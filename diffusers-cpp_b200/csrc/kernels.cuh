@@ -136,9 +136,11 @@ cudaError_t launch_softmax_rows(const float* S, int64_t rows, int64_t n, int64_t
                                 int64_t ld_p, cudaStream_t s);
 cudaError_t launch_transpose_bf16(const uint16_t* in, int64_t rows, int64_t cols, int64_t ld_in, uint16_t* out,
                                   int64_t ld_out, cudaStream_t s);
-// 3x3 convolution (pad 1) with Cout in {1, 3, 4}: X bf16 NHWC [B, H, W, C],
-// w f32 [Cout][9][C] (tap = 3 ky + kx), bias [Cout] -> out f32 NCHW.
-cudaError_t launch_conv3x3_small(const uint16_t* X, int B, int H, int W, int C, int Cout, const float* w,
-                                 const float* bias, float* out, cudaStream_t s);
+// GroupNorm statistics from convolution-epilogue partial sums (gn_part of
+// EpilogueArgs): n_regions launches, each region_stride floats, of
+// B x slots_per_img slots of 2 G floats -> stats [B, G, 2] (double,
+// accumulated: zero it first).
+cudaError_t launch_gn_finalize(const float* part, int n_regions, int64_t region_stride, int64_t slots_per_img, int B,
+                               int G, double* stats, cudaStream_t s);
 
 }  // namespace dcpp

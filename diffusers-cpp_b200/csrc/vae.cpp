@@ -369,16 +369,7 @@ void AutoencoderKLFlux2Decoder::build_weights() {
     prev = out;
   }
   norms_["decoder.conv_norm_out"] = make_norm("decoder.conv_norm_out");
-  {
-    const auto& w = host("decoder.conv_out.weight");  // [Cout, C, 3, 3] -> [Cout][9][C]
-    const int64_t Co = c.out_channels, C = ch[0];
-    std::vector<float> r(static_cast<size_t>(Co * 9 * C));
-    for (int64_t co = 0; co < Co; ++co)
-      for (int64_t ci = 0; ci < C; ++ci)
-        for (int t = 0; t < 9; ++t) r[(co * 9 + t) * C + ci] = w[(co * C + ci) * 9 + t];
-    conv_out_w_ = f32_upload(r);
-    conv_out_b_ = f32_upload(host("decoder.conv_out.bias"));
-  }
+  convs_["decoder.conv_out"] = make_conv("decoder.conv_out", ch[0], false);
   weights_built_ = true;
 }
 
@@ -388,7 +379,7 @@ void AutoencoderKLFlux2Decoder::free_weights() {
   convs_.clear();
   norms_.clear();
   attn_qkv_w_ = attn_out_w_ = nullptr;
-  attn_qkv_b_ = attn_out_b_ = conv_out_w_ = conv_out_b_ = bn_mean_ = bn_var_ = nullptr;
+  attn_qkv_b_ = attn_out_b_ = bn_mean_ = bn_var_ = nullptr;
   weights_built_ = false;
 }
 
@@ -451,8 +442,14 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   cuda_check(cudaMemset(zq, 0, B * P0 * Lpad * 2), "memset zq");
   float* X[2] = {static_cast<float*>(alloc(E * 4)), static_cast<float*>(alloc(E * 4))};
   uint16_t* Xb[2] = {static_cast<uint16_t*>(alloc(E * 2)), static_cast<uint16_t*>(alloc(E * 2))};
-  auto* Hb = static_cast<float*>(alloc(E * 4));
+  auto* Hb = static_cast<uint16_t*>(alloc(E * 2));  // conv1 outputs (bf16: only GroupNorm reads them)
   auto* Sc = static_cast<float*>(alloc(E * 4));
+  // GroupNorm partial sums written by the producing convolution's epilogue
+  // (one buffer for the residual stream's producer, one for conv1).
+  const int64_t Hf = h0 * c.scale_factor(), Wf = w0 * c.scale_factor();
+  const int64_t part_floats = B * 4 * (round_up(Wf, 128) * round_up(Hf, 8) / 128) * 2 * G + 64;
+  float* part_x = static_cast<float*>(alloc(part_floats * 4));
+  float* part_h = static_cast<float*>(alloc(part_floats * 4));
   auto* A = static_cast<uint16_t*>(alloc(E * 2));
   constexpr int kMaxNorms = 128;
   auto* stats = static_cast<double*>(alloc(kMaxNorms * B * G * 2 * sizeof(double)));
@@ -474,13 +471,18 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   int* err = ctx_.d_err;
   begin_ops(ops_);
 
+  // N tile: the narrowest of 32 / 64 / 128 / 256 columns holding N (32 and
+  // 64 only on the one-SM kernel).
+  auto tile_for = [](int64_t N) { return N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256; };
+
   // Plain GEMM: Y[M, N] = A[M, K] . W[N, K]^T with the conv epilogue.
   auto add_mm = [&](const std::string& tag, const uint16_t* a, int64_t lda, int64_t M, int64_t K, const uint16_t* w,
                     int64_t ldw, int64_t N, EpilogueArgs ep, int mode = kEpiConv) {
-    const bool pair = cx->use_pair(M);
+    const int tn = tile_for(N);
+    const bool pair = cx->use_pair(M) && tn >= 128;
     auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
     cuda_check(make_tmap_bf16(&(*maps)[0], a, K, M, lda, kGemmBM), "tensor map A");
-    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, ldw, pair ? 128 : kGemmBN), "tensor map W");
+    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, ldw, pair ? tn / 2 : tn), "tensor map W");
     GemmArgs g{};
     g.N = static_cast<int32_t>(N);
     g.K = static_cast<int32_t>(K);
@@ -490,7 +492,7 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     if (mode == kEpiConv) ep.up_phase = -1;
     g.ep = ep;
     g.err = err;
-    gemm_finalize_groups(g, pair ? 256 : kGemmBM);
+    gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
     building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
                             const auto& m = *maps;
                             if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "vae gemm (pair)");
@@ -500,9 +502,17 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   };
 
   // Implicit-GEMM convolution over x [B, H, W, C] bf16 with the given taps.
+  // Where the GroupNorm of a tensor finds its statistics: partial sums from
+  // the producing convolutions (n regions of `stride` floats, `slots` 32-row
+  // slots per image), or none (a statistics pass over the tensor).
+  struct StatSrc {
+    float* part = nullptr;
+    int n = 0;
+    int64_t stride = 0, slots = 0;
+  };
   auto add_conv = [&](const std::string& tag, const uint16_t* x, int64_t H, int64_t W, int64_t C,
                       const std::vector<std::pair<int, int>>& taps, const uint16_t* w, int64_t N, EpilogueArgs ep,
-                      int up_phase) {
+                      int up_phase, StatSrc* stats_out = nullptr, int region = 0) {
     int tw = 128;
     int64_t best = -1;
     for (int cand : {128, 64, 32, 16}) {
@@ -520,10 +530,11 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     if (taps.empty() || taps.size() > 9 || C % 64) fail(DCPP_ERR_UNSUPPORTED, "internal: convolution taps / channels");
     const size_t n_taps = std::min<size_t>(taps.size(), 9);
     const int64_t K = static_cast<int64_t>(n_taps) * C;
-    const bool pair = cx->use_pair(rows);
+    const int tn = tile_for(N);
+    const bool pair = cx->use_pair(rows) && tn >= 128;
     auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
     cuda_check(make_tmap_conv(&(*maps)[0], x, B, H, W, C, tw, th), "tensor map conv");
-    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, K, pair ? 128 : kGemmBN), "tensor map conv W");
+    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, K, pair ? tn / 2 : tn), "tensor map conv W");
     GemmArgs g{};
     g.N = static_cast<int32_t>(N);
     g.K = static_cast<int32_t>(K);
@@ -531,6 +542,22 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     g.groups[0].rows = static_cast<int32_t>(rows);
     ep.mode = kEpiConv;
     ep.up_phase = up_phase;
+    if (stats_out) {
+      const int64_t cpg = N / G;
+      const int64_t slots = tiles_x * tiles_y * 4;
+      const int64_t stride = B * slots * 2 * G;
+      if (N % G == 0 && (cpg == 2 || cpg == 4 || cpg == 8 || cpg == 16 || cpg == 32) &&
+          (region + 1) * stride <= part_floats && (region == 0 || stats_out->stride == stride)) {
+        ep.gn_part = stats_out->part + region * stride;
+        ep.gn_cpg = static_cast<int32_t>(cpg);
+        ep.gn_groups = static_cast<int32_t>(G);
+        stats_out->n = region + 1;
+        stats_out->stride = stride;
+        stats_out->slots = slots;
+      } else {
+        stats_out->part = nullptr;  // the GroupNorm computes its own statistics
+      }
+    }
     g.ep = ep;
     g.err = err;
     g.conv.taps = static_cast<int32_t>(n_taps);
@@ -545,7 +572,7 @@ void AutoencoderKLFlux2Decoder::build_plan() {
       g.conv.dy[t] = static_cast<int8_t>(taps[t].first);
       g.conv.dx[t] = static_cast<int8_t>(taps[t].second);
     }
-    gemm_finalize_groups(g, pair ? 256 : kGemmBM);
+    gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
     building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
                             const auto& m = *maps;
                             if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "conv (pair)");
@@ -568,19 +595,31 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     return e;
   };
 
-  // GroupNorm (+ SiLU) of x (f32 [B, HW, C]) into the bf16 operand A.
-  auto group_norm = [&](const std::string& tag, const float* x, int64_t HW, int64_t C, const Norm& n, bool silu) {
+  // GroupNorm (+ SiLU) of x (bf16 [B, HW, C]) into the bf16 operand A, with
+  // the statistics from the producer's partial sums when it left them.
+  auto group_norm = [&](const std::string& tag, const uint16_t* x, int64_t HW, int64_t C, const Norm& n, bool silu,
+                        const StatSrc& src) {
     if (n_norms >= kMaxNorms) fail(DCPP_ERR_UNSUPPORTED, "too many GroupNorms");
     double* st = stats + static_cast<int64_t>(n_norms++) * B * G * 2;
     const float eps = 1e-6f;
+    if (src.part) {
+      const StatSrc sc = src;
+      building_->push_back({[=](cudaStream_t s) {
+                              cuda_check(launch_gn_finalize(sc.part, sc.n, sc.stride, sc.slots, static_cast<int>(B),
+                                                            static_cast<int>(G), st, s),
+                                         "gn finalize");
+                            },
+                            1, kOpNorm, 0.0, tag + " stats"});
+    } else {
+      building_->push_back({[=](cudaStream_t s) {
+                              cuda_check(launch_gn_stats(x, true, static_cast<int>(B), HW, static_cast<int>(C),
+                                                         static_cast<int>(G), st, s),
+                                         "gn stats");
+                            },
+                            1, kOpNorm, 0.0, tag + " stats"});
+    }
     building_->push_back({[=](cudaStream_t s) {
-                            cuda_check(launch_gn_stats(x, false, static_cast<int>(B), HW, static_cast<int>(C),
-                                                       static_cast<int>(G), st, s),
-                                       "gn stats");
-                          },
-                          1, kOpNorm, 0.0, tag + " stats"});
-    building_->push_back({[=](cudaStream_t s) {
-                            cuda_check(launch_gn_apply(x, false, static_cast<int>(B), HW, static_cast<int>(C),
+                            cuda_check(launch_gn_apply(x, true, static_cast<int>(B), HW, static_cast<int>(C),
                                                        static_cast<int>(G), st, n.gamma, n.beta, eps, silu, A, s),
                                        "gn apply");
                           },
@@ -614,9 +653,11 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     z = zq;
   }
   int cur = 0;
+  StatSrc x_src;  // statistics of the residual stream X[cur]
   {
     const Conv& ci = convs_.at("decoder.conv_in");
-    add_conv("conv_in", z, h0, w0, Lpad, taps3, ci.w, top, conv_ep(X[0], Xb[0], top, ci.bias, nullptr), -1);
+    x_src.part = part_x;
+    add_conv("conv_in", z, h0, w0, Lpad, taps3, ci.w, top, conv_ep(X[0], Xb[0], top, ci.bias, nullptr), -1, &x_src);
   }
 
   // ResnetBlock2D (ResnetBlock2D.inl:108-190) at H x W: X[cur] (+ Xb[cur]) -> X[cur ^ 1] (+ Xb[cur ^ 1]).
@@ -624,9 +665,11 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     const Conv& c1 = convs_.at(n + ".conv1");
     const Conv& c2 = convs_.at(n + ".conv2");
     const int64_t cout = c1.cout, HW = H * W;
-    group_norm(n + ".norm1", X[cur], HW, cin, norms_.at(n + ".norm1"), true);
-    add_conv(n + ".conv1", A, H, W, cin, taps3, c1.w, cout, conv_ep(Hb, nullptr, cout, c1.bias, nullptr), -1);
-    group_norm(n + ".norm2", Hb, HW, cout, norms_.at(n + ".norm2"), true);
+    group_norm(n + ".norm1", Xb[cur], HW, cin, norms_.at(n + ".norm1"), true, x_src);
+    StatSrc h_src;
+    h_src.part = part_h;
+    add_conv(n + ".conv1", A, H, W, cin, taps3, c1.w, cout, conv_ep(nullptr, Hb, cout, c1.bias, nullptr), -1, &h_src);
+    group_norm(n + ".norm2", Hb, HW, cout, norms_.at(n + ".norm2"), true, h_src);
     const float* resid = X[cur];
     auto sc = convs_.find(n + ".conv_shortcut");
     if (sc != convs_.end()) {
@@ -634,7 +677,10 @@ void AutoencoderKLFlux2Decoder::build_plan() {
              conv_ep(Sc, nullptr, cout, sc->second.bias, nullptr));
       resid = Sc;
     }
-    add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout, conv_ep(X[cur ^ 1], Xb[cur ^ 1], cout, c2.bias, resid), -1);
+    x_src = StatSrc();
+    x_src.part = part_x;
+    add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout, conv_ep(X[cur ^ 1], Xb[cur ^ 1], cout, c2.bias, resid), -1,
+             &x_src);
     cur ^= 1;
   };
 
@@ -643,7 +689,7 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   if (c.mid_block_add_attention) {
     const std::string p = "decoder.mid_block.attentions.0";
     const int64_t C = top;
-    group_norm(p + ".group_norm", X[cur], P0, C, norms_.at(p + ".group_norm"), false);
+    group_norm(p + ".group_norm", Xb[cur], P0, C, norms_.at(p + ".group_norm"), false, x_src);
     add_mm(p + ".to_qkv", A, C, B * P0, C, attn_qkv_w_, C, 3 * C, conv_ep(nullptr, qkv, 3 * C, attn_qkv_b_, nullptr));
     const float scale = 1.0f / std::sqrt(static_cast<float>(C));
     for (int64_t b = 0; b < B; ++b) {
@@ -664,6 +710,7 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     }
     add_mm(p + ".to_out", O, C, B * P0, C, attn_out_w_, C, C, conv_ep(X[cur ^ 1], Xb[cur ^ 1], C, attn_out_b_, X[cur]));
     cur ^= 1;
+    x_src = StatSrc();  // the next GroupNorm runs its own statistics pass
   }
   resnet("decoder.mid_block.resnets.1", h0, w0, top);
 
@@ -678,13 +725,15 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     }
     if (i < n_up - 1) {
       const Conv& up = convs_.at(b + ".upsamplers.0.conv");
+      x_src = StatSrc();
+      x_src.part = part_x;
       for (int ph = 0; ph < 4; ++ph) {
         const int a = ph >> 1, bb = ph & 1;
         std::vector<std::pair<int, int>> taps;
         for (int ty = 0; ty < 2; ++ty)
           for (int tx = 0; tx < 2; ++tx) taps.push_back({a - 1 + ty, bb - 1 + tx});
         add_conv(b + ".upsample phase " + std::to_string(ph), Xb[cur], H, W, out, taps, up.phase[ph], out,
-                 conv_ep(X[cur ^ 1], Xb[cur ^ 1], out, up.bias, nullptr), ph);
+                 conv_ep(X[cur ^ 1], Xb[cur ^ 1], out, up.bias, nullptr), ph, x_src.part ? &x_src : nullptr, ph);
       }
       cur ^= 1;
       H *= 2;
@@ -694,17 +743,14 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   }
 
   // 5. conv_norm_out, SiLU, conv_out (Decoder.hpp:132-162) -> NCHW image.
-  group_norm("decoder.conv_norm_out", X[cur], H * W, ch[0], norms_.at("decoder.conv_norm_out"), true);
+  group_norm("decoder.conv_norm_out", Xb[cur], H * W, ch[0], norms_.at("decoder.conv_norm_out"), true, x_src);
   {
-    float* img = img_dev_;
-    const float *w = conv_out_w_, *bias = conv_out_b_;
-    const int Cin = static_cast<int>(ch[0]), Co = static_cast<int>(c.out_channels);
-    const int Hi = static_cast<int>(H), Wi = static_cast<int>(W);
-    building_->push_back({[=](cudaStream_t s) {
-                            cuda_check(launch_conv3x3_small(A, static_cast<int>(B), Hi, Wi, Cin, Co, w, bias, img, s),
-                                       "conv_out");
-                          },
-                          1, kOpOther, 2.0 * B * H * W * Co * 9 * Cin, "decoder.conv_out"});
+    // A few output channels: a 32-column tile on one SM, the epilogue
+    // storing the f32 image planes (NCHW) directly.
+    const Conv& co = convs_.at("decoder.conv_out");
+    EpilogueArgs e = conv_ep(img_dev_, nullptr, c.out_channels, co.bias, nullptr);
+    e.nchw_hw = static_cast<int32_t>(H * W);
+    add_conv("decoder.conv_out", A, H, W, ch[0], taps3, co.w, c.out_channels, e, -1);
   }
   end_ops();
   launches_per_step_ = 0;

@@ -18,7 +18,8 @@
 // upsampled image is never materialised; GroupNorm is a statistics pass and
 // an apply (+ SiLU) pass producing the bf16 GEMM operand; the mid-block
 // attention (one head of dim C over all pixels) is QK^T GEMM -> row softmax
-// -> PV GEMM; conv_out (3 channels) is a CUDA-core kernel.
+// -> PV GEMM; conv_out (3 channels) runs on 32-column tiles of the one-SM
+// GEMM with an epilogue that writes the NCHW image.
 #pragma once
 
 #include <cuda.h>
@@ -109,8 +110,6 @@ class AutoencoderKLFlux2Decoder : public StepPlanner {
   float* attn_qkv_b_ = nullptr;     // [3C]
   uint16_t* attn_out_w_ = nullptr;
   float* attn_out_b_ = nullptr;
-  float* conv_out_w_ = nullptr;     // [Cout][9][C] f32
-  float* conv_out_b_ = nullptr;
   float* bn_mean_ = nullptr;
   float* bn_var_ = nullptr;
 

@@ -5,9 +5,11 @@
 //   GroupNorm statistics and GroupNorm (+ SiLU) application
 //       (GroupNorm.cpp: ggml_norm over (C/G) x H x W per group, eps 1e-6, affine)
 //   row softmax of the mid-block attention scores (SoftmaxAttentionOp.cpp)
-//   bf16 transpose, 3x3 convolution with few output channels (conv_out)
+//   bf16 transpose
 // Images are NHWC: pixel (b, y, x) is row (b H + y) W + x, channels contiguous.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -101,45 +103,67 @@ __global__ void __launch_bounds__(256) gn_stats_kernel(const T* __restrict__ x, 
 }
 
 // y = (x - mean_g) * rstd_g * gamma + beta (optionally SiLU), bf16 out;
-// grid (x, b): 8 channels per thread and step.
+// grid (x, b).  Every thread owns one 8-channel column block for the whole
+// launch (the grid stride is a multiple of C / 8), so its scale / shift
+// coefficients stay in registers and the loop is 16-byte loads and stores.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float v[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float v[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<uint16_t>(const uint16_t* p, float v[8]) {
+  const uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = __uint_as_float(w[k] << 16);
+    v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) gn_apply_kernel(const T* __restrict__ x, int64_t HW, int C, int G,
                                                         const double* __restrict__ stats,
                                                         const float* __restrict__ gamma,
                                                         const float* __restrict__ beta, float eps, int silu,
                                                         uint16_t* __restrict__ y) {
-  extern __shared__ float coef[];  // [2 C]: scale, shift
   const int b = blockIdx.y;
   const int cpg = C / G;
-  const double n = static_cast<double>(HW) * cpg;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    const int g = c / cpg;
-    const double mean = stats[(static_cast<int64_t>(b) * G + g) * 2] / n;
-    const double var = fmax(stats[(static_cast<int64_t>(b) * G + g) * 2 + 1] / n - mean * mean, 0.0);
-    const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
-    const float a = rstd * gamma[c];
-    coef[c] = a;
-    coef[C + c] = beta[c] - static_cast<float>(mean) * a;
+  const int cu = C / 8;  // 8-channel blocks per pixel; divides 256
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c0 = (tid % cu) * 8;
+  float a[8], sh[8];
+  const double inv_n = 1.0 / (static_cast<double>(HW) * cpg);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int c = c0 + k, g = c / cpg;
+    // Mean and variance in double (the sums are large), rstd in float.
+    const double mean = stats[(static_cast<int64_t>(b) * G + g) * 2] * inv_n;
+    const double var = fmax(stats[(static_cast<int64_t>(b) * G + g) * 2 + 1] * inv_n - mean * mean, 0.0);
+    const float rstd = rsqrtf(static_cast<float>(var) + eps);
+    a[k] = rstd * __ldg(gamma + c);
+    sh[k] = __ldg(beta + c) - static_cast<float>(mean) * a[k];
   }
-  __syncthreads();
-  const int64_t units = HW * (C / 8);
+  const int64_t units = HW * cu;
   const T* xb = x + static_cast<int64_t>(b) * HW * C;
   uint16_t* yb = y + static_cast<int64_t>(b) * HW * C;
-  for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < units;
-       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+#pragma unroll 4
+  for (int64_t u = tid; u < units; u += stride) {
     const int64_t e = u * 8;
-    const int c0 = static_cast<int>(e % C);
     float v[8];
-    load4<T>(xb + e, v);
-    load4<T>(xb + e + 4, v + 4);
+    load8<T>(xb + e, v);
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
-      float a0 = v[k] * coef[c0 + k] + coef[C + c0 + k];
-      float a1 = v[k + 1] * coef[c0 + k + 1] + coef[C + c0 + k + 1];
-      if (silu) {
-        a0 = a0 / (1.f + __expf(-a0));
-        a1 = a1 / (1.f + __expf(-a1));
+      float a0 = fmaf(v[k], a[k], sh[k]);
+      float a1 = fmaf(v[k + 1], a[k + 1], sh[k + 1]);
+      if (silu) {  // the result is rounded to bf16: fast division suffices
+        a0 = __fdividef(a0, 1.f + __expf(-a0));
+        a1 = __fdividef(a1, 1.f + __expf(-a1));
       }
       o[k / 2] = pack_bf16x2(a0, a1);
     }
@@ -222,48 +246,32 @@ __global__ void transpose_bf16_kernel(const uint16_t* __restrict__ in, int64_t r
   }
 }
 
-// ------------------------------------------------------- small-Cout conv3x3
-// out[b, co, y, x] = bias[co] + sum_{tap, c} w[co][tap][c] * X[b, y+dy, x+dx, c]
-// (pad 1), X bf16 NHWC, out f32 NCHW; one thread per pixel, weights in smem.
-template <int kCout>
-__global__ void __launch_bounds__(128) conv3x3_small_kernel(const uint16_t* __restrict__ X, int B, int H, int W,
-                                                            int C, const float* __restrict__ w,
-                                                            const float* __restrict__ bias, float* __restrict__ out) {
-  extern __shared__ float ws[];  // [kCout][9][C]
-  for (int i = threadIdx.x; i < kCout * 9 * C; i += blockDim.x) ws[i] = w[i];
+// GroupNorm statistics from the partial sums a convolution epilogue wrote
+// (gn_part, EpilogueArgs): stats[b, g] += sums over regions and slots (stats
+// zeroed first).  Block (x, b, region) reads kSlots consecutive slots as
+// whole coalesced rows of 2 G floats; thread t keeps element t % 2G.
+constexpr int kFinalizeSlots = 64;
+__global__ void __launch_bounds__(256) gn_finalize_kernel(const float* __restrict__ part, int64_t region_stride,
+                                                          int64_t slots_per_img, int G,
+                                                          double* __restrict__ stats) {
+  const int b = blockIdx.y;
+  const int e2 = 2 * G;
+  const int el = threadIdx.x % e2;
+  const int sub = threadIdx.x / e2, nsub = blockDim.x / e2;
+  const float* base = part + blockIdx.z * region_stride + static_cast<int64_t>(b) * slots_per_img * e2;
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kFinalizeSlots;
+  const int64_t s1 = min(slots_per_img, s0 + kFinalizeSlots);
+  double acc = 0.0;
+  if (sub < nsub)
+    for (int64_t sl = s0 + sub; sl < s1; sl += nsub) acc += base[sl * e2 + el];
+  __shared__ double red[256];
+  red[threadIdx.x] = acc;
   __syncthreads();
-  const int64_t HW = static_cast<int64_t>(H) * W;
-  const int64_t pix = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (pix >= B * HW) return;
-  const int b = static_cast<int>(pix / HW);
-  const int64_t hw = pix - b * HW;
-  const int y = static_cast<int>(hw / W), x = static_cast<int>(hw % W);
-  float acc[kCout];
-#pragma unroll
-  for (int co = 0; co < kCout; ++co) acc[co] = bias[co];
-  for (int tap = 0; tap < 9; ++tap) {
-    const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
-    if (yy < 0 || yy >= H || xx < 0 || xx >= W) continue;
-    const uint16_t* src = X + ((static_cast<int64_t>(b) * H + yy) * W + xx) * C;
-    for (int c = 0; c < C; c += 8) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(src + c));
-      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-      float v[8];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[2 * k] = __uint_as_float(wd[k] << 16);
-        v[2 * k + 1] = __uint_as_float(wd[k] & 0xFFFF0000u);
-      }
-#pragma unroll
-      for (int co = 0; co < kCout; ++co) {
-        const float* wr = ws + (co * 9 + tap) * C + c;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[co] = fmaf(wr[k], v[k], acc[co]);
-      }
-    }
+  if (threadIdx.x < e2) {
+    double t = 0.0;
+    for (int k = 0; k < nsub; ++k) t += red[k * e2 + threadIdx.x];
+    atomicAdd(&stats[static_cast<int64_t>(b) * e2 + threadIdx.x], t);
   }
-#pragma unroll
-  for (int co = 0; co < kCout; ++co) out[(static_cast<int64_t>(b) * kCout + co) * HW + hw] = acc[co];
 }
 
 int grid_for(int64_t units, int threads) {
@@ -298,16 +306,17 @@ cudaError_t launch_gn_stats(const void* x, bool bf16, int B, int64_t HW, int C, 
 cudaError_t launch_gn_apply(const void* x, bool bf16, int B, int64_t HW, int C, int G, const double* stats,
                             const float* gamma, const float* beta, float eps, bool silu, uint16_t* y,
                             cudaStream_t s) {
-  if (C % 8 != 0 || C % G != 0) return cudaErrorInvalidValue;
+  if (C % 8 != 0 || C % G != 0 || 256 % (C / 8) != 0) return cudaErrorInvalidValue;
   const int64_t units = HW * (C / 8);
-  dim3 grid(static_cast<unsigned>(grid_for(units, 256) / B + 1), static_cast<unsigned>(B));
-  const size_t sh = sizeof(float) * 2 * C;
+  // Eight resident blocks per SM over the whole launch.
+  int64_t blocks = std::min<int64_t>((units + 255) / 256, std::max<int64_t>(1, 148 * 8 / B));
+  dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(B));
   if (bf16)
-    gn_apply_kernel<uint16_t><<<grid, 256, sh, s>>>(static_cast<const uint16_t*>(x), HW, C, G, stats, gamma, beta,
-                                                    eps, silu ? 1 : 0, y);
+    gn_apply_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), HW, C, G, stats, gamma, beta,
+                                                   eps, silu ? 1 : 0, y);
   else
-    gn_apply_kernel<float><<<grid, 256, sh, s>>>(static_cast<const float*>(x), HW, C, G, stats, gamma, beta, eps,
-                                                 silu ? 1 : 0, y);
+    gn_apply_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), HW, C, G, stats, gamma, beta, eps,
+                                                silu ? 1 : 0, y);
   return cudaGetLastError();
 }
 
@@ -325,29 +334,12 @@ cudaError_t launch_transpose_bf16(const uint16_t* in, int64_t rows, int64_t cols
   return cudaGetLastError();
 }
 
-cudaError_t launch_conv3x3_small(const uint16_t* X, int B, int H, int W, int C, int Cout, const float* w,
-                                 const float* bias, float* out, cudaStream_t s) {
-  if (C % 8 != 0) return cudaErrorInvalidValue;
-  const int64_t pixels = static_cast<int64_t>(B) * H * W;
-  const unsigned grid = static_cast<unsigned>((pixels + 127) / 128);
-  const size_t sh = sizeof(float) * Cout * 9 * C;
-  if (sh > 200 * 1024) return cudaErrorInvalidValue;
-  switch (Cout) {
-    case 1:
-      cudaFuncSetAttribute(conv3x3_small_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sh));
-      conv3x3_small_kernel<1><<<grid, 128, sh, s>>>(X, B, H, W, C, w, bias, out);
-      break;
-    case 3:
-      cudaFuncSetAttribute(conv3x3_small_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sh));
-      conv3x3_small_kernel<3><<<grid, 128, sh, s>>>(X, B, H, W, C, w, bias, out);
-      break;
-    case 4:
-      cudaFuncSetAttribute(conv3x3_small_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sh));
-      conv3x3_small_kernel<4><<<grid, 128, sh, s>>>(X, B, H, W, C, w, bias, out);
-      break;
-    default:
-      return cudaErrorInvalidValue;
-  }
+cudaError_t launch_gn_finalize(const float* part, int n_regions, int64_t region_stride, int64_t slots_per_img, int B,
+                               int G, double* stats, cudaStream_t s) {
+  if (2 * G > 256) return cudaErrorInvalidValue;
+  dim3 grid(static_cast<unsigned>((slots_per_img + kFinalizeSlots - 1) / kFinalizeSlots), static_cast<unsigned>(B),
+            static_cast<unsigned>(n_regions));
+  gn_finalize_kernel<<<grid, 256, 0, s>>>(part, region_stride, slots_per_img, G, stats);
   return cudaGetLastError();
 }
 
