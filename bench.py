@@ -556,7 +556,7 @@ def run_qwen3(args):
     return 0
 
 
-VAE_METRIC = "Flux2 VAE decode images/s at 1024x1024"
+VAE_METRIC = "Flux2 VAE decode images/s (1024x1024 by default)"
 
 
 def run_vae(args):
@@ -574,7 +574,7 @@ def run_vae(args):
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         raise SystemExit("--config vae runs on one GPU")
     c = synth.VAECfg()
-    B, ph, pw = 1, 64, 64
+    B, ph, pw = 1, args.vae_packed, args.vae_packed
     ctx = dcpp_b200.Context(0)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -590,7 +590,7 @@ def run_vae(args):
     lat = synth.make_vae_latents(c, B, ph, pw, seed=1)
     lat_dev = lat.cuda()
     lat_p = lat.pin_memory()
-    H = W = 2 * ph * 8
+    H, W = 2 * ph * 8, 2 * pw * 8
     img = torch.empty(B, c.out_channels, H, W, device="cuda")
     img_p = torch.empty(B, c.out_channels, H, W).pin_memory()
     for _ in range(args.warmup):
@@ -616,7 +616,7 @@ def run_vae(args):
     assert torch.isfinite(img_p).all(), "non-finite image"
     if args.ops_csv:
         os.makedirs(args.ops_csv, exist_ok=True)
-        os.environ["DCPP_PROFILE_OPS"] = os.path.join(args.ops_csv, "ops_vae_1024.csv")
+        os.environ["DCPP_PROFILE_OPS"] = os.path.join(args.ops_csv, f"ops_vae_{H}.csv")
     m.set_profiling(True)
     m.prepare(B, ph, pw, use_graph=False)
     for _ in range(2):
@@ -641,8 +641,8 @@ def run_vae(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1/fan_in) F32 weights; N(0,1) packed latents)",
-        "config": {"workload": "vae: Flux2 VAE decode (128/256/512/512 channels, 2 layers per block, 32 latent "
-                               "channels), 64 x 64 packed tokens -> 1024 x 1024 image, untiled",
+        "config": {"workload": f"vae: Flux2 VAE decode (128/256/512/512 channels, 2 layers per block, 32 latent "
+                               f"channels), {ph} x {pw} packed tokens -> {H} x {W} image, untiled",
                    "global_batch": B, "parallelism": "tp1",
                    "l2": "no flush: every decode streams > 10 GB of activations through the 126 MB L2",
                    "cuda_graph": not args.no_graph},
@@ -676,6 +676,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
     ap.add_argument("--attn-kernel", type=int, default=0, help="0 auto, 1 one query tile per CTA, 2 two tiles")
+    ap.add_argument("--vae-packed", type=int, default=64, help="--config vae: packed tokens per side (64: 1024^2)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1227,6 +1227,181 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
   }
 }
 
+// ------------------------------------------------------------------ conv halo
+// Implicit 3x3 / phase convolution on CTA pairs with halo reuse (ConvGeom.halo):
+// each CTA's 128-row A block is one image row segment of 128 pixels; per
+// 64-channel block the producer loads the 3 x 130-pixel patch around it
+// once (one 4-D TMA box, zero fill outside the image), and the MMA of tap
+// (dy, dx) reads the 128 rows of the patch starting at row
+// (dy + 1) * 130 + dx + 1 -- a shifted view of the 128-byte-swizzled patch
+// (the swizzle follows the shared-memory address bits, which TMA and the
+// MMA both use, so a view may start at any 128-byte row with a plain
+// descriptor; checked against the float64 oracle).  B (bf16 weights) streams one
+// (tap, channel block) stage at a time as in gemm_pair_kernel; the
+// epilogue is the same.
+constexpr int kPatchW = 130, kPatchH = 3;
+constexpr int kPatchTxBytes = kPatchW * kPatchH * 128;      // 49920
+constexpr int kPatchBytes = (kPatchTxBytes + 1023) / 1024 * 1024;
+template <int BN>
+__host__ __device__ constexpr int halo_stages() { return BN >= 256 ? 6 : 8; }
+template <int BN>
+__host__ __device__ constexpr int halo_smem_bytes() {
+  return 2 * kPatchBytes + halo_stages<BN>() * (BN / 2) * kGemmBK * 2 + kEpiStageBytes + 1024 + 256;
+}
+static_assert(halo_smem_bytes<256>() <= 232448 && halo_smem_bytes<128>() <= 232448,
+              "halo conv shared memory above the 227 KB per-CTA limit");
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    conv_halo_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ GemmArgs p) {
+  constexpr int kStages = halo_stages<BN>();
+  constexpr int kPB = (BN / 2) * kGemmBK * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smP = smem;                      // [2] patches
+  uint8_t* smB = smP + 2 * kPatchBytes;     // [kStages] this CTA's half of the B stage
+  float* epi_stage = reinterpret_cast<float*>(smB + kStages * kPB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smB + kStages * kPB + kEpiStageBytes);
+  uint64_t* bfull = bars;                   // [stages] rank 0: B bytes of both CTAs
+  uint64_t* bempty = bars + kStages;        // [stages] both
+  uint64_t* pfull = bars + 2 * kStages;     // [2] rank 0: patch bytes of both CTAs
+  uint64_t* pempty = pfull + 2;             // [2] both
+  uint64_t* acc_full = pempty + 2;          // [2] both
+  uint64_t* acc_empty = acc_full + 2;       // [2] rank 0
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const ConvGeom& cg = p.conv;
+  const int ncb = cg.cin_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&pfull[a], 1);
+      mbar_init(&pempty[a], 1);
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 256);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int bs = 0, ps = 0;
+      uint32_t bph = 0, pph = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        const TileCoord tc = decode_tile(p, t);
+        const GemmGroup& G = p.groups[tc.g];
+        const int blk = (G.row0 + tc.m_tile * 256 + static_cast<int>(rank) * 128) >> 7;
+        const int per_img = cg.tiles_x * cg.tiles_y;
+        const int b = blk / per_img;
+        const int rem = blk - b * per_img;
+        const int y0 = rem / cg.tiles_x;
+        const int x0 = (rem - y0 * cg.tiles_x) * 128;
+        const int yb = tc.n_tile * BN + static_cast<int>(rank) * (BN / 2);
+        for (int cb = 0; cb < ncb && ok; ++cb) {
+          if (!mbar_wait(&pempty[ps], pph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&pfull[ps], 2 * kPatchTxBytes);
+          tma_load_4d_pair(smP + ps * kPatchBytes, &tmP, mapa_shared(smem_u32(&pfull[ps]), 0), cb * 64, x0 - 1,
+                           y0 - 1, b);
+          for (int tap = 0; tap < cg.taps; ++tap) {
+            if (!mbar_wait(&bempty[bs], bph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+            if (rank == 0) mbar_arrive_expect_tx(&bfull[bs], 2 * kPB);
+            tma_load_2d_pair(smB + bs * kPB, &tmB, mapa_shared(smem_u32(&bfull[bs]), 0),
+                             (tap * ncb + cb) * kGemmBK, yb);
+            if (++bs == kStages) { bs = 0; bph ^= 1; }
+          }
+          if (++ps == 2) { ps = 0; pph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(256, BN);
+      int bs = 0, ps = 0, acc = 0;
+      uint32_t bph = 0, pph = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool first = true;
+        for (int cb = 0; cb < ncb && ok; ++cb) {
+          if (!mbar_wait(&pfull[ps], pph, p.err, kDevTimeoutFull)) { ok = false; break; }
+          const uint32_t patch = smem_u32(smP + ps * kPatchBytes);
+          for (int tap = 0; tap < cg.taps; ++tap) {
+            if (!mbar_wait(&bfull[bs], bph, p.err, kDevTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a0 = patch + static_cast<uint32_t>((cg.dy[tap] + 1) * kPatchW + cg.dx[tap] + 1) * 128u;
+            const uint32_t b0 = smem_u32(smB + bs * kPB);
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
+                             (first && k == 0) ? 0u : 1u);
+            }
+            first = false;
+            umma_commit_pair(&bempty[bs], 0x3);
+            if (++bs == kStages) { bs = 0; bph ^= 1; }
+          }
+          umma_commit_pair(&pempty[ps], 0x3);
+          if (++ps == 2) { ps = 0; pph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc], 0x3);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < p.total_tiles; t += npairs) {
+      bool ok = mbar_wait(&acc_full[acc], acc_phase, p.err, kDevTimeoutAccum);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const TileCoord tc = decode_tile(p, t);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      epilogue_row<BN, true>(p, tc, tc.m_tile * 256 + static_cast<int>(rank) * 128, row_in_tile, taddr,
+                             epi_stage + quarter * 32 * kEpiStageStride);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
                                    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
@@ -1292,12 +1467,52 @@ cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, cons
   return cudaGetLastError();
 }
 
+template <int BN>
+cudaError_t launch_conv_halo_t(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int num_sms,
+                               cudaStream_t stream) {
+  static int max_clusters = 0;
+  if (max_clusters == 0) {
+    cudaError_t e = cudaFuncSetAttribute(conv_halo_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         halo_smem_bytes<BN>());
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = halo_smem_bytes<BN>();
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, conv_halo_pair_kernel<BN>, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    max_clusters = n;
+  }
+  const int pairs = std::min(args.total_tiles, max_clusters);
+  conv_halo_pair_kernel<BN><<<2 * pairs, 192, halo_smem_bytes<BN>(), stream>>>(a, b, args);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                              int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
   if (args.tile_n != kGemmBN && (bsrc != kBSrcBf16 || args.tile_n != 128)) return cudaErrorInvalidValue;
+  if (args.conv.halo) {
+    if (bsrc != kBSrcBf16 || args.conv.taps < 1 || args.conv.taps > 9 || args.conv.tile_w != 128 ||
+        args.conv.tile_h != 1)
+      return cudaErrorInvalidValue;
+    for (int t = 0; t < args.conv.taps; ++t)
+      if (args.conv.dy[t] < -1 || args.conv.dy[t] > 1 || args.conv.dx[t] < -1 || args.conv.dx[t] > 1)
+        return cudaErrorInvalidValue;
+    return args.tile_n == 128 ? launch_conv_halo_t<128>(a, b0, args, num_sms, stream)
+                              : launch_conv_halo_t<256>(a, b0, args, num_sms, stream);
+  }
   switch (bsrc) {
     case kBSrcBf16:
       return args.tile_n == 128 ? launch_gemm_pair_t<kBSrcBf16, 128>(a, b0, b1, args, num_sms, stream)
@@ -1343,6 +1558,23 @@ cudaError_t make_tmap_conv(CUtensorMap* map, const void* base, int64_t B, int64_
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(C * 2), static_cast<cuuint64_t>(W * C * 2),
                            static_cast<cuuint64_t>(H * W * C * 2)};
   cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tile_w), static_cast<cuuint32_t>(tile_h), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t make_tmap_conv_patch(CUtensorMap* map, const void* base, int64_t B, int64_t H, int64_t W, int64_t C) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return cudaErrorMisalignedAddress;
+  if (C % 64 != 0) return cudaErrorInvalidValue;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C * 2), static_cast<cuuint64_t>(W * C * 2),
+                           static_cast<cuuint64_t>(H * W * C * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(kPatchW), static_cast<cuuint32_t>(kPatchH), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -123,7 +123,12 @@ struct ConvGeom {
   int32_t H, W;
   int32_t tile_w, tile_h;
   int32_t tiles_x, tiles_y;
-  int8_t dy[9], dx[9];
+  int8_t dy[9], dx[9];  // tap offsets, each in [-1, 1]
+  // 1 (CTA-pair kernel, bf16 weights, 128 x 1 rectangles): the A map is a
+  // halo patch map (make_tmap_conv_patch) and every 64-channel block of a
+  // rectangle is loaded once as a 3 x 130-pixel patch, each tap reading its
+  // shifted 128-row view of it, instead of one box per tap.
+  int32_t halo;
 };
 
 // A quantised weight packed per (256-row tile, 64-K stage) by
@@ -156,6 +161,9 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, u
 // of an implicit-GEMM convolution (ConvGeom).
 cudaError_t make_tmap_conv(CUtensorMap* map, const void* base, int64_t B, int64_t H, int64_t W, int64_t C,
                            int tile_w, int tile_h);
+
+// The halo patch map of the same image: (64 channel, 130, 3, 1) boxes.
+cudaError_t make_tmap_conv_patch(CUtensorMap* map, const void* base, int64_t B, int64_t H, int64_t W, int64_t C);
 
 // Launch the grouped GEMM.  `a` maps X (box 64 x 128), b0/b1 map the two
 // bf16 weights (box 64 x 256) when bsrc == kBSrcBf16.

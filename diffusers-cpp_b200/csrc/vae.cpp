@@ -532,8 +532,14 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     const int64_t K = static_cast<int64_t>(n_taps) * C;
     const int tn = tile_for(N);
     const bool pair = cx->use_pair(rows) && tn >= 128;
+    // Rows of 128 pixels on CTA pairs: halo patches (one load per channel
+    // block serves every tap).
+    const bool halo = pair && tw == 128 && th == 1;
     auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
-    cuda_check(make_tmap_conv(&(*maps)[0], x, B, H, W, C, tw, th), "tensor map conv");
+    if (halo)
+      cuda_check(make_tmap_conv_patch(&(*maps)[0], x, B, H, W, C), "tensor map conv patch");
+    else
+      cuda_check(make_tmap_conv(&(*maps)[0], x, B, H, W, C, tw, th), "tensor map conv");
     cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, K, pair ? tn / 2 : tn), "tensor map conv W");
     GemmArgs g{};
     g.N = static_cast<int32_t>(N);
@@ -568,6 +574,7 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     g.conv.tile_h = th;
     g.conv.tiles_x = static_cast<int32_t>(tiles_x);
     g.conv.tiles_y = static_cast<int32_t>(tiles_y);
+    g.conv.halo = halo ? 1 : 0;
     for (size_t t = 0; t < n_taps; ++t) {
       g.conv.dy[t] = static_cast<int8_t>(taps[t].first);
       g.conv.dx[t] = static_cast<int8_t>(taps[t].second);

@@ -50,6 +50,7 @@ CASES = [
     ((64, 128, 128), 1, 2, 3, 5),      # ragged: widths 10, 20, 40 -> partial rectangles
     ((128, 128, 256, 256), 1, 1, 4, 8),
     ((64, 64), 2, 1, 9, 16),           # wide rows (W = 32, 64), shortcut-free
+    ((64, 128, 128), 1, 1, 6, 40),     # W = 160, 320: halo patches with a partial last patch per row
 ]
 
 
