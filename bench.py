@@ -586,7 +586,7 @@ def run_vae(args):
         m.set_param(name, gt, shp, data.cpu())
     del params
     load_s = time.time() - t0
-    m.prepare(B, ph, pw, use_graph=not args.no_graph)
+    m.prepare(B, ph, pw, use_graph=not args.no_graph, tile_size=args.vae_tile)
     lat = synth.make_vae_latents(c, B, ph, pw, seed=1)
     lat_dev = lat.cuda()
     lat_p = lat.pin_memory()
@@ -618,7 +618,7 @@ def run_vae(args):
         os.makedirs(args.ops_csv, exist_ok=True)
         os.environ["DCPP_PROFILE_OPS"] = os.path.join(args.ops_csv, f"ops_vae_{H}.csv")
     m.set_profiling(True)
-    m.prepare(B, ph, pw, use_graph=False)
+    m.prepare(B, ph, pw, use_graph=False, tile_size=args.vae_tile)
     for _ in range(2):
         m.decode(lat_dev, img)
     torch.cuda.synchronize()
@@ -642,7 +642,8 @@ def run_vae(args):
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1/fan_in) F32 weights; N(0,1) packed latents)",
         "config": {"workload": f"vae: Flux2 VAE decode (128/256/512/512 channels, 2 layers per block, 32 latent "
-                               f"channels), {ph} x {pw} packed tokens -> {H} x {W} image, untiled",
+                               f"channels), {ph} x {pw} packed tokens -> {H} x {W} image, "
+                               + (f"tiled ({args.vae_tile}-pixel tiles)" if args.vae_tile else "untiled"),
                    "global_batch": B, "parallelism": "tp1",
                    "l2": "no flush: every decode streams > 10 GB of activations through the 126 MB L2",
                    "cuda_graph": not args.no_graph},
@@ -677,6 +678,7 @@ def main():
     ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
     ap.add_argument("--attn-kernel", type=int, default=0, help="0 auto, 1 one query tile per CTA, 2 two tiles")
     ap.add_argument("--vae-packed", type=int, default=64, help="--config vae: packed tokens per side (64: 1024^2)")
+    ap.add_argument("--vae-tile", type=int, default=0, help="--config vae: decode_tiled tile size in pixels (0: untiled)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

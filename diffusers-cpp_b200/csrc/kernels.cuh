@@ -131,7 +131,8 @@ cudaError_t launch_gn_stats(const void* x, bool bf16, int B, int64_t HW, int C, 
 cudaError_t launch_gn_apply(const void* x, bool bf16, int B, int64_t HW, int C, int G, const double* stats,
                             const float* gamma, const float* beta, float eps, bool silu, uint16_t* y,
                             cudaStream_t s);
-// P = softmax(scale * S) over each row of n columns (bf16 out).
+// P = softmax(scale * S) over each row of n columns (bf16 out); row strides
+// multiples of 4 elements.
 cudaError_t launch_softmax_rows(const float* S, int64_t rows, int64_t n, int64_t ld_s, float scale, uint16_t* P,
                                 int64_t ld_p, cudaStream_t s);
 cudaError_t launch_transpose_bf16(const uint16_t* in, int64_t rows, int64_t cols, int64_t ld_in, uint16_t* out,
@@ -142,5 +143,14 @@ cudaError_t launch_transpose_bf16(const uint16_t* in, int64_t rows, int64_t cols
 // accumulated: zero it first).
 cudaError_t launch_gn_finalize(const float* part, int n_regions, int64_t region_stride, int64_t slots_per_img, int B,
                                int G, double* stats, cudaStream_t s);
+
+// Tiled VAE decode: blend tile T [B, C, h, w] (f32 NCHW) in place with the
+// tile above (ha rows high; its last ev rows, may be null) and then the tile
+// to the left (wl columns wide; its last eh columns, may be null) with the
+// linear ramps of diffusers' blend_v / blend_h, and copy its top-left
+// keep_h x keep_w band into out [B, C, H, W] at (oy, ox).
+cudaError_t launch_tile_blend(float* T, const float* above, int64_t ha, const float* left, int64_t wl, int B, int C,
+                              int64_t h, int64_t w, int64_t ev, int64_t eh, int64_t keep_h, int64_t keep_w, float* out,
+                              int64_t H, int64_t W, int64_t oy, int64_t ox, cudaStream_t s);
 
 }  // namespace dcpp

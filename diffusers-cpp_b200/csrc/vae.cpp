@@ -394,16 +394,27 @@ void AutoencoderKLFlux2Decoder::free_plan() {
   planned_ = false;
 }
 
-void AutoencoderKLFlux2Decoder::prepare(int64_t batch, int64_t packed_h, int64_t packed_w, bool use_graph) {
+void AutoencoderKLFlux2Decoder::prepare(int64_t batch, int64_t packed_h, int64_t packed_w, bool use_graph,
+                                        int64_t tile_size) {
   auto miss = missing();
   if (!miss.empty())
     fail(DCPP_ERR_STATE, "parameters not set: " + miss.front() + " (+" + std::to_string(miss.size() - 1) + " more)");
   if (batch < 1 || packed_h < 1 || packed_w < 1 || batch * packed_h * packed_w * 256 > (int64_t(1) << 26))
     fail(DCPP_ERR_UNSUPPORTED, "batch x image size out of range");
-  if (planned_ && batch == B_ && packed_h == ph_ && packed_w == pw_ && use_graph == use_graph_) return;
+  if (tile_size < 0) fail(DCPP_ERR_INVALID_ARG, "decode_tiled(): tile size must be positive");
+  if (tile_size > 0) {
+    const int64_t scale = cfg_.scale_factor();
+    if (tile_size % scale != 0)
+      fail(DCPP_ERR_INVALID_ARG, "decode_tiled(): tile size must be divisible by the VAE's scale factor");
+    if (tile_size / scale * 3 / 4 < 1)
+      fail(DCPP_ERR_INVALID_ARG, "tiled_forward(): tile size too small (3/4 of it must be >= 1)");
+  }
+  if (planned_ && batch == B_ && packed_h == ph_ && packed_w == pw_ && use_graph == use_graph_ && tile_size == tile_)
+    return;
   cudaStreamSynchronize(ctx_.stream);
   free_plan();
   if (!weights_built_) build_weights();
+  tile_ = tile_size;
   B_ = batch;
   ph_ = packed_h;
   pw_ = packed_w;
@@ -416,228 +427,80 @@ void AutoencoderKLFlux2Decoder::build_plan() {
   const auto& c = cfg_;
   const auto& ch = c.block_out_channels;
   const int64_t B = B_, L = c.latent_channels, Lpad = round_up(L, 64), G = c.norm_num_groups;
-  const int64_t h0 = 2 * ph_, w0 = 2 * pw_, P0 = h0 * w0;
   const int n_up = static_cast<int>(ch.size());
   const int64_t top = ch.back();
   auto alloc = [&](size_t bytes) { return dev_alloc(bytes, allocs_); };
 
-  // Largest pixels x channels of any activation.
-  int64_t max_pc = P0 * std::max(top, Lpad);
-  {
-    int64_t P = P0, prev = top;
-    for (int i = 0; i < n_up; ++i) {
-      const int64_t out = ch[n_up - 1 - i];
-      max_pc = std::max(max_pc, P * std::max(prev, out));
-      if (i < n_up - 1) P *= 4;
-      max_pc = std::max(max_pc, P * out);
-      prev = out;
-    }
-  }
-  const int64_t E = B * max_pc;
   lat_dev_ = static_cast<float*>(alloc(B * ph_ * pw_ * 4 * L * 4));
+  const int64_t h0 = 2 * ph_, w0 = 2 * pw_;
   const int64_t Hout = h0 * c.scale_factor(), Wout = w0 * c.scale_factor();
   img_dev_ = static_cast<float*>(alloc(B * c.out_channels * Hout * Wout * 4));
-  auto* zin = static_cast<uint16_t*>(alloc(B * P0 * Lpad * 2));
-  auto* zq = static_cast<uint16_t*>(alloc(B * P0 * Lpad * 2));
-  cuda_check(cudaMemset(zq, 0, B * P0 * Lpad * 2), "memset zq");
-  float* X[2] = {static_cast<float*>(alloc(E * 4)), static_cast<float*>(alloc(E * 4))};
-  uint16_t* Xb[2] = {static_cast<uint16_t*>(alloc(E * 2)), static_cast<uint16_t*>(alloc(E * 2))};
-  auto* Hb = static_cast<uint16_t*>(alloc(E * 2));  // conv1 outputs (bf16: only GroupNorm reads them)
-  auto* Sc = static_cast<float*>(alloc(E * 4));
-  // GroupNorm partial sums written by the producing convolution's epilogue
-  // (one buffer for the residual stream's producer, one for conv1).
-  const int64_t Hf = h0 * c.scale_factor(), Wf = w0 * c.scale_factor();
-  const int64_t part_floats = B * 4 * (round_up(Wf, 128) * round_up(Hf, 8) / 128) * 2 * G + 64;
-  float* part_x = static_cast<float*>(alloc(part_floats * 4));
-  float* part_h = static_cast<float*>(alloc(part_floats * 4));
-  auto* A = static_cast<uint16_t*>(alloc(E * 2));
+  auto* zfull = static_cast<uint16_t*>(alloc(B * h0 * w0 * Lpad * 2));
   constexpr int kMaxNorms = 128;
-  auto* stats = static_cast<double*>(alloc(kMaxNorms * B * G * 2 * sizeof(double)));
-  int n_norms = 0;
-  const int64_t Pk = round_up(P0, 64);
-  uint16_t *qkv = nullptr, *vt = nullptr, *Pm = nullptr, *O = nullptr;
-  float* S = nullptr;
-  if (c.mid_block_add_attention) {
-    qkv = static_cast<uint16_t*>(alloc(B * P0 * 3 * top * 2));
-    vt = static_cast<uint16_t*>(alloc(top * Pk * 2));
-    cuda_check(cudaMemset(vt, 0, top * Pk * 2), "memset vt");
-    S = static_cast<float*>(alloc(P0 * Pk * 4));
-    Pm = static_cast<uint16_t*>(alloc(P0 * Pk * 2));
-    cuda_check(cudaMemset(Pm, 0, P0 * Pk * 2), "memset P");
-    O = static_cast<uint16_t*>(alloc(B * P0 * top * 2));
-  }
+
+  // Activation buffers of one decode of an h x w latent image (one set per
+  // distinct size: the tiles of a tiled decode share them).
+  struct Bufs {
+    float* X[2] = {nullptr, nullptr};
+    uint16_t* Xb[2] = {nullptr, nullptr};
+    uint16_t *Hb = nullptr, *A = nullptr, *zq = nullptr, *qkv = nullptr, *vt = nullptr, *Pm = nullptr, *O = nullptr;
+    float *Sc = nullptr, *S = nullptr, *part_x = nullptr, *part_h = nullptr;
+    double* stats = nullptr;
+    int64_t part_floats = 0;
+  };
+  std::map<std::pair<int64_t, int64_t>, Bufs> bufs;
+  auto get_bufs = [&](int64_t h0, int64_t w0) -> Bufs& {
+    auto key = std::make_pair(h0, w0);
+    auto it = bufs.find(key);
+    if (it != bufs.end()) return it->second;
+    Bufs& d = bufs[key];
+    const int64_t P0 = h0 * w0;
+    // Largest pixels x channels of any activation.
+    int64_t max_pc = P0 * std::max(top, Lpad);
+    {
+      int64_t P = P0, prev = top;
+      for (int i = 0; i < n_up; ++i) {
+        const int64_t out = ch[n_up - 1 - i];
+        max_pc = std::max(max_pc, P * std::max(prev, out));
+        if (i < n_up - 1) P *= 4;
+        max_pc = std::max(max_pc, P * out);
+        prev = out;
+      }
+    }
+    const int64_t E = B * max_pc;
+    d.zq = static_cast<uint16_t*>(alloc(B * P0 * Lpad * 2));
+    cuda_check(cudaMemset(d.zq, 0, B * P0 * Lpad * 2), "memset zq");
+    for (int k = 0; k < 2; ++k) {
+      d.X[k] = static_cast<float*>(alloc(E * 4));
+      d.Xb[k] = static_cast<uint16_t*>(alloc(E * 2));
+    }
+    d.Hb = static_cast<uint16_t*>(alloc(E * 2));  // conv1 outputs (bf16: only GroupNorm reads them)
+    d.Sc = static_cast<float*>(alloc(E * 4));
+    // GroupNorm partial sums written by the producing convolution's epilogue
+    // (one buffer for the residual stream's producer, one for conv1).
+    const int64_t Hf = h0 * c.scale_factor(), Wf = w0 * c.scale_factor();
+    d.part_floats = B * 4 * (round_up(Wf, 128) * round_up(Hf, 8) / 128) * 2 * G + 64;
+    d.part_x = static_cast<float*>(alloc(d.part_floats * 4));
+    d.part_h = static_cast<float*>(alloc(d.part_floats * 4));
+    d.A = static_cast<uint16_t*>(alloc(E * 2));
+    d.stats = static_cast<double*>(alloc(kMaxNorms * B * G * 2 * sizeof(double)));
+    const int64_t Pk = round_up(P0, 64);
+    if (c.mid_block_add_attention) {
+      d.qkv = static_cast<uint16_t*>(alloc(B * P0 * 3 * top * 2));
+      d.vt = static_cast<uint16_t*>(alloc(top * Pk * 2));
+      cuda_check(cudaMemset(d.vt, 0, top * Pk * 2), "memset vt");
+      d.S = static_cast<float*>(alloc(P0 * Pk * 4));
+      d.Pm = static_cast<uint16_t*>(alloc(P0 * Pk * 2));
+      cuda_check(cudaMemset(d.Pm, 0, P0 * Pk * 2), "memset P");
+      d.O = static_cast<uint16_t*>(alloc(B * P0 * top * 2));
+    }
+
+  return d;
+  };
 
   Ctx* cx = &ctx_;
   int* err = ctx_.d_err;
   begin_ops(ops_);
-
-  // N tile: the narrowest of 32 / 64 / 128 / 256 columns holding N (32 and
-  // 64 only on the one-SM kernel).
-  auto tile_for = [](int64_t N) { return N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256; };
-
-  // Plain GEMM: Y[M, N] = A[M, K] . W[N, K]^T with the conv epilogue.
-  auto add_mm = [&](const std::string& tag, const uint16_t* a, int64_t lda, int64_t M, int64_t K, const uint16_t* w,
-                    int64_t ldw, int64_t N, EpilogueArgs ep, int mode = kEpiConv) {
-    const int tn = tile_for(N);
-    const bool pair = cx->use_pair(M) && tn >= 128;
-    auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
-    cuda_check(make_tmap_bf16(&(*maps)[0], a, K, M, lda, kGemmBM), "tensor map A");
-    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, ldw, pair ? tn / 2 : tn), "tensor map W");
-    GemmArgs g{};
-    g.N = static_cast<int32_t>(N);
-    g.K = static_cast<int32_t>(K);
-    g.n_groups = 1;
-    g.groups[0].rows = static_cast<int32_t>(M);
-    ep.mode = mode;
-    if (mode == kEpiConv) ep.up_phase = -1;
-    g.ep = ep;
-    g.err = err;
-    gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
-    building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
-                            const auto& m = *maps;
-                            if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "vae gemm (pair)");
-                            else cuda_check(launch_gemm(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "vae gemm");
-                          },
-                          1, kOpGemm, 2.0 * M * N * K, tag});
-  };
-
-  // Implicit-GEMM convolution over x [B, H, W, C] bf16 with the given taps.
-  // Where the GroupNorm of a tensor finds its statistics: partial sums from
-  // the producing convolutions (n regions of `stride` floats, `slots` 32-row
-  // slots per image), or none (a statistics pass over the tensor).
-  struct StatSrc {
-    float* part = nullptr;
-    int n = 0;
-    int64_t stride = 0, slots = 0;
-  };
-  auto add_conv = [&](const std::string& tag, const uint16_t* x, int64_t H, int64_t W, int64_t C,
-                      const std::vector<std::pair<int, int>>& taps, const uint16_t* w, int64_t N, EpilogueArgs ep,
-                      int up_phase, StatSrc* stats_out = nullptr, int region = 0) {
-    int tw = 128;
-    int64_t best = -1;
-    for (int cand : {128, 64, 32, 16}) {
-      const int th = 128 / cand;
-      const int64_t cover = round_up(W, cand) * round_up(H, th);
-      if (best < 0 || cover < best) {
-        best = cover;
-        tw = cand;
-      }
-    }
-    const int th = 128 / tw;
-    const int64_t tiles_x = (W + tw - 1) / tw, tiles_y = (H + th - 1) / th;
-    const int64_t rows = B * tiles_x * tiles_y * 128;
-    if (rows >= (int64_t(1) << 31)) fail(DCPP_ERR_UNSUPPORTED, "convolution too large");
-    if (taps.empty() || taps.size() > 9 || C % 64) fail(DCPP_ERR_UNSUPPORTED, "internal: convolution taps / channels");
-    const size_t n_taps = std::min<size_t>(taps.size(), 9);
-    const int64_t K = static_cast<int64_t>(n_taps) * C;
-    const int tn = tile_for(N);
-    const bool pair = cx->use_pair(rows) && tn >= 128;
-    // Rows of 128 pixels on CTA pairs: halo patches (one load per channel
-    // block serves every tap).
-    const bool halo = pair && tw == 128 && th == 1;
-    auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
-    if (halo)
-      cuda_check(make_tmap_conv_patch(&(*maps)[0], x, B, H, W, C), "tensor map conv patch");
-    else
-      cuda_check(make_tmap_conv(&(*maps)[0], x, B, H, W, C, tw, th), "tensor map conv");
-    cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, K, pair ? tn / 2 : tn), "tensor map conv W");
-    GemmArgs g{};
-    g.N = static_cast<int32_t>(N);
-    g.K = static_cast<int32_t>(K);
-    g.n_groups = 1;
-    g.groups[0].rows = static_cast<int32_t>(rows);
-    ep.mode = kEpiConv;
-    ep.up_phase = up_phase;
-    if (stats_out) {
-      const int64_t cpg = N / G;
-      const int64_t slots = tiles_x * tiles_y * 4;
-      const int64_t stride = B * slots * 2 * G;
-      if (N % G == 0 && (cpg == 2 || cpg == 4 || cpg == 8 || cpg == 16 || cpg == 32) &&
-          (region + 1) * stride <= part_floats && (region == 0 || stats_out->stride == stride)) {
-        ep.gn_part = stats_out->part + region * stride;
-        ep.gn_cpg = static_cast<int32_t>(cpg);
-        ep.gn_groups = static_cast<int32_t>(G);
-        stats_out->n = region + 1;
-        stats_out->stride = stride;
-        stats_out->slots = slots;
-      } else {
-        stats_out->part = nullptr;  // the GroupNorm computes its own statistics
-      }
-    }
-    g.ep = ep;
-    g.err = err;
-    g.conv.taps = static_cast<int32_t>(n_taps);
-    g.conv.cin_blocks = static_cast<int32_t>(C / 64);
-    g.conv.H = static_cast<int32_t>(H);
-    g.conv.W = static_cast<int32_t>(W);
-    g.conv.tile_w = tw;
-    g.conv.tile_h = th;
-    g.conv.tiles_x = static_cast<int32_t>(tiles_x);
-    g.conv.tiles_y = static_cast<int32_t>(tiles_y);
-    g.conv.halo = halo ? 1 : 0;
-    for (size_t t = 0; t < n_taps; ++t) {
-      g.conv.dy[t] = static_cast<int8_t>(taps[t].first);
-      g.conv.dx[t] = static_cast<int8_t>(taps[t].second);
-    }
-    gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
-    building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
-                            const auto& m = *maps;
-                            if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "conv (pair)");
-                            else cuda_check(launch_gemm(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "conv");
-                          },
-                          1, kOpGemm, 2.0 * B * H * W * N * K, tag});
-  };
-  std::vector<std::pair<int, int>> taps3;
-  for (int ky = 0; ky < 3; ++ky)
-    for (int kx = 0; kx < 3; ++kx) taps3.push_back({ky - 1, kx - 1});
-
-  auto conv_ep = [](float* out_f32, uint16_t* out_bf16, int64_t ld, const float* bias, const float* resid) {
-    EpilogueArgs e{};
-    e.out_f32 = out_f32;
-    e.out_bf16 = out_bf16;
-    e.ld_out = ld;
-    e.bias = bias;
-    e.resid = resid;
-    e.ld_resid = ld;
-    return e;
-  };
-
-  // GroupNorm (+ SiLU) of x (bf16 [B, HW, C]) into the bf16 operand A, with
-  // the statistics from the producer's partial sums when it left them.
-  auto group_norm = [&](const std::string& tag, const uint16_t* x, int64_t HW, int64_t C, const Norm& n, bool silu,
-                        const StatSrc& src) {
-    if (n_norms >= kMaxNorms) fail(DCPP_ERR_UNSUPPORTED, "too many GroupNorms");
-    double* st = stats + static_cast<int64_t>(n_norms++) * B * G * 2;
-    const float eps = 1e-6f;
-    if (src.part) {
-      const StatSrc sc = src;
-      building_->push_back({[=](cudaStream_t s) {
-                              cuda_check(launch_gn_finalize(sc.part, sc.n, sc.stride, sc.slots, static_cast<int>(B),
-                                                            static_cast<int>(G), st, s),
-                                         "gn finalize");
-                            },
-                            1, kOpNorm, 0.0, tag + " stats"});
-    } else {
-      building_->push_back({[=](cudaStream_t s) {
-                              cuda_check(launch_gn_stats(x, true, static_cast<int>(B), HW, static_cast<int>(C),
-                                                         static_cast<int>(G), st, s),
-                                         "gn stats");
-                            },
-                            1, kOpNorm, 0.0, tag + " stats"});
-    }
-    building_->push_back({[=](cudaStream_t s) {
-                            cuda_check(launch_gn_apply(x, true, static_cast<int>(B), HW, static_cast<int>(C),
-                                                       static_cast<int>(G), st, n.gamma, n.beta, eps, silu, A, s),
-                                       "gn apply");
-                          },
-                          1, kOpNorm, 0.0, tag});
-  };
-
-  // Zero every GroupNorm statistics slot once per decode.
-  building_->push_back({[=](cudaStream_t s) {
-                          cuda_check(cudaMemsetAsync(stats, 0, kMaxNorms * B * G * 2 * sizeof(double), s), "memset stats");
-                        },
-                        0, kOpOther, 0.0, "zero stats"});
 
   // 1. Packed tokens -> de-normalised, unpatchified z (Flux2KleinPipeline.cpp:538-551).
   {
@@ -647,117 +510,369 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     const int ph = static_cast<int>(ph_), pw = static_cast<int>(pw_);
     building_->push_back({[=](cudaStream_t s) {
                             cuda_check(launch_latent_unpack(lat, mean, var, eps, static_cast<int>(B), ph, pw,
-                                                            static_cast<int>(L), static_cast<int>(Lpad), zin, s),
+                                                            static_cast<int>(L), static_cast<int>(Lpad), zfull, s),
                                        "latent unpack");
                           },
                           1, kOpOther, 0.0, "latent unpack"});
   }
-  // 2. post_quant_conv (1x1) and conv_in (AutoencoderKLFlux2.cpp:139-150, Decoder.hpp:110-115).
-  const uint16_t* z = zin;
-  if (c.use_post_quant_conv) {
-    const Conv& pq = convs_.at("post_quant_conv");
-    add_mm("post_quant_conv", zin, Lpad, B * P0, Lpad, pq.w, Lpad, L, conv_ep(nullptr, zq, Lpad, pq.bias, nullptr));
-    z = zq;
-  }
-  int cur = 0;
-  StatSrc x_src;  // statistics of the residual stream X[cur]
-  {
-    const Conv& ci = convs_.at("decoder.conv_in");
-    x_src.part = part_x;
-    add_conv("conv_in", z, h0, w0, Lpad, taps3, ci.w, top, conv_ep(X[0], Xb[0], top, ci.bias, nullptr), -1, &x_src);
-  }
 
-  // ResnetBlock2D (ResnetBlock2D.inl:108-190) at H x W: X[cur] (+ Xb[cur]) -> X[cur ^ 1] (+ Xb[cur ^ 1]).
-  auto resnet = [&](const std::string& n, int64_t H, int64_t W, int64_t cin) {
-    const Conv& c1 = convs_.at(n + ".conv1");
-    const Conv& c2 = convs_.at(n + ".conv2");
-    const int64_t cout = c1.cout, HW = H * W;
-    group_norm(n + ".norm1", Xb[cur], HW, cin, norms_.at(n + ".norm1"), true, x_src);
-    StatSrc h_src;
-    h_src.part = part_h;
-    add_conv(n + ".conv1", A, H, W, cin, taps3, c1.w, cout, conv_ep(nullptr, Hb, cout, c1.bias, nullptr), -1, &h_src);
-    group_norm(n + ".norm2", Hb, HW, cout, norms_.at(n + ".norm2"), true, h_src);
-    const float* resid = X[cur];
-    auto sc = convs_.find(n + ".conv_shortcut");
-    if (sc != convs_.end()) {
-      add_mm(n + ".conv_shortcut", Xb[cur], cin, B * HW, cin, sc->second.w, cin, cout,
-             conv_ep(Sc, nullptr, cout, sc->second.bias, nullptr));
-      resid = Sc;
-    }
-    x_src = StatSrc();
-    x_src.part = part_x;
-    add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout, conv_ep(X[cur ^ 1], Xb[cur ^ 1], cout, c2.bias, resid), -1,
-             &x_src);
-    cur ^= 1;
-  };
+  // One AutoencoderKLFlux2::decode (AutoencoderKLFlux2.cpp:139-150) of the
+  // NHWC latent z_in [B, h0, w0, Lpad] into the NCHW image img.
+  auto emit_decode = [&](const uint16_t* z_in, int64_t h0, int64_t w0, float* img) {
+      Bufs& d = get_bufs(h0, w0);
+      const int64_t P0 = h0 * w0, Pk = round_up(P0, 64);
+      float* X[2] = {d.X[0], d.X[1]};
+      uint16_t* Xb[2] = {d.Xb[0], d.Xb[1]};
+      uint16_t* const Hb = d.Hb;
+      float* const Sc = d.Sc;
+      uint16_t* const A = d.A;
+      double* const stats = d.stats;
+      float* const part_x = d.part_x;
+      float* const part_h = d.part_h;
+      const int64_t part_floats = d.part_floats;
+      uint16_t *const zq = d.zq, *const qkv = d.qkv, *const vt = d.vt, *const Pm = d.Pm, *const O = d.O;
+      float* const S = d.S;
+      int n_norms = 0;
 
-  // 3. Mid block (UNetMidBlock2D.cpp): resnet, attention, resnet.
-  resnet("decoder.mid_block.resnets.0", h0, w0, top);
-  if (c.mid_block_add_attention) {
-    const std::string p = "decoder.mid_block.attentions.0";
-    const int64_t C = top;
-    group_norm(p + ".group_norm", Xb[cur], P0, C, norms_.at(p + ".group_norm"), false, x_src);
-    add_mm(p + ".to_qkv", A, C, B * P0, C, attn_qkv_w_, C, 3 * C, conv_ep(nullptr, qkv, 3 * C, attn_qkv_b_, nullptr));
-    const float scale = 1.0f / std::sqrt(static_cast<float>(C));
-    for (int64_t b = 0; b < B; ++b) {
-      const uint16_t* q = qkv + b * P0 * 3 * C;
-      EpilogueArgs se{};
-      se.out_f32 = S;
-      se.ld_out = Pk;
-      add_mm(p + ".scores", q, 3 * C, P0, C, q + C, 3 * C, P0, se, kEpiF32);
-      building_->push_back({[=](cudaStream_t s) {
-                              cuda_check(launch_softmax_rows(S, P0, P0, Pk, scale, Pm, Pk, s), "softmax");
+    // N tile: the narrowest of 32 / 64 / 128 / 256 columns holding N (32 and
+    // 64 only on the one-SM kernel).
+    auto tile_for = [](int64_t N) { return N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256; };
+
+    // Plain GEMM: Y[M, N] = A[M, K] . W[N, K]^T with the conv epilogue.
+    auto add_mm = [&](const std::string& tag, const uint16_t* a, int64_t lda, int64_t M, int64_t K, const uint16_t* w,
+                      int64_t ldw, int64_t N, EpilogueArgs ep, int mode = kEpiConv) {
+      const int tn = tile_for(N);
+      const bool pair = cx->use_pair(M) && tn >= 128;
+      auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
+      cuda_check(make_tmap_bf16(&(*maps)[0], a, K, M, lda, kGemmBM), "tensor map A");
+      cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, ldw, pair ? tn / 2 : tn), "tensor map W");
+      GemmArgs g{};
+      g.N = static_cast<int32_t>(N);
+      g.K = static_cast<int32_t>(K);
+      g.n_groups = 1;
+      g.groups[0].rows = static_cast<int32_t>(M);
+      ep.mode = mode;
+      if (mode == kEpiConv) ep.up_phase = -1;
+      g.ep = ep;
+      g.err = err;
+      gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
+      building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
+                              const auto& m = *maps;
+                              if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "vae gemm (pair)");
+                              else cuda_check(launch_gemm(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "vae gemm");
                             },
-                            1, kOpAttention, 0.0, p + ".softmax"});
-      building_->push_back({[=](cudaStream_t s) {
-                              cuda_check(launch_transpose_bf16(q + 2 * C, P0, C, 3 * C, vt, Pk, s), "transpose v");
-                            },
-                            1, kOpOther, 0.0, p + ".v^T"});
-      add_mm(p + ".pv", Pm, Pk, P0, P0, vt, Pk, C, conv_ep(nullptr, O + b * P0 * C, C, nullptr, nullptr));
-    }
-    add_mm(p + ".to_out", O, C, B * P0, C, attn_out_w_, C, C, conv_ep(X[cur ^ 1], Xb[cur ^ 1], C, attn_out_b_, X[cur]));
-    cur ^= 1;
-    x_src = StatSrc();  // the next GroupNorm runs its own statistics pass
-  }
-  resnet("decoder.mid_block.resnets.1", h0, w0, top);
+                            1, kOpGemm, 2.0 * M * N * K, tag});
+    };
 
-  // 4. Up blocks (UpDecoderBlock2D.cpp): resnets, then Upsample2D as four
-  //    phase convolutions over the low-resolution image.
-  int64_t H = h0, W = w0, prev = top;
-  for (int i = 0; i < n_up; ++i) {
-    const int64_t out = ch[n_up - 1 - i];
-    const std::string b = "decoder.up_blocks." + std::to_string(i);
-    for (int j = 0; j <= c.layers_per_block; ++j) {
-      resnet(b + ".resnets." + std::to_string(j), H, W, j == 0 ? prev : out);
+    // Implicit-GEMM convolution over x [B, H, W, C] bf16 with the given taps.
+    // Where the GroupNorm of a tensor finds its statistics: partial sums from
+    // the producing convolutions (n regions of `stride` floats, `slots` 32-row
+    // slots per image), or none (a statistics pass over the tensor).
+    struct StatSrc {
+      float* part = nullptr;
+      int n = 0;
+      int64_t stride = 0, slots = 0;
+    };
+    auto add_conv = [&](const std::string& tag, const uint16_t* x, int64_t H, int64_t W, int64_t C,
+                        const std::vector<std::pair<int, int>>& taps, const uint16_t* w, int64_t N, EpilogueArgs ep,
+                        int up_phase, StatSrc* stats_out = nullptr, int region = 0) {
+      int tw = 128;
+      int64_t best = -1;
+      for (int cand : {128, 64, 32, 16}) {
+        const int th = 128 / cand;
+        const int64_t cover = round_up(W, cand) * round_up(H, th);
+        if (best < 0 || cover < best) {
+          best = cover;
+          tw = cand;
+        }
+      }
+      const int th = 128 / tw;
+      const int64_t tiles_x = (W + tw - 1) / tw, tiles_y = (H + th - 1) / th;
+      const int64_t rows = B * tiles_x * tiles_y * 128;
+      if (rows >= (int64_t(1) << 31)) fail(DCPP_ERR_UNSUPPORTED, "convolution too large");
+      if (taps.empty() || taps.size() > 9 || C % 64) fail(DCPP_ERR_UNSUPPORTED, "internal: convolution taps / channels");
+      const size_t n_taps = std::min<size_t>(taps.size(), 9);
+      const int64_t K = static_cast<int64_t>(n_taps) * C;
+      const int tn = tile_for(N);
+      const bool pair = cx->use_pair(rows) && tn >= 128;
+      // Rows of 128 pixels on CTA pairs: halo patches (one load per channel
+      // block serves every tap).
+      const bool halo = pair && tw == 128 && th == 1;
+      auto maps = std::make_shared<std::array<CUtensorMap, 2>>();
+      if (halo)
+        cuda_check(make_tmap_conv_patch(&(*maps)[0], x, B, H, W, C), "tensor map conv patch");
+      else
+        cuda_check(make_tmap_conv(&(*maps)[0], x, B, H, W, C, tw, th), "tensor map conv");
+      cuda_check(make_tmap_bf16(&(*maps)[1], w, K, N, K, pair ? tn / 2 : tn), "tensor map conv W");
+      GemmArgs g{};
+      g.N = static_cast<int32_t>(N);
+      g.K = static_cast<int32_t>(K);
+      g.n_groups = 1;
+      g.groups[0].rows = static_cast<int32_t>(rows);
+      ep.mode = kEpiConv;
+      ep.up_phase = up_phase;
+      if (stats_out) {
+        const int64_t cpg = N / G;
+        const int64_t slots = tiles_x * tiles_y * 4;
+        const int64_t stride = B * slots * 2 * G;
+        if (N % G == 0 && (cpg == 2 || cpg == 4 || cpg == 8 || cpg == 16 || cpg == 32) &&
+            (region + 1) * stride <= part_floats && (region == 0 || stats_out->stride == stride)) {
+          ep.gn_part = stats_out->part + region * stride;
+          ep.gn_cpg = static_cast<int32_t>(cpg);
+          ep.gn_groups = static_cast<int32_t>(G);
+          stats_out->n = region + 1;
+          stats_out->stride = stride;
+          stats_out->slots = slots;
+        } else {
+          stats_out->part = nullptr;  // the GroupNorm computes its own statistics
+        }
+      }
+      g.ep = ep;
+      g.err = err;
+      g.conv.taps = static_cast<int32_t>(n_taps);
+      g.conv.cin_blocks = static_cast<int32_t>(C / 64);
+      g.conv.H = static_cast<int32_t>(H);
+      g.conv.W = static_cast<int32_t>(W);
+      g.conv.tile_w = tw;
+      g.conv.tile_h = th;
+      g.conv.tiles_x = static_cast<int32_t>(tiles_x);
+      g.conv.tiles_y = static_cast<int32_t>(tiles_y);
+      g.conv.halo = halo ? 1 : 0;
+      for (size_t t = 0; t < n_taps; ++t) {
+        g.conv.dy[t] = static_cast<int8_t>(taps[t].first);
+        g.conv.dx[t] = static_cast<int8_t>(taps[t].second);
+      }
+      gemm_finalize_groups(g, pair ? 256 : kGemmBM, tn);
+      building_->push_back({[maps, g, cx, pair](cudaStream_t s) {
+                              const auto& m = *maps;
+                              if (pair) cuda_check(launch_gemm_pair(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "conv (pair)");
+                              else cuda_check(launch_gemm(m[0], m[1], m[1], g, kBSrcBf16, cx->num_sms, s), "conv");
+                            },
+                            1, kOpGemm, 2.0 * B * H * W * N * K, tag});
+    };
+    std::vector<std::pair<int, int>> taps3;
+    for (int ky = 0; ky < 3; ++ky)
+      for (int kx = 0; kx < 3; ++kx) taps3.push_back({ky - 1, kx - 1});
+
+    auto conv_ep = [](float* out_f32, uint16_t* out_bf16, int64_t ld, const float* bias, const float* resid) {
+      EpilogueArgs e{};
+      e.out_f32 = out_f32;
+      e.out_bf16 = out_bf16;
+      e.ld_out = ld;
+      e.bias = bias;
+      e.resid = resid;
+      e.ld_resid = ld;
+      return e;
+    };
+
+    // GroupNorm (+ SiLU) of x (bf16 [B, HW, C]) into the bf16 operand A, with
+    // the statistics from the producer's partial sums when it left them.
+    auto group_norm = [&](const std::string& tag, const uint16_t* x, int64_t HW, int64_t C, const Norm& n, bool silu,
+                          const StatSrc& src) {
+      if (n_norms >= kMaxNorms) fail(DCPP_ERR_UNSUPPORTED, "too many GroupNorms");
+      double* st = stats + static_cast<int64_t>(n_norms++) * B * G * 2;
+      const float eps = 1e-6f;
+      if (src.part) {
+        const StatSrc sc = src;
+        building_->push_back({[=](cudaStream_t s) {
+                                cuda_check(launch_gn_finalize(sc.part, sc.n, sc.stride, sc.slots, static_cast<int>(B),
+                                                              static_cast<int>(G), st, s),
+                                           "gn finalize");
+                              },
+                              1, kOpNorm, 0.0, tag + " stats"});
+      } else {
+        building_->push_back({[=](cudaStream_t s) {
+                                cuda_check(launch_gn_stats(x, true, static_cast<int>(B), HW, static_cast<int>(C),
+                                                           static_cast<int>(G), st, s),
+                                           "gn stats");
+                              },
+                              1, kOpNorm, 0.0, tag + " stats"});
+      }
+      building_->push_back({[=](cudaStream_t s) {
+                              cuda_check(launch_gn_apply(x, true, static_cast<int>(B), HW, static_cast<int>(C),
+                                                         static_cast<int>(G), st, n.gamma, n.beta, eps, silu, A, s),
+                                         "gn apply");
+                            },
+                            1, kOpNorm, 0.0, tag});
+    };
+
+    // Zero every GroupNorm statistics slot once per decode.
+    building_->push_back({[=](cudaStream_t s) {
+                            cuda_check(cudaMemsetAsync(stats, 0, kMaxNorms * B * G * 2 * sizeof(double), s), "memset stats");
+                          },
+                          0, kOpOther, 0.0, "zero stats"});
+
+    // 2. post_quant_conv (1x1) and conv_in (AutoencoderKLFlux2.cpp:139-150, Decoder.hpp:110-115).
+    const uint16_t* z = z_in;
+    if (c.use_post_quant_conv) {
+      const Conv& pq = convs_.at("post_quant_conv");
+      add_mm("post_quant_conv", z_in, Lpad, B * P0, Lpad, pq.w, Lpad, L, conv_ep(nullptr, zq, Lpad, pq.bias, nullptr));
+      z = zq;
     }
-    if (i < n_up - 1) {
-      const Conv& up = convs_.at(b + ".upsamplers.0.conv");
+    int cur = 0;
+    StatSrc x_src;  // statistics of the residual stream X[cur]
+    {
+      const Conv& ci = convs_.at("decoder.conv_in");
+      x_src.part = part_x;
+      add_conv("conv_in", z, h0, w0, Lpad, taps3, ci.w, top, conv_ep(X[0], Xb[0], top, ci.bias, nullptr), -1, &x_src);
+    }
+
+    // ResnetBlock2D (ResnetBlock2D.inl:108-190) at H x W: X[cur] (+ Xb[cur]) -> X[cur ^ 1] (+ Xb[cur ^ 1]).
+    auto resnet = [&](const std::string& n, int64_t H, int64_t W, int64_t cin) {
+      const Conv& c1 = convs_.at(n + ".conv1");
+      const Conv& c2 = convs_.at(n + ".conv2");
+      const int64_t cout = c1.cout, HW = H * W;
+      group_norm(n + ".norm1", Xb[cur], HW, cin, norms_.at(n + ".norm1"), true, x_src);
+      StatSrc h_src;
+      h_src.part = part_h;
+      add_conv(n + ".conv1", A, H, W, cin, taps3, c1.w, cout, conv_ep(nullptr, Hb, cout, c1.bias, nullptr), -1, &h_src);
+      group_norm(n + ".norm2", Hb, HW, cout, norms_.at(n + ".norm2"), true, h_src);
+      const float* resid = X[cur];
+      auto sc = convs_.find(n + ".conv_shortcut");
+      if (sc != convs_.end()) {
+        add_mm(n + ".conv_shortcut", Xb[cur], cin, B * HW, cin, sc->second.w, cin, cout,
+               conv_ep(Sc, nullptr, cout, sc->second.bias, nullptr));
+        resid = Sc;
+      }
       x_src = StatSrc();
       x_src.part = part_x;
-      for (int ph = 0; ph < 4; ++ph) {
-        const int a = ph >> 1, bb = ph & 1;
-        std::vector<std::pair<int, int>> taps;
-        for (int ty = 0; ty < 2; ++ty)
-          for (int tx = 0; tx < 2; ++tx) taps.push_back({a - 1 + ty, bb - 1 + tx});
-        add_conv(b + ".upsample phase " + std::to_string(ph), Xb[cur], H, W, out, taps, up.phase[ph], out,
-                 conv_ep(X[cur ^ 1], Xb[cur ^ 1], out, up.bias, nullptr), ph, x_src.part ? &x_src : nullptr, ph);
-      }
+      add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout, conv_ep(X[cur ^ 1], Xb[cur ^ 1], cout, c2.bias, resid), -1,
+               &x_src);
       cur ^= 1;
-      H *= 2;
-      W *= 2;
-    }
-    prev = out;
-  }
+    };
 
-  // 5. conv_norm_out, SiLU, conv_out (Decoder.hpp:132-162) -> NCHW image.
-  group_norm("decoder.conv_norm_out", Xb[cur], H * W, ch[0], norms_.at("decoder.conv_norm_out"), true, x_src);
-  {
-    // A few output channels: a 32-column tile on one SM, the epilogue
-    // storing the f32 image planes (NCHW) directly.
-    const Conv& co = convs_.at("decoder.conv_out");
-    EpilogueArgs e = conv_ep(img_dev_, nullptr, c.out_channels, co.bias, nullptr);
-    e.nchw_hw = static_cast<int32_t>(H * W);
-    add_conv("decoder.conv_out", A, H, W, ch[0], taps3, co.w, c.out_channels, e, -1);
+    // 3. Mid block (UNetMidBlock2D.cpp): resnet, attention, resnet.
+    resnet("decoder.mid_block.resnets.0", h0, w0, top);
+    if (c.mid_block_add_attention) {
+      const std::string p = "decoder.mid_block.attentions.0";
+      const int64_t C = top;
+      group_norm(p + ".group_norm", Xb[cur], P0, C, norms_.at(p + ".group_norm"), false, x_src);
+      add_mm(p + ".to_qkv", A, C, B * P0, C, attn_qkv_w_, C, 3 * C, conv_ep(nullptr, qkv, 3 * C, attn_qkv_b_, nullptr));
+      const float scale = 1.0f / std::sqrt(static_cast<float>(C));
+      for (int64_t b = 0; b < B; ++b) {
+        const uint16_t* q = qkv + b * P0 * 3 * C;
+        EpilogueArgs se{};
+        se.out_f32 = S;
+        se.ld_out = Pk;
+        add_mm(p + ".scores", q, 3 * C, P0, C, q + C, 3 * C, P0, se, kEpiF32);
+        building_->push_back({[=](cudaStream_t s) {
+                                cuda_check(launch_softmax_rows(S, P0, P0, Pk, scale, Pm, Pk, s), "softmax");
+                              },
+                              1, kOpAttention, 0.0, p + ".softmax"});
+        building_->push_back({[=](cudaStream_t s) {
+                                cuda_check(launch_transpose_bf16(q + 2 * C, P0, C, 3 * C, vt, Pk, s), "transpose v");
+                              },
+                              1, kOpOther, 0.0, p + ".v^T"});
+        add_mm(p + ".pv", Pm, Pk, P0, P0, vt, Pk, C, conv_ep(nullptr, O + b * P0 * C, C, nullptr, nullptr));
+      }
+      add_mm(p + ".to_out", O, C, B * P0, C, attn_out_w_, C, C, conv_ep(X[cur ^ 1], Xb[cur ^ 1], C, attn_out_b_, X[cur]));
+      cur ^= 1;
+      x_src = StatSrc();  // the next GroupNorm runs its own statistics pass
+    }
+    resnet("decoder.mid_block.resnets.1", h0, w0, top);
+
+    // 4. Up blocks (UpDecoderBlock2D.cpp): resnets, then Upsample2D as four
+    //    phase convolutions over the low-resolution image.
+    int64_t H = h0, W = w0, prev = top;
+    for (int i = 0; i < n_up; ++i) {
+      const int64_t out = ch[n_up - 1 - i];
+      const std::string b = "decoder.up_blocks." + std::to_string(i);
+      for (int j = 0; j <= c.layers_per_block; ++j) {
+        resnet(b + ".resnets." + std::to_string(j), H, W, j == 0 ? prev : out);
+      }
+      if (i < n_up - 1) {
+        const Conv& up = convs_.at(b + ".upsamplers.0.conv");
+        x_src = StatSrc();
+        x_src.part = part_x;
+        for (int ph = 0; ph < 4; ++ph) {
+          const int a = ph >> 1, bb = ph & 1;
+          std::vector<std::pair<int, int>> taps;
+          for (int ty = 0; ty < 2; ++ty)
+            for (int tx = 0; tx < 2; ++tx) taps.push_back({a - 1 + ty, bb - 1 + tx});
+          add_conv(b + ".upsample phase " + std::to_string(ph), Xb[cur], H, W, out, taps, up.phase[ph], out,
+                   conv_ep(X[cur ^ 1], Xb[cur ^ 1], out, up.bias, nullptr), ph, x_src.part ? &x_src : nullptr, ph);
+        }
+        cur ^= 1;
+        H *= 2;
+        W *= 2;
+      }
+      prev = out;
+    }
+
+    // 5. conv_norm_out, SiLU, conv_out (Decoder.hpp:132-162) -> NCHW image.
+    group_norm("decoder.conv_norm_out", Xb[cur], H * W, ch[0], norms_.at("decoder.conv_norm_out"), true, x_src);
+    {
+      // A few output channels: a 32-column tile on one SM, the epilogue
+      // storing the f32 image planes (NCHW) directly.
+      const Conv& co = convs_.at("decoder.conv_out");
+      EpilogueArgs e = conv_ep(img, nullptr, c.out_channels, co.bias, nullptr);
+      e.nchw_hw = static_cast<int32_t>(H * W);
+      add_conv("decoder.conv_out", A, H, W, ch[0], taps3, co.w, c.out_channels, e, -1);
+    }
+
+  };
+
+  if (tile_ <= 0) {
+    emit_decode(zfull, h0, w0, img_dev_);
+  } else {
+    // AutoencoderKLFlux2::decode_tiled (AutoencoderKLFlux2.cpp:380-405) with
+    // tiled_forward (:262-378): latent tiles at a 3/4 stride, each decoded
+    // alone; each decoded tile is blended in place with the (blended) tile
+    // above, then with the one to its left, over a quarter tile with the
+    // linear ramp x / extent, and its top-left band goes to the image.
+    const int64_t scale = c.scale_factor();
+    const int64_t lt = tile_ / scale, stride = lt * 3 / 4;
+    const int64_t blend = tile_ / 4, band = tile_ - blend;
+    std::vector<int64_t> ys, xs;
+    for (int64_t i = 0; i < h0; i += stride) ys.push_back(i);
+    for (int64_t j = 0; j < w0; j += stride) xs.push_back(j);
+    const int Co = static_cast<int>(c.out_channels);
+    std::vector<std::vector<float*>> timg(ys.size(), std::vector<float*>(xs.size(), nullptr));
+    std::map<std::pair<int64_t, int64_t>, uint16_t*> tz;  // contiguous latent tiles, one per size
+    int64_t oy = 0;
+    for (size_t a = 0; a < ys.size(); ++a) {
+      const int64_t th = std::min(lt, h0 - ys[a]), hp = th * scale;
+      int64_t ox = 0;
+      for (size_t bx = 0; bx < xs.size(); ++bx) {
+        const int64_t tw = std::min(lt, w0 - xs[bx]), wp = tw * scale;
+        uint16_t*& zt = tz[std::make_pair(th, tw)];
+        if (!zt) zt = static_cast<uint16_t*>(alloc(B * th * tw * Lpad * 2));
+        {
+          uint16_t* dst = zt;
+          const uint16_t* src = zfull + (ys[a] * w0 + xs[bx]) * Lpad;
+          building_->push_back({[=](cudaStream_t s) {
+                                  for (int64_t bb = 0; bb < B; ++bb)
+                                    cuda_check(cudaMemcpy2DAsync(dst + bb * th * tw * Lpad, tw * Lpad * 2,
+                                                                 src + bb * h0 * w0 * Lpad, w0 * Lpad * 2,
+                                                                 tw * Lpad * 2, th, cudaMemcpyDeviceToDevice, s),
+                                               "latent tile");
+                                },
+                                0, kOpOther, 0.0, "latent tile"});
+        }
+        float* img = static_cast<float*>(alloc(B * Co * hp * wp * 4));
+        timg[a][bx] = img;
+        emit_decode(zt, th, tw, img);
+        const float* above = a > 0 ? timg[a - 1][bx] : nullptr;
+        const float* left = bx > 0 ? timg[a][bx - 1] : nullptr;
+        const int64_t ha = a > 0 ? std::min(lt, h0 - ys[a - 1]) * scale : 0;
+        const int64_t wl = bx > 0 ? std::min(lt, w0 - xs[bx - 1]) * scale : 0;
+        const int64_t ev = above ? std::min({ha, hp, blend}) : 0;
+        const int64_t eh = left ? std::min({wl, wp, blend}) : 0;
+        const int64_t keep_h = std::min(hp, band), keep_w = std::min(wp, band);
+        float* out = img_dev_;
+        const int64_t y0 = oy, x0 = ox;
+        building_->push_back({[=](cudaStream_t s) {
+                                cuda_check(launch_tile_blend(img, above, ha, left, wl, static_cast<int>(B), Co, hp, wp,
+                                                             ev, eh, keep_h, keep_w, out, Hout, Wout, y0, x0, s),
+                                           "tile blend");
+                              },
+                              1, kOpOther, 0.0, "tile blend"});
+        ox += keep_w;
+        if (bx + 1 == xs.size() && ox != Wout) fail(DCPP_ERR_STATE, "internal: tiled decode width");
+      }
+      oy += std::min(hp, band);
+    }
+    if (oy != Hout) fail(DCPP_ERR_STATE, "internal: tiled decode height");
   }
   end_ops();
   launches_per_step_ = 0;
@@ -930,7 +1045,15 @@ dcpp_status dcpp_vae_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_vae** 
 
 dcpp_status dcpp_vae_prepare(dcpp_vae* m, int64_t batch, int64_t packed_h, int64_t packed_w, int use_graph) {
   return vae_call(m, "dcpp_vae_prepare", [&](dcpp::AutoencoderKLFlux2Decoder& mm) {
-    mm.prepare(batch, packed_h, packed_w, use_graph != 0);
+    mm.prepare(batch, packed_h, packed_w, use_graph != 0, 0);
+  });
+}
+
+dcpp_status dcpp_vae_prepare_tiled(dcpp_vae* m, int64_t batch, int64_t packed_h, int64_t packed_w, int64_t tile_size,
+                                   int use_graph) {
+  return vae_call(m, "dcpp_vae_prepare_tiled", [&](dcpp::AutoencoderKLFlux2Decoder& mm) {
+    if (tile_size <= 0) dcpp::fail(DCPP_ERR_INVALID_ARG, "decode_tiled(): tile size must be positive");
+    mm.prepare(batch, packed_h, packed_w, use_graph != 0, tile_size);
   });
 }
 

@@ -67,8 +67,9 @@ class AutoencoderKLFlux2Decoder : public StepPlanner {
   std::vector<std::string> missing() const;
 
   // Plan a decode of `batch` packed latents of packed_h x packed_w tokens
-  // (image 16 packed_h x 16 packed_w for the default config).
-  void prepare(int64_t batch, int64_t packed_h, int64_t packed_w, bool use_graph);
+  // (image 16 packed_h x 16 packed_w for the default config); tile_size > 0:
+  // the tiled decode with tiles of tile_size pixels (decode_tiled).
+  void prepare(int64_t batch, int64_t packed_h, int64_t packed_w, bool use_graph, int64_t tile_size = 0);
   // Flux2KleinPipeline::decode (untiled): latents [B, ph*pw, 4 latent_channels]
   // f32 -> image [B, out_channels, H, W] f32.  Host or device pointers.
   void decode(const float* latents, float* image);
@@ -113,7 +114,7 @@ class AutoencoderKLFlux2Decoder : public StepPlanner {
   float* bn_mean_ = nullptr;
   float* bn_var_ = nullptr;
 
-  int64_t B_ = 0, ph_ = 0, pw_ = 0;
+  int64_t B_ = 0, ph_ = 0, pw_ = 0, tile_ = 0;
   bool planned_ = false;
   std::vector<void*> allocs_;
   float* lat_dev_ = nullptr;

@@ -180,11 +180,18 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restri
   uint16_t* out = P + blockIdx.x * ld_p;
   const float c = scale * 1.4426950408889634f;
   float m = -INFINITY, l = 0.f;
-  for (int64_t i = threadIdx.x * 4; i < n; i += 4 * blockDim.x) {
+  const int64_t n4 = n & ~int64_t(3);  // float4 part; the n % 4 tail one element per thread
+  for (int64_t i = threadIdx.x * 4; i < n4; i += 4 * blockDim.x) {
     const float4 t = __ldg(reinterpret_cast<const float4*>(row + i));
     const float mx = fmaxf(fmaxf(t.x, t.y), fmaxf(t.z, t.w)) * c;
     const float mn = fmaxf(m, mx);
     l = l * exp2f(m - mn) + exp2f(t.x * c - mn) + exp2f(t.y * c - mn) + exp2f(t.z * c - mn) + exp2f(t.w * c - mn);
+    m = mn;
+  }
+  if (n4 + threadIdx.x < n) {
+    const float v = row[n4 + threadIdx.x] * c;
+    const float mn = fmaxf(m, v);
+    l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + exp2f(v - mn);
     m = mn;
   }
   __shared__ float sm[32], sl[32];
@@ -222,12 +229,13 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restri
   __syncthreads();
   m = sm[0];
   const float inv = sl[0];
-  for (int64_t i = threadIdx.x * 4; i < n; i += 4 * blockDim.x) {
+  for (int64_t i = threadIdx.x * 4; i < n4; i += 4 * blockDim.x) {
     const float4 t = __ldg(reinterpret_cast<const float4*>(row + i));
     const uint32_t lo = pack_bf16x2(exp2f(t.x * c - m) * inv, exp2f(t.y * c - m) * inv);
     const uint32_t hi = pack_bf16x2(exp2f(t.z * c - m) * inv, exp2f(t.w * c - m) * inv);
     *reinterpret_cast<uint2*>(out + i) = make_uint2(lo, hi);
   }
+  if (n4 + threadIdx.x < n) out[n4 + threadIdx.x] = f32_to_bf16(exp2f(row[n4 + threadIdx.x] * c - m) * inv);
 }
 
 // --------------------------------------------------------------- transpose
@@ -271,6 +279,34 @@ __global__ void __launch_bounds__(256) gn_finalize_kernel(const float* __restric
     double t = 0.0;
     for (int k = 0; k < nsub; ++k) t += red[k * e2 + threadIdx.x];
     atomicAdd(&stats[static_cast<int64_t>(b) * e2 + threadIdx.x], t);
+  }
+}
+
+// Tiled decode: blend the decoded tile T [B, C, h, w] in place with the
+// tile above (its last ev rows) and then the tile to the left (its last eh
+// columns), weights y / ev and x / eh on T, and copy the top-left
+// keep_h x keep_w band to out [B, C, H, W] at (oy, ox).
+__global__ void tile_blend_kernel(float* __restrict__ T, const float* __restrict__ above, int64_t ha,
+                                  const float* __restrict__ left, int64_t wl, int64_t BC, int64_t h, int64_t w,
+                                  int64_t ev, int64_t eh, int64_t keep_h, int64_t keep_w, float* __restrict__ out,
+                                  int64_t H, int64_t W, int64_t oy, int64_t ox) {
+  const int64_t total = BC * h * w;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t x = i % w;
+    const int64_t y = (i / w) % h;
+    const int64_t bc = i / (h * w);
+    float t = T[i];
+    if (y < ev) {
+      const float wv = static_cast<float>(y) / static_cast<float>(ev);
+      t = above[(bc * ha + (ha - ev + y)) * w + x] * (1.0f - wv) + t * wv;
+    }
+    if (x < eh) {
+      const float wh = static_cast<float>(x) / static_cast<float>(eh);
+      t = left[(bc * h + y) * wl + (wl - eh + x)] * (1.0f - wh) + t * wh;
+    }
+    T[i] = t;
+    if (y < keep_h && x < keep_w) out[(bc * H + oy + y) * W + ox + x] = t;
   }
 }
 
@@ -322,7 +358,7 @@ cudaError_t launch_gn_apply(const void* x, bool bf16, int B, int64_t HW, int C, 
 
 cudaError_t launch_softmax_rows(const float* S, int64_t rows, int64_t n, int64_t ld_s, float scale, uint16_t* P,
                                 int64_t ld_p, cudaStream_t s) {
-  if (n % 4 != 0 || ld_s % 4 != 0 || ld_p % 4 != 0) return cudaErrorInvalidValue;
+  if (ld_s % 4 != 0 || ld_p % 4 != 0) return cudaErrorInvalidValue;
   softmax_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(S, n, ld_s, scale, P, ld_p);
   return cudaGetLastError();
 }
@@ -340,6 +376,15 @@ cudaError_t launch_gn_finalize(const float* part, int n_regions, int64_t region_
   dim3 grid(static_cast<unsigned>((slots_per_img + kFinalizeSlots - 1) / kFinalizeSlots), static_cast<unsigned>(B),
             static_cast<unsigned>(n_regions));
   gn_finalize_kernel<<<grid, 256, 0, s>>>(part, region_stride, slots_per_img, G, stats);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tile_blend(float* T, const float* above, int64_t ha, const float* left, int64_t wl, int B, int C,
+                              int64_t h, int64_t w, int64_t ev, int64_t eh, int64_t keep_h, int64_t keep_w, float* out,
+                              int64_t H, int64_t W, int64_t oy, int64_t ox, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(B) * C * h * w;
+  tile_blend_kernel<<<grid_for(total, 256), 256, 0, s>>>(T, above, ha, left, wl, static_cast<int64_t>(B) * C, h, w, ev,
+                                                          eh, keep_h, keep_w, out, H, W, oy, ox);
   return cudaGetLastError();
 }
 

@@ -184,6 +184,8 @@ _SIGNATURES = {
     "dcpp_vae_load_gguf": (ctypes.c_int, [_vp, _vp, _c_i64p, _c_i64p]),
     "dcpp_vae_from_pretrained": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "dcpp_vae_prepare": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]),
+    "dcpp_vae_prepare_tiled": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int]),
     "dcpp_vae_decode": (ctypes.c_int, [_vp, _vp, _vp]),
     "dcpp_vae_set_profiling": (ctypes.c_int, [_vp, ctypes.c_int]),
     "dcpp_vae_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
@@ -801,8 +803,13 @@ class VAEModel:
         self.ctx.check(lib().dcpp_vae_missing(self.h, ctypes.byref(n), buf, 512), "missing")
         return n.value, buf.value.decode()
 
-    def prepare(self, batch: int, packed_h: int, packed_w: int, use_graph: bool = True):
-        self.ctx.check(lib().dcpp_vae_prepare(self.h, batch, packed_h, packed_w, 1 if use_graph else 0), "prepare")
+    def prepare(self, batch: int, packed_h: int, packed_w: int, use_graph: bool = True, tile_size: int = 0):
+        """tile_size > 0: the tiled decode (decode_tiled) with tiles of that many pixels."""
+        if tile_size:
+            self.ctx.check(lib().dcpp_vae_prepare_tiled(self.h, batch, packed_h, packed_w, tile_size,
+                                                        1 if use_graph else 0), "prepare_tiled")
+        else:
+            self.ctx.check(lib().dcpp_vae_prepare(self.h, batch, packed_h, packed_w, 1 if use_graph else 0), "prepare")
 
     def decode(self, latents, image):
         """latents [B, ph*pw, 4*latent_channels] f32 -> image [B, out_channels, H, W] f32."""

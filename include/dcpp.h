@@ -512,8 +512,16 @@ dcpp_status dcpp_vae_from_pretrained(dcpp_ctx* ctx, const char* dir, dcpp_vae** 
 /* Plan the decode of `batch` packed latents of packed_h x packed_w tokens
  * (the DiT's image tokens; image = 2 * scale_factor * packed_h pixels high). */
 dcpp_status dcpp_vae_prepare(dcpp_vae* model, int64_t batch, int64_t packed_h, int64_t packed_w, int use_graph);
-/* Flux2KleinPipeline::decode (Flux2KleinPipeline.cpp:538-556, untiled):
- * latents [B, packed_h * packed_w, 4 * latent_channels] f32 (the denoised
+/* The same with decode_tiled (AutoencoderKLFlux2.cpp:380-405; the
+ * pipeline's tile_size argument): tiles of tile_size x tile_size pixels
+ * (divisible by the VAE's scale factor) at a 3/4 stride, each decoded on
+ * its own and blended with its upper and left neighbours over a quarter
+ * tile, so that the activation memory follows the tile size.  Invalid
+ * sizes: DCPP_ERR_INVALID_ARG with the reference's message. */
+dcpp_status dcpp_vae_prepare_tiled(dcpp_vae* model, int64_t batch, int64_t packed_h, int64_t packed_w,
+                                   int64_t tile_size, int use_graph);
+/* Flux2KleinPipeline::decode (Flux2KleinPipeline.cpp:538-556), untiled or
+ * tiled as prepared: latents [B, packed_h * packed_w, 4 * latent_channels] f32 (the denoised
  * tokens) -> image [B, out_channels, H, W] f32.  Host or device pointers. */
 dcpp_status dcpp_vae_decode(dcpp_vae* model, const float* p_latents, float* p_image);
 dcpp_status dcpp_vae_set_profiling(dcpp_vae* model, int on);

@@ -66,6 +66,35 @@ def test_decode_matches_oracle(ctx, ch, lpb, B, ph, pw):
     assert r < IMG_TOL, (r, err)
 
 
+@pytest.mark.parametrize("ph,pw,tile", [(8, 12, 32), (9, 6, 48), (4, 4, 64)])
+def test_tiled_decode_matches_oracle(ctx, ph, pw, tile):
+    """decode_tiled: ragged tile rows / columns (tiles clipped at the image
+    border, a non-last clipped row), blending with the upper and left
+    neighbours; a tile covering the image equals the untiled decode."""
+    c = synth.VAECfg(block_out_channels=(64, 128, 128), layers_per_block=1)
+    params = synth.make_vae_params(c, seed=17)
+    m = dcpp_b200.VAEModel(ctx, c)
+    m.load_params(params)
+    m.prepare(1, ph, pw, tile_size=tile)
+    lat = synth.make_vae_latents(c, 1, ph, pw, seed=18)
+    img = torch.empty(1, 3, 8 * ph, 8 * pw, dtype=torch.float32)
+    m.decode(lat, img)
+    o = oracle(c, params)
+    ref = o.decode_packed(lat, ph, pw, tile=tile)
+    assert ref.shape == img.shape
+    r = rel(img, ref)
+    assert r < IMG_TOL, r
+    if tile >= 8 * max(ph, pw) * 2:
+        m.prepare(1, ph, pw)
+        whole = torch.empty_like(img)
+        m.decode(lat, whole)
+        assert torch.equal(whole, img)
+    with pytest.raises(dcpp_b200.DcppError) as e:
+        m.prepare(1, ph, pw, tile_size=30)
+    assert "divisible by the VAE's scale factor" in str(e.value)
+    m.close()
+
+
 def test_decode_without_attention_and_post_quant(ctx):
     c = synth.VAECfg(block_out_channels=(64, 128), layers_per_block=1, use_post_quant_conv=False,
                      mid_block_add_attention=False)
