@@ -117,10 +117,10 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
 
   if (e.mode == kEpiQkvMlp) {
     const int tok = G.tok0 + local_row;
-    // Two 128-column halves; each is one head of q, k or v, or 64 SwiGLU
+    // 128-column halves (two per 256-column tile); each is one head of q, k or v, or 64 SwiGLU
     // outputs (gate/up interleaved in 64-column blocks by the loader).
 #pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
+    for (int half = 0; half < BN / 128; ++half) {
       const int c0 = col0 + half * 128;
       if (c0 >= p.N) break;
       const uint32_t hbase = taddr + half * 128;

@@ -318,6 +318,17 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
   for (auto& g : groups) total_rows += g.rows;
   const bool pair = ctx_.use_pair(total_rows, fused);
   const int tile_m = pair ? 256 : kGemmBM;
+  // N tile (bf16 B): 256 columns.  128-column tiles fill the waves of CTA
+  // pairs better for some shapes (N = 2560 at M = 2048: 160 tiles for 74
+  // pairs instead of 80) but measured slower there (each K block then feeds
+  // half the MMA work per A tile loaded); DCPP_GEMM_TILE_N = 128 selects them.
+  int tile_n = kGemmBN;
+  if (!fused) {
+    if (const char* f = getenv("DCPP_GEMM_TILE_N")) {
+      const int v = atoi(f);
+      if (v == 128 || v == kGemmBN) tile_n = v;
+    }
+  }
   if (fused) {
     int64_t a_rows = 0;
     for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
@@ -363,8 +374,8 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
   for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
   auto st = std::make_shared<std::array<CUtensorMap, 3>>();
   cuda_check(make_tmap_bf16(&(*st)[0], a, K, a_rows, lda, kGemmBM), "tensor map A");
-  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, pair ? 128 : kGemmBN), "tensor map B0");
-  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, pair ? 128 : kGemmBN), "tensor map B1");
+  cuda_check(make_tmap_bf16(&(*st)[1], b0, K, N, K, pair ? tile_n / 2 : tile_n), "tensor map B0");
+  cuda_check(make_tmap_bf16(&(*st)[2], b1, K, N, K, pair ? tile_n / 2 : tile_n), "tensor map B1");
   Ctx* c = &ctx_;
   // Weight expansion on the side stream: it waits only for the last GEMM
   // that read this scratch pair (two expanding GEMMs back), so it overlaps
@@ -400,7 +411,7 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
     for (size_t i = 0; i < pg.size(); ++i) args.groups[i] = pg[i];
     args.ep = ep;
     args.err = ctx_.d_err;
-    gemm_finalize_groups(args, tile_m);
+    gemm_finalize_groups(args, tile_m, tile_n);
     double flops = 0.0;
     for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
     building_->push_back({[st, args, c, pair](cudaStream_t s) {
