@@ -718,7 +718,9 @@ void AutoencoderKLFlux2Decoder::build_plan() {
     }
 
     // ResnetBlock2D (ResnetBlock2D.inl:108-190) at H x W: X[cur] (+ Xb[cur]) -> X[cur ^ 1] (+ Xb[cur ^ 1]).
-    auto resnet = [&](const std::string& n, int64_t H, int64_t W, int64_t cin) {
+    // f32_out: whether the f32 copy of the output is read (as the next
+    // residual); GroupNorm, shortcuts and upsamplers read the bf16 copy.
+    auto resnet = [&](const std::string& n, int64_t H, int64_t W, int64_t cin, bool f32_out) {
       const Conv& c1 = convs_.at(n + ".conv1");
       const Conv& c2 = convs_.at(n + ".conv2");
       const int64_t cout = c1.cout, HW = H * W;
@@ -736,13 +738,14 @@ void AutoencoderKLFlux2Decoder::build_plan() {
       }
       x_src = StatSrc();
       x_src.part = part_x;
-      add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout, conv_ep(X[cur ^ 1], Xb[cur ^ 1], cout, c2.bias, resid), -1,
+      add_conv(n + ".conv2", A, H, W, cout, taps3, c2.w, cout,
+               conv_ep(f32_out ? X[cur ^ 1] : nullptr, Xb[cur ^ 1], cout, c2.bias, resid), -1,
                &x_src);
       cur ^= 1;
     };
 
     // 3. Mid block (UNetMidBlock2D.cpp): resnet, attention, resnet.
-    resnet("decoder.mid_block.resnets.0", h0, w0, top);
+    resnet("decoder.mid_block.resnets.0", h0, w0, top, true);
     if (c.mid_block_add_attention) {
       const std::string p = "decoder.mid_block.attentions.0";
       const int64_t C = top;
@@ -769,7 +772,10 @@ void AutoencoderKLFlux2Decoder::build_plan() {
       cur ^= 1;
       x_src = StatSrc();  // the next GroupNorm runs its own statistics pass
     }
-    resnet("decoder.mid_block.resnets.1", h0, w0, top);
+    // The first up-block resnet reads X as its residual unless it has a
+    // shortcut (channel change).
+    const int64_t top_next = ch[n_up - 1];
+    resnet("decoder.mid_block.resnets.1", h0, w0, top, top_next == top);
 
     // 4. Up blocks (UpDecoderBlock2D.cpp): resnets, then Upsample2D as four
     //    phase convolutions over the low-resolution image.
@@ -778,7 +784,8 @@ void AutoencoderKLFlux2Decoder::build_plan() {
       const int64_t out = ch[n_up - 1 - i];
       const std::string b = "decoder.up_blocks." + std::to_string(i);
       for (int j = 0; j <= c.layers_per_block; ++j) {
-        resnet(b + ".resnets." + std::to_string(j), H, W, j == 0 ? prev : out);
+        // The last resnet of a block feeds an upsampler or the final norm.
+        resnet(b + ".resnets." + std::to_string(j), H, W, j == 0 ? prev : out, j < c.layers_per_block);
       }
       if (i < n_up - 1) {
         const Conv& up = convs_.at(b + ".upsamplers.0.conv");
@@ -789,8 +796,12 @@ void AutoencoderKLFlux2Decoder::build_plan() {
           std::vector<std::pair<int, int>> taps;
           for (int ty = 0; ty < 2; ++ty)
             for (int tx = 0; tx < 2; ++tx) taps.push_back({a - 1 + ty, bb - 1 + tx});
+          // The next block's first resnet reads X as its residual unless it
+          // has a shortcut.
+          const bool f32_out = ch[n_up - 2 - i] == out;
           add_conv(b + ".upsample phase " + std::to_string(ph), Xb[cur], H, W, out, taps, up.phase[ph], out,
-                   conv_ep(X[cur ^ 1], Xb[cur ^ 1], out, up.bias, nullptr), ph, x_src.part ? &x_src : nullptr, ph);
+                   conv_ep(f32_out ? X[cur ^ 1] : nullptr, Xb[cur ^ 1], out, up.bias, nullptr), ph,
+                   x_src.part ? &x_src : nullptr, ph);
         }
         cur ^= 1;
         H *= 2;
