@@ -31,9 +31,15 @@ struct TileCoord {
   int g;       // group
   int m_tile;  // within group
   int n_tile;
+  int split;   // K slice (0 without a K split)
 };
 
 __device__ __forceinline__ TileCoord decode_tile(const GemmArgs& p, int t) {
+  int split = 0;
+  if (p.k_splits > 1) {
+    split = t / p.tiles_per_split;
+    t -= split * p.tiles_per_split;
+  }
   int g = 0;
 #pragma unroll 1
   for (int i = 1; i < p.n_groups; ++i)
@@ -44,7 +50,19 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmArgs& p, int t) {
   c.g = g;
   c.n_tile = local / G.m_tiles;
   c.m_tile = local - c.n_tile * G.m_tiles;
+  c.split = split;
   return c;
+}
+
+// K blocks [kb0, kb1) of a work unit.
+__device__ __forceinline__ void k_range(const GemmArgs& p, const TileCoord& tc, int nk, int& kb0, int& kb1) {
+  if (p.k_splits > 1) {
+    kb0 = tc.split * nk / p.k_splits;
+    kb1 = (tc.split + 1) * nk / p.k_splits;
+  } else {
+    kb0 = 0;
+    kb1 = nk;
+  }
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
@@ -569,7 +587,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
       }
       continue;
     }
-    float* dst = e.out_f32 + row * e.ld_out + cb;
+    float* dst = e.out_f32 + static_cast<int64_t>(tc.split) * p.split_stride + row * e.ld_out + cb;
     full = full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) &&
            (!gate || (reinterpret_cast<uintptr_t>(gate + cb) & 15) == 0) &&
            (e.mode != kEpiEuler || (reinterpret_cast<uintptr_t>(e.x_in + row * e.ld_out + cb) & 15) == 0);
@@ -1109,7 +1127,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         const int yb = tc.n_tile * BN + static_cast<int>(rank) * (BN / 2);
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
         const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
-        for (int kb = 0; kb < nk; ++kb) {
+        int kb0, kb1;
+        k_range(p, tc, nk, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           const uint32_t full0 = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPB));
@@ -1143,7 +1163,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        int kb0, kb1;
+        k_range(p, decode_tile(p, t), nk, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
           if (kQuant && (!mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant) ||
                          !mbar_wait_cluster(&bpeer[stage], phase, p.err, kDevTimeoutDequant))) {
@@ -1156,7 +1178,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
-                           (kb | k) != 0 ? 1u : 0u);
+                           (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -1503,6 +1525,10 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
                              int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
   if (args.tile_n != kGemmBN && (bsrc != kBSrcBf16 || args.tile_n != 128)) return cudaErrorInvalidValue;
+  if (args.k_splits > 1 && (bsrc != kBSrcBf16 || args.ep.mode != kEpiF32 || args.conv.taps ||
+                            args.tiles_per_split * args.k_splits != args.total_tiles ||
+                            args.k_splits > (args.K + kGemmBK - 1) / kGemmBK))
+    return cudaErrorInvalidValue;
   if (args.conv.halo) {
     if (bsrc != kBSrcBf16 || args.conv.taps < 1 || args.conv.taps > 9 || args.conv.tile_w != 128 ||
         args.conv.tile_h != 1)
@@ -1582,6 +1608,13 @@ cudaError_t make_tmap_conv_patch(CUtensorMap* map, const void* base, int64_t B, 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+void gemm_set_k_splits(GemmArgs& a, int k_splits, int64_t split_stride) {
+  a.k_splits = k_splits;
+  a.tiles_per_split = a.total_tiles;
+  a.total_tiles *= k_splits;
+  a.split_stride = split_stride;
+}
+
 void gemm_finalize_groups(GemmArgs& a, int tile_m, int tile_n) {
   a.tile_n = tile_n;
   a.n_tiles_n = (a.N + tile_n - 1) / tile_n;
@@ -1597,6 +1630,7 @@ void gemm_finalize_groups(GemmArgs& a, int tile_m, int tile_n) {
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
                         int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
+  if (args.k_splits > 1) return cudaErrorInvalidValue;  // the one-SM kernel has no K split
   if (args.tile_n != kGemmBN && bsrc != kBSrcBf16) return cudaErrorInvalidValue;
   switch (bsrc) {
     case kBSrcBf16:

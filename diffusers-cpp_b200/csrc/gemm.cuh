@@ -148,6 +148,13 @@ struct GemmArgs {
   QuantB qb[2];
   ConvGeom conv;
   int32_t tile_n;  // columns per tile (set by gemm_finalize_groups)
+  // K split (CTA-pair kernel, bf16 B, kEpiF32 only): work unit t covers tile
+  // t % tiles_per_split over the K-blocks of slice t / tiles_per_split, and
+  // slice s stores its f32 partial at out_f32 + s * split_stride (a reduce
+  // kernel sums the slices).  k_splits 0 / 1: none.
+  int32_t k_splits;
+  int32_t tiles_per_split;
+  int64_t split_stride;
   int* err;
 };
 
@@ -186,5 +193,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
 // 256, or for bf16 weights 128 (both kernels) and 64 / 32 (launch_gemm) --
 // the B tensor map's box is tile_n rows, tile_n / 2 for the pair).
 void gemm_finalize_groups(GemmArgs& args, int tile_m = kGemmBM, int tile_n = kGemmBN);
+// Turn a finalised kEpiF32 launch into k_splits K slices (see GemmArgs).
+void gemm_set_k_splits(GemmArgs& args, int k_splits, int64_t split_stride);
 
 }  // namespace dcpp

@@ -221,6 +221,7 @@ void set_vector_param(DevVector& v, int type, const std::vector<int64_t>& shape,
 
 // ----------------------------------------------------------------- planner
 StepPlanner::~StepPlanner() {
+  if (split_ws_) cudaFree(split_ws_);
   for (auto e : ev_) cudaEventDestroy(e);
   release_plan_events();
   if (side_) cudaStreamDestroy(side_);
@@ -229,6 +230,7 @@ StepPlanner::~StepPlanner() {
 void StepPlanner::release_plan_events() {
   for (auto e : plan_events_) cudaEventDestroy(e);
   plan_events_.clear();
+  split_launches_ = 0;  // the plans that used the split workspace are gone
 }
 
 void StepPlanner::alloc_expansion_scratch(const std::function<void*(size_t)>& alloc, size_t s0, size_t s1) {
@@ -399,6 +401,56 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
     ready = plan_event();
     add_record(ready, 1);
   }
+  // K split: a single-piece residual GEMM (h += acc, no gate) whose tiles
+  // fill the waves of CTA pairs poorly (N = 2560 at M = 2048: 80 tiles for 74
+  // pairs) runs as S K-slices writing f32 partials, then one reduce adds
+  // them to h in slice order.  DCPP_GEMM_KSPLIT = 0 turns it off.
+  int splits = 1;
+  int64_t split_rows = 0;
+  if (pair && pieces.size() == 1 && ep.mode == kEpiResidGate && !ep.gate[0] && !ep.gate[1] && N % 4 == 0 &&
+      ep.ld_out % 4 == 0) {
+    const char* f = getenv("DCPP_GEMM_KSPLIT");
+    if (!f || atoi(f) != 0) {
+      int64_t m_tiles = 0;
+      for (auto& g : groups) {
+        m_tiles += (g.rows + tile_m - 1) / tile_m;
+        split_rows = std::max<int64_t>(split_rows, g.orow0 + g.rows);
+      }
+      const int64_t units = ctx_.num_sms / 2, tiles = m_tiles * ((N + tile_n - 1) / tile_n);
+      const int64_t nk = (K + kGemmBK - 1) / kGemmBK;
+      auto fill = [&](int64_t u) { return static_cast<double>(u) / (static_cast<double>((u + units - 1) / units) * units); };
+      // Time model: tensor work at ~1.3 PFLOP/s scaled by the wave fill, plus
+      // the reduce's HBM traffic (S partials read, the residual read and
+      // written) at ~5 TB/s; split only for a clear (> 5 %) gain.
+      const double flops = 2.0 * static_cast<double>(split_rows) * N * K;
+      auto cost = [&](int sp) {
+        const double t = flops / (1.3e15 * fill(tiles * sp));
+        return sp == 1 ? t : t + (sp + 2.0) * static_cast<double>(split_rows) * N * 4.0 / 5e12;
+      };
+      double best = cost(1);
+      const double base = best;
+      for (int sp = 2; sp <= 4; ++sp) {
+        if (nk / sp < 16) break;
+        const double c2 = cost(sp);
+        if (c2 < best && c2 < 0.95 * base) {
+          best = c2;
+          splits = sp;
+        }
+      }
+      const size_t need = static_cast<size_t>(splits) * split_rows * N * 4;
+      if (splits > 1 && need > split_ws_bytes_) {
+        if (split_ws_) cuda_check(cudaFree(split_ws_), "free split workspace");
+        split_ws_ = nullptr;
+        split_ws_bytes_ = 0;
+        // Plans built earlier keep the old pointer: only grow before any split launch exists.
+        if (split_launches_ == 0) {
+          cuda_check(cudaMalloc(&split_ws_, std::max<size_t>(need, size_t(64) << 20)), "split workspace");
+          split_ws_bytes_ = std::max<size_t>(need, size_t(64) << 20);
+        }
+      }
+      if (splits > 1 && need > split_ws_bytes_) splits = 1;
+    }
+  }
   for (size_t p = 0; p < pieces.size(); ++p) {
     if (before_piece) before_piece(static_cast<int>(p));
     if (p == 0 && ready) add_wait(ready, 0);
@@ -412,6 +464,14 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
     args.ep = ep;
     args.err = ctx_.d_err;
     gemm_finalize_groups(args, tile_m, tile_n);
+    if (splits > 1) {
+      args.ep = EpilogueArgs{};
+      args.ep.mode = kEpiF32;
+      args.ep.out_f32 = split_ws_;
+      args.ep.ld_out = N;
+      gemm_set_k_splits(args, splits, split_rows * N);
+      ++split_launches_;
+    }
     double flops = 0.0;
     for (auto& g : pg) flops += 2.0 * g.rows * static_cast<double>(N) * static_cast<double>(K);
     building_->push_back({[st, args, c, pair](cudaStream_t s) {
@@ -423,6 +483,16 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
                                          "gemm");
                           },
                           1, kOpGemm, flops, tag});
+    if (splits > 1) {
+      const float* ws = split_ws_;
+      float* out = ep.out_f32;
+      const int64_t ld_out = ep.ld_out, rows = split_rows, n = N, stride = split_rows * N;
+      const int sp = splits;
+      building_->push_back({[=](cudaStream_t s) {
+                              cuda_check(launch_split_reduce(ws, sp, stride, rows, n, n, out, ld_out, s), "split reduce");
+                            },
+                            1, kOpOther, 0.0, tag + " split reduce"});
+    }
   }
   if (expand0 || expand1) {
     scratch_free_[pair_idx] = plan_event();

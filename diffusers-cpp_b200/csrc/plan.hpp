@@ -125,6 +125,11 @@ class StepPlanner {
   cudaEvent_t plan_start_ = nullptr;                   // recorded on the main stream first in a plan
   cudaStream_t side_ = nullptr;
   std::vector<cudaEvent_t> plan_events_;
+  // f32 partials of K-split GEMMs (shared by every split launch of the
+  // model's plans, which run in order on one stream).
+  float* split_ws_ = nullptr;
+  size_t split_ws_bytes_ = 0;
+  int64_t split_launches_ = 0;  // split launches in the current plans (the workspace may grow only at 0)
 };
 
 }  // namespace dcpp

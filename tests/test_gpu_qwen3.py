@@ -131,3 +131,26 @@ def test_bad_token_id_and_missing_parameter(ctx):
         m2.prepare(1, 8)
     assert e.value.status == 7
     m2.close()
+
+
+def test_prefill_k_split_projections(ctx, monkeypatch):
+    """The config-4 projection shapes (M = 4 x 512, N = 2560, K = 4096 / 9728)
+    run as K-split GEMMs (f32 partials, ordered reduce): against the oracle,
+    against the unsplit GEMMs, and deterministic from run to run."""
+    c = synth.Qwen3Cfg(vocab_size=1000, num_hidden_layers=1)
+    B, S, taps = 4, 512, (1,)
+    params = synth.make_qwen3_params(c, seed=21)
+    ids = synth.make_qwen3_ids(c, B, S, seed=22)
+    outs = []
+    for ksplit in ("1", "1", "0"):
+        monkeypatch.setenv("DCPP_GEMM_KSPLIT", ksplit)
+        m = dcpp_b200.Qwen3Model(ctx, c)
+        m.load_params(params)
+        m.prepare(B, S, taps)
+        outs.append(run(m, c, ids, len(taps)))
+        m.close()
+    assert torch.equal(outs[0][0], outs[1][0])
+    ref_last, _ = qo.Qwen3Oracle(qo.Qwen3Config(**c.__dict__), params).forward(ids, taps=taps)
+    for last, _ in (outs[0], outs[2]):
+        assert rel(last, ref_last) < H_TOL, rel(last, ref_last)
+    assert rel(outs[0][0], outs[2][0]) < 2e-3
