@@ -395,7 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Two-tile variant: one CTA = two 128-row query tiles (A, B) of one (batch,
 // head), 128-key K / V tiles, 320 threads:
 //   warp 0      TMA: Q_A, Q_B once, then K_j and V_j^T into a 2-stage ring
-//   warp 1      TMEM allocation and the MMA thread; order
+//   warp 1      TMEM allocation and the MMAs (the warp runs the loop with
+//               descriptors built once; one elected lane issues); order
 //                 S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 PV_B1 S_B2 ...
 //               so that while one tile's softmax runs, the tensor core
 //               computes the other tile's P.V and next scores
@@ -404,11 +405,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 //               per SM sub-partition hide each other's latencies.
 // TMEM (512 columns): S_A / P_A at 0, S_B / P_B at 128, O_A at 256, O_B at
 // 384.  S_X(j+1) overwrites S_X only after PV_X(j) (which reads P_X(j) from
-// it) has completed.
+// it) has completed.  The warps that mostly wait (TMA, MMA) sleep in their
+// barrier waits, leaving issue slots to the softmax warps beside them.
 constexpr int k2Tiles = 2;
 constexpr int k2Stages = 2;
 constexpr int k2Threads = 320;
 constexpr int k2SmemBytes = (k2Tiles + 2 * k2Stages) * kTileBytes + 1024 + 256;
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
 
 __global__ void __launch_bounds__(k2Threads, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -473,7 +485,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
       }
       for (int j = 0; j < nkv; ++j) {
         const int st = j % k2Stages;
-        if (!mbar_wait(&kv_empty[st], ((j / k2Stages) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
+        if (!mbar_wait_sleep(&kv_empty[st], ((j / k2Stages) & 1) ^ 1, p.err, kDevTimeoutAttn)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
         uint8_t* k = sK + st * kTileBytes;
         uint8_t* v = sV + st * kTileBytes;
@@ -484,45 +496,49 @@ __global__ void __launch_bounds__(k2Threads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(128, 128);
-      const uint32_t aQ = smem_u32(sQ);
-      auto issue_s = [&](int x, int j) -> bool {
-        const int st = j % k2Stages;
-        if (!mbar_wait(&kv_full[st], (j / k2Stages) & 1, p.err, kDevTimeoutAttn)) return false;
-        tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * kTileBytes);
+    // The whole warp runs the loop (waits, descriptors: warp-uniform); one
+    // elected lane issues the MMAs and their commits.
+    constexpr uint32_t idesc = make_idesc_bf16(128, 128);
+    const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ));
+    const uint64_t dK = make_sdesc_sw128(smem_u32(sK));
+    const uint64_t dV = make_sdesc_sw128(smem_u32(sV));
+    auto koff = [](int k) -> uint64_t { return static_cast<uint64_t>(((k >> 2) * kHalfBytes + (k & 3) * 32) >> 4); };
+    constexpr uint64_t kTileD = kTileBytes >> 4;
+    const bool leader = elect_one();
+    auto issue_s = [&](int x, int j) -> bool {
+      const int st = j % k2Stages;
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(&kv_full[st], (j / k2Stages) & 1, p.err, kDevTimeoutAttn))) return false;
+      tc_fence_after();
+      const uint64_t q = dQ + x * kTileD, kd = dK + st * kTileD;
+      const uint32_t tS = tmem_base + x * 128;
+      if (leader) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-          umma_bf16(tmem_base + x * 128, make_sdesc_sw128(aQ + x * kTileBytes + off), make_sdesc_sw128(aK + off),
-                    idesc, k > 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < 8; ++k) umma_bf16(tS, q + koff(k), kd + koff(k), idesc, k > 0 ? 1u : 0u);
         umma_commit(&s_full[x]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
-      for (int x = 0; x < k2Tiles && ok; ++x) ok = issue_s(x, 0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % k2Stages;
-        const uint32_t aV = smem_u32(sV + st * kTileBytes);
-        for (int x = 0; x < k2Tiles && ok; ++x) {
-          if (!mbar_wait(&p_full[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t tO = tmem_base + 256 + x * 128;
+      }
+      __syncwarp();
+      return true;
+    };
+    bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(q_full, 0, p.err, kDevTimeoutAttn));
+    for (int x = 0; x < k2Tiles && ok; ++x) ok = issue_s(x, 0);
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int st = j % k2Stages;
+      const uint64_t vd = dV + st * kTileD;
+      for (int x = 0; x < k2Tiles && ok; ++x) {
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&p_full[x], j & 1, p.err, kDevTimeoutAttn))) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tO = tmem_base + 256 + x * 128, tP = tmem_base + x * 128;
+        if (leader) {
+          umma_bf16_ts(tO, tP, vd, idesc, j > 0 ? 1u : 0u);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-            umma_bf16_ts(tO, tmem_base + x * 128 + k * 8, make_sdesc_sw128(aV + off), idesc,
-                         (j > 0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 1; k < 8; ++k) umma_bf16_ts(tO, tP + k * 8, vd + koff(k), idesc, 1u);
           umma_commit(&pv_done[x]);
           if (x == k2Tiles - 1) umma_commit(&kv_empty[st]);
-          if (j + 1 < nkv) {
-            // S_X(j+1) overwrites P_X(j): wait until PV_X(j) has read it.
-            if (!mbar_wait(&pv_done[x], j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-            ok = issue_s(x, j + 1);
-          }
+        }
+        __syncwarp();
+        if (j + 1 < nkv) {
+          if (!__all_sync(0xffffffffu, mbar_wait_sleep(&pv_done[x], j & 1, p.err, kDevTimeoutAttn))) { ok = false; break; }
+          ok = issue_s(x, j + 1);
         }
       }
     }
@@ -538,7 +554,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, p.err, kDevTimeoutAttn));
+      ok = __all_sync(0xffffffffu, mbar_wait_sleep(&s_full[x], j & 1, p.err, kDevTimeoutAttn));
       if (!ok) break;
       tc_fence_after();
       uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -575,7 +591,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
       l = l * alpha + sum;
       m = m_use;
       if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (j - 1) & 1, p.err, kDevTimeoutAttn));
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep(&pv_done[x], (j - 1) & 1, p.err, kDevTimeoutAttn));
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
@@ -596,7 +612,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
       tc_fence_before();
       mbar_arrive(&p_full[x]);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv - 1) & 1, p.err, kDevTimeoutAttn));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep(&pv_done[x], (nkv - 1) & 1, p.err, kDevTimeoutAttn));
     if (ok) {
       tc_fence_after();
       const int q = q0 + x * kBQ + row;

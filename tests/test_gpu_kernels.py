@@ -155,3 +155,38 @@ def test_attention_matches_oracle(ctx, attn_kind, B, S, H):
     ref = fo.sdpa(q, k, v).flatten(2)
     rel = ((out.cpu().double() - ref).norm() / ref.norm()).item()
     assert rel < 1e-2, rel
+
+
+@pytest.mark.parametrize("S", [1024, 333])
+def test_attention_growing_scores(ctx, attn_kind, S):
+    """Keys turn from anti-aligned to aligned with every query along the
+    sequence, the score rising linearly with the key index (no rotary
+    rotation: all position ids 0), so each key tile's row maximum exceeds the
+    running one by more than the lazy-rescale threshold (2^8): every tile
+    takes the rescale path."""
+    H, D = 2, 256
+    g = torch.Generator().manual_seed(5)
+    u = torch.randn(128, generator=g)
+    v = torch.randn(128, generator=g)
+    v -= (v @ u) / (u @ u) * u
+    u, v = u / u.norm(), v / v.norm()
+    cs = torch.linspace(-1.0, 1.0, S)
+    keys = cs[:, None] * u + torch.sqrt(1 - cs * cs)[:, None] * v
+    qkv = torch.zeros(1, S, 3 * D)
+    for h in range(H):
+        qkv[0, :, h * 128:(h + 1) * 128] = u + 0.05 * torch.randn(S, 128, generator=g)
+        qkv[0, :, D + h * 128:D + (h + 1) * 128] = keys
+        qkv[0, :, 2 * D + h * 128:2 * D + (h + 1) * 128] = torch.randn(S, 128, generator=g)
+    qkv = qkv.to(torch.bfloat16)
+    w = torch.full((128,), 2.0)
+    ids = torch.zeros(S, 4, dtype=torch.int32)
+    out = torch.empty(1, S, D, dtype=torch.bfloat16, device="cuda")
+    ctx.attention(qkv.cuda(), 1, S, H, w.cuda(), w.cuda(), 1e-6, ids.cuda(), (32, 32, 32, 32), 2000.0, out)
+    ctx.synchronize()
+    x = qkv.double()
+    q, k, vv = x[..., :D].unflatten(-1, (H, 128)), x[..., D:2 * D].unflatten(-1, (H, 128)), x[..., 2 * D:].unflatten(-1, (H, 128))
+    q = fo.rms_norm(q, w.double(), 1e-6)
+    k = fo.rms_norm(k, w.double(), 1e-6)
+    ref = fo.sdpa(q, k, vv).flatten(2)
+    rel = ((out.cpu().double() - ref).norm() / ref.norm()).item()
+    assert rel < 1e-2, rel
