@@ -412,16 +412,6 @@ constexpr int k2Stages = 2;
 constexpr int k2Threads = 320;
 constexpr int k2SmemBytes = (k2Tiles + 2 * k2Stages) * kTileBytes + 1024 + 256;
 
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "elect.sync _|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
-
 __global__ void __launch_bounds__(k2Threads, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnTcArgs p) {
@@ -504,7 +494,7 @@ __global__ void __launch_bounds__(k2Threads, 1)
     const uint64_t dV = make_sdesc_sw128(smem_u32(sV));
     auto koff = [](int k) -> uint64_t { return static_cast<uint64_t>(((k >> 2) * kHalfBytes + (k & 3) * 32) >> 4); };
     constexpr uint64_t kTileD = kTileBytes >> 4;
-    const bool leader = elect_one();
+    const bool leader = elect_one_sync();
     auto issue_s = [&](int x, int j) -> bool {
       const int st = j % k2Stages;
       if (!__all_sync(0xffffffffu, mbar_wait_sleep(&kv_full[st], (j / k2Stages) & 1, p.err, kDevTimeoutAttn))) return false;

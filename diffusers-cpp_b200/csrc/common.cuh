@@ -366,4 +366,16 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
 
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// One lane of a converged warp (elect.sync), so that the warp's other work
+// stays warp-uniform around a single-thread issue.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 }  // namespace dcpp

@@ -897,7 +897,7 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
         const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           if (kQuant) {
             mbar_arrive_expect_tx(&full[stage], kAStageBytes + kRaw);
             tma_load_2d(smA + stage * kAStageBytes, &tmA, &full[stage], kb * kGemmBK, ya);
@@ -918,35 +918,44 @@ __global__ void __launch_bounds__(gemm_threads<BSRC>(), 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < nk; ++kb) {
-          uint64_t* ready = kQuant ? &bready[stage] : &full[stage];
-          if (!mbar_wait(ready, phase, p.err, kDevTimeoutFull)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(smA + stage * kAStageBytes);
-          const uint32_t b0 = smem_u32(smB + stage * kBSt);
-#pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_bf16(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
-          }
-          umma_commit(&empty[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
-        }
-        if (!ok) break;
-        umma_commit(&acc_full[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    // Converged warp, descriptors built once, one elected lane issuing (as in
+    // the pair kernel).
+    constexpr uint32_t idesc = make_idesc_bf16(kGemmBM, BN);
+    const bool leader = elect_one_sync();
+    const uint64_t dA = make_sdesc_sw128(smem_u32(smA)), dB = make_sdesc_sw128(smem_u32(smB));
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree))) {
+        ok = false;
+        break;
       }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < nk; ++kb) {
+        uint64_t* ready = kQuant ? &bready[stage] : &full[stage];
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(ready, phase, p.err, kDevTimeoutFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t a = dA + static_cast<uint64_t>(stage * (kAStageBytes >> 4));
+        const uint64_t b = dB + static_cast<uint64_t>(stage * (kBSt >> 4));
+        if (leader) {
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) umma_bf16(d_tmem, a + 2 * k, b + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (leader) umma_commit(&acc_full[acc]);
+      __syncwarp();
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   } else if (warp < 6) {
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
@@ -1130,7 +1139,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         int kb0, kb1;
         k_range(p, tc, nk, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           const uint32_t full0 = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], kQuant ? 2 * kPairA : 2 * (kPairA + kPB));
           if (!kQuant && p.conv.taps) {
@@ -1152,39 +1161,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    if (rank == 0) {
+      // The whole warp runs the loop (waits and descriptors are warp-uniform,
+      // the descriptors built once); one elected lane issues the MMAs and
+      // their commits.  A k step or a stage only moves the descriptor's
+      // start-address field (16-byte units, no carry out of its 14 bits).
       constexpr uint32_t idesc = make_idesc_bf16(256, BN);
+      const bool leader = elect_one_sync();
+      const uint64_t dA = make_sdesc_sw128(smem_u32(smA)), dB = make_sdesc_sw128(smem_u32(smB));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = pair; t < p.total_tiles && ok; t += npairs) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         int kb0, kb1;
         k_range(p, decode_tile(p, t), nk, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err, kDevTimeoutFull)) { ok = false; break; }
-          if (kQuant && (!mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant) ||
-                         !mbar_wait_cluster(&bpeer[stage], phase, p.err, kDevTimeoutDequant))) {
+          bool w = mbar_wait_sleep(&full[stage], phase, p.err, kDevTimeoutFull);
+          if (kQuant)
+            w = w && mbar_wait(&bready[stage], phase, p.err, kDevTimeoutDequant) &&
+                mbar_wait_cluster(&bpeer[stage], phase, p.err, kDevTimeoutDequant);
+          if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smA + stage * kPairA);
-          const uint32_t b0 = smem_u32(smB + stage * kPB);
+          const uint64_t a = dA + static_cast<uint64_t>(stage * (kPairA >> 4));
+          const uint64_t b = dB + static_cast<uint64_t>(stage * (kPB >> 4));
+          if (leader) {
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
-                           (kb != kb0 || k != 0) ? 1u : 0u);
+            for (int k = 0; k < kGemmBK / 16; ++k)
+              umma_bf16_pair(d_tmem, a + 2 * k, b + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            umma_commit_pair(&empty[stage], 0x3);
           }
-          umma_commit_pair(&empty[stage], 0x3);
+          __syncwarp();
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit_pair(&acc_full[acc], 0x3);
+        if (leader) umma_commit_pair(&acc_full[acc], 0x3);
+        __syncwarp();
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     } else if (lane == 0 && kQuant) {
@@ -1344,12 +1366,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int x0 = (rem - y0 * cg.tiles_x) * 128;
         const int yb = tc.n_tile * BN + static_cast<int>(rank) * (BN / 2);
         for (int cb = 0; cb < ncb && ok; ++cb) {
-          if (!mbar_wait(&pempty[ps], pph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait_sleep(&pempty[ps], pph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&pfull[ps], 2 * kPatchTxBytes);
           tma_load_4d_pair(smP + ps * kPatchBytes, &tmP, mapa_shared(smem_u32(&pfull[ps]), 0), cb * 64, x0 - 1,
                            y0 - 1, b);
           for (int tap = 0; tap < cg.taps; ++tap) {
-            if (!mbar_wait(&bempty[bs], bph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+            if (!mbar_wait_sleep(&bempty[bs], bph ^ 1, p.err, kDevTimeoutEmpty)) { ok = false; break; }
             if (rank == 0) mbar_arrive_expect_tx(&bfull[bs], 2 * kPB);
             tma_load_2d_pair(smB + bs * kPB, &tmB, mapa_shared(smem_u32(&bfull[bs]), 0),
                              (tap * ncb + cb) * kGemmBK, yb);
@@ -1360,38 +1382,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    if (rank == 0) {
+      // Converged warp, descriptors built once, one elected lane issuing (as
+      // in the pair GEMM); a tap's view of the patch moves the start field
+      // by its row offset.
       constexpr uint32_t idesc = make_idesc_bf16(256, BN);
+      const bool leader = elect_one_sync();
+      const uint64_t dP = make_sdesc_sw128(smem_u32(smP)), dB = make_sdesc_sw128(smem_u32(smB));
       int bs = 0, ps = 0, acc = 0;
       uint32_t bph = 0, pph = 0, acc_phase = 0;
       bool ok = true;
       for (int t = pair; t < p.total_tiles && ok; t += npairs) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&acc_empty[acc], acc_phase ^ 1, p.err, kDevTimeoutAccumFree))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool first = true;
         for (int cb = 0; cb < ncb && ok; ++cb) {
-          if (!mbar_wait(&pfull[ps], pph, p.err, kDevTimeoutFull)) { ok = false; break; }
-          const uint32_t patch = smem_u32(smP + ps * kPatchBytes);
+          if (!__all_sync(0xffffffffu, mbar_wait_sleep(&pfull[ps], pph, p.err, kDevTimeoutFull))) {
+            ok = false;
+            break;
+          }
+          const uint64_t patch = dP + static_cast<uint64_t>(ps * (kPatchBytes >> 4));
           for (int tap = 0; tap < cg.taps; ++tap) {
-            if (!mbar_wait(&bfull[bs], bph, p.err, kDevTimeoutFull)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t a0 = patch + static_cast<uint32_t>((cg.dy[tap] + 1) * kPatchW + cg.dx[tap] + 1) * 128u;
-            const uint32_t b0 = smem_u32(smB + bs * kPB);
-#pragma unroll
-            for (int k = 0; k < kGemmBK / 16; ++k) {
-              umma_bf16_pair(d_tmem, make_sdesc_sw128(a0 + k * 32), make_sdesc_sw128(b0 + k * 32), idesc,
-                             (first && k == 0) ? 0u : 1u);
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&bfull[bs], bph, p.err, kDevTimeoutFull))) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            const uint64_t a = patch + static_cast<uint64_t>(((cg.dy[tap] + 1) * kPatchW + cg.dx[tap] + 1) * 8);
+            const uint64_t b = dB + static_cast<uint64_t>(bs * (kPB >> 4));
+            if (leader) {
+#pragma unroll
+              for (int k = 0; k < kGemmBK / 16; ++k)
+                umma_bf16_pair(d_tmem, a + 2 * k, b + 2 * k, idesc, (first && k == 0) ? 0u : 1u);
+              umma_commit_pair(&bempty[bs], 0x3);
+            }
+            __syncwarp();
             first = false;
-            umma_commit_pair(&bempty[bs], 0x3);
             if (++bs == kStages) { bs = 0; bph ^= 1; }
           }
-          umma_commit_pair(&pempty[ps], 0x3);
+          if (leader) umma_commit_pair(&pempty[ps], 0x3);
+          __syncwarp();
           if (++ps == 2) { ps = 0; pph ^= 1; }
         }
         if (!ok) break;
-        umma_commit_pair(&acc_full[acc], 0x3);
+        if (leader) umma_commit_pair(&acc_full[acc], 0x3);
+        __syncwarp();
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }

@@ -245,6 +245,20 @@ class Context:
         self.h = h
         self.device = device
         self._children = weakref.WeakSet()
+        # With torch present the context runs on a torch stream, and every call
+        # that touches device memory is ordered against torch's current stream
+        # (_call): tensors torch has just produced (a .cuda() copy, a fill) are
+        # complete before the library reads them, and torch work queued after
+        # the call sees its results.
+        self._stream = self._own_stream = None
+        try:
+            import torch
+        except ImportError:
+            torch = None
+        if torch is not None and torch.cuda.is_available():
+            self._own_stream = torch.cuda.Stream(device=device)
+            self.check(lib().dcpp_set_stream(h, self._own_stream.cuda_stream), "set_stream")
+            self._stream = self._own_stream
 
     def check(self, status: int, what: str = ""):
         if status != DCPP_OK:
@@ -268,7 +282,32 @@ class Context:
         self.check(lib().dcpp_synchronize(self.h), "synchronize")
 
     def set_stream(self, stream_ptr: Optional[int]):
-        self.check(lib().dcpp_set_stream(self.h, stream_ptr), "set_stream")
+        """Run on an external cudaStream_t (None: back to the context's own)."""
+        if stream_ptr:
+            self.check(lib().dcpp_set_stream(self.h, stream_ptr), "set_stream")
+            if self._own_stream is not None:
+                import torch
+                self._stream = torch.cuda.ExternalStream(stream_ptr, device=self.device)
+        else:
+            own = self._own_stream.cuda_stream if self._own_stream is not None else None
+            self.check(lib().dcpp_set_stream(self.h, own), "set_stream")
+            self._stream = self._own_stream
+
+    def _call(self, fn, *args):
+        """fn(*args) (a C entry point that reads or writes device memory),
+        ordered with torch's current stream on both sides."""
+        s = self._stream
+        if s is None:
+            return fn(*args)
+        import torch
+        cur = torch.cuda.current_stream(self.device)
+        same = cur.cuda_stream == s.cuda_stream
+        if not same:
+            s.wait_stream(cur)
+        st = fn(*args)
+        if not same:
+            cur.wait_stream(s)
+        return st
 
     GEMM_AUTO, GEMM_SINGLE_SM, GEMM_PAIR = 0, 1, 2
 
@@ -285,37 +324,37 @@ class Context:
 
     # op-level entry points (device pointers)
     def dequant(self, gtype: int, blocks, n: int, out):
-        self.check(lib().dcpp_dequant(self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant")
+        self.check(self._call(lib().dcpp_dequant, self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant")
 
     def dequant_bf16(self, gtype: int, blocks, n: int, out):
-        self.check(lib().dcpp_dequant_bf16(self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant_bf16")
+        self.check(self._call(lib().dcpp_dequant_bf16, self.h, gtype, _ptr(blocks), n, _ptr(out)), "dequant_bf16")
 
     def f32_to_bf16(self, x, n: int, out):
-        self.check(lib().dcpp_f32_to_bf16(self.h, _ptr(x), n, _ptr(out)), "f32_to_bf16")
+        self.check(self._call(lib().dcpp_f32_to_bf16, self.h, _ptr(x), n, _ptr(out)), "f32_to_bf16")
 
     def gemm(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
-        self.check(lib().dcpp_gemm(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm")
+        self.check(self._call(lib().dcpp_gemm, self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm")
 
     def pack_weight(self, wtype: int, raw, N: int, K: int, out):
-        self.check(lib().dcpp_pack_weight(self.h, wtype, _ptr(raw), N, K, _ptr(out)), "pack_weight")
+        self.check(self._call(lib().dcpp_pack_weight, self.h, wtype, _ptr(raw), N, K, _ptr(out)), "pack_weight")
 
     def gemm_packed(self, wtype: int, packed, N: int, K: int, x_bf16, M: int, y):
-        self.check(lib().dcpp_gemm_packed(self.h, wtype, _ptr(packed), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_packed")
+        self.check(self._call(lib().dcpp_gemm_packed, self.h, wtype, _ptr(packed), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_packed")
 
     def gemm_noalloc(self, wtype: int, w, N: int, K: int, x_bf16, M: int, y):
         """Like gemm(), but allocates no device memory: for callers whose
         device memory is owned by someone else or must not change mid-run
         (see dcpp_gemm_noalloc in include/dcpp.h for the limits)."""
-        self.check(lib().dcpp_gemm_noalloc(self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_noalloc")
+        self.check(self._call(lib().dcpp_gemm_noalloc, self.h, wtype, _ptr(w), N, K, _ptr(x_bf16), M, _ptr(y)), "gemm_noalloc")
 
     def layernorm_mod(self, x, rows: int, D: int, shift, scale, eps: float, y):
-        self.check(lib().dcpp_layernorm_mod(self.h, _ptr(x), rows, D, _ptr(shift), _ptr(scale), eps, _ptr(y)),
+        self.check(self._call(lib().dcpp_layernorm_mod, self.h, _ptr(x), rows, D, _ptr(shift), _ptr(scale), eps, _ptr(y)),
                    "layernorm_mod")
 
     def attention(self, qkv, B: int, S: int, H: int, norm_q, norm_k, eps: float, ids, axes_dims: Sequence[int],
                   theta: float, out):
         arr = (ctypes.c_int64 * len(axes_dims))(*axes_dims)
-        self.check(lib().dcpp_attention(self.h, _ptr(qkv), B, S, H, 128, _ptr(norm_q), _ptr(norm_k), eps, _ptr(ids),
+        self.check(self._call(lib().dcpp_attention, self.h, _ptr(qkv), B, S, H, 128, _ptr(norm_q), _ptr(norm_k), eps, _ptr(ids),
                                         len(axes_dims), arr, theta, _ptr(out)), "attention")
 
     # tensor parallelism
@@ -332,7 +371,7 @@ class Context:
         self.check(lib().dcpp_tp_init(self.h, rank, nranks, buf), "tp_init")
 
     def allreduce(self, buf, count: int, dtype: int = TYPE_F32):
-        self.check(lib().dcpp_allreduce(self.h, _ptr(buf), count, dtype), "allreduce")
+        self.check(self._call(lib().dcpp_allreduce, self.h, _ptr(buf), count, dtype), "allreduce")
 
 
 def packed_bytes(gtype: int, N: int, K: int) -> int:
@@ -411,6 +450,10 @@ class Flux2Model:
             msg = lib().dcpp_flux2_last_error(self.h).decode()
             raise DcppError(status, f"{what}: {msg}" if what else msg)
 
+    def _run(self, fn, *args):
+        # host-only models have no context (their compute calls fail in the library)
+        return self.ctx._call(fn, *args) if self.ctx is not None else fn(*args)
+
     def read_param(self, name: str):
         """(ggml type, (rows, cols), uint8 array) of an assembled parameter."""
         t, r, c, n = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_size_t()
@@ -464,25 +507,25 @@ class Flux2Model:
         self._check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
 
     def forward(self, hidden, encoder, timestep, img_ids, txt_ids, out, guidance=None):
-        self._check(lib().dcpp_flux2_forward(self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
+        self._check(self._run(lib().dcpp_flux2_forward, self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
                                                 _ptr(txt_ids), _ptr(guidance), _ptr(out)), "forward")
 
     def denoise_step(self, latents, encoder, timestep, dt: float, img_ids, txt_ids, latents_out):
-        self._check(lib().dcpp_flux2_denoise_step(self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
+        self._check(self._run(lib().dcpp_flux2_denoise_step, self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
                                                      _ptr(img_ids), _ptr(txt_ids), _ptr(latents_out)), "denoise_step")
 
     def load_inputs(self, latents, encoder, img_ids, txt_ids):
-        self._check(lib().dcpp_flux2_load_inputs(self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
+        self._check(self._run(lib().dcpp_flux2_load_inputs, self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
                                                     _ptr(txt_ids)), "load_inputs")
 
     def set_timestep(self, timestep: float, dt: float):
         self._check(lib().dcpp_flux2_set_timestep(self.h, float(timestep), float(dt)), "set_timestep")
 
     def run_resident(self):
-        self._check(lib().dcpp_flux2_run_resident(self.h), "run_resident")
+        self._check(self._run(lib().dcpp_flux2_run_resident, self.h), "run_resident")
 
     def read_latents(self, out):
-        self._check(lib().dcpp_flux2_read_latents(self.h, _ptr(out)), "read_latents")
+        self._check(self._run(lib().dcpp_flux2_read_latents, self.h, _ptr(out)), "read_latents")
 
     PROFILE_KINDS = {"gemm": 0, "attention": 1, "norm": 2, "gemv": 3, "dequant": 4, "other": 5, "allreduce": 6}
 
@@ -702,7 +745,7 @@ class Qwen3Model:
     def forward(self, input_ids, last_hidden=None, taps=None, attention_mask=None):
         """input_ids [B, S] int32; attention_mask [B, S] f32 (1 attend, 0 padding)
         or None; last_hidden [B, S, D] f32; taps [B, S, n_taps * D] f32."""
-        self.ctx.check(lib().dcpp_qwen3_forward(self.h, _ptr(input_ids), _ptr(attention_mask), _ptr(last_hidden),
+        self.ctx.check(self.ctx._call(lib().dcpp_qwen3_forward, self.h, _ptr(input_ids), _ptr(attention_mask), _ptr(last_hidden),
                                                 _ptr(taps)), "forward")
 
     def set_profiling(self, on: bool):
@@ -813,7 +856,7 @@ class VAEModel:
 
     def decode(self, latents, image):
         """latents [B, ph*pw, 4*latent_channels] f32 -> image [B, out_channels, H, W] f32."""
-        self.ctx.check(lib().dcpp_vae_decode(self.h, _ptr(latents), _ptr(image)), "decode")
+        self.ctx.check(self.ctx._call(lib().dcpp_vae_decode, self.h, _ptr(latents), _ptr(image)), "decode")
 
     def set_profiling(self, on: bool):
         self.ctx.check(lib().dcpp_vae_set_profiling(self.h, 1 if on else 0), "set_profiling")
