@@ -1,7 +1,7 @@
 """Benchmark of the Flux2 DiT denoise step (BASELINE.json metric: DiT denoise
 steps/s at 1024^2, Q4_K, on 1/2/4/8 B200, plus tensor-pipe fraction of peak).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|vae]
 
 One step = one Flux2Transformer2DModel::forward + Euler update on the
 resident latent (hidden 3072, 24 heads x 128, 5 double +
@@ -666,19 +666,117 @@ def run_vae(args):
     return 0
 
 
+GEMM_METRIC = "quantized GEMM TFLOP/s (config-5 sweep)"
+GEMM_TYPES = {"Q4_K": 12, "Q8_0": 8, "F16": 1, "BF16": 30}
+GEMM_SWEEP_M = (256, 1024, 4096, 8192)
+GEMM_SWEEP_NK = ((3072, 3072), (9216, 3072), (3072, 9216), (12288, 4096))
+
+
+def run_gemm_sweep(args):
+    """dcpp_gemm (weight expansion to bf16 + tcgen05 GEMM,
+    f32 output) for Q4_K / Q8_0 / F16 weights N(0, 1/K) and bf16 activations
+    N(0, 1), M x (N, K) over the sweep grid (or --gemm-shapes
+    TYPE:M:N:K,...).  Each timed call runs after a 256 MB write that flushes
+    L2 and behind a device-side sleep that hides the host's launch time;
+    CUDA events bracket the call alone.  One GPU."""
+    import torch
+
+    import dcpp_b200
+    from dcpp_b200 import quant
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--config 5 runs on one GPU")
+    if args.gemm_shapes:
+        shapes = []
+        for item in args.gemm_shapes.split(","):
+            t, m, n, k = item.split(":")
+            shapes.append((t, int(m), int(n), int(k)))
+    else:
+        shapes = [(t, m, n, k) for t in ("Q4_K", "Q8_0", "F16") for (n, k) in GEMM_SWEEP_NK for m in GEMM_SWEEP_M]
+    ctx = dcpp_b200.Context(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    peak_b, peak_s, hbm, peak_src = measured_peaks()
+    g = torch.Generator().manual_seed(0)
+    weights = {}
+    results = []
+    clocks = ClockSampler(0)
+    clocks.start()
+    tot_fl = tot_ms = 0.0
+    for t, M, N, K in shapes:
+        key = (t, N, K)
+        if key not in weights:
+            weights.clear()
+            w = torch.randn(N, K, generator=g) / K ** 0.5
+            weights[key] = (quant.quantize(w, GEMM_TYPES[t]) if t != "BF16" else w.to(torch.bfloat16).view(torch.uint8)).cuda()
+        wq = weights[key]
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+        y = torch.empty(M, N, dtype=torch.float32, device="cuda")
+        for _ in range(args.warmup):
+            ctx.gemm(GEMM_TYPES[t], wq, N, K, x, M, y)
+        ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda._sleep(2_000_000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ctx.gemm(GEMM_TYPES[t], wq, N, K, x, M, y)
+            e1.record(stream)
+            e1.synchronize()
+            ms += e0.elapsed_time(e1)
+        ms /= args.steps
+        assert torch.isfinite(y).all(), "non-finite GEMM output"
+        fl = 2.0 * M * N * K
+        tf = fl / (ms * 1e-3) / 1e12
+        tot_fl += fl
+        tot_ms += ms
+        results.append({"wtype": t, "M": M, "N": N, "K": K, "ms": round(ms, 4), "tflops": round(tf, 1),
+                        "frac_of_peak": round(tf / peak_b, 3)})
+    clk = clocks.stop()
+    agg = tot_fl / (tot_ms * 1e-3) / 1e12
+    line = {
+        "metric": GEMM_METRIC,
+        "value": agg,
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tot_ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (weights N(0,1/K) quantised on the host; activations N(0,1) bf16)",
+        "config": {"workload": "config5: dcpp_gemm sweep, weight expansion + tcgen05 GEMM, f32 output; value = "
+                               "total FLOP / total time over the shapes",
+                   "l2": "flushed (256 MB write) before every timed call", "parallelism": "tp1"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (after the bf16 expansion)", "achieved": agg,
+                     "peak": peak_b, "unit": "TFLOP/s", "frac": agg / peak_b, "peak_kind": f"bf16 burst ({peak_src})",
+                     "traffic": None},
+        "shapes": results,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["4", "vae"], default="2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["4", "5", "vae"], default="2")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops-csv", default=None, help="directory for a per-op time CSV of the profiled step (rank 0)")
     ap.add_argument("--attn-kernel", type=int, default=0, help="0 auto, 1 one query tile per CTA, 2 two tiles")
     ap.add_argument("--vae-packed", type=int, default=64, help="--config vae: packed tokens per side (64: 1024^2)")
     ap.add_argument("--vae-tile", type=int, default=0, help="--config vae: decode_tiled tile size in pixels (0: untiled)")
+    ap.add_argument("--gemm-shapes", default=None, help="--config 5: TYPE:M:N:K[,...] instead of the sweep grid")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -687,6 +785,11 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "config 4 has no CPU reference arm in this bench"}))
             return 0
         return run_qwen3(args)
+    if args.config == "5":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU reference arm in this bench"}))
+            return 0
+        return run_gemm_sweep(args)
     if args.config == "vae":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the VAE decode has no CPU reference arm in this bench"}))

@@ -1647,6 +1647,30 @@ cudaError_t make_tmap_conv_patch(CUtensorMap* map, const void* base, int64_t B, 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+int gemm_choose_k_splits(int64_t tiles, int num_sms, int64_t rows, int64_t N, int64_t K, int max_splits, int min_kb,
+                         bool reduce_adds, double min_gain) {
+  const int64_t units = std::max(num_sms / 2, 1), nk = (K + kGemmBK - 1) / kGemmBK;
+  auto fill = [&](int64_t u) { return static_cast<double>(u) / (static_cast<double>((u + units - 1) / units) * units); };
+  const double flops = 2.0 * static_cast<double>(rows) * static_cast<double>(N) * static_cast<double>(K);
+  const double out_bytes = static_cast<double>(rows) * static_cast<double>(N) * 4.0;
+  auto cost = [&](int sp) {
+    const double t = flops / (1.3e15 * fill(tiles * sp));
+    return sp == 1 ? t : t + (sp + (reduce_adds ? 2.0 : 1.0)) * out_bytes / 5e12;
+  };
+  const double base = cost(1);
+  double best = base;
+  int splits = 1;
+  for (int sp = 2; sp <= max_splits; ++sp) {
+    if (nk / sp < min_kb) break;
+    const double c = cost(sp);
+    if (c < best && c < (1.0 - min_gain) * base) {
+      best = c;
+      splits = sp;
+    }
+  }
+  return splits;
+}
+
 void gemm_set_k_splits(GemmArgs& a, int k_splits, int64_t split_stride) {
   a.k_splits = k_splits;
   a.tiles_per_split = a.total_tiles;

@@ -193,6 +193,16 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
 // 256, or for bf16 weights 128 (both kernels) and 64 / 32 (launch_gemm) --
 // the B tensor map's box is tile_n rows, tile_n / 2 for the pair).
 void gemm_finalize_groups(GemmArgs& args, int tile_m = kGemmBM, int tile_n = kGemmBN);
+// K slices for a CTA-pair bf16 GEMM of `tiles` output tiles whose waves of
+// num_sms / 2 pairs are poorly filled: a time model of the tensor work at
+// ~1.3 PFLOP/s scaled by the wave fill, plus the reduce's HBM traffic at
+// ~5 TB/s (S partials read, the output written, and read as well when the
+// reduce adds to it).  Splits only when the model's time drops below
+// (1 - min_gain) of the unsplit one, up to max_splits slices of at least
+// min_kb K blocks; returns 1 otherwise.
+int gemm_choose_k_splits(int64_t tiles, int num_sms, int64_t rows, int64_t N, int64_t K, int max_splits, int min_kb,
+                         bool reduce_adds, double min_gain);
+
 // Turn a finalised kEpiF32 launch into k_splits K slices (see GemmArgs).
 void gemm_set_k_splits(GemmArgs& args, int k_splits, int64_t split_stride);
 

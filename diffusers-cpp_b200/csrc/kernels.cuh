@@ -153,9 +153,10 @@ cudaError_t launch_tile_blend(float* T, const float* above, int64_t ha, const fl
                               int64_t h, int64_t w, int64_t ev, int64_t eh, int64_t keep_h, int64_t keep_w, float* out,
                               int64_t H, int64_t W, int64_t oy, int64_t ox, cudaStream_t s);
 
-// K-split GEMM reduction: out[r, c] += sum_{s < S} ws[s * stride + r * ld_ws + c]
-// (slices summed in order: deterministic), rows x N f32.
+// K-split GEMM reduction: out[r, c] (+)= sum_{s < S} ws[s * stride + r * ld_ws + c]
+// (slices summed in order, then added to out when `add`: deterministic),
+// rows x N f32.
 cudaError_t launch_split_reduce(const float* ws, int S, int64_t stride, int64_t rows, int64_t N, int64_t ld_ws,
-                                float* out, int64_t ld_out, cudaStream_t s);
+                                float* out, int64_t ld_out, cudaStream_t s, bool add);
 
 }  // namespace dcpp

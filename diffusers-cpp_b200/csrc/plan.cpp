@@ -416,27 +416,8 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
         m_tiles += (g.rows + tile_m - 1) / tile_m;
         split_rows = std::max<int64_t>(split_rows, g.orow0 + g.rows);
       }
-      const int64_t units = ctx_.num_sms / 2, tiles = m_tiles * ((N + tile_n - 1) / tile_n);
-      const int64_t nk = (K + kGemmBK - 1) / kGemmBK;
-      auto fill = [&](int64_t u) { return static_cast<double>(u) / (static_cast<double>((u + units - 1) / units) * units); };
-      // Time model: tensor work at ~1.3 PFLOP/s scaled by the wave fill, plus
-      // the reduce's HBM traffic (S partials read, the residual read and
-      // written) at ~5 TB/s; split only for a clear (> 5 %) gain.
-      const double flops = 2.0 * static_cast<double>(split_rows) * N * K;
-      auto cost = [&](int sp) {
-        const double t = flops / (1.3e15 * fill(tiles * sp));
-        return sp == 1 ? t : t + (sp + 2.0) * static_cast<double>(split_rows) * N * 4.0 / 5e12;
-      };
-      double best = cost(1);
-      const double base = best;
-      for (int sp = 2; sp <= 4; ++sp) {
-        if (nk / sp < 16) break;
-        const double c2 = cost(sp);
-        if (c2 < best && c2 < 0.95 * base) {
-          best = c2;
-          splits = sp;
-        }
-      }
+      const int64_t tiles = m_tiles * ((N + tile_n - 1) / tile_n);
+      splits = gemm_choose_k_splits(tiles, ctx_.num_sms, split_rows, N, K, 4, 16, /*reduce_adds=*/true, 0.05);
       const size_t need = static_cast<size_t>(splits) * split_rows * N * 4;
       if (splits > 1 && need > split_ws_bytes_) {
         if (split_ws_) cuda_check(cudaFree(split_ws_), "free split workspace");
@@ -489,7 +470,7 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
       const int64_t ld_out = ep.ld_out, rows = split_rows, n = N, stride = split_rows * N;
       const int sp = splits;
       building_->push_back({[=](cudaStream_t s) {
-                              cuda_check(launch_split_reduce(ws, sp, stride, rows, n, n, out, ld_out, s), "split reduce");
+                              cuda_check(launch_split_reduce(ws, sp, stride, rows, n, n, out, ld_out, s, /*add=*/true), "split reduce");
                             },
                             1, kOpOther, 0.0, tag + " split reduce"});
     }

@@ -762,7 +762,7 @@ cudaError_t launch_add_f32(float* y, const float* a, int64_t n, cudaStream_t s) 
 namespace {
 // out[r, c] += sum over s (in order) of ws[s * stride + r * ld_ws + c].
 __global__ void split_reduce_kernel(const float* __restrict__ ws, int S, int64_t stride, int64_t rows, int64_t n4,
-                                    int64_t ld_ws, float* __restrict__ out, int64_t ld_out) {
+                                    int64_t ld_ws, float* __restrict__ out, int64_t ld_out, bool add) {
   const int64_t total = rows * n4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -773,20 +773,22 @@ __global__ void split_reduce_kernel(const float* __restrict__ ws, int S, int64_t
       acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
     }
     float4* o = reinterpret_cast<float4*>(out + r * ld_out + c);
-    float4 h = *o;
-    h.x += acc.x; h.y += acc.y; h.z += acc.z; h.w += acc.w;
-    *o = h;
+    if (add) {
+      const float4 h = *o;
+      acc.x += h.x; acc.y += h.y; acc.z += h.z; acc.w += h.w;
+    }
+    *o = acc;
   }
 }
 }  // namespace
 
 cudaError_t launch_split_reduce(const float* ws, int S, int64_t stride, int64_t rows, int64_t N, int64_t ld_ws,
-                                float* out, int64_t ld_out, cudaStream_t s) {
+                                float* out, int64_t ld_out, cudaStream_t s, bool add) {
   if (N % 4 || ld_ws % 4 || ld_out % 4 || stride % 4 || S < 1) return cudaErrorInvalidValue;
   const int64_t total = rows * (N / 4);
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
   split_reduce_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, s>>>(ws, S, stride, rows, N / 4,
-                                                                                          ld_ws, out, ld_out);
+                                                                                          ld_ws, out, ld_out, add);
   return cudaGetLastError();
 }
 

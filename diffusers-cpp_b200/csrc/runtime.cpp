@@ -58,6 +58,19 @@ void* Ctx::ensure_scratch(size_t bytes) {
   return scratch;
 }
 
+void* Ctx::ensure_split_ws(size_t bytes) {
+  if (bytes <= split_ws_bytes) return split_ws;
+  if (split_ws) cuda_check(cudaFree(split_ws), "cudaFree(split workspace)");
+  split_ws = nullptr;
+  split_ws_bytes = 0;
+  if (cudaMalloc(&split_ws, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    fail(DCPP_ERR_OOM, "split workspace allocation of " + std::to_string(bytes) + " bytes failed");
+  }
+  split_ws_bytes = bytes;
+  return split_ws;
+}
+
 void PeerBuffer::open(Ctx& ctx, size_t nbytes) {
   if (local) fail(DCPP_ERR_STATE, "peer buffer already open");
   if (!ctx.comm || ctx.nranks < 2 || ctx.nranks > 8) fail(DCPP_ERR_STATE, "peer buffer needs a TP group of 2..8");
@@ -193,10 +206,23 @@ void gemm_op(Ctx& c, int wtype, const void* w, int64_t N, int64_t K, const uint1
   a.ep.ld_out = N;
   a.err = c.d_err;
   gemm_finalize_groups(a, pair ? 256 : kGemmBM);
+  // Few tiles for the 74 CTA pairs (small M): K slices into f32 partials,
+  // then an ordered reduce into y.  Only for a large modelled gain: measured
+  // on the config-5 sweep, modest ones (M 1024, K 9216) did not materialise.
+  int splits = 1;
+  if (pair && N % 4 == 0)
+    splits = gemm_choose_k_splits(a.total_tiles, c.num_sms, M, N, K, 8, 8, /*reduce_adds=*/false, 0.4);
+  if (splits > 1) {
+    a.ep.out_f32 = static_cast<float*>(c.ensure_split_ws(static_cast<size_t>(splits) * M * N * 4));
+    gemm_set_k_splits(a, splits, M * N);
+  }
   if (pair)
     cuda_check(launch_gemm_pair(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm (pair)");
   else
     cuda_check(launch_gemm(ta, tb, tb, a, kBSrcBf16, c.num_sms, c.stream), "launch gemm");
+  if (splits > 1)
+    cuda_check(launch_split_reduce(a.ep.out_f32, splits, M * N, M, N, N, y, N, c.stream, /*add=*/false),
+               "split reduce");
 }
 
 }  // namespace dcpp
@@ -267,6 +293,7 @@ dcpp_status dcpp_destroy(dcpp_ctx* ctx) {
   }
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->split_ws) cudaFree(ctx->split_ws);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;

@@ -52,9 +52,12 @@ struct Ctx {
   // Fault injection (host side only).
   std::string fault_name;
   int fault_countdown = 0;
-  // Scratch for the op-level GEMM (bf16 weights) and staging.
+  // Scratch for the op-level GEMM (bf16 weights) and staging, and the K-split
+  // partials of the op-level GEMM.
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  void* split_ws = nullptr;
+  size_t split_ws_bytes = 0;
   // GEMM kernel choice: 0 auto, 1 single-SM 128 x 256 tiles, 2 CTA-pair
   // 256 x 256 tiles.  Auto takes CTA pairs for bf16 weights and >= 256 rows,
   // and the single-SM kernel for fused dequantisation (measured faster: the
@@ -71,6 +74,7 @@ struct Ctx {
 
   void maybe_inject(const char* entry);
   void* ensure_scratch(size_t bytes);
+  void* ensure_split_ws(size_t bytes);
   // Read and clear the device error word (synchronises the stream).
   void check_device_error();
 };
