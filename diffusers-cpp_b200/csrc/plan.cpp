@@ -234,7 +234,8 @@ void StepPlanner::release_plan_events() {
 }
 
 void StepPlanner::alloc_expansion_scratch(const std::function<void*(size_t)>& alloc, size_t s0, size_t s1) {
-  for (int pi = 0; pi < 2; ++pi) {
+  if (const char* f = getenv("DCPP_EXPAND_AHEAD")) n_scratch_ = std::min(std::max(atoi(f), 2), kMaxScratch);
+  for (int pi = 0; pi < n_scratch_; ++pi) {
     wscratch_[pi][0] = static_cast<uint16_t*>(alloc(std::max<size_t>(s0, 8) * 2));
     wscratch_[pi][1] = static_cast<uint16_t*>(alloc(std::max<size_t>(s1, 8) * 2));
   }
@@ -248,7 +249,7 @@ void StepPlanner::begin_ops(std::vector<Op>& ops) {
   }
   building_ = &ops;
   scratch_pair_ = 0;
-  scratch_free_[0] = scratch_free_[1] = nullptr;
+  for (auto& e : scratch_free_) e = nullptr;
   plan_start_ = plan_event();
   add_record(plan_start_, 0);
   add_wait(plan_start_, 1);  // the side stream joins the plan (and a capture) at its start
@@ -367,7 +368,7 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
   if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
   const bool expand0 = w0->type != kTypeBF16, expand1 = w1 && w1->type != kTypeBF16;
   const int pair_idx = scratch_pair_;
-  if (expand0 || expand1) scratch_pair_ ^= 1;
+  if (expand0 || expand1) scratch_pair_ = (scratch_pair_ + 1) % n_scratch_;
   uint16_t* const* sc = wscratch_[pair_idx];
   const uint16_t* b0 = expand0 ? sc[0] : reinterpret_cast<const uint16_t*>(w0->data);
   const uint16_t* b1 = b0;

@@ -119,9 +119,13 @@ class StepPlanner {
   // bf16 expansion of quantised GEMM weights: two pairs (first / second
   // weight of one launch), used alternately, so that the expansion of the
   // next projection runs on the side stream while the current GEMM computes.
-  uint16_t* wscratch_[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+  // Ring of expansion scratch pairs: a GEMM's weight expansion may start once
+  // the GEMM that used its pair n_scratch_ expanding GEMMs back has finished.
+  static constexpr int kMaxScratch = 3;
+  int n_scratch_ = 2;
+  uint16_t* wscratch_[kMaxScratch][2] = {};
   int scratch_pair_ = 0;
-  cudaEvent_t scratch_free_[2] = {nullptr, nullptr};  // last GEMM that read the pair (null: none yet)
+  cudaEvent_t scratch_free_[kMaxScratch] = {};  // last GEMM that read the pair (null: none yet)
   cudaEvent_t plan_start_ = nullptr;                   // recorded on the main stream first in a plan
   cudaStream_t side_ = nullptr;
   std::vector<cudaEvent_t> plan_events_;
