@@ -131,7 +131,10 @@ dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* d_in, int64_t n, uint16
  * The ggml_mul_mat(W, x) of Linear::forward (src/nn/Linear.cpp:17-36,
  * Runtime.hpp:136 mul_mat).  Runs on the tcgen05/TMEM tensor-core GEMM; a
  * non-bf16 W is first expanded to bf16 (the exact dequantised values rounded
- * once) in a context scratch buffer.  K % 8 == 0; M, N arbitrary. */
+ * once) in a context scratch buffer.  When the output tiles fill the CTA pairs
+ * poorly (few rows, long K) the product is computed in K slices into f32
+ * partials in a second context buffer and summed in slice order into y
+ * (deterministic).  K % 8 == 0; M, N arbitrary. */
 dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
                       const uint16_t* d_x, int64_t M, float* d_y);
 
