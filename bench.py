@@ -451,6 +451,70 @@ def qwen3_flops(c, B, S):
     return c.num_hidden_layers * (lin + attn)
 
 
+def qwen3_cpu_sample(steps, warmup, threads):
+    """Time the Qwen3 CPU restatement (oracle/qwen3_oracle.py, float32) on a
+    bounded sample of one config-4 prefill: the full batch (4 x 512 tokens)
+    through one and through two full-width layers, the difference being one
+    layer, extrapolated to 36 layers.  The embedding table is cut to 4096
+    rows (the gather's cost does not depend on its size).  Returns (seconds
+    per prefill, sample description)."""
+    import torch
+
+    import qwen3_oracle as qo
+    from dcpp_b200 import TYPE_Q8_0, synth
+
+    torch.set_num_threads(threads)
+    full = synth.Qwen3Cfg()
+    sample = synth.Qwen3Cfg(vocab_size=4096, num_hidden_layers=2)
+    params = synth.make_qwen3_params(sample, TYPE_Q8_0, seed=0)
+    o = qo.Qwen3Oracle(qo.Qwen3Config(**{k: getattr(sample, k) for k in qo.Qwen3Config.__dataclass_fields__}),
+                       params, dtype=torch.float32)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, sample.vocab_size, (4, 512), generator=g)
+    o.forward(ids[:, :16], n_layers=2)  # dequantise the weights once (ggml keeps them quantised)
+
+    def one():
+        t0 = time.perf_counter()
+        o.forward(ids, n_layers=1)
+        t1 = time.perf_counter()
+        o.forward(ids, n_layers=2)
+        t2 = time.perf_counter()
+        layer = (t2 - t1) - (t1 - t0)
+        return (t1 - t0) - layer + full.num_hidden_layers * layer
+
+    for _ in range(warmup):
+        one()
+    times = [one() for _ in range(steps)]
+    desc = (f"CPU restatement (oracle/qwen3_oracle.py, torch float32, {threads} threads) of config 4 "
+            f"(4 x 512 tokens): one and two full-width layers timed, extrapolated to "
+            f"{full.num_hidden_layers} layers; ggml CPU path unavailable (submodule not vendored)")
+    return statistics.median(times), desc
+
+
+def run_qwen3_reference(args):
+    """--impl reference --config 4: the CPU restatement's bounded sample of a
+    prefill (qwen3_cpu_sample), at most 3 timed samples after at most 1
+    warm-up (each sample is ~10-20 s of CPU work); rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    steps, warmup = max(1, min(args.steps, 3)), min(args.warmup, 1)
+    sec, desc = qwen3_cpu_sample(steps, warmup, threads)
+    tokens = 4 * 512
+    value = tokens / sec
+    line = {
+        "impl": "reference", "metric": QWEN3_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: Qwen3 text-encoder prefill, Q8_0, batch 4 x 512 tokens",
+                   "global_batch": 4, "seq_len": 512, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_qwen3(args):
     """36 layers, hidden 2560, 32 / 8 heads x 128, SwiGLU
     9728, Q8_0 weights N(0, 0.02); batch 4 x 512 token ids uniform in the
@@ -550,6 +614,11 @@ def run_qwen3(args):
         "clocks": clk,
         "load_seconds": load_s,
     }
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sec, desc = qwen3_cpu_sample(1, 0, threads)
+        line["cpu_baseline"] = {"value": tokens / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": desc}
     print(json.dumps(line), flush=True)
     m.close()
     ctx.close()
@@ -782,8 +851,7 @@ def main():
         args.warmup = 3
     if args.config == "4":
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "config 4 has no CPU reference arm in this bench"}))
-            return 0
+            return run_qwen3_reference(args)
         return run_qwen3(args)
     if args.config == "5":
         if args.impl == "reference":
