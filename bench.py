@@ -53,6 +53,42 @@ CONFIGS = {
 }
 
 
+# DRAM traffic of the step's dominant kernel (gemm_pair_kernel), per launch,
+# averaged over one step's GEMM launches: dram__bytes_read.sum +
+# dram__bytes_write.sum from one ncu capture of this bench's own command
+# (summary and command in the named profile).  Keyed by (config, n_gpus).
+GEMM_TRAFFIC = {}
+
+
+def weight_bytes(cfg, wtype, world):
+    """Weight bytes one GPU moves per step for the block projections
+    (the conditioning GEMVs and embedders are excluded): the algorithmic
+    quantised bytes, and what the default path moves through memory: the
+    quantised read + the bf16 expansion written + the bf16 read back by the
+    GEMM (at least once).  Row-parallel shards that are not on the
+    quantisation blocks are held as bf16 from load and expanded per step by
+    nobody (TP 8 with Q4_K)."""
+    D, F = cfg.inner_dim, cfg.mlp_hidden
+    bpw = {"Q4_K": 144 / 256, "Q8_0": 34 / 32}[wtype]
+    bs = {"Q4_K": 256, "Q8_0": 32}[wtype]
+    Dl, Fl = D // world, F // world
+    col_par = 3 * Dl * D + 2 * Fl * D            # qkv + gate/up rows of this rank, K = D
+    row_dbl = D * Dl + D * Fl                    # to_out (K = Dl) + ff.linear_out (K = Fl)
+    row_sgl = D * (Dl + Fl)                      # single-block fused to_out
+    aligned = Dl % bs == 0 and Fl % bs == 0
+    q_w = cfg.num_layers * 2 * col_par + cfg.num_single_layers * col_par
+    r_w = cfg.num_layers * 2 * row_dbl + cfg.num_single_layers * row_sgl
+    if aligned:
+        q_w += r_w
+        bf16_w = 0
+    else:
+        bf16_w = r_w
+    return {"quantised_weights": q_w, "bf16_weights_held_from_load": bf16_w,
+            "algorithmic_bytes": q_w * bpw + bf16_w * 2,
+            "quantised_read": q_w * bpw, "bf16_expansion_written": q_w * 2, "bf16_gemm_read_min": (q_w + bf16_w) * 2,
+            "moved_bytes_min": q_w * bpw + q_w * 2 + (q_w + bf16_w) * 2}
+
+
 def algorithmic_flops(cfg, batch, n_img, n_txt):
     """FLOPs of one DiT forward: per block 2*S*13*D^2 + 4*S^2*D, embedders,
     batch-1 GEMVs; per batch element."""
@@ -194,6 +230,8 @@ def cpu_sample(cfg_name, steps, warmup, threads):
     # weights; dequantisation is not part of the timed sample).
     orc.forward(hid[:, :64], enc[:, :16], t, iid[:64], tid[:16], n_double=1, n_single=1)
 
+    sample_s = []
+
     def one():
         t0 = time.perf_counter()
         orc.forward(hid, enc, t, iid, tid, n_double=0, n_single=0)
@@ -202,6 +240,7 @@ def cpu_sample(cfg_name, steps, warmup, threads):
         t2 = time.perf_counter()
         orc.forward(hid, enc, t, iid, tid, n_double=0, n_single=1)
         t3 = time.perf_counter()
+        sample_s.append(t3 - t0)
         base = t1 - t0
         dbl = (t2 - t1) - base
         sgl = (t3 - t2) - base
@@ -213,7 +252,7 @@ def cpu_sample(cfg_name, steps, warmup, threads):
     desc = (f"CPU restatement (oracle/flux2_oracle.py, torch float32, {threads} threads) of {spec['workload']}; "
             f"each step = 1 double + 1 single block at full size plus embeddings/output, extrapolated to "
             f"{full.num_layers} + {full.num_single_layers} blocks; ggml CPU path unavailable (submodule not vendored)")
-    return statistics.median(times), desc
+    return statistics.median(times), desc, statistics.median(sample_s[warmup:] or sample_s)
 
 
 def run_reference(args):
@@ -221,11 +260,17 @@ def run_reference(args):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sec, desc = cpu_sample(args.config, args.steps, args.warmup, threads)
+    # Each sample is a few seconds of CPU work: at most 3 timed samples after
+    # at most 1 warm-up keeps the arm within minutes whatever --steps says.
+    steps, warmup = max(1, min(args.steps, 3)), min(args.warmup, 1)
+    sec, desc, sample_sec = cpu_sample(args.config, steps, warmup, threads)
     value = 1.0 / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "extrapolated": True, "sample_seconds": sample_sec,
+        "extrapolation": "ms_per_step is the full step extrapolated from the timed sample (1 double + 1 single "
+                         "block + embeddings/output); each timed sample took sample_seconds of wall time",
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": CONFIGS[args.config]["workload"], "global_batch": CONFIGS[args.config]["batch"],
                    "seq_len": CONFIGS[args.config]["grid"][0] * CONFIGS[args.config]["grid"][1] + CONFIGS[args.config]["n_txt"],
@@ -339,6 +384,35 @@ def run_ours(args):
     e2e_ms = e0.elapsed_time(e1) / args.steps
     barrier()
 
+    # ---- multi-GPU parity: one denoise step of the N-GPU model on fixed inputs
+    # against the same step of an unsharded model on rank 0's GPU (all ranks
+    # run the sharded step; rank 0 then builds the 1-GPU model from the same
+    # seeded weights).
+    tp_parity = None
+    if world > 1:
+        t_par = torch.tensor([sched[1][0]], dtype=torch.float32)
+        tp_out = torch.empty_like(hid).pin_memory()
+        model.denoise_step(hid_p, enc_p, t_par, sched[1][1], iid, tid, tp_out)
+        torch.cuda.synchronize()
+        if rank == 0:
+            solo = dcpp_b200.Flux2Model(ctx, cfg)
+            sp = synth.make_params(cfg, wt, seed=0, device="cuda", to_cpu=False)
+            for name, (gt, shp, data) in sp.items():
+                solo.set_param(name, gt, shp, data.cpu())
+            del sp
+            torch.cuda.empty_cache()
+            solo.prepare(B, ni, nt, use_graph=False)
+            solo_out = torch.empty_like(hid)
+            solo.denoise_step(hid_p, enc_p, t_par, sched[1][1], iid, tid, solo_out)
+            torch.cuda.synchronize()
+            solo.close()
+            torch.cuda.empty_cache()
+            d = tp_out.double() - solo_out.double()
+            tp_parity = {"rel_l2": (d.norm() / solo_out.double().norm()).item(), "max_abs": d.abs().max().item(),
+                         "against": "the same denoise step (sigma %.2f) on an unsharded 1-GPU model, same seeded "
+                                    "weights and inputs" % sched[1][0]}
+        barrier()
+
     # ---- per-kernel-kind device times: the same step replayed eagerly with a
     # CUDA event pair around every launch (not inside the graph, whose event
     # nodes would perturb the timing).
@@ -364,6 +438,7 @@ def run_ours(args):
 
     if rank == 0:
         peak_b, peak_s, hbm, peak_src = measured_peaks()
+        traffic = GEMM_TRAFFIC.get((args.config, world), {})
         g_ms, g_fl, g_n = prof["gemm"]
         achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else 0.0
         step_flops = algorithmic_flops(cfg, B, ni, nt)
@@ -392,6 +467,13 @@ def run_ours(args):
                 "cuda_graph": not args.no_graph,
                 "dequant": ("fused into the GEMM" if os.environ.get("DCPP_FUSED_DEQUANT") == "1"
                             else "per-projection expansion to bf16 before each GEMM"),
+                "row_parallel_weights": (None if world == 1 else
+                                         "bf16, expanded once at load (row-parallel shards of %d / %d columns are "
+                                         "not on the %s blocks), not expanded per step" % (
+                                             cfg.inner_dim // world, cfg.mlp_hidden // world, spec["wtype"])
+                                         if weight_bytes(cfg, spec["wtype"], world)["bf16_weights_held_from_load"]
+                                         else "%s, expanded to bf16 per step like the column-parallel ones"
+                                         % spec["wtype"]),
                 "tp_exchange": (None if world == 1 else
                                 "ncclAllReduce of the row-parallel partials" if os.environ.get("DCPP_TP_COMM") == "nccl"
                                 else "GEMM epilogue stores partials into the owner GPU (NVLink peer memory); "
@@ -400,20 +482,27 @@ def run_ours(args):
             "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "dcpp_flux2_denoise_step with pinned host latents/encoder/ids in, latents out"},
             "gpu_launches": launches * args.steps,
+            "tp_parity_rel": tp_parity["rel_l2"] if tp_parity else None,
+            "tp_parity": tp_parity,
             "roofline": {
                 "bound": "tensor",
-                "kernel": "gemm_bf16_kernel (tcgen05 grouped GEMM)",
+                "kernel": "gemm_pair_kernel<0, 256> (bf16 B operand, 256 x 256 tiles; persistent tcgen05 "
+                          "cta_group::2 grouped GEMM)",
                 "achieved": achieved,
                 "peak": peak_s,
                 "unit": "TFLOP/s",
                 "frac": achieved / peak_s if peak_s else None,
                 "peak_kind": f"bf16 sustained ({peak_src})",
-                "traffic": None,
+                "traffic": traffic.get("dram_bytes_per_launch"),
+                "traffic_source": traffic.get("source"),
+                "algorithmic_bytes_per_launch": traffic.get("algorithmic_bytes_per_launch"),
                 "gemm_ms_per_step": g_ms,
                 "gemm_launches_per_step": g_n,
                 "step_tflops": step_flops / 1e12,
-                "step_frac_of_peak": step_flops / (ms * 1e-3) / 1e12 / peak_s,
+                "step_frac_of_peak": step_flops / (ms * 1e-3) / 1e12 / (world * peak_s),
+                "step_frac_of_peak_note": "whole-job FLOP/s over n_gpus x the per-GPU peak",
             },
+            "weight_bytes_per_step": weight_bytes(cfg, spec["wtype"], world),
             "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
             "kernel_ms_sum": prof_step_ms,
             "kernel_timing": "eager replay of one step, CUDA events around each launch on the launching stream",
@@ -425,9 +514,9 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             try:
                 threads = os.cpu_count() or 1
-                sec, desc = cpu_sample(args.config, 1, 0, threads)
+                sec, desc, sample_sec = cpu_sample(args.config, 1, 0, threads)
                 line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "steps/s", "cores": threads, "kind": "port",
-                                        "sample": desc}
+                                        "sample": desc, "extrapolated": True, "sample_seconds": sample_sec}
             except Exception as e:  # the baseline is reported, never the target
                 line["cpu_baseline"] = {"value": None, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
                                         "sample": f"failed: {e}"}

@@ -531,20 +531,23 @@ void Flux2Transformer2DModel::free_plan() {
   planned_ = false;
 }
 
-void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph) {
+void Flux2Transformer2DModel::prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph, int64_t n_ref) {
   require_device("prepare");
   auto miss = missing();
   if (!miss.empty()) fail(DCPP_ERR_STATE, "parameters not set: " + miss.front() + " (+" + std::to_string(miss.size() - 1) + " more)");
   if (batch < 1 || batch > 4) fail(DCPP_ERR_UNSUPPORTED, "batch must be 1..4");
   if (n_img < 1 || n_txt < 1) fail(DCPP_ERR_INVALID_ARG, "token counts must be positive");
-  if ((batch * (n_img + n_txt)) > (1 << 24)) fail(DCPP_ERR_UNSUPPORTED, "too many tokens");
-  if (planned_ && batch == B_ && n_img == Ni_ && n_txt == Nt_ && use_graph == use_graph_) return;
+  if (n_ref < 0) fail(DCPP_ERR_INVALID_ARG, "the reference token count must not be negative");
+  if ((batch * (n_img + n_ref + n_txt)) > (1 << 24)) fail(DCPP_ERR_UNSUPPORTED, "too many tokens");
+  if (planned_ && batch == B_ && n_img == Nl_ && n_ref == Nr_ && n_txt == Nt_ && use_graph == use_graph_) return;
   cudaStreamSynchronize(ctx_.stream);
   free_plan();
   B_ = batch;
-  Ni_ = n_img;
+  Nl_ = n_img;
+  Nr_ = n_ref;
+  Ni_ = n_img + n_ref;
   Nt_ = n_txt;
-  S_ = n_img + n_txt;
+  S_ = Ni_ + n_txt;
   use_graph_ = use_graph;
   build_plan();
   planned_ = true;
@@ -574,13 +577,14 @@ void Flux2Transformer2DModel::add_tp_barrier(int set, int stream) {
   a.err = ctx_.d_err;
   a.rank = rank_;
   a.nranks = nranks_;
+  a.timeout_ns = ctx_.wait_timeout_ns;
   Op o{[a](cudaStream_t s) { cuda_check(launch_tp_barrier(a, s), "tp barrier"); }, 1, kOpAllreduce, 0.0, "tp_barrier"};
   o.stream = stream;
   building_->push_back(o);
 }
 
 void Flux2Transformer2DModel::build_plan() {
-  const int64_t B = B_, S = S_, Ni = Ni_, Nt = Nt_, D = D_, Dl = Dl_, Fl = Fl_, Hl = Hl_;
+  const int64_t B = B_, S = S_, Ni = Ni_, Nt = Nt_, Nl = Nl_, D = D_, Dl = Dl_, Fl = Fl_, Hl = Hl_;
   const int64_t R = B * S;
   const int64_t ldc = Dl + Fl;
   const int64_t in_ch = cfg_.in_channels, jd = cfg_.joint_attention_dim, out_ch = cfg_.out_ch();
@@ -707,8 +711,10 @@ void Flux2Transformer2DModel::build_plan() {
     }
     return g;
   };
+  // img_only: only the first img_rows image tokens of each batch element
+  // (norm_out), written to rows b * Ni of y.
   auto norm_args = [&](const float* const* mods, int64_t mod_stride, int64_t shift_off, int64_t scale_off,
-                       bool img_only, uint16_t* y, int64_t dst_ld, const float* resid) {
+                       bool img_only, uint16_t* y, int64_t dst_ld, const float* resid, int64_t img_rows) {
     NormArgs n{};
     n.x = h_;
     n.x_out = h_;
@@ -727,7 +733,8 @@ void Flux2Transformer2DModel::build_plan() {
       }
       const float* m = mods[1] + b * mod_stride;
       const int32_t dst = img_only ? static_cast<int32_t>(b * Ni) : static_cast<int32_t>(b * S + Nt);
-      n.seg[k++] = {static_cast<int32_t>(b * S + Nt), dst, static_cast<int32_t>(Ni), m + shift_off, m + scale_off};
+      n.seg[k++] = {static_cast<int32_t>(b * S + Nt), dst, static_cast<int32_t>(img_only ? img_rows : Ni), m + shift_off,
+                    m + scale_off};
     }
     n.n_segments = k;
     return n;
@@ -736,7 +743,7 @@ void Flux2Transformer2DModel::build_plan() {
   auto build_ops = [&](std::vector<Op>& ops, float* lat_in, float* lat_out, bool euler) {
     begin_ops(ops);
     // 1. timestep (and guidance) embedding, modulation vectors
-    //    (Flux2Transformer2DModel.cpp:199-214).
+    //    (Flux2Transformer2DModel.cpp:130-145).
     ops.push_back({[=](cudaStream_t s) {
                      cuda_check(launch_timestep_proj(t_dev_, static_cast<int>(B), static_cast<int>(tg), 1000.0f, tproj_, s),
                                 "timestep_proj");
@@ -785,7 +792,7 @@ void Flux2Transformer2DModel::build_plan() {
       add_gemm("x_embedder", xb_, in_ch, in_ch, &x_embed_, nullptr, gi, e, D);
       add_gemm("context_embedder", eb_, jd, jd, &ctx_embed_, nullptr, gt, e, D);
     }
-    // 3. rotary table from cat(txt_ids, img_ids) (Flux2Transformer2DModel.cpp:233-238).
+    // 3. rotary table from cat(txt_ids, img_ids) (Flux2Transformer2DModel.cpp:164-169).
     ops.push_back({[=](cudaStream_t s) {
                      cuda_check(launch_rope_table(ids_dev_, S, n_axes, axes.data(), theta, rope_, s), "rope_table");
                    },
@@ -946,7 +953,7 @@ void Flux2Transformer2DModel::build_plan() {
       e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
-      norm_gemm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, nullptr), true, stream_groups(true),
+      norm_gemm(norm_args(mods_dbl, 6 * D, 0, D, false, a_, D, nullptr, Ni), true, stream_groups(true),
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], pcs, e, 3 * Dl, hook);
                 });
@@ -956,7 +963,7 @@ void Flux2Transformer2DModel::build_plan() {
       site();
       EpilogueArgs f = e;
       f.qkv_cols = 0;
-      norm_gemm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, nullptr), true, stream_groups(true),
+      norm_gemm(norm_args(mods_dbl, 6 * D, 3 * D, 4 * D, false, a_, D, nullptr, Ni), true, stream_groups(true),
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("ff_in", a_, D, D, &blk.ff_in[0], &blk.ff_in[1], pcs, f, 2 * Fl, hook);
                 });
@@ -983,7 +990,7 @@ void Flux2Transformer2DModel::build_plan() {
       e.vt_stride = sp;
       e.mlp_out = cat_ + Dl;
       e.ld_mlp = ldc;
-      norm_gemm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, nullptr), true, stream_groups(false),
+      norm_gemm(norm_args(mods_s, 3 * D, 0, D, false, a_, D, nullptr, Ni), true, stream_groups(false),
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, pcs, e, 3 * Dl + 2 * Fl, hook);
                 });
@@ -993,13 +1000,16 @@ void Flux2Transformer2DModel::build_plan() {
       site();
     }
     // 6. drop text tokens, norm_out (scale first, then shift; AdaLayerNormContinuous.inl:26-43), proj_out.
+    //    The denoise step also drops the reference tokens: only the Nl latent
+    //    tokens of each batch element are integrated (Flux2KleinPipeline.cpp:531-536).
     const float* mods_o[2] = {mod_o_v_, mod_o_v_};
     {
+      const int64_t out_rows = euler ? Nl : Ni;
       std::vector<GemmGroup> g;
       for (int64_t b = 0; b < B; ++b) {
         GemmGroup gg{};
         gg.row0 = gg.orow0 = static_cast<int32_t>(b * Ni);
-        gg.rows = static_cast<int32_t>(Ni);
+        gg.rows = static_cast<int32_t>(out_rows);
         gg.batch = static_cast<int32_t>(b);
         g.push_back(gg);
       }
@@ -1014,7 +1024,7 @@ void Flux2Transformer2DModel::build_plan() {
         e.mode = kEpiF32;
         e.out_f32 = lat_out;
       }
-      norm_gemm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, nullptr), false, g,
+      norm_gemm(norm_args(mods_o, 2 * D, D, 0, true, a_, D, nullptr, out_rows), false, g,
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("proj_out", a_, D, D, &proj_out_, nullptr, pcs, e, out_ch, hook);
                 });
@@ -1067,27 +1077,72 @@ void Flux2Transformer2DModel::forward(const float* hidden, const float* encoder,
   ctx_.check_device_error();
 }
 
-void Flux2Transformer2DModel::denoise(const float* latents, const float* encoder, const float* timestep, float dt,
-                                      const int32_t* img_ids, const int32_t* txt_ids, float* latents_out) {
+void Flux2Transformer2DModel::copy_latents(const float* latents, int buf) {
+  const size_t C = static_cast<size_t>(cfg_.in_channels) * 4;
+  cuda_check(cudaMemcpy2DAsync(lat_[buf], Ni_ * C, latents, Nl_ * C, Nl_ * C, B_, cudaMemcpyDefault, ctx_.stream),
+             "copy latents");
+}
+
+void Flux2Transformer2DModel::copy_ref(const float* ref_latents, const int32_t* ref_ids) {
+  if (Nr_ == 0) return;
+  const size_t C = static_cast<size_t>(cfg_.in_channels) * 4;
+  for (int k = 0; k < 2; ++k)
+    cuda_check(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(lat_[k]) + Nl_ * C, Ni_ * C, ref_latents, Nr_ * C, Nr_ * C,
+                                 B_, cudaMemcpyDefault, ctx_.stream),
+               "copy reference latents");
+  const size_t na = cfg_.axes_dims_rope.size();
+  cuda_check(cudaMemcpyAsync(ids_dev_ + (Nt_ + Nl_) * na, ref_ids, Nr_ * na * 4, cudaMemcpyDefault, ctx_.stream),
+             "copy reference ids");
+}
+
+void Flux2Transformer2DModel::copy_latents_out(float* out, int buf) {
+  const size_t C = static_cast<size_t>(cfg_.in_channels) * 4;
+  cuda_check(cudaMemcpy2DAsync(out, Nl_ * C, lat_[buf], Ni_ * C, Nl_ * C, B_, cudaMemcpyDefault, ctx_.stream),
+             "copy latents");
+}
+
+void Flux2Transformer2DModel::check_ref_args(const float* ref_latents, const int32_t* ref_ids, const char* what) const {
+  if (Nr_ > 0 && (!ref_latents || !ref_ids))
+    fail(DCPP_ERR_INVALID_ARG, std::string(what) + ": the plan has " + std::to_string(Nr_) +
+                                   " reference tokens, so image_latents and image_latent_ids are required");
+  if (Nr_ == 0 && (ref_latents || ref_ids))
+    fail(DCPP_ERR_INVALID_ARG, std::string(what) + ": reference latents given but the plan has no reference tokens "
+                                                   "(prepare with n_ref > 0)");
+}
+
+void Flux2Transformer2DModel::denoise(const float* latents, const float* ref_latents, const int32_t* ref_ids,
+                                      const float* encoder, const float* timestep, float dt, const int32_t* img_ids,
+                                      const int32_t* txt_ids, float* latents_out) {
   if (!planned_) fail(DCPP_ERR_STATE, "denoise before prepare");
   if (step_ops_[0].empty()) fail(DCPP_ERR_UNSUPPORTED, "denoise needs out_channels == in_channels");
   if (cfg_.guidance_embeds) fail(DCPP_ERR_UNSUPPORTED, "denoise passes no guidance (Flux2KleinPipeline.cpp:527)");
   if (!latents || !encoder || !timestep || !img_ids || !txt_ids || !latents_out)
     fail(DCPP_ERR_INVALID_ARG, "denoise: null input");
+  check_ref_args(ref_latents, ref_ids, "denoise");
   cur_ = 0;
-  copy_inputs(latents, encoder, timestep, img_ids, txt_ids, nullptr);
+  copy_latents(latents, 0);
+  copy_ref(ref_latents, ref_ids);
+  const size_t na = cfg_.axes_dims_rope.size();
+  copy_inputs(nullptr, encoder, timestep, nullptr, txt_ids, nullptr);
+  cuda_check(cudaMemcpyAsync(ids_dev_ + Nt_ * na, img_ids, Nl_ * na * 4, cudaMemcpyDefault, ctx_.stream), "copy img_ids");
   cuda_check(cudaMemcpyAsync(dt_dev_, &dt, 4, cudaMemcpyHostToDevice, ctx_.stream), "copy dt");
   run_ops(step_ops_[0], &graph_step_[0]);
-  cuda_check(cudaMemcpyAsync(latents_out, lat_[1], B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, ctx_.stream),
-             "copy latents");
+  copy_latents_out(latents_out, 1);
   ctx_.check_device_error();
 }
 
-void Flux2Transformer2DModel::load_inputs(const float* latents, const float* encoder, const int32_t* img_ids,
-                                          const int32_t* txt_ids) {
+void Flux2Transformer2DModel::load_inputs(const float* latents, const float* ref_latents, const int32_t* ref_ids,
+                                          const float* encoder, const int32_t* img_ids, const int32_t* txt_ids) {
   if (!planned_) fail(DCPP_ERR_STATE, "load_inputs before prepare");
+  check_ref_args(ref_latents, ref_ids, "load_inputs");
   cur_ = 0;
-  copy_inputs(latents, encoder, nullptr, img_ids, txt_ids, nullptr);
+  if (latents) copy_latents(latents, 0);
+  copy_ref(ref_latents, ref_ids);
+  const size_t na = cfg_.axes_dims_rope.size();
+  copy_inputs(nullptr, encoder, nullptr, nullptr, txt_ids, nullptr);
+  if (img_ids)
+    cuda_check(cudaMemcpyAsync(ids_dev_ + Nt_ * na, img_ids, Nl_ * na * 4, cudaMemcpyDefault, ctx_.stream),
+               "copy img_ids");
 }
 
 void Flux2Transformer2DModel::set_timestep(float timestep, float dt) {
@@ -1116,8 +1171,7 @@ void Flux2Transformer2DModel::set_profiling(bool on) {
 
 void Flux2Transformer2DModel::read_latents(float* out) {
   if (!planned_) fail(DCPP_ERR_STATE, "read_latents before prepare");
-  cuda_check(cudaMemcpyAsync(out, lat_[cur_], B_ * Ni_ * cfg_.in_channels * 4, cudaMemcpyDefault, ctx_.stream),
-             "copy latents");
+  copy_latents_out(out, cur_);
   ctx_.check_device_error();
 }
 
@@ -1266,14 +1320,37 @@ dcpp_status dcpp_flux2_denoise_step(dcpp_flux2* m, const float* latents_in, cons
                                     const float* timestep, float dt, const int32_t* img_ids, const int32_t* txt_ids,
                                     float* latents_out) {
   return model_call(m, "dcpp_flux2_denoise_step", [&](dcpp::Flux2Transformer2DModel& mm) {
-    mm.denoise(latents_in, encoder, timestep, dt, img_ids, txt_ids, latents_out);
+    mm.denoise(latents_in, nullptr, nullptr, encoder, timestep, dt, img_ids, txt_ids, latents_out);
+  });
+}
+
+dcpp_status dcpp_flux2_prepare_ref(dcpp_flux2* m, int64_t batch, int64_t n_img, int64_t n_ref, int64_t n_txt,
+                                   int use_graph) {
+  return model_call(m, "dcpp_flux2_prepare_ref", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.prepare(batch, n_img, n_txt, use_graph != 0, n_ref);
+  });
+}
+
+dcpp_status dcpp_flux2_denoise_step_ref(dcpp_flux2* m, const float* latents_in, const float* image_latents,
+                                        const int32_t* image_latent_ids, const float* encoder, const float* timestep,
+                                        float dt, const int32_t* img_ids, const int32_t* txt_ids, float* latents_out) {
+  return model_call(m, "dcpp_flux2_denoise_step_ref", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.denoise(latents_in, image_latents, image_latent_ids, encoder, timestep, dt, img_ids, txt_ids, latents_out);
+  });
+}
+
+dcpp_status dcpp_flux2_load_inputs_ref(dcpp_flux2* m, const float* latents, const float* image_latents,
+                                       const int32_t* image_latent_ids, const float* encoder, const int32_t* img_ids,
+                                       const int32_t* txt_ids) {
+  return model_call(m, "dcpp_flux2_load_inputs_ref", [&](dcpp::Flux2Transformer2DModel& mm) {
+    mm.load_inputs(latents, image_latents, image_latent_ids, encoder, img_ids, txt_ids);
   });
 }
 
 dcpp_status dcpp_flux2_load_inputs(dcpp_flux2* m, const float* latents, const float* encoder, const int32_t* img_ids,
                                    const int32_t* txt_ids) {
   return model_call(m, "dcpp_flux2_load_inputs", [&](dcpp::Flux2Transformer2DModel& mm) {
-    mm.load_inputs(latents, encoder, img_ids, txt_ids);
+    mm.load_inputs(latents, nullptr, nullptr, encoder, img_ids, txt_ids);
   });
 }
 

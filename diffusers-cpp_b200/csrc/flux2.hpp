@@ -1,7 +1,7 @@
 // C++ host API of the Flux2 DiT denoise step.  Mirrors the reference's
 // module and pipeline surface:
-//   Flux2Transformer2DModel::Config / from_file  (Flux2Transformer2DModel.hpp:10-31, .cpp:322-353)
-//   Flux2Transformer2DModel::forward             (Flux2Transformer2DModel.cpp:180-300)
+//   Flux2Transformer2DModel::Config / from_file  (Flux2Transformer2DModel.hpp:10-31, .cpp:253-284)
+//   Flux2Transformer2DModel::forward             (Flux2Transformer2DModel.cpp:111-231)
 //   Flux2KleinPipeline::denoise                  (Flux2KleinPipeline.cpp:496-537)
 //   FlowMatchEulerDiscreteScheduler::schedule / integrate (FlowMatchEulerDiscreteScheduler.cpp:68-222)
 // Parameters bind by their GGUF names (module paths, ModulePath.hpp) as the
@@ -73,19 +73,28 @@ class Flux2Transformer2DModel : public StepPlanner {
   void read_param(const std::string& name, int* type, int64_t* rows, int64_t* cols, void* dst, size_t cap,
                   size_t* nbytes);
 
-  // Plan buffers / tensor maps / graph for B x (n_img + n_txt) tokens.
-  void prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph);
+  // Plan buffers / tensor maps / graph for B x (n_img + n_ref + n_txt)
+  // tokens.  n_ref reference-image tokens (img2img / edit) follow the n_img
+  // latent tokens in the image stream (Flux2KleinPipeline.cpp:511-519); the
+  // denoise step integrates only the latent tokens (:531-536).
+  void prepare(int64_t batch, int64_t n_img, int64_t n_txt, bool use_graph, int64_t n_ref = 0);
 
-  // forward(): output = noise prediction.  denoise(): output = latents + dt * v.
+  // forward(): output = noise prediction of every image token (hidden and
+  // img_ids cover the n_img + n_ref image tokens, as the reference's forward
+  // receives them).  denoise(): output = latents + dt * v over the n_img
+  // latent tokens; ref_latents [B, n_ref, C] / ref_ids [n_ref, n_axes] are
+  // the reference tokens (null when the plan has none).
   void forward(const float* hidden, const float* encoder, const float* timestep, const int32_t* img_ids,
                const int32_t* txt_ids, const float* guidance, float* out);
-  void denoise(const float* latents, const float* encoder, const float* timestep, float dt,
-               const int32_t* img_ids, const int32_t* txt_ids, float* latents_out);
+  void denoise(const float* latents, const float* ref_latents, const int32_t* ref_ids, const float* encoder,
+               const float* timestep, float dt, const int32_t* img_ids, const int32_t* txt_ids, float* latents_out);
 
   // Resident execution (inputs already in the model's device buffers):
   // load the inputs once, then run steps; each run integrates the latent
-  // in place (ping-pong) so repeated runs follow a schedule.
-  void load_inputs(const float* latents, const float* encoder, const int32_t* img_ids, const int32_t* txt_ids);
+  // in place (ping-pong) so repeated runs follow a schedule.  Reference
+  // tokens are loaded into both latent buffers and never integrated.
+  void load_inputs(const float* latents, const float* ref_latents, const int32_t* ref_ids, const float* encoder,
+                   const int32_t* img_ids, const int32_t* txt_ids);
   void set_timestep(float timestep, float dt);
   void run_resident_step();
   void read_latents(float* out);
@@ -116,6 +125,13 @@ class Flux2Transformer2DModel : public StepPlanner {
   void build_plan();
   void copy_inputs(const float* hidden, const float* encoder, const float* timestep, const int32_t* img_ids,
                    const int32_t* txt_ids, const float* guidance);
+  // Latent tokens [B, Nl, C] into latent buffer `buf` (rows strided by the
+  // Ni image tokens), reference tokens [B, Nr, C] into both buffers, their
+  // ids after the latent tokens' ids.
+  void copy_latents(const float* latents, int buf);
+  void copy_ref(const float* ref_latents, const int32_t* ref_ids);
+  void copy_latents_out(float* out, int buf);
+  void check_ref_args(const float* ref_latents, const int32_t* ref_ids, const char* what) const;
 
   // Plan helpers (tensor parallelism).
   void add_allreduce(float* buf, int64_t count);
@@ -137,7 +153,8 @@ class Flux2Transformer2DModel : public StepPlanner {
   std::vector<DevVector*> vectors_;
 
   // Plan state.
-  int64_t B_ = 0, Ni_ = 0, Nt_ = 0, S_ = 0;
+  // Ni_ image tokens per batch element = Nl_ latent tokens + Nr_ reference tokens.
+  int64_t B_ = 0, Ni_ = 0, Nt_ = 0, S_ = 0, Nl_ = 0, Nr_ = 0;
   bool planned_ = false;
   bool guidance_given_ = false;
   std::vector<void*> allocs_;

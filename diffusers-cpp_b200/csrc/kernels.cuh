@@ -84,6 +84,7 @@ struct TpBarrierArgs {
   int* err;
   int32_t rank;
   int32_t nranks;
+  uint64_t timeout_ns;  // wait limit; 0 = the library default (1 s)
 };
 cudaError_t launch_tp_barrier(const TpBarrierArgs& a, cudaStream_t s);
 

@@ -19,7 +19,10 @@
 // start at zero.  Calls whose GPU work overlaps (two streams, or two
 // contexts on one device) race on the array and must be serialised by the
 // caller.
+#include <cuda.h>
+
 #include <mutex>
+#include <vector>
 
 #include "gemm.cuh"
 #include "kernels.cuh"
@@ -32,28 +35,54 @@ size_t row_bytes_of(int type, int64_t n);
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
-constexpr int kMaxDevices = 64;
 
 // Device-side scratch.  In host code this name is only a stand-in for the
 // symbol: its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
+// Device address of the scratch, looked up once per CUDA context: keyed on
+// the current context (not the device id), so a context that the host
+// destroys and re-creates (cudaDeviceReset, primary-context release) gets
+// its own lookup instead of a stale address.
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+  CUcontext cu_ctx;
+  void* addr;
+};
+std::vector<ScratchAddr> g_scratch_addrs;
 
-// Device address of the scratch on `device` (which must be current).  The
-// first call on a device looks it up once; later calls reuse it.
-void* noalloc_scratch(int device) {
-  if (device < 0 || device >= kMaxDevices) fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm_noalloc: device id out of range");
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[device]) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CUcontext current_cu_context() {
+  static CtxGetCurrentFn fn = [] {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      fail(DCPP_ERR_CUDA, std::string("dcpp_gemm_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
-    g_scratch_addr[device] = p;
-  }
-  return g_scratch_addr[device];
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  if (!fn) fail(DCPP_ERR_CUDA, "dcpp_gemm_noalloc: cuCtxGetCurrent is unavailable");
+  CUcontext c = nullptr;
+  if (fn(&c) != CUDA_SUCCESS || !c) fail(DCPP_ERR_CUDA, "dcpp_gemm_noalloc: no current CUDA context");
+  return c;
+}
+
+// Device address of the scratch in the current context (the caller made
+// the context's device current and the runtime initialised it).  The first
+// call in a context looks it up with cudaGetSymbolAddress; later calls
+// reuse it.
+void* noalloc_scratch() {
+  const CUcontext cu = current_cu_context();
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  for (const auto& e : g_scratch_addrs)
+    if (e.cu_ctx == cu) return e.addr;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    fail(DCPP_ERR_CUDA, std::string("dcpp_gemm_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+  g_scratch_addrs.push_back({cu, p});
+  return p;
 }
 
 void gemm_chunk(Ctx& c, const uint16_t* wb, int64_t rows, int64_t K, const uint16_t* x, int64_t M, float* y,
@@ -89,7 +118,7 @@ void gemm_noalloc(Ctx& c, int wtype, const void* w, int64_t N, int64_t K, const 
   if (max_rows < kGemmBN)
     fail(DCPP_ERR_UNSUPPORTED, "dcpp_gemm_noalloc: K = " + std::to_string(K) +
                                    " exceeds the allocation-free scratch (32 MiB holds 256 bf16 rows of K <= 65536)");
-  uint16_t* scratch = static_cast<uint16_t*>(noalloc_scratch(c.device));
+  uint16_t* scratch = static_cast<uint16_t*>(noalloc_scratch());
   const uint8_t* wbytes = static_cast<const uint8_t*>(w);
   for (int64_t n0 = 0; n0 < N; n0 += max_rows) {
     const int64_t rows = std::min(max_rows, N - n0);

@@ -420,15 +420,16 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
       const int64_t tiles = m_tiles * ((N + tile_n - 1) / tile_n);
       splits = gemm_choose_k_splits(tiles, ctx_.num_sms, split_rows, N, K, 4, 16, /*reduce_adds=*/true, 0.05);
       const size_t need = static_cast<size_t>(splits) * split_rows * N * 4;
-      if (splits > 1 && need > split_ws_bytes_) {
+      // Ops built earlier hold the workspace pointer: it may be replaced by
+      // a larger one only while no split launch refers to it.  Otherwise
+      // this GEMM runs unsplit.
+      if (splits > 1 && need > split_ws_bytes_ && split_launches_ == 0) {
         if (split_ws_) cuda_check(cudaFree(split_ws_), "free split workspace");
         split_ws_ = nullptr;
         split_ws_bytes_ = 0;
-        // Plans built earlier keep the old pointer: only grow before any split launch exists.
-        if (split_launches_ == 0) {
-          cuda_check(cudaMalloc(&split_ws_, std::max<size_t>(need, size_t(64) << 20)), "split workspace");
-          split_ws_bytes_ = std::max<size_t>(need, size_t(64) << 20);
-        }
+        const size_t bytes = std::max<size_t>(need, size_t(64) << 20);
+        cuda_check(cudaMalloc(&split_ws_, bytes), "split workspace");
+        split_ws_bytes_ = bytes;
       }
       if (splits > 1 && need > split_ws_bytes_) splits = 1;
     }

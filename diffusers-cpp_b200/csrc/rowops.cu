@@ -169,12 +169,13 @@ __global__ void tp_barrier_kernel(const __grid_constant__ TpBarrierArgs a) {
     __threadfence_system();
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[j] + a.rank), "r"(ep) : "memory");
     const uint32_t* mine = a.flags[a.rank] + j;
+    const unsigned long long limit = a.timeout_ns ? a.timeout_ns : kWaitTimeoutNs;
     const unsigned long long t0 = globaltimer();
     while (true) {
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if (static_cast<int32_t>(v - ep) >= 0) break;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > limit) {
         atomicCAS(a.err, 0, kDevTimeoutPeer);
         break;
       }

@@ -401,6 +401,41 @@ dcpp_status dcpp_set_attention_kernel(dcpp_ctx* ctx, int kind) {
   });
 }
 
+dcpp_status dcpp_set_wait_timeout(dcpp_ctx* ctx, double seconds) {
+  return guarded(ctx, "dcpp_set_wait_timeout", [&] {
+    if (!(seconds == 0.0 || (seconds >= 1e-3 && seconds <= 60.0)))
+      dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_set_wait_timeout: 0 (default) or 0.001 .. 60 seconds");
+    ctx->wait_timeout_ns = static_cast<uint64_t>(seconds * 1e9);
+  });
+}
+
+dcpp_status dcpp_tp_barrier_selftest(dcpp_ctx* ctx, int nranks, uint32_t arrived_mask) {
+  return guarded(ctx, "dcpp_tp_barrier_selftest", [&] {
+    if (nranks < 1 || nranks > 8) dcpp::fail(DCPP_ERR_INVALID_ARG, "dcpp_tp_barrier_selftest: nranks must be 1..8");
+    // One 32-word flag array per emulated rank, then the epoch counter.
+    uint32_t* buf = nullptr;
+    const size_t words = 32 * 8 + 32;
+    dcpp::cuda_check(cudaMalloc(&buf, words * 4), "dcpp_tp_barrier_selftest: cudaMalloc");
+    std::vector<uint32_t> init(words, 0u);
+    // Rank j that "arrived" has already stored epoch 1 into rank 0's array.
+    for (int j = 1; j < nranks; ++j)
+      if (arrived_mask & (1u << j)) init[j] = 1u;
+    dcpp::TpBarrierArgs a{};
+    for (int j = 0; j < nranks; ++j) a.flags[j] = buf + 32 * j;
+    a.epoch = buf + 32 * 8;
+    a.err = ctx->d_err;
+    a.rank = 0;
+    a.nranks = nranks;
+    a.timeout_ns = ctx->wait_timeout_ns;
+    cudaError_t e = cudaMemcpyAsync(buf, init.data(), words * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = dcpp::launch_tp_barrier(a, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(buf);
+    dcpp::cuda_check(e, "dcpp_tp_barrier_selftest");
+    ctx->check_device_error();
+  });
+}
+
 dcpp_status dcpp_packed_bytes(int type, int64_t N, int64_t K, size_t* out) {
   if (!out || N <= 0 || K <= 0) return DCPP_ERR_INVALID_ARG;
   if ((type != DCPP_TYPE_Q4_K && type != DCPP_TYPE_Q8_0) || (type == DCPP_TYPE_Q4_K && K % 256) || K % 64)

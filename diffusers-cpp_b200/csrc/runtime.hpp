@@ -64,6 +64,9 @@ struct Ctx {
   // pair kernel is bound by shared-memory bandwidth once B is written there).
   int gemm_kernel = 0;
   int attn_kernel = 0;  // 0 auto, 1 one query tile per CTA, 2 two tiles
+  // Limit of the cross-GPU barrier waits of plans prepared afterwards
+  // (dcpp_set_wait_timeout); 0 = the library default of 1 s.
+  uint64_t wait_timeout_ns = 0;
   bool use_pair(int64_t rows, bool fused_dequant = false) const {
     return gemm_kernel == 2 || (gemm_kernel == 0 && rows >= 256 && !fused_dequant);
   }

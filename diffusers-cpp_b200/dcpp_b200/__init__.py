@@ -109,6 +109,8 @@ _SIGNATURES = {
     "dcpp_inject_fault": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_int]),
     "dcpp_set_gemm_kernel": (ctypes.c_int, [_vp, ctypes.c_int]),
     "dcpp_set_attention_kernel": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "dcpp_set_wait_timeout": (ctypes.c_int, [_vp, ctypes.c_double]),
+    "dcpp_tp_barrier_selftest": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_uint32]),
     "dcpp_dequant": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
     "dcpp_dequant_bf16": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int64, _vp]),
     "dcpp_f32_to_bf16": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
@@ -132,6 +134,10 @@ _SIGNATURES = {
     "dcpp_flux2_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dcpp_flux2_denoise_step": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]),
     "dcpp_flux2_load_inputs": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "dcpp_flux2_prepare_ref": (ctypes.c_int, [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int]),
+    "dcpp_flux2_denoise_step_ref": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]),
+    "dcpp_flux2_load_inputs_ref": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dcpp_flux2_set_timestep": (ctypes.c_int, [_vp, ctypes.c_float, ctypes.c_float]),
     "dcpp_flux2_run_resident": (ctypes.c_int, [_vp]),
     "dcpp_flux2_read_latents": (ctypes.c_int, [_vp, _vp]),
@@ -319,6 +325,16 @@ class Context:
     def set_attention_kernel(self, kind: int):
         self.check(lib().dcpp_set_attention_kernel(self.h, kind), "set_attention_kernel")
 
+    def set_wait_timeout(self, seconds: float):
+        """Limit of the cross-GPU barrier waits in plans prepared afterwards
+        (0: the default 1 s)."""
+        self.check(lib().dcpp_set_wait_timeout(self.h, float(seconds)), "set_wait_timeout")
+
+    def tp_barrier_selftest(self, nranks: int, arrived_mask: int) -> int:
+        """Run the barrier kernel as rank 0 of an emulated group on this GPU;
+        returns the status (DCPP_ERR_TIMEOUT when a rank never arrives)."""
+        return self._call(lib().dcpp_tp_barrier_selftest, self.h, nranks, arrived_mask)
+
     def inject_fault(self, name: Optional[str], nth: int = 1):
         lib().dcpp_inject_fault(self.h, name.encode() if name else None, nth)
 
@@ -503,18 +519,38 @@ class Flux2Model:
         self._check(lib().dcpp_flux2_missing(self.h, ctypes.byref(n), buf, 512), "missing")
         return n.value, buf.value.decode()
 
-    def prepare(self, batch: int, n_img: int, n_txt: int, use_graph: bool = True):
-        self._check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
+    def prepare(self, batch: int, n_img: int, n_txt: int, use_graph: bool = True, n_ref: int = 0):
+        """Plan batch x (n_img + n_ref + n_txt) tokens; n_ref reference-image
+        tokens follow the latent tokens (dcpp_flux2_prepare_ref)."""
+        if n_ref:
+            self._check(lib().dcpp_flux2_prepare_ref(self.h, batch, n_img, n_ref, n_txt, 1 if use_graph else 0),
+                        "prepare_ref")
+        else:
+            self._check(lib().dcpp_flux2_prepare(self.h, batch, n_img, n_txt, 1 if use_graph else 0), "prepare")
 
     def forward(self, hidden, encoder, timestep, img_ids, txt_ids, out, guidance=None):
         self._check(self._run(lib().dcpp_flux2_forward, self.h, _ptr(hidden), _ptr(encoder), _ptr(timestep), _ptr(img_ids),
                                                 _ptr(txt_ids), _ptr(guidance), _ptr(out)), "forward")
 
-    def denoise_step(self, latents, encoder, timestep, dt: float, img_ids, txt_ids, latents_out):
+    def denoise_step(self, latents, encoder, timestep, dt: float, img_ids, txt_ids, latents_out,
+                     image_latents=None, image_latent_ids=None):
+        """Flux2KleinPipeline::denoise for one step; with image_latents (and
+        their ids) the reference tokens join the image stream and only the
+        latent tokens are integrated (dcpp_flux2_denoise_step_ref)."""
+        if image_latents is not None or image_latent_ids is not None:
+            self._check(self._run(lib().dcpp_flux2_denoise_step_ref, self.h, _ptr(latents), _ptr(image_latents),
+                                  _ptr(image_latent_ids), _ptr(encoder), _ptr(timestep), float(dt), _ptr(img_ids),
+                                  _ptr(txt_ids), _ptr(latents_out)), "denoise_step_ref")
+            return
         self._check(self._run(lib().dcpp_flux2_denoise_step, self.h, _ptr(latents), _ptr(encoder), _ptr(timestep), float(dt),
                                                      _ptr(img_ids), _ptr(txt_ids), _ptr(latents_out)), "denoise_step")
 
-    def load_inputs(self, latents, encoder, img_ids, txt_ids):
+    def load_inputs(self, latents, encoder, img_ids, txt_ids, image_latents=None, image_latent_ids=None):
+        if image_latents is not None or image_latent_ids is not None:
+            self._check(self._run(lib().dcpp_flux2_load_inputs_ref, self.h, _ptr(latents), _ptr(image_latents),
+                                  _ptr(image_latent_ids), _ptr(encoder), _ptr(img_ids), _ptr(txt_ids)),
+                        "load_inputs_ref")
+            return
         self._check(self._run(lib().dcpp_flux2_load_inputs, self.h, _ptr(latents), _ptr(encoder), _ptr(img_ids),
                                                     _ptr(txt_ids)), "load_inputs")
 

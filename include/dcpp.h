@@ -104,6 +104,25 @@ dcpp_status dcpp_set_gemm_kernel(dcpp_ctx* ctx, int kind);
  * use 128-key tiles. */
 dcpp_status dcpp_set_attention_kernel(dcpp_ctx* ctx, int kind);
 
+/* Limit of the cross-GPU barrier waits (the tensor-parallel exchange's flag
+ * barriers) in plans prepared after this call, in seconds: 0 restores the
+ * default of 1 s, else 0.001 .. 60.  A wait that runs out makes the kernel
+ * record an error and return; the call that ran it returns DCPP_ERR_TIMEOUT
+ * ("a peer GPU did not arrive") and the context stays usable.  Plays the
+ * role of the process-group timeout around the reference's AllReduce
+ * (ExecutionRuntime.cpp:227-228 throws on a failed graph compute). */
+dcpp_status dcpp_set_wait_timeout(dcpp_ctx* ctx, double seconds);
+
+/* Failure-path self-test of the cross-GPU barrier on one GPU (no counterpart
+ * in the reference): runs the tensor-parallel barrier kernel as rank 0 of a
+ * group of `nranks` (1..8) whose other ranks are flag slots in local device
+ * memory.  Ranks whose bit is set in `arrived_mask` have already arrived;
+ * the others never do, so the wait runs out after the context's wait limit
+ * (dcpp_set_wait_timeout) and the call returns DCPP_ERR_TIMEOUT.  With every
+ * rank arrived it returns DCPP_OK.  Nothing faults or hangs: the kernel
+ * gives up and returns. */
+dcpp_status dcpp_tp_barrier_selftest(dcpp_ctx* ctx, int nranks, uint32_t arrived_mask);
+
 /* Host-side fault injection for failure-path tests: the `nth` next call
  * (1 = the next one) of entry point `name` (e.g. "dcpp_gemm") returns
  * DCPP_ERR_INJECTED without touching the GPU.  name == NULL clears. */
@@ -138,7 +157,9 @@ dcpp_status dcpp_f32_to_bf16(dcpp_ctx* ctx, const float* d_in, int64_t n, uint16
 dcpp_status dcpp_gemm(dcpp_ctx* ctx, int wtype, const void* d_w, int64_t N, int64_t K,
                       const uint16_t* d_x, int64_t M, float* d_y);
 
-/* Dequantisation fused into the GEMM (what the model runs).  A Q4_K / Q8_0
+/* Dequantisation fused into the GEMM (the models use it when the environment
+ * sets DCPP_FUSED_DEQUANT=1; by default they expand each quantised projection
+ * to bf16 right before its GEMM, which measured faster).  A Q4_K / Q8_0
  * weight is first packed once (dcpp_pack_weight) from its GGUF rows into
  * stages of 256 rows x 64 K, each one contiguous block that a bulk TMA copy
  * brings into shared memory, holding the raw 4-bit / 8-bit codes and the
@@ -161,8 +182,9 @@ dcpp_status dcpp_gemm_packed(dcpp_ctx* ctx, int wtype, const void* d_packed, int
  * not make a synchronising cudaMalloc / cudaFree call mid-sequence, and
  * deployments with a memory budget fixed in advance.
  * Limits: K <= 65536 (else DCPP_ERR_UNSUPPORTED with the reason).  The first
- * call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * call in each CUDA context (per device; again after the host re-creates the
+ * context) looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.
  * The array is shared by every call on the device and keeps the last call's
  * contents: calls whose GPU work overlaps (other streams or contexts on the
  * same device) race on it and must be serialised by the caller. */
@@ -217,11 +239,11 @@ typedef struct dcpp_flux2 dcpp_flux2;
 void dcpp_flux2_config_default(dcpp_flux2_config* cfg);
 
 /* Parse a diffusers transformer/config.json (Config::from_file,
- * Flux2Transformer2DModel.cpp:322-353) into `cfg` (defaults kept for
+ * Flux2Transformer2DModel.cpp:253-284) into `cfg` (defaults kept for
  * missing keys). */
 dcpp_status dcpp_flux2_config_from_file(const char* path, dcpp_flux2_config* cfg);
 
-/* Build the module tree (Flux2Transformer2DModel.cpp:104-178).  Device
+/* Build the module tree (Flux2Transformer2DModel.cpp:35-109).  Device
  * memory for parameters is allocated as they are set. */
 dcpp_status dcpp_flux2_create(dcpp_ctx* ctx, const dcpp_flux2_config* cfg, dcpp_flux2** out_model);
 dcpp_status dcpp_flux2_destroy(dcpp_flux2* model);
@@ -244,7 +266,7 @@ dcpp_status dcpp_flux2_missing(dcpp_flux2* model, int* count, char* first_missin
 dcpp_status dcpp_flux2_prepare(dcpp_flux2* model, int64_t batch, int64_t n_img, int64_t n_txt,
                                int use_graph);
 
-/* Flux2Transformer2DModel::forward (Flux2Transformer2DModel.cpp:180-300):
+/* Flux2Transformer2DModel::forward (Flux2Transformer2DModel.cpp:111-231):
  *   hidden [B, n_img, in_channels] f32, encoder [B, n_txt, joint_dim] f32,
  *   timestep [B] f32 (in [0,1]; multiplied by 1000 inside, :199),
  *   img_ids [B?, n_img, n_axes] int32, txt_ids [B?, n_txt, n_axes] int32
@@ -262,6 +284,34 @@ dcpp_status dcpp_flux2_denoise_step(dcpp_flux2* model, const float* p_latents_in
                                     const float* p_encoder, const float* p_timestep, float dt,
                                     const int32_t* p_img_ids, const int32_t* p_txt_ids,
                                     float* p_latents_out);
+
+/* Reference-image (img2img / edit) denoising, Flux2KleinPipeline::denoise
+ * with image_latents (Flux2KleinPipeline.cpp:511-536): the n_ref reference
+ * tokens and their ids join the image stream after the n_img latent tokens
+ * (the transformer sees n_img + n_ref image tokens, num_ref_tokens = n_ref),
+ * and only the n_img latent tokens' noise prediction is integrated.
+ *   prepare_ref        plans B x (n_img + n_ref + n_txt) tokens; n_ref = 0
+ *                      is dcpp_flux2_prepare.  forward() on such a plan takes
+ *                      the concatenated [B, n_img + n_ref, C] input and ids
+ *                      and returns every image token's prediction, as the
+ *                      reference's forward does;
+ *   denoise_step_ref   latents [B, n_img, C], image_latents [B, n_ref, C],
+ *                      image_latent_ids [n_ref, n_axes], the rest as
+ *                      dcpp_flux2_denoise_step; latents_out [B, n_img, C];
+ *   load_inputs_ref    the resident form: the reference tokens are held
+ *                      fixed across run_resident steps; read_latents returns
+ *                      [B, n_img, C].
+ * On a plan with reference tokens the calls without _ref return
+ * DCPP_ERR_INVALID_ARG, and the _ref calls need non-NULL reference inputs. */
+dcpp_status dcpp_flux2_prepare_ref(dcpp_flux2* model, int64_t batch, int64_t n_img, int64_t n_ref, int64_t n_txt,
+                                   int use_graph);
+dcpp_status dcpp_flux2_denoise_step_ref(dcpp_flux2* model, const float* p_latents_in, const float* p_image_latents,
+                                        const int32_t* p_image_latent_ids, const float* p_encoder,
+                                        const float* p_timestep, float dt, const int32_t* p_img_ids,
+                                        const int32_t* p_txt_ids, float* p_latents_out);
+dcpp_status dcpp_flux2_load_inputs_ref(dcpp_flux2* model, const float* p_latents, const float* p_image_latents,
+                                       const int32_t* p_image_latent_ids, const float* p_encoder,
+                                       const int32_t* p_img_ids, const int32_t* p_txt_ids);
 
 /* Resident execution, for callers that keep the latent on the device across
  * the schedule (the reference instead copies the latent through host

@@ -7,7 +7,7 @@ and ``--impl reference`` legs) may import this module; the product path
 A PyTorch-CPU restatement (float64 by default, float32 for the timed CPU
 baseline) of the reference's forward, op by op, with ggml op semantics:
 
-* ``Flux2Transformer2DModel::forward``  src/diffusers/models/transformers/flux2/Flux2Transformer2DModel.cpp:180-300
+* ``Flux2Transformer2DModel::forward``  src/diffusers/models/transformers/flux2/Flux2Transformer2DModel.cpp:111-231
 * ``Flux2TransformerBlock::forward``    Flux2TransformerBlock.hpp:45-117
 * ``Flux2Attention::forward``           Flux2Attention.hpp:64-159
 * ``Flux2SingleTransformerBlock``       Flux2SingleTransformerBlock.hpp:36-72
@@ -116,16 +116,19 @@ class Config:
 class Weights:
     """Resolves GGUF-named raw parameters into float matrices on demand."""
 
-    def __init__(self, params: Dict[str, Tuple[int, Tuple[int, ...], np.ndarray]], dtype=torch.float64):
+    def __init__(self, params: Dict[str, Tuple[int, Tuple[int, ...], np.ndarray]], dtype=torch.float64,
+                 device: str = "cpu"):
         self.params = params
         self.dtype = dtype
+        self.device = torch.device(device)
         self.cache: Dict[str, torch.Tensor] = {}
 
     def get(self, name: str) -> torch.Tensor:
         if name not in self.cache:
             gtype, shape, data = self.params[name]
             n = int(np.prod(shape))
-            self.cache[name] = torch.from_numpy(dequant(gtype, data, n).reshape(shape)).to(self.dtype)
+            w = torch.from_numpy(dequant(gtype, data, n).reshape(shape))
+            self.cache[name] = w.to(self.device).to(self.dtype)
         return self.cache[name]
 
     def has(self, name: str) -> bool:
@@ -175,12 +178,12 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 def timestep_proj(t: torch.Tensor, channels: int) -> torch.Tensor:
     # Timesteps(channels, flip_sin_to_cos=True, shift=0, scale=1) (Timesteps.cpp:17-46).
     half = channels // 2
-    exponent = torch.arange(half, dtype=t.dtype) * (-math.log(10000.0) / half)
+    exponent = torch.arange(half, dtype=t.dtype, device=t.device) * (-math.log(10000.0) / half)
     emb = torch.exp(exponent)
     emb = t[:, None] * emb[None, :]
     out = torch.cat([torch.cos(emb), torch.sin(emb)], dim=-1)
     if channels % 2 == 1:
-        out = torch.cat([out, torch.zeros(out.shape[0], 1, dtype=out.dtype)], dim=-1)
+        out = torch.cat([out, torch.zeros(out.shape[0], 1, dtype=out.dtype, device=out.device)], dim=-1)
     return out
 
 
@@ -190,7 +193,7 @@ def rope_cos_sin(ids: torch.Tensor, axes_dims, theta: float, dtype) -> Tuple[tor
     Flux2PosEmbed.hpp:18-109)."""
     cs, sn = [], []
     for a, nd in enumerate(axes_dims):
-        p = torch.arange(nd // 2, dtype=dtype)
+        p = torch.arange(nd // 2, dtype=dtype, device=ids.device)
         freq = float(theta) ** (-2.0 * p / nd)
         ang = ids[:, a].to(dtype)[:, None] * freq[None, :]
         cs.append(torch.cos(ang))
@@ -226,21 +229,27 @@ def _heads(x: torch.Tensor, H: int) -> torch.Tensor:
 
 
 class Flux2Oracle:
-    def __init__(self, cfg: Config, params, dtype=torch.float64, keep_weights: bool = True):
+    """``device``: where the float arithmetic runs.  The default is the CPU;
+    the real-width parity tests run the same float64 restatement on a GPU
+    (torch's float64 kernels) only to finish in seconds.  The weights are
+    always dequantised by the C oracle on the host first."""
+
+    def __init__(self, cfg: Config, params, dtype=torch.float64, keep_weights: bool = True, device: str = "cpu"):
         self.cfg = cfg
-        self.w = Weights(params, dtype)
+        self.device = torch.device(device)
+        self.w = Weights(params, dtype, device)
         self.dtype = dtype
         self.keep = keep_weights
 
     # -- conditioning --------------------------------------------------------
     def temb(self, timestep: torch.Tensor, guidance: Optional[torch.Tensor]) -> torch.Tensor:
         c, w = self.cfg, self.w
-        t = timestep.to(self.dtype) * 1000.0
+        t = timestep.to(self.device, self.dtype) * 1000.0
         p = "time_guidance_embed."
         e = linear(silu(linear(timestep_proj(t, c.timestep_guidance_channels), w.get(p + "timestep_embedder.linear_1.weight"))),
                    w.get(p + "timestep_embedder.linear_2.weight"))
         if c.guidance_embeds:
-            g = guidance.to(self.dtype) * 1000.0
+            g = guidance.to(self.device, self.dtype) * 1000.0
             e = e + linear(silu(linear(timestep_proj(g, c.timestep_guidance_channels), w.get(p + "guidance_embedder.linear_1.weight"))),
                            w.get(p + "guidance_embedder.linear_2.weight"))
         return e
@@ -314,7 +323,7 @@ class Flux2Oracle:
         n_double / n_single limit the blocks run (bounded CPU samples)."""
         c, w = self.cfg, self.w
         dt = self.dtype
-        hidden, encoder = hidden.to(dt), encoder.to(dt)
+        hidden, encoder = hidden.to(self.device, dt), encoder.to(self.device, dt)
         temb = self.temb(timestep, guidance)
         st = silu(temb)
         mod_img = linear(st, w.get("double_stream_modulation_img.linear.weight"))
@@ -326,7 +335,7 @@ class Flux2Oracle:
             img_ids = img_ids[0]
         if txt_ids.dim() == 3:
             txt_ids = txt_ids[0]
-        ids = torch.cat([txt_ids, img_ids], dim=0)
+        ids = torch.cat([txt_ids, img_ids], dim=0).to(self.device)
         cos, sin = rope_cos_sin(ids, c.axes_dims_rope, c.rope_theta, dt)
         nd = c.num_layers if n_double is None else n_double
         ns = c.num_single_layers if n_single is None else n_single
@@ -342,10 +351,26 @@ class Flux2Oracle:
         hs = layer_norm(hs, c.eps) * (1.0 + scale)[:, None, :] + shift[:, None, :]
         return linear(hs, w.get("proj_out.weight"))
 
-    def denoise(self, latents, encoder, timestep, dt, img_ids, txt_ids) -> torch.Tensor:
-        """Flux2KleinPipeline::denoise + FlowMatchEulerDiscreteScheduler::integrate."""
-        v = self.forward(latents, encoder, timestep, img_ids, txt_ids, None)
-        return latents.to(self.dtype) + dt * v
+    def denoise(self, latents, encoder, timestep, dt, img_ids, txt_ids,
+                image_latents=None, image_latent_ids=None) -> torch.Tensor:
+        """Flux2KleinPipeline::denoise (Flux2KleinPipeline.cpp:496-537) +
+        FlowMatchEulerDiscreteScheduler::integrate.  With image_latents the
+        reference tokens and their ids are appended to the image tokens
+        (:511-519), the forward runs on both, and the noise prediction is
+        sliced back to the latent tokens before the Euler update (:531-536)."""
+        x, ids = latents, img_ids
+        if image_latents is not None:
+            if image_latent_ids is None:
+                raise ValueError("denoise(): image_latent_ids is required when image_latents is provided")
+            if img_ids.dim() == 3:
+                img_ids = img_ids[0]
+            if image_latent_ids.dim() == 3:
+                image_latent_ids = image_latent_ids[0]
+            x = torch.cat([latents.to(image_latents.dtype), image_latents], dim=1)
+            ids = torch.cat([img_ids, image_latent_ids], dim=0)
+        v = self.forward(x, encoder, timestep, ids, txt_ids, None)
+        v = v[:, : latents.shape[1]]
+        return latents.to(self.device, self.dtype) + dt * v
 
 
 def flow_match_schedule(n: int, shift: float = 1.0):

@@ -103,8 +103,10 @@ def test_layernorm_mod_matches_reference(ctx):
     assert ((y.cpu().double() - ref).norm() / ref.norm()).item() < 4e-3
 
 
-def test_attention_full_size_heads_subset(ctx, attn_kind):
-    """The config-2 attention shape (S = 4608, 24 heads); the oracle checks two heads."""
+def test_attention_full_size_all_heads(ctx, attn_kind):
+    """The config-2 attention shape (S = 4608, 24 heads), every head checked
+    against the float64 restatement (run on the GPU in float64 only to
+    finish in seconds)."""
     B, S, H = 1, 4608, 24
     g = torch.Generator().manual_seed(11)
     D = H * 128
@@ -118,19 +120,21 @@ def test_attention_full_size_heads_subset(ctx, attn_kind):
     out = torch.empty(B, S, D, dtype=torch.bfloat16, device="cuda")
     ctx.attention(qkv.cuda(), B, S, H, wq.cuda(), wk.cuda(), 1e-6, ids.cuda(), (32, 32, 32, 32), 2000.0, out)
     ctx.synchronize()
-    cos, sin = fo.rope_cos_sin(ids, (32, 32, 32, 32), 2000, torch.float64)
-    x = qkv.double()
-    for h in (0, H - 1):
-        sl = slice(h * 128, (h + 1) * 128)
-        q = x[..., sl].unsqueeze(2)
-        k = x[..., D:2 * D][..., sl].unsqueeze(2)
-        v = x[..., 2 * D:][..., sl].unsqueeze(2)
-        q = fo.apply_rope(fo.rms_norm(q, wq.double(), 1e-6), cos, sin)
-        k = fo.apply_rope(fo.rms_norm(k, wk.double(), 1e-6), cos, sin)
-        ref = fo.sdpa(q, k, v).flatten(2)
-        got = out[..., sl].cpu().double()
-        rel = ((got - ref).norm() / ref.norm()).item()
+    cos, sin = fo.rope_cos_sin(ids.cuda(), (32, 32, 32, 32), 2000, torch.float64)
+    x = qkv.cuda().double()
+    q = x[..., :D].unflatten(-1, (H, 128))
+    k = x[..., D:2 * D].unflatten(-1, (H, 128))
+    v = x[..., 2 * D:].unflatten(-1, (H, 128))
+    q = fo.apply_rope(fo.rms_norm(q, wq.cuda().double(), 1e-6), cos, sin)
+    k = fo.apply_rope(fo.rms_norm(k, wk.cuda().double(), 1e-6), cos, sin)
+    ref = fo.sdpa(q, k, v)
+    got = out.double().unflatten(-1, (H, 128))
+    worst = 0.0
+    for h in range(H):
+        rel = ((got[:, :, h] - ref[:, :, h]).norm() / ref[:, :, h].norm()).item()
+        worst = max(worst, rel)
         assert rel < 1e-2, (h, rel)
+    print(f"attention S={S} H={H}: worst per-head rel-L2 {worst:.2e}")
 
 
 @pytest.mark.parametrize("B,S,H", [(1, 200, 2), (2, 333, 3), (1, 1024, 4), (1, 64, 1), (1, 300, 1)])

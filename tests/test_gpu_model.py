@@ -231,3 +231,111 @@ def test_injected_fault_surfaces_as_error_then_recovers(ctx):
     assert e.value.status == 9
     m.forward(hid, enc, t, iid, tid, out)
     assert torch.isfinite(out).all()
+
+
+def make_ref_tokens(c, B, n_ref, seed):
+    """Reference-image latents [B, n_ref, C] and ids [n_ref, 4] on a second
+    time coordinate (T = 10), as the pipeline's prepare_image_latents gives
+    its first reference image."""
+    g = torch.Generator().manual_seed(seed)
+    lat = torch.randn(B, n_ref, c.in_channels, generator=g)
+    ids = torch.zeros(n_ref, len(c.axes_dims_rope), dtype=torch.int32)
+    ids[:, 0] = 10
+    ids[:, 1] = torch.arange(n_ref, dtype=torch.int32) // 4
+    ids[:, 2] = torch.arange(n_ref, dtype=torch.int32) % 4
+    return lat, ids
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_denoise_with_ref_images_matches_oracle(ctx, B):
+    """Flux2KleinPipeline::denoise with image_latents (Flux2KleinPipeline.cpp:511-536),
+    in the shape of test_denoise_with_ref_images
+    (test/src/diffusers/pipelines/flux2/Flux2KleinPipeline.py:500-734): a 2 x 3
+    packed latent grid, 12 reference tokens, one step."""
+    c = cfg_small()
+    params = synth.make_params(c, fo.GGML_Q8_0, seed=31)
+    hid, enc, iid, tid = synth.make_inputs(c, B, 2, 3, 16, seed=32)
+    ref_lat, ref_ids = make_ref_tokens(c, B, 12, seed=33)
+    m = dcpp_b200.Flux2Model(ctx, c)
+    m.load_params(params)
+    m.prepare(B, 6, 16, n_ref=12)
+    t = torch.full((B,), 1.0)
+    out = torch.full_like(hid, float("nan"))
+    m.denoise_step(hid, enc, t, -1.0, iid, tid, out, image_latents=ref_lat, image_latent_ids=ref_ids)
+    o = fo.Flux2Oracle(oracle_cfg(c), params)
+    ref = o.denoise(hid, enc, t, -1.0, iid, tid, image_latents=ref_lat, image_latent_ids=ref_ids)
+    r = rel(out, ref)
+    assert r < LAT_TOL, (r, (out.double() - ref).abs().max().item())
+    # The reference tokens change the result (they are attended to), by far
+    # more than the GPU path's error.
+    plain = o.denoise(hid, enc, t, -1.0, iid, tid)
+    assert rel(plain, ref) > 2 * LAT_TOL and r < rel(plain, ref) / 5, (rel(plain, ref), r)
+    m.close()
+
+
+def test_forward_on_ref_plan_returns_every_image_token(ctx):
+    """forward() on a plan with reference tokens takes the concatenated
+    image tokens and returns all of their predictions, as the reference's
+    forward does (it slices nothing, Flux2Transformer2DModel.cpp:217-230)."""
+    c = cfg_small()
+    params = synth.make_params(c, fo.GGML_Q8_0, seed=34)
+    hid, enc, iid, tid = synth.make_inputs(c, 1, 2, 3, 16, seed=35)
+    ref_lat, ref_ids = make_ref_tokens(c, 1, 12, seed=36)
+    x = torch.cat([hid, ref_lat], dim=1).contiguous()
+    ids = torch.cat([iid, ref_ids], dim=0).contiguous()
+    m = dcpp_b200.Flux2Model(ctx, c)
+    m.load_params(params)
+    m.prepare(1, 6, 16, n_ref=12)
+    t = torch.tensor([0.5])
+    out = torch.empty(1, 18, c.in_channels)
+    m.forward(x, enc, t, ids, tid, out)
+    ref = fo.Flux2Oracle(oracle_cfg(c), params).forward(x, enc, t, ids, tid)
+    assert rel(out, ref) < V_TOL
+    m.close()
+
+
+def test_resident_schedule_with_ref_images(ctx):
+    """Two resident steps with reference tokens: the reference latents stay
+    fixed while the latent tokens follow the schedule."""
+    c = cfg_small()
+    params = synth.make_params(c, fo.GGML_Q4_K, seed=37)
+    hid, enc, iid, tid = synth.make_inputs(c, 1, 4, 4, 8, seed=38)
+    ref_lat, ref_ids = make_ref_tokens(c, 1, 8, seed=39)
+    m = dcpp_b200.Flux2Model(ctx, c)
+    m.load_params(params)
+    m.prepare(1, 16, 8, n_ref=8)
+    ts, sg = dcpp_b200.flow_match_schedule(2)
+    m.load_inputs(hid, enc, iid, tid, image_latents=ref_lat, image_latent_ids=ref_ids)
+    for i in range(2):
+        m.set_timestep(float(ts[i]) / 1000.0, float(sg[i + 1] - sg[i]))
+        m.run_resident()
+    out = torch.empty_like(hid)
+    m.read_latents(out)
+    o = fo.Flux2Oracle(oracle_cfg(c), params)
+    x = hid.double()
+    for i in range(2):
+        x = o.denoise(x, enc, torch.tensor([float(ts[i]) / 1000.0]), float(sg[i + 1] - sg[i]), iid, tid,
+                      image_latents=ref_lat.double(), image_latent_ids=ref_ids)
+    r = rel(out, x)
+    assert r < LAT_TOL, r
+    m.close()
+
+
+def test_ref_plan_rejects_calls_without_ref_inputs(ctx):
+    c = cfg_small()
+    m, _ = build(ctx, c, fo.GGML_Q8_0)
+    hid, enc, iid, tid = synth.make_inputs(c, 1, 4, 4, 8, seed=3)
+    ref_lat, ref_ids = make_ref_tokens(c, 1, 4, seed=40)
+    out = torch.empty_like(hid)
+    t = torch.tensor([0.5])
+    # a plan without reference tokens refuses reference inputs
+    with pytest.raises(dcpp_b200.DcppError) as e:
+        m.denoise_step(hid, enc, t, -0.25, iid, tid, out, image_latents=ref_lat, image_latent_ids=ref_ids)
+    assert e.value.status == 1
+    m.prepare(1, 16, 8, n_ref=4)
+    with pytest.raises(dcpp_b200.DcppError) as e:
+        m.denoise_step(hid, enc, t, -0.25, iid, tid, out)
+    assert e.value.status == 1 and "reference tokens" in str(e.value)
+    m.denoise_step(hid, enc, t, -0.25, iid, tid, out, image_latents=ref_lat, image_latent_ids=ref_ids)
+    assert torch.isfinite(out).all()
+    m.close()
