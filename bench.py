@@ -57,7 +57,11 @@ CONFIGS = {
 # averaged over one step's GEMM launches: dram__bytes_read.sum +
 # dram__bytes_write.sum from one ncu capture of this bench's own command
 # (summary and command in the named profile).  Keyed by (config, n_gpus).
-GEMM_TRAFFIC = {}
+GEMM_TRAFFIC = {
+    ("2", 1): {"dram_bytes_per_launch": 428.2e6, "algorithmic_bytes_per_launch": 298.9e6,
+               "source": "profiles/dram_traffic_config2_step.md: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                         "over the 63 gemm_pair_kernel launches of one step (cold cache), per launch"},
+}
 
 
 def weight_bytes(cfg, wtype, world):

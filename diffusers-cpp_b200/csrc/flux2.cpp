@@ -108,6 +108,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) == "1";
   if (const char* e = getenv("DCPP_TP_COMM")) tp_peer_ = std::string(e) != "nccl";
   if (const char* e = getenv("DCPP_TP_PIECES")) tp_pieces_env_ = std::string(e) == "1" ? 1 : 2;
+  if (const char* e = getenv("DCPP_BLOCK_PREFETCH")) block_prefetch_ = std::string(e) == "1";
   build_registry();
 }
 
@@ -570,6 +571,15 @@ void Flux2Transformer2DModel::add_allreduce(float* buf, int64_t count) {
 
 
 
+std::vector<const DevWeight*> Flux2Transformer2DModel::block_weights(size_t k) const {
+  if (k < dbl_.size()) {
+    const DoubleBlock& b = dbl_[k];
+    return {&b.qkv[0], &b.qkv[1], &b.out[0], &b.out[1], &b.ff_in[0], &b.ff_in[1], &b.ff_out[0], &b.ff_out[1]};
+  }
+  const SingleBlock& b = sgl_[k - dbl_.size()];
+  return {&b.qkv_mlp, &b.out};
+}
+
 void Flux2Transformer2DModel::add_tp_barrier(int set, int stream) {
   TpBarrierArgs a{};
   for (int j = 0; j < nranks_; ++j) a.flags[j] = flags_peer_[set][j];
@@ -674,13 +684,28 @@ void Flux2Transformer2DModel::build_plan() {
   auto needs = [](const DevWeight* w) { return w->type != kTypeBF16 && !w->packed; };
   for (const DevWeight* w : {&x_embed_, &ctx_embed_, &proj_out_})
     if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
-  for (auto& blk : dbl_)
-    for (int s = 0; s < 2; ++s)
-      for (const DevWeight* w : {&blk.qkv[s], &blk.out[s], &blk.ff_in[s], &blk.ff_out[s]})
-        if (needs(w)) (s == 0 ? s1 : s0) = std::max(s == 0 ? s1 : s0, static_cast<size_t>(w->rows * w->cols));
-  for (auto& blk : sgl_)
-    for (const DevWeight* w : {&blk.qkv_mlp, &blk.out})
-      if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
+  // Block weights: expanded a whole block ahead (block_weights / add_prefetch)
+  // into two block-sized sets, or, with block prefetch off, each projection
+  // right before its GEMM into the per-GEMM scratch pairs.
+  size_t pf = 0;
+  for (size_t k = 0; k < dbl_.size() + sgl_.size(); ++k) {
+    size_t n = 0;
+    for (const DevWeight* w : block_weights(k))
+      if (needs(w)) n += (static_cast<size_t>(w->rows * w->cols) + 127) / 128 * 128;
+    pf = std::max(pf, n);
+  }
+  if (block_prefetch_) {
+    alloc_prefetch_scratch(alloc, pf);
+  } else {
+    alloc_prefetch_scratch(alloc, 0);
+    for (auto& blk : dbl_)
+      for (int s = 0; s < 2; ++s)
+        for (const DevWeight* w : {&blk.qkv[s], &blk.out[s], &blk.ff_in[s], &blk.ff_out[s]})
+          if (needs(w)) (s == 0 ? s1 : s0) = std::max(s == 0 ? s1 : s0, static_cast<size_t>(w->rows * w->cols));
+    for (auto& blk : sgl_)
+      for (const DevWeight* w : {&blk.qkv_mlp, &blk.out})
+        if (needs(w)) s0 = std::max(s0, static_cast<size_t>(w->rows * w->cols));
+  }
   alloc_expansion_scratch(alloc, s0, s1);
 
   const int n_axes = static_cast<int>(cfg_.axes_dims_rope.size());
@@ -740,8 +765,20 @@ void Flux2Transformer2DModel::build_plan() {
     return n;
   };
 
+  const size_t n_blocks = dbl_.size() + sgl_.size();
   auto build_ops = [&](std::vector<Op>& ops, float* lat_in, float* lat_out, bool euler) {
     begin_ops(ops);
+    // Block-ahead expansion: block 0's quantised weights from the start of
+    // the step (under the conditioning GEMVs and embedders), block k + 1's
+    // while block k's attention runs (after its QKV GEMM, when the set that
+    // block k - 1 used is free).  The attention leaves HBM and most issue
+    // slots idle; expansions beside a GEMM slow it instead.
+    size_t blk_idx = 0;
+    auto prefetch_next = [&]() {
+      if (block_prefetch_ && blk_idx + 1 < n_blocks) add_prefetch(block_weights(blk_idx + 1), static_cast<int>((blk_idx + 1) & 1));
+      ++blk_idx;
+    };
+    if (block_prefetch_ && n_blocks) add_prefetch(block_weights(0), 0);
     // 1. timestep (and guidance) embedding, modulation vectors
     //    (Flux2Transformer2DModel.cpp:130-145).
     ops.push_back({[=](cudaStream_t s) {
@@ -957,6 +994,7 @@ void Flux2Transformer2DModel::build_plan() {
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("qkv", a_, D, D, &blk.qkv[0], &blk.qkv[1], pcs, e, 3 * Dl, hook);
                 });
+      prefetch_next();
       attn_op();
       add_gemm("attn_out", cat_, ldc, Dl, &blk.out[0], &blk.out[1], stream_groups(true),
                out_epi(mod_txt_v_ + 2 * D, mod_img_v_ + 2 * D, 6 * D), D);
@@ -994,6 +1032,7 @@ void Flux2Transformer2DModel::build_plan() {
                 [&](const std::vector<std::vector<GemmGroup>>& pcs, const std::function<void(int)>& hook) {
                   add_gemm_pieces("qkv_mlp", a_, D, D, &blk.qkv_mlp, nullptr, pcs, e, 3 * Dl + 2 * Fl, hook);
                 });
+      prefetch_next();
       attn_op();
       add_gemm("out", cat_, ldc, Dl + Fl, &blk.out, nullptr, stream_groups(false),
                out_epi(mod_s_v_ + 2 * D, mod_s_v_ + 2 * D, 3 * D), D);

@@ -136,6 +136,8 @@ class Flux2Transformer2DModel : public StepPlanner {
   // Plan helpers (tensor parallelism).
   void add_allreduce(float* buf, int64_t count);
   void add_tp_barrier(int set, int stream);
+  // The projection weights of block k (double blocks first, then single).
+  std::vector<const DevWeight*> block_weights(size_t k) const;
 
   Flux2Config cfg_;
   bool host_only_ = false;
@@ -195,6 +197,12 @@ class Flux2Transformer2DModel : public StepPlanner {
   // bf16 right before its GEMM, which measured faster for these 4608-row
   // GEMMs (the fused kernels are bound by shared-memory traffic).
   bool fused_dequant_ = false;
+  // DCPP_BLOCK_PREFETCH=1: expand each block's quantised weights a whole
+  // block ahead, under the previous block's attention, instead of each
+  // projection right before its GEMM (overlapping the GEMM before it).
+  // Measured equal within noise on config 2 (the step is power-capped), so
+  // the default stays per projection.
+  bool block_prefetch_ = false;
 };
 
 // FlowMatchEulerDiscreteScheduler (default: shift 1, no dynamic shifting,

@@ -40,16 +40,34 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmArgs& p, int t) {
     split = t / p.tiles_per_split;
     t -= split * p.tiles_per_split;
   }
+  // (outer, inner) extents: raster 0 bands M tiles, raster 1 bands N tiles.
+  const int n_out = p.raster ? p.n_tiles_n : p.m_tiles_all;  // the banded dimension
+  const int n_in = p.raster ? p.m_tiles_all : p.n_tiles_n;   // walked whole inside a band
+  const int band = p.band;
+  const int full = n_out / band;
+  int b0, bw, u;
+  if (t < full * band * n_in) {
+    const int b = t / (band * n_in);
+    b0 = b * band;
+    bw = band;
+    u = t - b * band * n_in;
+  } else {
+    b0 = full * band;
+    bw = n_out - b0;
+    u = t - full * band * n_in;
+  }
+  const int across = u / bw;            // index in the unbanded dimension
+  const int within = b0 + (u - across * bw);  // index in the banded dimension
+  const int m_all = p.raster ? across : within;
+  const int n_tile = p.raster ? within : across;
   int g = 0;
 #pragma unroll 1
   for (int i = 1; i < p.n_groups; ++i)
-    if (t >= p.groups[i].tile0) g = i;
-  const GemmGroup& G = p.groups[g];
-  int local = t - G.tile0;
+    if (m_all >= p.groups[i].tile0) g = i;
   TileCoord c;
   c.g = g;
-  c.n_tile = local / G.m_tiles;
-  c.m_tile = local - c.n_tile * G.m_tiles;
+  c.n_tile = n_tile;
+  c.m_tile = m_all - p.groups[g].tile0;
   c.split = split;
   return c;
 }
@@ -1681,13 +1699,43 @@ void gemm_set_k_splits(GemmArgs& a, int k_splits, int64_t split_stride) {
 void gemm_finalize_groups(GemmArgs& a, int tile_m, int tile_n) {
   a.tile_n = tile_n;
   a.n_tiles_n = (a.N + tile_n - 1) / tile_n;
-  int t = 0;
+  int mt = 0;
+  bool w_used[2] = {false, false};
   for (int g = 0; g < a.n_groups; ++g) {
     a.groups[g].m_tiles = (a.groups[g].rows + tile_m - 1) / tile_m;
-    a.groups[g].tile0 = t;
-    t += a.groups[g].m_tiles * a.n_tiles_n;
+    a.groups[g].tile0 = mt;
+    mt += a.groups[g].m_tiles;
+    w_used[a.groups[g].wsel & 1] = true;
   }
-  a.total_tiles = t;
+  a.m_tiles_all = mt;
+  a.total_tiles = mt * a.n_tiles_n;
+  // Tile order: keep one operand's band in L2 and stream the other once per
+  // band, picking the order and band width with the fewest modelled DRAM
+  // bytes (bf16 operands; a band's resident bytes at most the L2 budget).
+  // Convolutions keep M-inner order with one band (their A is an image).
+  a.raster = 0;
+  a.band = std::max(mt, 1);
+  if (a.conv.taps == 0 && mt > 0) {
+    double budget = 64.0 * (1 << 20);
+    if (const char* f = getenv("DCPP_GEMM_L2_MB")) budget = std::max(1.0, atof(f)) * (1 << 20);
+    const double a_row = static_cast<double>(tile_m) * a.K * 2.0;                              // one M tile of A
+    const double b_col = static_cast<double>(tile_n) * a.K * 2.0 * (w_used[0] + w_used[1]);  // one N tile of B
+    const double a_all = a_row * mt, b_all = b_col * a.n_tiles_n;
+    const int bm = std::max(1, std::min(mt, static_cast<int>(budget / a_row)));
+    const int bn = std::max(1, std::min(a.n_tiles_n, static_cast<int>(budget / b_col)));
+    const double cost_m = a_all + b_all * ((mt + bm - 1) / bm);
+    const double cost_n = b_all + a_all * ((a.n_tiles_n + bn - 1) / bn);
+    if (cost_n < cost_m) {
+      a.raster = 1;
+      a.band = bn;
+    } else {
+      a.band = bm;
+    }
+    if (const char* f = getenv("DCPP_GEMM_RASTER")) {  // 0 / 1 force the order with one band (measurements)
+      a.raster = atoi(f) ? 1 : 0;
+      a.band = a.raster ? a.n_tiles_n : mt;
+    }
+  }
 }
 
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,

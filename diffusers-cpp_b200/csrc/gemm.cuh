@@ -142,6 +142,16 @@ struct GemmArgs {
   int32_t N, K;
   int32_t n_tiles_n;
   int32_t total_tiles;
+  // Tile order (set by gemm_finalize_groups).  The M tiles of all groups form
+  // one sequence of m_tiles_all tiles (group g's start at groups[g].tile0).
+  // raster 0: bands of `band` M tiles; within a band, N tiles outer and the
+  // band's M tiles inner, so the band's A rows stay in L2 while each B tile
+  // is read once per band.  raster 1: bands of `band` N tiles; within a band,
+  // M tiles outer and the band's N tiles inner (B stays in L2, A is read once
+  // per band).  The persistent CTAs walk this order.
+  int32_t m_tiles_all;
+  int32_t raster;
+  int32_t band;
   int32_t n_groups;
   GemmGroup groups[kGemmMaxGroups];
   EpilogueArgs ep;

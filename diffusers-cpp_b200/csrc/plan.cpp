@@ -225,6 +225,7 @@ StepPlanner::~StepPlanner() {
   for (auto e : ev_) cudaEventDestroy(e);
   release_plan_events();
   if (side_) cudaStreamDestroy(side_);
+  if (side2_) cudaStreamDestroy(side2_);
 }
 
 void StepPlanner::release_plan_events() {
@@ -242,24 +243,65 @@ void StepPlanner::alloc_expansion_scratch(const std::function<void*(size_t)>& al
 }
 
 void StepPlanner::begin_ops(std::vector<Op>& ops) {
-  if (!side_) {
+  if (!side_ || !side2_) {
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
-    cuda_check(cudaStreamCreateWithPriority(&side_, cudaStreamNonBlocking, lo), "side stream");
+    if (!side_) cuda_check(cudaStreamCreateWithPriority(&side_, cudaStreamNonBlocking, lo), "side stream");
+    if (!side2_) cuda_check(cudaStreamCreateWithPriority(&side2_, cudaStreamNonBlocking, lo), "expansion stream");
   }
   building_ = &ops;
   scratch_pair_ = 0;
   for (auto& e : scratch_free_) e = nullptr;
+  prefetched_.clear();
   plan_start_ = plan_event();
   add_record(plan_start_, 0);
-  add_wait(plan_start_, 1);  // the side stream joins the plan (and a capture) at its start
+  add_wait(plan_start_, 1);  // the side streams join the plan (and a capture) at its start
+  add_wait(plan_start_, 2);
 }
 
 void StepPlanner::end_ops() {
-  cudaEvent_t side_done = plan_event();
-  add_record(side_done, 1);
-  add_wait(side_done, 0);
+  for (int st = 1; st <= 2; ++st) {
+    cudaEvent_t side_done = plan_event();
+    add_record(side_done, st);
+    add_wait(side_done, 0);
+  }
+  prefetched_.clear();
   building_ = nullptr;
+}
+
+void StepPlanner::alloc_prefetch_scratch(const std::function<void*(size_t)>& alloc, size_t elems) {
+  pf_scratch_elems_ = elems;
+  for (int k = 0; k < 2; ++k) pf_scratch_[k] = elems ? static_cast<uint16_t*>(alloc(elems * 2)) : nullptr;
+}
+
+void StepPlanner::add_prefetch(const std::vector<const DevWeight*>& ws, int set) {
+  std::vector<const DevWeight*> todo;
+  size_t need = 0;
+  for (const DevWeight* w : ws)
+    if (w && w->data && !w->packed && w->type != kTypeBF16) {
+      todo.push_back(w);
+      need += (static_cast<size_t>(w->rows * w->cols) + 127) / 128 * 128;
+    }
+  if (todo.empty()) return;
+  if (need > pf_scratch_elems_ || !pf_scratch_[set & 1])
+    fail(DCPP_ERR_STATE, "internal: prefetch scratch too small for " + todo.front()->name);
+  cudaEvent_t go = plan_event();
+  add_record(go, 0);
+  add_wait(go, 2);
+  size_t off = 0;
+  cudaEvent_t ready = plan_event();
+  for (const DevWeight* w : todo) {
+    uint16_t* dst = pf_scratch_[set & 1] + off;
+    off += (static_cast<size_t>(w->rows * w->cols) + 127) / 128 * 128;
+    Op o{[w, dst](cudaStream_t s) {
+           cuda_check(launch_dequant_bf16(w->type, w->data, w->rows * w->cols, dst, s), "dequant");
+         },
+         1, kOpDequant, 0.0, "dequant (ahead) " + w->name};
+    o.stream = 2;
+    building_->push_back(o);
+    prefetched_[w] = {dst, ready};
+  }
+  add_record(ready, 2);
 }
 
 cudaEvent_t StepPlanner::plan_event() {
@@ -366,13 +408,18 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
     return;
   }
   if (!w0->data || (w1 && !w1->data)) fail(DCPP_ERR_STATE, "internal: mixed packed / raw weights in " + w0->name);
-  const bool expand0 = w0->type != kTypeBF16, expand1 = w1 && w1->type != kTypeBF16;
+  // Weights expanded ahead (add_prefetch): read the expansion, after it is done.
+  const auto pf0 = prefetched_.find(w0);
+  const auto pf1 = w1 ? prefetched_.find(w1) : prefetched_.end();
+  const bool ahead0 = pf0 != prefetched_.end(), ahead1 = pf1 != prefetched_.end();
+  cudaEvent_t ahead_ready[2] = {ahead0 ? pf0->second.ready : nullptr, ahead1 ? pf1->second.ready : nullptr};
+  const bool expand0 = w0->type != kTypeBF16 && !ahead0, expand1 = w1 && w1->type != kTypeBF16 && !ahead1;
   const int pair_idx = scratch_pair_;
   if (expand0 || expand1) scratch_pair_ = (scratch_pair_ + 1) % n_scratch_;
   uint16_t* const* sc = wscratch_[pair_idx];
-  const uint16_t* b0 = expand0 ? sc[0] : reinterpret_cast<const uint16_t*>(w0->data);
+  const uint16_t* b0 = ahead0 ? pf0->second.dst : expand0 ? sc[0] : reinterpret_cast<const uint16_t*>(w0->data);
   const uint16_t* b1 = b0;
-  if (w1) b1 = expand1 ? sc[1] : reinterpret_cast<const uint16_t*>(w1->data);
+  if (w1) b1 = ahead1 ? pf1->second.dst : expand1 ? sc[1] : reinterpret_cast<const uint16_t*>(w1->data);
   int64_t a_rows = 0;
   for (auto& g : groups) a_rows = std::max<int64_t>(a_rows, g.row0 + g.rows);
   auto st = std::make_shared<std::array<CUtensorMap, 3>>();
@@ -437,6 +484,10 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
   for (size_t p = 0; p < pieces.size(); ++p) {
     if (before_piece) before_piece(static_cast<int>(p));
     if (p == 0 && ready) add_wait(ready, 0);
+    if (p == 0) {
+      if (ahead_ready[0]) add_wait(ahead_ready[0], 0);
+      if (ahead_ready[1] && ahead_ready[1] != ahead_ready[0]) add_wait(ahead_ready[1], 0);
+    }
     const auto& pg = pieces[p];
     GemmArgs args{};
     args.N = static_cast<int32_t>(N);
@@ -488,7 +539,7 @@ void StepPlanner::run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph) {
   last_ops_ = &ops;
   auto issue = [&]() {
     if (!profiling_) {
-      for (auto& o : ops) o.fn(o.stream ? side_ : s);
+      for (auto& o : ops) o.fn(op_stream(o.stream));
       return;
     }
     if (ev_.size() < 2 * ops.size()) {
@@ -504,7 +555,7 @@ void StepPlanner::run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph) {
     cuda_check(cudaStreamIsCapturing(s, &cs), "cudaStreamIsCapturing");
     const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
     for (size_t i = 0; i < ops.size(); ++i) {
-      cudaStream_t os = ops[i].stream ? side_ : s;
+      cudaStream_t os = op_stream(ops[i].stream);
       if (!ops[i].timed) {  // stream record / wait
         ops[i].fn(os);
         continue;

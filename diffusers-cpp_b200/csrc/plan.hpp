@@ -81,17 +81,26 @@ class StepPlanner {
     int kind = kOpOther;   // ProfileKind
     double flops = 0.0;    // algorithmic FLOPs of the op
     std::string tag;       // what the op is (profile dumps)
-    int stream = 0;        // 0: the context's stream, 1: the side stream
+    int stream = 0;        // 0: the context's stream, 1: the side stream, 2: the expansion stream
     bool timed = true;     // false for stream records / waits (not profiled)
   };
 
-  // Start / finish building one op list: the side stream joins the list at
-  // its start and rejoins the main stream at its end (a captured graph must
+  // Start / finish building one op list: the side streams join the list at
+  // its start and rejoin the main stream at its end (a captured graph must
   // end on its origin stream).
   void begin_ops(std::vector<Op>& ops);
   void end_ops();
   // Allocate the bf16 expansion scratch (two pairs of s0 / s1 elements).
   void alloc_expansion_scratch(const std::function<void*(size_t)>& alloc, size_t s0, size_t s1);
+  // Block-ahead weight expansion: two sets of `elems` bf16 elements.
+  void alloc_prefetch_scratch(const std::function<void*(size_t)>& alloc, size_t elems);
+  // Expand the quantised (raw, not packed) weights of `ws` into prefetch set
+  // `set` on the expansion stream, starting when the main stream reaches
+  // this point of the plan; later GEMMs reading these weights use the
+  // expansion and wait for it.  The caller guarantees that every GEMM that
+  // read the set's previous contents precedes this point on the main stream.
+  void add_prefetch(const std::vector<const DevWeight*>& ws, int set);
+  cudaStream_t op_stream(int i) const { return i == 0 ? ctx_.stream : (i == 1 ? side_ : side2_); }
   void release_plan_events();
   void run_ops(std::vector<Op>& ops, cudaGraphExec_t* graph);
 
@@ -128,6 +137,14 @@ class StepPlanner {
   cudaEvent_t scratch_free_[kMaxScratch] = {};  // last GEMM that read the pair (null: none yet)
   cudaEvent_t plan_start_ = nullptr;                   // recorded on the main stream first in a plan
   cudaStream_t side_ = nullptr;
+  cudaStream_t side2_ = nullptr;  // block-ahead weight expansions
+  struct Prefetched {
+    uint16_t* dst;
+    cudaEvent_t ready;
+  };
+  std::map<const DevWeight*, Prefetched> prefetched_;  // of the op list being built
+  uint16_t* pf_scratch_[2] = {};
+  size_t pf_scratch_elems_ = 0;
   std::vector<cudaEvent_t> plan_events_;
   // f32 partials of K-split GEMMs (shared by every split launch of the
   // model's plans, which run in order on one stream).
