@@ -125,16 +125,68 @@ Flux2Transformer2DModel::~Flux2Transformer2DModel() {
     if (v->data) cudaFree(v->data);
 }
 
-void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks) {
+// Split `units` indivisible units over the ranks in proportion to `ratios`
+// (ShardingRuntime::compute_split_groups, ShardingRuntime.cpp:280-296): with
+// c_j = units * f_j / sum f, every rank first gets floor(c_j); the remaining
+// units go one by one to the ranks with the largest fractional parts (ties:
+// the later rank, as the even split does).  Equal ratios give the even split.
+std::vector<int64_t> plan_tensor_split(int64_t units, const std::vector<double>& ratios) {
+  const int n = static_cast<int>(ratios.size());
+  if (n < 1) fail(DCPP_ERR_INVALID_ARG, "tensor split: no ranks");
+  double sum = 0.0;
+  for (double f : ratios) {
+    if (!(f > 0.0) || !std::isfinite(f)) fail(DCPP_ERR_INVALID_ARG, "tensor split: ratios must be positive");
+    sum += f;
+  }
+  std::vector<int64_t> m(n);
+  std::vector<double> frac(n);
+  int64_t given = 0;
+  for (int j = 0; j < n; ++j) {
+    const double c = static_cast<double>(units) * ratios[j] / sum;
+    m[j] = static_cast<int64_t>(std::floor(c));
+    frac[j] = c - static_cast<double>(m[j]);
+    given += m[j];
+  }
+  for (int64_t left = units - given; left > 0; --left) {
+    int best = 0;
+    for (int j = 1; j < n; ++j)
+      if (frac[j] >= frac[best]) best = j;
+    ++m[best];
+    frac[best] = -1.0;
+  }
+  return m;
+}
+
+void Flux2Transformer2DModel::set_tensor_parallel(int rank, int nranks, const std::vector<double>& ratios) {
   if (nranks < 1 || rank < 0 || rank >= nranks) fail(DCPP_ERR_INVALID_ARG, "bad tensor-parallel rank");
+  if (nranks > 8) fail(DCPP_ERR_UNSUPPORTED, "tensor parallelism over at most 8 GPUs");
   for (auto* w : weights_)
     if (w->type >= 0) fail(DCPP_ERR_STATE, "set_tensor_parallel must come before set_param");
+  std::vector<double> f = ratios.empty() ? std::vector<double>(static_cast<size_t>(nranks), 1.0) : ratios;
+  if (static_cast<int>(f.size()) != nranks) fail(DCPP_ERR_INVALID_ARG, "tensor split: one ratio per rank");
   const int64_t H = cfg_.num_attention_heads;
   const int64_t F = cfg_.mlp_hidden();
-  if (H % nranks) fail(DCPP_ERR_UNSUPPORTED, "num_attention_heads must divide by the TP size");
-  if ((F / nranks) % 64 || F % nranks) fail(DCPP_ERR_UNSUPPORTED, "mlp hidden / TP size must be a multiple of 64");
+  if (F % 64) fail(DCPP_ERR_UNSUPPORTED, "mlp hidden must be a multiple of 64");
+  // Two ratio groups: whole heads (q / k / v rows, to_out columns) and MLP
+  // features in units of 64 (the gate / up interleave of the fused GEMM).
+  const auto heads = plan_tensor_split(H, f);
+  const auto mlp = plan_tensor_split(F / 64, f);
+  for (int j = 0; j < nranks; ++j)
+    if (heads[j] < 1 || mlp[j] < 1)
+      fail(DCPP_ERR_UNSUPPORTED, "tensor split leaves rank " + std::to_string(j) +
+                                     " without a head or 64 MLP features (" + std::to_string(H) + " heads over " +
+                                     std::to_string(nranks) + " ranks)");
+  int64_t h0 = 0, u0 = 0;
+  for (int j = 0; j < rank; ++j) {
+    h0 += heads[j];
+    u0 += mlp[j];
+  }
   rank_ = rank;
   nranks_ = nranks;
+  h0_ = h0;
+  hn_ = heads[rank];
+  f0_ = u0 * 64;
+  fn_ = mlp[rank] * 64;
   build_registry();
 }
 
@@ -145,12 +197,17 @@ void Flux2Transformer2DModel::build_registry() {
   D_ = cfg_.inner_dim();
   F_ = cfg_.mlp_hidden();
   H_ = cfg_.num_attention_heads;
-  Dl_ = D_ / nranks_;
-  Fl_ = F_ / nranks_;
-  Hl_ = H_ / nranks_;
+  if (nranks_ == 1) {
+    h0_ = f0_ = 0;
+    hn_ = H_;
+    fn_ = F_;
+  }
+  Hl_ = hn_;
+  Dl_ = hn_ * cfg_.attention_head_dim;
+  Fl_ = fn_;
   const int64_t D = D_, F = F_, Dl = Dl_, Fl = Fl_;
+  const int64_t d0 = h0_ * cfg_.attention_head_dim, f0 = f0_;  // this rank's first q/k/v row and MLP feature
   const int64_t tg = cfg_.timestep_guidance_channels;
-  const int r = rank_;
 
   auto init = [&](DevWeight& w, const std::string& name, int64_t rows, int64_t cols, std::set<std::string> parts) {
     w = DevWeight();
@@ -188,14 +245,14 @@ void Flux2Transformer2DModel::build_registry() {
   auto full_cols = [](int64_t c) { return Cols{{0, c, 0}}; };
   // Rows of a [D, *] head-major projection kept by this rank, placed at region g.
   auto head_rows = [=](int g) {
-    return RowMap([=](int64_t i) { return (i >= r * Dl && i < (r + 1) * Dl) ? g * Dl + (i - r * Dl) : -1; });
+    return RowMap([=](int64_t i) { return (i >= d0 && i < d0 + Dl) ? g * Dl + (i - d0) : -1; });
   };
   // Rows of a [F, *] gate/up projection kept by this rank, interleaved in
   // 64-row blocks (gate block j, up block j, ...) after `base` rows.
   auto mlp_rows = [=](int64_t base, bool up) {
     return RowMap([=](int64_t i) {
-      if (i < r * Fl || i >= (r + 1) * Fl) return int64_t(-1);
-      const int64_t j = i - r * Fl;
+      if (i < f0 || i >= f0 + Fl) return int64_t(-1);
+      const int64_t j = i - f0;
       return base + (j / 64) * 128 + (up ? 64 : 0) + (j % 64);
     });
   };
@@ -240,7 +297,7 @@ void Flux2Transformer2DModel::build_registry() {
       for (int g = 0; g < 3; ++g)
         reg(p + stream_qkv[s][g] + ".weight", &blk.qkv[s], std::string(1, "qkv"[g]), D, D, head_rows(g), full_cols(D));
       init(blk.out[s], p + stream_out[s] + ".weight", D, Dl, {"all"});
-      reg(p + stream_out[s] + ".weight", &blk.out[s], "all", D, D, ident, Cols{{r * Dl, Dl, 0}});
+      reg(p + stream_out[s] + ".weight", &blk.out[s], "all", D, D, ident, Cols{{d0, Dl, 0}});
       const std::string ff = p + stream_ff[s];
       init(blk.ff_in[s], ff + ".linear_in.weight", 2 * Fl, D, {"gate", "up"});
       // fused GGUF tensor [2F, D]: rows [0, F) gate, [F, 2F) up (GGUFLoaderVisitor.cpp:370-408)
@@ -264,7 +321,7 @@ void Flux2Transformer2DModel::build_registry() {
       reg(ff + ".linear_in_gate.weight", &blk.ff_in[s], "gate", F, D, mlp_rows(0, false), full_cols(D));
       reg(ff + ".linear_in_up.weight", &blk.ff_in[s], "up", F, D, mlp_rows(0, true), full_cols(D));
       init(blk.ff_out[s], ff + ".linear_out.weight", D, Fl, {"all"});
-      reg(ff + ".linear_out.weight", &blk.ff_out[s], "all", D, F, ident, Cols{{r * Fl, Fl, 0}});
+      reg(ff + ".linear_out.weight", &blk.ff_out[s], "all", D, F, ident, Cols{{f0, Fl, 0}});
       initv(blk.norm_q[s], p + nq[s] + ".weight", cfg_.attention_head_dim);
       initv(blk.norm_k[s], p + nk[s] + ".weight", cfg_.attention_head_dim);
     }
@@ -303,7 +360,7 @@ void Flux2Transformer2DModel::build_registry() {
       DevWeight* w = &blk.out;
       const std::string fname = p + "to_out.weight";
       // fused GGUF tensor [D, D + F]: columns attn | mlp (GGUFLoaderVisitor.cpp:331-368)
-      setters_[fname] = [this, w, D, F, Dl, Fl, r, fname](int type, const std::vector<int64_t>& shape,
+      setters_[fname] = [this, w, D, F, Dl, Fl, d0, f0, fname](int type, const std::vector<int64_t>& shape,
                                                           const void* data, size_t nbytes) {
         if (shape.size() != 2 || shape[0] != D || shape[1] != D + F)
           fail(DCPP_ERR_INVALID_ARG, "Error while loading Tensor '" + fname + "': Parameter shape mismatch: expected " +
@@ -311,12 +368,12 @@ void Flux2Transformer2DModel::build_registry() {
         if (nbytes != row_bytes_of(type, D + F) * D) fail(DCPP_ERR_INVALID_ARG, "Tensor '" + fname + "': byte size mismatch");
         const uint8_t* src = static_cast<const uint8_t*>(data);
         auto id = [](int64_t i) { return i; };
-        place_rows(*w, "attn", type, shape, src, id, Cols{{r * Dl, Dl, 0}});
-        place_rows(*w, "mlp", type, shape, src, id, Cols{{D + r * Fl, Fl, Dl}});
+        place_rows(*w, "attn", type, shape, src, id, Cols{{d0, Dl, 0}});
+        place_rows(*w, "mlp", type, shape, src, id, Cols{{D + f0, Fl, Dl}});
       };
     }
-    reg(p + "to_out.attn.weight", &blk.out, "attn", D, D, ident, Cols{{r * Dl, Dl, 0}});
-    reg(p + "to_out.mlp.weight", &blk.out, "mlp", D, F, ident, Cols{{r * Fl, Fl, Dl}});
+    reg(p + "to_out.attn.weight", &blk.out, "attn", D, D, ident, Cols{{d0, Dl, 0}});
+    reg(p + "to_out.mlp.weight", &blk.out, "mlp", D, F, ident, Cols{{f0, Fl, Dl}});
     initv(blk.norm_q, p + "norm_q.weight", cfg_.attention_head_dim);
     initv(blk.norm_k, p + "norm_k.weight", cfg_.attention_head_dim);
   }
@@ -1427,6 +1484,38 @@ dcpp_status dcpp_flux2_profile(dcpp_flux2* m, int kind, double* ms, double* flop
 dcpp_status dcpp_flux2_set_tensor_parallel(dcpp_flux2* m, int rank, int nranks) {
   return model_call(m, "dcpp_flux2_set_tensor_parallel",
                     [&](dcpp::Flux2Transformer2DModel& mm) { mm.set_tensor_parallel(rank, nranks); });
+}
+
+dcpp_status dcpp_flux2_set_tensor_split(dcpp_flux2* m, int rank, int nranks, const float* ratios) {
+  return model_call(m, "dcpp_flux2_set_tensor_split", [&](dcpp::Flux2Transformer2DModel& mm) {
+    std::vector<double> f;
+    if (ratios) f.assign(ratios, ratios + std::max(nranks, 0));
+    mm.set_tensor_parallel(rank, nranks, f);
+  });
+}
+
+dcpp_status dcpp_flux2_shard(dcpp_flux2* m, int64_t* head0, int64_t* heads, int64_t* mlp0, int64_t* mlp_features) {
+  return model_call(m, "dcpp_flux2_shard", [&](dcpp::Flux2Transformer2DModel& mm) {
+    int64_t a = 0, b = 0, c = 0, d = 0;
+    mm.shard(&a, &b, &c, &d);
+    if (head0) *head0 = a;
+    if (heads) *heads = b;
+    if (mlp0) *mlp0 = c;
+    if (mlp_features) *mlp_features = d;
+  });
+}
+
+dcpp_status dcpp_tp_plan_split(int64_t units, int nranks, const float* ratios, int64_t* out_units) {
+  if (units < 0 || nranks < 1 || !out_units) return DCPP_ERR_INVALID_ARG;
+  try {
+    std::vector<double> f(static_cast<size_t>(nranks), 1.0);
+    if (ratios) f.assign(ratios, ratios + nranks);
+    const auto m = dcpp::plan_tensor_split(units, f);
+    for (int j = 0; j < nranks; ++j) out_units[j] = m[j];
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    return e.status;
+  }
 }
 
 dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float* sigmas) {

@@ -63,7 +63,17 @@ class Flux2Transformer2DModel : public StepPlanner {
   ~Flux2Transformer2DModel();
 
   const Flux2Config& config() const { return cfg_; }
-  void set_tensor_parallel(int rank, int nranks);
+  // Shard over nranks GPUs: rank keeps a contiguous run of heads and of MLP
+  // features, in proportion to `ratios` (one per rank; empty = even), split
+  // by plan_tensor_split.
+  void set_tensor_parallel(int rank, int nranks, const std::vector<double>& ratios = {});
+  // This rank's shard: first head, heads, first MLP feature, MLP features.
+  void shard(int64_t* h0, int64_t* hn, int64_t* f0, int64_t* fn) const {
+    *h0 = h0_;
+    *hn = hn_;
+    *f0 = f0_;
+    *fn = fn_;
+  }
   void set_param(const std::string& name, int type, const std::vector<int64_t>& shape, const void* data,
                  size_t nbytes);
   std::vector<std::string> missing() const;
@@ -142,6 +152,7 @@ class Flux2Transformer2DModel : public StepPlanner {
   Flux2Config cfg_;
   bool host_only_ = false;
   int rank_ = 0, nranks_ = 1;
+  int64_t h0_ = 0, hn_ = 0, f0_ = 0, fn_ = 0;  // this rank's heads [h0, h0 + hn), MLP features [f0, f0 + fn)
   int64_t D_ = 0, F_ = 0, H_ = 0, Dl_ = 0, Fl_ = 0, Hl_ = 0;
 
   // Parameters.
@@ -204,6 +215,11 @@ class Flux2Transformer2DModel : public StepPlanner {
   // the default stays per projection.
   bool block_prefetch_ = false;
 };
+
+// Units per rank of a tensor-parallel split in proportion to `ratios`
+// (floor, then the remainder by largest fractional part, ties to the later
+// rank).
+std::vector<int64_t> plan_tensor_split(int64_t units, const std::vector<double>& ratios);
 
 // FlowMatchEulerDiscreteScheduler (default: shift 1, no dynamic shifting,
 // no terminal stretch, not inverted) with the pipeline's sigmas 1 - i/n.

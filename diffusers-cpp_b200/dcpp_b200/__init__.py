@@ -150,6 +150,9 @@ _SIGNATURES = {
     "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
     "dcpp_flux2_set_tensor_parallel": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
+    "dcpp_flux2_set_tensor_split": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "dcpp_flux2_shard": (ctypes.c_int, [_vp, _c_i64p, _c_i64p, _c_i64p, _c_i64p]),
+    "dcpp_tp_plan_split": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int, _vp, _c_i64p]),
     "dcpp_flux2_create_host": (ctypes.c_int, [ctypes.POINTER(Flux2ConfigC), ctypes.POINTER(_vp)]),
     "dcpp_qwen3_config_default": (None, [ctypes.POINTER(Qwen3ConfigC)]),
     "dcpp_qwen3_config_from_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(Qwen3ConfigC)]),
@@ -429,7 +432,7 @@ class Flux2Model:
     are assembled and sharded exactly as on a device, but stay on the host
     (``read_param``) and the model cannot execute."""
 
-    def __init__(self, ctx: Optional[Context], cfg, tp_rank: int = 0, tp_size: int = 1):
+    def __init__(self, ctx: Optional[Context], cfg, tp_rank: int = 0, tp_size: int = 1, tp_split=None):
         self.ctx = ctx
         self.cfg = cfg
         c = config_to_c(cfg)
@@ -442,7 +445,10 @@ class Flux2Model:
             ctx.check(lib().dcpp_flux2_create(ctx.h, ctypes.byref(c), ctypes.byref(h)), "flux2_create")
             ctx._children.add(self)
         self.h = h
-        if tp_size > 1:
+        if tp_split is not None:
+            arr = (ctypes.c_float * tp_size)(*[float(f) for f in tp_split])
+            self._check(lib().dcpp_flux2_set_tensor_split(h, tp_rank, tp_size, arr), "set_tensor_split")
+        elif tp_size > 1:
             self._check(lib().dcpp_flux2_set_tensor_parallel(h, tp_rank, tp_size), "set_tensor_parallel")
 
     @classmethod
@@ -469,6 +475,12 @@ class Flux2Model:
     def _run(self, fn, *args):
         # host-only models have no context (their compute calls fail in the library)
         return self.ctx._call(fn, *args) if self.ctx is not None else fn(*args)
+
+    def shard(self):
+        """(first head, heads, first MLP feature, MLP features) of this rank."""
+        v = [ctypes.c_int64() for _ in range(4)]
+        self._check(lib().dcpp_flux2_shard(self.h, *[ctypes.byref(x) for x in v]), "shard")
+        return tuple(x.value for x in v)
 
     def read_param(self, name: str):
         """(ggml type, (rows, cols), uint8 array) of an assembled parameter."""
@@ -685,6 +697,16 @@ class GGUFFile:
             else:
                 out[k] = (GGUF_VALUE_TYPES.get(t.value, t.value), self._get(k, t.value, -1))
         return out
+
+
+def tp_plan_split(units: int, nranks: int, ratios=None):
+    """The sharding planner's split of `units` over nranks (dcpp_tp_plan_split)."""
+    out = (ctypes.c_int64 * nranks)()
+    arr = (ctypes.c_float * nranks)(*[float(f) for f in ratios]) if ratios is not None else None
+    st = lib().dcpp_tp_plan_split(units, nranks, arr, out)
+    if st != DCPP_OK:
+        raise DcppError(st, "tp_plan_split")
+    return list(out)
 
 
 def flow_match_schedule(n: int, shift: float = 1.0):

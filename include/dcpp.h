@@ -366,11 +366,32 @@ dcpp_status dcpp_tp_init(dcpp_ctx* ctx, int rank, int nranks, const void* nccl_i
  * DCPP_TYPE_* (F32 or BF16). */
 dcpp_status dcpp_allreduce(dcpp_ctx* ctx, void* d_buf, int64_t count, int dtype);
 
-/* Shard a model created on this context: rank keeps heads/nranks heads and
- * mlp_hidden/nranks MLP features.  Must be called before set_param.  The
- * split follows ShardingRuntime.cpp:47-57 (column-parallel q/k/v/gate/up,
- * row-parallel out projections, one all-reduce per row-parallel site). */
+/* Shard a model created on this context over nranks GPUs with equal ratios
+ * (heads and MLP features split as evenly as whole heads and 64-feature
+ * units allow; see dcpp_flux2_set_tensor_split).  Must be called before
+ * set_param.  The layout follows ShardingRuntime.cpp:47-57 (column-parallel
+ * q/k/v/gate/up, row-parallel out projections, one all-reduce per
+ * row-parallel site). */
 dcpp_status dcpp_flux2_set_tensor_parallel(dcpp_flux2* model, int rank, int nranks);
+
+/* The sharding planner's uneven split (tensor_split ratios,
+ * ShardingRuntime.cpp:280-296 and :296-528): rank keeps a contiguous run of
+ * heads and of MLP features (in units of 64) in proportion to
+ * ratios[0..nranks) (NULL = equal ratios, i.e. dcpp_flux2_set_tensor_parallel,
+ * which now also accepts head counts that do not divide by nranks).  Each
+ * ratio group is rounded like the reference planner: floor of the
+ * proportional share, then the remaining units one by one to the ranks with
+ * the largest fractional parts, ties to the later rank.  A rank left without
+ * a head or without 64 features gives DCPP_ERR_UNSUPPORTED.  Before
+ * set_param. */
+dcpp_status dcpp_flux2_set_tensor_split(dcpp_flux2* model, int rank, int nranks, const float* ratios);
+/* This rank's shard: heads [head0, head0 + heads), MLP features
+ * [mlp0, mlp0 + mlp_features) (outputs may be NULL). */
+dcpp_status dcpp_flux2_shard(dcpp_flux2* model, int64_t* head0, int64_t* heads, int64_t* mlp0,
+                             int64_t* mlp_features);
+/* The planner's rounding alone: `units` split over nranks in proportion to
+ * ratios (NULL = equal) into out_units[nranks]. */
+dcpp_status dcpp_tp_plan_split(int64_t units, int nranks, const float* ratios, int64_t* out_units);
 
 /* A model that assembles parameters on the host only: set_param and
  * set_tensor_parallel work as on a device model (same checks, same shard

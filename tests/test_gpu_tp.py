@@ -28,11 +28,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def run_ranks(tmp_path, heads, wtype, comm, pieces=2, n=2, timeout=600):
+def run_ranks(tmp_path, heads, wtype, comm, pieces=2, n=2, timeout=600, ratios="even"):
     out = tmp_path / "tp.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(HERE, "tp_gpu_worker.py"), str(out), str(heads), str(wtype), comm, str(pieces)]
+           os.path.join(HERE, "tp_gpu_worker.py"), str(out), str(heads), str(wtype), comm, str(pieces), ratios]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     p = subprocess.Popen(cmd, env=env, start_new_session=True, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
     try:
@@ -58,6 +58,20 @@ def test_tp2_matches_oracle(tmp_path, heads, wtype, comm, pieces):
     r = run_ranks(tmp_path, heads, wtype, comm, pieces)
     assert r["ranks_identical"], r
     assert r["replay_identical"], r
+    assert r["forward_rel"] < V_TOL, r
+    assert r["denoise_rel"] < LAT_TOL, r
+    assert r["resident_rel"] < LAT_TOL, r
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("heads,ratios,comm", [(6, "2,1", "peer"), (5, "even", "peer"), (6, "1,2", "nccl")],
+                         ids=["6_heads_2_to_1_peer", "5_heads_even_peer", "6_heads_1_to_2_nccl"])
+def test_tp2_uneven_split_matches_oracle(tmp_path, heads, ratios, comm):
+    """The planner's uneven tensor_split (ratio-rounded heads and MLP units,
+    dcpp_flux2_set_tensor_split): each rank computes a different number of
+    heads, the exchange still sums full rows."""
+    r = run_ranks(tmp_path, heads, fo.GGML_Q8_0, comm, 1, ratios=ratios)
+    assert r["ranks_identical"], r
     assert r["forward_rel"] < V_TOL, r
     assert r["denoise_rel"] < LAT_TOL, r
     assert r["resident_rel"] < LAT_TOL, r

@@ -36,6 +36,8 @@ def main():
     os.environ["DCPP_TP_COMM"] = comm  # "peer" (default) or "nccl"; read when a model is created
     if len(sys.argv) > 5:
         os.environ["DCPP_TP_PIECES"] = sys.argv[5]  # row pieces of the peer exchange (1 or 2)
+    # tensor_split ratios ("2,1"), or "even"
+    ratios = None if len(sys.argv) <= 6 or sys.argv[6] == "even" else [float(x) for x in sys.argv[6].split(",")]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -55,7 +57,7 @@ def main():
     ni = gh * gw
     res = {}
 
-    m = dcpp_b200.Flux2Model(ctx, c, tp_rank=rank, tp_size=world)
+    m = dcpp_b200.Flux2Model(ctx, c, tp_rank=rank, tp_size=world, tp_split=ratios)
     m.load_params(params)
     m.prepare(B, ni, nt, use_graph=True)
     out = torch.empty(B, ni, c.in_channels, dtype=torch.float32)
@@ -67,7 +69,7 @@ def main():
     # model without the guidance embedder, same other weights.
     c_ng = synth.Flux2Cfg(**{**c.__dict__, "guidance_embeds": False})
     params_ng = {k: v for k, v in params.items() if "guidance_embedder" not in k}
-    m = dcpp_b200.Flux2Model(ctx, c_ng, tp_rank=rank, tp_size=world)
+    m = dcpp_b200.Flux2Model(ctx, c_ng, tp_rank=rank, tp_size=world, tp_split=ratios)
     m.load_params(params_ng)
     m.prepare(B, ni, nt, use_graph=True)
     lat = torch.empty_like(hid)

@@ -77,11 +77,37 @@ def deinterleave64(y: torch.Tensor):
     return z[..., 0, :].flatten(-2), z[..., 1, :].flatten(-2)
 
 
-def expected_shards(c, w: fo.Weights, rank: int, n: int) -> Dict[str, torch.Tensor]:
+def plan_split(units: int, ratios) -> List[int]:
+    """The sharding planner's rounding (ShardingRuntime.cpp:280-296), restated:
+    floor(units * f_j / sum f), then the remaining units one by one to the
+    ranks with the largest fractional parts (ties: the later rank)."""
+    s = sum(ratios)
+    c = [units * f / s for f in ratios]
+    m = [int(x // 1) for x in c]
+    frac = [x - mi for x, mi in zip(c, m)]
+    for _ in range(units - sum(m)):
+        best = 0
+        for j in range(1, len(ratios)):
+            if frac[j] >= frac[best]:
+                best = j
+        m[best] += 1
+        frac[best] = -1.0
+    return m
+
+
+def shard_of(c, rank: int, n: int, ratios=None):
+    """(first head, heads, first MLP feature, MLP features) of `rank`."""
+    ratios = ratios or [1.0] * n
+    heads = plan_split(c.num_attention_heads, ratios)
+    units = plan_split(c.mlp_hidden // 64, ratios)
+    return sum(heads[:rank]), heads[rank], 64 * sum(units[:rank]), 64 * units[rank]
+
+
+def expected_shards(c, w: fo.Weights, rank: int, n: int, ratios=None) -> Dict[str, torch.Tensor]:
     """Float weights each shard must hold, sliced from the full (unsharded) weights."""
     D, F = c.inner_dim, c.mlp_hidden
-    Dl, Fl = D // n, F // n
-    hs, fs = slice(rank * Dl, (rank + 1) * Dl), slice(rank * Fl, (rank + 1) * Fl)
+    h0, hn, f0, fn = shard_of(c, rank, n, ratios)
+    hs, fs = slice(h0 * 128, (h0 + hn) * 128), slice(f0, f0 + fn)
     out = {}
     for name in weight_names(c):
         if not (name.startswith("transformer_blocks.") or name.startswith("single_transformer_blocks.")):
@@ -121,10 +147,11 @@ class TPOracle(fo.Flux2Oracle):
     the ranks and returns it."""
 
     def __init__(self, cfg: fo.Config, shards: Dict[str, torch.Tensor], n: int,
-                 allreduce: Callable[[torch.Tensor], torch.Tensor]):
+                 allreduce: Callable[[torch.Tensor], torch.Tensor], heads: int = 0):
         super().__init__(cfg, {}, dtype=torch.float64)
         self.s = shards
         self.n = n
+        self.hl = heads or cfg.num_attention_heads // n  # this rank's heads
         self.allreduce = allreduce
         # Replicated weights resolve through the base class's Weights cache.
         self.w.cache.update({k: v for k, v in shards.items()
@@ -132,8 +159,8 @@ class TPOracle(fo.Flux2Oracle):
 
     def double_block(self, i, hs, ehs, mod_img, mod_txt, cos, sin):
         c, S = self.cfg, self.s
-        eps, Hl = c.eps, c.num_attention_heads // self.n
-        Dl = c.inner_dim // self.n
+        eps, Hl = c.eps, self.hl
+        Dl = Hl * c.attention_head_dim
         p = f"transformer_blocks.{i}."
         sh, sc, g, sh2, sc2, g2 = mod_img[:, None, :].chunk(6, dim=-1)
         csh, csc, cg, csh2, csc2, cg2 = mod_txt[:, None, :].chunk(6, dim=-1)
@@ -168,8 +195,8 @@ class TPOracle(fo.Flux2Oracle):
 
     def single_block(self, i, hs, mod, cos, sin):
         c, S = self.cfg, self.s
-        eps, Hl = c.eps, c.num_attention_heads // self.n
-        Dl = c.inner_dim // self.n
+        eps, Hl = c.eps, self.hl
+        Dl = Hl * c.attention_head_dim
         p = f"single_transformer_blocks.{i}.attn."
         sh, sc, g = mod[:, None, :].chunk(3, dim=-1)
         n = (1.0 + sc) * fo.layer_norm(hs, eps) + sh
