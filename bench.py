@@ -766,6 +766,56 @@ def run_qwen3(args):
 VAE_METRIC = "Flux2 VAE decode images/s (1024x1024 by default)"
 
 
+def vae_cpu_sample(packed, threads, steps=1, warmup=0):
+    """The whole VAE decode of one image through the CPU restatement
+    (oracle/vae_oracle.py, float32, all host threads); returns (seconds per
+    image, description)."""
+    import torch
+
+    import vae_oracle as vo
+    from dcpp_b200 import synth
+
+    torch.set_num_threads(threads)
+    c = synth.VAECfg()
+    params = synth.make_vae_params(c, seed=0)
+    ocfg = vo.VAEConfig(**{k: getattr(c, k) for k in vo.VAEConfig.__dataclass_fields__ if hasattr(c, k)})
+    o = vo.VAEDecoderOracle(ocfg, params, dtype=torch.float32)
+    lat = synth.make_vae_latents(c, 1, packed, packed, seed=1)
+    o.decode_packed(lat[:, :4], 2, 2)  # dequantise / convert every weight once
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        o.decode_packed(lat, packed, packed)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    px = 16 * packed
+    desc = (f"CPU restatement (oracle/vae_oracle.py, torch float32, {threads} threads) of the Flux2 VAE decode of one "
+            f"{px} x {px} image, the whole decode timed; ggml CPU path unavailable (submodule not vendored)")
+    return statistics.median(times), desc
+
+
+def run_vae_reference(args):
+    """--impl reference --config vae: one timed decode (after none or one
+    warm-up) through the CPU restatement; rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    steps, warmup = 1, min(args.warmup, 1)
+    sec, desc = vae_cpu_sample(args.vae_packed, threads, steps, warmup)
+    value = 1.0 / sec
+    line = {
+        "impl": "reference", "metric": VAE_METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "extrapolated": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"vae: Flux2 VAE decode, {args.vae_packed} x {args.vae_packed} packed tokens",
+                   "global_batch": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_vae(args):
     """The pipeline's VAE decode (Flux2KleinPipeline::decode, untiled) of one
     1024 x 1024 image from 64 x 64 packed tokens, the Flux2 VAE config
@@ -867,6 +917,11 @@ def run_vae(args):
         "clocks": clk,
         "load_seconds": load_s,
     }
+    if not args.no_cpu_baseline and not args.vae_tile:
+        threads = os.cpu_count() or 1
+        sec, desc = vae_cpu_sample(args.vae_packed, threads)
+        line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "images/s", "cores": threads, "kind": "port",
+                                "sample": desc}
     print(json.dumps(line), flush=True)
     m.close()
     ctx.close()
@@ -877,6 +932,49 @@ GEMM_METRIC = "quantized GEMM TFLOP/s (config-5 sweep)"
 GEMM_TYPES = {"Q4_K": 12, "Q8_0": 8, "F16": 1, "BF16": 30}
 GEMM_SWEEP_M = (256, 1024, 4096, 8192)
 GEMM_SWEEP_NK = ((3072, 3072), (9216, 3072), (3072, 9216), (12288, 4096))
+
+
+def run_gemm_reference(args):
+    """--impl reference --config 5: the CPU restatement of the quantised GEMM
+    (dequantisation by oracle/dequant.c, then a torch float32 matmul on all
+    host threads) over the Q4_K rows of the sweep (every M, every (N, K));
+    value = total FLOP / total time, as the GPU arm reports it.  Rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import torch
+
+    import flux2_oracle as fo
+    from dcpp_b200 import quant
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    tot_fl = tot_s = 0.0
+    for (N, K) in GEMM_SWEEP_NK:
+        w = torch.randn(N, K, generator=g) / K ** 0.5
+        wq = quant.quantize(w, GEMM_TYPES["Q4_K"]).numpy()
+        for M in GEMM_SWEEP_M:
+            x = torch.randn(M, K, generator=g).to(torch.bfloat16).float()
+            t0 = time.perf_counter()
+            wd = torch.from_numpy(fo.dequant(GEMM_TYPES["Q4_K"], wq, N * K).reshape(N, K))
+            y = x @ wd.t()
+            tot_s += time.perf_counter() - t0
+            tot_fl += 2.0 * M * N * K
+            del y, wd
+    value = tot_fl / tot_s / 1e12
+    desc = (f"CPU restatement (oracle/dequant.c dequantisation + torch float32 matmul, {threads} threads) of the "
+            f"config-5 sweep's Q4_K shapes (M in {list(GEMM_SWEEP_M)}, (N, K) in {list(GEMM_SWEEP_NK)}); ggml CPU "
+            f"path unavailable (submodule not vendored)")
+    line = {
+        "impl": "reference", "metric": GEMM_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": 1, "warmup": 0, "ms_per_step": tot_s * 1e3, "higher_is_better": True, "extrapolated": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config5: quantized GEMM sweep, Q4_K shapes", "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def run_gemm_sweep(args):
@@ -993,13 +1091,11 @@ def main():
         return run_qwen3(args)
     if args.config == "5":
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU reference arm in this bench"}))
-            return 0
+            return run_gemm_reference(args)
         return run_gemm_sweep(args)
     if args.config == "vae":
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the VAE decode has no CPU reference arm in this bench"}))
-            return 0
+            return run_vae_reference(args)
         return run_vae(args)
     if args.impl == "reference":
         return run_reference(args)

@@ -108,6 +108,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   if (const char* e = getenv("DCPP_FUSED_DEQUANT")) fused_dequant_ = std::string(e) == "1";
   if (const char* e = getenv("DCPP_TP_COMM")) tp_peer_ = std::string(e) != "nccl";
   if (const char* e = getenv("DCPP_TP_PIECES")) tp_pieces_env_ = std::string(e) == "1" ? 1 : 2;
+  if (const char* e = getenv("DCPP_TP_PULL")) tp_pull_ = std::string(e) == "1";
   if (const char* e = getenv("DCPP_BLOCK_PREFETCH")) block_prefetch_ = std::string(e) == "1";
   build_registry();
 }
@@ -682,7 +683,10 @@ void Flux2Transformer2DModel::build_plan() {
     chunk_ = (piece_rows_ + nranks_ - 1) / nranks_;
     auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
     const size_t off_recv = up(R * D * 2);
-    const size_t off_flags = off_recv + up(static_cast<size_t>(nranks_) * tp_pieces_ * chunk_ * D * 2);
+    // recv: the push form's receive slots, or the pull form's full-row partials.
+    const size_t recv_bytes = std::max<size_t>(static_cast<size_t>(nranks_) * tp_pieces_ * chunk_ * D * 2,
+                                               static_cast<size_t>(R) * D * 2);
+    const size_t off_flags = off_recv + up(recv_bytes);
     sym_.open(ctx_, off_flags + 512);
     for (int j = 0; j < nranks_; ++j) {
       a_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j]);
@@ -916,7 +920,16 @@ void Flux2Transformer2DModel::build_plan() {
       e.gate[0] = g0;
       e.gate[1] = g1;
       e.gate_bstride = bstride;
-      if (peer) {
+      if (peer && tp_pull_) {
+        // Pull form: the gated bf16 partial stays in this GPU's own memory
+        // (one piece of R rows owned by slot 0 = this buffer); the owners
+        // read it over NVLink in their LayerNorm.
+        e.peer_bf16[0] = recv_peer_[rank_];
+        e.chunk_rows = static_cast<int32_t>(R);
+        e.piece_rows = static_cast<int32_t>(R);
+        e.slot_rows = static_cast<int32_t>(R);
+        e.peer_slot = 0;
+      } else if (peer) {
         for (int j = 0; j < nranks_; ++j) e.peer_bf16[j] = recv_peer_[j];
         e.chunk_rows = static_cast<int32_t>(chunk_);
         e.piece_rows = static_cast<int32_t>(piece_rows_);
@@ -962,10 +975,15 @@ void Flux2Transformer2DModel::build_plan() {
         n.seg[k++] = sg;
       }
       n.n_segments = k;
-      n.slots = recv_peer_[rank_];
       n.n_slots = nranks_;
-      n.slot_stride = tp_pieces_ * chunk_ * D;
-      n.slot_row0 = own[0] - p * chunk_;  // slot row of source row r: p * chunk + (r - own[0])
+      if (tp_pull_) {  // every rank's full-row partial, read from its memory
+        for (int j = 0; j < nranks_; ++j) n.slot_ptr[j] = recv_peer_[j];
+        n.slot_row0 = 0;
+      } else {
+        n.slots = recv_peer_[rank_];
+        n.slot_stride = tp_pieces_ * chunk_ * D;
+        n.slot_row0 = own[0] - p * chunk_;  // slot row of source row r: p * chunk + (r - own[0])
+      }
       n.n_peer_out = 0;
       for (int j = 0; j < nranks_; ++j)
         if (j != rank_) n.y_peer[n.n_peer_out++] = a_peer_[j] + (n.y - a_);

@@ -190,6 +190,15 @@ class Flux2Transformer2DModel : public StepPlanner {
   // (side stream) overlaps the column-parallel GEMM of piece 0.  Chosen per
   // plan from the exchange size unless DCPP_TP_PIECES sets it.
   bool tp_peer_ = true;
+  // Pull form of the peer exchange (DCPP_TP_PULL=1): each
+  // row-parallel GEMM keeps its gated bf16 partial in local memory and the
+  // row owners read all ranks' partials over NVLink in the LayerNorm, so the
+  // GEMM is not held up by NVLink stores and the reads (ingress) overlap the
+  // all-gather stores (egress) of the same kernel.  Default (push form): the
+  // GEMM epilogue stores each partial into its owner's receive slot, which
+  // measured faster at 2 GPUs (the LayerNorm's remote reads cost more than
+  // the GEMM saves there).
+  bool tp_pull_ = false;
   int tp_pieces_ = 1;
   int tp_pieces_env_ = 0;
   PeerBuffer sym_;

@@ -48,10 +48,14 @@ struct NormArgs {
   // slots[s * slot_stride + (r - slot_row0) * ld_x], added in slot order;
   // the bf16 output row is also stored to y_peer[k] (k < n_peer_out, other
   // GPUs' buffers mapped into this process).
+  // With slot_ptr[0] set, slot s is instead slot_ptr[s] + (r - slot_row0) * ld_x
+  // (the pull form: each rank's full-row partials in its own memory, read
+  // over NVLink by the row's owner).
   const uint16_t* slots;
   int32_t n_slots;
   int64_t slot_stride;
   int64_t slot_row0;
+  const uint16_t* slot_ptr[8];
   int32_t n_peer_out;
   uint16_t* y_peer[7];
   // RMSNorm form (rms != 0): no mean subtraction, y = weight * x / rms(x)

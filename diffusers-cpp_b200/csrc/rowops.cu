@@ -37,6 +37,10 @@ __device__ __forceinline__ void add_bf16x4(float4& t, uint2 u) {
   t.z += __uint_as_float(u.y << 16); t.w += __uint_as_float(u.y & 0xFFFF0000u);
 }
 
+// Four bf16 of a slot load: the load itself (4-wide) or its half f (8-wide).
+__device__ __forceinline__ uint2 slot_half(uint2 u, int) { return u; }
+__device__ __forceinline__ uint2 slot_half(uint4 u, int f) { return f ? make_uint2(u.z, u.w) : make_uint2(u.x, u.y); }
+
 // kW elements (4 or 8) per thread and step: one or two float4 loads of x,
 // one 8- or 16-byte bf16 store per output buffer.
 template <int kThreads, int kVec, int kW>
@@ -60,33 +64,47 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
   const int ng = D / kW;
   const float4* x4 = reinterpret_cast<const float4*>(a.x + src * a.ld_x);
   const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + src * a.ld_x) : nullptr;
-  const uint16_t* sl = a.n_slots > 0 ? a.slots + (src - a.slot_row0) * a.ld_x : nullptr;
-  float4* xo4 = (a.resid || sl) ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
+  const bool slotted = a.n_slots > 0;
+  const int64_t srow = (src - a.slot_row0) * a.ld_x;
+  float4* xo4 = (a.resid || slotted) ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
 
   float4 v[kVec][kF4];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int idx = threadIdx.x + i * kThreads;
+    if (idx < ng) {
+      // The slot loads first (over NVLink in the pull form, so they must be
+      // in flight together): one kW-element (8- or 16-byte) load per slot.
+      OutT pv[8];
+      if (slotted) {
 #pragma unroll
-    for (int f = 0; f < kF4; ++f) {
-      if (idx < ng) {
+        for (int k = 0; k < 8; ++k) {
+          if (k < a.n_slots) {
+            const uint16_t* base = a.slot_ptr[0] ? a.slot_ptr[k] : a.slots + k * a.slot_stride;
+            pv[k] = reinterpret_cast<const OutT*>(base + srow)[idx];
+          }
+        }
+      }
+#pragma unroll
+      for (int f = 0; f < kF4; ++f) {
         float4 t = x4[idx * kF4 + f];
         if (r4) {
           const float4 r = r4[idx * kF4 + f];
           t.x += r.x; t.y += r.y; t.z += r.z; t.w += r.w;
         }
-        if (sl) {
-#pragma unroll 1
-          for (int k = 0; k < a.n_slots; ++k)
-            add_bf16x4(t, reinterpret_cast<const uint2*>(sl + k * a.slot_stride)[idx * kF4 + f]);
+        if (slotted) {  // the sums in slot order
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (k < a.n_slots) add_bf16x4(t, slot_half(pv[k], f));
         }
         if (xo4) xo4[idx * kF4 + f] = t;
         v[i][f] = t;
         sum += (t.x + t.y) + (t.z + t.w);
-      } else {
-        v[i][f] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    } else {
+#pragma unroll
+      for (int f = 0; f < kF4; ++f) v[i][f] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   sum = warp_sum(sum);
@@ -609,7 +627,11 @@ cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
   if (a.D % 4 != 0 || a.D > 8192 || (a.ld_x % 4) || (a.ld_y % 4)) return cudaErrorInvalidValue;
   if (a.n_slots < 0 || a.n_slots > 8 || (a.slot_stride % 8) || a.n_peer_out < 0 || a.n_peer_out > 7)
     return cudaErrorInvalidValue;
-  if (a.n_slots > 0 && (!a.slots || (reinterpret_cast<uintptr_t>(a.slots) & 15))) return cudaErrorInvalidValue;
+  if (a.n_slots > 0 && !a.slot_ptr[0] && (!a.slots || (reinterpret_cast<uintptr_t>(a.slots) & 15)))
+    return cudaErrorInvalidValue;
+  if (a.n_slots > 0 && a.slot_ptr[0])
+    for (int k = 0; k < a.n_slots; ++k)
+      if (!a.slot_ptr[k] || (reinterpret_cast<uintptr_t>(a.slot_ptr[k]) & 15)) return cudaErrorInvalidValue;
   int64_t rows = 0;
   for (int i = 0; i < a.n_segments; ++i) rows += a.seg[i].rows;
   if (rows == 0) return cudaSuccess;
