@@ -13,8 +13,8 @@ The GPU path (C ABI, bf16 operands, f32 accumulation) is compared with the
 float64 restatement in oracle/flux2_oracle.py.  The oracle runs its float64
 arithmetic on the GPU (torch's float64 kernels) only to finish in seconds;
 its weights come from the C dequantisation oracle.  Bars: per-step latent
-relative L2 <= 1e-2 (the north star's), noise prediction <= 3e-2; max-abs
-errors are printed."""
+relative L2 <= 1e-2 (the north star's), noise prediction <= 1e-2 (measured
+2.4-2.7e-3 on a B200); max-abs errors are printed."""
 import pytest
 import torch
 
@@ -25,7 +25,7 @@ from dcpp_b200 import synth
 pytestmark = pytest.mark.gpu
 
 LAT_TOL = 1e-2
-V_TOL = 3e-2
+V_TOL = 1e-2
 
 
 def oracle_cfg(c):
