@@ -48,16 +48,17 @@ def run_ranks(tmp_path, heads, wtype, comm, pieces=2, n=2, timeout=600, ratios="
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("heads,wtype,comm,pieces", [(4, fo.GGML_Q8_0, "peer", 2), (6, fo.GGML_Q4_K, "peer", 2),
                                                      (4, fo.GGML_Q8_0, "peer", 1), (4, fo.GGML_Q8_0, "nccl", 1),
-                                                     (6, fo.GGML_Q4_K, "nccl", 1), (4, fo.GGML_Q8_0, "push", 2),
-                                                     (6, fo.GGML_Q4_K, "push", 1)],
+                                                     (6, fo.GGML_Q4_K, "nccl", 1), (4, fo.GGML_Q8_0, "pull", 2),
+                                                     (6, fo.GGML_Q4_K, "pull", 1)],
                          ids=["q8_0_peer", "q4_k_bf16_shards_peer", "q8_0_peer_one_piece", "q8_0_nccl",
-                              "q4_k_bf16_shards_nccl", "q8_0_push", "q4_k_bf16_shards_push_one_piece"])
+                              "q4_k_bf16_shards_nccl", "q8_0_pull", "q4_k_bf16_shards_pull_one_piece"])
 def test_tp2_matches_oracle(tmp_path, heads, wtype, comm, pieces):
-    """peer: each GPU keeps its bf16 partial, the row owners read every GPU's
-    partial in their LayerNorm and store the normalised rows into every GPU
-    (all-gather), in one or two row pieces (the second overlapping the first
-    piece's GEMM); push: the GEMM epilogue stores the partials into the
-    owners' receive slots instead; nccl: ncclAllReduce of the partials."""
+    """peer: the GEMM epilogue stores each partial into the owning GPU's
+    receive slot, the owner's LayerNorm sums the slots and stores the
+    normalised rows into every GPU (all-gather), in one or two row pieces (the
+    second overlapping the first piece's GEMM); pull: each GPU keeps its bf16
+    partial and the owners read them in their LayerNorm; nccl: ncclAllReduce
+    of the partials."""
     r = run_ranks(tmp_path, heads, wtype, comm, pieces)
     assert r["ranks_identical"], r
     assert r["replay_identical"], r
