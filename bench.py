@@ -67,7 +67,7 @@ CONFIGS = {
 # dram__bytes_write.sum from one ncu capture of this bench's own command
 # (summary and command in the named profile).  Keyed by (config, n_gpus).
 GEMM_TRAFFIC = {
-    ("2", 1): {"dram_bytes_per_launch": 428.2e6, "algorithmic_bytes_per_launch": 298.9e6,
+    ("2", 1): {"dram_bytes_per_launch": 356.4e6, "algorithmic_bytes_per_launch": 298.9e6,
                "source": "profiles/dram_traffic_config2_step.md: ncu dram__bytes_read.sum + dram__bytes_write.sum "
                          "over the 63 gemm_pair_kernel launches of one step (cold cache), per launch"},
 }
