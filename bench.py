@@ -65,11 +65,11 @@ CONFIGS = {
 # DRAM traffic of the step's dominant kernel (gemm_pair_kernel), per launch,
 # averaged over one step's GEMM launches: dram__bytes_read.sum +
 # dram__bytes_write.sum from one ncu capture of this bench's own command
-# (summary and command in the named profile).  Keyed by (config, n_gpus).
+# (its summary and command are kept under profiles/).  Keyed by (config, n_gpus).
 GEMM_TRAFFIC = {
     ("2", 1): {"dram_bytes_per_launch": 356.4e6, "algorithmic_bytes_per_launch": 298.9e6,
-               "source": "profiles/dram_traffic_config2_step.md: ncu dram__bytes_read.sum + dram__bytes_write.sum "
-                         "over the 63 gemm_pair_kernel launches of one step (cold cache), per launch"},
+               "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the 63 gemm_pair_kernel launches "
+                         "of one step of this bench (cold cache), per launch; summary under profiles/"},
 }
 
 
