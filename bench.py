@@ -525,6 +525,10 @@ def run_ours(args):
                 "tp_exchange": (None if world == 1 else
                                 "ncclAllReduce of the row-parallel partials" if os.environ.get("DCPP_TP_COMM") == "nccl"
                                 else "GEMM epilogue stores partials into the owner GPU (NVLink peer memory); "
+                                     "owner LayerNorm; the next GEMM pushes the rows to the other GPUs and waits "
+                                     "per 128-row granule (all-gather overlapped); cross-GPU flag barrier"
+                                if os.environ.get("DCPP_TP_OVERLAP") == "1"
+                                else "GEMM epilogue stores partials into the owner GPU (NVLink peer memory); "
                                      "owner LayerNorm + all-gather stores; cross-GPU flag barriers"),
             },
             "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -109,6 +109,7 @@ Flux2Transformer2DModel::Flux2Transformer2DModel(Ctx& ctx, const Flux2Config& cf
   if (const char* e = getenv("DCPP_TP_COMM")) tp_peer_ = std::string(e) != "nccl";
   if (const char* e = getenv("DCPP_TP_PIECES")) tp_pieces_env_ = std::string(e) == "1" ? 1 : 2;
   if (const char* e = getenv("DCPP_TP_PULL")) tp_pull_ = std::string(e) == "1";
+  if (const char* e = getenv("DCPP_TP_OVERLAP")) tp_overlap_ = std::string(e) == "1";
   if (const char* e = getenv("DCPP_BLOCK_PREFETCH")) block_prefetch_ = std::string(e) == "1";
   build_registry();
 }
@@ -578,11 +579,14 @@ void Flux2Transformer2DModel::free_plan() {
   sym_.close(ctx_);
   release_plan_events();
   for (int j = 0; j < 8; ++j) {
+    ag_flags_peer_[j] = nullptr;
     recv_peer_[j] = nullptr;
     a_peer_[j] = nullptr;
     flags_peer_[0][j] = flags_peer_[1][j] = nullptr;
   }
   epoch_[0] = epoch_[1] = nullptr;
+  ag_count_ = step_dev_ = nullptr;
+  overlap_ = false;
   ops_fwd_.clear();
   step_ops_[0].clear();
   step_ops_[1].clear();
@@ -678,22 +682,36 @@ void Flux2Transformer2DModel::build_plan() {
     // Two row pieces pay off once the per-site exchange is large and spread
     // over >= 4 GPUs (measured at 8 GPUs: config 3, B*S*D = 37.7 M, gains
     // 2%; config 2, 14.2 M, loses 7%; at 2 GPUs one piece is faster).
-    tp_pieces_ = tp_pieces_env_ > 0 ? tp_pieces_env_ : (nranks_ >= 4 && R * D >= (int64_t{24} << 20) ? 2 : 1);
+    // (the flags' epochs give each step kAgSitesPerStep - 1 sites)
+    overlap_ = tp_overlap_ && !tp_pull_ && ctx_.use_pair(R) && !fused_dequant_ &&
+               2 * cfg_.num_layers + cfg_.num_single_layers < static_cast<int64_t>(kAgSitesPerStep) - 1;
+    tp_pieces_ = overlap_ ? 1
+                          : (tp_pieces_env_ > 0 ? tp_pieces_env_
+                                                : (nranks_ >= 4 && R * D >= (int64_t{24} << 20) ? 2 : 1));
     piece_rows_ = (R + tp_pieces_ - 1) / tp_pieces_;
     chunk_ = (piece_rows_ + nranks_ - 1) / nranks_;
+    const int64_t ngr = (R + kGranuleRows - 1) / kGranuleRows;
+    own_max_ = (ngr + nranks_ - 1) / nranks_;
     auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
     const size_t off_recv = up(R * D * 2);
-    // recv: the push form's receive slots, or the pull form's full-row partials.
-    const size_t recv_bytes = std::max<size_t>(static_cast<size_t>(nranks_) * tp_pieces_ * chunk_ * D * 2,
-                                               static_cast<size_t>(R) * D * 2);
+    // recv: the push form's receive slots (by chunk or, overlapped, by
+    // granule), or the pull form's full-row partials.
+    const size_t recv_bytes = std::max<size_t>(
+        std::max<size_t>(static_cast<size_t>(nranks_) * tp_pieces_ * chunk_ * D * 2, static_cast<size_t>(R) * D * 2),
+        static_cast<size_t>(nranks_) * own_max_ * kGranuleRows * D * 2);
     const size_t off_flags = off_recv + up(recv_bytes);
-    sym_.open(ctx_, off_flags + 512);
+    const size_t off_ag = off_flags + 512;  // per-granule arrival flags
+    sym_.open(ctx_, off_ag + up(static_cast<size_t>(ngr) * 4));
     for (int j = 0; j < nranks_; ++j) {
       a_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j]);
       recv_peer_[j] = reinterpret_cast<uint16_t*>(sym_.peer[j] + off_recv);
       flags_peer_[0][j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags);
       flags_peer_[1][j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_flags + 256);
+      ag_flags_peer_[j] = reinterpret_cast<uint32_t*>(sym_.peer[j] + off_ag);
     }
+    ag_count_ = static_cast<uint32_t*>(alloc(static_cast<size_t>(kAgSitesPerStep) * own_max_ * 4));
+    step_dev_ = static_cast<uint32_t*>(alloc(256));
+    cuda_check(cudaMemsetAsync(step_dev_, 0, 256, ctx_.stream), "clear step counter");
     a_ = a_peer_[rank_];
     epoch_[0] = static_cast<uint32_t*>(alloc(256));
     epoch_[1] = epoch_[0] + 32;
@@ -834,6 +852,13 @@ void Flux2Transformer2DModel::build_plan() {
     // while block k's attention runs (after its QKV GEMM, when the set that
     // block k - 1 used is free).  The attention leaves HBM and most issue
     // slots idle; expansions beside a GEMM slow it instead.
+    if (overlap_)
+      ops.push_back({[=](cudaStream_t s) {
+                       cuda_check(launch_step_counter(step_dev_, s), "step counter");
+                       cuda_check(cudaMemsetAsync(ag_count_, 0, static_cast<size_t>(kAgSitesPerStep) * own_max_ * 4, s),
+                                  "clear all-gather counts");
+                     },
+                     1});
     size_t blk_idx = 0;
     auto prefetch_next = [&]() {
       if (block_prefetch_ && blk_idx + 1 < n_blocks) add_prefetch(block_weights(blk_idx + 1), static_cast<int>((blk_idx + 1) & 1));
@@ -933,8 +958,9 @@ void Flux2Transformer2DModel::build_plan() {
         for (int j = 0; j < nranks_; ++j) e.peer_bf16[j] = recv_peer_[j];
         e.chunk_rows = static_cast<int32_t>(chunk_);
         e.piece_rows = static_cast<int32_t>(piece_rows_);
-        e.slot_rows = static_cast<int32_t>(tp_pieces_ * chunk_);
+        e.slot_rows = static_cast<int32_t>(overlap_ ? own_max_ * kGranuleRows : tp_pieces_ * chunk_);
         e.peer_slot = rank_;
+        e.gran_n = overlap_ ? nranks_ : 0;
       }
       return e;
     };
@@ -961,6 +987,43 @@ void Flux2Transformer2DModel::build_plan() {
       const auto pr = piece_range(p);
       const int64_t lo = std::min<int64_t>(pr[1], pr[0] + rank_ * chunk_);
       return std::array<int64_t, 2>{lo, std::min<int64_t>(pr[1], lo + chunk_)};
+    };
+    // Granule form (overlap_): the segments stay whole; the kernel walks this
+    // rank's 128-row granules.  push_rows: also store every row into the other
+    // GPUs' buffers (for a LayerNorm whose GEMM is not overlapped).
+    auto gran_norm = [&](NormArgs n, bool push_rows) {
+      n.gran_rank = rank_;
+      n.gran_n = nranks_;
+      n.n_slots = nranks_;
+      n.slots = recv_peer_[rank_];
+      n.slot_stride = own_max_ * kGranuleRows * D;
+      n.n_peer_out = 0;
+      if (push_rows)
+        for (int j = 0; j < nranks_; ++j)
+          if (j != rank_) n.y_peer[n.n_peer_out++] = a_peer_[j] + (n.y - a_);
+      return n;
+    };
+    int ag_site = 0;
+    // The all-gather of this rank's rows of `a` (which the LayerNorm just
+    // wrote) runs inside the next GEMM: its epilogue warps push the rows,
+    // its producer waits for the other ranks' granules.
+    auto ag_push = [&]() {
+      AgWait w{};
+      w.flags = ag_flags_peer_[rank_];
+      w.step = step_dev_;
+      w.site = ag_site;
+      w.rank = rank_;
+      w.n = nranks_;
+      w.rows = static_cast<int32_t>(R);
+      w.ld = D;
+      w.a = a_;
+      for (int j = 0; j < nranks_; ++j) {
+        w.a_peer[j] = a_peer_[j];
+        w.flags_peer[j] = ag_flags_peer_[j];
+      }
+      w.count = ag_count_ + static_cast<size_t>(ag_site) * own_max_;
+      next_ag_ = w;
+      ++ag_site;
     };
     auto peer_norm = [&](NormArgs n, int p) {
       const auto own = own_range(p);
@@ -1018,6 +1081,16 @@ void Flux2Transformer2DModel::build_plan() {
         return;
       }
       pending = false;
+      if (overlap_) {
+        add_norm(gran_norm(n, !joint_rows));
+        if (joint_rows) {
+          ag_push();
+        } else {
+          add_tp_barrier(0, 0);
+        }
+        emit({groups}, nullptr);
+        return;
+      }
       if (!joint_rows || tp_pieces_ == 1) {
         for (int p = 0; p < tp_pieces_; ++p) {
           NormArgs q = peer_norm(n, p);

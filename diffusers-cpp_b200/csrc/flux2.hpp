@@ -199,6 +199,22 @@ class Flux2Transformer2DModel : public StepPlanner {
   // measured faster at 2 GPUs (the LayerNorm's remote reads cost more than
   // the GEMM saves there).
   bool tp_pull_ = false;
+  // Overlapped all-gather (DCPP_TP_OVERLAP=1, with the push form and CTA-pair
+  // GEMMs): rows are owned in 128-row granules round-robin over the ranks;
+  // the owner's LayerNorm writes only its own rows, and the next
+  // column-parallel GEMM starts at once: two extra warps per CTA copy this
+  // rank's rows to the other GPUs in row order and raise a per-granule flag
+  // there, while its TMA producer waits (bounded) for each tile's granules
+  // from the others instead of a barrier for all rows.  Off by default: on
+  // the 1024^2 step it measured slower at 2, 4 and 8 GPUs (the GEMM's first
+  // wave already needs a third of the rows at 8 GPUs, so it mostly waits for
+  // the transfer, and it runs slower beside the NVLink stores).
+  bool tp_overlap_ = false;
+  bool overlap_ = false;  // in effect for the current plan
+  int64_t own_max_ = 0;   // granules per rank, at most
+  uint32_t* ag_flags_peer_[8] = {};
+  uint32_t* ag_count_ = nullptr;  // [kAgSitesPerStep][own_max_] rows pushed, cleared every step
+  uint32_t* step_dev_ = nullptr;
   int tp_pieces_ = 1;
   int tp_pieces_env_ = 0;
   PeerBuffer sym_;

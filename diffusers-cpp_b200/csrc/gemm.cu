@@ -17,6 +17,7 @@
 // tile i overlap the main loop of tile i+1.
 #include "common.cuh"
 #include "gemm.cuh"
+#include "kernels.cuh"
 
 #include <algorithm>
 
@@ -70,6 +71,116 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmArgs& p, int t) {
   c.m_tile = m_all - p.groups[g].tile0;
   c.split = split;
   return c;
+}
+
+// Wait (bounded) until the rows [r0, r1) of A that other GPUs store have
+// arrived: every 128-row granule they touch that another rank owns must show
+// the epoch in its flag.  Then the generic-proxy stores that brought them
+// are made visible to the async proxy (TMA) of this thread.
+__device__ __forceinline__ bool wait_rows_arrived(const GemmArgs& p, int r0, int r1, uint32_t epoch) {
+  if (r1 <= r0) return true;
+  bool waited = false;
+  for (int g = r0 / kGranuleRows; g <= (r1 - 1) / kGranuleRows; ++g) {
+    if (g % p.ag_n == p.ag_rank) continue;  // this rank's own rows: written before the launch
+    const uint32_t* f = p.ag_flags + g;
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (static_cast<int32_t>(v - epoch) >= 0) {
+      waited = true;
+      continue;
+    }
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+      __nanosleep(200);
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (static_cast<int32_t>(v - epoch) >= 0) break;
+      if (error_raised(p.err)) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        record_error(p.err, kDevTimeoutPeer);
+        return false;
+      }
+    }
+    waited = true;
+  }
+  if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+// The push half of the overlapped all-gather (GemmArgs::ag_a), run by two
+// extra warps per CTA beside the GEMM's roles.  This rank's rows are
+// numbered i = 0.. granule by granule (its k-th granule is
+// g = k * ag_n + ag_rank; all but the globally last granule are full) and
+// cut into pieces of at most 128 16-byte vectors (ppr per row); piece
+// q = i * ppr + c.  Warp w of the grid's W push warps takes pieces w,
+// w + W, ... in rounds of kAgRound (all loads of a round in flight, then
+// the stores to every other rank), so the first rows complete first, which
+// is the order the M-outer tile walk consumes them.  After a round, one lane
+// per piece makes the stores visible system-wide (fence), counts the piece on
+// its granule and, if it was the granule's last, publishes the granule
+// (flag = epoch, release) on every other rank.
+constexpr int kAgRound = 8;
+
+__device__ __forceinline__ void ag_push_all(const GemmArgs& p, int64_t w, int64_t W, int lane) {
+  const int n = p.ag_n, me = p.ag_rank;
+  const int64_t ngr = (static_cast<int64_t>(p.ag_rows) + kGranuleRows - 1) / kGranuleRows;
+  const int64_t own = ngr > me ? (ngr - me + n - 1) / n : 0;
+  if (own == 0) return;
+  const int64_t last_g = (own - 1) * n + me;
+  const int64_t own_rows =
+      (own - 1) * kGranuleRows + min(static_cast<int64_t>(kGranuleRows), p.ag_rows - last_g * kGranuleRows);
+  const int vpr = static_cast<int>(p.ag_ld / 8);  // 16-byte vectors per row
+  const int ppr = (vpr + 127) / 128;
+  const int pv = (vpr + ppr - 1) / ppr;
+  const int64_t pieces = own_rows * ppr;
+  const uint32_t epoch = *p.ag_step * kAgSitesPerStep + static_cast<uint32_t>(p.ag_site) + 1u;
+  for (int64_t q0 = w; q0 < pieces; q0 += kAgRound * W) {
+    int64_t off[kAgRound];
+    int cnt[kAgRound];
+    uint4 v[kAgRound][4];
+#pragma unroll
+    for (int b = 0; b < kAgRound; ++b) {
+      const int64_t q = q0 + b * W;
+      cnt[b] = 0;
+      off[b] = 0;
+      if (q < pieces) {
+        const int64_t i = q / ppr;
+        const int c0 = static_cast<int>(q - i * ppr) * pv;
+        const int64_t k = i / kGranuleRows;
+        cnt[b] = min(pv, vpr - c0);
+        off[b] = ((k * n + me) * kGranuleRows + (i - k * kGranuleRows)) * p.ag_ld + static_cast<int64_t>(c0) * 8;
+        const uint4* src = reinterpret_cast<const uint4*>(p.ag_a + off[b]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u * 32 + lane < cnt[b]) v[b][u] = src[u * 32 + lane];
+      }
+    }
+#pragma unroll 1
+    for (int j = 0; j < n; ++j) {
+      if (j == me) continue;
+#pragma unroll
+      for (int b = 0; b < kAgRound; ++b) {
+        uint4* dst = reinterpret_cast<uint4*>(p.ag_a_peer[j] + off[b]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u * 32 + lane < cnt[b]) dst[u * 32 + lane] = v[b][u];
+      }
+    }
+    __syncwarp();
+    const int64_t q = q0 + lane * W;
+    if (lane < kAgRound && q < pieces) {
+      __threadfence_system();
+      const int64_t k = q / ppr / kGranuleRows;
+      const int64_t g = k * n + me;
+      const int64_t rows_g = min(static_cast<int64_t>(kGranuleRows), p.ag_rows - g * kGranuleRows);
+      if (atomicAdd(p.ag_count + k, 1u) + 1u == static_cast<uint32_t>(rows_g * ppr)) {
+        __threadfence_system();
+        for (int j = 0; j < n; ++j)
+          if (j != me)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.ag_flags_peer[j] + g), "r"(epoch) : "memory");
+      }
+    }
+    __syncwarp();
+  }
 }
 
 // K blocks [kb0, kb1) of a work unit.
@@ -517,10 +628,17 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, const TileCoord&
     const int lane = row_in_tile & 31;
     uintptr_t rdst = 0;
     if (row_ok) {
-      const int64_t pc = row / e.piece_rows;
-      const int64_t rp = row - pc * e.piece_rows;
-      const int64_t owner = rp / e.chunk_rows;
-      const int64_t l = pc * e.chunk_rows + (rp - owner * e.chunk_rows);
+      int64_t owner, l;
+      if (e.gran_n > 0) {
+        const int64_t g = row / kGranuleRows;
+        owner = g % e.gran_n;
+        l = (g / e.gran_n) * kGranuleRows + (row - g * kGranuleRows);
+      } else {
+        const int64_t pc = row / e.piece_rows;
+        const int64_t rp = row - pc * e.piece_rows;
+        owner = rp / e.chunk_rows;
+        l = pc * e.chunk_rows + (rp - owner * e.chunk_rows);
+      }
       rdst = reinterpret_cast<uintptr_t>(e.peer_bf16[owner] +
                                          (static_cast<int64_t>(e.peer_slot) * e.slot_rows + l) * e.ld_out);
     }
@@ -1057,8 +1175,14 @@ constexpr int kPairA = 128 * kGemmBK * 2;  // 16 KB per CTA
 
 template <int BSRC>
 __host__ __device__ constexpr int pair_raw_bytes() { return 128 * (PairCfg<BSRC>::kQs + PairCfg<BSRC>::kSc); }
-template <int BSRC>
-__host__ __device__ constexpr int pair_threads() { return (6 + PairCfg<BSRC>::kDequantWarps) * 32; }
+// kPush: two more warps for the overlapped all-gather push (GemmArgs::ag_a;
+// bf16 B only).  Only the GEMMs that carry one use this variant: the extra
+// warps' registers would keep weight-expansion CTAs off the GEMM's SMs.
+// That variant is its own kernel, gemm_pair_ag_kernel<BN>.
+template <int BSRC, bool kPush = false>
+__host__ __device__ constexpr int pair_threads() {
+  return (6 + PairCfg<BSRC>::kDequantWarps + (kPush ? 2 : 0)) * 32;
+}
 template <int BSRC, int BN>
 __host__ __device__ constexpr int pair_stages() {
   return BSRC != kBSrcBf16 || BN >= 256 ? PairCfg<BSRC>::kStages : 8;
@@ -1077,10 +1201,9 @@ static_assert(pair_smem_bytes<kBSrcBf16>() <= 232448 && pair_smem_bytes<kBSrcQ4_
                   pair_smem_bytes<kBSrcQ8_0>() <= 232448 && pair_smem_bytes<kBSrcBf16, 128>() <= 232448,
               "pair GEMM shared memory above the 227 KB per-CTA limit");
 
-template <int BSRC, int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>(), 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+template <int BSRC, int BN, bool kPush>
+__device__ __forceinline__ void gemm_pair_body(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1,
+                                               const GemmArgs& p) {
   constexpr int kStages = pair_stages<BSRC, BN>();
   constexpr int kPB = (BN / 2) * kGemmBK * 2;  // this CTA's half of the B stage
   constexpr bool kQuant = BSRC != kBSrcBf16;
@@ -1147,11 +1270,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint32_t ag_epoch = p.ag_flags ? *p.ag_step * kAgSitesPerStep + static_cast<uint32_t>(p.ag_site) + 1u : 0u;
       for (int t = pair; t < p.total_tiles && ok; t += npairs) {
         const TileCoord tc = decode_tile(p, t);
         const GemmGroup& G = p.groups[tc.g];
         const int ya = G.row0 + tc.m_tile * 256 + static_cast<int>(rank) * 128;
         const int yb = tc.n_tile * BN + static_cast<int>(rank) * (BN / 2);
+        if (p.ag_flags && !wait_rows_arrived(p, ya, min(ya + 128, G.row0 + G.rows), ag_epoch)) {
+          ok = false;
+          break;
+        }
         const void* tmB = G.wsel ? static_cast<const void*>(&tmB1) : static_cast<const void*>(&tmB0);
         const uint8_t* packed = kQuant ? static_cast<const uint8_t*>(p.qb[G.wsel].packed) : nullptr;
         int kb0, kb1;
@@ -1278,6 +1406,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
+  } else {
+    // The all-gather push warps (kPush).
+    if constexpr (kPush && !kQuant) {
+      if (p.ag_a) ag_push_all(p, static_cast<int64_t>(blockIdx.x) * 2 + (warp - 6), static_cast<int64_t>(gridDim.x) * 2, lane);
+    }
   }
 
   tc_fence_before();
@@ -1287,6 +1420,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>()
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+}
+
+template <int BSRC, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<BSRC>(), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+  gemm_pair_body<BSRC, BN, false>(tmA, tmB0, tmB1, p);
+}
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kBSrcBf16, true>(), 1)
+    gemm_pair_ag_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                        const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ GemmArgs p) {
+  gemm_pair_body<kBSrcBf16, BN, true>(tmA, tmB0, tmB1, p);
 }
 
 // ------------------------------------------------------------------ conv halo
@@ -1513,19 +1660,24 @@ cudaError_t launch_gemm_t(const CUtensorMap& a, const CUtensorMap& b0, const CUt
   return cudaGetLastError();
 }
 
-template <int BSRC, int BN = kGemmBN>
+template <int BSRC, int BN = kGemmBN, bool kPush = false>
 cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                                const GemmArgs& args, int num_sms, cudaStream_t stream) {
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmArgs) = nullptr;
+  if constexpr (kPush)
+    kern = gemm_pair_ag_kernel<BN>;
+  else
+    kern = gemm_pair_kernel<BSRC, BN>;
   static int max_clusters = 0;
   if (max_clusters == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<BSRC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          pair_smem_bytes<BSRC, BN>());
     if (e != cudaSuccess) return e;
     // Persistent grid: only as many pairs as can be resident at once (a GPC
     // with an odd SM count leaves one SM out of the pairs).
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-    cfg.blockDim = dim3(pair_threads<BSRC>(), 1, 1);
+    cfg.blockDim = dim3(pair_threads<BSRC, kPush>(), 1, 1);
     cfg.dynamicSmemBytes = pair_smem_bytes<BSRC, BN>();
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -1535,14 +1687,13 @@ cudaError_t launch_gemm_pair_t(const CUtensorMap& a, const CUtensorMap& b0, cons
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BSRC, BN>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
     if (e != cudaSuccess) return e;
     if (n <= 0) return cudaErrorInvalidConfiguration;
     max_clusters = n;
   }
   const int pairs = std::min(args.total_tiles, max_clusters);
-  gemm_pair_kernel<BSRC, BN><<<2 * pairs, pair_threads<BSRC>(), pair_smem_bytes<BSRC, BN>(), stream>>>(a, b0, b1,
-                                                                                                       args);
+  kern<<<2 * pairs, pair_threads<BSRC, kPush>(), pair_smem_bytes<BSRC, BN>(), stream>>>(a, b0, b1, args);
   return cudaGetLastError();
 }
 
@@ -1582,6 +1733,18 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
                              int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
   if (args.tile_n != kGemmBN && (bsrc != kBSrcBf16 || args.tile_n != 128)) return cudaErrorInvalidValue;
+  if (args.ag_flags && (args.conv.taps || args.ag_n < 2 || args.ag_n > 8 || args.ag_rank < 0 ||
+                        args.ag_rank >= args.ag_n || !args.ag_step))
+    return cudaErrorInvalidValue;
+  if (args.ag_a) {
+    if (!args.ag_flags || bsrc != kBSrcBf16 || !args.ag_count || args.ag_rows <= 0 || args.ag_ld <= 0 ||
+        args.ag_ld % 8 || (reinterpret_cast<uintptr_t>(args.ag_a) & 15))
+      return cudaErrorInvalidValue;
+    for (int j = 0; j < args.ag_n; ++j)
+      if (j != args.ag_rank && (!args.ag_a_peer[j] || !args.ag_flags_peer[j] ||
+                                (reinterpret_cast<uintptr_t>(args.ag_a_peer[j]) & 15)))
+        return cudaErrorInvalidValue;
+  }
   if (args.k_splits > 1 && (bsrc != kBSrcBf16 || args.ep.mode != kEpiF32 || args.conv.taps ||
                             args.tiles_per_split * args.k_splits != args.total_tiles ||
                             args.k_splits > (args.K + kGemmBK - 1) / kGemmBK))
@@ -1598,6 +1761,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const 
   }
   switch (bsrc) {
     case kBSrcBf16:
+      if (args.ag_a)
+        return args.tile_n == 128 ? launch_gemm_pair_t<kBSrcBf16, 128, true>(a, b0, b1, args, num_sms, stream)
+                                  : launch_gemm_pair_t<kBSrcBf16, kGemmBN, true>(a, b0, b1, args, num_sms, stream);
       return args.tile_n == 128 ? launch_gemm_pair_t<kBSrcBf16, 128>(a, b0, b1, args, num_sms, stream)
                                 : launch_gemm_pair_t<kBSrcBf16>(a, b0, b1, args, num_sms, stream);
     case kBSrcQ4_K:
@@ -1742,6 +1908,7 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUten
                         int bsrc, int num_sms, cudaStream_t stream) {
   if (args.total_tiles <= 0) return cudaSuccess;
   if (args.k_splits > 1) return cudaErrorInvalidValue;  // the one-SM kernel has no K split
+  if (args.ag_flags || args.ag_a) return cudaErrorInvalidValue;  // nor the overlapped all-gather
   if (args.tile_n != kGemmBN && bsrc != kBSrcBf16) return cudaErrorInvalidValue;
   switch (bsrc) {
     case kBSrcBf16:

@@ -80,11 +80,15 @@ struct EpilogueArgs {
   // rank's receive slots (peer_bf16[o], mapped from its GPU; slot_rows rows
   // per source rank).  This rank writes slot peer_slot:
   //   peer_bf16[o] + (peer_slot * slot_rows + l) * ld_out.
+  // gran_n > 0 (granule ownership): row r belongs to rank (r / 128) % gran_n
+  // and is row ((r / 128) / gran_n) 128 + r % 128 of its receive slots
+  // (chunk_rows / piece_rows unused).
   uint16_t* peer_bf16[8];
   int32_t chunk_rows;
   int32_t piece_rows;
   int32_t slot_rows;
   int32_t peer_slot;
+  int32_t gran_n;
   // kEpiConv: output row r' of accumulator row r is r itself for a plain
   //   GEMM, and for an implicit convolution (ConvGeom) the row-major index
   //   (b H + y) W + x of the pixel the row computes (rows outside the image
@@ -166,6 +170,30 @@ struct GemmArgs {
   int32_t tiles_per_split;
   int64_t split_stride;
   int* err;
+  // The tensor-parallel all-gather of A, overlapped with this GEMM (CTA-pair
+  // kernel only).  A's rows are cut into 128-row granules; granule g belongs
+  // to rank g % ag_n.  epoch = *ag_step * kAgSitesPerStep + ag_site + 1.
+  //  * push: two extra warps per CTA (the gemm_pair_ag_kernel variant) copy
+  //    this rank's granules of A (ag_rows rows of ag_ld bf16 at ag_a, in
+  //    pieces of up to 2 KB, in row order) into every other rank's copy
+  //    ag_a_peer[j]; when all pieces of granule g are out, the warp that
+  //    stored the last one sets ag_flags_peer[j][g] = epoch (release, system
+  //    scope).  ag_count[k] counts the pieces of this rank's k-th granule
+  //    stored so far (zero at launch).
+  //  * wait: before loading an A tile, the producer waits (bounded) until
+  //    ag_flags[g] (this rank's flags, which the others set) reached the epoch
+  //    for every granule g of the tile's rows that another rank owns.
+  const uint32_t* ag_flags;
+  const uint32_t* ag_step;
+  int32_t ag_site;
+  int32_t ag_rank;
+  int32_t ag_n;
+  int32_t ag_rows;
+  int64_t ag_ld;
+  const uint16_t* ag_a;
+  uint16_t* ag_a_peer[8];
+  uint32_t* ag_flags_peer[8];
+  uint32_t* ag_count;
 };
 
 // Host-side: build a 2-D bf16 tensor map with 128-byte swizzle for a

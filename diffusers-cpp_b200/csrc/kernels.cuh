@@ -22,6 +22,8 @@ cudaError_t launch_pack_weight(int type, const void* raw, int64_t N, int64_t K, 
 
 // ---- rowops.cu
 constexpr int kMaxNormSegments = 8;
+constexpr int kGranuleRows = 128;  // row granule of the tensor-parallel exchange's ownership
+constexpr uint32_t kAgSitesPerStep = 256;  // epochs of the all-gather flags: step * 256 + site + 1
 
 // One contiguous run of rows normalised with one (shift, scale) pair.
 struct NormSegment {
@@ -63,7 +65,17 @@ struct NormArgs {
   int32_t rms;
   const float* weight;
   float* y_f32;         // optional f32 copy of the output (row stride ld_y)
+  // Granule form (gran_n > 0): this kernel normalises the rows of the
+  // 128-row granules g with g % gran_n == gran_rank, in granule order (block
+  // b: granule k = b / 128 of this rank, g = k gran_n + gran_rank, row
+  // 128 g + b % 128); each row takes the segment that contains it as src
+  // (dst = dst_row0 + row - src_row0), and its slot row is 128 k + b % 128.
+  int32_t gran_rank;
+  int32_t gran_n;
 };
+
+// *step += 1 (one thread): the per-step base of the granule flags' epochs.
+cudaError_t launch_step_counter(uint32_t* step, cudaStream_t s);
 
 // out[i, :] = dequantised row ids[i] of table [n_rows, dim] (ggml_get_rows,
 // Embedding::forward).  An id outside [0, n_rows) gives a zero row and

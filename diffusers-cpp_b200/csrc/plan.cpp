@@ -358,7 +358,10 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
   for (auto& pg : pieces) groups.insert(groups.end(), pg.begin(), pg.end());
   // Fused dequantisation when every weight of the launch is packed and of
   // one quantised type; otherwise expand to bf16 first (or use bf16 as is).
+  const AgWait ag = next_ag_;
+  next_ag_ = AgWait{};
   const bool fused = w0->packed && (!w1 || (w1->packed && w1->type == w0->type));
+  if (fused && ag.flags) fail(DCPP_ERR_STATE, "internal: arrival waits are not built for the fused-dequant GEMM");
   int64_t total_rows = 0;
   for (auto& g : groups) total_rows += g.rows;
   const bool pair = ctx_.use_pair(total_rows, fused);
@@ -498,6 +501,29 @@ void StepPlanner::add_gemm_pieces(const std::string& tag, const uint16_t* a, int
     args.ep = ep;
     args.err = ctx_.d_err;
     gemm_finalize_groups(args, tile_m, tile_n);
+    if (ag.flags) {
+      if (!pair || splits > 1 || pieces.size() != 1)
+        fail(DCPP_ERR_STATE, "internal: the overlapped all-gather needs one unsplit CTA-pair GEMM launch");
+      args.ag_flags = ag.flags;
+      args.ag_step = ag.step;
+      args.ag_site = ag.site;
+      args.ag_rank = ag.rank;
+      args.ag_n = ag.n;
+      args.ag_rows = ag.rows;
+      args.ag_ld = ag.ld;
+      args.ag_a = ag.a;
+      for (int j = 0; j < 8; ++j) {
+        args.ag_a_peer[j] = ag.a_peer[j];
+        args.ag_flags_peer[j] = ag.flags_peer[j];
+      }
+      args.ag_count = ag.count;
+      // M tile by M tile within bands of N tiles whose weight stays in L2
+      // (64 MB, as the default tile order budgets): the rows arrive in row
+      // order, and the first band's sweep overlaps their arrival.
+      const double b_col = static_cast<double>(tile_n) * K * 2.0 * (w1 && w1 != w0 ? 2 : 1);
+      args.raster = 1;
+      args.band = std::max(1, std::min(args.n_tiles_n, static_cast<int>(64.0 * (1 << 20) / b_col)));
+    }
     if (splits > 1) {
       args.ep = EpilogueArgs{};
       args.ep.mode = kEpiF32;

@@ -112,6 +112,23 @@ class StepPlanner {
                        const DevWeight* w1, const std::vector<std::vector<GemmGroup>>& pieces, const EpilogueArgs& ep,
                        int64_t N, const std::function<void(int)>& before_piece);
   void add_norm(const NormArgs& a, int stream = 0);
+  // Arrival waits for the next GEMM built (consumed by it): its CTA-pair
+  // kernel waits for the A rows other GPUs push (GemmArgs::ag_*) and walks
+  // its tiles M tile by M tile, in the order the rows arrive.
+  // The overlapped all-gather the next GEMM runs (GemmArgs::ag_*): it
+  // pushes this rank's granules of `a` and waits for the others'.
+  struct AgWait {
+    const uint32_t* flags = nullptr;
+    const uint32_t* step = nullptr;
+    int32_t site = 0, rank = 0, n = 0;
+    int32_t rows = 0;
+    int64_t ld = 0;
+    const uint16_t* a = nullptr;
+    uint16_t* a_peer[8] = {};
+    uint32_t* flags_peer[8] = {};
+    uint32_t* count = nullptr;
+  };
+  AgWait next_ag_{};
   void add_gemv(const DevWeight& w, const float* x, int batch, int act_in, int act_out, float* y);
   // Cross-stream dependencies inside a plan (graph edges when captured).
   cudaEvent_t plan_event();

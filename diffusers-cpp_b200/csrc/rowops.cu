@@ -51,21 +51,34 @@ __global__ void __launch_bounds__(kThreads) layernorm_mod_kernel(const __grid_co
   __shared__ float stat;
   int blk = blockIdx.x;
   int sidx = 0;
+  int64_t src, dst, slot_row;
+  if (a.gran_n > 0) {  // this rank's granules, in order
+    const int64_t k = blk / kGranuleRows, off = blk % kGranuleRows;
+    src = (k * a.gran_n + a.gran_rank) * kGranuleRows + off;
+    slot_row = k * kGranuleRows + off;
 #pragma unroll 1
-  for (; sidx < a.n_segments; ++sidx) {
-    if (blk < a.seg[sidx].rows) break;
-    blk -= a.seg[sidx].rows;
+    for (; sidx < a.n_segments; ++sidx)
+      if (src >= a.seg[sidx].src_row0 && src < a.seg[sidx].src_row0 + a.seg[sidx].rows) break;
+    if (sidx >= a.n_segments) return;
+    dst = a.seg[sidx].dst_row0 + (src - a.seg[sidx].src_row0);
+  } else {
+#pragma unroll 1
+    for (; sidx < a.n_segments; ++sidx) {
+      if (blk < a.seg[sidx].rows) break;
+      blk -= a.seg[sidx].rows;
+    }
+    if (sidx >= a.n_segments) return;
+    src = a.seg[sidx].src_row0 + blk;
+    dst = a.seg[sidx].dst_row0 + blk;
+    slot_row = src - a.slot_row0;
   }
-  if (sidx >= a.n_segments) return;
   const NormSegment& sg = a.seg[sidx];
-  const int64_t src = sg.src_row0 + blk;
-  const int64_t dst = sg.dst_row0 + blk;
   const int D = a.D;
   const int ng = D / kW;
   const float4* x4 = reinterpret_cast<const float4*>(a.x + src * a.ld_x);
   const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + src * a.ld_x) : nullptr;
   const bool slotted = a.n_slots > 0;
-  const int64_t srow = (src - a.slot_row0) * a.ld_x;
+  const int64_t srow = slot_row * a.ld_x;
   float4* xo4 = (a.resid || slotted) ? reinterpret_cast<float4*>(a.x_out + src * a.ld_x) : nullptr;
 
   float4 v[kVec][kF4];
@@ -615,6 +628,8 @@ __global__ void mask_bits_kernel(const float* __restrict__ mask, int64_t S, int6
   bits[b * words + w] = v;
 }
 
+__global__ void step_counter_kernel(uint32_t* step) { *step += 1u; }
+
 __global__ void add_f32_kernel(float* __restrict__ y, const float* __restrict__ a, int64_t n) {
   int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -635,6 +650,15 @@ cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
   int64_t rows = 0;
   for (int i = 0; i < a.n_segments; ++i) rows += a.seg[i].rows;
   if (rows == 0) return cudaSuccess;
+  if (a.gran_n > 0) {  // blocks over this rank's granules of the rows the segments cover
+    if (a.gran_rank < 0 || a.gran_rank >= a.gran_n) return cudaErrorInvalidValue;
+    int64_t end = 0;
+    for (int i = 0; i < a.n_segments; ++i) end = std::max<int64_t>(end, a.seg[i].src_row0 + a.seg[i].rows);
+    const int64_t ngr = (end + kGranuleRows - 1) / kGranuleRows;
+    const int64_t own = ngr > a.gran_rank ? (ngr - a.gran_rank + a.gran_n - 1) / a.gran_n : 0;
+    rows = own * kGranuleRows;
+    if (rows == 0) return cudaSuccess;
+  }
   const bool w8 = a.D % 8 == 0 && a.ld_y % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
   for (int k = 0; k < a.n_peer_out; ++k)
     if (reinterpret_cast<uintptr_t>(a.y_peer[k]) & (w8 ? 15 : 7)) return cudaErrorInvalidValue;
@@ -650,6 +674,11 @@ cudaError_t launch_layernorm_mod(const NormArgs& a, cudaStream_t s) {
     else
       layernorm_mod_kernel<256, 8, 4><<<grid, 256, 0, s>>>(a);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_step_counter(uint32_t* step, cudaStream_t s) {
+  step_counter_kernel<<<1, 1, 0, s>>>(step);
   return cudaGetLastError();
 }
 

@@ -49,16 +49,21 @@ def run_ranks(tmp_path, heads, wtype, comm, pieces=2, n=2, timeout=600, ratios="
 @pytest.mark.parametrize("heads,wtype,comm,pieces", [(4, fo.GGML_Q8_0, "peer", 2), (6, fo.GGML_Q4_K, "peer", 2),
                                                      (4, fo.GGML_Q8_0, "peer", 1), (4, fo.GGML_Q8_0, "nccl", 1),
                                                      (6, fo.GGML_Q4_K, "nccl", 1), (4, fo.GGML_Q8_0, "pull", 2),
-                                                     (6, fo.GGML_Q4_K, "pull", 1)],
+                                                     (6, fo.GGML_Q4_K, "pull", 1), (4, fo.GGML_Q8_0, "overlap", 1),
+                                                     (6, fo.GGML_Q4_K, "overlap", 1)],
                          ids=["q8_0_peer", "q4_k_bf16_shards_peer", "q8_0_peer_one_piece", "q8_0_nccl",
-                              "q4_k_bf16_shards_nccl", "q8_0_pull", "q4_k_bf16_shards_pull_one_piece"])
+                              "q4_k_bf16_shards_nccl", "q8_0_pull", "q4_k_bf16_shards_pull_one_piece", "q8_0_overlap",
+                              "q4_k_bf16_shards_overlap"])
 def test_tp2_matches_oracle(tmp_path, heads, wtype, comm, pieces):
     """peer: the GEMM epilogue stores each partial into the owning GPU's
-    receive slot, the owner's LayerNorm sums the slots and stores the
-    normalised rows into every GPU (all-gather), in one or two row pieces (the
-    second overlapping the first piece's GEMM); pull: each GPU keeps its bf16
-    partial and the owners read them in their LayerNorm; nccl: ncclAllReduce
-    of the partials."""
+    receive slot, the owner's LayerNorm sums its slots and stores the
+    normalised rows into every GPU, and a barrier precedes the next GEMM, in
+    one or two row pieces (the second overlapping the first piece's GEMM);
+    overlap: rows owned in 128-row granules, the owner's LayerNorm writes only
+    its own rows, and the next GEMM pushes them to the other GPU from two
+    extra warps while its producer waits per granule; pull: each GPU keeps
+    its bf16 partial and the owners read them in their LayerNorm; nccl:
+    ncclAllReduce of the partials."""
     r = run_ranks(tmp_path, heads, wtype, comm, pieces)
     assert r["ranks_identical"], r
     assert r["replay_identical"], r

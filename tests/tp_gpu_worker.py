@@ -34,10 +34,14 @@ def rel(a, b):
 def main():
     out_path, heads, wtype, comm = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
     # "peer": the peer exchange (default push form: partials stored into the
-    # owners' slots); "pull": its pull form (DCPP_TP_PULL=1, partials read by
-    # their owners); "nccl": ncclAllReduce.  Read when a model is created.
-    os.environ["DCPP_TP_COMM"] = "peer" if comm == "pull" else comm
+    # owners' slots, the owners' LayerNorm stores the rows into every GPU, a
+    # barrier before the next GEMM); "overlap": the same with the all-gather
+    # overlapped with the next GEMM (DCPP_TP_OVERLAP=1); "pull": its pull form
+    # (DCPP_TP_PULL=1, partials read by their owners); "nccl": ncclAllReduce.
+    # Read when a model is created.
+    os.environ["DCPP_TP_COMM"] = "peer" if comm in ("pull", "overlap") else comm
     os.environ["DCPP_TP_PULL"] = "1" if comm == "pull" else "0"
+    os.environ["DCPP_TP_OVERLAP"] = "1" if comm == "overlap" else "0"
     if len(sys.argv) > 5:
         os.environ["DCPP_TP_PIECES"] = sys.argv[5]  # row pieces of the peer exchange (1 or 2)
     # tensor_split ratios ("2,1"), or "even"
