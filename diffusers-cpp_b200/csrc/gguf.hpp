@@ -1,5 +1,5 @@
 // GGUF checkpoint reader: the on-disk format the reference's models load
-// (GGUFLoaderVisitor, src/ggml/GGUFLoaderVisitor.cpp:15-430, which parses
+// (GGUFLoaderVisitor, src/ggml/GGUFLoaderVisitor.cpp:15-429, which parses
 // metadata with ggml's gguf_init_from_file and streams each tensor's bytes
 // from the file).  Here the file is memory-mapped once and every tensor is
 // handed to a model's set_param straight from the mapping: the block bytes

@@ -6,7 +6,7 @@ type map (utils/convert-model/flux2-klein-9b-q8.json): every projection in the
 blocks and the modulations in the chosen quantised type, the input / output
 projections and the time embedding in BF16, the RMSNorm weights in F32.
 Tensor names are the GGUF names, with the fused tensors the reference's
-loader byte-slices (GGUFLoaderVisitor.cpp:283-430) unless ``split=True``.
+loader byte-slices (GGUFLoaderVisitor.cpp:283-429) unless ``split=True``.
 """
 from __future__ import annotations
 

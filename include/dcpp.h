@@ -251,7 +251,7 @@ dcpp_status dcpp_flux2_destroy(dcpp_flux2* model);
 /* Bind one parameter by its GGUF / module-path name (ModulePath.hpp:7-44),
  * e.g. "single_transformer_blocks.3.attn.to_qkv_mlp_proj.weight".  Accepts
  * the fused GGUF tensors (to_qkv_mlp_proj, to_out, ff.linear_in) that the
- * reference's loader byte-slices (GGUFLoaderVisitor.cpp:283-430) as well as
+ * reference's loader byte-slices (GGUFLoaderVisitor.cpp:283-429) as well as
  * the split per-module names.  Shapes are checked like Parameter::set /
  * GGUFLoaderVisitor::visit (:244-250).  `p_data` holds the raw GGUF bytes. */
 dcpp_status dcpp_flux2_set_param(dcpp_flux2* model, const char* name, int type, int n_dims,

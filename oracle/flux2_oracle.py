@@ -20,7 +20,7 @@ baseline) of the reference's forward, op by op, with ggml op semantics:
 * ``LayerNorm`` / ``RMSNorm`` (ggml_norm / ggml_rms_norm, eps)  src/nn/modules/normalization/*.cpp
 * ``FlashAttentionOp`` (softmax(q k^T / sqrt(d)) v, no mask)  src/nn/attention/FlashAttentionOp.cpp:6-105
 * Euler ``x + dt * v``                  src/diffusers/schedulers/FlowMatchEulerDiscreteScheduler.cpp:210-222
-* fused GGUF tensors split like GGUFLoaderVisitor.cpp:283-430
+* fused GGUF tensors split like GGUFLoaderVisitor.cpp:283-429
 
 Weights are dequantised with the C oracle (``oracle/dequant.c``), which is
 pinned bit-for-bit against gguf-py 0.19.0 ``gguf.dequantize``.
