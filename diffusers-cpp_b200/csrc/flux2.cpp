@@ -682,7 +682,8 @@ void Flux2Transformer2DModel::build_plan() {
     // Two row pieces pay off once the per-site exchange is large and spread
     // over >= 4 GPUs (measured at 8 GPUs: config 3, B*S*D = 37.7 M, gains
     // 2%; config 2, 14.2 M, loses 7%; at 2 GPUs one piece is faster).
-    // (the flags' epochs give each step kAgSitesPerStep - 1 sites)
+    // Overlapped all-gather: the granule flags' epochs give each step
+    // kAgSitesPerStep - 1 sites.
     overlap_ = tp_overlap_ && !tp_pull_ && ctx_.use_pair(R) && !fused_dequant_ &&
                2 * cfg_.num_layers + cfg_.num_single_layers < static_cast<int64_t>(kAgSitesPerStep) - 1;
     tp_pieces_ = overlap_ ? 1
@@ -1005,8 +1006,8 @@ void Flux2Transformer2DModel::build_plan() {
     };
     int ag_site = 0;
     // The all-gather of this rank's rows of `a` (which the LayerNorm just
-    // wrote) runs inside the next GEMM: its epilogue warps push the rows,
-    // its producer waits for the other ranks' granules.
+    // wrote) runs inside the next GEMM: its two push warps per CTA store the
+    // rows into the other GPUs, its producer waits for their granules.
     auto ag_push = [&]() {
       AgWait w{};
       w.flags = ag_flags_peer_[rank_];
