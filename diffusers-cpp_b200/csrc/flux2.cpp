@@ -87,14 +87,67 @@ void Flux2Config::to_c(dcpp_flux2_config& s) const {
   s.guidance_embeds = guidance_embeds ? 1 : 0;
 }
 
-void FlowMatchEulerDiscreteScheduler::schedule(int n, std::vector<float>& timesteps, std::vector<float>& sigmas) const {
+// All arithmetic in float, in the reference's order, so the schedule is the
+// reference's bit for bit.
+void FlowMatchEulerDiscreteScheduler::schedule(int n, float mu, const std::vector<float>& sigmas_in,
+                                               std::vector<float>& timesteps, std::vector<float>& sigmas) const {
+  if (num_train_timesteps <= 0) fail(DCPP_ERR_INVALID_ARG, "num_train_timesteps must be positive");
   if (n <= 0) fail(DCPP_ERR_INVALID_ARG, "num_inference_steps must be positive");
-  sigmas.resize(n);
-  for (int i = 0; i < n; ++i) sigmas[i] = static_cast<float>(1.0 - static_cast<double>(i) / n);
-  for (float& s : sigmas) s = shift * s / (1.0f + (shift - 1.0f) * s);
-  timesteps.resize(n);
-  for (int i = 0; i < n; ++i) timesteps[i] = sigmas[i] * static_cast<float>(num_train_timesteps);
-  sigmas.push_back(0.0f);
+  const float nt = static_cast<float>(num_train_timesteps);
+  if (!sigmas_in.empty()) {
+    if (sigmas_in.size() != static_cast<size_t>(n)) fail(DCPP_ERR_INVALID_ARG, "sigmas must have n entries");
+    sigmas = sigmas_in;
+  } else {
+    // timesteps evenly spaced from sigma_max * T down to sigma_min * T
+    const float hi = 1.0f * nt, lo = (1.0f / nt) * nt;
+    sigmas.assign(static_cast<size_t>(n), 0.0f);
+    if (n == 1) {
+      sigmas[0] = hi / nt;
+    } else {
+      const float step_den = static_cast<float>(n - 1);
+      for (int i = 0; i < n; ++i) sigmas[i] = (hi - static_cast<float>(i) * (hi - lo) / step_den) / nt;
+    }
+  }
+  for (float& s : sigmas) {
+    if (use_dynamic_shifting) {
+      // time_shift(mu, 1, s): e / (e + (1/s - 1)^1), e = exp(mu) or mu
+      if (s <= 0.0f) fail(DCPP_ERR_INVALID_ARG, "dynamic shifting needs every sigma > 0");
+      const float odds = std::pow(1.0f / s - 1.0f, 1.0f);
+      const float e = linear_time_shift ? mu : std::exp(mu);
+      s = e / (e + odds);
+    } else {
+      s = shift * s / (1.0f + (shift - 1.0f) * s);
+    }
+  }
+  if (has_shift_terminal) {
+    const float stretch = (1.0f - sigmas.back()) / (1.0f - shift_terminal);
+    for (float& s : sigmas) s = 1.0f - (1.0f - s) / stretch;
+  }
+  if (invert_sigmas)
+    for (float& s : sigmas) s = 1.0f - s;
+  timesteps.resize(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) timesteps[i] = sigmas[i] * nt;
+  sigmas.push_back(invert_sigmas ? 1.0f : 0.0f);
+}
+
+void FlowMatchEulerDiscreteScheduler::pipeline_schedule(int n, int64_t image_seq_len, std::vector<float>& timesteps,
+                                                        std::vector<float>& sigmas) const {
+  if (n <= 0) fail(DCPP_ERR_INVALID_ARG, "num_inference_steps must be positive");
+  std::vector<float> base(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) base[i] = static_cast<float>(1.0 - static_cast<double>(i) / n);
+  schedule(n, flux2_empirical_mu(image_seq_len, n), base, timesteps, sigmas);
+}
+
+float flux2_empirical_mu(int64_t image_seq_len, int num_steps) {
+  // Two linear fits of mu in the sequence length, at 10 and at 200 steps,
+  // interpolated linearly in the step count; long sequences use the
+  // 200-step fit alone.
+  const float len = static_cast<float>(image_seq_len);
+  const float at200 = 0.00016927f * len + 0.45666666f;
+  if (image_seq_len > 4300) return at200;
+  const float at10 = 8.73809524e-05f * len + 1.89833333f;
+  const float slope = (at200 - at10) / 190.0f;
+  return slope * static_cast<float>(num_steps) + (at200 - 200.0f * slope);
 }
 
 // ----------------------------------------------------------------- model
@@ -1615,14 +1668,54 @@ dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float
   try {
     dcpp::FlowMatchEulerDiscreteScheduler sch;
     sch.shift = shift;
-    std::vector<float> t, s;
-    sch.schedule(n, t, s);
+    std::vector<float> t, s, base(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) base[i] = static_cast<float>(1.0 - static_cast<double>(i) / n);
+    sch.schedule(n, 0.0f, base, t, s);
     memcpy(timesteps, t.data(), n * sizeof(float));
     memcpy(sigmas, s.data(), (n + 1) * sizeof(float));
     return DCPP_OK;
   } catch (const dcpp::Error& e) {
     return e.status;
   }
+}
+
+void dcpp_flow_match_config_default(dcpp_flow_match_config* c) {
+  if (!c) return;
+  *c = dcpp_flow_match_config{};
+  c->num_train_timesteps = 1000;
+  c->shift = 1.0f;
+  c->time_shift_type = DCPP_TIME_SHIFT_EXPONENTIAL;
+}
+
+dcpp_status dcpp_flow_match_schedule_ex(const dcpp_flow_match_config* c, int n, float mu, const float* sigmas_in,
+                                        float* timesteps, float* sigmas) {
+  if (!c || n <= 0 || !timesteps || !sigmas) return DCPP_ERR_INVALID_ARG;
+  if (c->time_shift_type != DCPP_TIME_SHIFT_EXPONENTIAL && c->time_shift_type != DCPP_TIME_SHIFT_LINEAR)
+    return DCPP_ERR_INVALID_ARG;
+  try {
+    dcpp::FlowMatchEulerDiscreteScheduler sch;
+    sch.num_train_timesteps = c->num_train_timesteps;
+    sch.shift = c->shift;
+    sch.use_dynamic_shifting = c->use_dynamic_shifting != 0;
+    sch.has_shift_terminal = c->has_shift_terminal != 0;
+    sch.shift_terminal = c->shift_terminal;
+    sch.invert_sigmas = c->invert_sigmas != 0;
+    sch.linear_time_shift = c->time_shift_type == DCPP_TIME_SHIFT_LINEAR;
+    std::vector<float> base, t, s;
+    if (sigmas_in) base.assign(sigmas_in, sigmas_in + n);
+    sch.schedule(n, mu, base, t, s);
+    memcpy(timesteps, t.data(), n * sizeof(float));
+    memcpy(sigmas, s.data(), (n + 1) * sizeof(float));
+    return DCPP_OK;
+  } catch (const dcpp::Error& e) {
+    return e.status;
+  }
+}
+
+dcpp_status dcpp_flux2_empirical_mu(int64_t image_seq_len, int num_steps, float* mu) {
+  if (!mu) return DCPP_ERR_INVALID_ARG;
+  *mu = dcpp::flux2_empirical_mu(image_seq_len, num_steps);
+  return DCPP_OK;
 }
 
 }  // extern "C"

@@ -246,13 +246,33 @@ class Flux2Transformer2DModel : public StepPlanner {
 // rank).
 std::vector<int64_t> plan_tensor_split(int64_t units, const std::vector<double>& ratios);
 
-// FlowMatchEulerDiscreteScheduler (default: shift 1, no dynamic shifting,
-// no terminal stretch, not inverted) with the pipeline's sigmas 1 - i/n.
+// FlowMatchEulerDiscreteScheduler with the reference constructor's options
+// and defaults (FlowMatchEulerDiscreteScheduler.hpp:11-18).
 struct FlowMatchEulerDiscreteScheduler {
-  float shift = 1.0f;
   int num_train_timesteps = 1000;
-  void schedule(int n, std::vector<float>& timesteps, std::vector<float>& sigmas) const;
+  float shift = 1.0f;
+  bool use_dynamic_shifting = false;
+  bool has_shift_terminal = false;
+  float shift_terminal = 0.0f;
+  bool invert_sigmas = false;
+  bool linear_time_shift = false;  // time_shift_type "linear" (default "exponential")
+  // schedule(n, mu, sigmas) (FlowMatchEulerDiscreteScheduler.cpp:68-208):
+  // base sigmas (`sigmas_in`, n values, or, when empty, n points from
+  // sigma_max = 1 down to sigma_min = 1 / num_train_timesteps), shifted
+  // (dynamically by mu or statically by `shift`), stretched to
+  // shift_terminal, n timesteps (sigma * num_train_timesteps), optionally
+  // inverted; n + 1 sigmas (the endpoint 0, or 1 when inverted).
+  void schedule(int n, float mu, const std::vector<float>& sigmas_in, std::vector<float>& timesteps,
+                std::vector<float>& sigmas) const;
+  // The pipeline's call (Flux2KleinPipeline.cpp:348-358): sigmas 1 - i/n,
+  // mu = flux2_empirical_mu(image_seq_len, n).
+  void pipeline_schedule(int n, int64_t image_seq_len, std::vector<float>& timesteps,
+                         std::vector<float>& sigmas) const;
 };
+
+// compute_empirical_mu of the Flux2 Klein pipeline (Flux2KleinPipeline.cpp:130-141):
+// the dynamic-shift mu for an image of image_seq_len tokens and num_steps steps.
+float flux2_empirical_mu(int64_t image_seq_len, int num_steps);
 
 }  // namespace dcpp
 

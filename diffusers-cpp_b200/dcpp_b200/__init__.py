@@ -21,6 +21,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdcpp_b200.so")
 
 DCPP_OK = 0
+DCPP_ERR_INVALID_ARG = 1
 STATUS_NAMES = {
     0: "DCPP_OK", 1: "DCPP_ERR_INVALID_ARG", 2: "DCPP_ERR_UNSUPPORTED", 3: "DCPP_ERR_CUDA",
     4: "DCPP_ERR_NCCL", 5: "DCPP_ERR_TIMEOUT", 6: "DCPP_ERR_OOM", 7: "DCPP_ERR_STATE",
@@ -57,6 +58,19 @@ class Flux2ConfigC(ctypes.Structure):
         ("rope_theta", ctypes.c_int64),
         ("eps", ctypes.c_float),
         ("guidance_embeds", ctypes.c_int32),
+    ]
+
+
+class FlowMatchConfigC(ctypes.Structure):
+    """dcpp_flow_match_config (the scheduler's constructor options)."""
+    _fields_ = [
+        ("num_train_timesteps", ctypes.c_int32),
+        ("shift", ctypes.c_float),
+        ("use_dynamic_shifting", ctypes.c_int32),
+        ("has_shift_terminal", ctypes.c_int32),
+        ("shift_terminal", ctypes.c_float),
+        ("invert_sigmas", ctypes.c_int32),
+        ("time_shift_type", ctypes.c_int32),
     ]
 
 
@@ -146,6 +160,10 @@ _SIGNATURES = {
     "dcpp_flux2_profile": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_double), _c_i64p]),
     "dcpp_flow_match_schedule": (ctypes.c_int, [ctypes.c_int, ctypes.c_float, _vp, _vp]),
+    "dcpp_flow_match_config_default": (None, [ctypes.POINTER(FlowMatchConfigC)]),
+    "dcpp_flow_match_schedule_ex": (ctypes.c_int, [ctypes.POINTER(FlowMatchConfigC), ctypes.c_int, ctypes.c_float,
+                                                   _vp, _vp, _vp]),
+    "dcpp_flux2_empirical_mu": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
     "dcpp_tp_get_unique_id": (ctypes.c_int, [_vp]),
     "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
@@ -716,6 +734,51 @@ def flow_match_schedule(n: int, shift: float = 1.0):
     if st != DCPP_OK:
         raise DcppError(st, "flow_match_schedule")
     return ts, sg
+
+
+class FlowMatchEulerDiscreteScheduler:
+    """The reference scheduler's constructor options and schedule(n, mu,
+    sigmas) (FlowMatchEulerDiscreteScheduler.hpp:11-23), through
+    dcpp_flow_match_schedule_ex.  schedule returns (timesteps[n],
+    sigmas[n + 1]) as float32 arrays."""
+
+    def __init__(self, num_train_timesteps=1000, shift=1.0, use_dynamic_shifting=False, shift_terminal=None,
+                 invert_sigmas=False, time_shift_type="exponential"):
+        if time_shift_type not in ("exponential", "linear"):
+            raise DcppError(DCPP_ERR_INVALID_ARG, f"unsupported time_shift_type: {time_shift_type}")
+        self.config = FlowMatchConfigC()
+        lib().dcpp_flow_match_config_default(ctypes.byref(self.config))
+        self.config.num_train_timesteps = int(num_train_timesteps)
+        self.config.shift = float(shift)
+        self.config.use_dynamic_shifting = int(bool(use_dynamic_shifting))
+        self.config.has_shift_terminal = int(shift_terminal is not None)
+        self.config.shift_terminal = float(shift_terminal) if shift_terminal is not None else 0.0
+        self.config.invert_sigmas = int(bool(invert_sigmas))
+        self.config.time_shift_type = 1 if time_shift_type == "linear" else 0
+
+    def schedule(self, n: int, mu: float = 0.0, sigmas=None):
+        ts = np.zeros(max(n, 0), dtype=np.float32)
+        sg = np.zeros(max(n, 0) + 1, dtype=np.float32)
+        base = None
+        if sigmas is not None:
+            base = np.ascontiguousarray(np.asarray(sigmas, dtype=np.float32))
+            if base.size != n:
+                raise DcppError(DCPP_ERR_INVALID_ARG, "sigmas must have n entries")
+        st = lib().dcpp_flow_match_schedule_ex(ctypes.byref(self.config), n, float(mu),
+                                               base.ctypes.data if base is not None else None, ts.ctypes.data,
+                                               sg.ctypes.data)
+        if st != DCPP_OK:
+            raise DcppError(st, "FlowMatchEulerDiscreteScheduler.schedule")
+        return ts, sg
+
+
+def flux2_empirical_mu(image_seq_len: int, num_steps: int) -> float:
+    """The Flux2 Klein pipeline's compute_empirical_mu (dynamic-shift mu)."""
+    mu = ctypes.c_float()
+    st = lib().dcpp_flux2_empirical_mu(int(image_seq_len), int(num_steps), ctypes.byref(mu))
+    if st != DCPP_OK:
+        raise DcppError(st, "flux2_empirical_mu")
+    return mu.value
 
 
 def qwen3_config_to_c(cfg) -> Qwen3ConfigC:

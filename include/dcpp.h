@@ -346,6 +346,38 @@ dcpp_status dcpp_flux2_profile(dcpp_flux2* model, int kind, double* ms, double* 
  * (1000*sigma) and n+1 sigmas. */
 dcpp_status dcpp_flow_match_schedule(int n, float shift, float* timesteps, float* sigmas);
 
+/* The scheduler's constructor options (FlowMatchEulerDiscreteScheduler.hpp:11-18);
+ * dcpp_flow_match_config_default gives the reference's defaults
+ * (1000 train timesteps, shift 1, no dynamic shifting, no shift_terminal,
+ * not inverted, exponential time shift). */
+#define DCPP_TIME_SHIFT_EXPONENTIAL 0
+#define DCPP_TIME_SHIFT_LINEAR 1
+typedef struct dcpp_flow_match_config {
+  int32_t num_train_timesteps;
+  float shift;
+  int32_t use_dynamic_shifting;
+  int32_t has_shift_terminal; /* shift_terminal is set (std::optional) */
+  float shift_terminal;
+  int32_t invert_sigmas;
+  int32_t time_shift_type; /* DCPP_TIME_SHIFT_* */
+} dcpp_flow_match_config;
+void dcpp_flow_match_config_default(dcpp_flow_match_config* config);
+
+/* FlowMatchEulerDiscreteScheduler::schedule(n, mu, sigmas)
+ * (FlowMatchEulerDiscreteScheduler.cpp:68-208) for any configuration:
+ * sigmas_in holds n base sigmas, or is NULL for n points from sigma_max = 1
+ * down to sigma_min = 1 / num_train_timesteps; writes n timesteps and n + 1
+ * sigmas (last 0, or 1 when inverted).  Same float arithmetic as the
+ * reference.  DCPP_ERR_INVALID_ARG for n <= 0, num_train_timesteps <= 0, an
+ * unknown time_shift_type, or a sigma <= 0 under dynamic shifting (the
+ * reference throws std::invalid_argument for each). */
+dcpp_status dcpp_flow_match_schedule_ex(const dcpp_flow_match_config* config, int n, float mu,
+                                        const float* sigmas_in, float* timesteps, float* sigmas);
+
+/* The pipeline's compute_empirical_mu (Flux2KleinPipeline.cpp:130-141): mu
+ * for dynamic shifting from the packed image token count and step count. */
+dcpp_status dcpp_flux2_empirical_mu(int64_t image_seq_len, int num_steps, float* mu);
+
 /* ---------------------------------------------------------------------- */
 /* Tensor parallelism (the sharding planner's column/row layout)           */
 /* ---------------------------------------------------------------------- */

@@ -14,7 +14,9 @@
  *   dcpp::Flux2Transformer2DModel           Flux2Transformer2DModel (Config,
  *                                           from_file, from_pretrained, forward;
  *                                           Flux2Transformer2DModel.hpp:10-50)
- *   dcpp::FlowMatchEulerDiscreteScheduler   schedule (FlowMatchEulerDiscreteScheduler.cpp:68-208)
+ *   dcpp::FlowMatchEulerDiscreteScheduler   schedule with every constructor option
+ *                                           (FlowMatchEulerDiscreteScheduler.cpp:8-208),
+ *                                           and compute_empirical_mu
  *   dcpp::Flux2KleinPipeline                denoise (Flux2KleinPipeline.cpp:496-537),
  *                                           with or without reference images
  * Errors become dcpp::Error (a std::runtime_error carrying the status), as the
@@ -197,13 +199,54 @@ private:
     dcpp_flux2* m_ = nullptr;
 };
 
+/* The pipeline's compute_empirical_mu (Flux2KleinPipeline.cpp:130-141). */
+inline float compute_empirical_mu(int64_t image_seq_len, int num_steps) {
+    float mu = 0.f;
+    check(dcpp_flux2_empirical_mu(image_seq_len, num_steps, &mu), "compute_empirical_mu");
+    return mu;
+}
+
+/* FlowMatchEulerDiscreteScheduler: the constructor's options with the
+ * reference's defaults (FlowMatchEulerDiscreteScheduler.hpp:11-18). */
 struct FlowMatchEulerDiscreteScheduler {
+    int num_train_timesteps = 1000;
     float shift = 1.0f;
-    /* n timesteps (1000 sigma) and n + 1 sigmas. */
-    std::pair<std::vector<float>, std::vector<float>> schedule(int n) const {
+    bool use_dynamic_shifting = false;
+    bool has_shift_terminal = false;
+    float shift_terminal = 0.0f;
+    bool invert_sigmas = false;
+    std::string time_shift_type = "exponential";
+
+    /* schedule(num_inference_steps, mu, sigmas) (FlowMatchEulerDiscreteScheduler.hpp:20-24):
+     * n timesteps and n + 1 sigmas; empty sigmas: n points from sigma_max
+     * down to sigma_min. */
+    std::pair<std::vector<float>, std::vector<float>> schedule(int n, float mu = 0.0f,
+                                                               const std::vector<float>& sigmas = {}) const {
+        dcpp_flow_match_config c;
+        dcpp_flow_match_config_default(&c);
+        c.num_train_timesteps = num_train_timesteps;
+        c.shift = shift;
+        c.use_dynamic_shifting = use_dynamic_shifting ? 1 : 0;
+        c.has_shift_terminal = has_shift_terminal ? 1 : 0;
+        c.shift_terminal = shift_terminal;
+        c.invert_sigmas = invert_sigmas ? 1 : 0;
+        if (time_shift_type == "linear")
+            c.time_shift_type = DCPP_TIME_SHIFT_LINEAR;
+        else if (time_shift_type != "exponential")
+            throw Error(DCPP_ERR_INVALID_ARG, "unsupported time_shift_type: " + time_shift_type);
+        if (!sigmas.empty() && sigmas.size() != static_cast<size_t>(n))
+            throw Error(DCPP_ERR_INVALID_ARG, "schedule: sigmas must have num_inference_steps entries");
         std::vector<float> t(static_cast<size_t>(n > 0 ? n : 0)), s(static_cast<size_t>(n > 0 ? n + 1 : 0));
-        check(dcpp_flow_match_schedule(n, shift, t.data(), s.data()), "schedule");
+        check(dcpp_flow_match_schedule_ex(&c, n, mu, sigmas.empty() ? nullptr : sigmas.data(), t.data(), s.data()),
+              "schedule");
         return {t, s};
+    }
+    /* The pipeline's denoise schedule (Flux2KleinPipeline.cpp:348-358):
+     * sigmas 1 - i/n and mu = compute_empirical_mu(image_seq_len, n). */
+    std::pair<std::vector<float>, std::vector<float>> pipeline_schedule(int n, int64_t image_seq_len) const {
+        std::vector<float> base(static_cast<size_t>(n > 0 ? n : 0));
+        for (int i = 0; i < n; ++i) base[static_cast<size_t>(i)] = static_cast<float>(1.0 - static_cast<double>(i) / n);
+        return schedule(n, compute_empirical_mu(image_seq_len, n), base);
     }
 };
 

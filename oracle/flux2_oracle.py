@@ -380,3 +380,60 @@ def flow_match_schedule(n: int, shift: float = 1.0):
     sig = [np.float32(shift * s / (1.0 + (shift - 1.0) * s)) for s in sig]
     ts = [np.float32(s * 1000.0) for s in sig]
     return ts, sig + [np.float32(0.0)]
+
+
+def flow_match_schedule_full(n: int, mu: float = 0.0, sigmas=None, num_train_timesteps: int = 1000,
+                             shift: float = 1.0, use_dynamic_shifting: bool = False, shift_terminal=None,
+                             invert_sigmas: bool = False, time_shift_type: str = "exponential"):
+    """FlowMatchEulerDiscreteScheduler::schedule(n, mu, sigmas) for every
+    constructor option, one float32 operation at a time
+    (FlowMatchEulerDiscreteScheduler.cpp:8-37 options, :43-66 time_shift,
+    :68-208 schedule).  Returns (timesteps[n], sigmas[n + 1]) as float32."""
+    f = np.float32
+    if num_train_timesteps <= 0 or n <= 0 or time_shift_type not in ("exponential", "linear"):
+        raise ValueError("invalid scheduler arguments")
+    T = f(num_train_timesteps)
+    if sigmas is not None:
+        if len(sigmas) != n:
+            raise ValueError("sigmas must have n entries")
+        base = [f(s) for s in sigmas]
+    else:
+        t_max = f(1.0) * T
+        t_min = (f(1.0) / T) * T
+        if n == 1:
+            base = [t_max / T]
+        else:
+            base = [(t_max - f(i) * (t_max - t_min) / f(n - 1)) / T for i in range(n)]
+    out = []
+    for s in base:
+        if use_dynamic_shifting:
+            if s <= 0:
+                raise ValueError("t must be positive")
+            odds = np.power(f(1.0) / s - f(1.0), f(1.0))
+            e = f(mu) if time_shift_type == "linear" else f(np.exp(np.float64(mu)))
+            out.append(e / (e + odds))
+        else:
+            sh = f(shift)
+            out.append(sh * s / (f(1.0) + (sh - f(1.0)) * s))
+    if shift_terminal is not None:
+        scale = (f(1.0) - out[-1]) / (f(1.0) - f(shift_terminal))
+        out = [f(1.0) - (f(1.0) - s) / scale for s in out]
+    if invert_sigmas:
+        out = [f(1.0) - s for s in out]
+    ts = np.array([s * T for s in out], dtype=np.float32)
+    return ts, np.array(out + [f(1.0) if invert_sigmas else f(0.0)], dtype=np.float32)
+
+
+def compute_empirical_mu(image_seq_len: int, num_steps: int) -> np.float32:
+    """The Flux2 Klein pipeline's dynamic-shift mu (Flux2KleinPipeline.cpp:130-141),
+    in float32."""
+    f = np.float32
+    a1, b1, a2, b2 = f(8.73809524e-05), f(1.89833333), f(0.00016927), f(0.45666666)
+    length = f(image_seq_len)
+    if image_seq_len > 4300:
+        return a2 * length + b2
+    m_200 = a2 * length + b2
+    m_10 = a1 * length + b1
+    a = (m_200 - m_10) / f(190.0)
+    b = m_200 - f(200.0) * a
+    return a * f(num_steps) + b

@@ -44,9 +44,27 @@ static int cpu_mode(const char* config_path) {
     EXPECT((dcpp::ShardingPlan::split(24, 5) == std::vector<int64_t>{4, 5, 5, 5, 5}));
     EXPECT((dcpp::ShardingPlan::split(6, 2, {2.f, 1.f}) == std::vector<int64_t>{4, 2}));
 
-    auto sched = dcpp::FlowMatchEulerDiscreteScheduler{}.schedule(4);
+    dcpp::FlowMatchEulerDiscreteScheduler sch;
+    auto sched = sch.pipeline_schedule(4, 4096);  // default: static shift 1, mu unused
     EXPECT(sched.first.size() == 4 && sched.second.size() == 5);
     EXPECT(sched.first[0] == 1000.f && sched.second[2] == 0.5f && sched.second[4] == 0.f);
+    auto lin = sch.schedule(2);  // sigma_max .. sigma_min
+    EXPECT(lin.second[0] == 1.f && lin.second[1] == 0.001f && lin.second[2] == 0.f);
+    sch.use_dynamic_shifting = true;
+    sch.time_shift_type = "linear";
+    auto dyn = sch.schedule(2, 1.0f, {0.5f, 0.25f});  // mu = 1, linear: the identity
+    EXPECT(dyn.second[0] == 0.5f && dyn.second[1] == 0.25f);
+    sch.time_shift_type = "cubic";
+    {
+        bool bad = false;
+        try {
+            sch.schedule(2);
+        } catch (const dcpp::Error& e) {
+            bad = e.status == DCPP_ERR_INVALID_ARG;
+        }
+        EXPECT(bad);
+    }
+    EXPECT(dcpp::compute_empirical_mu(8192, 4) == 0.00016927f * 8192.f + 0.45666666f);
 
     dcpp::Flux2Transformer2DModel host(nullptr, cfg);  // loader / shard layout only
     host.set_sharding(1, 2, {2.f, 1.f});
