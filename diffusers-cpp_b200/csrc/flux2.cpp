@@ -1712,6 +1712,53 @@ dcpp_status dcpp_flow_match_schedule_ex(const dcpp_flow_match_config* c, int n, 
   }
 }
 
+dcpp_status dcpp_flux2_prepare_txt_ids(int64_t batch, int64_t seq_len, int32_t* out) {
+  if (batch < 0 || seq_len < 0 || (!out && batch * seq_len > 0)) return DCPP_ERR_INVALID_ARG;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t l = 0; l < seq_len; ++l) {
+      int32_t* id = out + (b * seq_len + l) * 4;
+      id[0] = id[1] = id[2] = 0;
+      id[3] = static_cast<int32_t>(l);
+    }
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_flux2_prepare_img_ids(int64_t batch, int64_t packed_h, int64_t packed_w, int32_t* out) {
+  if (batch < 0 || packed_h < 0 || packed_w < 0 || (!out && batch * packed_h * packed_w > 0))
+    return DCPP_ERR_INVALID_ARG;
+  int32_t* id = out;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t y = 0; y < packed_h; ++y)
+      for (int64_t x = 0; x < packed_w; ++x, id += 4) {
+        id[0] = 0;
+        id[1] = static_cast<int32_t>(y);
+        id[2] = static_cast<int32_t>(x);
+        id[3] = 0;
+      }
+  return DCPP_OK;
+}
+
+dcpp_status dcpp_flux2_prepare_ref_image_ids(int64_t batch, int64_t n_images, const int64_t* packed_hw, int32_t* out) {
+  if (batch < 0 || n_images < 0 || (n_images > 0 && !packed_hw)) return DCPP_ERR_INVALID_ARG;
+  int64_t tokens = 0;
+  for (int64_t i = 0; i < n_images; ++i) {
+    if (packed_hw[2 * i] < 0 || packed_hw[2 * i + 1] < 0) return DCPP_ERR_INVALID_ARG;
+    tokens += packed_hw[2 * i] * packed_hw[2 * i + 1];
+  }
+  if (!out && batch * tokens > 0) return DCPP_ERR_INVALID_ARG;
+  int32_t* id = out;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t i = 0; i < n_images; ++i)  // image i sits at time coordinate 10 (i + 1)
+      for (int64_t y = 0; y < packed_hw[2 * i]; ++y)
+        for (int64_t x = 0; x < packed_hw[2 * i + 1]; ++x, id += 4) {
+          id[0] = static_cast<int32_t>(10 + 10 * i);
+          id[1] = static_cast<int32_t>(y);
+          id[2] = static_cast<int32_t>(x);
+          id[3] = 0;
+        }
+  return DCPP_OK;
+}
+
 dcpp_status dcpp_flux2_empirical_mu(int64_t image_seq_len, int num_steps, float* mu) {
   if (!mu) return DCPP_ERR_INVALID_ARG;
   *mu = dcpp::flux2_empirical_mu(image_seq_len, num_steps);

@@ -164,6 +164,9 @@ _SIGNATURES = {
     "dcpp_flow_match_schedule_ex": (ctypes.c_int, [ctypes.POINTER(FlowMatchConfigC), ctypes.c_int, ctypes.c_float,
                                                    _vp, _vp, _vp]),
     "dcpp_flux2_empirical_mu": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
+    "dcpp_flux2_prepare_txt_ids": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _vp]),
+    "dcpp_flux2_prepare_img_ids": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
+    "dcpp_flux2_prepare_ref_image_ids": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _vp, _vp]),
     "dcpp_tp_get_unique_id": (ctypes.c_int, [_vp]),
     "dcpp_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     "dcpp_allreduce": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int]),
@@ -770,6 +773,37 @@ class FlowMatchEulerDiscreteScheduler:
         if st != DCPP_OK:
             raise DcppError(st, "FlowMatchEulerDiscreteScheduler.schedule")
         return ts, sg
+
+
+def prepare_txt_ids(batch: int, seq_len: int):
+    """The pipeline's txt_ids [batch, seq_len, 4] int32 (dcpp_flux2_prepare_txt_ids)."""
+    out = np.zeros((batch, seq_len, 4), dtype=np.int32)
+    st = lib().dcpp_flux2_prepare_txt_ids(batch, seq_len, out.ctypes.data)
+    if st != DCPP_OK:
+        raise DcppError(st, "prepare_txt_ids")
+    return out
+
+
+def prepare_img_ids(batch: int, packed_h: int, packed_w: int):
+    """The pipeline's img_ids [batch, packed_h * packed_w, 4] int32."""
+    out = np.zeros((batch, packed_h * packed_w, 4), dtype=np.int32)
+    st = lib().dcpp_flux2_prepare_img_ids(batch, packed_h, packed_w, out.ctypes.data)
+    if st != DCPP_OK:
+        raise DcppError(st, "prepare_img_ids")
+    return out
+
+
+def prepare_ref_image_ids(batch: int, packed_sizes):
+    """The pipeline's image_latent_ids [batch, sum h*w, 4] int32 for reference
+    images of packed sizes [(h, w), ...] (image size / (VAE scale factor * 2))."""
+    hw = np.ascontiguousarray(np.asarray(packed_sizes, dtype=np.int64).reshape(-1, 2))
+    tokens = int((hw[:, 0] * hw[:, 1]).sum()) if hw.size else 0
+    out = np.zeros((batch, tokens, 4), dtype=np.int32)
+    st = lib().dcpp_flux2_prepare_ref_image_ids(batch, hw.shape[0], hw.ctypes.data if hw.size else None,
+                                                out.ctypes.data)
+    if st != DCPP_OK:
+        raise DcppError(st, "prepare_ref_image_ids")
+    return out
 
 
 def flux2_empirical_mu(image_seq_len: int, num_steps: int) -> float:

@@ -378,6 +378,18 @@ dcpp_status dcpp_flow_match_schedule_ex(const dcpp_flow_match_config* config, in
  * for dynamic shifting from the packed image token count and step count. */
 dcpp_status dcpp_flux2_empirical_mu(int64_t image_seq_len, int num_steps, float* mu);
 
+/* The pipeline's RoPE position ids (host memory, int32, 4 axes (t, h, w, l)
+ * per token, batch-major):
+ *   txt_ids [batch, seq_len, 4] = (0, 0, 0, l)           (prepare_txt_ids, Flux2KleinPipeline.cpp:26-46)
+ *   img_ids [batch, packed_h * packed_w, 4] = (0, y, x, 0) (prepare_img_ids, :48-72)
+ *   image_latent_ids [batch, sum_i h_i * w_i, 4] = (10 + 10 i, y, x, 0) for
+ *     reference image i of packed size packed_hw[2 i] x packed_hw[2 i + 1]
+ *     (the image size / (VAE scale factor * 2))      (prepare_ref_image_ids, :75-127)
+ * The token counts are batch * ... ; out must hold 4 int32 per token. */
+dcpp_status dcpp_flux2_prepare_txt_ids(int64_t batch, int64_t seq_len, int32_t* out);
+dcpp_status dcpp_flux2_prepare_img_ids(int64_t batch, int64_t packed_h, int64_t packed_w, int32_t* out);
+dcpp_status dcpp_flux2_prepare_ref_image_ids(int64_t batch, int64_t n_images, const int64_t* packed_hw, int32_t* out);
+
 /* ---------------------------------------------------------------------- */
 /* Tensor parallelism (the sharding planner's column/row layout)           */
 /* ---------------------------------------------------------------------- */

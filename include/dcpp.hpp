@@ -199,6 +199,34 @@ private:
     dcpp_flux2* m_ = nullptr;
 };
 
+/* The pipeline's RoPE position ids, int32 (t, h, w, l) per token,
+ * batch-major (Flux2KleinPipeline.cpp:26-127). */
+inline std::vector<int32_t> prepare_txt_ids(int64_t batch, int64_t seq_len) {
+    std::vector<int32_t> ids(static_cast<size_t>(batch > 0 && seq_len > 0 ? batch * seq_len * 4 : 0));
+    check(dcpp_flux2_prepare_txt_ids(batch, seq_len, ids.data()), "prepare_txt_ids");
+    return ids;
+}
+inline std::vector<int32_t> prepare_img_ids(int64_t batch, int64_t packed_h, int64_t packed_w) {
+    std::vector<int32_t> ids(
+        static_cast<size_t>(batch > 0 && packed_h > 0 && packed_w > 0 ? batch * packed_h * packed_w * 4 : 0));
+    check(dcpp_flux2_prepare_img_ids(batch, packed_h, packed_w, ids.data()), "prepare_img_ids");
+    return ids;
+}
+/* packed_sizes: (h, w) of each reference image (its size / (VAE scale factor * 2)). */
+inline std::vector<int32_t> prepare_ref_image_ids(int64_t batch, const std::vector<std::pair<int64_t, int64_t>>& packed_sizes) {
+    std::vector<int64_t> hw;
+    int64_t tokens = 0;
+    for (const auto& s : packed_sizes) {
+        hw.push_back(s.first);
+        hw.push_back(s.second);
+        tokens += s.first * s.second;
+    }
+    std::vector<int32_t> ids(static_cast<size_t>(batch > 0 && tokens > 0 ? batch * tokens * 4 : 0));
+    check(dcpp_flux2_prepare_ref_image_ids(batch, static_cast<int64_t>(packed_sizes.size()), hw.data(), ids.data()),
+          "prepare_ref_image_ids");
+    return ids;
+}
+
 /* The pipeline's compute_empirical_mu (Flux2KleinPipeline.cpp:130-141). */
 inline float compute_empirical_mu(int64_t image_seq_len, int num_steps) {
     float mu = 0.f;

@@ -424,6 +424,36 @@ def flow_match_schedule_full(n: int, mu: float = 0.0, sigmas=None, num_train_tim
     return ts, np.array(out + [f(1.0) if invert_sigmas else f(0.0)], dtype=np.float32)
 
 
+def prepare_txt_ids(batch: int, seq_len: int) -> np.ndarray:
+    """txt_ids [B, L, 4] = (0, 0, 0, l) (Flux2KleinPipeline.cpp:26-46)."""
+    ids = np.zeros((batch, seq_len, 4), dtype=np.int32)
+    ids[:, :, 3] = np.arange(seq_len, dtype=np.int32)
+    return ids
+
+
+def prepare_img_ids(batch: int, packed_h: int, packed_w: int) -> np.ndarray:
+    """img_ids [B, h*w, 4] = (0, y, x, 0), row-major over (y, x)
+    (Flux2KleinPipeline.cpp:48-72)."""
+    ids = np.zeros((batch, packed_h * packed_w, 4), dtype=np.int32)
+    for y in range(packed_h):
+        for x in range(packed_w):
+            ids[:, y * packed_w + x, 1] = y
+            ids[:, y * packed_w + x, 2] = x
+    return ids
+
+
+def prepare_ref_image_ids(batch: int, packed_sizes) -> np.ndarray:
+    """image_latent_ids [B, sum h_i*w_i, 4] = (10 + 10 i, y, x, 0) per
+    reference image i (Flux2KleinPipeline.cpp:75-127)."""
+    rows = []
+    for i, (h, w) in enumerate(packed_sizes):
+        for y in range(h):
+            for x in range(w):
+                rows.append((10 + 10 * i, y, x, 0))
+    one = np.array(rows, dtype=np.int32).reshape(-1, 4)
+    return np.repeat(one[None], batch, axis=0)
+
+
 def compute_empirical_mu(image_seq_len: int, num_steps: int) -> np.float32:
     """The Flux2 Klein pipeline's dynamic-shift mu (Flux2KleinPipeline.cpp:130-141),
     in float32."""

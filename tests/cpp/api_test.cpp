@@ -65,6 +65,12 @@ static int cpu_mode(const char* config_path) {
         EXPECT(bad);
     }
     EXPECT(dcpp::compute_empirical_mu(8192, 4) == 0.00016927f * 8192.f + 0.45666666f);
+    auto img = dcpp::prepare_img_ids(1, 2, 3);
+    EXPECT(img.size() == 24 && img[4 * 5 + 1] == 1 && img[4 * 5 + 2] == 2 && img[4 * 5 + 0] == 0);
+    auto txt = dcpp::prepare_txt_ids(2, 3);
+    EXPECT(txt.size() == 24 && txt[4 * 5 + 3] == 2);
+    auto refi = dcpp::prepare_ref_image_ids(1, {{1, 2}, {2, 1}});
+    EXPECT(refi.size() == 16 && refi[0] == 10 && refi[4 * 3 + 0] == 20 && refi[4 * 3 + 1] == 1);
 
     dcpp::Flux2Transformer2DModel host(nullptr, cfg);  // loader / shard layout only
     host.set_sharding(1, 2, {2.f, 1.f});
