@@ -319,7 +319,9 @@ def run_reference(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": CONFIGS[args.config]["workload"], "global_batch": CONFIGS[args.config]["batch"],
                    "seq_len": CONFIGS[args.config]["grid"][0] * CONFIGS[args.config]["grid"][1] + CONFIGS[args.config]["n_txt"],
-                   "parallelism": "cpu"},
+                   # the GPU arm's job description (the same workload); this
+                   # arm runs it on rank 0's host cores (cpu_baseline)
+                   "parallelism": f"tp{args.gpus}", "weights": CONFIGS[args.config]["wtype"]},
         "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
